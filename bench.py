@@ -1,0 +1,407 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 routed-expert FFN (ramvamp's MoE block).
+
+Default workload (expert-FFN half): batch-1 greedy decode
+of Qwen3-30B-A3B through all 48 MoE layers with every expert resident in HBM
+(17.5 GB of Q4_K/Q6_K blobs).  A step is one token through the 48 MoE
+blocks (RMSNorm, router, top-8, Q8_K, gate/up/SwiGLU/down, combine); the
+attention half of the model is not part of this path.  Each step decodes a
+different seeded token, and a step streams 1.1 GB of expert weights, far
+more than the 126 MB L2, so nothing is served from L2 between steps.
+
+Arms:
+  default            the CUDA path (one CUDA graph per step, replayed)
+  --impl reference   the reference's CPU algorithm (the C oracle restating
+                     ramvamp's AVX2 path) on this host's cores, on a bounded
+                     sample of layers, scaled to 48 layers
+
+Prints one JSON line (rank 0).  Multi-GPU (torchrun, N>1): batch-1 decode
+does not shard, so every rank runs an independent replica ("replicas only");
+the value is the sum over ranks, timed as the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, M, E, K, LAYERS = 2048, 768, 128, 8, 48
+SEED = 20261201
+METRIC = "decode tok/s (expert FFN, 48 MoE layers, batch 1)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def layouts(rv, n_layers):
+    return [rv.qwen3_layer_layout(l) for l in range(n_layers)]
+
+
+def expert_bytes_per_token(lays):
+    return sum(K * (L.gate_len + L.up_len + L.down_len) for L in lays)
+
+
+# ------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.idx = gpu_id
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(kernel: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f).get(kernel)
+
+
+# ------------------------------------------------------- CPU baseline
+def cpu_baseline_sample(orc, lays, blobs_by_layer, routers, norm, tokens, threads):
+    """The oracle (AVX2 restatement of the reference) on a sample of layers:
+    returns seconds per token scaled to len(lays) layers."""
+    sample_layers = sorted(blobs_by_layer)
+    oracle_layers = {}
+    for l in sample_layers:
+        L = lays[l]
+        oracle_layers[l] = orc.make_layer(H, M, E, K, 1e-6, norm, routers[l], blobs_by_layer[l], L.stride,
+                                          L.gate_off, L.up_off, L.down_off, L.gate_format, L.up_format,
+                                          L.down_format)
+    x = tokens[:1].copy()
+    for l in sample_layers:  # warm-up
+        x, _, _, _ = orc.moe_decode(oracle_layers[l], x, threads=threads)
+    t0 = time.perf_counter()
+    n_tok = 0
+    while True:
+        for i in range(tokens.shape[0]):
+            x = tokens[i:i + 1].copy()
+            for l in sample_layers:
+                x, _, _, _ = orc.moe_decode(oracle_layers[l], x, threads=threads)
+            n_tok += 1
+        if time.perf_counter() - t0 > 10.0 or n_tok >= 64:
+            break
+    dt = time.perf_counter() - t0
+    return dt / n_tok * len(lays) / len(sample_layers), n_tok, sample_layers
+
+
+# ----------------------------------------------------------- CUDA arm
+def run_cuda(args):
+    import torch
+    import torch.distributed as dist
+
+    import ramvamp_b200 as rv
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=120))
+    dev = local if world > 1 else 0
+    torch.cuda.set_device(dev)
+    n_layers = args.layers
+    lays = layouts(rv, n_layers)
+    table = rv.ExpertTable(lays, device=dev)
+    for l in range(n_layers):
+        table.fill_synthetic(l, SEED + l, 0.02)
+    routers = [rv.synth_normal(SEED + 1000 + l, 0, 0.02, E * H).view(E, H).contiguous() for l in range(n_layers)]
+    norm = torch.ones(H, dtype=torch.float32, device="cuda")
+    eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=1, device=dev)
+    n_steps = args.warmup + args.steps
+    tokens = rv.synth_normal(SEED + 7 + rank, 0, 1.0, n_steps * H).view(n_steps, H).contiguous()
+    resid = torch.empty(1, H, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def step_body():
+        for l in range(n_layers):
+            eng.forward(table, l, norm, routers[l], resid)
+
+    # Capture one decode step (48 MoE blocks) into a CUDA graph.
+    with torch.cuda.stream(stream):
+        resid.copy_(tokens[0:1])
+        step_body()  # eager run: also initializes everything
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_body()
+    torch.cuda.synchronize()
+
+    # Parity spot-check of the graph against the eager path on token 0.
+    with torch.cuda.stream(stream):
+        resid.copy_(tokens[0:1])
+        graph.replay()
+        g_out = resid.clone()
+        resid.copy_(tokens[0:1])
+        step_body()
+    stream.synchronize()
+    assert torch.equal(g_out, resid), "graph replay differs from eager forward"
+
+    def run_steps(lo, hi):
+        with torch.cuda.stream(stream):
+            for i in range(lo, hi):
+                resid.copy_(tokens[i:i + 1])
+                graph.replay()
+
+    run_steps(0, args.warmup)
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(dev)
+    uuid = str(getattr(props, "uuid", ""))
+    clocks = ClockSampler(("GPU-" + uuid if uuid and not uuid.startswith("GPU-") else uuid) or str(dev))
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    run_steps(args.warmup, n_steps)
+    ev1.record(stream)
+    ev1.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_per_step = ms / args.steps
+    tok_s = world * args.steps / (ms / 1e3)
+
+    # Per-kernel durations, measured with events baked into a profiling graph
+    # (back-to-back launches, no host gaps), over the same steps.
+    eng.profile_enable(n_layers)
+    pgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        eng.profile_rewind()
+        resid.copy_(tokens[0:1])
+    stream.synchronize()
+    with torch.cuda.graph(pgraph, stream=stream):
+        step_body()
+    stage = []
+    for i in range(args.warmup, n_steps):
+        with torch.cuda.stream(stream):
+            resid.copy_(tokens[i:i + 1])
+            pgraph.replay()
+        stream.synchronize()
+        stage.append(eng.profile_read())
+    stage = np.stack(stage)  # [steps][layers][4]
+    gu_ms = float(stage[:, :, 1].mean())
+    dn_ms = float(stage[:, :, 2].mean())
+    route_ms = float(stage[:, :, 0].mean())
+    comb_ms = float(stage[:, :, 3].mean())
+    del pgraph
+
+    gu_bytes = K * (lays[0].gate_len + lays[0].up_len)  # same for every layer
+    peak, peak_kind = measured_peaks()
+    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    tb = ncu_traffic("k_gate_up")
+
+    # e2e through the host-buffer C-ABI call (rv_moe_forward_host), one call
+    # per layer as a caller holding host residuals makes it.
+    import torch as _t
+    host_tok = _t.empty(n_steps, H, dtype=_t.float32).pin_memory()
+    host_tok.copy_(tokens.cpu())
+    hres = _t.empty(1, H, dtype=_t.float32).pin_memory()
+    for i in range(min(3, args.warmup)):
+        hres.copy_(host_tok[i:i + 1])
+        for l in range(n_layers):
+            eng.forward_host(table, l, norm, routers[l], hres)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.warmup, n_steps):
+        hres.copy_(host_tok[i:i + 1])
+        for l in range(n_layers):
+            eng.forward_host(table, l, norm, routers[l], hres)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_tok_s = world * args.steps / e2e_s
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        from oracle import oracle as orc
+        orc.build()
+        sample = [0, 6] if n_layers > 6 else [0]
+        blobs = {l: rv.alias(table.view(l, 0).blob, E * lays[l].stride).cpu().numpy() for l in sample}
+        rnp = {l: routers[l].cpu().numpy() for l in sample}
+        threads = os.cpu_count() or 1
+        s_per_tok, n_tok, used = cpu_baseline_sample(orc, lays, blobs, rnp, norm.cpu().numpy(),
+                                                     tokens[:8].cpu().numpy(), threads)
+        cpu = {"value": round(1.0 / s_per_tok, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{n_tok} tokens through layers {used} (one Q6_K-down, one Q4_K-down) on the "
+                         f"C oracle's AVX2 arm, time scaled to {n_layers} layers"}
+
+    if rank == 0:
+        step_bytes = expert_bytes_per_token(lays)
+        line = {
+            "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 (dp4a) + f32",
+            "data": "synthetic: seeded N(0,1) tokens, N(0,0.02) router and expert weights quantized by the "
+                    "reference's Q4_K/Q6_K quantizers",
+            "config": {"workload": f"config1 expert FFN: batch-1 decode through {n_layers} MoE layers of "
+                                   "Qwen3-30B-A3B (hidden 2048, moe 768, 128 experts, top-8), all experts "
+                                   "resident in HBM",
+                       "layers": n_layers, "tokens_per_step": 1, "router": "exact (serial f32 chains)",
+                       "numerics": "bit-identical to the reference AVX2 path",
+                       "l2": "inputs larger than L2: each step streams %.2f GB of expert weights" % (step_bytes / 1e9),
+                       "parallelism": "replicas" if world > 1 else "single GPU", "cuda_graph": True},
+            "expert_hbm_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
+            "stage_ms_per_layer": {"routing": round(route_ms, 5), "gate_up": round(gu_ms, 5),
+                                   "down": round(dn_ms, 5), "combine": round(comb_ms, 5)},
+            "roofline": {"kernel": "k_gate_up", "bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": gu_bytes,
+                         "traffic": tb},
+            "e2e": {"value": round(e2e_tok_s, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": n_layers * H * 4, "d2h_bytes_per_step": n_layers * H * 4,
+                    "path": "rv_moe_forward_host per layer (pinned host residual in, result out)"},
+            "gpu_launches": args.steps * n_layers * 7,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        del graph
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    import ramvamp_b200 as rv  # layout arithmetic only (no GPU calls)
+
+    orc.build()
+    n_layers = args.layers
+    lays = layouts(rv, n_layers)
+    threads = os.cpu_count() or 1
+    sample = [0, 6] if n_layers > 6 else [0]
+    blobs = {l: orc.fill_layer_synthetic(lays[l], SEED + l, 0.02, threads) for l in sample}
+    routers = {l: orc.synth_normal(SEED + 1000 + l, 0, 0.02, E * H).reshape(E, H) for l in sample}
+    norm = np.ones(H, np.float32)
+    n_steps = args.warmup + args.steps
+    tokens = orc.synth_normal(SEED + 7, 0, 1.0, n_steps * H).reshape(n_steps, H)
+    oracle_layers = {l: orc.make_layer(H, M, E, K, 1e-6, norm, routers[l], blobs[l], lays[l].stride,
+                                       lays[l].gate_off, lays[l].up_off, lays[l].down_off,
+                                       lays[l].gate_format, lays[l].up_format, lays[l].down_format)
+                     for l in sample}
+
+    def step(i):
+        x = tokens[i:i + 1].copy()
+        for l in sample:
+            x, _, _, _ = orc.moe_decode(oracle_layers[l], x, threads=threads)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.warmup, n_steps):
+        step(i)
+    dt = time.perf_counter() - t0
+    s_per_tok = dt / args.steps * n_layers / len(sample)
+    v = 1.0 / s_per_tok
+    sample_desc = (f"each step: one token through layers {sample} (one Q6_K-down, one Q4_K-down) on the C "
+                   f"oracle's AVX2 arm with {threads} threads, time scaled to {n_layers} layers")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(s_per_tok * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 + f32",
+        "data": "synthetic (same seeds and weights as the CUDA arm)",
+        "config": {"workload": f"config1 expert FFN: batch-1 decode through {n_layers} MoE layers of "
+                               "Qwen3-30B-A3B (sampled layers, scaled)", "layers": n_layers,
+                   "tokens_per_step": 1},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample_desc},
+        "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_cuda(args)
+
+
+if __name__ == "__main__":
+    main()

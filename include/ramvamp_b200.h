@@ -1,0 +1,338 @@
+/*
+ * ramvamp_b200.h -- C ABI of the B200 (sm_100a) routed-expert FFN path.
+ *
+ * A drop-in replacement for ramvamp's CPU MoE-layer and quantized-matvec
+ * entry points.  Every function takes plain pointers and sizes (no
+ * CUDA, torch or Rust types), returns an rv_status, and never panics or
+ * aborts on bad input: validation happens once per call, before any launch,
+ * with the same checks and error precedence as the Rust function it
+ * replaces.  A human-readable detail of the most recent failure on the
+ * calling thread is available from rv_last_error().
+ *
+ * Pointers documented as "device" are CUDA device addresses on the device
+ * current when the call is made; "host" pointers are ordinary CPU memory.
+ * `stream` is a cudaStream_t passed as void* (NULL = the legacy default
+ * stream).  Calls that only enqueue work do not synchronize, so they can be
+ * captured into a CUDA graph; the *_host variants synchronize on `stream`.
+ *
+ * Reference citations are paths inside the ramvamp tree
+ * (crates/core/src/...).
+ */
+#ifndef RAMVAMP_B200_H
+#define RAMVAMP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RV_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define RV_API __attribute__((visibility("default")))
+#else
+#define RV_API
+#endif
+
+typedef void *rv_stream;
+
+/* Status codes.  1..9 map one-to-one onto the variants of
+ * kernels/error.rs:20-110 (KernelError); the rest are GPU-side conditions
+ * the CPU reference cannot hit. */
+typedef enum rv_status {
+  RV_OK = 0,
+  RV_ERR_INDIVISIBLE_ROW = 1,              /* KernelError::IndivisibleRow */
+  RV_ERR_ROW_BYTES_NOT_BLOCK_MULTIPLE = 2, /* KernelError::RowBytesNotBlockMultiple */
+  RV_ERR_BLOCK_COUNT_MISMATCH = 3,         /* KernelError::BlockCountMismatch */
+  RV_ERR_QUANTIZE_LEN_MISMATCH = 4,        /* KernelError::QuantizeLenMismatch */
+  RV_ERR_LENGTH_MISMATCH = 5,              /* KernelError::LengthMismatch */
+  RV_ERR_EMPTY = 6,                        /* KernelError::Empty */
+  RV_ERR_INVALID_HEAD_DIM = 7,             /* KernelError::InvalidHeadDim */
+  RV_ERR_UNIMPLEMENTED = 8,                /* KernelError::Unimplemented */
+  RV_ERR_UNSUPPORTED_FORMAT = 9,           /* KernelError::UnsupportedFormat */
+  RV_ERR_ROUTED_OUT_OF_RANGE = 10,         /* ForwardError::RoutedExpertOutOfRange */
+  RV_ERR_LAYER_OUT_OF_RANGE = 11,          /* IoError::LayerOutOfRange */
+  RV_ERR_PROTOCOL = 12,                    /* IoError::Io protocol misuse (step state) */
+  RV_ERR_INVALID_ARGUMENT = 13,            /* null pointer, misaligned buffer, bad flag */
+  RV_ERR_CUDA = 14,                        /* a CUDA runtime call failed */
+  RV_ERR_NCCL = 15,                        /* a collective failed */
+  RV_ERR_TIMEOUT = 16                      /* a bounded device-side wait ran out */
+} rv_status;
+
+/* Quantization formats (kernels/quants/mod.rs:57-70). */
+typedef enum rv_quant_format {
+  RV_Q4_K = 0, /* 144 B / 256 weights */
+  RV_Q5_K = 1, /* 176 B / 256 weights */
+  RV_Q6_K = 2, /* 210 B / 256 weights */
+  RV_Q8_0 = 3, /*  34 B /  32 weights */
+  RV_Q8_K = 4  /* 292 B / 256 weights (activations) */
+} rv_quant_format;
+
+/* One Q8_K activation block.  The reference's BlockQ8K
+ * (kernels/quants/blocks.rs:260-268) is not repr(C); this is the packed
+ * 292-byte C layout every rv_ call uses: d at 0, qs at 4, bsums at 260. */
+typedef struct rv_block_q8k {
+  float d;
+  int8_t qs[256];
+  int16_t bsums[16];
+} rv_block_q8k;
+
+/* ------------------------------------------------------------ library */
+/* Version string of the library build. */
+RV_API const char *rv_version(void);
+/* Name of a status code ("LengthMismatch", ...). */
+RV_API const char *rv_status_name(int status);
+/* Copies the detail message of the calling thread's most recent failure
+ * into buf (NUL-terminated, truncated to len); returns its full length. */
+RV_API size_t rv_last_error(char *buf, size_t len);
+/* Block geometry: QuantFormat::block_bytes / block_weights
+ * (kernels/quants/mod.rs:74-90). 0 for an unknown format. */
+RV_API size_t rv_block_bytes(int format);
+RV_API size_t rv_block_weights(int format);
+/* QuantFormat::row_bytes (kernels/quants/mod.rs:96-105):
+ * RV_ERR_INDIVISIBLE_ROW when in_dim is not a block multiple. */
+RV_API int rv_row_bytes(int format, size_t in_dim, size_t *out);
+/* Reads and clears the device-side error word the kernels of this library
+ * set when a bounded wait ran out (RV_ERR_TIMEOUT) or a device check failed.
+ * Synchronizes `stream`. */
+RV_API int rv_device_status(int device, rv_stream stream);
+
+/* ----------------------------------------------------------- kernels */
+/* Replaces quants::quantize_row_q8_k (kernels/quants/quantize.rs:68-103,
+ * AVX2 arm avx2.rs:1070-1130).  x: device, n floats; out: device,
+ * out_blocks blocks.  Byte-identical to the reference on finite input.
+ * Any number of rows may be passed as one long row (blocks are
+ * independent).  RV_ERR_QUANTIZE_LEN_MISMATCH when n != 256*out_blocks. */
+RV_API int rv_quantize_row_q8_k(const float *x, size_t n, rv_block_q8k *out, size_t out_blocks,
+                         rv_stream stream);
+
+/* Replaces gemv::gemv_q8_k / Backend::gemv_q8_k (kernels/gemv.rs:347-371,
+ * kernels/backend.rs:115-124): out[r] = weight_row_r . acts for r in
+ * 0..out_dim.  weight: device, weight_len bytes (any byte alignment);
+ * acts: device, acts_len blocks; out: device, out_len floats.  Bit-identical
+ * to the reference's AVX2 path. */
+RV_API int rv_gemv_q8_k(int format, const uint8_t *weight, size_t weight_len, size_t in_dim,
+                 size_t out_dim, const rv_block_q8k *acts, size_t acts_len, float *out,
+                 size_t out_len, rv_stream stream);
+
+/* Replaces gemv::gemv_q8_k_rows (kernels/gemv.rs:386-410): the rows
+ * [row_start, row_end) only; weight/in_dim/out_dim describe the whole
+ * matrix, out holds row_end-row_start floats. */
+RV_API int rv_gemv_q8_k_rows(int format, const uint8_t *weight, size_t weight_len, size_t in_dim,
+                      size_t out_dim, const rv_block_q8k *acts, size_t acts_len, size_t row_start,
+                      size_t row_end, float *out, size_t out_len, rv_stream stream);
+
+/* Replaces gemv::gemv_q8_k_batched (kernels/gemv.rs:444-477):
+ * out[i*n_acts + a] = weight_row_(row_start+i) . act_row_a. */
+RV_API int rv_gemv_q8_k_batched(int format, const uint8_t *weight, size_t weight_len, size_t in_dim,
+                         size_t out_dim, const rv_block_q8k *acts, size_t acts_len, size_t n_acts,
+                         size_t row_start, size_t row_end, float *out, size_t out_len,
+                         rv_stream stream);
+
+/* One matrix of a fused row space (gemv::FusedPart, kernels/gemv.rs:655-686).
+ * weight and acts are device pointers. */
+typedef struct rv_fused_part {
+  int32_t format;
+  const uint8_t *weight;
+  size_t weight_len;
+  size_t in_dim;
+  size_t out_dim;
+  const rv_block_q8k *acts;
+  size_t acts_len;
+} rv_fused_part;
+
+/* Replaces gemv::gemv_q8_k_fused_rows (kernels/gemv.rs:747-823): rows
+ * [row_start,row_end) of the concatenated row spaces of parts (host array).
+ * out: device, row_end-row_start floats. */
+RV_API int rv_gemv_q8_k_fused_rows(const rv_fused_part *parts, size_t n_parts, size_t row_start,
+                            size_t row_end, float *out, size_t out_len, rv_stream stream);
+
+/* Replaces Backend::rmsnorm / primitives::rmsnorm (kernels/primitives/norm.rs:
+ * 275-298) for n_rows rows of `n` floats (x, out: device [n_rows][n];
+ * weight: device [n]).  f64 mean of squares, bit-identical. */
+RV_API int rv_rmsnorm(const float *x, const float *weight, size_t n, size_t n_rows, float eps, float *out,
+               rv_stream stream);
+
+/* Replaces Backend::softmax / primitives::softmax (kernels/primitives/softmax.rs:
+ * 18-40), in place on n_rows rows of n floats (device).  n <= 1024. */
+RV_API int rv_softmax(float *x, size_t n, size_t n_rows, rv_stream stream);
+
+/* Replaces Backend::swiglu_combine / primitives::swiglu_combine
+ * (kernels/primitives/activation.rs:153-165): gate[i] <- silu(gate[i]) * up[i]
+ * (device).  The SiLU's exponential reproduces glibc expf bit for bit. */
+RV_API int rv_swiglu_combine(float *gate, size_t gate_len, const float *up, size_t up_len,
+                      rv_stream stream);
+
+/* Integer taps for parity tests (no reference counterpart beyond the
+ * integer stages of avx2.rs:554-838): for each of the n_blocks blocks of one
+ * weight row against one activation row, the eight i32 lane sums the AVX2
+ * dot forms (lanes_out[n_blocks][8]) and, for Q4_K/Q5_K, the four min-lane
+ * sums (mins_out[n_blocks][4], zero for Q6_K).  All device pointers. */
+RV_API int rv_debug_block_sums(int format, const uint8_t *weight_row, size_t w_len,
+                        const rv_block_q8k *acts, size_t n_blocks, int32_t *lanes_out,
+                        int32_t *mins_out, rv_stream stream);
+
+/* ------------------------------------------------------- expert table */
+/* Geometry of one layer's expert file (format/layout.rs:1-60,
+ * io/expert.rs:27-86): blob e occupies [e*stride, (e+1)*stride). */
+typedef struct rv_layer_layout {
+  uint32_t n_experts;
+  uint32_t _pad;
+  uint64_t stride;
+  uint64_t gate_off, gate_len;
+  uint64_t up_off, up_len;
+  uint64_t down_off, down_len;
+  int32_t gate_format, up_format, down_format;
+  uint32_t hidden, moe; /* gate/up are [moe][hidden], down [hidden][moe] */
+} rv_layer_layout;
+
+/* Device pointers of one resident expert (io/expert.rs:49-86). */
+typedef struct rv_expert_view {
+  const uint8_t *blob;
+  const uint8_t *gate, *up, *down;
+  uint64_t gate_len, up_len, down_len;
+  int32_t gate_format, up_format, down_format;
+} rv_expert_view;
+
+typedef struct rv_expert_table rv_expert_table;
+
+/* Creates the HBM-resident expert table that stands in for
+ * io::ExpertStream (io/stream.rs:1147-1472): every layer's expert file is
+ * allocated once on `device` (n_layers layouts, host array). */
+RV_API int rv_expert_table_create(int device, const rv_layer_layout *layers, uint32_t n_layers,
+                           rv_expert_table **out);
+RV_API void rv_expert_table_destroy(rv_expert_table *t);
+/* Copies n_experts consecutive blobs starting at expert_first into layer
+ * `layer`.  src is host memory unless src_on_device != 0; len must be
+ * n_experts*stride.  Synchronizes `stream`. */
+RV_API int rv_expert_table_upload(rv_expert_table *t, uint32_t layer, uint32_t expert_first,
+                           uint32_t n_experts, const void *src, size_t len, int src_on_device,
+                           rv_stream stream);
+RV_API int rv_expert_table_layout(const rv_expert_table *t, uint32_t layer, rv_layer_layout *out);
+RV_API uint32_t rv_expert_table_n_layers(const rv_expert_table *t);
+/* io/stream.rs:1472 (begin_layer): opens a step for `experts` (host array).
+ * Every expert is resident, so every request is a hit; a duplicate id is
+ * listed once, at its first position, like the reference. */
+RV_API int rv_expert_table_begin_layer(rv_expert_table *t, uint32_t layer, const uint32_t *experts,
+                                size_t n);
+/* io/stream.rs:1551/1558 (hits/misses): (index into the request, slot)
+ * pairs of the open step, written to host arrays of capacity cap; the
+ * count is returned in *n_out.  The slot of expert e is e.  misses is
+ * always empty. */
+RV_API int rv_expert_table_hits(const rv_expert_table *t, uint32_t *index_out, uint32_t *slot_out,
+                         size_t cap, size_t *n_out);
+RV_API int rv_expert_table_misses(const rv_expert_table *t, uint32_t *index_out, uint32_t *slot_out,
+                           size_t cap, size_t *n_out);
+/* io/stream.rs:1575 (await_misses): nothing is ever in flight; returns
+ * RV_OK, or RV_ERR_PROTOCOL without an open step. */
+RV_API int rv_expert_table_await_misses(rv_expert_table *t);
+/* io/stream.rs:1604 (view): device view of a resident slot. */
+RV_API int rv_expert_table_view(const rv_expert_table *t, uint32_t layer, uint32_t slot,
+                         rv_expert_view *out);
+/* io/stream.rs:2123 (end_layer): closes the open step. */
+RV_API int rv_expert_table_end_layer(rv_expert_table *t, uint32_t layer);
+/* Access counters (io/stream.rs:297-400 StreamStats subset): requests and
+ * hits since creation. */
+RV_API int rv_expert_table_stats(const rv_expert_table *t, uint64_t *accesses, uint64_t *hits);
+
+/* ------------------------------------------------------ MoE layer */
+/* Layer geometry (model ArchInfo subset, format/manifest.rs:72-105). */
+typedef struct rv_moe_config {
+  uint32_t hidden;     /* 2048 for Qwen3-30B-A3B */
+  uint32_t moe;        /* moe_intermediate, 768 */
+  uint32_t n_experts;  /* 128 (GPU path: <= 256) */
+  uint32_t top_k;      /* 8 (<= 16) */
+  int32_t norm_topk_prob;
+  float eps;           /* rms_norm_eps, 1e-6 */
+} rv_moe_config;
+
+typedef struct rv_moe rv_moe;
+
+/* Flags of rv_moe_forward. */
+#define RV_MOE_EXACT 0u        /* every stage bit-identical to the reference */
+#define RV_MOE_TENSOR 1u       /* prefill experts on tcgen05 tensor cores:
+                                  integer sub-block sums exact, fp32 outputs
+                                  within tolerance */
+
+/* Creates a MoE engine on `device` with scratch for up to max_tokens rows per
+ * call.  All device memory the hot path touches is allocated here; forward
+ * calls allocate nothing. */
+RV_API int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_tokens, rv_moe **out);
+RV_API void rv_moe_destroy(rv_moe *m);
+
+/* The MoE block of one layer for n_tokens rows, in place on `residual`:
+ * residual += sum_k w_k * expert_k(quantize(rmsnorm(residual))).
+ * Replaces the inline MoE blocks of model::forward_token_traced
+ * (model/forward.rs:2654-2754) and model::prefill::run_chunk
+ * (model/prefill.rs:2136-2263, 2749-2778): same RMSNorm, router, top-k,
+ * renormalization, Q8_K activations, expert FFN and fixed top-k-order
+ * reduction.  Device pointers: ffn_norm [hidden], router [n_experts][hidden],
+ * residual [n_tokens][hidden]; topk_ids/topk_weights [n_tokens][top_k] are
+ * optional outputs (NULL to skip).  Experts come from `table`'s `layer`. */
+RV_API int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t layer,
+                   const float *ffn_norm, const float *router, float *residual, size_t n_tokens,
+                   uint32_t *topk_ids, float *topk_weights, uint32_t flags, rv_stream stream);
+
+/* rv_moe_forward with a HOST residual (and optional host top-k outputs):
+ * copies in, runs, copies out and synchronizes `stream`.  This is the call
+ * a Rust caller holding `&mut [f32]` makes. */
+RV_API int rv_moe_forward_host(rv_moe *m, const rv_expert_table *table, uint32_t layer,
+                        const float *ffn_norm, const float *router, float *residual_host,
+                        size_t n_tokens, uint32_t *topk_ids_host, float *topk_weights_host,
+                        uint32_t flags, rv_stream stream);
+
+/* Device addresses of the intermediates the most recent forward left in the
+ * engine's scratch, for parity tests.  Layout per field below. */
+typedef struct rv_moe_taps {
+  const float *normed;          /* [n_tokens][hidden] ffn RMSNorm output */
+  const rv_block_q8k *acts;     /* Q8_K of normed, acts_stride bytes per token */
+  size_t acts_stride;           /* bytes between tokens' Q8_K rows */
+  const float *logits;          /* [n_tokens][n_experts] router logits */
+  const float *weights;         /* [n_tokens][top_k] renormalized weights */
+  const uint32_t *ids;          /* [n_tokens][top_k] expert ids */
+  const uint32_t *index;        /* [n_tokens*top_k] pair ids (t*top_k+k) by expert */
+  const uint32_t *index_start;  /* [n_experts+1] CSR offsets into index */
+  const float *swiglu;          /* [n_tokens*top_k][moe] SwiGLU output, CSR order */
+  const uint8_t *acts_moe;      /* CSR order, acts_moe_stride bytes per pair */
+  size_t acts_moe_stride;       /* bytes between pairs' Q8_K rows */
+  const float *staged;          /* [n_tokens][top_k][hidden] expert outputs */
+} rv_moe_taps;
+RV_API int rv_moe_get_taps(const rv_moe *m, rv_moe_taps *out);
+
+/* Per-stage timing, the GPU analogue of the reference's PhaseClock
+ * (model/prefill.rs:414-520): rv_moe_profile_enable(m, slots) creates
+ * `slots` sets of five CUDA events (0 releases them).  Each following
+ * rv_moe_forward -- also one being captured into a CUDA graph, which then
+ * records into the same set on every replay -- takes the next unused set and
+ * records an event before routing, before the gate/up kernel, before the
+ * down kernel, before the combine and after it.  rv_moe_profile_rewind makes
+ * the next forward take set 0 again.  rv_moe_profile_read synchronizes the
+ * used sets and writes four floats per set (routing, gate_up, down, combine
+ * milliseconds) to ms_out (host, capacity cap floats); *n_sets gets the
+ * number of sets used. */
+RV_API int rv_moe_profile_enable(rv_moe *m, size_t slots);
+RV_API int rv_moe_profile_rewind(rv_moe *m);
+RV_API int rv_moe_profile_read(rv_moe *m, float *ms_out, size_t cap, size_t *n_sets);
+
+/* ------------------------------------------------ synthetic inputs */
+/* Seeded N(0, sigma^2)-like values: element i is the Irwin-Hall sum of
+ * twelve 24-bit uniforms drawn from SplitMix64(seed, offset + i), so the
+ * same (seed, offset) gives the same floats on every device and host.
+ * out: device. */
+RV_API int rv_synth_normal(uint64_t seed, uint64_t offset, float sigma, float *out, size_t n,
+                    rv_stream stream);
+/* The reference's weight quantizers on the GPU
+ * (kernels/quants/test_support.rs:106-219), byte-identical to them:
+ * n floats (device) -> n/256 blocks of `format` (device). */
+RV_API int rv_quantize_weights(int format, const float *x, size_t n, uint8_t *out, rv_stream stream);
+/* Fills every expert blob of `layer` with seeded N(0, sigma^2) weights
+ * quantized by rv_quantize_weights (gate, up, down at their offsets). */
+RV_API int rv_expert_table_fill_synthetic(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
+                                   rv_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RAMVAMP_B200_H */

@@ -1,0 +1,379 @@
+// rv_kernels.cuh -- stand-alone kernels behind the rv_ kernel-level entry
+// points: Q8_K quantization, the lane-exact k-quant GEMV (rows / batched),
+// RMSNorm, softmax, SwiGLU, integer taps, and the synthetic-weight
+// generator with the GPU restatement of the reference's weight quantizers.
+#pragma once
+#include "rv_expf.cuh"
+#include "rv_internal.cuh"
+
+// ------------------------------------------------------------ Q8_K
+// One warp per 256-float block; x may have any 4-byte alignment.
+__global__ void k_quantize_q8k(const float *__restrict__ x, uint8_t *__restrict__ out,
+                               size_t n_blocks) {
+  const int lane = threadIdx.x & 31;
+  const size_t b = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= n_blocks) return;  // warp-uniform
+  float v[8];
+  const float *src = x + b * 256 + 8 * lane;
+#pragma unroll
+  for (int e = 0; e < 8; e++) v[e] = src[e];
+  q8k_quantize_warp(v, lane, out + b * 292);
+}
+
+// ------------------------------------------------------------ GEMV
+// out[(r - r0) * n_acts + a] = row(r) . act_a for r in [r0, r0 + nrows).
+// Block = R rows x 8 lanes.  The weight tile is staged once into shared
+// memory (bulk copy when 16-byte aligned, else a cooperative byte copy);
+// activations are staged MT rows at a time.
+struct GemvArgs {
+  const uint8_t *w;   // whole matrix
+  size_t row_bytes;
+  int nb;             // blocks per row
+  size_t r0, nrows;   // rows to compute
+  const uint8_t *acts;  // packed Q8_K rows, nb*292 bytes each
+  size_t n_acts;
+  float *out;
+  int R;              // rows per CTA
+};
+
+template <int FMT, int MT>
+__global__ void __launch_bounds__(256) k_gemv(GemvArgs g) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint64_t *bar = (uint64_t *)sm;
+  const int R = g.R;
+  const size_t act_row = (size_t)g.nb * 292;
+  uint8_t *wsm = sm + 16;
+  uint8_t *asm_ = wsm + ((R * g.row_bytes + 15) & ~(size_t)15) + 16;
+  const size_t tile0 = (size_t)blockIdx.x * R;
+  const int rows_here = (int)min((size_t)R, g.nrows - tile0);
+  const uint8_t *wsrc = g.w + (g.r0 + tile0) * g.row_bytes;
+  const size_t wbytes = (size_t)rows_here * g.row_bytes;
+  const bool bulk = rv_bulk_ok(wsrc, wsm, wbytes);
+  if (threadIdx.x == 0) mbar_init(bar, 1);
+  __syncthreads();
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(bar, (uint32_t)wbytes);
+      bulk_g2s(wsm, wsrc, (uint32_t)wbytes, bar);
+    }
+  } else {
+    rv_copy_bytes_block(wsm, wsrc, wbytes);
+  }
+  const int r = threadIdx.x >> 3, lane = threadIdx.x & 7;
+  const int rr = r < rows_here ? r : 0;  // idle rows compute row 0, never store
+  const uint8_t *wrow = wsm + (size_t)rr * g.row_bytes;
+  constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
+  bool ok = true;
+  for (size_t a0 = 0; a0 < g.n_acts; a0 += MT) {
+    const int mt = (int)min((size_t)MT, g.n_acts - a0);
+    __syncthreads();  // previous chunk fully consumed
+    {
+      const uint32_t *src = (const uint32_t *)(g.acts + a0 * act_row);
+      uint32_t *dst = (uint32_t *)asm_;
+      const size_t words = (size_t)mt * act_row / 4;
+      for (size_t k = threadIdx.x; k < words; k += blockDim.x) dst[k] = src[k];
+    }
+    if (a0 == 0 && bulk) ok = mbar_wait_bounded(bar, 0);
+    __syncthreads();
+    if (!ok) return;
+    float acc[MT], accm[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) acc[m] = accm[m] = 0.0f;
+    for (int b = 0; b < g.nb; b++) {
+      WBlock w;
+      load_wblock<FMT>(wrow + (size_t)b * BB, lane, w);
+#pragma unroll
+      for (int m = 0; m < MT; m++)
+        if (m < mt) lane_step<FMT>(w, asm_ + m * act_row + (size_t)b * 292, lane, acc[m], accm[m]);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      const float res = lane_reduce<FMT>(acc[m], accm[m]);
+      if (lane == 0 && r < rows_here && m < mt)
+        g.out[(tile0 + r) * g.n_acts + a0 + m] = res;
+    }
+  }
+}
+
+// ------------------------------------------------------- integer taps
+// One warp per block: lanes 0..7 write the eight lane sums, 0..3 the mins.
+template <int FMT>
+__global__ void k_block_sums(const uint8_t *w, const uint8_t *acts, int nb, int32_t *lanes_out,
+                             int32_t *mins_out) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
+  const int b = blockIdx.x;
+  if (b >= nb) return;
+  for (int k = threadIdx.x; k < BB; k += blockDim.x) sm[k] = w[(size_t)b * BB + k];
+  uint32_t *as = (uint32_t *)(sm + 256);
+  const uint32_t *src = (const uint32_t *)(acts + (size_t)b * 292);
+  for (int k = threadIdx.x; k < 73; k += blockDim.x) as[k] = src[k];
+  __syncthreads();
+  const int lane = threadIdx.x;
+  if (lane < 8) {
+    WBlock wb;
+    load_wblock<FMT>(sm, lane, wb);
+    int S, Mn;
+    lane_sums<FMT>(wb, (const uint8_t *)as, lane, S, Mn);
+    lanes_out[b * 8 + lane] = S;
+    if (lane < 4) mins_out[b * 4 + lane] = FMT == RV_Q6_K ? 0 : Mn;
+  }
+}
+
+// ------------------------------------------------------------ RMSNorm
+// One CTA of 256 threads per row; n <= 256 * RV_NORM_MAXE.
+#define RV_NORM_MAXE 16
+
+// inv = (float)(1/sqrt(sum/n + eps)) with every double step correctly
+// rounded, as norm.rs:51-60 computes it.
+RV_DEVFN float rms_inv_from_sum(double sum, size_t n, float eps) {
+  const double mean = __ddiv_rn(sum, (double)n);
+  return __double2float_rn(__drcp_rn(__dsqrt_rn(__dadd_rn(mean, (double)eps))));
+}
+
+// The reference sums v*v serially in f64 (norm.rs:38-60).  The tree sum
+// used here differs from it by at most 2^-41 relative; when the resulting
+// inverse RMS lies that close to a float rounding midpoint, thread 0 redoes
+// the sum serially, so the float result is always the reference's.
+RV_DEVFN float rms_inv_block(const float *xs /*smem*/, size_t n, float eps, double *red /*smem[33]*/) {
+  double part = 0.0;
+  for (size_t k = threadIdx.x; k < n; k += blockDim.x) {
+    const double v = (double)xs[k];
+    part = __dadd_rn(part, __dmul_rn(v, v));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = part;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) s = __dadd_rn(s, red[w]);
+    const double mean = __ddiv_rn(s, (double)n);
+    const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(mean, (double)eps)));
+    const float f = __double2float_rn(r);
+    const double df = (double)f;
+    const double up = (double)nextafterf(f, INFINITY), dn = (double)nextafterf(f, -INFINITY);
+    const double mh = 0.5 * (df + up), ml = 0.5 * (df + dn);
+    const double tol = fabs(r) * 0x1p-38;
+    float inv = f;
+    if (fabs(mh - r) <= tol || fabs(r - ml) <= tol || !isfinite(r)) {
+      double ser = 0.0;
+      for (size_t k = 0; k < n; k++) {
+        const double v = (double)xs[k];
+        ser = __dadd_rn(ser, __dmul_rn(v, v));
+      }
+      inv = rms_inv_from_sum(ser, n, eps);
+    }
+    red[32] = (double)inv;
+  }
+  __syncthreads();
+  return (float)red[32];
+}
+
+__global__ void __launch_bounds__(256) k_rmsnorm(const float *x, const float *w, size_t n, float eps,
+                                                 float *out) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  double *red = (double *)sm;
+  float *xs = (float *)(sm + 34 * sizeof(double));
+  const size_t row = blockIdx.x;
+  for (size_t k = threadIdx.x; k < n; k += blockDim.x) xs[k] = x[row * n + k];
+  __syncthreads();
+  const float inv = rms_inv_block(xs, n, eps, red);
+  for (size_t k = threadIdx.x; k < n; k += blockDim.x)
+    out[row * n + k] = __fmul_rn(__fmul_rn(xs[k], inv), w[k]);
+}
+
+// ------------------------------------------------------------ softmax
+// One warp per row (softmax.rs:18-40): f32 max, f64 exp of (x - max), f32
+// copy of each exponential, serial f64 sum in index order, f32 reciprocal.
+__global__ void k_softmax(float *x, size_t n, size_t n_rows) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  double *e = (double *)sm + (size_t)warp * n;
+  if (row >= n_rows) return;
+  float *xr = x + row * n;
+  float mx = -INFINITY;
+  for (size_t k = lane; k < n; k += 32) mx = fmaxf(mx, xr[k]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(RV_FULL, mx, o));
+  const double dmx = (double)mx;
+  for (size_t k = lane; k < n; k += 32) e[k] = exp(__dsub_rn((double)xr[k], dmx));
+  __syncwarp();
+  double sum = 0.0;
+  if (lane == 0)
+    for (size_t k = 0; k < n; k++) sum = __dadd_rn(sum, e[k]);
+  sum = __shfl_sync(RV_FULL, sum, 0);
+  const float inv = __double2float_rn(__drcp_rn(sum));
+  for (size_t k = lane; k < n; k += 32) xr[k] = __fmul_rn(__double2float_rn(e[k]), inv);
+}
+
+// ------------------------------------------------------------ SwiGLU
+__global__ void k_swiglu(float *gate, const float *up, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) gate[i] = swiglu_ref(gate[i], up[i]);
+}
+
+// --------------------------------------------------- synthetic weights
+// SplitMix64 output function (Steele, Lea, Flood 2014).
+RV_DEVFN uint64_t splitmix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Irwin-Hall(12): sum of twelve 24-bit uniforms, centred, scaled.  Exact
+// integer arithmetic up to one float rounding and one multiply by sigma,
+// so hosts and devices agree bit for bit.
+__global__ void k_synth_normal(uint64_t seed, uint64_t offset, float sigma, float *out, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t j = offset + i;
+  int64_t s = 0;
+#pragma unroll
+  for (int k = 0; k < 6; k++) {
+    const uint64_t z = splitmix64(seed + (j * 6 + (uint64_t)k + 1) * 0x9E3779B97F4A7C15ull);
+    s += (int64_t)(z >> 40) + (int64_t)((z >> 16) & 0xFFFFFFull);
+  }
+  s -= (int64_t)6 << 24;
+  const float v = __fmul_rn((float)s, 0x1p-24f);
+  out[i] = __fmul_rn(v, sigma);
+}
+
+// ----------------------------------------- the reference's weight quantizers
+// kernels/quants/test_support.rs:59-219, one thread per 256-weight block,
+// every float step with the reference's rounding (IEEE division, roundf =
+// half away from zero, ceil, f16 round-to-nearest-even).
+RV_DEVFN float f16_round(float v) { return __half2float(__float2half_rn(v)); }
+RV_DEVFN uint8_t clamp_u8(float v, float lo, float hi) {
+  if (v < lo) v = lo;
+  else if (v > hi) v = hi;
+  if (v != v) return 0;
+  return (uint8_t)v;
+}
+RV_DEVFN void put_f16(uint8_t *p, float v) {
+  const uint16_t h = __half_as_ushort(__float2half_rn(v));
+  p[0] = (uint8_t)(h & 255);
+  p[1] = (uint8_t)(h >> 8);
+}
+
+template <int LEVELS>
+RV_DEVFN void affine_scales_dev(const float *xs, uint8_t *scales, float &d, float &dmin,
+                                float *step, float *minv) {
+  float scale_f[8], min_f[8];
+  for (int j = 0; j < 8; j++) {
+    float vmin = INFINITY, vmax = -INFINITY;
+    for (int l = 0; l < 32; l++) {
+      const float v = xs[32 * j + l];
+      vmin = fminf(vmin, v);
+      vmax = fmaxf(vmax, v);
+    }
+    min_f[j] = fmaxf(-vmin, 0.0f);
+    scale_f[j] = fmaxf(__fdiv_rn(__fadd_rn(vmax, min_f[j]), (float)LEVELS), 0.0f);
+  }
+  float max_scale = 0.0f, max_min = 0.0f;
+  for (int j = 0; j < 8; j++) {
+    max_scale = fmaxf(max_scale, scale_f[j]);
+    max_min = fmaxf(max_min, min_f[j]);
+  }
+  d = f16_round(__fdiv_rn(max_scale, 63.0f));
+  dmin = f16_round(__fdiv_rn(max_min, 63.0f));
+  uint8_t ls[8], lm[8];
+  for (int j = 0; j < 8; j++) {
+    ls[j] = d > 0.0f ? clamp_u8(ceilf(__fdiv_rn(scale_f[j], d)), 0.0f, 63.0f) : 0;
+    lm[j] = dmin > 0.0f ? clamp_u8(roundf(__fdiv_rn(min_f[j], dmin)), 0.0f, 63.0f) : 0;
+    step[j] = __fmul_rn(d, (float)ls[j]);
+    minv[j] = __fmul_rn(dmin, (float)lm[j]);
+  }
+  for (int k = 0; k < 12; k++) scales[k] = 0;
+  for (int j = 0; j < 8; j++) {  // pack_scales_k4, test_support.rs:45-58
+    if (j < 4) {
+      scales[j] = ls[j] & 63;
+      scales[j + 4] = lm[j] & 63;
+    } else {
+      scales[j + 4] = (uint8_t)((ls[j] & 0xF) | ((lm[j] & 0xF) << 4));
+      scales[j - 4] |= (uint8_t)((ls[j] >> 4) << 6);
+      scales[j] |= (uint8_t)((lm[j] >> 4) << 6);
+    }
+  }
+}
+
+RV_DEVFN uint8_t affine_q_dev(float v, float step, float min, float levels) {
+  if (step <= 0.0f) return 0;
+  return clamp_u8(roundf(__fdiv_rn(__fadd_rn(v, min), step)), 0.0f, levels);
+}
+
+template <int FMT>
+__global__ void k_quantize_weights(const float *__restrict__ x, uint8_t *__restrict__ out,
+                                   size_t n_blocks) {
+  const size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= n_blocks) return;
+  const float *xs = x + b * 256;
+  if constexpr (FMT == RV_Q4_K || FMT == RV_Q5_K) {
+    constexpr int L = FMT == RV_Q4_K ? 15 : 31;
+    constexpr int BB = FMT == RV_Q4_K ? 144 : 176;
+    uint8_t *o = out + b * BB;
+    uint8_t scales[12];
+    float d, dmin, step[8], minv[8];
+    affine_scales_dev<L>(xs, scales, d, dmin, step, minv);
+    put_f16(o, d);
+    put_f16(o + 2, dmin);
+    for (int k = 0; k < 12; k++) o[4 + k] = scales[k];
+    if constexpr (FMT == RV_Q4_K) {
+      for (int span = 0; span < 4; span++)
+        for (int l = 0; l < 32; l++) {
+          const int j0 = 2 * span, j1 = 2 * span + 1;
+          const uint8_t q0 = affine_q_dev(xs[64 * span + l], step[j0], minv[j0], 15.0f);
+          const uint8_t q1 = affine_q_dev(xs[64 * span + 32 + l], step[j1], minv[j1], 15.0f);
+          o[16 + 32 * span + l] = (uint8_t)(q0 | (q1 << 4));
+        }
+    } else {
+      uint8_t qh[32];
+      for (int l = 0; l < 32; l++) qh[l] = 0;
+      for (int span = 0; span < 4; span++)
+        for (int l = 0; l < 32; l++) {
+          const int j0 = 2 * span, j1 = 2 * span + 1;
+          const uint8_t q0 = affine_q_dev(xs[64 * span + l], step[j0], minv[j0], 31.0f);
+          const uint8_t q1 = affine_q_dev(xs[64 * span + 32 + l], step[j1], minv[j1], 31.0f);
+          if (q0 >= 16) qh[l] |= (uint8_t)(1u << j0);
+          if (q1 >= 16) qh[l] |= (uint8_t)(1u << j1);
+          o[48 + 32 * span + l] = (uint8_t)((q0 & 0xF) | ((q1 & 0xF) << 4));
+        }
+      for (int l = 0; l < 32; l++) o[16 + l] = qh[l];
+    }
+  } else {
+    uint8_t *o = out + b * 210;
+    float scale_f[16];
+    float max_scale = 0.0f;
+    for (int g = 0; g < 16; g++) {
+      float amax = 0.0f;
+      for (int l = 0; l < 16; l++) amax = fmaxf(amax, fabsf(xs[16 * g + l]));
+      scale_f[g] = __fdiv_rn(amax, 31.0f);
+      max_scale = fmaxf(max_scale, scale_f[g]);
+    }
+    const float d = f16_round(__fdiv_rn(max_scale, 127.0f));
+    uint8_t ls[16];
+    for (int g = 0; g < 16; g++) ls[g] = d > 0.0f ? clamp_u8(ceilf(__fdiv_rn(scale_f[g], d)), 0.0f, 127.0f) : 0;
+    for (int k = 0; k < 192; k++) o[k] = 0;
+    for (int g = 0; g < 16; g++) {
+      const float step = __fmul_rn(d, (float)ls[g]);
+      for (int l = 0; l < 16; l++) {
+        int v = 0;
+        if (step > 0.0f) {
+          float q = roundf(__fdiv_rn(xs[16 * g + l], step));
+          q = q < -32.0f ? -32.0f : (q > 31.0f ? 31.0f : q);
+          v = (int)q;
+        }
+        const uint8_t qq = (uint8_t)(v + 32);
+        const int w = 16 * g + l, half = w >> 7, p = w & 127, quarter = p >> 5, l32 = p & 31;
+        // inverse of the ql/qh packing in test_support.rs:197-210
+        uint8_t *ql = o + 64 * half + (quarter & 1) * 32 + l32;
+        *ql |= (uint8_t)((qq & 0xF) << (quarter >= 2 ? 4 : 0));
+        o[128 + 32 * half + l32] |= (uint8_t)((qq >> 4) << (2 * quarter));
+      }
+    }
+    for (int g = 0; g < 16; g++) o[192 + g] = ls[g];
+    put_f16(o + 208, d);
+  }
+}

@@ -1,0 +1,890 @@
+// rv_lib.cu -- host side of libramvamp_b200.so: the C ABI declared in
+// include/ramvamp_b200.h.  One translation unit (the kernels come in as
+// headers) so every device global lives in one module.
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "rv_expf.cuh"
+#include "rv_internal.cuh"
+#include "rv_kernels.cuh"
+#include "rv_moe.cuh"
+
+#include "_gen/expf_exceptions.inc"
+
+#define RV_VERSION_STRING "ramvamp_b200 0.1 (sm_100a)"
+
+// ================================================================ errors
+static thread_local char t_err[1024];
+static thread_local size_t t_err_len;
+
+void rv_set_error(int status, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  int n = snprintf(t_err, sizeof t_err, "%s: ", rv_status_name(status));
+  if (n < 0) n = 0;
+  int m = vsnprintf(t_err + n, sizeof t_err - (size_t)n, fmt, ap);
+  va_end(ap);
+  t_err_len = (size_t)n + (m > 0 ? (size_t)m : 0);
+}
+
+extern "C" const char *rv_version(void) { return RV_VERSION_STRING; }
+
+extern "C" const char *rv_status_name(int s) {
+  switch (s) {
+    case RV_OK: return "Ok";
+    case RV_ERR_INDIVISIBLE_ROW: return "IndivisibleRow";
+    case RV_ERR_ROW_BYTES_NOT_BLOCK_MULTIPLE: return "RowBytesNotBlockMultiple";
+    case RV_ERR_BLOCK_COUNT_MISMATCH: return "BlockCountMismatch";
+    case RV_ERR_QUANTIZE_LEN_MISMATCH: return "QuantizeLenMismatch";
+    case RV_ERR_LENGTH_MISMATCH: return "LengthMismatch";
+    case RV_ERR_EMPTY: return "Empty";
+    case RV_ERR_INVALID_HEAD_DIM: return "InvalidHeadDim";
+    case RV_ERR_UNIMPLEMENTED: return "Unimplemented";
+    case RV_ERR_UNSUPPORTED_FORMAT: return "UnsupportedFormat";
+    case RV_ERR_ROUTED_OUT_OF_RANGE: return "RoutedExpertOutOfRange";
+    case RV_ERR_LAYER_OUT_OF_RANGE: return "LayerOutOfRange";
+    case RV_ERR_PROTOCOL: return "Protocol";
+    case RV_ERR_INVALID_ARGUMENT: return "InvalidArgument";
+    case RV_ERR_CUDA: return "Cuda";
+    case RV_ERR_NCCL: return "Nccl";
+    case RV_ERR_TIMEOUT: return "Timeout";
+  }
+  return "Unknown";
+}
+
+extern "C" size_t rv_last_error(char *buf, size_t len) {
+  if (buf && len) {
+    size_t k = t_err_len < len - 1 ? t_err_len : len - 1;
+    memcpy(buf, t_err, k);
+    buf[k] = 0;
+  }
+  return t_err_len;
+}
+
+extern "C" size_t rv_block_bytes(int f) { return (size_t)rv_fmt_block_bytes(f); }
+extern "C" size_t rv_block_weights(int f) {
+  return f == RV_Q8_0 ? 32 : (f >= RV_Q4_K && f <= RV_Q8_K ? 256 : 0);
+}
+
+extern "C" int rv_row_bytes(int f, size_t in_dim, size_t *out) {
+  const size_t bw = rv_block_weights(f);
+  if (bw == 0) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "unknown format %d", f);
+  if (in_dim % bw != 0)
+    RV_FAIL(RV_ERR_INDIVISIBLE_ROW, "format %d row of %zu weights: not a multiple of the %zu-weight block",
+            f, in_dim, bw);
+  if (out) *out = in_dim / bw * (size_t)rv_fmt_block_bytes(f);
+  return RV_OK;
+}
+
+// Saturating multiply, as gemv.rs:207-211 validates with saturating_mul.
+static size_t sat_mul(size_t a, size_t b) {
+  if (a == 0 || b == 0) return 0;
+  return a > SIZE_MAX / b ? SIZE_MAX : a * b;
+}
+
+// ===================================================== per-device set-up
+// The SiLU exception table goes to each device once, before the first
+// kernel that uses it; rv_moe_create does it, so forward calls never do.
+static std::mutex g_init_mu;
+static bool g_dev_ready[64];
+
+static int ensure_device(int dev) {
+  if (dev < 0 || dev >= 64) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (g_dev_ready[dev]) return RV_OK;
+  std::vector<uint2> table(RV_EXPF_TABLE_SIZE, make_uint2(RV_EXPF_EMPTY, 0u));
+  int max_probe = 0;
+  for (unsigned i = 0; i < kExpfExceptionCount; i++) {
+    const uint32_t key = kExpfExceptions[i][0];
+    if (key == RV_EXPF_EMPTY) continue;
+    uint32_t h = rv_expf_hash(key);
+    int p = 0;
+    while (table[(h + p) & (RV_EXPF_TABLE_SIZE - 1)].x != RV_EXPF_EMPTY) p++;
+    table[(h + p) & (RV_EXPF_TABLE_SIZE - 1)] = make_uint2(key, kExpfExceptions[i][1]);
+    if (p > max_probe) max_probe = p;
+  }
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(dev));
+  cudaError_t e1 = cudaMemcpyToSymbol(g_expf_table, table.data(), table.size() * sizeof(uint2));
+  cudaError_t e2 = cudaMemcpyToSymbol(g_expf_max_probe, &max_probe, sizeof(int));
+  // Kernels whose shared memory exceeds the 48 KB default.
+  const int big = 200 * 1024;
+  cudaFuncSetAttribute(k_gemv<RV_Q4_K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv<RV_Q4_K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv<RV_Q5_K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv<RV_Q5_K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv<RV_Q6_K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv<RV_Q6_K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gate_up<RV_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gate_up<RV_Q5_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gate_up<RV_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_down<RV_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_down<RV_Q5_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_down<RV_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_prologue, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaError_t e3 = cudaGetLastError();
+  cudaSetDevice(prev);
+  if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
+    RV_FAIL(RV_ERR_CUDA, "device %d set-up failed: %s", dev,
+            cudaGetErrorString(e1 != cudaSuccess ? e1 : e2 != cudaSuccess ? e2 : e3));
+  g_dev_ready[dev] = true;
+  return RV_OK;
+}
+
+static int ensure_current_device() {
+  int dev = 0;
+  RV_CUDA(cudaGetDevice(&dev));
+  return ensure_device(dev);
+}
+
+extern "C" int rv_device_status(int device, rv_stream stream) {
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(device));
+  int v = 0, zero = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_rv_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_rv_dev_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) RV_FAIL(RV_ERR_CUDA, "rv_device_status: %s", cudaGetErrorString(e));
+  if (v != 0) RV_FAIL(v, "a device-side check failed on device %d", device);
+  return RV_OK;
+}
+
+// =============================================================== kernels
+extern "C" int rv_quantize_row_q8_k(const float *x, size_t n, rv_block_q8k *out, size_t out_blocks,
+                                    rv_stream stream) {
+  if (n != sat_mul(out_blocks, 256))
+    RV_FAIL(RV_ERR_QUANTIZE_LEN_MISMATCH, "Q8_K quantize: %zu input floats do not fill %zu output blocks exactly",
+            n, out_blocks);
+  if (out_blocks == 0) return RV_OK;
+  if (!x || !out || ((uintptr_t)x & 3) || ((uintptr_t)out & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "quantize_row_q8_k: null or misaligned pointer");
+  const size_t grid = (out_blocks + 7) / 8;
+  k_quantize_q8k<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(x, (uint8_t *)out, out_blocks);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+// gemv.rs:212-264 (validate): same checks, same precedence.
+static int validate_gemv(const char *what, int format, size_t weight_len, size_t in_dim,
+                         size_t out_dim, size_t acts_len, size_t n_acts, size_t r0, size_t r1,
+                         size_t out_len, size_t *row_bytes) {
+  if (!rv_fmt_is_kquant(format))
+    RV_FAIL(RV_ERR_UNSUPPORTED_FORMAT, "%s: unsupported weight format %d", what, format);
+  int rc = rv_row_bytes(format, in_dim, row_bytes);
+  if (rc) return rc;
+  if (sat_mul(*row_bytes, out_dim) != weight_len)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "%s: weight bytes vs rows (%zu vs %zu)", what, weight_len,
+            sat_mul(*row_bytes, out_dim));
+  if (r0 > r1) RV_FAIL(RV_ERR_LENGTH_MISMATCH, "gemv rows: row range start vs end (%zu vs %zu)", r0, r1);
+  if (r1 > out_dim)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "gemv rows: row range end vs out_dim (%zu vs %zu)", r1, out_dim);
+  if (out_len != sat_mul(r1 - r0, n_acts))
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "%s: out vs range (%zu vs %zu)", what, out_len, sat_mul(r1 - r0, n_acts));
+  const size_t wb = sat_mul(in_dim / 256, n_acts);
+  if (wb != acts_len)
+    RV_FAIL(RV_ERR_BLOCK_COUNT_MISMATCH,
+            "dot length mismatch: weight row has %zu blocks, activations %zu", wb, acts_len);
+  return RV_OK;
+}
+
+template <int FMT>
+static void launch_gemv(const GemvArgs &g, cudaStream_t s) {
+  const size_t act_row = (size_t)g.nb * 292;
+  const int mt = g.n_acts > 1 ? 8 : 1;
+  const size_t smem = 16 + ((g.R * g.row_bytes + 15) & ~(size_t)15) + 16 + mt * act_row + 16;
+  const unsigned grid = (unsigned)((g.nrows + g.R - 1) / g.R);
+  if (mt == 1) k_gemv<FMT, 1><<<grid, g.R * 8, smem, s>>>(g);
+  else k_gemv<FMT, 8><<<grid, g.R * 8, smem, s>>>(g);
+}
+
+static int gemv_launch(int format, const uint8_t *weight, size_t row_bytes, size_t in_dim,
+                       const rv_block_q8k *acts, size_t n_acts, size_t r0, size_t r1, float *out,
+                       cudaStream_t s) {
+  if (n_acts == 0 || r1 == r0) return RV_OK;
+  if (!weight || !acts || !out || ((uintptr_t)acts & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "gemv: null pointer or activations not 4-byte aligned");
+  int rc = ensure_current_device();
+  if (rc) return rc;
+  GemvArgs g;
+  g.w = weight;
+  g.row_bytes = row_bytes;
+  g.nb = (int)(in_dim / 256);
+  g.r0 = r0;
+  g.nrows = r1 - r0;
+  g.acts = (const uint8_t *)acts;
+  g.n_acts = n_acts;
+  g.out = out;
+  g.R = row_bytes <= 2048 ? 32 : row_bytes <= 4096 ? 16 : 8;
+  const size_t act_row = (size_t)g.nb * 292;
+  if ((size_t)g.R * row_bytes + 8 * act_row > 180 * 1024)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "gemv: rows of %zu bytes exceed the staged-tile limit", row_bytes);
+  switch (format) {
+    case RV_Q4_K: launch_gemv<RV_Q4_K>(g, s); break;
+    case RV_Q5_K: launch_gemv<RV_Q5_K>(g, s); break;
+    default: launch_gemv<RV_Q6_K>(g, s); break;
+  }
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_gemv_q8_k(int format, const uint8_t *weight, size_t weight_len, size_t in_dim,
+                            size_t out_dim, const rv_block_q8k *acts, size_t acts_len, float *out,
+                            size_t out_len, rv_stream stream) {
+  size_t rb = 0;
+  int rc = validate_gemv("gemv_q8_k", format, weight_len, in_dim, out_dim, acts_len, 1, 0, out_dim,
+                         out_len, &rb);
+  if (rc) return rc;
+  return gemv_launch(format, weight, rb, in_dim, acts, 1, 0, out_dim, out, (cudaStream_t)stream);
+}
+
+extern "C" int rv_gemv_q8_k_rows(int format, const uint8_t *weight, size_t weight_len, size_t in_dim,
+                                 size_t out_dim, const rv_block_q8k *acts, size_t acts_len,
+                                 size_t row_start, size_t row_end, float *out, size_t out_len,
+                                 rv_stream stream) {
+  size_t rb = 0;
+  int rc = validate_gemv("gemv_q8_k_rows", format, weight_len, in_dim, out_dim, acts_len, 1,
+                         row_start, row_end, out_len, &rb);
+  if (rc) return rc;
+  return gemv_launch(format, weight, rb, in_dim, acts, 1, row_start, row_end, out, (cudaStream_t)stream);
+}
+
+extern "C" int rv_gemv_q8_k_batched(int format, const uint8_t *weight, size_t weight_len,
+                                    size_t in_dim, size_t out_dim, const rv_block_q8k *acts,
+                                    size_t acts_len, size_t n_acts, size_t row_start,
+                                    size_t row_end, float *out, size_t out_len, rv_stream stream) {
+  size_t rb = 0;
+  int rc = validate_gemv("gemv_q8_k_batched", format, weight_len, in_dim, out_dim, acts_len, n_acts,
+                         row_start, row_end, out_len, &rb);
+  if (rc) return rc;
+  return gemv_launch(format, weight, rb, in_dim, acts, n_acts, row_start, row_end, out,
+                     (cudaStream_t)stream);
+}
+
+// gemv.rs:747-823: rows of the concatenated row spaces, part by part.
+extern "C" int rv_gemv_q8_k_fused_rows(const rv_fused_part *parts, size_t n_parts, size_t row_start,
+                                       size_t row_end, float *out, size_t out_len,
+                                       rv_stream stream) {
+  if (n_parts && !parts) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "fused_rows: null parts");
+  size_t total = 0;
+  for (size_t p = 0; p < n_parts; p++) total = total > SIZE_MAX - parts[p].out_dim ? SIZE_MAX : total + parts[p].out_dim;
+  if (row_start > row_end)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "gemv rows: row range start vs end (%zu vs %zu)", row_start, row_end);
+  if (row_end > total)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "gemv rows: row range end vs out_dim (%zu vs %zu)", row_end, total);
+  if (out_len != row_end - row_start)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "gemv_q8_k_fused_rows: out vs range (%zu vs %zu)", out_len,
+            row_end - row_start);
+  // Validate every touched part first, then launch (fused_row_parts, gemv.rs:713-728).
+  struct Job { size_t p, lo, hi, rb, at; };
+  std::vector<Job> jobs;
+  size_t base = 0, at = 0;
+  for (size_t p = 0; p < n_parts; p++) {
+    const size_t end = base > SIZE_MAX - parts[p].out_dim ? SIZE_MAX : base + parts[p].out_dim;
+    const size_t lo = row_start < base ? base : (row_start > end ? end : row_start);
+    const size_t hi = row_end < base ? base : (row_end > end ? end : row_end);
+    if (lo < hi) {
+      size_t rb = 0;
+      int rc = validate_gemv("gemv_q8_k_fused_rows: part weight bytes vs rows / out vs range",
+                             parts[p].format, parts[p].weight_len, parts[p].in_dim, parts[p].out_dim,
+                             parts[p].acts_len, 1, lo - base, hi - base, hi - lo, &rb);
+      if (rc) return rc;
+      jobs.push_back({p, lo - base, hi - base, rb, at});
+      at += hi - lo;
+    }
+    base = end;
+  }
+  for (const Job &j : jobs) {
+    int rc = gemv_launch(parts[j.p].format, parts[j.p].weight, j.rb, parts[j.p].in_dim, parts[j.p].acts,
+                         1, j.lo, j.hi, out + j.at, (cudaStream_t)stream);
+    if (rc) return rc;
+  }
+  return RV_OK;
+}
+
+extern "C" int rv_rmsnorm(const float *x, const float *weight, size_t n, size_t n_rows, float eps,
+                          float *out, rv_stream stream) {
+  if (n == 0) RV_FAIL(RV_ERR_EMPTY, "rmsnorm: input is empty");
+  if (n > 16384) RV_FAIL(RV_ERR_UNIMPLEMENTED, "rmsnorm rows longer than 16384 are not implemented");
+  if (n_rows == 0) return RV_OK;
+  if (!x || !weight || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rmsnorm: null pointer");
+  int rc = ensure_current_device();
+  if (rc) return rc;
+  k_rmsnorm<<<(unsigned)n_rows, 256, 34 * sizeof(double) + n * sizeof(float), (cudaStream_t)stream>>>(
+      x, weight, n, eps, out);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_softmax(float *x, size_t n, size_t n_rows, rv_stream stream) {
+  if (n == 0) RV_FAIL(RV_ERR_EMPTY, "softmax: input is empty");
+  if (n > 1024) RV_FAIL(RV_ERR_UNIMPLEMENTED, "softmax rows longer than 1024 are not implemented");
+  if (n_rows == 0) return RV_OK;
+  if (!x) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "softmax: null pointer");
+  const unsigned grid = (unsigned)((n_rows + 3) / 4);
+  k_softmax<<<grid, 128, 4 * n * sizeof(double), (cudaStream_t)stream>>>(x, n, n_rows);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_swiglu_combine(float *gate, size_t gate_len, const float *up, size_t up_len,
+                                 rv_stream stream) {
+  if (gate_len != up_len)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "swiglu_combine: gate vs up (%zu vs %zu)", gate_len, up_len);
+  if (gate_len == 0) return RV_OK;
+  if (!gate || !up) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "swiglu_combine: null pointer");
+  int rc = ensure_current_device();
+  if (rc) return rc;
+  k_swiglu<<<(unsigned)((gate_len + 255) / 256), 256, 0, (cudaStream_t)stream>>>(gate, up, gate_len);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_debug_block_sums(int format, const uint8_t *w, size_t w_len, const rv_block_q8k *acts,
+                                   size_t n_blocks, int32_t *lanes_out, int32_t *mins_out,
+                                   rv_stream stream) {
+  if (!rv_fmt_is_kquant(format)) RV_FAIL(RV_ERR_UNSUPPORTED_FORMAT, "debug_block_sums: format %d", format);
+  const size_t bb = (size_t)rv_fmt_block_bytes(format);
+  if (w_len % bb) RV_FAIL(RV_ERR_ROW_BYTES_NOT_BLOCK_MULTIPLE, "row of %zu bytes", w_len);
+  if (w_len / bb != n_blocks)
+    RV_FAIL(RV_ERR_BLOCK_COUNT_MISMATCH, "weight row has %zu blocks, activations %zu", w_len / bb, n_blocks);
+  if (n_blocks == 0) return RV_OK;
+  if (!w || !acts || !lanes_out || !mins_out || ((uintptr_t)acts & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "debug_block_sums: bad pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned g = (unsigned)n_blocks;
+  const uint8_t *a = (const uint8_t *)acts;
+  if (format == RV_Q4_K) k_block_sums<RV_Q4_K><<<g, 32, 256 + 304, s>>>(w, a, (int)n_blocks, lanes_out, mins_out);
+  else if (format == RV_Q5_K) k_block_sums<RV_Q5_K><<<g, 32, 256 + 304, s>>>(w, a, (int)n_blocks, lanes_out, mins_out);
+  else k_block_sums<RV_Q6_K><<<g, 32, 256 + 304, s>>>(w, a, (int)n_blocks, lanes_out, mins_out);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+// ========================================================== expert table
+struct rv_expert_table {
+  int device;
+  std::vector<rv_layer_layout> layouts;
+  std::vector<uint8_t *> base;  // device, one allocation per layer
+  bool step_active = false;
+  uint32_t step_layer = 0;
+  std::vector<uint32_t> hit_index, hit_slot;
+  uint64_t accesses = 0, hits = 0;
+};
+
+static int check_layout(const rv_layer_layout &L, uint32_t i) {
+  const rv_layer_layout *p = &L;
+  if (!rv_fmt_is_kquant(p->gate_format) || !rv_fmt_is_kquant(p->up_format) || !rv_fmt_is_kquant(p->down_format))
+    RV_FAIL(RV_ERR_UNSUPPORTED_FORMAT, "layer %u: expert slabs must be Q4_K/Q5_K/Q6_K", i);
+  size_t rg, ru, rd;
+  int rc = rv_row_bytes(p->gate_format, p->hidden, &rg);
+  if (!rc) rc = rv_row_bytes(p->up_format, p->hidden, &ru);
+  if (!rc) rc = rv_row_bytes(p->down_format, p->moe, &rd);
+  if (rc) return rc;
+  if (p->gate_len != (uint64_t)rg * p->moe || p->up_len != (uint64_t)ru * p->moe ||
+      p->down_len != (uint64_t)rd * p->hidden)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "layer %u: slab lengths do not match [moe][hidden] / [hidden][moe]", i);
+  if (p->gate_off + p->gate_len > p->stride || p->up_off + p->up_len > p->stride ||
+      p->down_off + p->down_len > p->stride)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "layer %u: a slab runs past the blob stride", i);
+  if (p->n_experts == 0) RV_FAIL(RV_ERR_EMPTY, "layer %u: no experts", i);
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_create(int device, const rv_layer_layout *layers, uint32_t n_layers,
+                                      rv_expert_table **out) {
+  if (!out || (n_layers && !layers)) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "expert_table_create: null pointer");
+  *out = nullptr;
+  for (uint32_t i = 0; i < n_layers; i++) {
+    int rc = check_layout(layers[i], i);
+    if (rc) return rc;
+  }
+  int rc = ensure_device(device);
+  if (rc) return rc;
+  rv_expert_table *t = new (std::nothrow) rv_expert_table();
+  if (!t) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "out of host memory");
+  t->device = device;
+  t->layouts.assign(layers, layers + n_layers);
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  for (uint32_t i = 0; i < n_layers; i++) {
+    uint8_t *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, (size_t)layers[i].n_experts * layers[i].stride);
+    if (e != cudaSuccess) {
+      for (uint8_t *q : t->base) cudaFree(q);
+      delete t;
+      cudaSetDevice(prev);
+      RV_FAIL(RV_ERR_CUDA, "expert table layer %u (%zu bytes): %s", i,
+              (size_t)layers[i].n_experts * layers[i].stride, cudaGetErrorString(e));
+    }
+    t->base.push_back(p);
+  }
+  cudaSetDevice(prev);
+  *out = t;
+  return RV_OK;
+}
+
+extern "C" void rv_expert_table_destroy(rv_expert_table *t) {
+  if (!t) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(t->device);
+  for (uint8_t *p : t->base) cudaFree(p);
+  cudaSetDevice(prev);
+  delete t;
+}
+
+extern "C" uint32_t rv_expert_table_n_layers(const rv_expert_table *t) {
+  return t ? (uint32_t)t->layouts.size() : 0;
+}
+
+extern "C" int rv_expert_table_layout(const rv_expert_table *t, uint32_t layer, rv_layer_layout *out) {
+  if (!t || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
+  *out = t->layouts[layer];
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_upload(rv_expert_table *t, uint32_t layer, uint32_t expert_first,
+                                      uint32_t n_experts, const void *src, size_t len,
+                                      int src_on_device, rv_stream stream) {
+  if (!t || (!src && len)) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
+  const rv_layer_layout &L = t->layouts[layer];
+  if ((uint64_t)expert_first + n_experts > L.n_experts)
+    RV_FAIL(RV_ERR_ROUTED_OUT_OF_RANGE, "experts [%u, %u) of %u", expert_first, expert_first + n_experts, L.n_experts);
+  if (len != (size_t)n_experts * L.stride)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "upload: %zu bytes vs %zu expected", len, (size_t)n_experts * L.stride);
+  if (len == 0) return RV_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  RV_CUDA(cudaMemcpyAsync(t->base[layer] + (size_t)expert_first * L.stride, src, len,
+                          src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+  RV_CUDA(cudaStreamSynchronize(s));
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_begin_layer(rv_expert_table *t, uint32_t layer, const uint32_t *experts,
+                                           size_t n) {
+  if (!t || (n && !experts)) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
+  if (t->step_active)
+    RV_FAIL(RV_ERR_PROTOCOL, "layer %u: begin_layer called with a step already open; end_layer first", layer);
+  for (size_t i = 0; i < n; i++)
+    if (experts[i] >= t->layouts[layer].n_experts)
+      RV_FAIL(RV_ERR_ROUTED_OUT_OF_RANGE, "expert %u of %u", experts[i], t->layouts[layer].n_experts);
+  t->hit_index.clear();
+  t->hit_slot.clear();
+  for (size_t i = 0; i < n; i++) {
+    bool dup = false;
+    for (size_t j = 0; j < i; j++) dup |= experts[j] == experts[i];
+    if (dup) continue;  // a duplicate resolves once, at its first position
+    t->hit_index.push_back((uint32_t)i);
+    t->hit_slot.push_back(experts[i]);
+  }
+  t->accesses += t->hit_slot.size();
+  t->hits += t->hit_slot.size();
+  t->step_active = true;
+  t->step_layer = layer;
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_hits(const rv_expert_table *t, uint32_t *index_out, uint32_t *slot_out,
+                                    size_t cap, size_t *n_out) {
+  if (!t || !n_out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  const size_t n = t->step_active ? t->hit_slot.size() : 0;
+  *n_out = n;
+  for (size_t i = 0; i < n && i < cap; i++) {
+    if (index_out) index_out[i] = t->hit_index[i];
+    if (slot_out) slot_out[i] = t->hit_slot[i];
+  }
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_misses(const rv_expert_table *t, uint32_t *index_out, uint32_t *slot_out,
+                                      size_t cap, size_t *n_out) {
+  (void)index_out;
+  (void)slot_out;
+  (void)cap;
+  if (!t || !n_out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  *n_out = 0;
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_await_misses(rv_expert_table *t) {
+  if (!t) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_view(const rv_expert_table *t, uint32_t layer, uint32_t slot,
+                                    rv_expert_view *out) {
+  if (!t || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
+  const rv_layer_layout &L = t->layouts[layer];
+  if (slot >= L.n_experts) RV_FAIL(RV_ERR_PROTOCOL, "layer %u: slot %u is not in the pool", layer, slot);
+  const uint8_t *b = t->base[layer] + (size_t)slot * L.stride;
+  out->blob = b;
+  out->gate = b + L.gate_off;
+  out->up = b + L.up_off;
+  out->down = b + L.down_off;
+  out->gate_len = L.gate_len;
+  out->up_len = L.up_len;
+  out->down_len = L.down_len;
+  out->gate_format = L.gate_format;
+  out->up_format = L.up_format;
+  out->down_format = L.down_format;
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_end_layer(rv_expert_table *t, uint32_t layer) {
+  if (!t) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!t->step_active) RV_FAIL(RV_ERR_PROTOCOL, "layer %u: end_layer without an open step", layer);
+  t->step_active = false;
+  t->hit_index.clear();
+  t->hit_slot.clear();
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_stats(const rv_expert_table *t, uint64_t *accesses, uint64_t *hits) {
+  if (!t) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (accesses) *accesses = t->accesses;
+  if (hits) *hits = t->hits;
+  return RV_OK;
+}
+
+// ============================================================ MoE engine
+struct rv_moe {
+  int device;
+  rv_moe_config cfg;
+  size_t max_tokens;
+  MoeDims d;
+  MoeBufs B;  // T and residual/ffn_norm/router set per call
+  int max_units;
+  void *arena;
+  float *dres;  // [max_tokens][H] device residual of rv_moe_forward_host
+  int last_T = 0;
+  std::vector<cudaEvent_t> prof;  // 5 events per set
+  size_t prof_next = 0;
+};
+
+static void prof_release(rv_moe *m) {
+  for (cudaEvent_t e : m->prof) cudaEventDestroy(e);
+  m->prof.clear();
+  m->prof_next = 0;
+}
+
+extern "C" int rv_moe_profile_enable(rv_moe *m, size_t slots) {
+  if (!m) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null engine");
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(m->device));
+  prof_release(m);
+  for (size_t i = 0; i < 5 * slots; i++) {
+    cudaEvent_t e;
+    cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) {
+      prof_release(m);
+      cudaSetDevice(prev);
+      RV_FAIL(RV_ERR_CUDA, "profile events: %s", cudaGetErrorString(err));
+    }
+    m->prof.push_back(e);
+  }
+  cudaSetDevice(prev);
+  return RV_OK;
+}
+
+extern "C" int rv_moe_profile_rewind(rv_moe *m) {
+  if (!m) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null engine");
+  m->prof_next = 0;
+  return RV_OK;
+}
+
+extern "C" int rv_moe_profile_read(rv_moe *m, float *ms_out, size_t cap, size_t *n_sets) {
+  if (!m || !n_sets) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  const size_t used = m->prof_next;
+  *n_sets = used;
+  for (size_t i = 0; i < used; i++) {
+    cudaEvent_t *ev = &m->prof[5 * i];
+    RV_CUDA(cudaEventSynchronize(ev[4]));
+    for (int k = 0; k < 4; k++) {
+      float ms = 0.0f;
+      RV_CUDA(cudaEventElapsedTime(&ms, ev[k], ev[k + 1]));
+      if (ms_out && 4 * i + k < cap) ms_out[4 * i + k] = ms;
+    }
+  }
+  return RV_OK;
+}
+
+static size_t round16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_tokens, rv_moe **out) {
+  if (!cfg || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_create: null pointer");
+  *out = nullptr;
+  if (cfg->hidden == 0 || cfg->hidden % 256)
+    RV_FAIL(RV_ERR_INDIVISIBLE_ROW, "hidden %u: not a multiple of the 256-weight block", cfg->hidden);
+  if (cfg->moe == 0 || cfg->moe % 256)
+    RV_FAIL(RV_ERR_INDIVISIBLE_ROW, "moe_intermediate %u: not a multiple of the 256-weight block", cfg->moe);
+  if (cfg->hidden > 4096 || cfg->moe > 4096)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "hidden/moe above 4096 are not implemented on the GPU path");
+  if (cfg->n_experts == 0 || cfg->n_experts > 256)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "n_experts %u: the GPU path handles 1..256", cfg->n_experts);
+  if (cfg->top_k == 0 || cfg->top_k > 16 || cfg->top_k > cfg->n_experts)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "top_k %u: the GPU path handles 1..min(16, n_experts)", cfg->top_k);
+  if (max_tokens == 0 || max_tokens > (1u << 20) / cfg->top_k)
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "max_tokens %zu out of range", max_tokens);
+  int rc = ensure_device(device);
+  if (rc) return rc;
+  rv_moe *m = new (std::nothrow) rv_moe();
+  if (!m) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "out of host memory");
+  m->device = device;
+  m->cfg = *cfg;
+  m->max_tokens = max_tokens;
+  MoeDims &d = m->d;
+  d.H = (int)cfg->hidden;
+  d.M = (int)cfg->moe;
+  d.E = (int)cfg->n_experts;
+  d.K = (int)cfg->top_k;
+  d.hb = d.H / 256;
+  d.mb = d.M / 256;
+  d.act_stride = round16((size_t)d.hb * 292);
+  d.amoe_stride = round16((size_t)d.mb * 292);
+  d.eps = cfg->eps;
+  d.norm_topk = cfg->norm_topk_prob;
+  const size_t T = max_tokens, K = d.K, P = T * K;
+  m->max_units = (int)(std::min<size_t>((size_t)d.E, P) + (P + RV_MOE_TOK_CHUNK - 1) / RV_MOE_TOK_CHUNK);
+  // One arena for every scratch buffer the forward touches.
+  struct Part { size_t bytes; void **slot; };
+  MoeBufs &B = m->B;
+  const Part parts[] = {
+      {T * d.H * 4, (void **)&B.normed},
+      {T * d.act_stride, (void **)&B.acts},
+      {T * d.E * 4, (void **)&B.logits},
+      {P * 4, (void **)&B.ids},
+      {P * 4, (void **)&B.w},
+      {(size_t)d.E * 4, (void **)&B.counts},
+      {((size_t)d.E + 1) * 4, (void **)&B.index_start},
+      {P * 4, (void **)&B.index},
+      {(size_t)m->max_units * 16, (void **)&B.units},
+      {16, (void **)&B.n_units},
+      {P * d.M * 4, (void **)&B.hbuf},
+      {P * d.amoe_stride, (void **)&B.acts_moe},
+      {P * d.H * 4, (void **)&B.staged},
+      {(size_t)m->max_units * d.mb * 4, (void **)&B.tile_cnt},
+      {T * d.H * 4, (void **)&m->dres},
+  };
+  size_t total = 0;
+  for (const Part &p : parts) total += (p.bytes + 255) & ~(size_t)255;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  cudaError_t e = cudaMalloc(&m->arena, total);
+  if (e == cudaSuccess) e = cudaMemset(m->arena, 0, total);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    delete m;
+    RV_FAIL(RV_ERR_CUDA, "moe_create: %zu bytes of scratch: %s", total, cudaGetErrorString(e));
+  }
+  size_t off = 0;
+  for (const Part &p : parts) {
+    *p.slot = (uint8_t *)m->arena + off;
+    off += (p.bytes + 255) & ~(size_t)255;
+  }
+  B.max_units = m->max_units;
+  *out = m;
+  return RV_OK;
+}
+
+extern "C" void rv_moe_destroy(rv_moe *m) {
+  if (!m) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(m->device);
+  prof_release(m);
+  cudaFree(m->arena);
+  cudaSetDevice(prev);
+  delete m;
+}
+
+template <int FMT>
+static void launch_gate_up(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
+  const MoeDims &d = m->d;
+  const size_t smem = 16 + round16(2 * (size_t)RV_GU_ROWS * W.gu_row_bytes) + 16 +
+                      RV_MOE_MT * d.act_stride + 16 + 2 * RV_GU_ROWS * RV_MOE_MT * 4;
+  dim3 grid((unsigned)m->max_units, (unsigned)(d.M / RV_GU_ROWS));
+  k_gate_up<FMT><<<grid, 256, smem, s>>>(d, B, W);
+}
+template <int FMT>
+static void launch_down(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
+  const MoeDims &d = m->d;
+  const size_t smem = 16 + round16((size_t)RV_DOWN_ROWS * W.down_row_bytes) + 16 + RV_MOE_MT * d.amoe_stride + 16;
+  dim3 grid((unsigned)m->max_units, (unsigned)(d.H / RV_DOWN_ROWS));
+  k_down<FMT><<<grid, 256, smem, s>>>(d, B, W);
+}
+
+extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t layer,
+                              const float *ffn_norm, const float *router, float *residual,
+                              size_t n_tokens, uint32_t *topk_ids, float *topk_weights,
+                              uint32_t flags, rv_stream stream) {
+  if (!m || !table) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward: null engine or table");
+  if (layer >= table->layouts.size())
+    RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, table->layouts.size());
+  const rv_layer_layout &L = table->layouts[layer];
+  const MoeDims &d = m->d;
+  if (L.hidden != (uint32_t)d.H || L.moe != (uint32_t)d.M || L.n_experts != (uint32_t)d.E)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "layer %u geometry (%u, %u, %u) vs engine (%d, %d, %d)", layer, L.hidden,
+            L.moe, L.n_experts, d.H, d.M, d.E);
+  if (L.gate_format != L.up_format)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "layer %u: gate and up in different formats", layer);
+  if (flags & ~RV_MOE_TENSOR) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+  if (flags & RV_MOE_TENSOR) RV_FAIL(RV_ERR_UNIMPLEMENTED, "the tensor-core prefill path is not built yet");
+  if (n_tokens > m->max_tokens)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_forward: %zu tokens vs engine capacity %zu", n_tokens, m->max_tokens);
+  if (n_tokens == 0) return RV_OK;
+  if (!ffn_norm || !router || !residual) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward: null pointer");
+  if (((uintptr_t)router & 15) || (d.H & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward: router must be 16-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  MoeBufs B = m->B;
+  B.ffn_norm = ffn_norm;
+  B.router = router;
+  B.residual = residual;
+  B.T = (int)n_tokens;
+  MoeWeights W;
+  W.base = table->base[layer];
+  W.stride = L.stride;
+  W.gate_off = L.gate_off;
+  W.up_off = L.up_off;
+  W.down_off = L.down_off;
+  rv_row_bytes(L.gate_format, L.hidden, &W.gu_row_bytes);
+  rv_row_bytes(L.down_format, L.moe, &W.down_row_bytes);
+  const int T = (int)n_tokens;
+  cudaEvent_t *ev = nullptr;
+  if (m->prof_next < m->prof.size() / 5) ev = &m->prof[5 * m->prof_next++];
+  if (ev) RV_CUDA(cudaEventRecord(ev[0], s));
+  k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
+  k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, 0, s>>>(d, B);
+  k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
+  k_index<<<1, 1024, 0, s>>>(d, B);
+  if (ev) RV_CUDA(cudaEventRecord(ev[1], s));
+  switch (L.gate_format) {
+    case RV_Q4_K: launch_gate_up<RV_Q4_K>(m, B, W, s); break;
+    case RV_Q5_K: launch_gate_up<RV_Q5_K>(m, B, W, s); break;
+    default: launch_gate_up<RV_Q6_K>(m, B, W, s); break;
+  }
+  if (ev) RV_CUDA(cudaEventRecord(ev[2], s));
+  switch (L.down_format) {
+    case RV_Q4_K: launch_down<RV_Q4_K>(m, B, W, s); break;
+    case RV_Q5_K: launch_down<RV_Q5_K>(m, B, W, s); break;
+    default: launch_down<RV_Q6_K>(m, B, W, s); break;
+  }
+  if (ev) RV_CUDA(cudaEventRecord(ev[3], s));
+  k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
+  if (ev) RV_CUDA(cudaEventRecord(ev[4], s));
+  RV_LAUNCH_CHECK();
+  if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+  if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+  m->last_T = T;
+  return RV_OK;
+}
+
+extern "C" int rv_moe_forward_host(rv_moe *m, const rv_expert_table *table, uint32_t layer,
+                                   const float *ffn_norm, const float *router, float *residual_host,
+                                   size_t n_tokens, uint32_t *topk_ids_host, float *topk_weights_host,
+                                   uint32_t flags, rv_stream stream) {
+  if (!m) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward_host: null engine");
+  if (n_tokens > m->max_tokens)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_forward: %zu tokens vs engine capacity %zu", n_tokens, m->max_tokens);
+  if (n_tokens == 0) return RV_OK;
+  if (!residual_host) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward_host: null residual");
+  cudaStream_t s = (cudaStream_t)stream;
+  const MoeDims &d = m->d;
+  float *dres = m->dres;
+  const size_t rbytes = n_tokens * (size_t)d.H * 4;
+  RV_CUDA(cudaMemcpyAsync(dres, residual_host, rbytes, cudaMemcpyHostToDevice, s));
+  int rc = rv_moe_forward(m, table, layer, ffn_norm, router, dres, n_tokens, nullptr, nullptr, flags, stream);
+  if (rc) return rc;
+  RV_CUDA(cudaMemcpyAsync(residual_host, dres, rbytes, cudaMemcpyDeviceToHost, s));
+  if (topk_ids_host) RV_CUDA(cudaMemcpyAsync(topk_ids_host, m->B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToHost, s));
+  if (topk_weights_host) RV_CUDA(cudaMemcpyAsync(topk_weights_host, m->B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToHost, s));
+  RV_CUDA(cudaStreamSynchronize(s));
+  return RV_OK;
+}
+
+extern "C" int rv_moe_get_taps(const rv_moe *m, rv_moe_taps *o) {
+  if (!m || !o) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null pointer");
+  o->normed = m->B.normed;
+  o->acts = (const rv_block_q8k *)m->B.acts;
+  o->acts_stride = m->d.act_stride;
+  o->logits = m->B.logits;
+  o->weights = m->B.w;
+  o->ids = m->B.ids;
+  o->index = m->B.index;
+  o->index_start = m->B.index_start;
+  o->swiglu = m->B.hbuf;
+  o->acts_moe = m->B.acts_moe;
+  o->acts_moe_stride = m->d.amoe_stride;
+  o->staged = m->B.staged;
+  return RV_OK;
+}
+
+// ==================================================== synthetic inputs
+extern "C" int rv_synth_normal(uint64_t seed, uint64_t offset, float sigma, float *out, size_t n,
+                               rv_stream stream) {
+  if (n == 0) return RV_OK;
+  if (!out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "synth_normal: null pointer");
+  k_synth_normal<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(seed, offset, sigma, out, n);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_quantize_weights(int format, const float *x, size_t n, uint8_t *out, rv_stream stream) {
+  if (!rv_fmt_is_kquant(format)) RV_FAIL(RV_ERR_UNSUPPORTED_FORMAT, "quantize_weights: format %d", format);
+  if (n % 256) RV_FAIL(RV_ERR_INDIVISIBLE_ROW, "quantize_weights: %zu weights", n);
+  if (n == 0) return RV_OK;
+  if (!x || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "quantize_weights: null pointer");
+  const size_t nb = n / 256;
+  const unsigned grid = (unsigned)((nb + 127) / 128);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (format == RV_Q4_K) k_quantize_weights<RV_Q4_K><<<grid, 128, 0, s>>>(x, out, nb);
+  else if (format == RV_Q5_K) k_quantize_weights<RV_Q5_K><<<grid, 128, 0, s>>>(x, out, nb);
+  else k_quantize_weights<RV_Q6_K><<<grid, 128, 0, s>>>(x, out, nb);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_expert_table_fill_synthetic(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
+                                              rv_stream stream) {
+  if (!t) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null table");
+  if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
+  const rv_layer_layout &L = t->layouts[layer];
+  const size_t mh = (size_t)L.moe * L.hidden;
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(t->device));
+  float *tmp = nullptr;
+  cudaError_t e = cudaMalloc(&tmp, 3 * mh * sizeof(float));
+  if (e != cudaSuccess) {
+    cudaSetDevice(prev);
+    RV_FAIL(RV_ERR_CUDA, "fill_synthetic scratch: %s", cudaGetErrorString(e));
+  }
+  int rc = RV_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  for (uint32_t ex = 0; ex < L.n_experts && rc == RV_OK; ex++) {
+    uint8_t *blob = t->base[layer] + (size_t)ex * L.stride;
+    rc = rv_synth_normal(seed, (uint64_t)ex * 3 * mh, sigma, tmp, 3 * mh, stream);
+    if (!rc) rc = rv_quantize_weights(L.gate_format, tmp, mh, blob + L.gate_off, stream);
+    if (!rc) rc = rv_quantize_weights(L.up_format, tmp + mh, mh, blob + L.up_off, stream);
+    if (!rc) rc = rv_quantize_weights(L.down_format, tmp + 2 * mh, mh, blob + L.down_off, stream);
+  }
+  e = cudaStreamSynchronize(s);
+  cudaFree(tmp);
+  cudaSetDevice(prev);
+  if (rc) return rc;
+  if (e != cudaSuccess) RV_FAIL(RV_ERR_CUDA, "fill_synthetic: %s", cudaGetErrorString(e));
+  return RV_OK;
+}
