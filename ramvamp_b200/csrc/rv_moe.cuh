@@ -224,10 +224,16 @@ __global__ void __launch_bounds__(1024) k_index(MoeDims d, MoeBufs B) {
   }
   __syncthreads();
   const int pairs = B.T * d.K;
+  if (start[d.E] != (uint32_t)pairs) rv_dev_fail(RV_ERR_LENGTH_MISMATCH);  // stale counts
   for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
     const uint32_t e = B.ids[p];
+    if (e >= (uint32_t)d.E) {
+      rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
+      continue;
+    }
     const uint32_t pos = atomicAdd(&cursor[e], 1u);
-    B.index[pos] = (uint32_t)p;
+    if (pos < (uint32_t)pairs) B.index[pos] = (uint32_t)p;
+    else rv_dev_fail(RV_ERR_LENGTH_MISMATCH);
   }
 }
 
