@@ -245,18 +245,41 @@ __global__ void k_synth_normal(uint64_t seed, uint64_t offset, float sigma, floa
 // kernels/quants/test_support.rs:59-219, one thread per 256-weight block,
 // every float step with the reference's rounding (IEEE division, roundf =
 // half away from zero, ceil, f16 round-to-nearest-even).
-RV_DEVFN float f16_round(float v) { return __half2float(__float2half_rn(v)); }
+// f32 -> f16 bits, round to nearest even, as kernels/quants/f16.rs:39-91
+// computes it (overflow to infinity, subnormals, quiet NaN).
+RV_DEVFN uint16_t f32_to_f16_bits(float x) {
+  const uint32_t bits = __float_as_uint(x);
+  const uint16_t sign = (uint16_t)((bits >> 16) & 0x8000u);
+  const int exp = (int)((bits >> 23) & 0xFFu);
+  const uint32_t frac = bits & 0x007FFFFFu;
+  if (exp == 0xFF) return frac == 0 ? (uint16_t)(sign | 0x7C00u)
+                                    : (uint16_t)(sign | 0x7C00u | 0x0200u | ((frac >> 13) & 0x03FFu));
+  const int e16 = exp - 112;
+  if (e16 >= 0x1F) return (uint16_t)(sign | 0x7C00u);
+  if (e16 <= 0) {
+    if (e16 < -10) return sign;
+    const uint32_t mant = exp == 0 ? frac : (frac | 0x00800000u);
+    const uint32_t shift = (uint32_t)(14 - e16);
+    const uint32_t ulp = 1u << shift, half = ulp >> 1;
+    uint32_t v = mant >> shift;
+    const uint32_t rem = mant & (ulp - 1);
+    if (rem > half || (rem == half && (v & 1u))) v += 1;
+    return (uint16_t)(sign | v);
+  }
+  uint32_t v = ((uint32_t)e16 << 10) | (frac >> 13);
+  const uint32_t rem = frac & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (v & 1u))) v += 1;
+  return (uint16_t)(sign | v);
+}
+RV_DEVFN float f16_round(float v) { return h2f(f32_to_f16_bits(v)); }
 RV_DEVFN uint8_t clamp_u8(float v, float lo, float hi) {
   if (v < lo) v = lo;
   else if (v > hi) v = hi;
   if (v != v) return 0;
   return (uint8_t)v;
 }
-RV_DEVFN void put_f16(uint8_t *p, float v) {
-  const uint16_t h = __half_as_ushort(__float2half_rn(v));
-  p[0] = (uint8_t)(h & 255);
-  p[1] = (uint8_t)(h >> 8);
-}
+// Both f16 fields of every weight block sit at even offsets.
+RV_DEVFN void put_f16(uint8_t *p, float v) { *(uint16_t *)p = f32_to_f16_bits(v); }
 
 template <int LEVELS>
 RV_DEVFN void affine_scales_dev(const float *xs, uint8_t *scales, float &d, float &dmin,

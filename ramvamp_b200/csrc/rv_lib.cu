@@ -764,27 +764,35 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   rv_row_bytes(L.down_format, L.moe, &W.down_row_bytes);
   const int T = (int)n_tokens;
   cudaEvent_t *ev = nullptr;
-  if (m->prof_next < m->prof.size() / 5) ev = &m->prof[5 * m->prof_next++];
-  if (ev) RV_CUDA(cudaEventRecord(ev[0], s));
+  unsigned evflags = 0;
+  if (m->prof_next < m->prof.size() / 5) {
+    ev = &m->prof[5 * m->prof_next++];
+    // Inside a stream capture an event record must be an external node to
+    // be recorded on every replay of the graph.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    RV_CUDA(cudaStreamIsCapturing(s, &cs));
+    if (cs == cudaStreamCaptureStatusActive) evflags = cudaEventRecordExternal;
+  }
+  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[0], s, evflags));
   k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
   k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, 0, s>>>(d, B);
   k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
   k_index<<<1, 1024, 0, s>>>(d, B);
-  if (ev) RV_CUDA(cudaEventRecord(ev[1], s));
+  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[1], s, evflags));
   switch (L.gate_format) {
     case RV_Q4_K: launch_gate_up<RV_Q4_K>(m, B, W, s); break;
     case RV_Q5_K: launch_gate_up<RV_Q5_K>(m, B, W, s); break;
     default: launch_gate_up<RV_Q6_K>(m, B, W, s); break;
   }
-  if (ev) RV_CUDA(cudaEventRecord(ev[2], s));
+  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[2], s, evflags));
   switch (L.down_format) {
     case RV_Q4_K: launch_down<RV_Q4_K>(m, B, W, s); break;
     case RV_Q5_K: launch_down<RV_Q5_K>(m, B, W, s); break;
     default: launch_down<RV_Q6_K>(m, B, W, s); break;
   }
-  if (ev) RV_CUDA(cudaEventRecord(ev[3], s));
+  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[3], s, evflags));
   k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
-  if (ev) RV_CUDA(cudaEventRecord(ev[4], s));
+  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[4], s, evflags));
   RV_LAUNCH_CHECK();
   if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
   if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
