@@ -137,6 +137,47 @@ RV_DEVFN void rv_copy_bytes_block(uint8_t *dst, const uint8_t *src, size_t bytes
   for (size_t i = threadIdx.x; i < bytes; i += blockDim.x) dst[i] = src[i];
 }
 
+// ------------------------------------------------------ phase clocks
+// Compiled out unless RV_PHASE_CLOCK is defined: thread 0 of each CTA stamps
+// clock64() at the phases of a kernel (the GPU analogue of the reference's
+// PhaseClock, model/prefill.rs:414-520), read back by rv_debug_phase_clock.
+#ifdef RV_PHASE_CLOCK
+#define RV_PHASE_KERNELS 3
+#define RV_PHASE_CTAS 8192
+#define RV_PHASES 10
+__device__ long long g_rv_phase[RV_PHASE_KERNELS][RV_PHASE_CTAS][RV_PHASES];
+#define RV_PHASE(k, i)                                                                     \
+  do {                                                                                    \
+    const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                            \
+    if (threadIdx.x == 0 && cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = clock64();     \
+  } while (0)
+#else
+#define RV_PHASE(k, i) \
+  do {                 \
+  } while (0)
+#endif
+
+// -------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream is still running; it must call
+// pdl_wait() before touching anything that kernel writes.  pdl_trigger()
+// lets the next such kernel start early.  Both are no-ops for ordinary
+// launches.
+RV_DEVFN void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+RV_DEVFN void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// True when every double within rel*|r| of r rounds to the same float as r:
+// the f32 result of a double computation is then independent of how the
+// double was summed, within that error bound.
+RV_DEVFN bool f32_rounding_stable(double r, double rel) {
+  if (!isfinite(r)) return false;
+  const float f = __double2float_rn(r);
+  const double df = (double)f, tol = fabs(r) * rel;
+  const double mh = 0.5 * (df + (double)nextafterf(f, INFINITY));
+  const double ml = 0.5 * (df + (double)nextafterf(f, -INFINITY));
+  return fabs(mh - r) > tol && fabs(r - ml) > tol;
+}
+
 // ------------------------------------------------ Q8_K warp quantizer
 // Quantizes 256 floats held 8 per lane (lane l holds elements 8l..8l+7)
 // into one packed 292-byte Q8_K block at `out` (4-byte aligned), exactly as
@@ -221,9 +262,10 @@ RV_DEVFN void unpack_k4_scales(const uint8_t *s12, int lane, WBlock &w) {
       mn[j] = (int)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
     }
   }
-  int i = lane & 3;
-  w.m0 = mn[2 * i];
-  w.m1 = mn[2 * i + 1];
+  // Min lane i (< 4) pairs sub-blocks 2i and 2i+1; selects keep mn in registers.
+  const int i = lane & 3;
+  w.m0 = i == 0 ? mn[0] : i == 1 ? mn[2] : i == 2 ? mn[4] : mn[6];
+  w.m1 = i == 0 ? mn[1] : i == 1 ? mn[3] : i == 2 ? mn[5] : mn[7];
 }
 
 template <int FMT>

@@ -117,14 +117,10 @@ static int ensure_device(int dev) {
   cudaFuncSetAttribute(k_gemv<RV_Q5_K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv<RV_Q6_K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv<RV_Q6_K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_gate_up<RV_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_gate_up<RV_Q5_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_gate_up<RV_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_down<RV_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_down<RV_Q5_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_down<RV_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_prologue, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_route_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaError_t e3 = cudaGetLastError();
   cudaSetDevice(prev);
   if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
@@ -675,6 +671,8 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
       {P * d.amoe_stride, (void **)&B.acts_moe},
       {P * d.H * 4, (void **)&B.staged},
       {(size_t)m->max_units * d.mb * 4, (void **)&B.tile_cnt},
+      {16, (void **)&B.route_cnt},
+      {((size_t)d.H / 8 + 1) * 4, (void **)&B.down_cnt},
       {T * d.H * 4, (void **)&m->dres},
   };
   size_t total = 0;
@@ -710,20 +708,60 @@ extern "C" void rv_moe_destroy(rv_moe *m) {
   delete m;
 }
 
-template <int FMT>
-static void launch_gate_up(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
+// Launch with programmatic stream serialization (the kernel may start
+// while the previous kernel of the stream runs; it calls pdl_wait()).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Split mode (G lanes per row, one token at a time) serves decode; token
+// mode (a thread per row, up to 8 tokens in flight) serves larger batches.
+template <int FMT, int G, int NBG, int R>
+static void launch_gate_up_t(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
   const MoeDims &d = m->d;
-  const size_t smem = 16 + round16(2 * (size_t)RV_GU_ROWS * W.gu_row_bytes) + 16 +
-                      RV_MOE_MT * d.act_stride + 16 + 2 * RV_GU_ROWS * RV_MOE_MT * 4;
-  dim3 grid((unsigned)m->max_units, (unsigned)(d.M / RV_GU_ROWS));
-  k_gate_up<FMT><<<grid, 256, smem, s>>>(d, B, W);
+  const size_t st = FMT == RV_Q6_K ? W.gu_row_bytes : W.gu_row_bytes + 16;
+  const size_t smem = 16 + round16(2 * (size_t)R * st) + 16 + (size_t)B.ms * d.act_stride +
+                      (FMT == RV_Q6_K ? (size_t)B.ms * d.hb * 64 * 4 : 0) + 2 * R * RV_MOE_MT * 4;
+  dim3 grid((unsigned)m->max_units, (unsigned)(d.M / R));
+  cudaFuncSetAttribute(k_gate_up<FMT, G, NBG, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_gate_up<FMT, G, NBG, R><<<grid, 2 * R * G, smem, s>>>(d, B, W);
 }
 template <int FMT>
-static void launch_down(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
+static void launch_gate_up(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, int T, cudaStream_t s) {
+  if (T <= RV_SMALL_T && m->d.hb == 8) launch_gate_up_t<FMT, 4, 2, 8>(m, B, W, s);
+  else launch_gate_up_t<FMT, 1, 1, 32>(m, B, W, s);
+}
+template <int FMT, int G, int NBG, int ROWS, bool COMBINE>
+static cudaError_t launch_down_t(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
   const MoeDims &d = m->d;
-  const size_t smem = 16 + round16((size_t)RV_DOWN_ROWS * W.down_row_bytes) + 16 + RV_MOE_MT * d.amoe_stride + 16;
-  dim3 grid((unsigned)m->max_units, (unsigned)(d.H / RV_DOWN_ROWS));
-  k_down<FMT><<<grid, 256, smem, s>>>(d, B, W);
+  const size_t st = FMT == RV_Q6_K ? W.down_row_bytes : W.down_row_bytes + 16;
+  const size_t smem = 16 + round16((size_t)ROWS * st) + 16 + (size_t)B.ms * d.amoe_stride +
+                      (FMT == RV_Q6_K ? (size_t)B.ms * d.mb * 64 * 4 : 0) + 16;
+  dim3 grid((unsigned)m->max_units, (unsigned)((d.H + ROWS - 1) / ROWS));
+  cudaFuncSetAttribute(k_down<FMT, G, NBG, ROWS, COMBINE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  return launch_pdl(k_down<FMT, G, NBG, ROWS, COMBINE>, grid, dim3(32), smem, s, d, B, W);
+}
+// Returns true when the down kernel also performed the combine.
+template <int FMT>
+static bool launch_down(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, int T, cudaStream_t s) {
+  if (T <= RV_SMALL_T && m->d.mb == 3) {
+    launch_down_t<FMT, 3, 1, 8, true>(m, B, W, s);
+    return true;
+  }
+  launch_down_t<FMT, 1, 1, 32, false>(m, B, W, s);
+  return false;
 }
 
 extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t layer,
@@ -774,24 +812,33 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
     if (cs == cudaStreamCaptureStatusActive) evflags = cudaEventRecordExternal;
   }
   if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[0], s, evflags));
-  k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
-  k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, 0, s>>>(d, B);
-  k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
-  k_index<<<1, 1024, 0, s>>>(d, B);
+  B.ms = T < RV_MOE_MT ? T : RV_MOE_MT;
+  if (T <= RV_SMALL_T) {
+    // decode: routing, norm, Q8_K and dispatch in one launch
+    const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)T * (d.H + 4) * 4 + 4 * sizeof(double) + 16;
+    RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
+  } else {
+    k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
+    const size_t smem = 16 + 2 * (size_t)(4 * RV_RCHUNK + 32 * (RV_RCHUNK + 4)) * 4;
+    k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, smem, s>>>(d, B);
+    k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
+    k_index<<<1, 1024, 0, s>>>(d, B);
+  }
   if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[1], s, evflags));
   switch (L.gate_format) {
-    case RV_Q4_K: launch_gate_up<RV_Q4_K>(m, B, W, s); break;
-    case RV_Q5_K: launch_gate_up<RV_Q5_K>(m, B, W, s); break;
-    default: launch_gate_up<RV_Q6_K>(m, B, W, s); break;
+    case RV_Q4_K: launch_gate_up<RV_Q4_K>(m, B, W, T, s); break;
+    case RV_Q5_K: launch_gate_up<RV_Q5_K>(m, B, W, T, s); break;
+    default: launch_gate_up<RV_Q6_K>(m, B, W, T, s); break;
   }
   if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[2], s, evflags));
+  bool combined;
   switch (L.down_format) {
-    case RV_Q4_K: launch_down<RV_Q4_K>(m, B, W, s); break;
-    case RV_Q5_K: launch_down<RV_Q5_K>(m, B, W, s); break;
-    default: launch_down<RV_Q6_K>(m, B, W, s); break;
+    case RV_Q4_K: combined = launch_down<RV_Q4_K>(m, B, W, T, s); break;
+    case RV_Q5_K: combined = launch_down<RV_Q5_K>(m, B, W, T, s); break;
+    default: combined = launch_down<RV_Q6_K>(m, B, W, T, s); break;
   }
   if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[3], s, evflags));
-  k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
+  if (!combined) k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
   if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[4], s, evflags));
   RV_LAUNCH_CHECK();
   if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
@@ -896,3 +943,16 @@ extern "C" int rv_expert_table_fill_synthetic(rv_expert_table *t, uint32_t layer
   if (e != cudaSuccess) RV_FAIL(RV_ERR_CUDA, "fill_synthetic: %s", cudaGetErrorString(e));
   return RV_OK;
 }
+
+#ifdef RV_PHASE_CLOCK
+// Copies the phase clocks of kernel k (0 route, 1 gate_up, 2 down) to out
+// ([RV_PHASE_CTAS][RV_PHASES] int64) and clears them.
+extern "C" __attribute__((visibility("default"))) int rv_debug_phase_clock(int k, long long *out) {
+  RV_CUDA(cudaDeviceSynchronize());
+  RV_CUDA(cudaMemcpyFromSymbol(out, g_rv_phase, sizeof(long long) * RV_PHASE_CTAS * RV_PHASES,
+                               sizeof(long long) * RV_PHASE_CTAS * RV_PHASES * k));
+  static long long zero[RV_PHASE_CTAS * RV_PHASES];
+  RV_CUDA(cudaMemcpyToSymbol(g_rv_phase, zero, sizeof zero, sizeof(long long) * RV_PHASE_CTAS * RV_PHASES * k));
+  return RV_OK;
+}
+#endif

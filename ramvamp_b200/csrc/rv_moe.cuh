@@ -19,11 +19,10 @@
 #include "rv_expf.cuh"
 #include "rv_internal.cuh"
 #include "rv_kernels.cuh"
+#include "rv_rowdot.cuh"
 
 #define RV_MOE_MT 8          // tokens staged per pass
 #define RV_MOE_TOK_CHUNK 64  // tokens per work unit
-#define RV_GU_ROWS 16        // gate (and up) rows per k_gate_up CTA
-#define RV_DOWN_ROWS 32      // down rows per k_down CTA
 
 struct MoeDims {
   int H, M, E, K;
@@ -51,7 +50,10 @@ struct MoeBufs {
   uint8_t *acts_moe;       // [T*K][amoe_stride]
   float *staged;           // [T][K][H]
   int *tile_cnt;           // [max_units][M/256], zero between calls
+  int *route_cnt;          // [1] CTAs done in k_route_decode, zero between calls
+  int *down_cnt;           // [H/8] units done per down row tile, zero between calls
   int T;
+  int ms;                  // activation slots per CTA pass: min(T, RV_MOE_MT)
   int max_units;
 };
 
@@ -86,43 +88,23 @@ __global__ void __launch_bounds__(256) k_prologue(MoeDims d, MoeBufs B) {
   }
 }
 
-// ------------------------------------------------------- router logits
-// Warp w of the CTA owns expert blockIdx.y*4+w; lane l owns token
-// blockIdx.x*32+l.  Each logit is the reference's serial f32 chain:
-// acc = acc + router[e][k] * normed[t][k] for k = 0..H-1, no FMA.
-__global__ void __launch_bounds__(128) k_router_logits(MoeDims d, MoeBufs B) {
-  const int e = blockIdx.y * 4 + (threadIdx.x >> 5);
-  const int t = blockIdx.x * 32 + (threadIdx.x & 31);
-  if (e >= d.E || t >= B.T) return;
-  const float4 *r4 = (const float4 *)(B.router + (size_t)e * d.H);
-  const float4 *x4 = (const float4 *)(B.normed + (size_t)t * d.H);
-  float acc = 0.0f;
-  const int n4 = d.H >> 2;
-#pragma unroll 4
-  for (int k = 0; k < n4; k++) {
-    const float4 r = __ldg(r4 + k), x = x4[k];
-    acc = __fadd_rn(acc, __fmul_rn(r.x, x.x));
-    acc = __fadd_rn(acc, __fmul_rn(r.y, x.y));
-    acc = __fadd_rn(acc, __fmul_rn(r.z, x.z));
-    acc = __fadd_rn(acc, __fmul_rn(r.w, x.w));
-  }
-  B.logits[(size_t)t * d.E + e] = acc;
-}
-
 // ----------------------------------------------------------- top-k route
-// One warp per token, E <= 256 (8 per lane), K <= 16.
-__global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
-  __shared__ double es[4][256];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + warp;
-  if (t >= B.T) return;
+// Softmax, top-k and renormalization of token t's logits by one warp
+// (forward.rs:2669-2705): f32 max, f64 exp of (x - max), f32 copy of each
+// exponential, serial f64 sum in index order, f32 reciprocal scale; top-k by
+// repeated argmax with a strict '>' scan (the lowest index wins a tie, the
+// winner is blanked with -inf); renormalization by the in-order f32 sum.
+// E <= 256 (8 per lane), K <= 16.  Writes ids/w and counts (any address
+// space: global in k_route, shared in k_route_decode).
+RV_DEVFN void route_token_warp(const MoeDims &d, const MoeBufs &B, int t, int lane, double *es,
+                               int *counts) {
   const float *lg = B.logits + (size_t)t * d.E;
   float p[8];
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int e = lane + 32 * j;
-    p[j] = e < d.E ? lg[e] : -INFINITY;
+    p[j] = e < d.E ? __ldcg(lg + e) : -INFINITY;
     if (e < d.E) mx = fmaxf(mx, p[j]);
   }
 #pragma unroll
@@ -133,22 +115,33 @@ __global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
     const int e = lane + 32 * j;
     if (e < d.E) {
       const double ex = exp(__dsub_rn((double)p[j], dmx));
-      es[warp][e] = ex;
+      es[e] = ex;
       p[j] = __double2float_rn(ex);
     }
   }
   __syncwarp();
-  double sum = 0.0;
-  if (lane == 0)
-    for (int e = 0; e < d.E; e++) sum = __dadd_rn(sum, es[warp][e]);
-  sum = __shfl_sync(RV_FULL, sum, 0);
-  const float inv = __double2float_rn(__drcp_rn(sum));
+  // The reference sums the exponentials serially in index order.  A tree sum
+  // of these <= 256 non-negative terms differs from it by < 2^-44 relative,
+  // so unless 1/sum lies that close to a float rounding midpoint the f32
+  // reciprocal is the same; otherwise lane 0 redoes the serial sum.
+  double part = 0.0;
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+    if (lane + 32 * j < d.E) part = __dadd_rn(part, es[lane + 32 * j]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+  double rinv = __drcp_rn(part);
+  if (!f32_rounding_stable(rinv, 0x1p-42)) {
+    double sum = 0.0;
+    if (lane == 0)
+      for (int e = 0; e < d.E; e++) sum = __dadd_rn(sum, es[e]);
+    rinv = __drcp_rn(__shfl_sync(RV_FULL, sum, 0));
+  }
+  const float inv = __double2float_rn(rinv);
 #pragma unroll
   for (int j = 0; j < 8; j++) p[j] = (lane + 32 * j) < d.E ? __fmul_rn(p[j], inv) : -INFINITY;
-  // Top-k by repeated argmax: strict '>' scan from expert 0, so the lowest
-  // index wins a tie; the winner is blanked with -inf (forward.rs:2688-2699).
-  uint32_t ids[16];
-  float ws[16];
+  uint32_t my_id = 0;
+  float my_w = 0.0f, wsum = -0.0f;
   for (int k = 0; k < d.K; k++) {
     float bp = -INFINITY;
     int be = 1 << 30;
@@ -168,164 +161,481 @@ __global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
       }
     }
     if (be == (1 << 30)) be = 0;  // nothing beat -inf: the scan keeps expert 0
-    ids[k] = (uint32_t)be;
-    ws[k] = bp;
+    if (lane == k) {
+      my_id = (uint32_t)be;
+      my_w = bp;
+    }
+    wsum = __fadd_rn(wsum, bp);  // the in-order sum of the selected weights
 #pragma unroll
     for (int j = 0; j < 8; j++)
       if (lane + 32 * j == be) p[j] = -INFINITY;
   }
-  if (d.norm_topk) {
-    float s = -0.0f;
-    for (int k = 0; k < d.K; k++) s = __fadd_rn(s, ws[k]);
-    for (int k = 0; k < d.K; k++) ws[k] = __fdiv_rn(ws[k], s);
-  }
   if (lane < d.K) {
-    uint32_t id = 0;
-    float wv = 0.0f;
-    for (int k = 0; k < d.K; k++)
-      if (k == lane) {
-        id = ids[k];
-        wv = ws[k];
-      }
-    B.ids[(size_t)t * d.K + lane] = id;
-    B.w[(size_t)t * d.K + lane] = wv;
-    atomicAdd(&B.counts[id], 1);
+    if (d.norm_topk) my_w = __fdiv_rn(my_w, wsum);
+    B.ids[(size_t)t * d.K + lane] = my_id;
+    B.w[(size_t)t * d.K + lane] = my_w;
+    atomicAdd(&counts[my_id], 1);
   }
 }
 
+__global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
+  __shared__ double es[4][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + warp;
+  if (t >= B.T) return;
+  route_token_warp(d, B, t, lane, es[warp], B.counts);
+}
+
 // ----------------------------------------------------------- dispatch
-__global__ void __launch_bounds__(1024) k_index(MoeDims d, MoeBufs B) {
-  __shared__ uint32_t start[257];
-  __shared__ uint32_t cursor[256];
-  if (threadIdx.x == 0) {
-    uint32_t s = 0;
-    int n = 0;
-    for (int e = 0; e < d.E; e++) {
-      const uint32_t c = (uint32_t)B.counts[e];
-      start[e] = s;
-      for (uint32_t p = 0; p < c; p += RV_MOE_TOK_CHUNK) {
-        if (n < B.max_units)
-          B.units[n] = make_int4(e, (int)(s + p), (int)(s + min(c, p + RV_MOE_TOK_CHUNK)), 0);
-        n++;
-      }
-      s += c;
-    }
-    start[d.E] = s;
-    if (n > B.max_units) rv_dev_fail(RV_ERR_LENGTH_MISMATCH);
-    *B.n_units = min(n, B.max_units);
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e <= d.E; e += blockDim.x) {
-    B.index_start[e] = start[e];
-    if (e < d.E) {
-      cursor[e] = start[e];
-      B.counts[e] = 0;  // ready for the next call
-    }
-  }
-  __syncthreads();
+// CSR inverse index (prefill.rs:2536-2580) and the work units, built by one
+// CTA from per-expert counts in shared memory: warp 0 scans the counts and
+// the unit counts, every thread writes units, then the (token, slot) pairs
+// are placed by expert.  s_cnt/s_cur: [256] ints, s_st/s_us: [257].
+RV_DEVFN void build_index_cta(const MoeDims &d, const MoeBufs &B, int *s_cnt, uint32_t *s_st,
+                              uint32_t *s_cur, int *s_us) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pairs = B.T * d.K;
-  if (start[d.E] != (uint32_t)pairs) rv_dev_fail(RV_ERR_LENGTH_MISMATCH);  // stale counts
+  if (warp == 0) {
+    int c[8], u[8], sc = 0, su = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int e = lane * 8 + i;
+      c[i] = e < d.E ? s_cnt[e] : 0;
+      u[i] = (c[i] + RV_MOE_TOK_CHUNK - 1) / RV_MOE_TOK_CHUNK;
+      sc += c[i];
+      su += u[i];
+    }
+    int xc = sc, xu = su;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int yc = __shfl_up_sync(RV_FULL, xc, o), yu = __shfl_up_sync(RV_FULL, xu, o);
+      if (lane >= o) {
+        xc += yc;
+        xu += yu;
+      }
+    }
+    const int tc = __shfl_sync(RV_FULL, xc, 31), tu = __shfl_sync(RV_FULL, xu, 31);
+    xc -= sc;
+    xu -= su;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int e = lane * 8 + i;
+      if (e < d.E) {
+        s_st[e] = (uint32_t)xc;
+        s_cur[e] = (uint32_t)xc;
+        s_us[e] = xu;
+      }
+      xc += c[i];
+      xu += u[i];
+    }
+    if (lane == 0) {
+      s_st[d.E] = (uint32_t)tc;
+      s_us[d.E] = tu;
+      if (tc != pairs || tu > B.max_units) rv_dev_fail(RV_ERR_LENGTH_MISMATCH);
+      *B.n_units = min(tu, B.max_units);
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e <= d.E; e += blockDim.x) B.index_start[e] = s_st[e];
+  for (int e = threadIdx.x; e < d.E; e += blockDim.x) {
+    const int c = s_cnt[e];
+    int u = s_us[e];
+    for (int p = 0; p < c; p += RV_MOE_TOK_CHUNK, u++)
+      if (u < B.max_units)
+        B.units[u] = make_int4(e, (int)s_st[e] + p, (int)s_st[e] + min(c, p + RV_MOE_TOK_CHUNK), 0);
+  }
   for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
     const uint32_t e = B.ids[p];
     if (e >= (uint32_t)d.E) {
       rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
       continue;
     }
-    const uint32_t pos = atomicAdd(&cursor[e], 1u);
+    const uint32_t pos = atomicAdd(&s_cur[e], 1u);
     if (pos < (uint32_t)pairs) B.index[pos] = (uint32_t)p;
     else rv_dev_fail(RV_ERR_LENGTH_MISMATCH);
   }
 }
 
-// ------------------------------------------------- gate/up + SwiGLU + Q8_K
-// grid = (max_units, M / RV_GU_ROWS), block = 256 threads:
-// thread (part, row, lane) = (tid/128, (tid/8)%16, tid%8).
-template <int FMT>
-__global__ void __launch_bounds__(256) k_gate_up(MoeDims d, MoeBufs B, MoeWeights W) {
+// Large-T dispatch: counts come from k_route's global atomics and are
+// cleared here for the next call.
+__global__ void __launch_bounds__(1024) k_index(MoeDims d, MoeBufs B) {
+  __shared__ int s_cnt[256];
+  __shared__ uint32_t s_st[257], s_cur[256];
+  __shared__ int s_us[257];
+  for (int e = threadIdx.x; e < 256; e += blockDim.x) s_cnt[e] = e < d.E ? B.counts[e] : 0;
+  __syncthreads();
+  for (int e = threadIdx.x; e < d.E; e += blockDim.x) B.counts[e] = 0;
+  build_index_cta(d, B, s_cnt, s_st, s_cur, s_us);
+}
+
+// ------------------------------------------------------- decode routing
+// Everything before the experts for T <= RV_SMALL_T tokens in one launch:
+// grid = E CTAs of four warps; CTA e owns expert e (one serial chain per SM,
+// so no two chains compete for an SM's issue slots).  Each CTA stages its
+// router row and the norm weight (before waiting on the previous kernel:
+// they do not depend on it) and the T residual rows with bulk copies, the
+// four warps compute the RMSNorm of every token, and lane t of warp 0 runs
+// the serial f32 chain of logit (t, e) from shared memory.  The last CTA to finish writes normed
+// and its Q8_K, routes every token and builds the dispatch index.
+#define RV_SMALL_T 8
+// dot_f32 (forward.rs:1231-1237): acc = acc + a[k]*b[k] for k in order, no
+// FMA.  The adds form one dependent chain; the operands of the next 32
+// products are loaded into registers before the current 32 adds so the
+// chain runs at the add latency.  n4 (float4 count) must be a multiple of 8.
+RV_DEVFN float serial_dot_f32(const float4 *a, const float4 *b, int n4) {
+  float acc = 0.0f;
+  float4 ra[8], rb[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    ra[j] = a[j];
+    rb[j] = b[j];
+  }
+  for (int k = 0; k < n4; k += 8) {
+    float4 na[8], nb[8];
+    const int kn = k + 8 < n4 ? k + 8 : k;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      na[j] = a[kn + j];
+      nb[j] = b[kn + j];
+    }
+    float p[32];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      p[4 * j + 0] = __fmul_rn(ra[j].x, rb[j].x);
+      p[4 * j + 1] = __fmul_rn(ra[j].y, rb[j].y);
+      p[4 * j + 2] = __fmul_rn(ra[j].z, rb[j].z);
+      p[4 * j + 3] = __fmul_rn(ra[j].w, rb[j].w);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++) acc = __fadd_rn(acc, p[j]);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      ra[j] = na[j];
+      rb[j] = nb[j];
+    }
+  }
+  return acc;
+}
+
+__global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   extern __shared__ __align__(16) uint8_t sm[];
-  constexpr int R = RV_GU_ROWS, MT = RV_MOE_MT;
-  constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
+  __shared__ double es[4][256];
+  __shared__ int s_cnt[256];
+  __shared__ uint32_t s_st[257], s_cur[256];
+  __shared__ int s_us[257];
+  __shared__ int s_last;
+  RV_PHASE(0, 0);
+  const int T = B.T, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x;
+  const int xstride = d.H + 4;  // padded rows: conflict-free per-lane reads
+  uint64_t *bar = (uint64_t *)sm;                // [2]: router rows + norm weight, residual rows
+  float *rows = (float *)(sm + 16);              // [H] router row e
+  float *nw = rows + d.H;                        // [H] ffn_norm weight
+  float *xs = nw + d.H;                          // [T][H + 4]
+  double *red = (double *)(xs + T * xstride);    // [4] per-warp scratch
+  const int n_rows = 1;
+  const float *rsrc = B.router + (size_t)e0 * d.H;
+  const size_t rbytes = (size_t)n_rows * d.H * 4;
+  const bool rbulk = rv_bulk_ok(rsrc, rows, rbytes) && rv_bulk_ok(B.ffn_norm, nw, (size_t)d.H * 4);
+  const bool xbulk = rv_bulk_ok(B.residual, xs, (size_t)d.H * 4);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
+    if (rbulk) {
+      mbar_arrive_expect_tx(bar, (uint32_t)(rbytes + (size_t)d.H * 4));
+      bulk_g2s(rows, rsrc, (uint32_t)rbytes, bar);
+      bulk_g2s(nw, B.ffn_norm, (uint32_t)(d.H * 4), bar);
+    }
+  }
+  if (!rbulk) {
+    for (size_t k = threadIdx.x; k < (size_t)n_rows * d.H; k += blockDim.x) rows[k] = rsrc[k];
+    for (int k = threadIdx.x; k < d.H; k += blockDim.x) nw[k] = B.ffn_norm[k];
+  }
+  pdl_wait();  // the residual is the previous kernel's output
+  RV_PHASE(0, 1);
+  if (threadIdx.x == 0 && xbulk) {
+    mbar_arrive_expect_tx(bar + 1, (uint32_t)(T * d.H * 4));
+    for (int t = 0; t < T; t++)
+      bulk_g2s(xs + t * xstride, B.residual + (size_t)t * d.H, (uint32_t)(d.H * 4), bar + 1);
+  }
+  if (!xbulk)
+    for (int t = 0; t < T; t++)
+      for (int k = threadIdx.x; k < d.H; k += blockDim.x) xs[t * xstride + k] = B.residual[(size_t)t * d.H + k];
+  __syncthreads();
+  if (xbulk && !mbar_wait_bounded(bar + 1, 0)) return;
+  if (rbulk && !mbar_wait_bounded(bar, 0)) return;
+  RV_PHASE(0, 2);
+  // RMSNorm (norm.rs:17-60): warp w normalizes tokens w, w+4, ... in place.
+  for (int t = warp; t < T; t += 4) {
+    float *x = xs + t * xstride;
+    double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
+    for (int k = 4 * lane; k < d.H; k += 128) {
+      const float4 v = *(const float4 *)(x + k);
+      p0 = __dadd_rn(p0, __dmul_rn((double)v.x, (double)v.x));
+      p1 = __dadd_rn(p1, __dmul_rn((double)v.y, (double)v.y));
+      p2 = __dadd_rn(p2, __dmul_rn((double)v.z, (double)v.z));
+      p3 = __dadd_rn(p3, __dmul_rn((double)v.w, (double)v.w));
+    }
+    double part = __dadd_rn(__dadd_rn(p0, p1), __dadd_rn(p2, p3));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+    if (lane == 0) {
+      const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(__ddiv_rn(part, (double)d.H), (double)d.eps)));
+      float inv = __double2float_rn(r);
+      if (!f32_rounding_stable(r, 0x1p-38)) {
+        double ser = 0.0;  // the reference's serial order
+        for (int k = 0; k < d.H; k++) {
+          const double v = (double)x[k];
+          ser = __dadd_rn(ser, __dmul_rn(v, v));
+        }
+        inv = rms_inv_from_sum(ser, (size_t)d.H, d.eps);
+      }
+      red[warp] = (double)inv;
+    }
+    __syncwarp();
+    const float inv = (float)red[warp];
+    for (int k = lane; k < d.H; k += 32) x[k] = __fmul_rn(__fmul_rn(x[k], inv), nw[k]);
+    __syncwarp();
+  }
+  __syncthreads();
+  RV_PHASE(0, 3);
+  RV_PHASE(0, 4);
+  // Router logits: acc = acc + router[e][k] * normed[t][k], k = 0..H-1.
+  if (warp < n_rows && lane < T)
+    B.logits[(size_t)lane * d.E + e0 + warp] =
+        serial_dot_f32((const float4 *)(rows + warp * d.H), (const float4 *)(xs + lane * xstride), d.H / 4);
+  RV_PHASE(0, 5);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(B.route_cnt, 1);
+    s_last = old == (int)gridDim.x - 1;
+    if (s_last) *B.route_cnt = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  RV_PHASE(0, 6);
+  __threadfence();
+  for (int e = threadIdx.x; e < 256; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  // Routing on warps 0.., normed and its Q8_K on the others (all when T > 3).
+  const int rw = min(T, 4);
+  for (int t = warp; t < T; t += 4) route_token_warp(d, B, t, lane, es[warp], s_cnt);
+  for (int tb = warp - (rw < 4 ? rw : 0); tb >= 0 && tb < T * d.hb; tb += (rw < 4 ? 4 - rw : 4)) {
+    const int t = tb / d.hb, b = tb % d.hb;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = xs[t * xstride + b * 256 + 8 * lane + e];
+    q8k_quantize_warp(v, lane, B.acts + (size_t)t * d.act_stride + (size_t)b * 292);
+#pragma unroll
+    for (int e = 0; e < 8; e++) B.normed[(size_t)t * d.H + b * 256 + 8 * lane + e] = v[e];
+  }
+  __syncthreads();
+  RV_PHASE(0, 7);
+  build_index_cta(d, B, s_cnt, s_st, s_cur, s_us);
+  RV_PHASE(0, 8);
+}
+
+// Large-T router logits: CTA = 4 experts x 32 tokens; lane t of warp w runs
+// the chain of (token blockIdx.x*32+t, expert blockIdx.y*4+w) over
+// RV_RCHUNK-wide slices of the router rows and normed rows staged in shared
+// memory (bulk copies, double-buffered).
+#define RV_RCHUNK 256
+__global__ void __launch_bounds__(128) k_router_logits(MoeDims d, MoeBufs B) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint64_t *bar = (uint64_t *)sm;               // [2]
+  const int xs_stride = RV_RCHUNK + 4;
+  float *buf = (float *)(sm + 16);
+  const int stage_floats = 4 * RV_RCHUNK + 32 * xs_stride;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.y * 4, t0 = blockIdx.x * 32;
+  const int ne = min(4, d.E - e0), nt = min(32, B.T - t0);
+  const int nchunks = d.H / RV_RCHUNK;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
+  }
+  __syncthreads();
+  auto issue = [&](int c) {
+    float *st = buf + (c & 1) * stage_floats;
+    mbar_arrive_expect_tx(bar + (c & 1), (uint32_t)((ne + nt) * RV_RCHUNK * 4));
+    for (int i = 0; i < ne; i++)
+      bulk_g2s(st + i * RV_RCHUNK, B.router + (size_t)(e0 + i) * d.H + (size_t)c * RV_RCHUNK, RV_RCHUNK * 4,
+               bar + (c & 1));
+    for (int i = 0; i < nt; i++)
+      bulk_g2s(st + 4 * RV_RCHUNK + i * xs_stride, B.normed + (size_t)(t0 + i) * d.H + (size_t)c * RV_RCHUNK,
+               RV_RCHUNK * 4, bar + (c & 1));
+  };
+  if (threadIdx.x == 0) {
+    issue(0);
+    if (nchunks > 1) issue(1);
+  }
+  float acc = 0.0f;
+  for (int c = 0; c < nchunks; c++) {
+    if (!mbar_wait_bounded(bar + (c & 1), (uint32_t)((c >> 1) & 1))) return;
+    const float *st = buf + (c & 1) * stage_floats;
+    if (warp < ne && lane < nt) {
+      const float4 *r4 = (const float4 *)(st + warp * RV_RCHUNK);
+      const float4 *x4 = (const float4 *)(st + 4 * RV_RCHUNK + lane * xs_stride);
+#pragma unroll 8
+      for (int k = 0; k < RV_RCHUNK / 4; k++) {
+        const float4 r = r4[k], x = x4[k];
+        acc = __fadd_rn(acc, __fmul_rn(r.x, x.x));
+        acc = __fadd_rn(acc, __fmul_rn(r.y, x.y));
+        acc = __fadd_rn(acc, __fmul_rn(r.z, x.z));
+        acc = __fadd_rn(acc, __fmul_rn(r.w, x.w));
+      }
+    }
+    __syncthreads();  // stage (c & 1) consumed
+    if (threadIdx.x == 0 && c + 2 < nchunks) {
+      fence_proxy_async();
+      issue(c + 2);
+    }
+  }
+  if (warp < ne && lane < nt) B.logits[(size_t)(t0 + lane) * d.E + e0 + warp] = acc;
+}
+
+// ------------------------------------------------- weight-tile staging
+// Rows [r0, r0+n) of a matrix with `row_bytes` per row go to shared memory.
+// Q4_K/Q5_K rows land at a padded stride (row_bytes + 16: 16-byte aligned
+// blocks, conflict-free 128-bit reads), one bulk copy per row; Q6_K rows
+// (630 bytes, only 2-byte aligned) land densely in one bulk copy when the
+// range is 16-byte aligned.  Misaligned sources fall back to a cooperative
+// byte copy into the same layout.  Returns the bytes that go through the
+// bulk-copy engine on `bar` (issued by thread 0 when `issue`); 0 means the
+// cooperative copy ran and a __syncthreads must follow.
+template <int FMT>
+RV_DEVFN size_t tile_stride(size_t row_bytes) {
+  return FMT == RV_Q6_K ? row_bytes : row_bytes + 16;
+}
+template <int FMT>
+RV_DEVFN uint32_t stage_rows(uint8_t *dst, const uint8_t *src, size_t row_bytes, int n, uint64_t *bar,
+                             bool issue) {
+  const size_t st = tile_stride<FMT>(row_bytes);
+  if constexpr (FMT == RV_Q6_K) {
+    if (rv_bulk_ok(src, dst, (size_t)n * row_bytes)) {
+      if (issue && threadIdx.x == 0) bulk_g2s(dst, src, (uint32_t)(n * row_bytes), bar);
+      return (uint32_t)(n * row_bytes);
+    }
+    if (issue) rv_copy_bytes_block(dst, src, (size_t)n * row_bytes);
+    return 0;
+  } else {
+    if (rv_bulk_ok(src, dst, row_bytes)) {
+      if (issue && threadIdx.x == 0)
+        for (int r = 0; r < n; r++) bulk_g2s(dst + r * st, src + r * row_bytes, (uint32_t)row_bytes, bar);
+      return (uint32_t)(n * row_bytes);
+    }
+    if (issue)
+      for (size_t i = threadIdx.x; i < (size_t)n * row_bytes; i += blockDim.x)
+        dst[(i / row_bytes) * st + i % row_bytes] = src[i];
+    return 0;
+  }
+}
+
+// ------------------------------------------------- gate/up + SwiGLU + Q8_K
+// grid = (max_units, M / R).  A CTA computes rows [tile*R, tile*R+R) of
+// both gate and up of one unit's expert for all of the unit's tokens, staged
+// B.ms at a time.  G > 1: split mode (one token at a time, G lanes per row,
+// NBG blocks each); G == 1: token mode (a thread per row, up to 8 tokens in
+// flight).  2*R*G/32 warps.  Then SwiGLU with the host-libm exponential, and
+// the last of the tiles of each 256-row block quantizes that block of every
+// token.  The kernel lets the next (down) kernel launch at once.
+template <int FMT, int G, int NBG, int R>
+__global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d, MoeBufs B, MoeWeights W) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  constexpr int MT = RV_MOE_MT, RPW = 32 / G, NW = 2 * R * G / 32;
+  RV_PHASE(1, 0);
+  pdl_trigger();
   const int u = blockIdx.x, tile = blockIdx.y;
   if (u >= *B.n_units) return;
   const int4 unit = B.units[u];
   const int e = unit.x, p0 = unit.y, p1 = unit.z;
-  uint64_t *bar = (uint64_t *)sm;
+  const int ms = B.ms;
+  RV_PHASE(1, 1);
   __shared__ int s_last;
-  const size_t wtile = (size_t)R * W.gu_row_bytes;
-  uint8_t *wsm = sm + 16;                              // [2][R][row]
-  uint8_t *asm_ = wsm + ((2 * wtile + 15) & ~(size_t)15) + 16;  // [MT][act_stride]
-  float *gu = (float *)(asm_ + MT * d.act_stride + 16);        // [2][R][MT]
+  uint64_t *bar = (uint64_t *)sm;
+  const size_t st = tile_stride<FMT>(W.gu_row_bytes);
+  const size_t wtile = (size_t)R * st;
+  uint8_t *wsm = sm + 16;                                       // [2][R][st]
+  uint8_t *asm_ = wsm + ((2 * wtile + 15) & ~(size_t)15) + 16;  // [ms][act_stride]
+  int *asum = (int *)(asm_ + ms * d.act_stride);                // [ms][hb*64] (Q6_K)
+  float *gu = (float *)(asum + (FMT == RV_Q6_K ? ms * d.hb * 64 : 0));  // [2][R][MT]
   const uint8_t *blob = W.base + (size_t)e * W.stride;
-  const uint8_t *gsrc = blob + W.gate_off + (size_t)tile * wtile;
-  const uint8_t *usrc = blob + W.up_off + (size_t)tile * wtile;
-  const bool wbulk = rv_bulk_ok(gsrc, wsm, wtile) && rv_bulk_ok(usrc, wsm + wtile, wtile);
+  const uint8_t *gsrc = blob + W.gate_off + (size_t)tile * R * W.gu_row_bytes;
+  const uint8_t *usrc = blob + W.up_off + (size_t)tile * R * W.gu_row_bytes;
   const bool abulk = rv_bulk_ok(B.acts, asm_, d.act_stride);
   if (threadIdx.x == 0) mbar_init(bar, 1);
   __syncthreads();
-  if (!wbulk) {
-    rv_copy_bytes_block(wsm, gsrc, wtile);
-    rv_copy_bytes_block(wsm + wtile, usrc, wtile);
-  }
-  const int part = threadIdx.x >> 7, r = (threadIdx.x >> 3) & 15, lane = threadIdx.x & 7;
-  const uint8_t *wrow = wsm + (size_t)part * wtile + (size_t)r * W.gu_row_bytes;
+  const uint32_t wtx = stage_rows<FMT>(wsm, gsrc, W.gu_row_bytes, R, bar, false) +
+                       stage_rows<FMT>(wsm + wtile, usrc, W.gu_row_bytes, R, bar, false);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int part = warp / (NW / 2);  // warps [0, NW/2) gate, [NW/2, NW) up
+  const int rsub = lane / G, g = lane % G;
+  const int r = (warp % (NW / 2)) * RPW + rsub;  // row within the part
+  const uint8_t *wrow = wsm + (size_t)part * wtile + (size_t)r * st;
   uint32_t phase = 0;
   bool ok = true;
-  for (int c0 = p0; c0 < p1; c0 += MT) {
-    const int mt = min(MT, p1 - c0);
+  for (int c0 = p0; c0 < p1; c0 += ms) {
+    const int mt = min(ms, p1 - c0);
     __syncthreads();
-    if (threadIdx.x == 0 && (abulk || (c0 == p0 && wbulk))) {
+    const bool first = c0 == p0;
+    const uint32_t tx = (first ? wtx : 0u) + (abulk ? (uint32_t)(mt * d.act_stride) : 0u);
+    if (threadIdx.x == 0 && tx) {
       fence_proxy_async();
-      uint32_t tx = 0;
-      if (c0 == p0 && wbulk) tx += (uint32_t)(2 * wtile);
-      if (abulk) tx += (uint32_t)(mt * d.act_stride);
       mbar_arrive_expect_tx(bar, tx);
-      if (c0 == p0 && wbulk) {
-        bulk_g2s(wsm, gsrc, (uint32_t)wtile, bar);
-        bulk_g2s(wsm + wtile, usrc, (uint32_t)wtile, bar);
-      }
-      if (abulk)
-        for (int m = 0; m < mt; m++) {
-          const uint32_t tok = B.index[c0 + m] / (uint32_t)d.K;
+    }
+    if (first) {
+      stage_rows<FMT>(wsm, gsrc, W.gu_row_bytes, R, bar, true);
+      stage_rows<FMT>(wsm + wtile, usrc, W.gu_row_bytes, R, bar, true);
+    }
+    for (int m = 0; m < mt; m++) {
+      const uint32_t tok = B.index[c0 + m] / (uint32_t)d.K;
+      if (abulk) {
+        if (threadIdx.x == 0)
           bulk_g2s(asm_ + (size_t)m * d.act_stride, B.acts + (size_t)tok * d.act_stride,
                    (uint32_t)d.act_stride, bar);
-        }
-    }
-    if (!abulk)
-      for (int m = 0; m < mt; m++) {
-        const uint32_t tok = B.index[c0 + m] / (uint32_t)d.K;
+      } else {
         rv_copy_bytes_block(asm_ + (size_t)m * d.act_stride, B.acts + (size_t)tok * d.act_stride,
                             d.act_stride);
       }
-    if (abulk || (c0 == p0 && wbulk)) {
+    }
+    if (tx) {
       ok = mbar_wait_bounded(bar, phase);
       phase ^= 1;
     }
     __syncthreads();
     if (!ok) return;
-    float acc[MT], accm[MT];
-#pragma unroll
-    for (int m = 0; m < MT; m++) acc[m] = accm[m] = 0.0f;
-    for (int b = 0; b < d.hb; b++) {
-      WBlock w;
-      load_wblock<FMT>(wrow + (size_t)b * BB, lane, w);
-#pragma unroll
-      for (int m = 0; m < MT; m++)
-        if (m < mt) lane_step<FMT>(w, asm_ + (size_t)m * d.act_stride + (size_t)b * 292, lane, acc[m], accm[m]);
+    RV_PHASE(1, 2);
+    if constexpr (FMT == RV_Q6_K) {
+      for (int m = 0; m < mt; m++) act_word_sums(asm_ + (size_t)m * d.act_stride, d.hb, asum + m * d.hb * 64);
+      __syncthreads();
     }
+    for (int m0 = 0; m0 < mt; m0 += MT) {
+      const int mm = min(MT, mt - m0);
+      if constexpr (G > 1) {
+        for (int m = 0; m < mm; m++) {
+          const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.act_stride,
+                                                        asum + (m0 + m) * d.hb * 64, g);
+          if (g == G - 1) gu[(part * R + r) * MT + m] = res;
+        }
+      } else {
+        float res[MT];
+        row_dot_tokens<FMT, MT>(wrow, d.hb, asm_ + (size_t)m0 * d.act_stride, d.act_stride,
+                                asum + m0 * d.hb * 64, (size_t)d.hb * 64, mm, res);
 #pragma unroll
-    for (int m = 0; m < MT; m++) {
-      const float res = lane_reduce<FMT>(acc[m], accm[m]);
-      if (lane == 0) gu[(part * R + r) * MT + m] = res;
-    }
-    __syncthreads();
-    if (threadIdx.x < R * MT) {
-      const int rr = threadIdx.x / MT, m = threadIdx.x % MT;
-      if (m < mt) {
-        const float h = swiglu_ref(gu[rr * MT + m], gu[(R + rr) * MT + m]);
-        B.hbuf[(size_t)(c0 + m) * d.M + (size_t)tile * R + rr] = h;
+        for (int m = 0; m < MT; m++)
+          if (m < mm) gu[(part * R + r) * MT + m] = res[m];
       }
+      __syncthreads();
+      for (int i = threadIdx.x; i < R * mm; i += blockDim.x) {
+        const int rr = i / mm, m = i % mm;
+        const float h = swiglu_ref(gu[rr * MT + m], gu[(R + rr) * MT + m]);
+        B.hbuf[(size_t)(c0 + m0 + m) * d.M + (size_t)tile * R + rr] = h;
+      }
+      __syncthreads();
     }
   }
+  RV_PHASE(1, 3);
   // The last of the 256/R tiles of this 256-row block quantizes it.
   __threadfence();
   __syncthreads();
@@ -338,79 +648,142 @@ __global__ void __launch_bounds__(256) k_gate_up(MoeDims d, MoeBufs B, MoeWeight
   }
   __syncthreads();
   if (!s_last) return;
+  RV_PHASE(1, 4);
   __threadfence();
-  const int warp = threadIdx.x >> 5, wl = threadIdx.x & 31;
-  for (int pos = p0 + warp; pos < p1; pos += 8) {
+  const int nwarps = blockDim.x >> 5;
+  for (int pos = p0 + warp; pos < p1; pos += nwarps) {
     float v[8];
-    const float *src = B.hbuf + (size_t)pos * d.M + (size_t)qb * 256 + 8 * wl;
+    const float *src = B.hbuf + (size_t)pos * d.M + (size_t)qb * 256 + 8 * lane;
 #pragma unroll
     for (int k = 0; k < 8; k++) v[k] = __ldcg(src + k);
-    q8k_quantize_warp(v, wl, B.acts_moe + (size_t)pos * d.amoe_stride + (size_t)qb * 292);
+    q8k_quantize_warp(v, lane, B.acts_moe + (size_t)pos * d.amoe_stride + (size_t)qb * 292);
   }
 }
 
 // ------------------------------------------------------------- down
-// grid = (max_units, H / RV_DOWN_ROWS), block = 256 = 32 rows x 8 lanes.
-template <int FMT>
-__global__ void __launch_bounds__(256) k_down(MoeDims d, MoeBufs B, MoeWeights W) {
+// grid = (max_units, ceil(H / ROWS)), one warp per CTA (ROWS * G <= 32):
+// ROWS rows of one unit's expert for all its tokens.  Launched as a
+// programmatic dependent of k_gate_up: the weight tile (which depends only
+// on the routing) is requested before waiting for gate/up to finish.
+// With COMBINE, the last unit to finish a row tile also performs the fixed
+// top-k-order reduction and residual add for those rows of every token
+// (forward.rs:2744-2753); otherwise k_combine does it.
+template <int FMT, int G, int NBG, int ROWS, bool COMBINE>
+__global__ void __launch_bounds__(32, 16) k_down(MoeDims d, MoeBufs B, MoeWeights W) {
   extern __shared__ __align__(16) uint8_t sm[];
-  constexpr int R = RV_DOWN_ROWS, MT = RV_MOE_MT;
-  constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
+  constexpr int MT = RV_MOE_MT;
+  static_assert(ROWS * G <= 32, "one warp per CTA");
+  RV_PHASE(2, 0);
+  pdl_trigger();
   const int u = blockIdx.x, tile = blockIdx.y;
-  if (u >= *B.n_units) return;
+  const int nu = *B.n_units;
+  if (u >= nu) return;
   const int4 unit = B.units[u];
   const int e = unit.x, p0 = unit.y, p1 = unit.z;
-  uint64_t *bar = (uint64_t *)sm;
-  const size_t wtile = (size_t)R * W.down_row_bytes;
+  const int ms = B.ms;
+  const int row0 = tile * ROWS, nrows = min(ROWS, d.H - row0);
+  __shared__ int s_last;
+  uint64_t *bar = (uint64_t *)sm;  // [2]: weights, activations
+  const size_t st = tile_stride<FMT>(W.down_row_bytes);
   uint8_t *wsm = sm + 16;
-  uint8_t *asm_ = wsm + ((wtile + 15) & ~(size_t)15) + 16;
-  const uint8_t *dsrc = W.base + (size_t)e * W.stride + W.down_off + (size_t)tile * wtile;
-  const bool wbulk = rv_bulk_ok(dsrc, wsm, wtile);
+  uint8_t *asm_ = wsm + (((size_t)ROWS * st + 15) & ~(size_t)15) + 16;
+  int *asum = (int *)(asm_ + ms * d.amoe_stride);
+  const uint8_t *dsrc = W.base + (size_t)e * W.stride + W.down_off + (size_t)row0 * W.down_row_bytes;
   const bool abulk = rv_bulk_ok(B.acts_moe, asm_, d.amoe_stride);
-  if (threadIdx.x == 0) mbar_init(bar, 1);
-  __syncthreads();
-  if (!wbulk) rv_copy_bytes_block(wsm, dsrc, wtile);
-  const int r = threadIdx.x >> 3, lane = threadIdx.x & 7;
-  const uint8_t *wrow = wsm + (size_t)r * W.down_row_bytes;
+  const int lane = threadIdx.x;
+  if (lane == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
+  }
+  __syncwarp();
+  const uint32_t wtx = stage_rows<FMT>(wsm, dsrc, W.down_row_bytes, nrows, bar, false);
+  if (lane == 0 && wtx) mbar_arrive_expect_tx(bar, wtx);
+  stage_rows<FMT>(wsm, dsrc, W.down_row_bytes, nrows, bar, true);
+  RV_PHASE(2, 1);
+  pdl_wait();  // acts_moe is k_gate_up's output
+  RV_PHASE(2, 2);
+  const int rsub = lane / G, g = lane % G;
+  const bool live = rsub < ROWS && rsub < nrows;
+  const uint8_t *wrow = wsm + (size_t)(live ? rsub : 0) * st;
   uint32_t phase = 0;
   bool ok = true;
-  for (int c0 = p0; c0 < p1; c0 += MT) {
-    const int mt = min(MT, p1 - c0);
-    __syncthreads();
+  bool wdone = wtx == 0;
+  for (int c0 = p0; c0 < p1; c0 += ms) {
+    const int mt = min(ms, p1 - c0);
+    __syncwarp();
     const uint8_t *asrc = B.acts_moe + (size_t)c0 * d.amoe_stride;
-    if (threadIdx.x == 0 && (abulk || (c0 == p0 && wbulk))) {
-      fence_proxy_async();
-      uint32_t tx = 0;
-      if (c0 == p0 && wbulk) tx += (uint32_t)wtile;
-      if (abulk) tx += (uint32_t)(mt * d.amoe_stride);
-      mbar_arrive_expect_tx(bar, tx);
-      if (c0 == p0 && wbulk) bulk_g2s(wsm, dsrc, (uint32_t)wtile, bar);
-      if (abulk) bulk_g2s(asm_, asrc, (uint32_t)(mt * d.amoe_stride), bar);
+    if (abulk) {
+      if (lane == 0) {
+        fence_proxy_async();
+        mbar_arrive_expect_tx(bar + 1, (uint32_t)(mt * d.amoe_stride));
+        bulk_g2s(asm_, asrc, (uint32_t)(mt * d.amoe_stride), bar + 1);
+      }
+    } else {
+      rv_copy_bytes_block(asm_, asrc, (size_t)mt * d.amoe_stride);
     }
-    if (!abulk) rv_copy_bytes_block(asm_, asrc, (size_t)mt * d.amoe_stride);
-    if (abulk || (c0 == p0 && wbulk)) {
-      ok = mbar_wait_bounded(bar, phase);
+    if (!wdone) {
+      ok = mbar_wait_bounded(bar, 0);
+      wdone = true;
+    }
+    if (abulk) {
+      ok = ok && mbar_wait_bounded(bar + 1, phase);
       phase ^= 1;
     }
-    __syncthreads();
+    __syncwarp();
     if (!ok) return;
-    float acc[MT], accm[MT];
-#pragma unroll
-    for (int m = 0; m < MT; m++) acc[m] = accm[m] = 0.0f;
-    for (int b = 0; b < d.mb; b++) {
-      WBlock w;
-      load_wblock<FMT>(wrow + (size_t)b * BB, lane, w);
-#pragma unroll
-      for (int m = 0; m < MT; m++)
-        if (m < mt) lane_step<FMT>(w, asm_ + (size_t)m * d.amoe_stride + (size_t)b * 292, lane, acc[m], accm[m]);
+    RV_PHASE(2, 3);
+    if constexpr (FMT == RV_Q6_K) {
+      for (int m = 0; m < mt; m++) act_word_sums(asm_ + (size_t)m * d.amoe_stride, d.mb, asum + m * d.mb * 64);
+      __syncwarp();
     }
+    for (int m0 = 0; m0 < mt; m0 += MT) {
+      const int mm = min(MT, mt - m0);
+      if constexpr (G > 1) {
+        for (int m = 0; m < mm; m++) {
+          const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.amoe_stride,
+                                                        asum + (m0 + m) * d.mb * 64, g);
+          if (g == G - 1 && live) {
+            const uint32_t pair = B.index[c0 + m0 + m];
+            B.staged[(size_t)pair * d.H + row0 + rsub] = res;
+          }
+        }
+      } else {
+        float res[MT];
+        row_dot_tokens<FMT, MT>(wrow, d.mb, asm_ + (size_t)m0 * d.amoe_stride, d.amoe_stride,
+                                asum + m0 * d.mb * 64, (size_t)d.mb * 64, mm, res);
 #pragma unroll
-    for (int m = 0; m < MT; m++) {
-      const float res = lane_reduce<FMT>(acc[m], accm[m]);
-      if (lane == 0 && m < mt) {
-        const uint32_t pair = B.index[c0 + m];
-        B.staged[(size_t)pair * d.H + (size_t)tile * R + r] = res;
+        for (int m = 0; m < MT; m++)
+          if (m < mm && live) {
+            const uint32_t pair = B.index[c0 + m0 + m];
+            B.staged[(size_t)pair * d.H + row0 + rsub] = res[m];
+          }
       }
+    }
+  }
+  RV_PHASE(2, 4);
+  if constexpr (COMBINE) {
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) {
+      int *cnt = &B.down_cnt[tile];
+      const int old = atomicAdd(cnt, 1);
+      s_last = old == nu - 1;
+      if (s_last) *cnt = 0;
+    }
+    __syncwarp();
+    if (!s_last) return;
+    RV_PHASE(2, 5);
+    __threadfence();
+    // acc = 0; acc += w_k * d_k in top-k order; residual += acc.
+    for (int i = lane; i < B.T * nrows; i += 32) {
+      const int t = i / nrows, h = row0 + i % nrows;
+      float acc = 0.0f;
+      for (int k = 0; k < d.K; k++) {
+        const size_t pair = (size_t)t * d.K + k;
+        acc = __fadd_rn(acc, __fmul_rn(B.w[pair], __ldcg(B.staged + pair * d.H + h)));
+      }
+      float *res = B.residual + (size_t)t * d.H + h;
+      *res = __fadd_rn(*res, acc);
     }
   }
 }
