@@ -316,6 +316,35 @@ RV_API int rv_moe_profile_enable(rv_moe *m, size_t slots);
 RV_API int rv_moe_profile_rewind(rv_moe *m);
 RV_API int rv_moe_profile_read(rv_moe *m, float *ms_out, size_t cap, size_t *n_sets);
 
+/* ------------------------------------------- allocation-free decode */
+/* No counterpart in the reference (which never runs on a GPU): the MoE block
+ * of rv_moe_forward for callers that cannot call cudaMalloc -- a host whose
+ * device memory belongs to another allocator (a serving runtime's pool, a
+ * process under a hard memory cap) or code that runs where allocation is not
+ * allowed (a real-time decode loop, a stream being captured into a graph).
+ * Nothing is allocated: the caller passes the layer's expert blobs
+ * (device, layout->n_experts * layout->stride bytes, laid out as in
+ * rv_layer_layout) and the other inputs and outputs exactly as for
+ * rv_moe_forward (device pointers), and the intermediates live in one
+ * file-scope device array of RV_STATIC_SCRATCH_BYTES that every GPU loading
+ * the library holds until the process exits.
+ * Limits: n_tokens <= RV_STATIC_MAX_TOKENS, hidden <= 2048, moe <= 1024,
+ * n_experts <= 128, top_k <= 8; anything larger returns
+ * RV_ERR_LENGTH_MISMATCH (or RV_ERR_UNIMPLEMENTED for the geometry) before
+ * any work is queued.  The first call on each device looks up the array's
+ * device address and uploads the SiLU exception table, so make that first
+ * call before any stream capture.  Every call shares the one array and it
+ * keeps the previous call's contents (counters are cleared at the start of
+ * each call): calls that overlap on the GPU -- on two streams, or from two
+ * threads -- race and must be serialized by the caller.  Results are
+ * bit-identical to rv_moe_forward. */
+#define RV_STATIC_MAX_TOKENS 4
+#define RV_STATIC_SCRATCH_BYTES (1u << 20)
+RV_API int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_layout *layout,
+                                 const uint8_t *expert_blobs, const float *ffn_norm,
+                                 const float *router, float *residual, size_t n_tokens,
+                                 uint32_t *topk_ids, float *topk_weights, rv_stream stream);
+
 /* ------------------------------------------------ synthetic inputs */
 /* Seeded N(0, sigma^2)-like values: element i is the Irwin-Hall sum of
  * twelve 24-bit uniforms drawn from SplitMix64(seed, offset + i), so the

@@ -110,6 +110,7 @@ SIGNATURES = {
     "rv_moe_profile_enable": (I32, [P, SZ]),
     "rv_moe_profile_rewind": (I32, [P]),
     "rv_moe_profile_read": (I32, [P, P, SZ, ctypes.POINTER(SZ)]),
+    "rv_moe_forward_static": (I32, [ctypes.POINTER(MoeConfig), ctypes.POINTER(LayerLayout), P, P, P, P, SZ, P, P, P]),
     "rv_synth_normal": (I32, [U64, U64, F32, P, SZ, P]),
     "rv_quantize_weights": (I32, [I32, P, SZ, P, P]),
     "rv_expert_table_fill_synthetic": (I32, [P, U32, U64, F32, P]),

@@ -956,3 +956,136 @@ extern "C" __attribute__((visibility("default"))) int rv_debug_phase_clock(int k
   return RV_OK;
 }
 #endif
+
+// ================================================ allocation-free decode
+// The MoE block for callers that cannot allocate device memory: every
+// intermediate lives in this file-scope array.  Host code reaches it only
+// through the address cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) uint8_t g_rv_static_scratch[RV_STATIC_SCRATCH_BYTES];
+static std::mutex g_static_mu;
+static void *g_static_ptr[64];
+
+extern "C" int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_layout *L,
+                                     const uint8_t *expert_blobs, const float *ffn_norm,
+                                     const float *router, float *residual, size_t n_tokens,
+                                     uint32_t *topk_ids, float *topk_weights, rv_stream stream) {
+  if (!cfg || !L) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward_static: null config or layout");
+  if (cfg->hidden == 0 || cfg->hidden % 256 || cfg->moe == 0 || cfg->moe % 256)
+    RV_FAIL(RV_ERR_INDIVISIBLE_ROW, "hidden %u / moe %u: not multiples of 256", cfg->hidden, cfg->moe);
+  if (cfg->hidden > 2048 || cfg->moe > 1024 || cfg->n_experts == 0 || cfg->n_experts > 128 ||
+      cfg->top_k == 0 || cfg->top_k > 8 || cfg->top_k > cfg->n_experts)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED,
+            "moe_forward_static handles hidden <= 2048, moe <= 1024, n_experts <= 128, top_k <= 8");
+  if (n_tokens > RV_STATIC_MAX_TOKENS)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_forward_static: %zu tokens exceed the static limit of %d",
+            n_tokens, RV_STATIC_MAX_TOKENS);
+  int rc = check_layout(*L, 0);
+  if (rc) return rc;
+  if (L->hidden != cfg->hidden || L->moe != cfg->moe || L->n_experts != cfg->n_experts)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "layout geometry (%u, %u, %u) vs config (%u, %u, %u)", L->hidden, L->moe,
+            L->n_experts, cfg->hidden, cfg->moe, cfg->n_experts);
+  if (L->gate_format != L->up_format) RV_FAIL(RV_ERR_UNIMPLEMENTED, "gate and up in different formats");
+  if (n_tokens == 0) return RV_OK;
+  if (!expert_blobs || !ffn_norm || !router || !residual)
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward_static: null pointer");
+  if ((uintptr_t)router & 15) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward_static: router must be 16-byte aligned");
+  int dev = 0;
+  RV_CUDA(cudaGetDevice(&dev));
+  rc = ensure_device(dev);
+  if (rc) return rc;
+  uint8_t *base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_ptr[dev]) {
+      void *ptr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&ptr, g_rv_static_scratch);
+      if (e != cudaSuccess || !ptr)
+        RV_FAIL(RV_ERR_CUDA, "moe_forward_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      g_static_ptr[dev] = ptr;
+    }
+    base = (uint8_t *)g_static_ptr[dev];
+  }
+  // The same geometry and scratch carving as rv_moe_create, for
+  // RV_STATIC_MAX_TOKENS rows; counters first so one memset clears them.
+  rv_moe m;
+  m.device = dev;
+  m.cfg = *cfg;
+  m.max_tokens = RV_STATIC_MAX_TOKENS;
+  MoeDims &d = m.d;
+  d.H = (int)cfg->hidden;
+  d.M = (int)cfg->moe;
+  d.E = (int)cfg->n_experts;
+  d.K = (int)cfg->top_k;
+  d.hb = d.H / 256;
+  d.mb = d.M / 256;
+  d.act_stride = round16((size_t)d.hb * 292);
+  d.amoe_stride = round16((size_t)d.mb * 292);
+  d.eps = cfg->eps;
+  d.norm_topk = cfg->norm_topk_prob;
+  const size_t T = RV_STATIC_MAX_TOKENS, K = d.K, P = T * K;
+  m.max_units = (int)(std::min<size_t>((size_t)d.E, P) + (P + RV_MOE_TOK_CHUNK - 1) / RV_MOE_TOK_CHUNK);
+  MoeBufs &B = m.B;
+  struct Part { size_t bytes; void **slot; };
+  const Part parts[] = {
+      {(size_t)d.E * 4, (void **)&B.counts},
+      {(size_t)m.max_units * d.mb * 4, (void **)&B.tile_cnt},
+      {16, (void **)&B.route_cnt},
+      {((size_t)d.H / 8 + 1) * 4, (void **)&B.down_cnt},
+      {16, (void **)&B.n_units},
+      {T * d.H * 4, (void **)&B.normed},
+      {T * d.act_stride, (void **)&B.acts},
+      {T * d.E * 4, (void **)&B.logits},
+      {P * 4, (void **)&B.ids},
+      {P * 4, (void **)&B.w},
+      {((size_t)d.E + 1) * 4, (void **)&B.index_start},
+      {P * 4, (void **)&B.index},
+      {(size_t)m.max_units * 16, (void **)&B.units},
+      {P * d.M * 4, (void **)&B.hbuf},
+      {P * d.amoe_stride, (void **)&B.acts_moe},
+      {P * d.H * 4, (void **)&B.staged},
+  };
+  size_t off = 0, counters = 0;
+  for (size_t i = 0; i < sizeof parts / sizeof parts[0]; i++) {
+    *parts[i].slot = base + off;
+    off += (parts[i].bytes + 255) & ~(size_t)255;
+    if (i == 4) counters = off;
+  }
+  if (off > RV_STATIC_SCRATCH_BYTES)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_forward_static: needs %zu scratch bytes, has %u", off,
+            (unsigned)RV_STATIC_SCRATCH_BYTES);
+  B.max_units = m.max_units;
+  cudaStream_t s = (cudaStream_t)stream;
+  RV_CUDA(cudaMemsetAsync(base, 0, counters, s));
+  B.ffn_norm = ffn_norm;
+  B.router = router;
+  B.residual = residual;
+  B.T = (int)n_tokens;
+  B.ms = B.T < RV_MOE_MT ? B.T : RV_MOE_MT;
+  MoeWeights W;
+  W.base = expert_blobs;
+  W.stride = L->stride;
+  W.gate_off = L->gate_off;
+  W.up_off = L->up_off;
+  W.down_off = L->down_off;
+  rv_row_bytes(L->gate_format, L->hidden, &W.gu_row_bytes);
+  rv_row_bytes(L->down_format, L->moe, &W.down_row_bytes);
+  const int Tn = (int)n_tokens;
+  const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)Tn * (d.H + 4) * 4 + 4 * sizeof(double) + 16;
+  RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
+  switch (L->gate_format) {
+    case RV_Q4_K: launch_gate_up<RV_Q4_K>(&m, B, W, Tn, s); break;
+    case RV_Q5_K: launch_gate_up<RV_Q5_K>(&m, B, W, Tn, s); break;
+    default: launch_gate_up<RV_Q6_K>(&m, B, W, Tn, s); break;
+  }
+  bool combined;
+  switch (L->down_format) {
+    case RV_Q4_K: combined = launch_down<RV_Q4_K>(&m, B, W, Tn, s); break;
+    case RV_Q5_K: combined = launch_down<RV_Q5_K>(&m, B, W, Tn, s); break;
+    default: combined = launch_down<RV_Q6_K>(&m, B, W, Tn, s); break;
+  }
+  if (!combined) k_combine<<<dim3((unsigned)Tn, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
+  RV_LAUNCH_CHECK();
+  if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+  if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+  return RV_OK;
+}
