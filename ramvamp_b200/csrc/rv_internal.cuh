@@ -139,17 +139,22 @@ RV_DEVFN void rv_copy_bytes_block(uint8_t *dst, const uint8_t *src, size_t bytes
 
 // ------------------------------------------------------ phase clocks
 // Compiled out unless RV_PHASE_CLOCK is defined: thread 0 of each CTA stamps
-// clock64() at the phases of a kernel (the GPU analogue of the reference's
+// %globaltimer (ns, common to all SMs) at the phases of a kernel (the GPU analogue of the reference's
 // PhaseClock, model/prefill.rs:414-520), read back by rv_debug_phase_clock.
 #ifdef RV_PHASE_CLOCK
 #define RV_PHASE_KERNELS 3
 #define RV_PHASE_CTAS 8192
 #define RV_PHASES 10
 __device__ long long g_rv_phase[RV_PHASE_KERNELS][RV_PHASE_CTAS][RV_PHASES];
-#define RV_PHASE(k, i)                                                                     \
-  do {                                                                                    \
-    const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                            \
-    if (threadIdx.x == 0 && cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = clock64();     \
+RV_DEVFN long long rv_globaltimer() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define RV_PHASE(k, i)                                                                       \
+  do {                                                                                      \
+    const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                              \
+    if (threadIdx.x == 0 && cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = rv_globaltimer(); \
   } while (0)
 #else
 #define RV_PHASE(k, i) \
