@@ -156,7 +156,16 @@ RV_DEVFN long long rv_globaltimer() {
     const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                              \
     if (threadIdx.x == 0 && cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = rv_globaltimer(); \
   } while (0)
+// Stamp from whichever thread calls it (one thread per CTA by construction).
+#define RV_PHASE_ANY(k, i)                                                        \
+  do {                                                                           \
+    const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                   \
+    if (cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = rv_globaltimer();         \
+  } while (0)
 #else
+#define RV_PHASE_ANY(k, i) \
+  do {                   \
+  } while (0)
 #define RV_PHASE(k, i) \
   do {                 \
   } while (0)

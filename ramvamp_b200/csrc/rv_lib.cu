@@ -5,10 +5,14 @@
 #include <new>
 #include <vector>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "rv_expf.cuh"
 #include "rv_internal.cuh"
 #include "rv_kernels.cuh"
 #include "rv_moe.cuh"
+#include "rv_tc.cuh"
 
 #include "_gen/expf_exceptions.inc"
 
@@ -653,6 +657,8 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
   d.norm_topk = cfg->norm_topk_prob;
   const size_t T = max_tokens, K = d.K, P = T * K;
   m->max_units = (int)(std::min<size_t>((size_t)d.E, P) + (P + RV_MOE_TOK_CHUNK - 1) / RV_MOE_TOK_CHUNK);
+  const size_t max_tc = std::min<size_t>((size_t)d.E, P) + P / RV_TC_NT + 1;
+  const size_t padded_rows = (P + 16 * (size_t)d.E + 16 + 15) & ~(size_t)15;  // every expert's rows rounded up to 16
   // One arena for every scratch buffer the forward touches.
   struct Part { size_t bytes; void **slot; };
   MoeBufs &B = m->B;
@@ -674,6 +680,16 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
       {16, (void **)&B.route_cnt},
       {((size_t)d.H / 8 + 1) * 4, (void **)&B.down_cnt},
       {T * d.H * 4, (void **)&m->dres},
+      {padded_rows * d.H * 2, (void **)&B.xq},
+      {padded_rows * d.hb * 32, (void **)&B.xm},
+      {padded_rows * d.hb * 4, (void **)&B.xd},
+      {padded_rows * d.M * 2, (void **)&B.hq},
+      {padded_rows * d.mb * 32, (void **)&B.hm},
+      {padded_rows * d.mb * 4, (void **)&B.hdsc},
+      {P * d.M * 8, (void **)&B.gu},
+      {max_tc * 16, (void **)&B.tc_units},
+      {16, (void **)&B.n_tc},
+      {(size_t)d.E * 4, (void **)&B.tc_pstart},
   };
   size_t total = 0;
   for (const Part &p : parts) total += (p.bytes + 255) & ~(size_t)255;
@@ -693,6 +709,8 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
     off += (p.bytes + 255) & ~(size_t)255;
   }
   B.max_units = m->max_units;
+  B.max_tc = (int)max_tc;
+  B.tc_groups = (int)(padded_rows / 8);
   *out = m;
   return RV_OK;
 }
@@ -764,6 +782,70 @@ static bool launch_down(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, 
   return false;
 }
 
+// ---------------------------------------------------- tensor-core prefill
+static PFN_cuTensorMapEncodeTiled_v12000 g_tmap_encode;
+
+// The driver's tensor-map encoder, looked up once through the runtime.
+static int tmap_encoder(PFN_cuTensorMapEncodeTiled_v12000 *out) {
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (!g_tmap_encode) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+      RV_FAIL(RV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (%s)", cudaGetErrorString(e));
+    g_tmap_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  }
+  *out = g_tmap_encode;
+  return RV_OK;
+}
+
+// Tensor map over a layer's gate and up slabs as one [E][2][M][row bytes]
+// byte array (strides: row bytes, up_off - gate_off, expert stride); box =
+// one super-block column of 128 rows.
+static int gate_up_map(const MoeWeights &W, const rv_layer_layout &L, CUtensorMap *map) {
+  if (L.up_off <= L.gate_off) RV_FAIL(RV_ERR_UNIMPLEMENTED, "the tensor path needs the up slab after the gate slab");
+  PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  int rc = tmap_encoder(&enc);
+  if (rc) return rc;
+  const cuuint64_t dims[4] = {W.gu_row_bytes, L.moe, 2, L.n_experts};
+  const cuuint64_t strides[3] = {W.gu_row_bytes, L.up_off - L.gate_off, L.stride};
+  const cuuint32_t box[4] = {(cuuint32_t)rv_fmt_block_bytes(L.gate_format), RV_TC_ROWS, 1, 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void *)(W.base + L.gate_off), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) RV_FAIL(RV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return RV_OK;
+}
+
+template <int FMT, bool DOWN>
+static cudaError_t launch_tc_gemm(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, const CUtensorMap &map,
+                                  cudaStream_t s) {
+  const MoeDims &d = m->d;
+  const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
+  const size_t smem = TcCfg<FMT, DOWN>::total(rb, (DOWN ? d.M : d.H) / 256);
+  cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT, DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const unsigned gx = DOWN ? (unsigned)(d.H / RV_TC_ROWS) : (unsigned)(2 * d.M / RV_TC_ROWS);
+  k_tc_gemm<FMT, DOWN><<<dim3(gx, (unsigned)B.max_tc), RV_TC_THREADS, smem, s>>>(d, B, W, map);
+  return cudaGetLastError();
+}
+
+// Checks the tensor path's layout requirements: gate/up Q4_K or Q5_K, and
+// every super-block row start and whole down tile 16-byte aligned for the
+// bulk copies.
+static int tc_check(const rv_layer_layout &L, const MoeWeights &W, uint32_t layer) {
+  if (L.gate_format != RV_Q4_K && L.gate_format != RV_Q5_K)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "layer %u: the tensor path takes Q4_K or Q5_K gate/up (format %d)", layer,
+            L.gate_format);
+  if (!rv_fmt_is_kquant(L.down_format))
+    RV_FAIL(RV_ERR_UNSUPPORTED_FORMAT, "layer %u: down format %d", layer, L.down_format);
+  if (((uintptr_t)W.base | W.stride | W.gate_off | W.up_off | W.down_off | W.gu_row_bytes) & 15)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "layer %u: the tensor path needs 16-byte aligned expert slabs", layer);
+  return RV_OK;
+}
+
 extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t layer,
                               const float *ffn_norm, const float *router, float *residual,
                               size_t n_tokens, uint32_t *topk_ids, float *topk_weights,
@@ -779,7 +861,6 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   if (L.gate_format != L.up_format)
     RV_FAIL(RV_ERR_UNIMPLEMENTED, "layer %u: gate and up in different formats", layer);
   if (flags & ~RV_MOE_TENSOR) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
-  if (flags & RV_MOE_TENSOR) RV_FAIL(RV_ERR_UNIMPLEMENTED, "the tensor-core prefill path is not built yet");
   if (n_tokens > m->max_tokens)
     RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_forward: %zu tokens vs engine capacity %zu", n_tokens, m->max_tokens);
   if (n_tokens == 0) return RV_OK;
@@ -813,6 +894,41 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   }
   if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[0], s, evflags));
   B.ms = T < RV_MOE_MT ? T : RV_MOE_MT;
+  if (flags & RV_MOE_TENSOR) {
+    int rc = tc_check(L, W, layer);
+    if (rc) return rc;
+    const unsigned P = (unsigned)(T * d.K);
+    k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
+    const size_t rsmem = 16 + 2 * (size_t)(4 * RV_RCHUNK + 32 * (RV_RCHUNK + 4)) * 4;
+    k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, rsmem, s>>>(d, B);
+    k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
+    k_index<<<1, 1024, 0, s>>>(d, B);
+    k_tc_tiles<<<1, 256, 0, s>>>(d, B);
+    k_tc_gather<<<P, 32 * d.hb, 0, s>>>(d, B);
+    RV_LAUNCH_CHECK();
+    if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[1], s, evflags));
+    CUtensorMap gmap;
+    rc = gate_up_map(W, L, &gmap);
+    if (rc) return rc;
+    RV_CUDA((L.gate_format == RV_Q4_K ? launch_tc_gemm<RV_Q4_K, false>(m, B, W, gmap, s)
+                                      : launch_tc_gemm<RV_Q5_K, false>(m, B, W, gmap, s)));
+    k_tc_quant<<<P, 32 * d.mb, 0, s>>>(d, B);
+    RV_LAUNCH_CHECK();
+    if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[2], s, evflags));
+    switch (L.down_format) {
+      case RV_Q4_K: RV_CUDA((launch_tc_gemm<RV_Q4_K, true>(m, B, W, gmap, s))); break;
+      case RV_Q5_K: RV_CUDA((launch_tc_gemm<RV_Q5_K, true>(m, B, W, gmap, s))); break;
+      default: RV_CUDA((launch_tc_gemm<RV_Q6_K, true>(m, B, W, gmap, s))); break;
+    }
+    if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[3], s, evflags));
+    k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
+    if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[4], s, evflags));
+    RV_LAUNCH_CHECK();
+    if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+    if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+    m->last_T = T;
+    return RV_OK;
+  }
   if (T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch
     const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)T * (d.H + 4) * 4 + 4 * sizeof(double) + 16;

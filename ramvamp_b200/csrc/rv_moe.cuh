@@ -55,6 +55,17 @@ struct MoeBufs {
   int T;
   int ms;                  // activation slots per CTA pass: min(T, RV_MOE_MT)
   int max_units;
+  // tensor-core path (RV_MOE_TENSOR); null when the engine has none
+  __half *xq, *xm;         // gate/up operand B: [padded rows][H] Q8_K levels, [..][hb*16] mins operand (f16, core-matrix order)
+  float *xd;               // [padded rows][hb] Q8_K scales
+  __half *hq, *hm;         // down operand B, the same for the Q8_K of the SwiGLU rows
+  float *hdsc;             // [padded rows][mb]
+  float *gu;               // [T*K][2M] gate | up outputs, CSR order
+  int tc_groups;           // 8-row groups of the operand matrices (padded rows / 8)
+  int4 *tc_units;          // [max_tc] (expert, pos0, pos1, padded pos0)
+  int *n_tc;               // [1]
+  uint32_t *tc_pstart;     // [E] padded first row of each expert
+  int max_tc;
 };
 
 struct MoeWeights {

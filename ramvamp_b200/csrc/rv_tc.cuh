@@ -1,0 +1,656 @@
+// rv_tc.cuh -- MoE prefill on the 5th-generation tensor cores (RV_MOE_TENSOR).
+//
+// The expert contractions run as tcgen05 matrix products whose every input
+// is an exactly representable small integer, so the tensor cores return the
+// reference's per-super-block integer sums exactly:
+//   sumi      = sum_j sc_j * sum_{32} q * a      A = sc*q (Q4_K <= 945, Q5_K <= 1953),
+//                                                B = a (the Q8_K levels), both exact in f16
+//   sumi_mins = sum_j m_j * bsum32_j             one K=16 product per block:
+//                                                A = [m_j, 32 m_j], B = [bsum32_j mod 32, bsum32_j div 32]
+//   Q6_K: sc = 32*sh + sl, A_l = sl*(q-32), A_h = sh*(q-32), sumi = D_l + 32*D_h
+// (every partial sum below 2^24, so the f32 accumulators hold the integers
+// exactly).  The epilogue then applies the reference's scalar per-block float
+// step (dot.rs:96-116, 152-184): acc += d_w*d_a*sumi - dmin_w*d_a*sumi_mins,
+// in block order, with the same roundings.  Routing, SwiGLU, both Q8_K
+// quantizations and the top-k-order combine are the exact path's, so the
+// layer output equals the reference's scalar CPU path bit for bit.
+//
+// Operands are K-major in the canonical layout without swizzle: 8x8 f16 core
+// matrices of 128 contiguous bytes.  A is dequantized into shared memory by
+// four producer warps from raw super-blocks staged with bulk copies; B lives
+// in global memory already in core-matrix order (one 1 KB bulk copy per 8
+// rows per stage).  The accumulators of a super-block sit in tensor memory,
+// double-buffered so the epilogue of block b overlaps the products of
+// block b+1.  Per CTA: warp 0 stages, lane 0 of warp 1 issues tcgen05.mma
+// and commits, warps 2-5 dequantize, warps 6-13 run the epilogue.  Every
+// wait is bounded.
+#pragma once
+#include <cuda.h>
+
+#include "rv_moe.cuh"
+
+#define RV_TC_NT 128       // pair columns per tile
+#define RV_TC_ROWS 128     // weight rows per CTA (the MMA's M)
+#define RV_TC_KS 64        // K elements per shared-memory stage
+#define RV_TC_THREADS 480  // 15 warps
+#define RV_TC_PROD_WARPS 4
+#define RV_TC_EPI_WARPS 8
+
+// ------------------------------------------------------ tcgen05 wrappers
+RV_DEVFN void tc_alloc(uint32_t *dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+}
+RV_DEVFN void tc_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+RV_DEVFN void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+RV_DEVFN void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+RV_DEVFN void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, issued by one thread.
+RV_DEVFN void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar` once every MMA this thread issued so far has completed.
+RV_DEVFN void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+// 16 consecutive f32 columns of this thread's tensor-memory lane.
+RV_DEVFN void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+RV_DEVFN void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+RV_DEVFN void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, no swizzle; leading (K) byte
+// offset 128 between the two core matrices one K=16 step reads, `sbo`
+// bytes between 8-row groups; descriptor version 1 (sm_100).
+RV_DEVFN uint64_t tc_desc(uint32_t saddr, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) |
+         (1ull << 46);
+}
+// Instruction descriptor, kind::f16: A, B f16 (K-major), D f32, M = 128.
+RV_DEVFN uint32_t tc_idesc(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(RV_TC_ROWS >> 4) << 24);
+}
+// Byte offset of 16-byte chunk `chunk` (8 f16 of K) of row `row` in a tile
+// with `cpr` chunks per row.
+RV_DEVFN uint32_t tc_core_off(int row, int chunk, int cpr = 8) {
+  return (uint32_t)(((row >> 3) * cpr + chunk) * 128 + (row & 7) * 16);
+}
+
+// ------------------------------------------- integer operands in f16
+// 8 byte-sized unsigned levels (one per byte of w0, w1; < 64) -> 8 f16 of
+// (level - bias) * a, exact: 0x6400 | v is the f16 1024 + v, the bias
+// subtraction is exact, and every product is an integer of magnitude
+// <= 2048.
+RV_DEVFN uint32_t tc_h2(uint32_t bits, __half2 bias, __half2 a) {
+  __half2 x = *(__half2 *)&bits;
+  x = __hmul2(__hsub2(x, bias), a);
+  return *(uint32_t *)&x;
+}
+RV_DEVFN uint4 tc_level8(uint32_t w0, uint32_t w1, __half2 bias, __half2 a) {
+  uint4 r;
+  r.x = tc_h2(__byte_perm(w0, 0x64646464u, 0x5150), bias, a);
+  r.y = tc_h2(__byte_perm(w0, 0x64646464u, 0x5352), bias, a);
+  r.z = tc_h2(__byte_perm(w1, 0x64646464u, 0x5150), bias, a);
+  r.w = tc_h2(__byte_perm(w1, 0x64646464u, 0x5352), bias, a);
+  return r;
+}
+RV_DEVFN __half2 tc_h2i(int v) { return __float2half2_rn((float)v); }
+
+// get_scale_min_k4 (blocks.rs:127-141) for sub-block j of the 12 packed bytes.
+RV_DEVFN void tc_scale_min(const uint8_t *s, int j, int &sc, int &mn) {
+  if (j < 4) {
+    sc = s[j] & 63;
+    mn = s[j + 4] & 63;
+  } else {
+    sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+    mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+// Stage j (elements 64j..64j+63) of Q4_K/Q5_K super-block blk (16-byte
+// aligned) for row r: sub-blocks 2j (chunks 0-3) and 2j+1 (chunks 4-7),
+// value sc*q.  With mins, stage 0 also writes the row's K=16 mins operand
+// [m_0..m_7, 32 m_0..32 m_7] into a2.
+template <int FMT>
+RV_DEVFN void tc_stage_k45(const uint8_t *blk, int j, uint8_t *a, uint8_t *a2, int r) {
+  const uint8_t *s = blk + 4;
+  const __half2 bias = tc_h2i(1024);
+  const uint8_t *qs = blk + (FMT == RV_Q4_K ? 16 : 48) + 32 * j;
+  const uint4 qa = *(const uint4 *)qs, qb = *(const uint4 *)(qs + 16);
+  const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  uint32_t hq[8];
+  if constexpr (FMT == RV_Q5_K) {
+    const uint4 ha = *(const uint4 *)(blk + 16), hb = *(const uint4 *)(blk + 32);
+    hq[0] = ha.x; hq[1] = ha.y; hq[2] = ha.z; hq[3] = ha.w;
+    hq[4] = hb.x; hq[5] = hb.y; hq[6] = hb.z; hq[7] = hb.w;
+  }
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int sb = 2 * j + h;
+    int sc, mn;
+    tc_scale_min(s, sb, sc, mn);
+    const __half2 av = tc_h2i(sc);
+#pragma unroll
+    for (int cc = 0; cc < 4; cc++) {
+      uint32_t w0 = (q[2 * cc] >> (4 * h)) & 0x0F0F0F0Fu, w1 = (q[2 * cc + 1] >> (4 * h)) & 0x0F0F0F0Fu;
+      if constexpr (FMT == RV_Q5_K) {
+        w0 |= ((hq[2 * cc] >> sb) & 0x01010101u) << 4;
+        w1 |= ((hq[2 * cc + 1] >> sb) & 0x01010101u) << 4;
+      }
+      *(uint4 *)(a + tc_core_off(r, 4 * h + cc)) = tc_level8(w0, w1, bias, av);
+    }
+  }
+  if (j == 0) {
+    uint32_t m[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      int sc, mn;
+      tc_scale_min(s, k, sc, mn);
+      m[k] = (uint32_t)mn;
+    }
+    uint4 lo, hi;
+    __half2 t;
+    t = __floats2half2_rn((float)m[0], (float)m[1]); lo.x = *(uint32_t *)&t;
+    t = __floats2half2_rn((float)m[2], (float)m[3]); lo.y = *(uint32_t *)&t;
+    t = __floats2half2_rn((float)m[4], (float)m[5]); lo.z = *(uint32_t *)&t;
+    t = __floats2half2_rn((float)m[6], (float)m[7]); lo.w = *(uint32_t *)&t;
+    t = __floats2half2_rn(32.0f * m[0], 32.0f * m[1]); hi.x = *(uint32_t *)&t;
+    t = __floats2half2_rn(32.0f * m[2], 32.0f * m[3]); hi.y = *(uint32_t *)&t;
+    t = __floats2half2_rn(32.0f * m[4], 32.0f * m[5]); hi.z = *(uint32_t *)&t;
+    t = __floats2half2_rn(32.0f * m[6], 32.0f * m[7]); hi.w = *(uint32_t *)&t;
+    *(uint4 *)(a2 + tc_core_off(r, 0, 2)) = lo;
+    *(uint4 *)(a2 + tc_core_off(r, 1, 2)) = hi;
+  }
+}
+
+// Stage j of a Q6_K super-block at any even address (rows of a whole-tile
+// copy are 630 bytes apart; words go through ld32u) for row r: groups
+// g = 2(j&1), 2(j&1)+1 of half j>>1, values sl*(q-32) into a and
+// sh*(q-32) into ah, sc = 32*sh + sl.
+RV_DEVFN void tc_stage_q6(const uint8_t *blk, int j, uint8_t *a, uint8_t *ah, int r) {
+  const int hh = j >> 1;
+  const __half2 bias = tc_h2i(1056);  // 1024 + 32
+  const uint8_t *qh = blk + 128 + 32 * hh;
+#pragma unroll
+  for (int gi = 0; gi < 2; gi++) {
+    const int g = 2 * (j & 1) + gi;
+    const uint8_t *ql = blk + 64 * hh + 32 * (g & 1);
+    const int lsh = 4 * (g >> 1), hsh = 2 * g;
+    const int s0 = (int8_t)blk[192 + 8 * hh + 2 * g], s1 = (int8_t)blk[192 + 8 * hh + 2 * g + 1];
+    const __half2 l0 = tc_h2i(s0 & 31), h0 = tc_h2i(s0 >> 5), l1 = tc_h2i(s1 & 31), h1 = tc_h2i(s1 >> 5);
+#pragma unroll
+    for (int cc = 0; cc < 4; cc++) {
+      const uint32_t x0 = ld32u(ql + 8 * cc), x1 = ld32u(ql + 8 * cc + 4);
+      const uint32_t y0 = ld32u(qh + 8 * cc), y1 = ld32u(qh + 8 * cc + 4);
+      const uint32_t w0 = ((x0 >> lsh) & 0x0F0F0F0Fu) | (((y0 >> hsh) & 0x03030303u) << 4);
+      const uint32_t w1 = ((x1 >> lsh) & 0x0F0F0F0Fu) | (((y1 >> hsh) & 0x03030303u) << 4);
+      const uint32_t off = tc_core_off(r, 4 * gi + cc);
+      *(uint4 *)(a + off) = tc_level8(w0, w1, bias, cc < 2 ? l0 : l1);
+      *(uint4 *)(ah + off) = tc_level8(w0, w1, bias, cc < 2 ? h0 : h1);
+    }
+  }
+}
+
+// -------------------------------------------------------------- tiles
+// Work list of the tensor path: (expert, pos0, pos1, padded pos0) with at
+// most RV_TC_NT positions each, and per expert the padded first row of its
+// positions in the operand matrices (every expert starts on a multiple of 16
+// so tiles cover whole 8-row core-matrix groups).  One CTA of 256 threads.
+__global__ void __launch_bounds__(256) k_tc_tiles(MoeDims d, MoeBufs B) {
+  __shared__ int s_t[256], s_p[256];
+  const int e = threadIdx.x;
+  const int cnt = e < d.E ? (int)(B.index_start[e + 1] - B.index_start[e]) : 0;
+  const int nt = (cnt + RV_TC_NT - 1) / RV_TC_NT, np = (cnt + 15) & ~15;
+  s_t[e] = nt;
+  s_p[e] = np;
+  __syncthreads();
+  for (int o = 1; o < 256; o <<= 1) {  // inclusive scans
+    const int t = e >= o ? s_t[e - o] : 0, p = e >= o ? s_p[e - o] : 0;
+    __syncthreads();
+    s_t[e] += t;
+    s_p[e] += p;
+    __syncthreads();
+  }
+  const int t0 = s_t[e] - nt, pp0 = s_p[e] - np;
+  if (e < d.E) {
+    B.tc_pstart[e] = (uint32_t)pp0;
+    const int p0 = (int)B.index_start[e];
+    for (int k = 0; k < nt; k++)
+      if (t0 + k < B.max_tc)
+        B.tc_units[t0 + k] = make_int4(e, p0 + k * RV_TC_NT, p0 + min(cnt, (k + 1) * RV_TC_NT), pp0 + k * RV_TC_NT);
+  }
+  if (e == 255) {
+    if (s_t[255] > B.max_tc) rv_dev_fail(RV_ERR_LENGTH_MISMATCH);
+    *B.n_tc = min(s_t[255], B.max_tc);
+  }
+}
+
+// Padded row of CSR position pos (binary search for its expert).
+RV_DEVFN uint32_t tc_padded(const MoeDims &d, const MoeBufs &B, uint32_t pos) {
+  int lo = 0, hi = d.E;  // index_start[lo] <= pos < index_start[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (B.index_start[mid] <= pos) lo = mid;
+    else hi = mid;
+  }
+  return B.tc_pstart[lo] + (pos - B.index_start[lo]);
+}
+
+// Operand B in global memory is stage-major, so that one stage of a tile
+// (8-row groups g0.. g0+ng, K elements 64*it.. 64*it+63) is one contiguous
+// run of ng KB: f16 element (row pp, k) of a matrix with G 8-row groups
+// sits at ((it*G + pp/8)*8 + chunk)*64 + (pp%8)*8 + k%8, it = k/64,
+// chunk = (k%64)/8.  The K=16 mins operand of super-block b: ((b*G +
+// pp/8)*2 + j/8)*64 + (pp%8)*8 + j%8.
+RV_DEVFN size_t tc_bidx(uint32_t pp, int k, int G) {
+  return ((((size_t)(k >> 6) * G + (pp >> 3)) * 8 + ((k >> 3) & 7)) << 6) + ((pp & 7) << 3) + (k & 7);
+}
+RV_DEVFN size_t tc_midx(uint32_t pp, int b, int j, int G) {
+  return ((((size_t)b * G + (pp >> 3)) * 2 + (j >> 3)) << 6) + ((pp & 7) << 3) + (j & 7);
+}
+
+// One warp: Q8_K block b (of nb) -> the B operands of padded row pp: the 256
+// levels as f16 (8 per lane), the K=16 mins operand [bsum32 mod 32,
+// bsum32 div 32] and the block scale d.
+RV_DEVFN void tc_q8k_operands(const uint8_t *blk, int b, int nb, int G, int lane, __half *q, __half *m, float *dsc,
+                              uint32_t pp) {
+  const uint32_t w0 = *(const uint32_t *)(blk + 4 + 8 * lane), w1 = *(const uint32_t *)(blk + 8 + 8 * lane);
+  uint4 o;
+  __half2 h;
+  h = __floats2half2_rn((float)(int8_t)w0, (float)(int8_t)(w0 >> 8)); o.x = *(uint32_t *)&h;
+  h = __floats2half2_rn((float)(int8_t)(w0 >> 16), (float)(int8_t)(w0 >> 24)); o.y = *(uint32_t *)&h;
+  h = __floats2half2_rn((float)(int8_t)w1, (float)(int8_t)(w1 >> 8)); o.z = *(uint32_t *)&h;
+  h = __floats2half2_rn((float)(int8_t)(w1 >> 16), (float)(int8_t)(w1 >> 24)); o.w = *(uint32_t *)&h;
+  *(uint4 *)(q + tc_bidx(pp, b * 256 + 8 * lane, G)) = o;
+  if (lane < 8) {
+    const int16_t *bs = (const int16_t *)(blk + 260);
+    const int s32 = (int)bs[2 * lane] + (int)bs[2 * lane + 1];
+    m[tc_midx(pp, b, lane, G)] = __float2half_rn((float)(s32 & 31));
+    m[tc_midx(pp, b, 8 + lane, G)] = __float2half_rn((float)(s32 >> 5));
+  }
+  if (lane == 0) dsc[(size_t)pp * nb + b] = *(const float *)blk;
+}
+
+// Gate/up operand B: the Q8_K row of each position's token.  grid = T*K
+// CTAs of hb warps.
+__global__ void k_tc_gather(MoeDims d, MoeBufs B) {
+  const uint32_t pos = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t tok = B.index[pos] / (uint32_t)d.K;
+  const uint32_t pp = tc_padded(d, B, pos);
+  for (int b = warp; b < d.hb; b += blockDim.x >> 5)
+    tc_q8k_operands(B.acts + (size_t)tok * d.act_stride + (size_t)b * 292, b, d.hb, B.tc_groups, lane, B.xq, B.xm,
+                    B.xd, pp);
+}
+
+// SwiGLU of each position's gate and up rows (the exact path's
+// swiglu_ref), the reference's Q8_K of the result (acts_moe, bit-identical
+// to the exact path) and the down operand B.  grid = T*K CTAs of mb warps.
+__global__ void k_tc_quant(MoeDims d, MoeBufs B) {
+  const uint32_t pos = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t pp = tc_padded(d, B, pos);
+  const float *g = B.gu + (size_t)pos * 2 * d.M, *u = g + d.M;
+  for (int b = warp; b < d.mb; b += blockDim.x >> 5) {
+    float v[8];
+    const int k0 = b * 256 + 8 * lane;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      v[k] = swiglu_ref(g[k0 + k], u[k0 + k]);
+      B.hbuf[(size_t)pos * d.M + k0 + k] = v[k];
+    }
+    uint8_t *blk = B.acts_moe + (size_t)pos * d.amoe_stride + (size_t)b * 292;
+    q8k_quantize_warp(v, lane, blk);
+    __syncwarp();
+    tc_q8k_operands(blk, b, d.mb, B.tc_groups, lane, B.hq, B.hm, B.hdsc, pp);
+  }
+}
+
+// ----------------------------------------------------- the GEMM kernel
+template <int FMT>
+struct TcFmt {
+  static constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
+  static constexpr bool MINS = FMT != RV_Q6_K;   // second accumulator: sumi_mins
+  static constexpr bool SPLIT = FMT == RV_Q6_K;  // second accumulator: the sh part of the scale
+};
+// One A stage: A (16 KB), then A_h (Q6_K) or the K=16 mins operand A2.
+template <int FMT>
+struct TcStage {
+  static constexpr size_t a = 0;
+  static constexpr size_t ah = RV_TC_ROWS * 128;
+  static constexpr size_t a2 = ah;
+  static constexpr size_t bytes = ah + (TcFmt<FMT>::SPLIT ? RV_TC_ROWS * 128 : RV_TC_ROWS * 32);
+};
+// Per-kernel shape: A stages, raw weight slots, activation ring bytes.
+// Shared layout from a 1 KB aligned base: [SA] A stages | raw slots |
+// activation ring | s_da [NT][nb] | s_pair [NT] | barriers | tmem address.
+template <int FMT, bool DOWN>
+struct TcCfg {
+  static constexpr int SA = FMT == RV_Q6_K ? 2 : 3;
+  static constexpr int R = DOWN ? 1 : 3;
+  static constexpr int SBMAX = 16;
+  static constexpr size_t RING = (DOWN && FMT == RV_Q6_K) ? 48 * 1024 : 64 * 1024;
+  static constexpr size_t raw = (size_t)SA * TcStage<FMT>::bytes;
+  __host__ __device__ static size_t raw_slot(size_t row_bytes) {
+    return DOWN ? ((RV_TC_ROWS * row_bytes + 16 + 1023) & ~(size_t)1023)
+                : (((size_t)RV_TC_ROWS * TcFmt<FMT>::BB + 1023) & ~(size_t)1023);
+  }
+  __host__ __device__ static size_t ring(size_t rb) { return raw + R * raw_slot(rb); }
+  __host__ __device__ static size_t da(size_t rb) { return ring(rb) + RING; }
+  __host__ __device__ static size_t pair(size_t rb, int nb) { return da(rb) + (size_t)RV_TC_NT * nb * 4; }
+  __host__ __device__ static size_t bars(size_t rb, int nb) { return pair(rb, nb) + RV_TC_NT * 4; }
+  static constexpr int NBARS = 2 * R + 2 * SA + 2 * SBMAX + 4;
+  __host__ __device__ static size_t total(size_t rb, int nb) { return 1024 + bars(rb, nb) + NBARS * 8 + 16; }
+};
+
+RV_DEVFN bool tc_wait_warp(uint64_t *bar, uint32_t parity) {
+  const bool ok = mbar_wait_bounded(bar, parity);
+  return __all_sync(RV_FULL, ok);
+}
+// 4-D tiled TMA load (no multicast) of the box at (x, y, z, w).
+RV_DEVFN void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z, int w, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(smem_addr(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar))
+      : "memory");
+}
+
+#define RV_TC_W_PROD 3  // warps 3-6: producers
+#define RV_TC_W_EPI 7   // warps 7-14: epilogue
+
+// One pair tile x 128 weight rows of one matrix.  Gate/up (DOWN = false):
+// grid.x = 2*M/128 row tiles (gate tiles first), output rows of gu
+// [pos][gate M | up M]; the raw super-blocks arrive one 128-row x 1-block
+// box per block through `wmap` (the layer's [E][gate|up][M][row bytes]
+// slabs).  Down: grid.x = H/128, the whole contiguous 128-row tile in one
+// bulk copy, output staged by (token, slot).  grid.y = max_tc pair tiles.
+// Roles: warp 0 lane 0 stages weights, warp 1 lane 0 issues the MMAs,
+// warp 2 lane 0 stages activations, warps 3-6 dequantize, 7-14 epilogue.
+template <int FMT, bool DOWN>
+__global__ void __launch_bounds__(RV_TC_THREADS, 1)
+    k_tc_gemm(MoeDims d, MoeBufs B, MoeWeights W, const __grid_constant__ CUtensorMap wmap) {
+  using F = TcFmt<FMT>;
+  using SL = TcStage<FMT>;
+  using C = TcCfg<FMT, DOWN>;
+  constexpr int BB = F::BB, SA = C::SA, R = C::R;
+  extern __shared__ __align__(16) uint8_t sm_raw_[];
+  uint8_t *sm = (uint8_t *)(((uintptr_t)sm_raw_ + 1023) & ~(uintptr_t)1023);
+  const int u = blockIdx.y;
+  if (u >= *B.n_tc) return;
+  constexpr int PK = DOWN ? 2 : 1;
+  (void)PK;
+  RV_PHASE(PK, 0);
+  const int4 tile = B.tc_units[u];
+  const int e = tile.x, p0 = tile.y, n = tile.z - tile.y, pp0 = tile.w;
+  const int nmma = (n + 15) & ~15, ng = nmma / 8, g0 = pp0 / 8;
+  const int kdim = DOWN ? d.M : d.H, nb = kdim / 256, NS = 4 * nb;
+  const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
+  const size_t slot_b = (size_t)nmma * (128 + (F::MINS ? 32 : 0));
+  const int SB = min(C::SBMAX, (int)(C::RING / slot_b));
+  int mat = 0, row0;
+  if constexpr (DOWN) {
+    row0 = blockIdx.x * RV_TC_ROWS;
+  } else {
+    const int rtm = d.M / RV_TC_ROWS;
+    mat = blockIdx.x / rtm;
+    row0 = (blockIdx.x % rtm) * RV_TC_ROWS;
+  }
+  const uint8_t *wsrc = W.base + (size_t)e * W.stride + (DOWN ? W.down_off : mat ? W.up_off : W.gate_off) +
+                        (size_t)row0 * rb;
+  const uint8_t *bq = (const uint8_t *)(DOWN ? B.hq : B.xq), *bm = (const uint8_t *)(DOWN ? B.hm : B.xm);
+  const float *bd = DOWN ? B.hdsc : B.xd;
+  const size_t rslot = C::raw_slot(rb);
+  uint8_t *raw = sm + C::raw, *ring = sm + C::ring(rb);
+  float *s_da = (float *)(sm + C::da(rb));
+  uint32_t *s_pair = (uint32_t *)(sm + C::pair(rb, nb));
+  uint64_t *bars = (uint64_t *)(sm + C::bars(rb, nb));
+  uint64_t *raw_full = bars, *raw_empty = bars + R, *a_full = bars + 2 * R, *a_empty = a_full + SA,
+           *b_full = a_empty + SA, *b_empty = b_full + C::SBMAX, *acc_full = b_empty + C::SBMAX,
+           *acc_empty = acc_full + 2;
+  uint32_t *s_tmem = (uint32_t *)(bars + C::NBARS);
+  volatile int *s_fail = (volatile int *)(s_tmem + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < R; i++) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], RV_TC_PROD_WARPS);
+    }
+    for (int i = 0; i < SA; i++) {
+      mbar_init(&a_full[i], RV_TC_PROD_WARPS);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < C::SBMAX; i++) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], RV_TC_EPI_WARPS);
+    }
+    *s_fail = 0;
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tc_alloc(s_tmem, 4 * RV_TC_NT);
+    tc_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  RV_PHASE(PK, 1);
+
+  if (warp == 0) {
+    // ------------------------------------------------ weight staging
+    if (lane == 0) {
+      bool ok = true;
+      if constexpr (DOWN) {
+        const size_t tb = (size_t)RV_TC_ROWS * rb;
+        mbar_arrive_expect_tx(&raw_full[0], (uint32_t)tb);
+        for (size_t o = 0; o < tb; o += 32768)
+          bulk_g2s(raw + o, wsrc + o, (uint32_t)(tb - o < 32768 ? tb - o : 32768), &raw_full[0]);
+      } else {
+        for (int b = 0; b < nb; b++) {
+          const int slot = b % R;
+          if (!mbar_wait_bounded(&raw_empty[slot], ((b / R) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(RV_TC_ROWS * BB));
+          tma_load_4d(raw + slot * rslot, &wmap, b * BB, row0, mat, e, &raw_full[slot]);
+          if (b == 0) RV_PHASE_ANY(PK, 2);
+        }
+      }
+      if (!ok) *s_fail = 1;
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // -------------------------------------------- activation staging
+    if (lane == 0) {
+      bool ok = true;
+      for (int it = 0; it < NS; it++) {
+        const int sb = it % SB;
+        if (!mbar_wait_bounded(&b_empty[sb], ((it / SB) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        const bool mins = F::MINS && (it & 3) == 0;
+        uint8_t *dst = ring + sb * slot_b;
+        mbar_arrive_expect_tx(&b_full[sb], (uint32_t)(ng * 1024 + (mins ? ng * 256 : 0)));
+        bulk_g2s(dst, bq + ((size_t)it * B.tc_groups + g0) * 1024, (uint32_t)(ng * 1024), &b_full[sb]);
+        if (mins)
+          bulk_g2s(dst + (size_t)nmma * 128, bm + ((size_t)(it >> 2) * B.tc_groups + g0) * 256, (uint32_t)(ng * 256),
+                   &b_full[sb]);
+      }
+      if (!ok) *s_fail = 1;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      const uint32_t idesc = tc_idesc(nmma);
+      bool ok = true;
+      for (int b = 0; b < nb && ok; b++) {
+        const int slot = b & 1;
+        if (!mbar_wait_bounded(&acc_empty[slot], ((b >> 1) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d1 = tmem + (uint32_t)(slot * 2 * RV_TC_NT), d2 = d1 + RV_TC_NT;
+        for (int j = 0; j < 4; j++) {
+          const int it = 4 * b + j, sa = it % SA, sb = it % SB;
+          if (!mbar_wait_bounded(&a_full[sa], (it / SA) & 1) || !mbar_wait_bounded(&b_full[sb], (it / SB) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (it == 0) RV_PHASE_ANY(PK, 3);
+          const uint32_t as = smem_addr(sm + (size_t)sa * SL::bytes), bs = smem_addr(ring + sb * slot_b);
+          if (F::MINS && j == 0)
+            tc_mma_f16(d2, tc_desc(as + SL::a2, 256), tc_desc(bs + nmma * 128, 256), idesc, 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++) {
+            const uint32_t acc = (j | kk) != 0;
+            tc_mma_f16(d1, tc_desc(as + SL::a + kk * 256, 1024), tc_desc(bs + kk * 256, 1024), idesc, acc);
+            if (F::SPLIT)
+              tc_mma_f16(d2, tc_desc(as + SL::ah + kk * 256, 1024), tc_desc(bs + kk * 256, 1024), idesc, acc);
+          }
+          tc_commit(&a_empty[sa]);
+          tc_commit(&b_empty[sb]);
+        }
+        tc_commit(&acc_full[slot]);
+      }
+      RV_PHASE_ANY(PK, 4);
+      if (!ok) *s_fail = 1;
+    }
+    __syncwarp();
+  } else if (warp < RV_TC_W_EPI) {
+    // ------------------------------------------------------ producers
+    const int r = threadIdx.x - 32 * RV_TC_W_PROD;
+    bool ok = true;
+    if (DOWN) ok = tc_wait_warp(&raw_full[0], 0);
+    for (int it = 0; it < NS && ok; it++) {
+      const int b = it >> 2, j = it & 3, sa = it % SA;
+      if (!DOWN && j == 0 && !tc_wait_warp(&raw_full[b % R], (b / R) & 1)) {
+        ok = false;
+        break;
+      }
+      if (!tc_wait_warp(&a_empty[sa], ((it / SA) & 1) ^ 1)) {
+        ok = false;
+        break;
+      }
+      if (it == 0 && r == 0) RV_PHASE_ANY(PK, 5);
+      const uint8_t *blk = DOWN ? raw + (size_t)r * rb + (size_t)b * BB : raw + (b % R) * rslot + (size_t)r * BB;
+      uint8_t *st = sm + (size_t)sa * SL::bytes;
+      if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, st + SL::a, st + SL::ah, r);
+      else tc_stage_k45<FMT>(blk, j, st + SL::a, st + SL::a2, r);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[sa]);
+        if (!DOWN && j == 3) mbar_arrive(&raw_empty[b % R]);
+      }
+    }
+    if (r == 0) RV_PHASE_ANY(PK, 6);
+    if (!ok) *s_fail = 1;
+  } else {
+    // ------------------------------------------------------- epilogue
+    // Thread (quadrant q, lane) owns weight row 32q + lane (its tensor-
+    // memory lane) and columns [64*half, 64*half + 64) of the tile.
+    const int et = threadIdx.x - 32 * RV_TC_W_EPI;
+    for (int i = et; i < nmma * nb; i += 32 * RV_TC_EPI_WARPS) s_da[i] = bd[(size_t)pp0 * nb + i];
+    if (DOWN)
+      for (int i = et; i < n; i += 32 * RV_TC_EPI_WARPS) s_pair[i] = B.index[p0 + i];
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * RV_TC_EPI_WARPS) : "memory");
+    const int q = warp & 3, half = (warp - RV_TC_W_EPI) >> 2;
+    const int r = 32 * q + lane;
+    const uint8_t *hrow = wsrc + (size_t)r * rb;  // the row's super-block headers (global)
+    float acc[4][16];
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+#pragma unroll
+      for (int i = 0; i < 16; i++) acc[c][i] = 0.0f;
+    bool ok = true;
+    uint32_t hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + 208) : *(const uint32_t *)hrow;
+    for (int b = 0; b < nb; b++) {
+      const int slot = b & 1;
+      const uint32_t hdr = hdr_next;
+      if (b + 1 < nb)
+        hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + (size_t)(b + 1) * BB + 208)
+                                  : *(const uint32_t *)(hrow + (size_t)(b + 1) * BB);
+      const float dw = h2f((uint16_t)(hdr & 0xFFFFu)), dmw = h2f((uint16_t)(hdr >> 16));
+      if (!tc_wait_warp(&acc_full[slot], (b >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (b == 0 && et == 0) RV_PHASE_ANY(PK, 7);
+      const uint32_t t1 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(slot * 2 * RV_TC_NT);
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const int col = 64 * half + 16 * c;
+        if (col < nmma) {
+          uint32_t v1[16], v2[16];
+          tc_ld16(t1 + (uint32_t)col, v1);
+          tc_ld16(t1 + (uint32_t)(RV_TC_NT + col), v2);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const float da = s_da[(col + i) * nb + b];
+            float blocksum;
+            if constexpr (FMT == RV_Q6_K) {
+              const int sumi = __float2int_rn(__uint_as_float(v1[i])) + 32 * __float2int_rn(__uint_as_float(v2[i]));
+              blocksum = __fmul_rn(__fmul_rn(dw, da), __int2float_rn(sumi));
+            } else {
+              const float dd = __fmul_rn(dw, da), dm = __fmul_rn(dmw, da);
+              blocksum = __fsub_rn(__fmul_rn(dd, __uint_as_float(v1[i])), __fmul_rn(dm, __uint_as_float(v2[i])));
+            }
+            acc[c][i] = __fadd_rn(acc[c][i], blocksum);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[slot]);
+    }
+    if (et == 0) RV_PHASE_ANY(PK, 8);
+    if (ok && !*s_fail) {
+#pragma unroll
+      for (int c = 0; c < 4; c++)
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int col = 64 * half + 16 * c + i;
+          if (col < n) {
+            if constexpr (DOWN) B.staged[(size_t)s_pair[col] * d.H + row0 + r] = acc[c][i];
+            else B.gu[(size_t)(p0 + col) * 2 * d.M + (size_t)mat * d.M + row0 + r] = acc[c][i];
+          }
+        }
+    }
+    if (!ok) *s_fail = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tc_dealloc(tmem, 4 * RV_TC_NT);
+  }
+  RV_PHASE(PK, 9);
+}
