@@ -142,7 +142,7 @@ RV_DEVFN void rv_copy_bytes_block(uint8_t *dst, const uint8_t *src, size_t bytes
 // %globaltimer (ns, common to all SMs) at the phases of a kernel (the GPU analogue of the reference's
 // PhaseClock, model/prefill.rs:414-520), read back by rv_debug_phase_clock.
 #ifdef RV_PHASE_CLOCK
-#define RV_PHASE_KERNELS 3
+#define RV_PHASE_KERNELS 5  // 3, 4: per-stage traces of one tensor-GEMM CTA
 #define RV_PHASE_CTAS 8192
 #define RV_PHASES 10
 __device__ long long g_rv_phase[RV_PHASE_KERNELS][RV_PHASE_CTAS][RV_PHASES];
@@ -162,7 +162,17 @@ RV_DEVFN long long rv_globaltimer() {
     const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                   \
     if (cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = rv_globaltimer();         \
   } while (0)
+// Per-stage event trace of one CTA (blockIdx.x == 0, blockIdx.y == 20):
+// row `stage` of kernel slot k.
+#define RV_TRACE(k, stage, ev)                                                          \
+  do {                                                                                 \
+    if (blockIdx.x == 0 && blockIdx.y == 20 && (stage) < RV_PHASE_CTAS)                \
+      g_rv_phase[k][stage][ev] = rv_globaltimer();                                     \
+  } while (0)
 #else
+#define RV_TRACE(k, stage, ev) \
+  do {                         \
+  } while (0)
 #define RV_PHASE_ANY(k, i) \
   do {                   \
   } while (0)

@@ -820,16 +820,22 @@ static int gate_up_map(const MoeWeights &W, const rv_layer_layout &L, CUtensorMa
 }
 
 template <int FMT, bool DOWN>
-static cudaError_t launch_tc_gemm(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, const CUtensorMap &map,
-                                  cudaStream_t s) {
+static int launch_tc_gemm(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, const CUtensorMap &map,
+                          cudaStream_t s) {
   const MoeDims &d = m->d;
   const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
   const size_t smem = TcCfg<FMT, DOWN>::total(rb, (DOWN ? d.M : d.H) / 256);
-  cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT, DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+  RV_CUDA(cudaFuncSetAttribute(k_tc_gemm<FMT, DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const unsigned gx = DOWN ? (unsigned)(d.H / RV_TC_ROWS) : (unsigned)(2 * d.M / RV_TC_ROWS);
   k_tc_gemm<FMT, DOWN><<<dim3(gx, (unsigned)B.max_tc), RV_TC_THREADS, smem, s>>>(d, B, W, map);
-  return cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa = {};
+    cudaFuncGetAttributes(&fa, k_tc_gemm<FMT, DOWN>);
+    RV_FAIL(RV_ERR_CUDA, "k_tc_gemm launch failed: %s (%d registers, at most %d threads, %zu bytes of shared memory)",
+            cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, smem);
+  }
+  return RV_OK;
 }
 
 // Checks the tensor path's layout requirements: gate/up Q4_K or Q5_K, and
@@ -910,16 +916,18 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
     CUtensorMap gmap;
     rc = gate_up_map(W, L, &gmap);
     if (rc) return rc;
-    RV_CUDA((L.gate_format == RV_Q4_K ? launch_tc_gemm<RV_Q4_K, false>(m, B, W, gmap, s)
-                                      : launch_tc_gemm<RV_Q5_K, false>(m, B, W, gmap, s)));
+    rc = L.gate_format == RV_Q4_K ? launch_tc_gemm<RV_Q4_K, false>(m, B, W, gmap, s)
+                                  : launch_tc_gemm<RV_Q5_K, false>(m, B, W, gmap, s);
+    if (rc) return rc;
     k_tc_quant<<<P, 32 * d.mb, 0, s>>>(d, B);
     RV_LAUNCH_CHECK();
     if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[2], s, evflags));
     switch (L.down_format) {
-      case RV_Q4_K: RV_CUDA((launch_tc_gemm<RV_Q4_K, true>(m, B, W, gmap, s))); break;
-      case RV_Q5_K: RV_CUDA((launch_tc_gemm<RV_Q5_K, true>(m, B, W, gmap, s))); break;
-      default: RV_CUDA((launch_tc_gemm<RV_Q6_K, true>(m, B, W, gmap, s))); break;
+      case RV_Q4_K: rc = launch_tc_gemm<RV_Q4_K, true>(m, B, W, gmap, s); break;
+      case RV_Q5_K: rc = launch_tc_gemm<RV_Q5_K, true>(m, B, W, gmap, s); break;
+      default: rc = launch_tc_gemm<RV_Q6_K, true>(m, B, W, gmap, s); break;
     }
+    if (rc) return rc;
     if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[3], s, evflags));
     k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
     if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[4], s, evflags));

@@ -32,9 +32,8 @@
 #define RV_TC_NT 128       // pair columns per tile
 #define RV_TC_ROWS 128     // weight rows per CTA (the MMA's M)
 #define RV_TC_KS 64        // K elements per shared-memory stage
-#define RV_TC_THREADS 480  // 15 warps
-#define RV_TC_PROD_WARPS 4
-#define RV_TC_EPI_WARPS 8
+#define RV_TC_THREADS 576  // 18 warps: 5 per scheduler at 96 registers fills its 16K-register file
+#define RV_TC_WORK_WARPS 16
 
 // ------------------------------------------------------ tcgen05 wrappers
 RV_DEVFN void tc_alloc(uint32_t *dst, uint32_t ncols) {
@@ -70,6 +69,12 @@ RV_DEVFN void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
 }
+// 8 consecutive f32 columns of this thread's tensor-memory lane.
+RV_DEVFN void tc_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+}
 RV_DEVFN void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 RV_DEVFN void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
@@ -93,117 +98,102 @@ RV_DEVFN uint32_t tc_core_off(int row, int chunk, int cpr = 8) {
 }
 
 // ------------------------------------------- integer operands in f16
-// 8 byte-sized unsigned levels (one per byte of w0, w1; < 64) -> 8 f16 of
-// (level - bias) * a, exact: 0x6400 | v is the f16 1024 + v, the bias
-// subtraction is exact, and every product is an integer of magnitude
-// <= 2048.
-RV_DEVFN uint32_t tc_h2(uint32_t bits, __half2 bias, __half2 a) {
+// Inside every 8-element chunk of K the operands hold elements in the order
+// PI = {0, 2, 1, 3, 4, 6, 5, 7} (the same for A and B, so the products are
+// unchanged): a 32-bit word of four byte-sized levels then turns into two
+// half2 (levels 0,2 and 1,3) with one mask each.  0x6400 | v is the f16
+// 1024 + v, and one fused multiply-add (1024 + v)*s - 1024*s gives v*s
+// exactly, because that integer is representable (|v*s| <= 2048) and
+// 1024*s is too.
+RV_DEVFN uint32_t tc_fma2(uint32_t bits, __half2 s, __half2 c) {
   __half2 x = *(__half2 *)&bits;
-  x = __hmul2(__hsub2(x, bias), a);
+  x = __hfma2(x, s, c);
   return *(uint32_t *)&x;
 }
-RV_DEVFN uint4 tc_level8(uint32_t w0, uint32_t w1, __half2 bias, __half2 a) {
-  uint4 r;
-  r.x = tc_h2(__byte_perm(w0, 0x64646464u, 0x5150), bias, a);
-  r.y = tc_h2(__byte_perm(w0, 0x64646464u, 0x5352), bias, a);
-  r.z = tc_h2(__byte_perm(w1, 0x64646464u, 0x5150), bias, a);
-  r.w = tc_h2(__byte_perm(w1, 0x64646464u, 0x5352), bias, a);
-  return r;
-}
 RV_DEVFN __half2 tc_h2i(int v) { return __float2half2_rn((float)v); }
-
-// get_scale_min_k4 (blocks.rs:127-141) for sub-block j of the 12 packed bytes.
-RV_DEVFN void tc_scale_min(const uint8_t *s, int j, int &sc, int &mn) {
-  if (j < 4) {
-    sc = s[j] & 63;
-    mn = s[j + 4] & 63;
-  } else {
-    sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
-    mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-  }
+// Levels at bits [0,6) and [16,22) of x -> half2 of level*s.
+RV_DEVFN uint32_t tc_lv2(uint32_t x, uint32_t mask, __half2 s, __half2 c) {
+  return tc_fma2((x & mask) | 0x64006400u, s, c);
 }
 
-// Stage j (elements 64j..64j+63) of Q4_K/Q5_K super-block blk (16-byte
-// aligned) for row r: sub-blocks 2j (chunks 0-3) and 2j+1 (chunks 4-7),
-// value sc*q.  With mins, stage 0 also writes the row's K=16 mins operand
-// [m_0..m_7, 32 m_0..32 m_7] into a2.
+// Quarter qr (16 elements, chunks 2qr, 2qr+1) of stage j of a Q4_K / Q5_K
+// super-block (16-byte aligned in shared memory) for row r: values sc*q of
+// sub-block 2j + qr/2.  u0..u3: the block's scales and mins
+// (k4_unpack_words).  Stage 0 also writes, for qr < 2, chunk qr of the row's
+// K=16 mins operand: m_0..m_7 (qr = 0) or 32*m_0..32*m_7 (qr = 1).
 template <int FMT>
-RV_DEVFN void tc_stage_k45(const uint8_t *blk, int j, uint8_t *a, uint8_t *a2, int r) {
-  const uint8_t *s = blk + 4;
-  const __half2 bias = tc_h2i(1024);
-  const uint8_t *qs = blk + (FMT == RV_Q4_K ? 16 : 48) + 32 * j;
-  const uint4 qa = *(const uint4 *)qs, qb = *(const uint4 *)(qs + 16);
-  const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  uint32_t hq[8];
+RV_DEVFN void tc_stage_k45(const uint8_t *blk, int j, int qr, uint32_t u0, uint32_t u1, uint32_t u2, uint32_t u3,
+                           uint8_t *a, uint8_t *a2, int r) {
+  const int hs = qr >> 1, sb = 2 * j + hs;
+  const int sc = byte_of(j < 2 ? u0 : u1, sb & 3);
+  const __half2 s2 = tc_h2i(sc), c2 = tc_h2i(-1024 * sc);
+  const uint4 qv = *(const uint4 *)(blk + (FMT == RV_Q4_K ? 16 : 48) + 32 * j + 16 * (qr & 1));
+  const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
+  uint32_t hw[4];
   if constexpr (FMT == RV_Q5_K) {
-    const uint4 ha = *(const uint4 *)(blk + 16), hb = *(const uint4 *)(blk + 32);
-    hq[0] = ha.x; hq[1] = ha.y; hq[2] = ha.z; hq[3] = ha.w;
-    hq[4] = hb.x; hq[5] = hb.y; hq[6] = hb.z; hq[7] = hb.w;
+    const uint4 hv = *(const uint4 *)(blk + 16 + 16 * (qr & 1));
+    hw[0] = hv.x; hw[1] = hv.y; hw[2] = hv.z; hw[3] = hv.w;
   }
+  const int sh = 4 * hs;
 #pragma unroll
-  for (int h = 0; h < 2; h++) {
-    const int sb = 2 * j + h;
-    int sc, mn;
-    tc_scale_min(s, sb, sc, mn);
-    const __half2 av = tc_h2i(sc);
+  for (int cc = 0; cc < 2; cc++) {
+    uint32_t o[4];
 #pragma unroll
-    for (int cc = 0; cc < 4; cc++) {
-      uint32_t w0 = (q[2 * cc] >> (4 * h)) & 0x0F0F0F0Fu, w1 = (q[2 * cc + 1] >> (4 * h)) & 0x0F0F0F0Fu;
+    for (int t = 0; t < 2; t++) {
+      const uint32_t w = q[2 * cc + t] >> sh;
+      uint32_t x0 = w, x1 = w >> 8;
       if constexpr (FMT == RV_Q5_K) {
-        w0 |= ((hq[2 * cc] >> sb) & 0x01010101u) << 4;
-        w1 |= ((hq[2 * cc + 1] >> sb) & 0x01010101u) << 4;
+        const uint32_t hb5 = hw[2 * cc + t] >> sb;
+        x0 = (x0 & 0x000F000Fu) | ((hb5 & 0x00010001u) << 4);
+        x1 = (x1 & 0x000F000Fu) | (((hb5 >> 8) & 0x00010001u) << 4);
+        o[2 * t] = tc_lv2(x0, 0x001F001Fu, s2, c2);
+        o[2 * t + 1] = tc_lv2(x1, 0x001F001Fu, s2, c2);
+      } else {
+        o[2 * t] = tc_lv2(x0, 0x000F000Fu, s2, c2);
+        o[2 * t + 1] = tc_lv2(x1, 0x000F000Fu, s2, c2);
       }
-      *(uint4 *)(a + tc_core_off(r, 4 * h + cc)) = tc_level8(w0, w1, bias, av);
     }
+    *(uint4 *)(a + tc_core_off(r, 2 * qr + cc)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
-  if (j == 0) {
-    uint32_t m[8];
+  if (j == 0 && qr < 2) {  // the mins operand is in natural order on both sides
+    const float f = qr ? 32.0f : 1.0f;
+    uint32_t o[4];
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-      int sc, mn;
-      tc_scale_min(s, k, sc, mn);
-      m[k] = (uint32_t)mn;
+    for (int k = 0; k < 4; k++) {
+      const uint32_t mw = k < 2 ? u2 : u3;
+      __half2 t2 = __floats2half2_rn((float)byte_of(mw, (2 * k) & 3) * f, (float)byte_of(mw, (2 * k + 1) & 3) * f);
+      o[k] = *(uint32_t *)&t2;
     }
-    uint4 lo, hi;
-    __half2 t;
-    t = __floats2half2_rn((float)m[0], (float)m[1]); lo.x = *(uint32_t *)&t;
-    t = __floats2half2_rn((float)m[2], (float)m[3]); lo.y = *(uint32_t *)&t;
-    t = __floats2half2_rn((float)m[4], (float)m[5]); lo.z = *(uint32_t *)&t;
-    t = __floats2half2_rn((float)m[6], (float)m[7]); lo.w = *(uint32_t *)&t;
-    t = __floats2half2_rn(32.0f * m[0], 32.0f * m[1]); hi.x = *(uint32_t *)&t;
-    t = __floats2half2_rn(32.0f * m[2], 32.0f * m[3]); hi.y = *(uint32_t *)&t;
-    t = __floats2half2_rn(32.0f * m[4], 32.0f * m[5]); hi.z = *(uint32_t *)&t;
-    t = __floats2half2_rn(32.0f * m[6], 32.0f * m[7]); hi.w = *(uint32_t *)&t;
-    *(uint4 *)(a2 + tc_core_off(r, 0, 2)) = lo;
-    *(uint4 *)(a2 + tc_core_off(r, 1, 2)) = hi;
+    *(uint4 *)(a2 + tc_core_off(r, qr, 2)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
-// Stage j of a Q6_K super-block at any even address (rows of a whole-tile
-// copy are 630 bytes apart; words go through ld32u) for row r: groups
-// g = 2(j&1), 2(j&1)+1 of half j>>1, values sl*(q-32) into a and
-// sh*(q-32) into ah, sc = 32*sh + sl.
-RV_DEVFN void tc_stage_q6(const uint8_t *blk, int j, uint8_t *a, uint8_t *ah, int r) {
-  const int hh = j >> 1;
-  const __half2 bias = tc_h2i(1056);  // 1024 + 32
-  const uint8_t *qh = blk + 128 + 32 * hh;
+// Quarter qr (16 elements of group g = 2(j&1) + qr/2, one scale) of stage j
+// of a Q6_K super-block at any even address (rows of a whole-tile copy are
+// 630 bytes apart; words go through ld32u) for row r: sl*(q-32) into a and
+// sh*(q-32) into ah, scale = 32*sh + sl.
+RV_DEVFN void tc_stage_q6(const uint8_t *blk, int j, int qr, uint8_t *a, uint8_t *ah, int r) {
+  const int hh = j >> 1, g = 2 * (j & 1) + (qr >> 1), l0 = 16 * (qr & 1);
+  const uint8_t *ql = blk + 64 * hh + 32 * (g & 1) + l0, *qh = blk + 128 + 32 * hh + l0;
+  const int lsh = 4 * (g >> 1), hsh = 2 * g;
+  const int sc = (int8_t)blk[192 + 8 * hh + 2 * g + (qr & 1)];
+  const __half2 sl = tc_h2i(sc & 31), sh = tc_h2i(sc >> 5);
+  const __half2 cl = tc_h2i(-1056 * (sc & 31)), chh = tc_h2i(-1056 * (sc >> 5));
 #pragma unroll
-  for (int gi = 0; gi < 2; gi++) {
-    const int g = 2 * (j & 1) + gi;
-    const uint8_t *ql = blk + 64 * hh + 32 * (g & 1);
-    const int lsh = 4 * (g >> 1), hsh = 2 * g;
-    const int s0 = (int8_t)blk[192 + 8 * hh + 2 * g], s1 = (int8_t)blk[192 + 8 * hh + 2 * g + 1];
-    const __half2 l0 = tc_h2i(s0 & 31), h0 = tc_h2i(s0 >> 5), l1 = tc_h2i(s1 & 31), h1 = tc_h2i(s1 >> 5);
+  for (int cc = 0; cc < 2; cc++) {
+    uint32_t oa[4], oh[4];
 #pragma unroll
-    for (int cc = 0; cc < 4; cc++) {
-      const uint32_t x0 = ld32u(ql + 8 * cc), x1 = ld32u(ql + 8 * cc + 4);
-      const uint32_t y0 = ld32u(qh + 8 * cc), y1 = ld32u(qh + 8 * cc + 4);
-      const uint32_t w0 = ((x0 >> lsh) & 0x0F0F0F0Fu) | (((y0 >> hsh) & 0x03030303u) << 4);
-      const uint32_t w1 = ((x1 >> lsh) & 0x0F0F0F0Fu) | (((y1 >> hsh) & 0x03030303u) << 4);
-      const uint32_t off = tc_core_off(r, 4 * gi + cc);
-      *(uint4 *)(a + off) = tc_level8(w0, w1, bias, cc < 2 ? l0 : l1);
-      *(uint4 *)(ah + off) = tc_level8(w0, w1, bias, cc < 2 ? h0 : h1);
+    for (int t = 0; t < 2; t++) {
+      const uint32_t lw = ld32u(ql + 8 * cc + 4 * t), hw = ld32u(qh + 8 * cc + 4 * t);
+      const uint32_t q6 = ((lw >> lsh) & 0x0F0F0F0Fu) | (((hw >> hsh) & 0x03030303u) << 4);
+      oa[2 * t] = tc_lv2(q6, 0x003F003Fu, sl, cl);
+      oa[2 * t + 1] = tc_lv2(q6 >> 8, 0x003F003Fu, sl, cl);
+      oh[2 * t] = tc_lv2(q6, 0x003F003Fu, sh, chh);
+      oh[2 * t + 1] = tc_lv2(q6 >> 8, 0x003F003Fu, sh, chh);
     }
+    const uint32_t off = tc_core_off(r, 2 * qr + cc);
+    *(uint4 *)(a + off) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+    *(uint4 *)(ah + off) = make_uint4(oh[0], oh[1], oh[2], oh[3]);
   }
 }
 
@@ -271,12 +261,12 @@ RV_DEVFN size_t tc_midx(uint32_t pp, int b, int j, int G) {
 RV_DEVFN void tc_q8k_operands(const uint8_t *blk, int b, int nb, int G, int lane, __half *q, __half *m, float *dsc,
                               uint32_t pp) {
   const uint32_t w0 = *(const uint32_t *)(blk + 4 + 8 * lane), w1 = *(const uint32_t *)(blk + 8 + 8 * lane);
-  uint4 o;
+  uint4 o;  // chunk slots in PI order: elements 0,2 | 1,3 | 4,6 | 5,7
   __half2 h;
-  h = __floats2half2_rn((float)(int8_t)w0, (float)(int8_t)(w0 >> 8)); o.x = *(uint32_t *)&h;
-  h = __floats2half2_rn((float)(int8_t)(w0 >> 16), (float)(int8_t)(w0 >> 24)); o.y = *(uint32_t *)&h;
-  h = __floats2half2_rn((float)(int8_t)w1, (float)(int8_t)(w1 >> 8)); o.z = *(uint32_t *)&h;
-  h = __floats2half2_rn((float)(int8_t)(w1 >> 16), (float)(int8_t)(w1 >> 24)); o.w = *(uint32_t *)&h;
+  h = __floats2half2_rn((float)(int8_t)w0, (float)(int8_t)(w0 >> 16)); o.x = *(uint32_t *)&h;
+  h = __floats2half2_rn((float)(int8_t)(w0 >> 8), (float)(int8_t)(w0 >> 24)); o.y = *(uint32_t *)&h;
+  h = __floats2half2_rn((float)(int8_t)w1, (float)(int8_t)(w1 >> 16)); o.z = *(uint32_t *)&h;
+  h = __floats2half2_rn((float)(int8_t)(w1 >> 8), (float)(int8_t)(w1 >> 24)); o.w = *(uint32_t *)&h;
   *(uint4 *)(q + tc_bidx(pp, b * 256 + 8 * lane, G)) = o;
   if (lane < 8) {
     const int16_t *bs = (const int16_t *)(blk + 260);
@@ -372,8 +362,7 @@ RV_DEVFN void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z
       : "memory");
 }
 
-#define RV_TC_W_PROD 3  // warps 3-6: producers
-#define RV_TC_W_EPI 7   // warps 7-14: epilogue
+#define RV_TC_W_WORK 2  // warps 2-17: producers and epilogue
 
 // One pair tile x 128 weight rows of one matrix.  Gate/up (DOWN = false):
 // grid.x = 2*M/128 row tiles (gate tiles first), output rows of gu
@@ -381,8 +370,10 @@ RV_DEVFN void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z
 // box per block through `wmap` (the layer's [E][gate|up][M][row bytes]
 // slabs).  Down: grid.x = H/128, the whole contiguous 128-row tile in one
 // bulk copy, output staged by (token, slot).  grid.y = max_tc pair tiles.
-// Roles: warp 0 lane 0 stages weights, warp 1 lane 0 issues the MMAs,
-// warp 2 lane 0 stages activations, warps 3-6 dequantize, 7-14 epilogue.
+// Roles: warp 0 lane 0 stages weights and lane 1 activations, warp 1 lane
+// 0 issues the MMAs, warps 2-17 dequantize super-block b and then drain
+// super-block b-1's accumulators out of tensor memory (the epilogue), so
+// the products of block b overlap the epilogue of block b-1.
 template <int FMT, bool DOWN>
 __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     k_tc_gemm(MoeDims d, MoeBufs B, MoeWeights W, const __grid_constant__ CUtensorMap wmap) {
@@ -430,10 +421,10 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < R; i++) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], RV_TC_PROD_WARPS);
+      mbar_init(&raw_empty[i], RV_TC_WORK_WARPS);
     }
     for (int i = 0; i < SA; i++) {
-      mbar_init(&a_full[i], RV_TC_PROD_WARPS);
+      mbar_init(&a_full[i], RV_TC_WORK_WARPS);
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < C::SBMAX; i++) {
@@ -442,10 +433,13 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], RV_TC_EPI_WARPS);
+      mbar_init(&acc_empty[i], RV_TC_WORK_WARPS);
     }
     *s_fail = 0;
   }
+  for (int i = threadIdx.x; i < nmma * nb; i += blockDim.x) s_da[i] = bd[(size_t)pp0 * nb + i];
+  if (DOWN)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s_pair[i] = B.index[p0 + i];
   __syncwarp();
   if (warp == 0) {
     tc_alloc(s_tmem, 4 * RV_TC_NT);
@@ -458,8 +452,8 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   RV_PHASE(PK, 1);
 
   if (warp == 0) {
-    // ------------------------------------------------ weight staging
     if (lane == 0) {
+      // ---------------------------------------------- weight staging
       bool ok = true;
       if constexpr (DOWN) {
         const size_t tb = (size_t)RV_TC_ROWS * rb;
@@ -475,15 +469,13 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
           }
           mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(RV_TC_ROWS * BB));
           tma_load_4d(raw + slot * rslot, &wmap, b * BB, row0, mat, e, &raw_full[slot]);
+          RV_TRACE(PK + 2, 4 * b, 6);
           if (b == 0) RV_PHASE_ANY(PK, 2);
         }
       }
       if (!ok) *s_fail = 1;
-    }
-    __syncwarp();
-  } else if (warp == 2) {
-    // -------------------------------------------- activation staging
-    if (lane == 0) {
+    } else if (lane == 1) {
+      // ------------------------------------------ activation staging
       bool ok = true;
       for (int it = 0; it < NS; it++) {
         const int sb = it % SB;
@@ -492,6 +484,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
           break;
         }
         const bool mins = F::MINS && (it & 3) == 0;
+        RV_TRACE(PK + 2, it, 5);
         uint8_t *dst = ring + sb * slot_b;
         mbar_arrive_expect_tx(&b_full[sb], (uint32_t)(ng * 1024 + (mins ? ng * 256 : 0)));
         bulk_g2s(dst, bq + ((size_t)it * B.tc_groups + g0) * 1024, (uint32_t)(ng * 1024), &b_full[sb]);
@@ -505,7 +498,17 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issue
     if (lane == 0) {
+      // The issue loop is kept short: this warp shares its scheduler with
+      // four dequantizing warps.  Descriptor words are formed by adding
+      // 16-byte units to precomputed low words; ring positions and phases
+      // advance without division.
       const uint32_t idesc = tc_idesc(nmma);
+      const uint32_t lbo = (128u >> 4) << 16, hi1024 = (1024u >> 4) | (1u << 14), hi256 = (256u >> 4) | (1u << 14);
+      const uint32_t a_lo0 = lbo | (smem_addr(sm) >> 4), b_lo0 = lbo | (smem_addr(ring) >> 4);
+      const uint32_t b_step = (uint32_t)(slot_b >> 4), a_step = (uint32_t)(SL::bytes >> 4);
+      auto mk = [](uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; };
+      int sa = 0, sb = 0;
+      uint32_t pa = 0, pb = 0;
       bool ok = true;
       for (int b = 0; b < nb && ok; b++) {
         const int slot = b & 1;
@@ -516,25 +519,40 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
         tc_fence_after();
         const uint32_t d1 = tmem + (uint32_t)(slot * 2 * RV_TC_NT), d2 = d1 + RV_TC_NT;
         for (int j = 0; j < 4; j++) {
-          const int it = 4 * b + j, sa = it % SA, sb = it % SB;
-          if (!mbar_wait_bounded(&a_full[sa], (it / SA) & 1) || !mbar_wait_bounded(&b_full[sb], (it / SB) & 1)) {
+          const int it = 4 * b + j;
+          if (!mbar_wait_bounded(&a_full[sa], pa)) {
             ok = false;
             break;
           }
+          RV_TRACE(PK + 2, it, 2);
+          if (!mbar_wait_bounded(&b_full[sb], pb)) {
+            ok = false;
+            break;
+          }
+          RV_TRACE(PK + 2, it, 3);
           tc_fence_after();
           if (it == 0) RV_PHASE_ANY(PK, 3);
-          const uint32_t as = smem_addr(sm + (size_t)sa * SL::bytes), bs = smem_addr(ring + sb * slot_b);
+          const uint32_t al = a_lo0 + (uint32_t)sa * a_step, bl = b_lo0 + (uint32_t)sb * b_step;
           if (F::MINS && j == 0)
-            tc_mma_f16(d2, tc_desc(as + SL::a2, 256), tc_desc(bs + nmma * 128, 256), idesc, 0u);
+            tc_mma_f16(d2, mk(al + (uint32_t)(SL::a2 >> 4), hi256), mk(bl + (uint32_t)nmma * 8, hi256), idesc, 0u);
 #pragma unroll
           for (int kk = 0; kk < 4; kk++) {
             const uint32_t acc = (j | kk) != 0;
-            tc_mma_f16(d1, tc_desc(as + SL::a + kk * 256, 1024), tc_desc(bs + kk * 256, 1024), idesc, acc);
-            if (F::SPLIT)
-              tc_mma_f16(d2, tc_desc(as + SL::ah + kk * 256, 1024), tc_desc(bs + kk * 256, 1024), idesc, acc);
+            tc_mma_f16(d1, mk(al + 16 * kk, hi1024), mk(bl + 16 * kk, hi1024), idesc, acc);
+            if (F::SPLIT) tc_mma_f16(d2, mk(al + (uint32_t)(SL::ah >> 4) + 16 * kk, hi1024), mk(bl + 16 * kk, hi1024), idesc, acc);
           }
+          RV_TRACE(PK + 2, it, 9);
           tc_commit(&a_empty[sa]);
           tc_commit(&b_empty[sb]);
+          RV_TRACE(PK + 2, it, 4);
+          if (++sa == SA) {
+            sa = 0;
+            pa ^= 1;
+          }
+          if (++sb == SB) {
+            sb = 0;
+            pb ^= 1;
+          }
         }
         tc_commit(&acc_full[slot]);
       }
@@ -542,88 +560,95 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       if (!ok) *s_fail = 1;
     }
     __syncwarp();
-  } else if (warp < RV_TC_W_EPI) {
-    // ------------------------------------------------------ producers
-    const int r = threadIdx.x - 32 * RV_TC_W_PROD;
-    bool ok = true;
-    if (DOWN) ok = tc_wait_warp(&raw_full[0], 0);
-    for (int it = 0; it < NS && ok; it++) {
-      const int b = it >> 2, j = it & 3, sa = it % SA;
-      if (!DOWN && j == 0 && !tc_wait_warp(&raw_full[b % R], (b / R) & 1)) {
-        ok = false;
-        break;
-      }
-      if (!tc_wait_warp(&a_empty[sa], ((it / SA) & 1) ^ 1)) {
-        ok = false;
-        break;
-      }
-      if (it == 0 && r == 0) RV_PHASE_ANY(PK, 5);
-      const uint8_t *blk = DOWN ? raw + (size_t)r * rb + (size_t)b * BB : raw + (b % R) * rslot + (size_t)r * BB;
-      uint8_t *st = sm + (size_t)sa * SL::bytes;
-      if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, st + SL::a, st + SL::ah, r);
-      else tc_stage_k45<FMT>(blk, j, st + SL::a, st + SL::a2, r);
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[sa]);
-        if (!DOWN && j == 3) mbar_arrive(&raw_empty[b % R]);
-      }
-    }
-    if (r == 0) RV_PHASE_ANY(PK, 6);
-    if (!ok) *s_fail = 1;
   } else {
-    // ------------------------------------------------------- epilogue
-    // Thread (quadrant q, lane) owns weight row 32q + lane (its tensor-
-    // memory lane) and columns [64*half, 64*half + 64) of the tile.
-    const int et = threadIdx.x - 32 * RV_TC_W_EPI;
-    for (int i = et; i < nmma * nb; i += 32 * RV_TC_EPI_WARPS) s_da[i] = bd[(size_t)pp0 * nb + i];
-    if (DOWN)
-      for (int i = et; i < n; i += 32 * RV_TC_EPI_WARPS) s_pair[i] = B.index[p0 + i];
-    asm volatile("bar.sync 1, %0;" ::"r"(32 * RV_TC_EPI_WARPS) : "memory");
-    const int q = warp & 3, half = (warp - RV_TC_W_EPI) >> 2;
-    const int r = 32 * q + lane;
-    const uint8_t *hrow = wsrc + (size_t)r * rb;  // the row's super-block headers (global)
-    float acc[4][16];
+    // ------------------------------------------- producers + epilogue
+    // Producing, thread p takes weight row p & 127, quarter p >> 7 of every
+    // stage.  Draining, thread (quadrant q, lane) owns weight row 32q + lane
+    // (its tensor-memory lane) and the 8-column chunks cq, cq+4, cq+8, cq+12
+    // of the tile, so small tiles spread over all sixteen warps.
+    const int p = threadIdx.x - 32 * RV_TC_W_WORK, r = p & 127, qr = p >> 7;
+    const int q = warp & 3, cq = (warp - RV_TC_W_WORK) >> 2, er = 32 * q + lane;
+    const uint8_t *hrow = wsrc + (size_t)er * rb;  // the drained row's super-block headers (global)
+    float acc[2][16];
 #pragma unroll
-    for (int c = 0; c < 4; c++)
+    for (int c = 0; c < 2; c++)
 #pragma unroll
       for (int i = 0; i < 16; i++) acc[c][i] = 0.0f;
     bool ok = true;
+    if (DOWN) ok = tc_wait_warp(&raw_full[0], 0);
+    uint32_t u0 = 0, u1 = 0, u2 = 0, u3 = 0;
     uint32_t hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + 208) : *(const uint32_t *)hrow;
-    for (int b = 0; b < nb; b++) {
-      const int slot = b & 1;
+    for (int b = 0; b <= nb && ok; b++) {
+      if (b < nb) {
+        for (int j = 0; j < 4; j++) {
+          const int it = 4 * b + j, sa = it % SA;
+          if (!DOWN && j == 0 && !tc_wait_warp(&raw_full[b % R], (b / R) & 1)) {
+            ok = false;
+            break;
+          }
+          if (p == 0 && j == 0) RV_TRACE(PK + 2, it, 8);
+          const uint8_t *blk = DOWN ? raw + (size_t)r * rb + (size_t)b * BB : raw + (b % R) * rslot + (size_t)r * BB;
+          if (F::MINS && j == 0) {
+            const uint4 hdr = *(const uint4 *)blk;
+            k4_unpack_words(hdr.y, hdr.z, hdr.w, u0, u1, u2, u3);
+          }
+          if (!tc_wait_warp(&a_empty[sa], ((it / SA) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          if (it == 0 && p == 0) RV_PHASE_ANY(PK, 5);
+          if (p == 0) RV_TRACE(PK + 2, it, 0);
+          uint8_t *st = sm + (size_t)sa * SL::bytes;
+          if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, qr, st + SL::a, st + SL::ah, r);
+          else tc_stage_k45<FMT>(blk, j, qr, u0, u1, u2, u3, st + SL::a, st + SL::a2, r);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&a_full[sa]);
+            if (!DOWN && j == 3) mbar_arrive(&raw_empty[b % R]);
+          }
+          if (p == 0) RV_TRACE(PK + 2, it, 1);
+        }
+        if (!ok) break;
+        if (b == nb - 1 && p == 0) RV_PHASE_ANY(PK, 6);
+      }
+      if (b == 0) continue;
+      // ---- epilogue of super-block eb = b - 1
+      const int eb = b - 1, slot = eb & 1;
       const uint32_t hdr = hdr_next;
-      if (b + 1 < nb)
-        hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + (size_t)(b + 1) * BB + 208)
-                                  : *(const uint32_t *)(hrow + (size_t)(b + 1) * BB);
+      if (eb + 1 < nb)
+        hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + (size_t)(eb + 1) * BB + 208)
+                                  : *(const uint32_t *)(hrow + (size_t)(eb + 1) * BB);
       const float dw = h2f((uint16_t)(hdr & 0xFFFFu)), dmw = h2f((uint16_t)(hdr >> 16));
-      if (!tc_wait_warp(&acc_full[slot], (b >> 1) & 1)) {
+      if (!tc_wait_warp(&acc_full[slot], (eb >> 1) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (b == 0 && et == 0) RV_PHASE_ANY(PK, 7);
+      if (eb == 0 && p == 0) RV_PHASE_ANY(PK, 7);
+      if (p == 0) RV_TRACE(PK + 2, 4 * eb, 7);
       const uint32_t t1 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(slot * 2 * RV_TC_NT);
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const int col = 64 * half + 16 * c;
+      for (int c8 = 0; c8 < 4; c8++) {
+        const int col = 8 * (cq + 4 * c8);
         if (col < nmma) {
-          uint32_t v1[16], v2[16];
-          tc_ld16(t1 + (uint32_t)col, v1);
-          tc_ld16(t1 + (uint32_t)(RV_TC_NT + col), v2);
+          uint32_t v1[8], v2[8];
+          tc_ld8(t1 + (uint32_t)col, v1);
+          tc_ld8(t1 + (uint32_t)(RV_TC_NT + col), v2);
           tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; i++) {
-            const float da = s_da[(col + i) * nb + b];
+          for (int i8 = 0; i8 < 8; i8++) {
+            const float da = s_da[(col + i8) * nb + eb];
             float blocksum;
             if constexpr (FMT == RV_Q6_K) {
-              const int sumi = __float2int_rn(__uint_as_float(v1[i])) + 32 * __float2int_rn(__uint_as_float(v2[i]));
+              const int sumi = __float2int_rn(__uint_as_float(v1[i8])) + 32 * __float2int_rn(__uint_as_float(v2[i8]));
               blocksum = __fmul_rn(__fmul_rn(dw, da), __int2float_rn(sumi));
             } else {
               const float dd = __fmul_rn(dw, da), dm = __fmul_rn(dmw, da);
-              blocksum = __fsub_rn(__fmul_rn(dd, __uint_as_float(v1[i])), __fmul_rn(dm, __uint_as_float(v2[i])));
+              blocksum = __fsub_rn(__fmul_rn(dd, __uint_as_float(v1[i8])), __fmul_rn(dm, __uint_as_float(v2[i8])));
             }
-            acc[c][i] = __fadd_rn(acc[c][i], blocksum);
+            float &ac = acc[c8 >> 1][8 * (c8 & 1) + i8];
+            ac = __fadd_rn(ac, blocksum);
           }
         }
       }
@@ -631,16 +656,16 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[slot]);
     }
-    if (et == 0) RV_PHASE_ANY(PK, 8);
+    if (p == 0) RV_PHASE_ANY(PK, 8);
     if (ok && !*s_fail) {
 #pragma unroll
-      for (int c = 0; c < 4; c++)
+      for (int c = 0; c < 2; c++)
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-          const int col = 64 * half + 16 * c + i;
+          const int col = 8 * (cq + 4 * (2 * c + (i >> 3))) + (i & 7);
           if (col < n) {
-            if constexpr (DOWN) B.staged[(size_t)s_pair[col] * d.H + row0 + r] = acc[c][i];
-            else B.gu[(size_t)(p0 + col) * 2 * d.M + (size_t)mat * d.M + row0 + r] = acc[c][i];
+            if constexpr (DOWN) B.staged[(size_t)s_pair[col] * d.H + row0 + er] = acc[c][i];
+            else B.gu[(size_t)(p0 + col) * 2 * d.M + (size_t)mat * d.M + row0 + er] = acc[c][i];
           }
         }
     }
