@@ -283,6 +283,51 @@ RV_API int rv_moe_forward_host(rv_moe *m, const rv_expert_table *table, uint32_t
                         size_t n_tokens, uint32_t *topk_ids_host, float *topk_weights_host,
                         uint32_t flags, rv_stream stream);
 
+/* ---- the MoE block in three parts (expert-parallel serving) ------------
+ * The same arithmetic as rv_moe_forward, split where an expert-parallel
+ * caller exchanges data between ranks.  The reference runs the block on one
+ * host and has no such split; these entries let its run_chunk
+ * (model/prefill.rs:2136-2263) run across GPUs with bit-identical results. */
+
+/* Bytes per Q8_K activation row (hidden/256 blocks of 292 bytes, rounded
+ * up to 16). */
+RV_API size_t rv_moe_act_stride(const rv_moe *m);
+
+/* Routing half (forward.rs:2655-2705, prefill.rs:2165-2204): ffn RMSNorm,
+ * Q8_K of the normed rows, router logits, softmax, top-k, renormalization.
+ * Writes topk_ids/topk_weights [n_tokens][top_k] and, if acts is not NULL,
+ * the Q8_K rows [n_tokens][rv_moe_act_stride] (16-byte aligned).  The
+ * residual is only read.  All device pointers. */
+RV_API int rv_moe_route(rv_moe *m, const float *ffn_norm, const float *router, const float *residual,
+                        size_t n_tokens, uint32_t *topk_ids, float *topk_weights, uint8_t *acts,
+                        rv_stream stream);
+
+/* Expert half for n_pairs (expert, Q8_K row) pairs of `layer` of `table`:
+ * gate/up, SwiGLU, Q8_K, down (forward.rs:2159-2261).  expert_ids
+ * [n_pairs] index the table's experts (0..n_experts-1 of that table);
+ * acts [n_pairs][rv_moe_act_stride]; out [n_pairs][hidden] receives the
+ * unweighted expert outputs.  n_pairs <= max_tokens * top_k of the engine.
+ * flags: RV_MOE_EXACT or RV_MOE_TENSOR. */
+RV_API int rv_moe_experts(rv_moe *m, const rv_expert_table *table, uint32_t layer, const uint32_t *expert_ids,
+                          const uint8_t *acts, size_t n_pairs, float *out, uint32_t flags, rv_stream stream);
+
+/* Weighted combine (forward.rs:2744-2753, prefill.rs:2749-2778): for each
+ * token, acc = 0; acc += w_k * out[row(t, k)] in top-k order; residual +=
+ * acc.  row(t, k) = pos_of[t*top_k + k], or t*top_k + k when pos_of is
+ * NULL.  expert_out has hidden floats per row. */
+RV_API int rv_moe_combine(rv_moe *m, float *residual, const float *topk_weights, const float *expert_out,
+                          const uint32_t *pos_of, size_t n_tokens, rv_stream stream);
+
+/* Expert-parallel dispatch plan over `world` ranks (1..64), expert e living
+ * on rank e % world as local expert e / world: send_counts[world] (int32)
+ * pairs per destination rank; pairs laid out rank by rank, pos_of
+ * [n_tokens*top_k] = each pair's row; send_local[row] = the local expert id;
+ * send_acts[row] = the pair's token's Q8_K row from acts.  No counterpart
+ * in the reference, which has no expert parallelism. */
+RV_API int rv_ep_plan(rv_moe *m, const uint32_t *topk_ids, const uint8_t *acts, size_t n_tokens, uint32_t world,
+                      int32_t *send_counts, uint32_t *pos_of, uint32_t *send_local, uint8_t *send_acts,
+                      rv_stream stream);
+
 /* Device addresses of the intermediates the most recent forward left in the
  * engine's scratch, for parity tests.  Layout per field below. */
 typedef struct rv_moe_taps {
@@ -360,6 +405,11 @@ RV_API int rv_quantize_weights(int format, const float *x, size_t n, uint8_t *ou
  * quantized by rv_quantize_weights (gate, up, down at their offsets). */
 RV_API int rv_expert_table_fill_synthetic(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
                                    rv_stream stream);
+/* The same weights for a shard of the experts: the table's expert i gets the
+ * weights of global expert first_expert + i*expert_step (an expert-parallel
+ * rank holding experts r, r+G, r+2G, ...). */
+RV_API int rv_expert_table_fill_synthetic_strided(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
+                                                  uint32_t first_expert, uint32_t expert_step, rv_stream stream);
 
 #ifdef __cplusplus
 }

@@ -282,8 +282,13 @@ class ExpertTable:
             _check(lib().rv_expert_table_upload(self.handle, layer, expert_first, n, buf, len(mv), 0,
                                                 _stream()))
 
-    def fill_synthetic(self, layer: int, seed: int, sigma: float = 0.02) -> None:
-        _check(lib().rv_expert_table_fill_synthetic(self.handle, layer, seed, sigma, _stream()))
+    def fill_synthetic(self, layer: int, seed: int, sigma: float = 0.02, first_expert: int = 0,
+                       expert_step: int = 1) -> None:
+        """Seeded N(0, sigma^2) weights quantized by the reference's
+        quantizers; expert i of this table gets global expert
+        first_expert + i*expert_step's weights (an expert-parallel shard)."""
+        _check(lib().rv_expert_table_fill_synthetic_strided(self.handle, layer, seed, sigma, first_expert,
+                                                            expert_step, _stream()))
 
     def begin_layer(self, layer: int, experts: Sequence[int]) -> None:
         arr = (ctypes.c_uint32 * max(len(experts), 1))(*experts)
@@ -412,6 +417,54 @@ class MoeEngine:
         out = np.zeros(max(n.value, 1) * 4, dtype=np.float32)
         _check(lib().rv_moe_profile_read(self.handle, out.ctypes.data, out.size, ctypes.byref(n)))
         return out[: n.value * 4].reshape(n.value, 4)
+
+    # -- the block in three parts (expert-parallel serving) -------------
+    @property
+    def act_stride(self) -> int:
+        return int(lib().rv_moe_act_stride(self.handle))
+
+    def route(self, ffn_norm: torch.Tensor, router: torch.Tensor, residual: torch.Tensor):
+        """Routing half: (topk_ids int32 [T, K], topk_weights f32 [T, K],
+        acts uint8 [T, act_stride] Q8_K rows).  residual is only read."""
+        T, K = residual.numel() // self.cfg.hidden, self.cfg.top_k
+        dev = residual.device
+        ids = torch.empty(T, K, dtype=torch.int32, device=dev)
+        w = torch.empty(T, K, dtype=torch.float32, device=dev)
+        acts = torch.empty(T, self.act_stride, dtype=torch.uint8, device=dev)
+        _check(lib().rv_moe_route(self.handle, _p(ffn_norm), _p(router), _p(residual), T, _p(ids), _p(w),
+                                  _p(acts), _stream()))
+        return ids, w, acts
+
+    def experts(self, table: ExpertTable, layer: int, expert_ids: torch.Tensor, acts: torch.Tensor,
+                flags: int = EXACT) -> torch.Tensor:
+        """Expert half for (expert id in `table`, Q8_K row) pairs: f32 [n, hidden]."""
+        n = expert_ids.numel()
+        out = torch.empty(n, self.cfg.hidden, dtype=torch.float32, device=acts.device)
+        _check(lib().rv_moe_experts(self.handle, table.handle, layer, _p(expert_ids), _p(acts), n, _p(out), flags,
+                                    _stream()))
+        return out
+
+    def combine(self, residual: torch.Tensor, topk_weights: torch.Tensor, expert_out: torch.Tensor,
+                pos_of: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """In place: residual += sum_k w_k * expert_out[row(t, k)] in top-k order."""
+        T = residual.numel() // self.cfg.hidden
+        _check(lib().rv_moe_combine(self.handle, _p(residual), _p(topk_weights), _p(expert_out), _p(pos_of), T,
+                                    _stream()))
+        return residual
+
+    def ep_plan(self, topk_ids: torch.Tensor, acts: torch.Tensor, world: int):
+        """Dispatch plan over `world` ranks (expert e on rank e % world):
+        (send_counts int32 [world], pos_of int32 [T*K], send_local int32
+        [T*K], send_acts uint8 [T*K, act_stride])."""
+        T, K = topk_ids.shape[0], self.cfg.top_k
+        dev = acts.device
+        counts = torch.empty(world, dtype=torch.int32, device=dev)
+        pos_of = torch.empty(T * K, dtype=torch.int32, device=dev)
+        send_local = torch.empty(T * K, dtype=torch.int32, device=dev)
+        send_acts = torch.empty(T * K, self.act_stride, dtype=torch.uint8, device=dev)
+        _check(lib().rv_ep_plan(self.handle, _p(topk_ids), _p(acts), T, world, _p(counts), _p(pos_of),
+                                _p(send_local), _p(send_acts), _stream()))
+        return counts, pos_of, send_local, send_acts
 
     def taps(self) -> _lib.MoeTaps:
         t = _lib.MoeTaps()

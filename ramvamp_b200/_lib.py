@@ -107,6 +107,11 @@ SIGNATURES = {
     "rv_moe_forward": (I32, [P, P, U32, P, P, P, SZ, P, P, U32, P]),
     "rv_moe_forward_host": (I32, [P, P, U32, P, P, P, SZ, P, P, U32, P]),
     "rv_moe_get_taps": (I32, [P, ctypes.POINTER(MoeTaps)]),
+    "rv_moe_act_stride": (SZ, [P]),
+    "rv_moe_route": (I32, [P, P, P, P, SZ, P, P, P, P]),
+    "rv_moe_experts": (I32, [P, P, U32, P, P, SZ, P, U32, P]),
+    "rv_moe_combine": (I32, [P, P, P, P, P, SZ, P]),
+    "rv_ep_plan": (I32, [P, P, P, SZ, U32, P, P, P, P, P]),
     "rv_moe_profile_enable": (I32, [P, SZ]),
     "rv_moe_profile_rewind": (I32, [P]),
     "rv_moe_profile_read": (I32, [P, P, SZ, ctypes.POINTER(SZ)]),
@@ -114,6 +119,7 @@ SIGNATURES = {
     "rv_synth_normal": (I32, [U64, U64, F32, P, SZ, P]),
     "rv_quantize_weights": (I32, [I32, P, SZ, P, P]),
     "rv_expert_table_fill_synthetic": (I32, [P, U32, U64, F32, P]),
+    "rv_expert_table_fill_synthetic_strided": (I32, [P, U32, U64, F32, U32, U32, P]),
 }
 
 _lib = None

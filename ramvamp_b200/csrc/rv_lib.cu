@@ -13,6 +13,7 @@
 #include "rv_kernels.cuh"
 #include "rv_moe.cuh"
 #include "rv_tc.cuh"
+#include "rv_ep.cuh"
 
 #include "_gen/expf_exceptions.inc"
 
@@ -747,38 +748,42 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 // Split mode (G lanes per row, one token at a time) serves decode; token
 // mode (a thread per row, up to 8 tokens in flight) serves larger batches.
 template <int FMT, int G, int NBG, int R>
-static void launch_gate_up_t(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
-  const MoeDims &d = m->d;
+static void launch_gate_up_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.gu_row_bytes : W.gu_row_bytes + 16;
   const size_t smem = 16 + round16(2 * (size_t)R * st) + 16 + (size_t)B.ms * d.act_stride +
                       (FMT == RV_Q6_K ? (size_t)B.ms * d.hb * 64 * 4 : 0) + 2 * R * RV_MOE_MT * 4;
-  dim3 grid((unsigned)m->max_units, (unsigned)(d.M / R));
+  dim3 grid((unsigned)B.max_units, (unsigned)(d.M / R));
   cudaFuncSetAttribute(k_gate_up<FMT, G, NBG, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k_gate_up<FMT, G, NBG, R><<<grid, 2 * R * G, smem, s>>>(d, B, W);
 }
 template <int FMT>
-static void launch_gate_up(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, int T, cudaStream_t s) {
-  if (T <= RV_SMALL_T && m->d.hb == 8) launch_gate_up_t<FMT, 4, 2, 8>(m, B, W, s);
-  else launch_gate_up_t<FMT, 1, 1, 32>(m, B, W, s);
+static void launch_gate_up(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int T, cudaStream_t s) {
+  if (T <= RV_SMALL_T && d.hb == 8) launch_gate_up_t<FMT, 4, 2, 8>(d, B, W, s);
+  else launch_gate_up_t<FMT, 1, 1, 32>(d, B, W, s);
 }
 template <int FMT, int G, int NBG, int ROWS, bool COMBINE>
-static cudaError_t launch_down_t(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
-  const MoeDims &d = m->d;
+static cudaError_t launch_down_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.down_row_bytes : W.down_row_bytes + 16;
   const size_t smem = 16 + round16((size_t)ROWS * st) + 16 + (size_t)B.ms * d.amoe_stride +
                       (FMT == RV_Q6_K ? (size_t)B.ms * d.mb * 64 * 4 : 0) + 16;
-  dim3 grid((unsigned)m->max_units, (unsigned)((d.H + ROWS - 1) / ROWS));
+  dim3 grid((unsigned)B.max_units, (unsigned)((d.H + ROWS - 1) / ROWS));
   cudaFuncSetAttribute(k_down<FMT, G, NBG, ROWS, COMBINE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   return launch_pdl(k_down<FMT, G, NBG, ROWS, COMBINE>, grid, dim3(32), smem, s, d, B, W);
 }
-// Returns true when the down kernel also performed the combine.
+// Returns true when the down kernel also performed the combine (only when
+// fuse_combine allows it).
 template <int FMT>
-static bool launch_down(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, int T, cudaStream_t s) {
-  if (T <= RV_SMALL_T && m->d.mb == 3) {
-    launch_down_t<FMT, 3, 1, 8, true>(m, B, W, s);
-    return true;
+static bool launch_down(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int T, bool fuse_combine,
+                        cudaStream_t s) {
+  if (T <= RV_SMALL_T && d.mb == 3) {
+    if (fuse_combine) {
+      launch_down_t<FMT, 3, 1, 8, true>(d, B, W, s);
+      return true;
+    }
+    launch_down_t<FMT, 3, 1, 8, false>(d, B, W, s);
+    return false;
   }
-  launch_down_t<FMT, 1, 1, 32, false>(m, B, W, s);
+  launch_down_t<FMT, 1, 1, 32, false>(d, B, W, s);
   return false;
 }
 
@@ -820,9 +825,8 @@ static int gate_up_map(const MoeWeights &W, const rv_layer_layout &L, CUtensorMa
 }
 
 template <int FMT, bool DOWN>
-static int launch_tc_gemm(const rv_moe *m, const MoeBufs &B, const MoeWeights &W, const CUtensorMap &map,
+static int launch_tc_gemm(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, const CUtensorMap &map,
                           cudaStream_t s) {
-  const MoeDims &d = m->d;
   const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
   const size_t smem = TcCfg<FMT, DOWN>::total(rb, (DOWN ? d.M : d.H) / 256);
   RV_CUDA(cudaFuncSetAttribute(k_tc_gemm<FMT, DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -852,20 +856,111 @@ static int tc_check(const rv_layer_layout &L, const MoeWeights &W, uint32_t laye
   return RV_OK;
 }
 
+// Event record for the per-stage profile (an external node inside a stream
+// capture, so that every replay of the graph records it).
+static int prof_record(cudaEvent_t *ev, int i, unsigned flags, cudaStream_t s) {
+  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[i], s, flags));
+  return RV_OK;
+}
+
+static MoeWeights layer_weights(const rv_expert_table *table, uint32_t layer) {
+  const rv_layer_layout &L = table->layouts[layer];
+  MoeWeights W;
+  W.base = table->base[layer];
+  W.stride = L.stride;
+  W.gate_off = L.gate_off;
+  W.up_off = L.up_off;
+  W.down_off = L.down_off;
+  rv_row_bytes(L.gate_format, L.hidden, &W.gu_row_bytes);
+  rv_row_bytes(L.down_format, L.moe, &W.down_row_bytes);
+  return W;
+}
+
+// The expert half for T rows of d.K slots whose dispatch index (B.index,
+// B.units, B.index_start) is built: gate/up, SwiGLU, Q8_K, down into
+// B.staged [pair][H].  Profile events 1-3 are recorded when ev is set.
+// *combined: the down kernel also performed the combine (only with
+// fuse_combine).
+static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, const rv_layer_layout &L,
+                        uint32_t layer, int T, uint32_t flags, bool fuse_combine, cudaEvent_t *ev, unsigned evflags,
+                        cudaStream_t s, bool *combined) {
+  *combined = false;
+  int rc;
+  if (flags & RV_MOE_TENSOR) {
+    rc = tc_check(L, W, layer);
+    if (rc) return rc;
+    const unsigned P = (unsigned)(T * d.K);
+    k_tc_tiles<<<1, 256, 0, s>>>(d, B);
+    k_tc_gather<<<P, 32 * d.hb, 0, s>>>(d, B);
+    RV_LAUNCH_CHECK();
+    if ((rc = prof_record(ev, 1, evflags, s))) return rc;
+    CUtensorMap gmap;
+    if ((rc = gate_up_map(W, L, &gmap))) return rc;
+    rc = L.gate_format == RV_Q4_K ? launch_tc_gemm<RV_Q4_K, false>(d, B, W, gmap, s)
+                                  : launch_tc_gemm<RV_Q5_K, false>(d, B, W, gmap, s);
+    if (rc) return rc;
+    k_tc_quant<<<P, 32 * d.mb, 0, s>>>(d, B);
+    RV_LAUNCH_CHECK();
+    if ((rc = prof_record(ev, 2, evflags, s))) return rc;
+    switch (L.down_format) {
+      case RV_Q4_K: rc = launch_tc_gemm<RV_Q4_K, true>(d, B, W, gmap, s); break;
+      case RV_Q5_K: rc = launch_tc_gemm<RV_Q5_K, true>(d, B, W, gmap, s); break;
+      default: rc = launch_tc_gemm<RV_Q6_K, true>(d, B, W, gmap, s); break;
+    }
+    if (rc) return rc;
+    return prof_record(ev, 3, evflags, s);
+  }
+  if ((rc = prof_record(ev, 1, evflags, s))) return rc;
+  switch (L.gate_format) {
+    case RV_Q4_K: launch_gate_up<RV_Q4_K>(d, B, W, T, s); break;
+    case RV_Q5_K: launch_gate_up<RV_Q5_K>(d, B, W, T, s); break;
+    default: launch_gate_up<RV_Q6_K>(d, B, W, T, s); break;
+  }
+  if ((rc = prof_record(ev, 2, evflags, s))) return rc;
+  switch (L.down_format) {
+    case RV_Q4_K: *combined = launch_down<RV_Q4_K>(d, B, W, T, fuse_combine, s); break;
+    case RV_Q5_K: *combined = launch_down<RV_Q5_K>(d, B, W, T, fuse_combine, s); break;
+    default: *combined = launch_down<RV_Q6_K>(d, B, W, T, fuse_combine, s); break;
+  }
+  RV_LAUNCH_CHECK();
+  return prof_record(ev, 3, evflags, s);
+}
+
+// Routing for T rows through the large-batch kernels: RMSNorm + Q8_K,
+// serial router chains, softmax/top-k/renormalization (counts into
+// B.counts).
+static int route_stage(const MoeDims &d, const MoeBufs &B, int T, cudaStream_t s) {
+  k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
+  const size_t smem = 16 + 2 * (size_t)(4 * RV_RCHUNK + 32 * (RV_RCHUNK + 4)) * 4;
+  k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, smem, s>>>(d, B);
+  k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+static int check_engine_layer(const rv_moe *m, const rv_expert_table *table, uint32_t layer, bool local) {
+  if (layer >= table->layouts.size())
+    RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, table->layouts.size());
+  const rv_layer_layout &L = table->layouts[layer];
+  const MoeDims &d = m->d;
+  if (L.hidden != (uint32_t)d.H || L.moe != (uint32_t)d.M || (!local && L.n_experts != (uint32_t)d.E))
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "layer %u geometry (%u, %u, %u) vs engine (%d, %d, %d)", layer, L.hidden,
+            L.moe, L.n_experts, d.H, d.M, d.E);
+  if (L.n_experts > 256) RV_FAIL(RV_ERR_UNIMPLEMENTED, "layer %u: more than 256 experts", layer);
+  if (L.gate_format != L.up_format)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "layer %u: gate and up in different formats", layer);
+  return RV_OK;
+}
+
 extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t layer,
                               const float *ffn_norm, const float *router, float *residual,
                               size_t n_tokens, uint32_t *topk_ids, float *topk_weights,
                               uint32_t flags, rv_stream stream) {
   if (!m || !table) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_forward: null engine or table");
-  if (layer >= table->layouts.size())
-    RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, table->layouts.size());
+  int rc = check_engine_layer(m, table, layer, false);
+  if (rc) return rc;
   const rv_layer_layout &L = table->layouts[layer];
   const MoeDims &d = m->d;
-  if (L.hidden != (uint32_t)d.H || L.moe != (uint32_t)d.M || L.n_experts != (uint32_t)d.E)
-    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "layer %u geometry (%u, %u, %u) vs engine (%d, %d, %d)", layer, L.hidden,
-            L.moe, L.n_experts, d.H, d.M, d.E);
-  if (L.gate_format != L.up_format)
-    RV_FAIL(RV_ERR_UNIMPLEMENTED, "layer %u: gate and up in different formats", layer);
   if (flags & ~RV_MOE_TENSOR) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
   if (n_tokens > m->max_tokens)
     RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_forward: %zu tokens vs engine capacity %zu", n_tokens, m->max_tokens);
@@ -879,95 +974,131 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   B.router = router;
   B.residual = residual;
   B.T = (int)n_tokens;
-  MoeWeights W;
-  W.base = table->base[layer];
-  W.stride = L.stride;
-  W.gate_off = L.gate_off;
-  W.up_off = L.up_off;
-  W.down_off = L.down_off;
-  rv_row_bytes(L.gate_format, L.hidden, &W.gu_row_bytes);
-  rv_row_bytes(L.down_format, L.moe, &W.down_row_bytes);
+  const MoeWeights W = layer_weights(table, layer);
   const int T = (int)n_tokens;
   cudaEvent_t *ev = nullptr;
   unsigned evflags = 0;
   if (m->prof_next < m->prof.size() / 5) {
     ev = &m->prof[5 * m->prof_next++];
-    // Inside a stream capture an event record must be an external node to
-    // be recorded on every replay of the graph.
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     RV_CUDA(cudaStreamIsCapturing(s, &cs));
     if (cs == cudaStreamCaptureStatusActive) evflags = cudaEventRecordExternal;
   }
-  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[0], s, evflags));
+  if ((rc = prof_record(ev, 0, evflags, s))) return rc;
   B.ms = T < RV_MOE_MT ? T : RV_MOE_MT;
-  if (flags & RV_MOE_TENSOR) {
-    int rc = tc_check(L, W, layer);
-    if (rc) return rc;
-    const unsigned P = (unsigned)(T * d.K);
-    k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
-    const size_t rsmem = 16 + 2 * (size_t)(4 * RV_RCHUNK + 32 * (RV_RCHUNK + 4)) * 4;
-    k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, rsmem, s>>>(d, B);
-    k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
-    k_index<<<1, 1024, 0, s>>>(d, B);
-    k_tc_tiles<<<1, 256, 0, s>>>(d, B);
-    k_tc_gather<<<P, 32 * d.hb, 0, s>>>(d, B);
-    RV_LAUNCH_CHECK();
-    if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[1], s, evflags));
-    CUtensorMap gmap;
-    rc = gate_up_map(W, L, &gmap);
-    if (rc) return rc;
-    rc = L.gate_format == RV_Q4_K ? launch_tc_gemm<RV_Q4_K, false>(m, B, W, gmap, s)
-                                  : launch_tc_gemm<RV_Q5_K, false>(m, B, W, gmap, s);
-    if (rc) return rc;
-    k_tc_quant<<<P, 32 * d.mb, 0, s>>>(d, B);
-    RV_LAUNCH_CHECK();
-    if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[2], s, evflags));
-    switch (L.down_format) {
-      case RV_Q4_K: rc = launch_tc_gemm<RV_Q4_K, true>(m, B, W, gmap, s); break;
-      case RV_Q5_K: rc = launch_tc_gemm<RV_Q5_K, true>(m, B, W, gmap, s); break;
-      default: rc = launch_tc_gemm<RV_Q6_K, true>(m, B, W, gmap, s); break;
-    }
-    if (rc) return rc;
-    if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[3], s, evflags));
-    k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
-    if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[4], s, evflags));
-    RV_LAUNCH_CHECK();
-    if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
-    if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
-    m->last_T = T;
-    return RV_OK;
-  }
-  if (T <= RV_SMALL_T) {
+  if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch
     const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)T * (d.H + 4) * 4 + 4 * sizeof(double) + 16;
     RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
   } else {
-    k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
-    const size_t smem = 16 + 2 * (size_t)(4 * RV_RCHUNK + 32 * (RV_RCHUNK + 4)) * 4;
-    k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, smem, s>>>(d, B);
-    k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
+    if ((rc = route_stage(d, B, T, s))) return rc;
     k_index<<<1, 1024, 0, s>>>(d, B);
   }
-  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[1], s, evflags));
-  switch (L.gate_format) {
-    case RV_Q4_K: launch_gate_up<RV_Q4_K>(m, B, W, T, s); break;
-    case RV_Q5_K: launch_gate_up<RV_Q5_K>(m, B, W, T, s); break;
-    default: launch_gate_up<RV_Q6_K>(m, B, W, T, s); break;
-  }
-  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[2], s, evflags));
-  bool combined;
-  switch (L.down_format) {
-    case RV_Q4_K: combined = launch_down<RV_Q4_K>(m, B, W, T, s); break;
-    case RV_Q5_K: combined = launch_down<RV_Q5_K>(m, B, W, T, s); break;
-    default: combined = launch_down<RV_Q6_K>(m, B, W, T, s); break;
-  }
-  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[3], s, evflags));
+  bool combined = false;
+  if ((rc = expert_stage(d, B, W, L, layer, T, flags, true, ev, evflags, s, &combined))) return rc;
   if (!combined) k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
-  if (ev) RV_CUDA(cudaEventRecordWithFlags(ev[4], s, evflags));
+  if ((rc = prof_record(ev, 4, evflags, s))) return rc;
   RV_LAUNCH_CHECK();
   if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
   if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
   m->last_T = T;
+  return RV_OK;
+}
+
+extern "C" size_t rv_moe_act_stride(const rv_moe *m) { return m ? m->d.act_stride : 0; }
+
+extern "C" int rv_moe_route(rv_moe *m, const float *ffn_norm, const float *router, const float *residual,
+                            size_t n_tokens, uint32_t *topk_ids, float *topk_weights, uint8_t *acts,
+                            rv_stream stream) {
+  if (!m) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_route: null engine");
+  if (n_tokens > m->max_tokens)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_route: %zu tokens vs engine capacity %zu", n_tokens, m->max_tokens);
+  if (n_tokens == 0) return RV_OK;
+  if (!ffn_norm || !router || !residual || !topk_ids || !topk_weights)
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_route: null pointer");
+  if ((uintptr_t)router & 15) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_route: router must be 16-byte aligned");
+  if (acts && ((uintptr_t)acts & 15)) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_route: acts must be 16-byte aligned");
+  const MoeDims &d = m->d;
+  cudaStream_t s = (cudaStream_t)stream;
+  MoeBufs B = m->B;
+  B.ffn_norm = ffn_norm;
+  B.router = router;
+  B.residual = (float *)residual;  // read only by the prologue
+  B.T = (int)n_tokens;
+  if (acts) B.acts = acts;
+  int rc = route_stage(d, B, (int)n_tokens, s);
+  if (rc) return rc;
+  RV_CUDA(cudaMemsetAsync(B.counts, 0, (size_t)d.E * 4, s));
+  RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+  RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+  m->last_T = (int)n_tokens;
+  return RV_OK;
+}
+
+extern "C" int rv_moe_experts(rv_moe *m, const rv_expert_table *table, uint32_t layer, const uint32_t *expert_ids,
+                              const uint8_t *acts, size_t n_pairs, float *out, uint32_t flags, rv_stream stream) {
+  if (!m || !table) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_experts: null engine or table");
+  int rc = check_engine_layer(m, table, layer, true);
+  if (rc) return rc;
+  if (flags & ~RV_MOE_TENSOR) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+  const size_t cap = m->max_tokens * (size_t)m->d.K;
+  if (n_pairs > cap) RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_experts: %zu pairs vs engine capacity %zu", n_pairs, cap);
+  if (n_pairs == 0) return RV_OK;
+  if (!expert_ids || !acts || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_experts: null pointer");
+  if ((uintptr_t)acts & 15) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_experts: acts must be 16-byte aligned");
+  const rv_layer_layout &L = table->layouts[layer];
+  MoeDims d = m->d;  // one slot per row, the table's local experts
+  d.K = 1;
+  d.E = (int)L.n_experts;
+  cudaStream_t s = (cudaStream_t)stream;
+  MoeBufs B = m->B;
+  B.T = (int)n_pairs;
+  B.ms = B.T < RV_MOE_MT ? B.T : RV_MOE_MT;
+  B.acts = (uint8_t *)acts;  // read only
+  B.staged = out;
+  RV_CUDA(cudaMemcpyAsync(B.ids, expert_ids, n_pairs * 4, cudaMemcpyDeviceToDevice, s));
+  k_count_ids<<<(unsigned)((n_pairs + 255) / 256), 256, 0, s>>>(d, B);
+  k_index<<<1, 1024, 0, s>>>(d, B);
+  RV_LAUNCH_CHECK();
+  bool combined = false;
+  return expert_stage(d, B, layer_weights(table, layer), L, layer, (int)n_pairs, flags, false, nullptr, 0, s,
+                      &combined);
+}
+
+extern "C" int rv_moe_combine(rv_moe *m, float *residual, const float *topk_weights, const float *expert_out,
+                              const uint32_t *pos_of, size_t n_tokens, rv_stream stream) {
+  if (!m) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_combine: null engine");
+  if (n_tokens == 0) return RV_OK;
+  if (!residual || !topk_weights || !expert_out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_combine: null pointer");
+  const MoeDims &d = m->d;
+  MoeBufs B = m->B;
+  B.residual = residual;
+  B.w = (float *)topk_weights;
+  B.staged = (float *)expert_out;
+  B.T = (int)n_tokens;
+  k_combine_rows<<<dim3((unsigned)n_tokens, (unsigned)((d.H + 255) / 256)), 256, 0, (cudaStream_t)stream>>>(
+      d, B, pos_of);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_ep_plan(rv_moe *m, const uint32_t *topk_ids, const uint8_t *acts, size_t n_tokens, uint32_t world,
+                          int32_t *send_counts, uint32_t *pos_of, uint32_t *send_local, uint8_t *send_acts,
+                          rv_stream stream) {
+  if (!m) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_plan: null engine");
+  if (world == 0 || world > 64) RV_FAIL(RV_ERR_UNIMPLEMENTED, "ep_plan: world size %u (1..64)", world);
+  if (n_tokens > m->max_tokens)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "ep_plan: %zu tokens vs engine capacity %zu", n_tokens, m->max_tokens);
+  if (!topk_ids || !acts || !send_counts || !pos_of || !send_local || !send_acts)
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_plan: null pointer");
+  if (((uintptr_t)acts | (uintptr_t)send_acts) & 15)
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_plan: activation rows must be 16-byte aligned");
+  const MoeDims &d = m->d;
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned P = (unsigned)(n_tokens * d.K);
+  k_ep_plan<<<1, 1024, 0, s>>>(d, topk_ids, P, world, send_counts, pos_of, send_local, m->B.index);
+  if (P) k_ep_pack<<<P, 128, 0, s>>>(d, acts, m->B.index, send_acts);
+  RV_LAUNCH_CHECK();
   return RV_OK;
 }
 
@@ -1038,7 +1169,13 @@ extern "C" int rv_quantize_weights(int format, const float *x, size_t n, uint8_t
 
 extern "C" int rv_expert_table_fill_synthetic(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
                                               rv_stream stream) {
+  return rv_expert_table_fill_synthetic_strided(t, layer, seed, sigma, 0, 1, stream);
+}
+
+extern "C" int rv_expert_table_fill_synthetic_strided(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
+                                                      uint32_t first_expert, uint32_t expert_step, rv_stream stream) {
   if (!t) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null table");
+  if (expert_step == 0) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "fill_synthetic: expert_step 0");
   if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
   const rv_layer_layout &L = t->layouts[layer];
   const size_t mh = (size_t)L.moe * L.hidden;
@@ -1055,7 +1192,8 @@ extern "C" int rv_expert_table_fill_synthetic(rv_expert_table *t, uint32_t layer
   cudaStream_t s = (cudaStream_t)stream;
   for (uint32_t ex = 0; ex < L.n_experts && rc == RV_OK; ex++) {
     uint8_t *blob = t->base[layer] + (size_t)ex * L.stride;
-    rc = rv_synth_normal(seed, (uint64_t)ex * 3 * mh, sigma, tmp, 3 * mh, stream);
+    const uint64_t ge = (uint64_t)first_expert + (uint64_t)ex * expert_step;  // global expert id
+    rc = rv_synth_normal(seed, ge * 3 * mh, sigma, tmp, 3 * mh, stream);
     if (!rc) rc = rv_quantize_weights(L.gate_format, tmp, mh, blob + L.gate_off, stream);
     if (!rc) rc = rv_quantize_weights(L.up_format, tmp + mh, mh, blob + L.up_off, stream);
     if (!rc) rc = rv_quantize_weights(L.down_format, tmp + 2 * mh, mh, blob + L.down_off, stream);
@@ -1197,15 +1335,15 @@ extern "C" int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_la
   const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)Tn * (d.H + 4) * 4 + 4 * sizeof(double) + 16;
   RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
   switch (L->gate_format) {
-    case RV_Q4_K: launch_gate_up<RV_Q4_K>(&m, B, W, Tn, s); break;
-    case RV_Q5_K: launch_gate_up<RV_Q5_K>(&m, B, W, Tn, s); break;
-    default: launch_gate_up<RV_Q6_K>(&m, B, W, Tn, s); break;
+    case RV_Q4_K: launch_gate_up<RV_Q4_K>(d, B, W, Tn, s); break;
+    case RV_Q5_K: launch_gate_up<RV_Q5_K>(d, B, W, Tn, s); break;
+    default: launch_gate_up<RV_Q6_K>(d, B, W, Tn, s); break;
   }
   bool combined;
   switch (L->down_format) {
-    case RV_Q4_K: combined = launch_down<RV_Q4_K>(&m, B, W, Tn, s); break;
-    case RV_Q5_K: combined = launch_down<RV_Q5_K>(&m, B, W, Tn, s); break;
-    default: combined = launch_down<RV_Q6_K>(&m, B, W, Tn, s); break;
+    case RV_Q4_K: combined = launch_down<RV_Q4_K>(d, B, W, Tn, true, s); break;
+    case RV_Q5_K: combined = launch_down<RV_Q5_K>(d, B, W, Tn, true, s); break;
+    default: combined = launch_down<RV_Q6_K>(d, B, W, Tn, true, s); break;
   }
   if (!combined) k_combine<<<dim3((unsigned)Tn, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
   RV_LAUNCH_CHECK();
