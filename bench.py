@@ -40,15 +40,25 @@ SEED = 20261201
 METRIC = "decode tok/s (expert FFN, 48 MoE layers, batch 1)"
 
 
+WORKLOADS = ("decode", "prefill", "batch", "ep")
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--workload", choices=WORKLOADS, default="decode",
+                    help="decode: config 1 (default); prefill: config 2; batch: config 3; ep: config 4")
     ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--exact", action="store_true", help="prefill/batch/ep: the exact (AVX2-order) path")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    steps, warmup = {"decode": (30, 5), "prefill": (20, 5), "batch": (10, 3), "ep": (5, 3)}[a.workload]
+    a.steps = steps if a.steps is None else a.steps
+    a.warmup = warmup if a.warmup is None else a.warmup
+    return a
 
 
 def layouts(rv, n_layers):
@@ -116,6 +126,15 @@ def measured_peaks():
             p = json.load(f)
         return float(p["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense bf16 TFLOP/s (burst, kernel timed alone); f16 runs at the same rate."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 def ncu_traffic(kernel: str):
@@ -395,8 +414,349 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ===================================================== configs 2, 3, 4
+# prefill (config 2): 512 tokens through one MoE layer (Q4_K gate/up, Q6_K
+#   down), near-uniform routing from N(0,1) rows and an N(0,0.02) router.
+# batch (config 3): 64 sequences, one token each, through all 48 MoE layers;
+#   router logits biased so expert popularity follows Zipf s=1.1.
+# ep (config 4): 4096 tokens (8 x 512) through all 48 MoE layers with the
+#   Zipf skew, experts sharded over the N GPUs (expert id mod N), NCCL
+#   all-to-all dispatch and combine.
+# The Zipf skew: every token carries a shared component c*u (u a fixed unit
+# vector, c = sqrt(H)/2) and router row e gets s_e*u/C added, s_e =
+# -1.1*ln(rank_e + 1) over a seeded permutation of the experts and C the
+# component's size after RMSNorm, so logit e is its N(0,0.02)-router logit
+# (the noise, std ~0.9) plus s_e: Plackett-Luce sampling with Zipf weights.
+ZIPF_S = 1.1
+
+
+def zipf_parts(seed):
+    """(u [H], s [E]) of the Zipf bias, from the seed (numpy, host)."""
+    rng = np.random.default_rng(seed)
+    u = rng.standard_normal(H).astype(np.float64)
+    u /= np.linalg.norm(u)
+    rank = rng.permutation(E)
+    s = -ZIPF_S * np.log(rank + 1.0)
+    return u.astype(np.float32), s.astype(np.float32)
+
+
+def zipf_inputs(base_router, tokens, seed):
+    """Bias an [E,H] router and [T,H] token rows (numpy float32 in, out)."""
+    u, s = zipf_parts(seed)
+    c = 0.5 * np.sqrt(H)
+    C = c / np.sqrt(1.0 + c * c / H)
+    router = (base_router + (s / C)[:, None] * u[None, :]).astype(np.float32)
+    x = (tokens + c * u[None, :]).astype(np.float32)
+    return np.ascontiguousarray(router), np.ascontiguousarray(x)
+
+
+def workload_shape(args):
+    n_layers = 1 if args.workload == "prefill" else args.layers
+    tokens = {"prefill": 512, "batch": 64, "ep": 4096}[args.workload]
+    return n_layers, tokens
+
+
+def workload_metric(args):
+    return {"prefill": "prefill tok/s (one MoE layer, 512 tokens)",
+            "batch": "batched decode tok/s (64 sequences, 48 MoE layers)",
+            "ep": "expert-parallel prefill tok/s (4096 tokens, 48 MoE layers)"}[args.workload]
+
+
+def workload_desc(args, n_layers, tokens, world):
+    d = {"prefill": f"config2 prefill: {tokens} tokens through one Qwen3-30B-A3B MoE layer (Q4_K gate/up, "
+                    "Q6_K down), near-uniform routing",
+         "batch": f"config3 batched decode: {tokens} sequences x 1 token through {n_layers} MoE layers, "
+                  "router biased to Zipf s=1.1 expert popularity",
+         "ep": f"config4 expert-parallel prefill: {tokens} tokens (8 x 512) through {n_layers} MoE layers, "
+               f"Zipf s=1.1, 128 experts sharded over {world} GPU(s) by id mod {world}"}
+    return d[args.workload]
+
+
+def run_cuda_batched(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ramvamp_b200 as rv
+    from ramvamp_b200.ep import EngineBackend, ExpertParallelMoe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = local if world > 1 else 0
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=120))
+    n_layers, n_tok = workload_shape(args)
+    flags = rv.EXACT if args.exact else rv.TENSOR
+    ep_mode = args.workload == "ep"
+    shard = world if ep_mode else 1
+    # Each rank of the ep workload holds experts rank, rank+N, ...; other
+    # workloads run independent replicas on N>1.
+    lays = [rv.qwen3_layer_layout(l, n_experts=E // shard) for l in range(n_layers)]
+    table = rv.ExpertTable(lays, device=dev)
+    for l in range(n_layers):
+        table.fill_synthetic(l, SEED + l, 0.02, first_expert=rank if ep_mode else 0, expert_step=shard)
+    zipf = args.workload in ("batch", "ep")
+    routers_np = []
+    for l in range(n_layers):
+        r = rv.synth_normal(SEED + 1000 + l, 0, 0.02, E * H).view(E, H).cpu().numpy()
+        if zipf:
+            r, _ = zipf_inputs(r, np.zeros((1, H), np.float32), SEED + 77 + l)
+        routers_np.append(r)
+    routers = [torch.from_numpy(r).cuda() for r in routers_np]
+    norm = torch.ones(H, dtype=torch.float32, device="cuda")
+    home = n_tok // world if ep_mode else n_tok
+    n_batches = 4
+    xs = rv.synth_normal(SEED + 7 + rank, 0, 1.0, n_batches * home * H).view(n_batches, home, H).cpu().numpy()
+    if zipf:
+        xs = np.stack([zipf_inputs(routers_np[0], xs[i], SEED + 77)[1] for i in range(n_batches)])
+    tokens = torch.from_numpy(np.ascontiguousarray(xs)).cuda()
+    eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=n_tok if ep_mode else home, device=dev)
+    resid = torch.empty(home, H, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    ep = ExpertParallelMoe(EngineBackend(eng, table, [norm] * n_layers, routers, flags), shard, rank if ep_mode else 0)
+
+    def step_body():
+        if ep_mode:
+            for l in range(n_layers):
+                ep.forward(l, resid)
+        else:
+            for l in range(n_layers):
+                eng.forward(table, l, norm, routers[l], resid, flags=flags)
+
+    with torch.cuda.stream(stream):
+        resid.copy_(tokens[0])
+        step_body()
+    stream.synchronize()
+    graph = None
+    if not ep_mode:  # the ep step synchronizes on the exchanged counts: no graph
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step_body()
+    torch.cuda.synchronize()
+
+    def run_steps(lo, hi):
+        with torch.cuda.stream(stream):
+            for i in range(lo, hi):
+                resid.copy_(tokens[i % n_batches])
+                graph.replay() if graph is not None else step_body()
+
+    run_steps(0, args.warmup)
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(dev)
+    uuid = str(getattr(props, "uuid", ""))
+    clocks = ClockSampler(("GPU-" + uuid if uuid and not uuid.startswith("GPU-") else uuid) or str(dev))
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    run_steps(args.warmup, args.warmup + args.steps)
+    ev1.record(stream)
+    ev1.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    total_tok = (n_tok if ep_mode else home * world)
+    tok_s = total_tok * args.steps / (ms / 1e3)
+
+    # Per-stage durations on the profile events (single-GPU forward path,
+    # outside the timed region): the expert GEMM stages bound the roofline.
+    stage = None
+    if not ep_mode or world == 1:
+        eng.profile_enable(n_layers)
+        sets = []
+        for i in range(3):
+            eng.profile_rewind()
+            with torch.cuda.stream(stream):
+                resid.copy_(tokens[i % n_batches])
+                for l in range(n_layers):
+                    eng.forward(table, l, norm, routers[l], resid, flags=flags)
+            stream.synchronize()
+            sets.append(eng.profile_read())
+        stage = np.stack(sets).mean(0)  # [layers][4] ms
+        eng.profile_enable(0)
+    # e2e: host rows in, host rows out, through the public call a caller makes
+    host_tok = torch.empty(n_batches, home, H, dtype=torch.float32).pin_memory()
+    host_tok.copy_(tokens.cpu())
+    hres = torch.empty(home, H, dtype=torch.float32).pin_memory()
+    if world > 1:
+        dist.barrier()
+    n_e2e = max(2, min(args.steps, 5))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        hres.copy_(host_tok[i % n_batches])
+        if ep_mode:
+            resid.copy_(hres, non_blocking=True)
+            for l in range(n_layers):
+                ep.forward(l, resid)
+            hres.copy_(resid)
+        else:
+            for l in range(n_layers):
+                eng.forward_host(table, l, norm, routers[l], hres, flags=flags)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_tok_s = total_tok * n_e2e / e2e_s
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_batched(args, rv, table if not ep_mode or world == 1 else None, routers_np,
+                                   tokens[0].cpu().numpy(), lays)
+
+    if rank == 0:
+        hbm, hbm_kind = measured_peaks()
+        tpk, tpk_kind = measured_tensor_peak()
+        line = {
+            "metric": workload_metric(args), "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "strong" if ep_mode else "weak", "vs_baseline": None,
+            "dtype": "int8/int4 levels as exact f16 integers on tcgen05, f32 accumulate" if flags == rv.TENSOR
+            else "int8 (dp4a) + f32",
+            "data": "synthetic: seeded N(0,1) rows, N(0,0.02) router and expert weights quantized by the "
+                    "reference's Q4_K/Q6_K quantizers" + (", Zipf-biased router" if zipf else ""),
+            "config": {"workload": workload_desc(args, n_layers, n_tok, world), "layers": n_layers,
+                       "tokens_per_step": total_tok,
+                       "path": "tensor (bit-identical to the reference's scalar arm)" if flags == rv.TENSOR
+                       else "exact (bit-identical to the reference's AVX2 arm)",
+                       "l2": "inputs larger than L2: each step streams every touched expert's weights "
+                             "(%.0f MB per layer resident)" % (sum(L.stride for L in lays[:1]) * lays[0].n_experts / 1e6),
+                       "parallelism": (f"ep{world}" if ep_mode else ("replicas" if world > 1 else "single GPU")),
+                       "cuda_graph": graph is not None},
+            "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": home * H * 4 * (1 if ep_mode else n_layers),
+                    "d2h_bytes_per_step": home * H * 4 * (1 if ep_mode else n_layers),
+                    "path": "ExpertParallelMoe.forward per layer" if ep_mode
+                    else "rv_moe_forward_host per layer (pinned host rows in, result out)"},
+            "gpu_launches": args.steps * n_layers * (10 if flags == rv.TENSOR else 7),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        if stage is not None:
+            gu_ms, dn_ms = float(stage[:, 1].mean()), float(stage[:, 2].mean())
+            L0 = lays[0]
+            gu_bytes = L0.n_experts * (L0.gate_len + L0.up_len)
+            pairs = home * K
+            gu_flop = 2.0 * pairs * 2 * M * H
+            line["stage_ms_per_layer"] = {"routing": round(float(stage[:, 0].mean()), 4),
+                                          "gate_up": round(gu_ms, 4), "down": round(dn_ms, 4),
+                                          "combine": round(float(stage[:, 3].mean()), 4)}
+            achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+            line["roofline"] = {"kernel": "k_tc_gemm gate/up (stage incl. SwiGLU+Q8_K)" if flags == rv.TENSOR
+                                else "k_gate_up", "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                                "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                                "peak_source": f"{hbm_kind} hbm_gbs",
+                                "bytes_per_launch": gu_bytes, "traffic": ncu_traffic("k_tc_gemm_gate_up"),
+                                "upper_bound_if_every_expert_is_touched": True}
+            line["tensor"] = {"achieved_tflops": round(gu_flop / (gu_ms * 1e-3) / 1e12, 2), "peak": tpk,
+                              "frac": round(gu_flop / (gu_ms * 1e-3) / 1e12 / tpk, 4),
+                              "peak_source": f"{tpk_kind} bf16_tflops (dense f16 runs at the same rate)",
+                              "flops": "2 * pairs * (gate + up) * hidden, useful products only"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline_batched(args, rv, table, routers_np, x0, lays):
+    """The oracle (AVX2 restatement of the reference) on a bounded sample of
+    the workload: up to 32 rows through layer 0 on every host core, scaled
+    to the workload's layers and tokens."""
+    from oracle import oracle as orc
+
+    import torch
+
+    orc.build()
+    threads = os.cpu_count() or 1
+    L = lays[0]
+    if table is not None and L.n_experts == E:
+        blobs = rv.alias(table.view(0, 0).blob, E * L.stride).cpu().numpy()
+    else:
+        full = rv.qwen3_layer_layout(0)
+        blobs = orc.fill_layer_synthetic(full, SEED, 0.02, threads)
+        L = full
+    norm = np.ones(H, np.float32)
+    OL = orc.make_layer(H, M, E, K, 1e-6, norm, routers_np[0], blobs, L.stride, L.gate_off, L.up_off, L.down_off,
+                        L.gate_format, L.up_format, L.down_format)
+    n = min(32, x0.shape[0])
+    x = np.ascontiguousarray(x0[:n])
+    orc.moe_prefill(OL, x[:2], threads=threads)  # warm-up
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        orc.moe_prefill(OL, x, threads=threads)
+        reps += 1
+        if time.perf_counter() - t0 > 8.0:
+            break
+    dt = (time.perf_counter() - t0) / reps  # one layer, n rows
+    n_layers, _ = workload_shape(args)
+    tok_s = n / (dt * n_layers)
+    return {"value": round(tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} rows through one Q6_K-down layer on the C oracle's AVX2 arm ({reps} repetitions), "
+                      f"time scaled to {n_layers} layer(s)"}
+
+
+def run_reference_batched(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    import ramvamp_b200 as rv  # layout arithmetic only (no GPU calls)
+
+    orc.build()
+    threads = os.cpu_count() or 1
+    n_layers, n_tok = workload_shape(args)
+    full = rv.qwen3_layer_layout(0)
+    blobs = orc.fill_layer_synthetic(full, SEED, 0.02, threads)
+    router = orc.synth_normal(SEED + 1000, 0, 0.02, E * H).reshape(E, H)
+    x = orc.synth_normal(SEED + 7, 0, 1.0, 32 * H).reshape(32, H)
+    if args.workload in ("batch", "ep"):
+        router, x = zipf_inputs(router, x, SEED + 77)
+    OL = orc.make_layer(H, M, E, K, 1e-6, np.ones(H, np.float32), router, blobs, full.stride, full.gate_off,
+                        full.up_off, full.down_off, full.gate_format, full.up_format, full.down_format)
+    sample = 64 if args.workload == "batch" else 128
+    xs = np.ascontiguousarray(x[:sample])
+    for _ in range(args.warmup):
+        orc.moe_prefill(OL, xs[:2], threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.moe_prefill(OL, xs, threads=threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    v = sample / (dt * n_layers)
+    line = {
+        "impl": "reference", "metric": workload_metric(args), "value": round(v, 3), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * n_layers * n_tok / sample * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if args.workload == "ep" else "weak", "vs_baseline": None, "dtype": "int8 + f32",
+        "data": "synthetic (same seeds as the CUDA arm)",
+        "config": {"workload": workload_desc(args, n_layers, n_tok, 1) + " (sampled rows, scaled)",
+                   "layers": n_layers, "tokens_per_step": n_tok},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"each step: {sample} rows through one Q6_K-down layer on the C oracle's "
+                                   f"AVX2 arm with {threads} threads, time scaled to {n_layers} layer(s)"},
+        "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload != "decode":
+        (run_reference_batched if args.impl == "reference" else run_cuda_batched)(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
