@@ -112,17 +112,20 @@ RV_DEVFN bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: false (and the device error word set) if the phase did not
-// complete within RV_WAIT_CYCLES.
-RV_DEVFN bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+// complete within RV_WAIT_CYCLES.  The clock is read only every 32nd probe,
+// and waiters off the critical path pass sleep_ns > 0 to back off between
+// probes, so spinning warps leave the issue slots to warps with work.
+RV_DEVFN bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t sleep_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
-  long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > RV_WAIT_CYCLES) {
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; i++) {
+    if (sleep_ns) __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 0 && clock64() - t0 > RV_WAIT_CYCLES) {
       rv_dev_fail(RV_ERR_TIMEOUT);
       return false;
     }
   }
-  return true;
 }
 
 // Stage `bytes` from global `src` into shared `dst`.  Aligned ranges go

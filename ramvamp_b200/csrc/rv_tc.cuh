@@ -349,8 +349,10 @@ struct TcCfg {
   __host__ __device__ static size_t total(size_t rb, int nb) { return 1024 + bars(rb, nb) + NBARS * 8 + 16; }
 };
 
+// Warp-uniform wait of the dequantizing / draining warps (backing off
+// between probes).
 RV_DEVFN bool tc_wait_warp(uint64_t *bar, uint32_t parity) {
-  const bool ok = mbar_wait_bounded(bar, parity);
+  const bool ok = mbar_wait_bounded(bar, parity, 64);
   return __all_sync(RV_FULL, ok);
 }
 // 4-D tiled TMA load (no multicast) of the box at (x, y, z, w).
@@ -463,7 +465,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       } else {
         for (int b = 0; b < nb; b++) {
           const int slot = b % R;
-          if (!mbar_wait_bounded(&raw_empty[slot], ((b / R) & 1) ^ 1)) {
+          if (!mbar_wait_bounded(&raw_empty[slot], ((b / R) & 1) ^ 1, 128)) {
             ok = false;
             break;
           }
@@ -479,7 +481,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       bool ok = true;
       for (int it = 0; it < NS; it++) {
         const int sb = it % SB;
-        if (!mbar_wait_bounded(&b_empty[sb], ((it / SB) & 1) ^ 1)) {
+        if (!mbar_wait_bounded(&b_empty[sb], ((it / SB) & 1) ^ 1, 128)) {
           ok = false;
           break;
         }
