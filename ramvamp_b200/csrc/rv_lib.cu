@@ -988,7 +988,7 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   B.ms = T < RV_MOE_MT ? T : RV_MOE_MT;
   if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch
-    const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)T * (d.H + 4) * 4 + 4 * sizeof(double) + 16;
+    const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)T * (d.H + 4) * 4 + 4 * (size_t)T * sizeof(double) + 16;
     RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
   } else {
     if ((rc = route_stage(d, B, T, s))) return rc;
@@ -1332,7 +1332,7 @@ extern "C" int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_la
   rv_row_bytes(L->gate_format, L->hidden, &W.gu_row_bytes);
   rv_row_bytes(L->down_format, L->moe, &W.down_row_bytes);
   const int Tn = (int)n_tokens;
-  const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)Tn * (d.H + 4) * 4 + 4 * sizeof(double) + 16;
+  const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)Tn * (d.H + 4) * 4 + 4 * (size_t)Tn * sizeof(double) + 16;
   RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
   switch (L->gate_format) {
     case RV_Q4_K: launch_gate_up<RV_Q4_K>(d, B, W, Tn, s); break;

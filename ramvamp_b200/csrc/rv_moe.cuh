@@ -189,6 +189,103 @@ RV_DEVFN void route_token_warp(const MoeDims &d, const MoeBufs &B, int t, int la
   }
 }
 
+// The same routing for one token by a whole CTA of 128 threads, thread i
+// owning experts i and i+128: block max, one f64 exponential per thread,
+// tree sum with the serial fallback, then top-k by rank (the number of
+// probabilities greater than p_e, or equal at a lower index) -- the order
+// the repeated strict-'>' argmax produces whenever every probability is a
+// number; otherwise warp 0 runs the warp version.  Scratch: es [256]
+// doubles, ps [256] floats, sel [16] floats, red [8] doubles, flag.
+RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, double *es, float *ps, float *sel,
+                                double *red, int *counts) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float *lg = B.logits + (size_t)t * d.E;
+  float x[2];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int e = tid + 128 * j;
+    x[j] = e < d.E ? __ldcg(lg + e) : -INFINITY;
+    if (e < d.E) mx = fmaxf(mx, x[j]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(RV_FULL, mx, o));
+  float *redf = (float *)(red + 4);
+  if (lane == 0) redf[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(redf[0], redf[1]), fmaxf(redf[2], redf[3]));
+  const double dmx = (double)mx;
+  double part = 0.0;
+  float pf[2];
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int e = tid + 128 * j;
+    pf[j] = -INFINITY;
+    if (e < d.E) {
+      const double ex = exp(__dsub_rn((double)x[j], dmx));
+      es[e] = ex;
+      pf[j] = __double2float_rn(ex);
+      part = __dadd_rn(part, ex);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+  __syncthreads();  // redf reads done, es complete
+  if (lane == 0) red[warp] = part;
+  __syncthreads();
+  // Any order of these <= 256 non-negative terms is within 2^-44 relative of
+  // the reference's serial sum; recompute serially when 1/sum is that close
+  // to a float rounding midpoint.
+  double rinv = __drcp_rn(__dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3])));
+  if (!f32_rounding_stable(rinv, 0x1p-42)) {
+    double sum = 0.0;
+    for (int e = 0; e < d.E; e++) sum = __dadd_rn(sum, es[e]);
+    rinv = __drcp_rn(sum);
+  }
+  const float inv = __double2float_rn(rinv);
+  bool finite = true;
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int e = tid + 128 * j;
+    if (e < 256) {
+      const float p = e < d.E ? __fmul_rn(pf[j], inv) : -INFINITY;
+      ps[e] = p;
+      if (e < d.E && !(p == p && p != INFINITY && p != -INFINITY)) finite = false;
+    }
+  }
+  const bool all_finite = __syncthreads_and(finite);
+  if (!all_finite) {
+    if (warp == 0) route_token_warp(d, B, t, lane, es, counts);
+    __syncthreads();
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int e = tid + 128 * j;
+    if (e < d.E) {
+      const float p = ps[e];
+      int rank = 0;
+      for (int i = 0; i < d.E; i++) {
+        const float q = ps[i];
+        rank += (q > p) | ((q == p) & (i < e));
+      }
+      if (rank < d.K) {
+        B.ids[(size_t)t * d.K + rank] = (uint32_t)e;
+        sel[rank] = p;
+        atomicAdd(&counts[e], 1);
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < d.K) {
+    float wsum = -0.0f;  // the in-order sum of the selected weights
+    for (int k = 0; k < d.K; k++) wsum = __fadd_rn(wsum, sel[k]);
+    const float w = d.norm_topk ? __fdiv_rn(sel[tid], wsum) : sel[tid];
+    B.w[(size_t)t * d.K + tid] = w;
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
   __shared__ double es[4][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -267,6 +364,43 @@ RV_DEVFN void build_index_cta(const MoeDims &d, const MoeBufs &B, int *s_cnt, ui
   }
 }
 
+// The dispatch index for at most 32 pairs (decode): positions in expert
+// order (pairs of one expert in pair order), per-expert CSR starts, one
+// work unit per distinct expert.  ids were written by this CTA (visible
+// after the caller's __syncthreads).
+RV_DEVFN void build_index_small(const MoeDims &d, const MoeBufs &B) {
+  const int P = B.T * d.K;
+  const int tid = threadIdx.x;
+  for (int e = tid; e <= d.E; e += blockDim.x) {
+    int below = 0;
+    for (int q = 0; q < P; q++) below += B.ids[q] < (uint32_t)e;
+    B.index_start[e] = (uint32_t)below;
+  }
+  if (tid < 32) {
+    const int p = tid;
+    const uint32_t e = p < P ? B.ids[p] : 0xFFFFFFFFu;
+    int pos = 0, cnt = 0;
+    bool first = true;
+    for (int q = 0; q < P; q++) {
+      const uint32_t eq = __shfl_sync(RV_FULL, e, q);
+      pos += (eq < e) | ((eq == e) & (q < p));
+      cnt += eq == e;
+      first = first && !((eq == e) & (q < p));
+    }
+    const unsigned firsts = __ballot_sync(RV_FULL, p < P && first);
+    int u = 0;  // distinct experts below e
+    for (int q = 0; q < P; q++) {
+      const uint32_t eq = __shfl_sync(RV_FULL, e, q);
+      u += ((firsts >> q) & 1u) && eq < e;
+    }
+    if (p < P) {
+      B.index[pos] = (uint32_t)p;
+      if (first) B.units[u] = make_int4((int)e, pos, pos + cnt, 0);
+    }
+    if (p == 0) *B.n_units = __popc(firsts);
+  }
+}
+
 // Large-T dispatch: counts come from k_route's global atomics and are
 // cleared here for the next call.
 __global__ void __launch_bounds__(1024) k_index(MoeDims d, MoeBufs B) {
@@ -335,6 +469,7 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   __shared__ uint32_t s_st[257], s_cur[256];
   __shared__ int s_us[257];
   __shared__ int s_last;
+  __shared__ float s_inv[RV_SMALL_T];
   RV_PHASE(0, 0);
   const int T = B.T, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = blockIdx.x;
@@ -343,7 +478,7 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   float *rows = (float *)(sm + 16);              // [H] router row e
   float *nw = rows + d.H;                        // [H] ffn_norm weight
   float *xs = nw + d.H;                          // [T][H + 4]
-  double *red = (double *)(xs + T * xstride);    // [4] per-warp scratch
+  double *red = (double *)(xs + T * xstride);    // [T][4] per-warp partial sums
   const int n_rows = 1;
   const float *rsrc = B.router + (size_t)e0 * d.H;
   const size_t rbytes = (size_t)n_rows * d.H * 4;
@@ -376,24 +511,35 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   if (xbulk && !mbar_wait_bounded(bar + 1, 0)) return;
   if (rbulk && !mbar_wait_bounded(bar, 0)) return;
   RV_PHASE(0, 2);
-  // RMSNorm (norm.rs:17-60): warp w normalizes tokens w, w+4, ... in place.
-  for (int t = warp; t < T; t += 4) {
-    float *x = xs + t * xstride;
-    double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
-    for (int k = 4 * lane; k < d.H; k += 128) {
-      const float4 v = *(const float4 *)(x + k);
-      p0 = __dadd_rn(p0, __dmul_rn((double)v.x, (double)v.x));
-      p1 = __dadd_rn(p1, __dmul_rn((double)v.y, (double)v.y));
-      p2 = __dadd_rn(p2, __dmul_rn((double)v.z, (double)v.z));
-      p3 = __dadd_rn(p3, __dmul_rn((double)v.w, (double)v.w));
-    }
-    double part = __dadd_rn(__dadd_rn(p0, p1), __dadd_rn(p2, p3));
+  // RMSNorm (norm.rs:17-60), in place.  The f64 sum of squares is split
+  // over the four warps (each token's row in four quarters); any summation
+  // order lies within the 2^-38 bound f32_rounding_stable checks, and the
+  // serial order is recomputed when the f32 result is not stable.
+  {
+    const int q = d.H / 4;  // elements per warp per token
+    for (int t = 0; t < T; t++) {
+      const float *x = xs + t * xstride + warp * q;
+      double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
+      for (int k = 4 * lane; k < q; k += 128) {
+        const float4 v = *(const float4 *)(x + k);
+        p0 = __dadd_rn(p0, __dmul_rn((double)v.x, (double)v.x));
+        p1 = __dadd_rn(p1, __dmul_rn((double)v.y, (double)v.y));
+        p2 = __dadd_rn(p2, __dmul_rn((double)v.z, (double)v.z));
+        p3 = __dadd_rn(p3, __dmul_rn((double)v.w, (double)v.w));
+      }
+      double part = __dadd_rn(__dadd_rn(p0, p1), __dadd_rn(p2, p3));
 #pragma unroll
-    for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
-    if (lane == 0) {
-      const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(__ddiv_rn(part, (double)d.H), (double)d.eps)));
+      for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+      if (lane == 0) red[4 * t + warp] = part;
+    }
+    __syncthreads();
+    if (threadIdx.x < T) {
+      const int t = threadIdx.x;
+      const double sum = __dadd_rn(__dadd_rn(red[4 * t], red[4 * t + 1]), __dadd_rn(red[4 * t + 2], red[4 * t + 3]));
+      const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)d.H), (double)d.eps)));
       float inv = __double2float_rn(r);
       if (!f32_rounding_stable(r, 0x1p-38)) {
+        const float *x = xs + t * xstride;
         double ser = 0.0;  // the reference's serial order
         for (int k = 0; k < d.H; k++) {
           const double v = (double)x[k];
@@ -401,14 +547,30 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
         }
         inv = rms_inv_from_sum(ser, (size_t)d.H, d.eps);
       }
-      red[warp] = (double)inv;
+      s_inv[t] = inv;
     }
-    __syncwarp();
-    const float inv = (float)red[warp];
-    for (int k = lane; k < d.H; k += 32) x[k] = __fmul_rn(__fmul_rn(x[k], inv), nw[k]);
-    __syncwarp();
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * d.H; i += blockDim.x) {
+      const int t = i / d.H, k = i % d.H;
+      float *x = xs + t * xstride + k;
+      *x = __fmul_rn(__fmul_rn(*x, s_inv[t]), nw[k]);
+    }
   }
   __syncthreads();
+  // The Q8_K rows of the normed tokens and the normed tap do not depend on
+  // the routing: CTA e's warps 1-3 write block e (of T*hb) while warp 0
+  // runs the router chain.
+  if (warp > 0) {
+    for (int tb = e0 + (int)gridDim.x * (warp - 1); tb < T * d.hb; tb += 3 * (int)gridDim.x) {
+      const int t = tb / d.hb, b = tb % d.hb;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = xs[t * xstride + b * 256 + 8 * lane + e];
+      q8k_quantize_warp(v, lane, B.acts + (size_t)t * d.act_stride + (size_t)b * 292);
+#pragma unroll
+      for (int e = 0; e < 8; e++) B.normed[(size_t)t * d.H + b * 256 + 8 * lane + e] = v[e];
+    }
+  }
   RV_PHASE(0, 3);
   RV_PHASE(0, 4);
   // Router logits: acc = acc + router[e][k] * normed[t][k], k = 0..H-1.
@@ -429,21 +591,18 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   __threadfence();
   for (int e = threadIdx.x; e < 256; e += blockDim.x) s_cnt[e] = 0;
   __syncthreads();
-  // Routing on warps 0.., normed and its Q8_K on the others (all when T > 3).
-  const int rw = min(T, 4);
-  for (int t = warp; t < T; t += 4) route_token_warp(d, B, t, lane, es[warp], s_cnt);
-  for (int tb = warp - (rw < 4 ? rw : 0); tb >= 0 && tb < T * d.hb; tb += (rw < 4 ? 4 - rw : 4)) {
-    const int t = tb / d.hb, b = tb % d.hb;
-    float v[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) v[e] = xs[t * xstride + b * 256 + 8 * lane + e];
-    q8k_quantize_warp(v, lane, B.acts + (size_t)t * d.act_stride + (size_t)b * 292);
-#pragma unroll
-    for (int e = 0; e < 8; e++) B.normed[(size_t)t * d.H + b * 256 + 8 * lane + e] = v[e];
+  // Routing: one or two tokens by the whole CTA, more by one warp each.
+  if (T <= 2) {
+    __shared__ float s_ps[256], s_sel[16];
+    __shared__ double s_red[8];
+    for (int t = 0; t < T; t++) route_token_block(d, B, t, es[0], s_ps, s_sel, s_red, s_cnt);
+  } else {
+    for (int t = warp; t < T; t += 4) route_token_warp(d, B, t, lane, es[warp], s_cnt);
   }
   __syncthreads();
   RV_PHASE(0, 7);
-  build_index_cta(d, B, s_cnt, s_st, s_cur, s_us);
+  if (T * d.K <= 32) build_index_small(d, B);
+  else build_index_cta(d, B, s_cnt, s_st, s_cur, s_us);
   RV_PHASE(0, 8);
 }
 
