@@ -94,6 +94,8 @@ static size_t sat_mul(size_t a, size_t b) {
 static std::mutex g_init_mu;
 static bool g_dev_ready[64];
 
+#define RV_ROUTE_SMEM_ONE_PER_SM (120u * 1024u)
+
 static int ensure_device(int dev) {
   if (dev < 0 || dev >= 64) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_init_mu);
@@ -988,7 +990,10 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   B.ms = T < RV_MOE_MT ? T : RV_MOE_MT;
   if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch
-    const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)T * (d.H + 4) * 4 + 4 * (size_t)T * sizeof(double) + 16;
+    // Shared memory padded past half an SM's so that no two routing CTAs
+    // (each running one serial router chain) share an SM.
+    const size_t need = 16 + (size_t)2 * d.H * 4 + (size_t)T * (d.H + 4) * 4 + 4 * (size_t)T * sizeof(double) + 16;
+    const size_t smem = need < RV_ROUTE_SMEM_ONE_PER_SM ? RV_ROUTE_SMEM_ONE_PER_SM : need;
     RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
   } else {
     if ((rc = route_stage(d, B, T, s))) return rc;
