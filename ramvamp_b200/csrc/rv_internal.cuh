@@ -172,7 +172,15 @@ RV_DEVFN long long rv_globaltimer() {
     if (blockIdx.x == 0 && blockIdx.y == 20 && (stage) < RV_PHASE_CTAS)                \
       g_rv_phase[k][stage][ev] = rv_globaltimer();                                     \
   } while (0)
+// Event ev of the decode routing tail (the last routing CTA, thread 0).
+#define RV_TRACE_TAIL(ev)                                                      \
+  do {                                                                        \
+    if (threadIdx.x == 0) g_rv_phase[3][0][ev] = rv_globaltimer();            \
+  } while (0)
 #else
+#define RV_TRACE_TAIL(ev) \
+  do {                    \
+  } while (0)
 #define RV_TRACE(k, stage, ev) \
   do {                         \
   } while (0)

@@ -197,7 +197,7 @@ RV_DEVFN void route_token_warp(const MoeDims &d, const MoeBufs &B, int t, int la
 // number; otherwise warp 0 runs the warp version.  Scratch: es [256]
 // doubles, ps [256] floats, sel [16] floats, red [8] doubles, flag.
 RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, double *es, float *ps, float *sel,
-                                double *red, int *counts) {
+                                double *red, int *counts, uint32_t *sids) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float *lg = B.logits + (size_t)t * d.E;
   float x[2];
@@ -210,10 +210,12 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(RV_FULL, mx, o));
+  RV_TRACE_TAIL(0);
   float *redf = (float *)(red + 4);
   if (lane == 0) redf[warp] = mx;
   __syncthreads();
   mx = fmaxf(fmaxf(redf[0], redf[1]), fmaxf(redf[2], redf[3]));
+  RV_TRACE_TAIL(1);
   const double dmx = (double)mx;
   double part = 0.0;
   float pf[2];
@@ -230,9 +232,11 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+  RV_TRACE_TAIL(2);
   __syncthreads();  // redf reads done, es complete
   if (lane == 0) red[warp] = part;
   __syncthreads();
+  RV_TRACE_TAIL(3);
   // Any order of these <= 256 non-negative terms is within 2^-44 relative of
   // the reference's serial sum; recompute serially when 1/sum is that close
   // to a float rounding midpoint.
@@ -254,8 +258,11 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
     }
   }
   const bool all_finite = __syncthreads_and(finite);
+  RV_TRACE_TAIL(4);
   if (!all_finite) {
     if (warp == 0) route_token_warp(d, B, t, lane, es, counts);
+    __syncthreads();
+    if (tid < d.K) sids[t * d.K + tid] = __ldcg(B.ids + (size_t)t * d.K + tid);
     __syncthreads();
     return;
   }
@@ -264,19 +271,33 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
     const int e = tid + 128 * j;
     if (e < d.E) {
       const float p = ps[e];
-      int rank = 0;
-      for (int i = 0; i < d.E; i++) {
-        const float q = ps[i];
-        rank += (q > p) | ((q == p) & (i < e));
+      // ps is padded with -inf to a multiple of 16 entries: 16 independent
+      // compares per step, four vector loads.
+      int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+      for (int i = 0; i < d.E; i += 16) {
+        const float4 a = *(const float4 *)(ps + i), b = *(const float4 *)(ps + i + 4);
+        const float4 c = *(const float4 *)(ps + i + 8), f = *(const float4 *)(ps + i + 12);
+        r0 += (a.x > p) + ((a.x == p) & (i + 0 < e)) + (a.y > p) + ((a.y == p) & (i + 1 < e)) + (a.z > p) +
+              ((a.z == p) & (i + 2 < e)) + (a.w > p) + ((a.w == p) & (i + 3 < e));
+        r1 += (b.x > p) + ((b.x == p) & (i + 4 < e)) + (b.y > p) + ((b.y == p) & (i + 5 < e)) + (b.z > p) +
+              ((b.z == p) & (i + 6 < e)) + (b.w > p) + ((b.w == p) & (i + 7 < e));
+        r2 += (c.x > p) + ((c.x == p) & (i + 8 < e)) + (c.y > p) + ((c.y == p) & (i + 9 < e)) + (c.z > p) +
+              ((c.z == p) & (i + 10 < e)) + (c.w > p) + ((c.w == p) & (i + 11 < e));
+        r3 += (f.x > p) + ((f.x == p) & (i + 12 < e)) + (f.y > p) + ((f.y == p) & (i + 13 < e)) + (f.z > p) +
+              ((f.z == p) & (i + 14 < e)) + (f.w > p) + ((f.w == p) & (i + 15 < e));
       }
+      const int rank = r0 + r1 + r2 + r3;
       if (rank < d.K) {
         B.ids[(size_t)t * d.K + rank] = (uint32_t)e;
+        sids[t * d.K + rank] = (uint32_t)e;
         sel[rank] = p;
         atomicAdd(&counts[e], 1);
       }
     }
   }
+  RV_TRACE_TAIL(5);
   __syncthreads();
+  RV_TRACE_TAIL(6);
   if (tid < d.K) {
     float wsum = -0.0f;  // the in-order sum of the selected weights
     for (int k = 0; k < d.K; k++) wsum = __fadd_rn(wsum, sel[k]);
@@ -284,6 +305,7 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
     B.w[(size_t)t * d.K + tid] = w;
   }
   __syncthreads();
+  RV_TRACE_TAIL(7);
 }
 
 __global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
@@ -366,19 +388,19 @@ RV_DEVFN void build_index_cta(const MoeDims &d, const MoeBufs &B, int *s_cnt, ui
 
 // The dispatch index for at most 32 pairs (decode): positions in expert
 // order (pairs of one expert in pair order), per-expert CSR starts, one
-// work unit per distinct expert.  ids were written by this CTA (visible
-// after the caller's __syncthreads).
-RV_DEVFN void build_index_small(const MoeDims &d, const MoeBufs &B) {
+// work unit per distinct expert.  sids: the pairs' expert ids in shared
+// memory.
+RV_DEVFN void build_index_small(const MoeDims &d, const MoeBufs &B, const uint32_t *sids) {
   const int P = B.T * d.K;
   const int tid = threadIdx.x;
   for (int e = tid; e <= d.E; e += blockDim.x) {
     int below = 0;
-    for (int q = 0; q < P; q++) below += B.ids[q] < (uint32_t)e;
+    for (int q = 0; q < P; q++) below += sids[q] < (uint32_t)e;
     B.index_start[e] = (uint32_t)below;
   }
   if (tid < 32) {
     const int p = tid;
-    const uint32_t e = p < P ? B.ids[p] : 0xFFFFFFFFu;
+    const uint32_t e = p < P ? sids[p] : 0xFFFFFFFFu;
     int pos = 0, cnt = 0;
     bool first = true;
     for (int q = 0; q < P; q++) {
@@ -592,16 +614,20 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   for (int e = threadIdx.x; e < 256; e += blockDim.x) s_cnt[e] = 0;
   __syncthreads();
   // Routing: one or two tokens by the whole CTA, more by one warp each.
+  __shared__ uint32_t s_ids[32];
   if (T <= 2) {
-    __shared__ float s_ps[256], s_sel[16];
+    __shared__ __align__(16) float s_ps[256];
+    __shared__ float s_sel[16];
     __shared__ double s_red[8];
-    for (int t = 0; t < T; t++) route_token_block(d, B, t, es[0], s_ps, s_sel, s_red, s_cnt);
+    for (int t = 0; t < T; t++) route_token_block(d, B, t, es[0], s_ps, s_sel, s_red, s_cnt, s_ids);
   } else {
     for (int t = warp; t < T; t += 4) route_token_warp(d, B, t, lane, es[warp], s_cnt);
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * d.K && i < 32; i += blockDim.x) s_ids[i] = __ldcg(B.ids + i);
   }
   __syncthreads();
   RV_PHASE(0, 7);
-  if (T * d.K <= 32) build_index_small(d, B);
+  if (T * d.K <= 32) build_index_small(d, B, s_ids);
   else build_index_cta(d, B, s_cnt, s_st, s_cur, s_us);
   RV_PHASE(0, 8);
 }
