@@ -756,7 +756,7 @@ static void launch_gate_up_t(const MoeDims &d, const MoeBufs &B, const MoeWeight
                       (FMT == RV_Q6_K ? (size_t)B.ms * d.hb * 64 * 4 : 0) + 2 * R * RV_MOE_MT * 4;
   dim3 grid((unsigned)B.max_units, (unsigned)(d.M / R));
   cudaFuncSetAttribute(k_gate_up<FMT, G, NBG, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_gate_up<FMT, G, NBG, R><<<grid, 2 * R * G, smem, s>>>(d, B, W);
+  launch_pdl(k_gate_up<FMT, G, NBG, R>, grid, dim3(2 * R * G), smem, s, d, B, W);
 }
 template <int FMT>
 static void launch_gate_up(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int T, cudaStream_t s) {

@@ -600,6 +600,9 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
     B.logits[(size_t)lane * d.E + e0 + warp] =
         serial_dot_f32((const float4 *)(rows + warp * d.H), (const float4 *)(xs + lane * xstride), d.H / 4);
   RV_PHASE(0, 5);
+  // The expert kernel may launch now (it waits for this grid's completion
+  // before reading the routing): its CTAs are resident when routing ends.
+  pdl_trigger();
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -735,12 +738,17 @@ RV_DEVFN uint32_t stage_rows(uint8_t *dst, const uint8_t *src, size_t row_bytes,
 // NBG blocks each); G == 1: token mode (a thread per row, up to 8 tokens in
 // flight).  2*R*G/32 warps.  Then SwiGLU with the host-libm exponential, and
 // the last of the tiles of each 256-row block quantizes that block of every
-// token.  The kernel lets the next (down) kernel launch at once.
+// token.  Launched as a programmatic dependent of the routing kernel; lets
+// the next (down) kernel launch at once.
 template <int FMT, int G, int NBG, int R>
 __global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d, MoeBufs B, MoeWeights W) {
   extern __shared__ __align__(16) uint8_t sm[];
   constexpr int MT = RV_MOE_MT, RPW = 32 / G, NW = 2 * R * G / 32;
   RV_PHASE(1, 0);
+  // The dispatch index and activations are the routing kernel's output.
+  // The down kernel reads the index before its own wait, so it may launch
+  // only once the routing grid has completed: trigger after the wait.
+  pdl_wait();
   pdl_trigger();
   const int u = blockIdx.x, tile = blockIdx.y;
   if (u >= *B.n_units) return;
