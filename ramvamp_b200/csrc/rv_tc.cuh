@@ -32,8 +32,9 @@
 #define RV_TC_NT 128       // pair columns per tile
 #define RV_TC_ROWS 128     // weight rows per CTA (the MMA's M)
 #define RV_TC_KS 64        // K elements per shared-memory stage
-#define RV_TC_THREADS 576  // 18 warps: 5 per scheduler at 96 registers fills its 16K-register file
-#define RV_TC_WORK_WARPS 16
+#define RV_TC_THREADS 640  // 20 warps: 5 per scheduler at 96 registers fills its 16K-register file
+#define RV_TC_PROD_WARPS 8
+#define RV_TC_EPI_WARPS 8
 
 // ------------------------------------------------------ tcgen05 wrappers
 RV_DEVFN void tc_alloc(uint32_t *dst, uint32_t ncols) {
@@ -91,8 +92,16 @@ RV_DEVFN uint64_t tc_desc(uint32_t saddr, uint32_t sbo) {
 RV_DEVFN uint32_t tc_idesc(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(RV_TC_ROWS >> 4) << 24);
 }
-// Byte offset of 16-byte chunk `chunk` (8 f16 of K) of row `row` in a tile
-// with `cpr` chunks per row.
+// Byte offset of 16-byte chunk `chunk` (8 f16 of K) of row `row` in a
+// [rows][64] K-major tile in the 128-byte-swizzle canonical layout: 8-row
+// atoms of 1024 bytes, row r of an atom at r*128 with its chunks permuted by
+// c ^ r (so the tensor core's reads of one K slice across rows hit
+// different banks).  Atoms must be 1024-byte aligned.
+RV_DEVFN uint32_t tc_sw_off(int row, int chunk) {
+  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
+}
+// Byte offset of 16-byte chunk `chunk` of row `row` in a tile without
+// swizzle with `cpr` chunks per row (the K=16 mins operands).
 RV_DEVFN uint32_t tc_core_off(int row, int chunk, int cpr = 8) {
   return (uint32_t)(((row >> 3) * cpr + chunk) * 128 + (row & 7) * 16);
 }
@@ -116,27 +125,29 @@ RV_DEVFN uint32_t tc_lv2(uint32_t x, uint32_t mask, __half2 s, __half2 c) {
   return tc_fma2((x & mask) | 0x64006400u, s, c);
 }
 
-// Quarter qr (16 elements, chunks 2qr, 2qr+1) of stage j of a Q4_K / Q5_K
-// super-block (16-byte aligned in shared memory) for row r: values sc*q of
-// sub-block 2j + qr/2.  u0..u3: the block's scales and mins
-// (k4_unpack_words).  Stage 0 also writes, for qr < 2, chunk qr of the row's
-// K=16 mins operand: m_0..m_7 (qr = 0) or 32*m_0..32*m_7 (qr = 1).
+// Half h (sub-block 2j+h: 32 elements, chunks 4h..4h+3) of stage j of a
+// Q4_K / Q5_K super-block (16-byte aligned in shared memory) for row r:
+// values sc*q.  u0..u3: the block's scales and mins (k4_unpack_words).
+// Stage 0 also writes chunk h of the row's K=16 mins operand: m_0..m_7
+// (h = 0) or 32*m_0..32*m_7 (h = 1).
 template <int FMT>
-RV_DEVFN void tc_stage_k45(const uint8_t *blk, int j, int qr, uint32_t u0, uint32_t u1, uint32_t u2, uint32_t u3,
+RV_DEVFN void tc_stage_k45(const uint8_t *blk, int j, int h, uint32_t u0, uint32_t u1, uint32_t u2, uint32_t u3,
                            uint8_t *a, uint8_t *a2, int r) {
-  const int hs = qr >> 1, sb = 2 * j + hs;
+  const int sb = 2 * j + h;
   const int sc = byte_of(j < 2 ? u0 : u1, sb & 3);
   const __half2 s2 = tc_h2i(sc), c2 = tc_h2i(-1024 * sc);
-  const uint4 qv = *(const uint4 *)(blk + (FMT == RV_Q4_K ? 16 : 48) + 32 * j + 16 * (qr & 1));
-  const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
-  uint32_t hw[4];
+  const uint8_t *qs = blk + (FMT == RV_Q4_K ? 16 : 48) + 32 * j;
+  const uint4 qa = *(const uint4 *)qs, qb = *(const uint4 *)(qs + 16);
+  const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  uint32_t hw[8];
   if constexpr (FMT == RV_Q5_K) {
-    const uint4 hv = *(const uint4 *)(blk + 16 + 16 * (qr & 1));
-    hw[0] = hv.x; hw[1] = hv.y; hw[2] = hv.z; hw[3] = hv.w;
+    const uint4 ha = *(const uint4 *)(blk + 16), hb = *(const uint4 *)(blk + 32);
+    hw[0] = ha.x; hw[1] = ha.y; hw[2] = ha.z; hw[3] = ha.w;
+    hw[4] = hb.x; hw[5] = hb.y; hw[6] = hb.z; hw[7] = hb.w;
   }
-  const int sh = 4 * hs;
+  const int sh = 4 * h;
 #pragma unroll
-  for (int cc = 0; cc < 2; cc++) {
+  for (int cc = 0; cc < 4; cc++) {
     uint32_t o[4];
 #pragma unroll
     for (int t = 0; t < 2; t++) {
@@ -153,10 +164,10 @@ RV_DEVFN void tc_stage_k45(const uint8_t *blk, int j, int qr, uint32_t u0, uint3
         o[2 * t + 1] = tc_lv2(x1, 0x000F000Fu, s2, c2);
       }
     }
-    *(uint4 *)(a + tc_core_off(r, 2 * qr + cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *(uint4 *)(a + tc_sw_off(r, 4 * h + cc)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
-  if (j == 0 && qr < 2) {  // the mins operand is in natural order on both sides
-    const float f = qr ? 32.0f : 1.0f;
+  if (j == 0) {  // the mins operand is in natural order on both sides
+    const float f = h ? 32.0f : 1.0f;
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; k++) {
@@ -164,36 +175,40 @@ RV_DEVFN void tc_stage_k45(const uint8_t *blk, int j, int qr, uint32_t u0, uint3
       __half2 t2 = __floats2half2_rn((float)byte_of(mw, (2 * k) & 3) * f, (float)byte_of(mw, (2 * k + 1) & 3) * f);
       o[k] = *(uint32_t *)&t2;
     }
-    *(uint4 *)(a2 + tc_core_off(r, qr, 2)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *(uint4 *)(a2 + tc_core_off(r, h, 2)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
-// Quarter qr (16 elements of group g = 2(j&1) + qr/2, one scale) of stage j
-// of a Q6_K super-block at any even address (rows of a whole-tile copy are
-// 630 bytes apart; words go through ld32u) for row r: sl*(q-32) into a and
-// sh*(q-32) into ah, scale = 32*sh + sl.
-RV_DEVFN void tc_stage_q6(const uint8_t *blk, int j, int qr, uint8_t *a, uint8_t *ah, int r) {
-  const int hh = j >> 1, g = 2 * (j & 1) + (qr >> 1), l0 = 16 * (qr & 1);
-  const uint8_t *ql = blk + 64 * hh + 32 * (g & 1) + l0, *qh = blk + 128 + 32 * hh + l0;
+// Half h (group g = 2(j&1) + h, 32 elements, scales for elements 0-15 and
+// 16-31) of stage j of a Q6_K super-block at any even address (rows of a
+// whole-tile copy are 630 bytes apart; words go through ld32u) for row r:
+// sl*(q-32) into a and sh*(q-32) into ah, scale = 32*sh + sl.
+RV_DEVFN void tc_stage_q6(const uint8_t *blk, int j, int h, uint8_t *a, uint8_t *ah, int r) {
+  const int hh = j >> 1, g = 2 * (j & 1) + h;
+  const uint8_t *ql = blk + 64 * hh + 32 * (g & 1), *qh = blk + 128 + 32 * hh;
   const int lsh = 4 * (g >> 1), hsh = 2 * g;
-  const int sc = (int8_t)blk[192 + 8 * hh + 2 * g + (qr & 1)];
-  const __half2 sl = tc_h2i(sc & 31), sh = tc_h2i(sc >> 5);
-  const __half2 cl = tc_h2i(-1056 * (sc & 31)), chh = tc_h2i(-1056 * (sc >> 5));
 #pragma unroll
-  for (int cc = 0; cc < 2; cc++) {
-    uint32_t oa[4], oh[4];
+  for (int half16 = 0; half16 < 2; half16++) {
+    const int sc = (int8_t)blk[192 + 8 * hh + 2 * g + half16];
+    const __half2 sl = tc_h2i(sc & 31), sh = tc_h2i(sc >> 5);
+    const __half2 cl = tc_h2i(-1056 * (sc & 31)), chh = tc_h2i(-1056 * (sc >> 5));
 #pragma unroll
-    for (int t = 0; t < 2; t++) {
-      const uint32_t lw = ld32u(ql + 8 * cc + 4 * t), hw = ld32u(qh + 8 * cc + 4 * t);
-      const uint32_t q6 = ((lw >> lsh) & 0x0F0F0F0Fu) | (((hw >> hsh) & 0x03030303u) << 4);
-      oa[2 * t] = tc_lv2(q6, 0x003F003Fu, sl, cl);
-      oa[2 * t + 1] = tc_lv2(q6 >> 8, 0x003F003Fu, sl, cl);
-      oh[2 * t] = tc_lv2(q6, 0x003F003Fu, sh, chh);
-      oh[2 * t + 1] = tc_lv2(q6 >> 8, 0x003F003Fu, sh, chh);
+    for (int c2 = 0; c2 < 2; c2++) {
+      const int cc = 2 * half16 + c2;
+      uint32_t oa[4], oh[4];
+#pragma unroll
+      for (int t = 0; t < 2; t++) {
+        const uint32_t lw = ld32u(ql + 8 * cc + 4 * t), hw = ld32u(qh + 8 * cc + 4 * t);
+        const uint32_t q6 = ((lw >> lsh) & 0x0F0F0F0Fu) | (((hw >> hsh) & 0x03030303u) << 4);
+        oa[2 * t] = tc_lv2(q6, 0x003F003Fu, sl, cl);
+        oa[2 * t + 1] = tc_lv2(q6 >> 8, 0x003F003Fu, sl, cl);
+        oh[2 * t] = tc_lv2(q6, 0x003F003Fu, sh, chh);
+        oh[2 * t + 1] = tc_lv2(q6 >> 8, 0x003F003Fu, sh, chh);
+      }
+      const uint32_t off = tc_sw_off(r, 4 * h + cc);
+      *(uint4 *)(a + off) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+      *(uint4 *)(ah + off) = make_uint4(oh[0], oh[1], oh[2], oh[3]);
     }
-    const uint32_t off = tc_core_off(r, 2 * qr + cc);
-    *(uint4 *)(a + off) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
-    *(uint4 *)(ah + off) = make_uint4(oh[0], oh[1], oh[2], oh[3]);
   }
 }
 
@@ -244,12 +259,13 @@ RV_DEVFN uint32_t tc_padded(const MoeDims &d, const MoeBufs &B, uint32_t pos) {
 
 // Operand B in global memory is stage-major, so that one stage of a tile
 // (8-row groups g0.. g0+ng, K elements 64*it.. 64*it+63) is one contiguous
-// run of ng KB: f16 element (row pp, k) of a matrix with G 8-row groups
-// sits at ((it*G + pp/8)*8 + chunk)*64 + (pp%8)*8 + k%8, it = k/64,
-// chunk = (k%64)/8.  The K=16 mins operand of super-block b: ((b*G +
+// run of ng KB, already in the 128-byte-swizzle layout: f16 element
+// (row pp, k) of a matrix with G 8-row groups sits at (it*G + pp/8)*512 +
+// (pp%8)*64 + ((chunk ^ pp%8)*8) + k%8, it = k/64, chunk = (k%64)/8.  The K=16 mins operand of super-block b: ((b*G +
 // pp/8)*2 + j/8)*64 + (pp%8)*8 + j%8.
 RV_DEVFN size_t tc_bidx(uint32_t pp, int k, int G) {
-  return ((((size_t)(k >> 6) * G + (pp >> 3)) * 8 + ((k >> 3) & 7)) << 6) + ((pp & 7) << 3) + (k & 7);
+  const uint32_t rr = pp & 7, c = (uint32_t)(k >> 3) & 7;
+  return (((size_t)(k >> 6) * G + (pp >> 3)) << 9) + (rr << 6) + ((c ^ rr) << 3) + (k & 7);
 }
 RV_DEVFN size_t tc_midx(uint32_t pp, int b, int j, int G) {
   return ((((size_t)b * G + (pp >> 3)) * 2 + (j >> 3)) << 6) + ((pp & 7) << 3) + (j & 7);
@@ -332,10 +348,13 @@ struct TcStage {
 // activation ring | s_da [NT][nb] | s_pair [NT] | barriers | tmem address.
 template <int FMT, bool DOWN>
 struct TcCfg {
-  static constexpr int SA = FMT == RV_Q6_K ? 2 : 3;
-  static constexpr int R = DOWN ? 1 : 3;
+  // Deep A pipelines: a stage's buffer comes back only once its MMAs have
+  // completed (about 1 us after issue), so throughput needs many stages in
+  // flight.  Sizes fill the 227 KB of shared memory.
+  static constexpr int SA = !DOWN ? 6 : FMT == RV_Q6_K ? 3 : FMT == RV_Q5_K ? 4 : 5;
+  static constexpr int R = DOWN ? 1 : 2;
   static constexpr int SBMAX = 16;
-  static constexpr size_t RING = (DOWN && FMT == RV_Q6_K) ? 48 * 1024 : 64 * 1024;
+  static constexpr size_t RING = (DOWN && FMT == RV_Q6_K) ? 40 * 1024 : 48 * 1024;
   static constexpr size_t raw = (size_t)SA * TcStage<FMT>::bytes;
   __host__ __device__ static size_t raw_slot(size_t row_bytes) {
     return DOWN ? ((RV_TC_ROWS * row_bytes + 16 + 1023) & ~(size_t)1023)
@@ -364,7 +383,25 @@ RV_DEVFN void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z
       : "memory");
 }
 
-#define RV_TC_W_WORK 2  // warps 2-17: producers and epilogue
+// Warp roles.  A warp's scheduler is warp % 4 and the tensor-memory lanes it
+// may read are 32*(warp % 4)..+31.  The MMA-issuing warp (1) keeps its
+// scheduler nearly to itself: the dequantizing warps sit on schedulers 0,
+// 2 and 3, the eight epilogue warps (two per lane quadrant) mostly sleep.
+RV_DEVFN int tc_prod_index(int warp) {  // -1: not a producer
+  switch (warp) {
+    case 2: return 0;
+    case 3: return 1;
+    case 12: return 2;
+    case 14: return 3;
+    case 15: return 4;
+    case 16: return 5;
+    case 18: return 6;
+    case 19: return 7;
+    default: return -1;
+  }
+}
+#define RV_TC_W_EPI0 4   // warps 4-11: epilogue
+#define RV_TC_W_EPI1 12
 
 // One pair tile x 128 weight rows of one matrix.  Gate/up (DOWN = false):
 // grid.x = 2*M/128 row tiles (gate tiles first), output rows of gu
@@ -373,9 +410,9 @@ RV_DEVFN void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z
 // slabs).  Down: grid.x = H/128, the whole contiguous 128-row tile in one
 // bulk copy, output staged by (token, slot).  grid.y = max_tc pair tiles.
 // Roles: warp 0 lane 0 stages weights and lane 1 activations, warp 1 lane
-// 0 issues the MMAs, warps 2-17 dequantize super-block b and then drain
-// super-block b-1's accumulators out of tensor memory (the epilogue), so
-// the products of block b overlap the epilogue of block b-1.
+// 0 issues the MMAs, eight warps dequantize (two threads per weight row),
+// eight warps drain each super-block's accumulators out of tensor memory
+// while the next block multiplies (the epilogue), two warps idle.
 template <int FMT, bool DOWN>
 __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     k_tc_gemm(MoeDims d, MoeBufs B, MoeWeights W, const __grid_constant__ CUtensorMap wmap) {
@@ -395,7 +432,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   const int nmma = (n + 15) & ~15, ng = nmma / 8, g0 = pp0 / 8;
   const int kdim = DOWN ? d.M : d.H, nb = kdim / 256, NS = 4 * nb;
   const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
-  const size_t slot_b = (size_t)nmma * (128 + (F::MINS ? 32 : 0));
+  const size_t slot_b = ((size_t)nmma * (128 + (F::MINS ? 32 : 0)) + 1023) & ~(size_t)1023;  // 1 KB atoms
   const int SB = min(C::SBMAX, (int)(C::RING / slot_b));
   int mat = 0, row0;
   if constexpr (DOWN) {
@@ -423,10 +460,10 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < R; i++) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], RV_TC_WORK_WARPS);
+      mbar_init(&raw_empty[i], RV_TC_PROD_WARPS);
     }
     for (int i = 0; i < SA; i++) {
-      mbar_init(&a_full[i], RV_TC_WORK_WARPS);
+      mbar_init(&a_full[i], RV_TC_PROD_WARPS);
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < C::SBMAX; i++) {
@@ -435,7 +472,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], RV_TC_WORK_WARPS);
+      mbar_init(&acc_empty[i], RV_TC_EPI_WARPS);
     }
     *s_fail = 0;
   }
@@ -505,8 +542,12 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       // 16-byte units to precomputed low words; ring positions and phases
       // advance without division.
       const uint32_t idesc = tc_idesc(nmma);
-      const uint32_t lbo = (128u >> 4) << 16, hi1024 = (1024u >> 4) | (1u << 14), hi256 = (256u >> 4) | (1u << 14);
-      const uint32_t a_lo0 = lbo | (smem_addr(sm) >> 4), b_lo0 = lbo | (smem_addr(ring) >> 4);
+      // A and B tiles: 128-byte swizzle, SBO 1024 (K advances 32 bytes per
+      // K=16 step inside the swizzled row); mins tiles: no swizzle, LBO 128,
+      // SBO 256.
+      const uint32_t hi_sw = (1024u >> 4) | (1u << 14) | (2u << 29), hi256 = (256u >> 4) | (1u << 14);
+      const uint32_t lbo_sw = 1u << 16, lbo_none = (128u >> 4) << 16;
+      const uint32_t a_lo0 = smem_addr(sm) >> 4, b_lo0 = smem_addr(ring) >> 4;
       const uint32_t b_step = (uint32_t)(slot_b >> 4), a_step = (uint32_t)(SL::bytes >> 4);
       auto mk = [](uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; };
       int sa = 0, sb = 0;
@@ -536,12 +577,15 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
           if (it == 0) RV_PHASE_ANY(PK, 3);
           const uint32_t al = a_lo0 + (uint32_t)sa * a_step, bl = b_lo0 + (uint32_t)sb * b_step;
           if (F::MINS && j == 0)
-            tc_mma_f16(d2, mk(al + (uint32_t)(SL::a2 >> 4), hi256), mk(bl + (uint32_t)nmma * 8, hi256), idesc, 0u);
+            tc_mma_f16(d2, mk(lbo_none | (al + (uint32_t)(SL::a2 >> 4)), hi256),
+                       mk(lbo_none | (bl + (uint32_t)nmma * 8), hi256), idesc, 0u);
 #pragma unroll
           for (int kk = 0; kk < 4; kk++) {
             const uint32_t acc = (j | kk) != 0;
-            tc_mma_f16(d1, mk(al + 16 * kk, hi1024), mk(bl + 16 * kk, hi1024), idesc, acc);
-            if (F::SPLIT) tc_mma_f16(d2, mk(al + (uint32_t)(SL::ah >> 4) + 16 * kk, hi1024), mk(bl + 16 * kk, hi1024), idesc, acc);
+            tc_mma_f16(d1, mk(lbo_sw | (al + 2 * kk), hi_sw), mk(lbo_sw | (bl + 2 * kk), hi_sw), idesc, acc);
+            if (F::SPLIT)
+              tc_mma_f16(d2, mk(lbo_sw | (al + (uint32_t)(SL::ah >> 4) + 2 * kk), hi_sw), mk(lbo_sw | (bl + 2 * kk), hi_sw),
+                         idesc, acc);
           }
           RV_TRACE(PK + 2, it, 9);
           tc_commit(&a_empty[sa]);
@@ -562,61 +606,60 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       if (!ok) *s_fail = 1;
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------- producers + epilogue
-    // Producing, thread p takes weight row p & 127, quarter p >> 7 of every
-    // stage.  Draining, thread (quadrant q, lane) owns weight row 32q + lane
-    // (its tensor-memory lane) and the 8-column chunks cq, cq+4, cq+8, cq+12
-    // of the tile, so small tiles spread over all sixteen warps.
-    const int p = threadIdx.x - 32 * RV_TC_W_WORK, r = p & 127, qr = p >> 7;
-    const int q = warp & 3, cq = (warp - RV_TC_W_WORK) >> 2, er = 32 * q + lane;
-    const uint8_t *hrow = wsrc + (size_t)er * rb;  // the drained row's super-block headers (global)
-    float acc[2][16];
-#pragma unroll
-    for (int c = 0; c < 2; c++)
-#pragma unroll
-      for (int i = 0; i < 16; i++) acc[c][i] = 0.0f;
+  } else if (tc_prod_index(warp) >= 0) {
+    // ------------------------------------------------------ producers
+    // Thread p: weight row p & 127, half p >> 7 of every stage.
+    const int p = 32 * tc_prod_index(warp) + lane, r = p & 127, h = p >> 7;
     bool ok = true;
     if (DOWN) ok = tc_wait_warp(&raw_full[0], 0);
     uint32_t u0 = 0, u1 = 0, u2 = 0, u3 = 0;
-    uint32_t hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + 208) : *(const uint32_t *)hrow;
-    for (int b = 0; b <= nb && ok; b++) {
-      if (b < nb) {
-        for (int j = 0; j < 4; j++) {
-          const int it = 4 * b + j, sa = it % SA;
-          if (!DOWN && j == 0 && !tc_wait_warp(&raw_full[b % R], (b / R) & 1)) {
-            ok = false;
-            break;
-          }
-          if (p == 0 && j == 0) RV_TRACE(PK + 2, it, 8);
-          const uint8_t *blk = DOWN ? raw + (size_t)r * rb + (size_t)b * BB : raw + (b % R) * rslot + (size_t)r * BB;
-          if (F::MINS && j == 0) {
-            const uint4 hdr = *(const uint4 *)blk;
-            k4_unpack_words(hdr.y, hdr.z, hdr.w, u0, u1, u2, u3);
-          }
-          if (!tc_wait_warp(&a_empty[sa], ((it / SA) & 1) ^ 1)) {
-            ok = false;
-            break;
-          }
-          if (it == 0 && p == 0) RV_PHASE_ANY(PK, 5);
-          if (p == 0) RV_TRACE(PK + 2, it, 0);
-          uint8_t *st = sm + (size_t)sa * SL::bytes;
-          if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, qr, st + SL::a, st + SL::ah, r);
-          else tc_stage_k45<FMT>(blk, j, qr, u0, u1, u2, u3, st + SL::a, st + SL::a2, r);
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&a_full[sa]);
-            if (!DOWN && j == 3) mbar_arrive(&raw_empty[b % R]);
-          }
-          if (p == 0) RV_TRACE(PK + 2, it, 1);
-        }
-        if (!ok) break;
-        if (b == nb - 1 && p == 0) RV_PHASE_ANY(PK, 6);
+    for (int it = 0; it < NS && ok; it++) {
+      const int b = it >> 2, j = it & 3, sa = it % SA;
+      if (!DOWN && j == 0 && !tc_wait_warp(&raw_full[b % R], (b / R) & 1)) {
+        ok = false;
+        break;
       }
-      if (b == 0) continue;
-      // ---- epilogue of super-block eb = b - 1
-      const int eb = b - 1, slot = eb & 1;
+      if (p == 0 && j == 0) RV_TRACE(PK + 2, it, 8);
+      const uint8_t *blk = DOWN ? raw + (size_t)r * rb + (size_t)b * BB : raw + (b % R) * rslot + (size_t)r * BB;
+      if (F::MINS && j == 0) {
+        const uint4 hdr = *(const uint4 *)blk;
+        k4_unpack_words(hdr.y, hdr.z, hdr.w, u0, u1, u2, u3);
+      }
+      if (!tc_wait_warp(&a_empty[sa], ((it / SA) & 1) ^ 1)) {
+        ok = false;
+        break;
+      }
+      if (it == 0 && p == 0) RV_PHASE_ANY(PK, 5);
+      if (p == 0) RV_TRACE(PK + 2, it, 0);
+      uint8_t *st = sm + (size_t)sa * SL::bytes;
+      if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, h, st + SL::a, st + SL::ah, r);
+      else tc_stage_k45<FMT>(blk, j, h, u0, u1, u2, u3, st + SL::a, st + SL::a2, r);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[sa]);
+        if (!DOWN && j == 3) mbar_arrive(&raw_empty[b % R]);
+      }
+      if (p == 0) RV_TRACE(PK + 2, it, 1);
+    }
+    if (p == 0) RV_PHASE_ANY(PK, 6);
+    if (!ok) *s_fail = 1;
+  } else if (warp >= RV_TC_W_EPI0 && warp < RV_TC_W_EPI1) {
+    // ------------------------------------------------------- epilogue
+    // Thread (quadrant q, lane) owns weight row 32q + lane (its tensor-
+    // memory lane) and the 8-column chunks half, half+2, ..., half+14 of the
+    // tile, so small tiles spread over both warps of a quadrant.
+    const int q = warp & 3, half = (warp - RV_TC_W_EPI0) >> 2, er = 32 * q + lane;
+    const uint8_t *hrow = wsrc + (size_t)er * rb;  // the drained row's super-block headers (global)
+    float acc[8][8];
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+#pragma unroll
+      for (int i = 0; i < 8; i++) acc[c][i] = 0.0f;
+    bool ok = true;
+    uint32_t hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + 208) : *(const uint32_t *)hrow;
+    for (int eb = 0; eb < nb; eb++) {
+      const int slot = eb & 1;
       const uint32_t hdr = hdr_next;
       if (eb + 1 < nb)
         hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + (size_t)(eb + 1) * BB + 208)
@@ -627,30 +670,29 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
         break;
       }
       tc_fence_after();
-      if (eb == 0 && p == 0) RV_PHASE_ANY(PK, 7);
-      if (p == 0) RV_TRACE(PK + 2, 4 * eb, 7);
+      if (eb == 0 && warp == RV_TC_W_EPI0 && lane == 0) RV_PHASE_ANY(PK, 7);
+      if (warp == RV_TC_W_EPI0 && lane == 0) RV_TRACE(PK + 2, 4 * eb, 7);
       const uint32_t t1 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(slot * 2 * RV_TC_NT);
 #pragma unroll
-      for (int c8 = 0; c8 < 4; c8++) {
-        const int col = 8 * (cq + 4 * c8);
+      for (int c = 0; c < 8; c++) {
+        const int col = 8 * (half + 2 * c);
         if (col < nmma) {
           uint32_t v1[8], v2[8];
           tc_ld8(t1 + (uint32_t)col, v1);
           tc_ld8(t1 + (uint32_t)(RV_TC_NT + col), v2);
           tc_wait_ld();
 #pragma unroll
-          for (int i8 = 0; i8 < 8; i8++) {
-            const float da = s_da[(col + i8) * nb + eb];
+          for (int i = 0; i < 8; i++) {
+            const float da = s_da[(col + i) * nb + eb];
             float blocksum;
             if constexpr (FMT == RV_Q6_K) {
-              const int sumi = __float2int_rn(__uint_as_float(v1[i8])) + 32 * __float2int_rn(__uint_as_float(v2[i8]));
+              const int sumi = __float2int_rn(__uint_as_float(v1[i])) + 32 * __float2int_rn(__uint_as_float(v2[i]));
               blocksum = __fmul_rn(__fmul_rn(dw, da), __int2float_rn(sumi));
             } else {
               const float dd = __fmul_rn(dw, da), dm = __fmul_rn(dmw, da);
-              blocksum = __fsub_rn(__fmul_rn(dd, __uint_as_float(v1[i8])), __fmul_rn(dm, __uint_as_float(v2[i8])));
+              blocksum = __fsub_rn(__fmul_rn(dd, __uint_as_float(v1[i])), __fmul_rn(dm, __uint_as_float(v2[i])));
             }
-            float &ac = acc[c8 >> 1][8 * (c8 & 1) + i8];
-            ac = __fadd_rn(ac, blocksum);
+            acc[c][i] = __fadd_rn(acc[c][i], blocksum);
           }
         }
       }
@@ -658,13 +700,13 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[slot]);
     }
-    if (p == 0) RV_PHASE_ANY(PK, 8);
+    if (warp == RV_TC_W_EPI0 && lane == 0) RV_PHASE_ANY(PK, 8);
     if (ok && !*s_fail) {
 #pragma unroll
-      for (int c = 0; c < 2; c++)
+      for (int c = 0; c < 8; c++)
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const int col = 8 * (cq + 4 * (2 * c + (i >> 3))) + (i & 7);
+        for (int i = 0; i < 8; i++) {
+          const int col = 8 * (half + 2 * c) + i;
           if (col < n) {
             if constexpr (DOWN) B.staged[(size_t)s_pair[col] * d.H + row0 + er] = acc[c][i];
             else B.gu[(size_t)(p0 + col) * 2 * d.M + (size_t)mat * d.M + row0 + er] = acc[c][i];
