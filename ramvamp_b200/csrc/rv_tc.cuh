@@ -335,27 +335,39 @@ struct TcFmt {
   static constexpr bool MINS = FMT != RV_Q6_K;   // second accumulator: sumi_mins
   static constexpr bool SPLIT = FMT == RV_Q6_K;  // second accumulator: the sh part of the scale
 };
-// One A stage: A (16 KB), then A_h (Q6_K) or the K=16 mins operand A2.
-template <int FMT>
+// Stage K per kernel: 128 (two 64-element sub-stages) where shared memory
+// allows, so that each dequantizing thread has two independent 32-level
+// units per stage and the per-stage waits, fences and commits are paid once
+// per 128 K; 64 for the Q6_K down tile (its 80 KB raw tile and two A
+// operands leave no room).
+template <int FMT, bool DOWN>
+struct TcK {
+  static constexpr int SUB = (DOWN && FMT == RV_Q6_K) ? 1 : 2;  // 64-K sub-stages per stage
+};
+// One A stage: SUB swizzled [128][64] sub-tiles (16 KB each), then as many
+// A_h sub-tiles (Q6_K) or the K=16 mins operand A2 (4 KB).
+template <int FMT, bool DOWN>
 struct TcStage {
+  static constexpr int SUB = TcK<FMT, DOWN>::SUB;
   static constexpr size_t a = 0;
-  static constexpr size_t ah = RV_TC_ROWS * 128;
+  static constexpr size_t ah = (size_t)SUB * RV_TC_ROWS * 128;
   static constexpr size_t a2 = ah;
-  static constexpr size_t bytes = ah + (TcFmt<FMT>::SPLIT ? RV_TC_ROWS * 128 : RV_TC_ROWS * 32);
+  static constexpr size_t bytes = ah + (TcFmt<FMT>::SPLIT ? (size_t)SUB * RV_TC_ROWS * 128 : (size_t)RV_TC_ROWS * 32);
 };
 // Per-kernel shape: A stages, raw weight slots, activation ring bytes.
 // Shared layout from a 1 KB aligned base: [SA] A stages | raw slots |
 // activation ring | s_da [NT][nb] | s_pair [NT] | barriers | tmem address.
 template <int FMT, bool DOWN>
 struct TcCfg {
-  // Deep A pipelines: a stage's buffer comes back only once its MMAs have
-  // completed (about 1 us after issue), so throughput needs many stages in
-  // flight.  Sizes fill the 227 KB of shared memory.
-  static constexpr int SA = !DOWN ? 6 : FMT == RV_Q6_K ? 3 : FMT == RV_Q5_K ? 4 : 5;
+  // A stage's buffer comes back only once its MMAs have completed, so
+  // throughput needs several stages in flight; sizes fill the 227 KB of
+  // shared memory.
+  // (The activation ring holds at least two slots of the largest tile.)
+  static constexpr int SA = (!DOWN && FMT == RV_Q4_K) || (DOWN && FMT == RV_Q6_K) ? 3 : 2;
   static constexpr int R = DOWN ? 1 : 2;
   static constexpr int SBMAX = 16;
-  static constexpr size_t RING = (DOWN && FMT == RV_Q6_K) ? 40 * 1024 : 48 * 1024;
-  static constexpr size_t raw = (size_t)SA * TcStage<FMT>::bytes;
+  static constexpr size_t RING = (DOWN && FMT == RV_Q6_K) ? 40 * 1024 : 72 * 1024;
+  static constexpr size_t raw = (size_t)SA * TcStage<FMT, DOWN>::bytes;
   __host__ __device__ static size_t raw_slot(size_t row_bytes) {
     return DOWN ? ((RV_TC_ROWS * row_bytes + 16 + 1023) & ~(size_t)1023)
                 : (((size_t)RV_TC_ROWS * TcFmt<FMT>::BB + 1023) & ~(size_t)1023);
@@ -417,9 +429,9 @@ template <int FMT, bool DOWN>
 __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     k_tc_gemm(MoeDims d, MoeBufs B, MoeWeights W, const __grid_constant__ CUtensorMap wmap) {
   using F = TcFmt<FMT>;
-  using SL = TcStage<FMT>;
+  using SL = TcStage<FMT, DOWN>;
   using C = TcCfg<FMT, DOWN>;
-  constexpr int BB = F::BB, SA = C::SA, R = C::R;
+  constexpr int BB = F::BB, SA = C::SA, R = C::R, SUB = SL::SUB, SPB = 4 / SUB;  // stages per super-block
   extern __shared__ __align__(16) uint8_t sm_raw_[];
   uint8_t *sm = (uint8_t *)(((uintptr_t)sm_raw_ + 1023) & ~(uintptr_t)1023);
   const int u = blockIdx.y;
@@ -430,9 +442,10 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   const int4 tile = B.tc_units[u];
   const int e = tile.x, p0 = tile.y, n = tile.z - tile.y, pp0 = tile.w;
   const int nmma = (n + 15) & ~15, ng = nmma / 8, g0 = pp0 / 8;
-  const int kdim = DOWN ? d.M : d.H, nb = kdim / 256, NS = 4 * nb;
+  const int kdim = DOWN ? d.M : d.H, nb = kdim / 256, NS = SPB * nb;
   const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
-  const size_t slot_b = ((size_t)nmma * (128 + (F::MINS ? 32 : 0)) + 1023) & ~(size_t)1023;  // 1 KB atoms
+  const size_t sub_b = (size_t)nmma * 128;  // one 64-K sub-stage of B (whole 1 KB atoms)
+  const size_t slot_b = ((size_t)SUB * sub_b + (F::MINS ? (size_t)nmma * 32 : 0) + 1023) & ~(size_t)1023;
   const int SB = min(C::SBMAX, (int)(C::RING / slot_b));
   int mat = 0, row0;
   if constexpr (DOWN) {
@@ -508,7 +521,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
           }
           mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(RV_TC_ROWS * BB));
           tma_load_4d(raw + slot * rslot, &wmap, b * BB, row0, mat, e, &raw_full[slot]);
-          RV_TRACE(PK + 2, 4 * b, 6);
+          RV_TRACE(PK + 2, SPB * b, 6);
           if (b == 0) RV_PHASE_ANY(PK, 2);
         }
       }
@@ -522,13 +535,15 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
           ok = false;
           break;
         }
-        const bool mins = F::MINS && (it & 3) == 0;
+        const bool mins = F::MINS && (it % SPB) == 0;
         RV_TRACE(PK + 2, it, 5);
         uint8_t *dst = ring + sb * slot_b;
-        mbar_arrive_expect_tx(&b_full[sb], (uint32_t)(ng * 1024 + (mins ? ng * 256 : 0)));
-        bulk_g2s(dst, bq + ((size_t)it * B.tc_groups + g0) * 1024, (uint32_t)(ng * 1024), &b_full[sb]);
+        mbar_arrive_expect_tx(&b_full[sb], (uint32_t)(SUB * ng * 1024 + (mins ? ng * 256 : 0)));
+        for (int u = 0; u < SUB; u++)
+          bulk_g2s(dst + u * sub_b, bq + ((size_t)(SUB * it + u) * B.tc_groups + g0) * 1024, (uint32_t)(ng * 1024),
+                   &b_full[sb]);
         if (mins)
-          bulk_g2s(dst + (size_t)nmma * 128, bm + ((size_t)(it >> 2) * B.tc_groups + g0) * 256, (uint32_t)(ng * 256),
+          bulk_g2s(dst + SUB * sub_b, bm + ((size_t)(it / SPB) * B.tc_groups + g0) * 256, (uint32_t)(ng * 256),
                    &b_full[sb]);
       }
       if (!ok) *s_fail = 1;
@@ -561,8 +576,8 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d1 = tmem + (uint32_t)(slot * 2 * RV_TC_NT), d2 = d1 + RV_TC_NT;
-        for (int j = 0; j < 4; j++) {
-          const int it = 4 * b + j;
+        for (int j = 0; j < SPB; j++) {
+          const int it = SPB * b + j;
           if (!mbar_wait_bounded(&a_full[sa], pa)) {
             ok = false;
             break;
@@ -578,14 +593,18 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
           const uint32_t al = a_lo0 + (uint32_t)sa * a_step, bl = b_lo0 + (uint32_t)sb * b_step;
           if (F::MINS && j == 0)
             tc_mma_f16(d2, mk(lbo_none | (al + (uint32_t)(SL::a2 >> 4)), hi256),
-                       mk(lbo_none | (bl + (uint32_t)nmma * 8), hi256), idesc, 0u);
+                       mk(lbo_none | (bl + (uint32_t)(SUB * sub_b >> 4)), hi256), idesc, 0u);
 #pragma unroll
-          for (int kk = 0; kk < 4; kk++) {
-            const uint32_t acc = (j | kk) != 0;
-            tc_mma_f16(d1, mk(lbo_sw | (al + 2 * kk), hi_sw), mk(lbo_sw | (bl + 2 * kk), hi_sw), idesc, acc);
-            if (F::SPLIT)
-              tc_mma_f16(d2, mk(lbo_sw | (al + (uint32_t)(SL::ah >> 4) + 2 * kk), hi_sw), mk(lbo_sw | (bl + 2 * kk), hi_sw),
-                         idesc, acc);
+          for (int u = 0; u < SUB; u++) {
+            const uint32_t au = al + (uint32_t)(u * RV_TC_ROWS * 128 >> 4), bu = bl + (uint32_t)(u * sub_b >> 4);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+              const uint32_t acc = (j | u | kk) != 0;
+              tc_mma_f16(d1, mk(lbo_sw | (au + 2 * kk), hi_sw), mk(lbo_sw | (bu + 2 * kk), hi_sw), idesc, acc);
+              if (F::SPLIT)
+                tc_mma_f16(d2, mk(lbo_sw | (au + (uint32_t)(SL::ah >> 4) + 2 * kk), hi_sw),
+                           mk(lbo_sw | (bu + 2 * kk), hi_sw), idesc, acc);
+            }
           }
           RV_TRACE(PK + 2, it, 9);
           tc_commit(&a_empty[sa]);
@@ -614,14 +633,14 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     if (DOWN) ok = tc_wait_warp(&raw_full[0], 0);
     uint32_t u0 = 0, u1 = 0, u2 = 0, u3 = 0;
     for (int it = 0; it < NS && ok; it++) {
-      const int b = it >> 2, j = it & 3, sa = it % SA;
-      if (!DOWN && j == 0 && !tc_wait_warp(&raw_full[b % R], (b / R) & 1)) {
+      const int b = it / SPB, js = it % SPB, sa = it % SA;
+      if (!DOWN && js == 0 && !tc_wait_warp(&raw_full[b % R], (b / R) & 1)) {
         ok = false;
         break;
       }
-      if (p == 0 && j == 0) RV_TRACE(PK + 2, it, 8);
+      if (p == 0 && js == 0) RV_TRACE(PK + 2, it, 8);
       const uint8_t *blk = DOWN ? raw + (size_t)r * rb + (size_t)b * BB : raw + (b % R) * rslot + (size_t)r * BB;
-      if (F::MINS && j == 0) {
+      if (F::MINS && js == 0) {
         const uint4 hdr = *(const uint4 *)blk;
         k4_unpack_words(hdr.y, hdr.z, hdr.w, u0, u1, u2, u3);
       }
@@ -632,13 +651,18 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       if (it == 0 && p == 0) RV_PHASE_ANY(PK, 5);
       if (p == 0) RV_TRACE(PK + 2, it, 0);
       uint8_t *st = sm + (size_t)sa * SL::bytes;
-      if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, h, st + SL::a, st + SL::ah, r);
-      else tc_stage_k45<FMT>(blk, j, h, u0, u1, u2, u3, st + SL::a, st + SL::a2, r);
+#pragma unroll
+      for (int u = 0; u < SUB; u++) {
+        const int j = SUB * js + u;  // 64-element stage of the super-block
+        uint8_t *a_sub = st + SL::a + (size_t)u * RV_TC_ROWS * 128;
+        if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, h, a_sub, st + SL::ah + (size_t)u * RV_TC_ROWS * 128, r);
+        else tc_stage_k45<FMT>(blk, j, h, u0, u1, u2, u3, a_sub, st + SL::a2, r);
+      }
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&a_full[sa]);
-        if (!DOWN && j == 3) mbar_arrive(&raw_empty[b % R]);
+        if (!DOWN && js == SPB - 1) mbar_arrive(&raw_empty[b % R]);
       }
       if (p == 0) RV_TRACE(PK + 2, it, 1);
     }
@@ -671,7 +695,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       }
       tc_fence_after();
       if (eb == 0 && warp == RV_TC_W_EPI0 && lane == 0) RV_PHASE_ANY(PK, 7);
-      if (warp == RV_TC_W_EPI0 && lane == 0) RV_TRACE(PK + 2, 4 * eb, 7);
+      if (warp == RV_TC_W_EPI0 && lane == 0) RV_TRACE(PK + 2, SPB * eb, 7);
       const uint32_t t1 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(slot * 2 * RV_TC_NT);
 #pragma unroll
       for (int c = 0; c < 8; c++) {
