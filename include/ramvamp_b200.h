@@ -337,12 +337,17 @@ typedef struct rv_moe_taps {
   const float *logits;          /* [n_tokens][n_experts] router logits */
   const float *weights;         /* [n_tokens][top_k] renormalized weights */
   const uint32_t *ids;          /* [n_tokens][top_k] expert ids */
-  const uint32_t *index;        /* [n_tokens*top_k] pair ids (t*top_k+k) by expert */
+  const uint32_t *index;        /* [index_start[n_experts]] pair ids (t*top_k+k) by expert;
+                                   decode (<= 8 tokens) lays out the speculated pairs, and
+                                   a position the exact routing did not select holds ~0 */
   const uint32_t *index_start;  /* [n_experts+1] CSR offsets into index */
-  const float *swiglu;          /* [n_tokens*top_k][moe] SwiGLU output, CSR order */
-  const uint8_t *acts_moe;      /* CSR order, acts_moe_stride bytes per pair */
-  size_t acts_moe_stride;       /* bytes between pairs' Q8_K rows */
+  const float *swiglu;          /* [positions][moe] SwiGLU output, CSR order */
+  const uint8_t *acts_moe;      /* CSR order, acts_moe_stride bytes per position */
+  size_t acts_moe_stride;       /* bytes between positions' Q8_K rows */
   const float *staged;          /* [n_tokens][top_k][hidden] expert outputs */
+  const float *logit_bounds;    /* decode: [n_tokens][n_experts] (lo, hi) pairs holding
+                                   each router logit, from which the speculated experts
+                                   are chosen; null when the engine has none */
 } rv_moe_taps;
 RV_API int rv_moe_get_taps(const rv_moe *m, rv_moe_taps *out);
 

@@ -69,7 +69,7 @@ class MoeConfig(ctypes.Structure):
 class MoeTaps(ctypes.Structure):
     _fields_ = [("normed", P), ("acts", P), ("acts_stride", SZ), ("logits", P), ("weights", P),
                 ("ids", P), ("index", P), ("index_start", P), ("swiglu", P), ("acts_moe", P),
-                ("acts_moe_stride", SZ), ("staged", P)]
+                ("acts_moe_stride", SZ), ("staged", P), ("logit_bounds", P)]
 
 
 # name -> (restype, argtypes); every symbol the header declares.

@@ -128,6 +128,72 @@ RV_DEVFN bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t sleep_n
   }
 }
 
+// ------------------------------------------------- thread-block clusters
+RV_DEVFN uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster arrives, then waits for all.  The
+// CTAs of a cluster are scheduled together, so each of them reaches it.
+RV_DEVFN void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of this CTA's shared variable `p` in CTA `rank`.
+RV_DEVFN uint32_t dsmem_addr(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+  return r;
+}
+RV_DEVFN void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// Arrive (release, cluster scope) on an mbarrier of another CTA of the cluster.
+RV_DEVFN void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+// Bounded wait (acquire, cluster scope) on this CTA's mbarrier.
+RV_DEVFN bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; i++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 "
+        "%0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 31) == 31 && clock64() - t0 > RV_WAIT_CYCLES) {
+      rv_dev_fail(RV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Barrier over the first NT threads of the block (named barrier 1), or the
+// whole block (__syncthreads) when NT == 0; the _and form also returns
+// whether the predicate held in every participating thread.
+template <int NT>
+RV_DEVFN void cta_sync() {
+  if constexpr (NT == 0) __syncthreads();
+  else asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+}
+template <int NT>
+RV_DEVFN bool cta_sync_and(bool p) {
+  if constexpr (NT == 0) {
+    return __syncthreads_and(p);
+  } else {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.and.pred b, 1, %2, a;\n selp.u32 %0, 1, 0, b;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)p), "n"(NT)
+        : "memory");
+    return r != 0;
+  }
+}
+
 // Stage `bytes` from global `src` into shared `dst`.  Aligned ranges go
 // through the bulk-copy engine (issued by the calling thread, completion
 // counted on `bar`); returns the bytes it put in flight.  Unaligned ranges
@@ -145,7 +211,7 @@ RV_DEVFN void rv_copy_bytes_block(uint8_t *dst, const uint8_t *src, size_t bytes
 // %globaltimer (ns, common to all SMs) at the phases of a kernel (the GPU analogue of the reference's
 // PhaseClock, model/prefill.rs:414-520), read back by rv_debug_phase_clock.
 #ifdef RV_PHASE_CLOCK
-#define RV_PHASE_KERNELS 5  // 3, 4: per-stage traces of one tensor-GEMM CTA
+#define RV_PHASE_KERNELS 6  // 3, 4: per-stage traces of one tensor-GEMM CTA; 5: exact router chains
 #define RV_PHASE_CTAS 8192
 #define RV_PHASES 10
 __device__ long long g_rv_phase[RV_PHASE_KERNELS][RV_PHASE_CTAS][RV_PHASES];

@@ -1,6 +1,8 @@
 // rv_lib.cu -- host side of libramvamp_b200.so: the C ABI declared in
 // include/ramvamp_b200.h.  One translation unit (the kernels come in as
 // headers) so every device global lives in one module.
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <new>
 #include <vector>
@@ -95,6 +97,12 @@ static std::mutex g_init_mu;
 static bool g_dev_ready[64];
 
 #define RV_ROUTE_SMEM_ONE_PER_SM (120u * 1024u)
+// Speculative decode: router rows per exact-chain CTA, that kernel's
+// shared-memory budget, and the units the expert grids cover beyond T*K
+// (more speculated experts than that are strided over).
+#define RV_CHAIN_EXPERTS 16
+#define RV_SMEM_PER_CTA (227u * 1024u)  // the per-CTA shared-memory limit of sm_100
+#define RV_SPEC_SLACK_UNITS 2
 
 static int ensure_device(int dev) {
   if (dev < 0 || dev >= 64) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
@@ -127,6 +135,8 @@ static int ensure_device(int dev) {
   cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_prologue, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_route_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_route_spec, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+
   cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaError_t e3 = cudaGetLastError();
   cudaSetDevice(prev);
@@ -571,6 +581,7 @@ struct rv_moe {
   void *arena;
   float *dres;  // [max_tokens][H] device residual of rv_moe_forward_host
   int last_T = 0;
+  bool spec = true;  // speculative expert dispatch for decode (RV_DECODE_SPEC=0 turns it off)
   std::vector<cudaEvent_t> prof;  // 5 events per set
   size_t prof_next = 0;
 };
@@ -660,6 +671,10 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
   d.norm_topk = cfg->norm_topk_prob;
   const size_t T = max_tokens, K = d.K, P = T * K;
   m->max_units = (int)(std::min<size_t>((size_t)d.E, P) + (P + RV_MOE_TOK_CHUNK - 1) / RV_MOE_TOK_CHUNK);
+  // Speculative decode lays out up to min(T, 8) * E positions, one unit per expert.
+  const size_t PS = std::max(P, std::min<size_t>(T, RV_SPEC_MAX_T) * (size_t)d.E);
+  const size_t units_cap = std::max<size_t>((size_t)m->max_units, (size_t)d.E);
+  if (const char *v = getenv("RV_DECODE_SPEC")) m->spec = atoi(v) != 0;
   const size_t max_tc = std::min<size_t>((size_t)d.E, P) + P / RV_TC_NT + 1;
   const size_t padded_rows = (P + 16 * (size_t)d.E + 16 + 15) & ~(size_t)15;  // every expert's rows rounded up to 16
   // One arena for every scratch buffer the forward touches.
@@ -673,15 +688,16 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
       {P * 4, (void **)&B.w},
       {(size_t)d.E * 4, (void **)&B.counts},
       {((size_t)d.E + 1) * 4, (void **)&B.index_start},
-      {P * 4, (void **)&B.index},
+      {PS * 4, (void **)&B.index},
       {(size_t)m->max_units * 16, (void **)&B.units},
       {16, (void **)&B.n_units},
-      {P * d.M * 4, (void **)&B.hbuf},
-      {P * d.amoe_stride, (void **)&B.acts_moe},
+      {PS * d.M * 4, (void **)&B.hbuf},
+      {PS * d.amoe_stride, (void **)&B.acts_moe},
       {P * d.H * 4, (void **)&B.staged},
-      {(size_t)m->max_units * d.mb * 4, (void **)&B.tile_cnt},
+      {units_cap * d.mb * 4, (void **)&B.tile_cnt},
       {16, (void **)&B.route_cnt},
       {((size_t)d.H / 8 + 1) * 4, (void **)&B.down_cnt},
+      {std::min<size_t>(T, RV_SPEC_MAX_T) * (size_t)d.E * 8, (void **)&B.spec},
       {T * d.H * 4, (void **)&m->dres},
       {padded_rows * d.H * 2, (void **)&B.xq},
       {padded_rows * d.hb * 32, (void **)&B.xm},
@@ -747,45 +763,106 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// The exact router chains of speculative decode: RV_CHAIN_EXPERTS router
+// rows per CTA (fewer when the rows and T residual rows would not fit), one
+// cluster of all the CTAs when there are at most 8 of them.  Each CTA takes
+// a whole SM's shared memory, so no other kernel's CTA shares an SM with a
+// serial chain.
+static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, cudaStream_t s) {
+  const size_t xrow = (size_t)(d.H + 4) * 4;
+  const size_t fixed = 16 + (size_t)T * xrow + (size_t)d.H * 4;
+  int ch = 0, grid = 0;
+  bool cluster = false;
+  void (*kern)(MoeDims, MoeBufs, int) = nullptr;
+  size_t room = 0;
+  for (int v = 0; v < 2 && !kern; v++) {  // the cluster variant first
+    void (*k)(MoeDims, MoeBufs, int) = v == 0 ? k_route_chain<true> : k_route_chain<false>;
+    cudaFuncAttributes fa;
+    RV_CUDA(cudaFuncGetAttributes(&fa, k));
+    room = (size_t)RV_SMEM_PER_CTA - fa.sharedSizeBytes;
+    if (room < fixed + xrow) continue;
+    ch = (int)std::min<size_t>(RV_CHAIN_EXPERTS, (room - fixed) / xrow);
+    grid = (d.E + ch - 1) / ch;
+    if (v == 0 && grid > 8) continue;
+    kern = k;
+    cluster = v == 0;
+  }
+  if (!kern) RV_FAIL(RV_ERR_UNIMPLEMENTED, "router chains: %d tokens of hidden %d do not fit in shared memory", T, d.H);
+  const size_t smem = room;
+  RV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(RV_CHAIN_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)grid;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cluster ? 2 : 1;
+  RV_CUDA(cudaLaunchKernelEx(&cfg, kern, d, B, ch));
+  return RV_OK;
+}
+
 // Split mode (G lanes per row, one token at a time) serves decode; token
 // mode (a thread per row, up to 8 tokens in flight) serves larger batches.
-template <int FMT, int G, int NBG, int R>
-static void launch_gate_up_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
+// units: the grid's first dimension (the unit capacity, or for the
+// speculative kernels the units expected; they stride over the rest).
+template <int FMT, int G, int NBG, int R, bool SPEC>
+static void launch_gate_up_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int units, cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.gu_row_bytes : W.gu_row_bytes + 16;
   const size_t smem = 16 + round16(2 * (size_t)R * st) + 16 + (size_t)B.ms * d.act_stride +
                       (FMT == RV_Q6_K ? (size_t)B.ms * d.hb * 64 * 4 : 0) + 2 * R * RV_MOE_MT * 4;
-  dim3 grid((unsigned)B.max_units, (unsigned)(d.M / R));
-  cudaFuncSetAttribute(k_gate_up<FMT, G, NBG, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl(k_gate_up<FMT, G, NBG, R>, grid, dim3(2 * R * G), smem, s, d, B, W);
+  dim3 grid((unsigned)units, (unsigned)(d.M / R));
+  cudaFuncSetAttribute(k_gate_up<FMT, G, NBG, R, SPEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl(k_gate_up<FMT, G, NBG, R, SPEC>, grid, dim3(2 * R * G), smem, s, d, B, W);
 }
 template <int FMT>
-static void launch_gate_up(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int T, cudaStream_t s) {
-  if (T <= RV_SMALL_T && d.hb == 8) launch_gate_up_t<FMT, 4, 2, 8>(d, B, W, s);
-  else launch_gate_up_t<FMT, 1, 1, 32>(d, B, W, s);
+static void launch_gate_up(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int T, int spec_units,
+                           cudaStream_t s) {
+  if (spec_units) {
+    if (d.hb == 8) launch_gate_up_t<FMT, 4, 2, 8, true>(d, B, W, spec_units, s);
+    else launch_gate_up_t<FMT, 1, 1, 32, true>(d, B, W, spec_units, s);
+  } else if (T <= RV_SMALL_T && d.hb == 8) {
+    launch_gate_up_t<FMT, 4, 2, 8, false>(d, B, W, B.max_units, s);
+  } else {
+    launch_gate_up_t<FMT, 1, 1, 32, false>(d, B, W, B.max_units, s);
+  }
 }
-template <int FMT, int G, int NBG, int ROWS, bool COMBINE>
-static cudaError_t launch_down_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
+template <int FMT, int G, int NBG, int ROWS, bool COMBINE, bool SPEC>
+static cudaError_t launch_down_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int units,
+                                 cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.down_row_bytes : W.down_row_bytes + 16;
   const size_t smem = 16 + round16((size_t)ROWS * st) + 16 + (size_t)B.ms * d.amoe_stride +
                       (FMT == RV_Q6_K ? (size_t)B.ms * d.mb * 64 * 4 : 0) + 16;
-  dim3 grid((unsigned)B.max_units, (unsigned)((d.H + ROWS - 1) / ROWS));
-  cudaFuncSetAttribute(k_down<FMT, G, NBG, ROWS, COMBINE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  return launch_pdl(k_down<FMT, G, NBG, ROWS, COMBINE>, grid, dim3(32), smem, s, d, B, W);
+  dim3 grid((unsigned)units, (unsigned)((d.H + ROWS - 1) / ROWS));
+  cudaFuncSetAttribute(k_down<FMT, G, NBG, ROWS, COMBINE, SPEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  return launch_pdl(k_down<FMT, G, NBG, ROWS, COMBINE, SPEC>, grid, dim3(32), smem, s, d, B, W);
 }
 // Returns true when the down kernel also performed the combine (only when
-// fuse_combine allows it).
+// fuse_combine allows it; always for the speculative kernels).
 template <int FMT>
 static bool launch_down(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int T, bool fuse_combine,
-                        cudaStream_t s) {
+                        int spec_units, cudaStream_t s) {
+  if (spec_units) {
+    if (d.mb == 3) launch_down_t<FMT, 3, 1, 8, true, true>(d, B, W, spec_units, s);
+    else launch_down_t<FMT, 1, 1, 32, true, true>(d, B, W, spec_units, s);
+    return true;
+  }
   if (T <= RV_SMALL_T && d.mb == 3) {
     if (fuse_combine) {
-      launch_down_t<FMT, 3, 1, 8, true>(d, B, W, s);
+      launch_down_t<FMT, 3, 1, 8, true, false>(d, B, W, B.max_units, s);
       return true;
     }
-    launch_down_t<FMT, 3, 1, 8, false>(d, B, W, s);
+    launch_down_t<FMT, 3, 1, 8, false, false>(d, B, W, B.max_units, s);
     return false;
   }
-  launch_down_t<FMT, 1, 1, 32, false>(d, B, W, s);
+  launch_down_t<FMT, 1, 1, 32, false, false>(d, B, W, B.max_units, s);
   return false;
 }
 
@@ -884,8 +961,8 @@ static MoeWeights layer_weights(const rv_expert_table *table, uint32_t layer) {
 // *combined: the down kernel also performed the combine (only with
 // fuse_combine).
 static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, const rv_layer_layout &L,
-                        uint32_t layer, int T, uint32_t flags, bool fuse_combine, cudaEvent_t *ev, unsigned evflags,
-                        cudaStream_t s, bool *combined) {
+                        uint32_t layer, int T, uint32_t flags, bool fuse_combine, int spec_units, cudaEvent_t *ev,
+                        unsigned evflags, cudaStream_t s, bool *combined) {
   *combined = false;
   int rc;
   if (flags & RV_MOE_TENSOR) {
@@ -914,15 +991,15 @@ static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
   }
   if ((rc = prof_record(ev, 1, evflags, s))) return rc;
   switch (L.gate_format) {
-    case RV_Q4_K: launch_gate_up<RV_Q4_K>(d, B, W, T, s); break;
-    case RV_Q5_K: launch_gate_up<RV_Q5_K>(d, B, W, T, s); break;
-    default: launch_gate_up<RV_Q6_K>(d, B, W, T, s); break;
+    case RV_Q4_K: launch_gate_up<RV_Q4_K>(d, B, W, T, spec_units, s); break;
+    case RV_Q5_K: launch_gate_up<RV_Q5_K>(d, B, W, T, spec_units, s); break;
+    default: launch_gate_up<RV_Q6_K>(d, B, W, T, spec_units, s); break;
   }
   if ((rc = prof_record(ev, 2, evflags, s))) return rc;
   switch (L.down_format) {
-    case RV_Q4_K: *combined = launch_down<RV_Q4_K>(d, B, W, T, fuse_combine, s); break;
-    case RV_Q5_K: *combined = launch_down<RV_Q5_K>(d, B, W, T, fuse_combine, s); break;
-    default: *combined = launch_down<RV_Q6_K>(d, B, W, T, fuse_combine, s); break;
+    case RV_Q4_K: *combined = launch_down<RV_Q4_K>(d, B, W, T, fuse_combine, spec_units, s); break;
+    case RV_Q5_K: *combined = launch_down<RV_Q5_K>(d, B, W, T, fuse_combine, spec_units, s); break;
+    default: *combined = launch_down<RV_Q6_K>(d, B, W, T, fuse_combine, spec_units, s); break;
   }
   RV_LAUNCH_CHECK();
   return prof_record(ev, 3, evflags, s);
@@ -988,7 +1065,17 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   }
   if ((rc = prof_record(ev, 0, evflags, s))) return rc;
   B.ms = T < RV_MOE_MT ? T : RV_MOE_MT;
-  if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
+  int spec_units = 0;
+  if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T && m->spec) {
+    // decode, speculative: norm, Q8_K and logit bounds; then the exact
+    // router chains beside gate/up on the speculated experts; then down
+    // and combine on the exact routing.
+    const size_t xrow = (size_t)(d.H + 4) * 4;
+    RV_CUDA(launch_pdl(k_route_spec, dim3((unsigned)((d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC)), dim3(128),
+                       16 + (size_t)(RV_SPEC_EPC + 1) * d.H * 4 + T * xrow, s, d, B));
+    if ((rc = launch_route_chain(d, B, T, s))) return rc;
+    spec_units = std::min(d.E, T * d.K + RV_SPEC_SLACK_UNITS);
+  } else if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch
     // Shared memory padded past half an SM's so that no two routing CTAs
     // (each running one serial router chain) share an SM.
@@ -1000,7 +1087,7 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
     k_index<<<1, 1024, 0, s>>>(d, B);
   }
   bool combined = false;
-  if ((rc = expert_stage(d, B, W, L, layer, T, flags, true, ev, evflags, s, &combined))) return rc;
+  if ((rc = expert_stage(d, B, W, L, layer, T, flags, true, spec_units, ev, evflags, s, &combined))) return rc;
   if (!combined) k_combine<<<dim3((unsigned)T, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
   if ((rc = prof_record(ev, 4, evflags, s))) return rc;
   RV_LAUNCH_CHECK();
@@ -1066,7 +1153,7 @@ extern "C" int rv_moe_experts(rv_moe *m, const rv_expert_table *table, uint32_t 
   k_index<<<1, 1024, 0, s>>>(d, B);
   RV_LAUNCH_CHECK();
   bool combined = false;
-  return expert_stage(d, B, layer_weights(table, layer), L, layer, (int)n_pairs, flags, false, nullptr, 0, s,
+  return expert_stage(d, B, layer_weights(table, layer), L, layer, (int)n_pairs, flags, false, 0, nullptr, 0, s,
                       &combined);
 }
 
@@ -1144,6 +1231,7 @@ extern "C" int rv_moe_get_taps(const rv_moe *m, rv_moe_taps *o) {
   o->acts_moe = m->B.acts_moe;
   o->acts_moe_stride = m->d.amoe_stride;
   o->staged = m->B.staged;
+  o->logit_bounds = (const float *)m->B.spec;
   return RV_OK;
 }
 
@@ -1215,6 +1303,7 @@ extern "C" int rv_expert_table_fill_synthetic_strided(rv_expert_table *t, uint32
 // Copies the phase clocks of kernel k (0 route, 1 gate_up, 2 down) to out
 // ([RV_PHASE_CTAS][RV_PHASES] int64) and clears them.
 extern "C" __attribute__((visibility("default"))) int rv_debug_phase_clock(int k, long long *out) {
+  if (k < 0 || k >= RV_PHASE_KERNELS || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "phase clock slot %d", k);
   RV_CUDA(cudaDeviceSynchronize());
   RV_CUDA(cudaMemcpyFromSymbol(out, g_rv_phase, sizeof(long long) * RV_PHASE_CTAS * RV_PHASES,
                                sizeof(long long) * RV_PHASE_CTAS * RV_PHASES * k));
@@ -1340,15 +1429,15 @@ extern "C" int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_la
   const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)Tn * (d.H + 4) * 4 + 4 * (size_t)Tn * sizeof(double) + 16;
   RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
   switch (L->gate_format) {
-    case RV_Q4_K: launch_gate_up<RV_Q4_K>(d, B, W, Tn, s); break;
-    case RV_Q5_K: launch_gate_up<RV_Q5_K>(d, B, W, Tn, s); break;
-    default: launch_gate_up<RV_Q6_K>(d, B, W, Tn, s); break;
+    case RV_Q4_K: launch_gate_up<RV_Q4_K>(d, B, W, Tn, 0, s); break;
+    case RV_Q5_K: launch_gate_up<RV_Q5_K>(d, B, W, Tn, 0, s); break;
+    default: launch_gate_up<RV_Q6_K>(d, B, W, Tn, 0, s); break;
   }
   bool combined;
   switch (L->down_format) {
-    case RV_Q4_K: combined = launch_down<RV_Q4_K>(d, B, W, Tn, true, s); break;
-    case RV_Q5_K: combined = launch_down<RV_Q5_K>(d, B, W, Tn, true, s); break;
-    default: combined = launch_down<RV_Q6_K>(d, B, W, Tn, true, s); break;
+    case RV_Q4_K: combined = launch_down<RV_Q4_K>(d, B, W, Tn, true, 0, s); break;
+    case RV_Q5_K: combined = launch_down<RV_Q5_K>(d, B, W, Tn, true, 0, s); break;
+    default: combined = launch_down<RV_Q6_K>(d, B, W, Tn, true, 0, s); break;
   }
   if (!combined) k_combine<<<dim3((unsigned)Tn, (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(d, B);
   RV_LAUNCH_CHECK();

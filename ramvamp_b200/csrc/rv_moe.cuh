@@ -20,6 +20,7 @@
 #include "rv_internal.cuh"
 #include "rv_kernels.cuh"
 #include "rv_rowdot.cuh"
+#include "rv_spec.cuh"
 
 #define RV_MOE_MT 8          // tokens staged per pass
 #define RV_MOE_TOK_CHUNK 64  // tokens per work unit
@@ -52,6 +53,7 @@ struct MoeBufs {
   int *tile_cnt;           // [max_units][M/256], zero between calls
   int *route_cnt;          // [1] CTAs done in k_route_decode, zero between calls
   int *down_cnt;           // [H/8] units done per down row tile, zero between calls
+  float2 *spec;            // [T][E] (lo, hi) bounds of the router logits (speculative decode)
   int T;
   int ms;                  // activation slots per CTA pass: min(T, RV_MOE_MT)
   int max_units;
@@ -107,15 +109,17 @@ __global__ void __launch_bounds__(256) k_prologue(MoeDims d, MoeBufs B) {
 // winner is blanked with -inf); renormalization by the in-order f32 sum.
 // E <= 256 (8 per lane), K <= 16.  Writes ids/w and counts (any address
 // space: global in k_route, shared in k_route_decode).
-RV_DEVFN void route_token_warp(const MoeDims &d, const MoeBufs &B, int t, int lane, double *es,
+RV_DEVFN float ld_logit(const float *p) { return __isShared(p) ? *p : __ldcg(p); }
+
+// lg: token t's E logits (global, written by other CTAs, or shared).
+RV_DEVFN void route_token_warp(const MoeDims &d, const MoeBufs &B, int t, const float *lg, int lane, double *es,
                                int *counts) {
-  const float *lg = B.logits + (size_t)t * d.E;
   float p[8];
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int e = lane + 32 * j;
-    p[j] = e < d.E ? __ldcg(lg + e) : -INFINITY;
+    p[j] = e < d.E ? ld_logit(lg + e) : -INFINITY;
     if (e < d.E) mx = fmaxf(mx, p[j]);
   }
 #pragma unroll
@@ -196,16 +200,16 @@ RV_DEVFN void route_token_warp(const MoeDims &d, const MoeBufs &B, int t, int la
 // the repeated strict-'>' argmax produces whenever every probability is a
 // number; otherwise warp 0 runs the warp version.  Scratch: es [256]
 // doubles, ps [256] floats, sel [16] floats, red [8] doubles, flag.
-RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, double *es, float *ps, float *sel,
-                                double *red, int *counts, uint32_t *sids) {
+template <int NT = 0>
+RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, const float *lg, double *es, float *ps,
+                                float *sel, double *red, int *counts, uint32_t *sids) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const float *lg = B.logits + (size_t)t * d.E;
   float x[2];
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 2; j++) {
     const int e = tid + 128 * j;
-    x[j] = e < d.E ? __ldcg(lg + e) : -INFINITY;
+    x[j] = e < d.E ? ld_logit(lg + e) : -INFINITY;
     if (e < d.E) mx = fmaxf(mx, x[j]);
   }
 #pragma unroll
@@ -213,7 +217,7 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
   RV_TRACE_TAIL(0);
   float *redf = (float *)(red + 4);
   if (lane == 0) redf[warp] = mx;
-  __syncthreads();
+  cta_sync<NT>();
   mx = fmaxf(fmaxf(redf[0], redf[1]), fmaxf(redf[2], redf[3]));
   RV_TRACE_TAIL(1);
   const double dmx = (double)mx;
@@ -233,9 +237,9 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
 #pragma unroll
   for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
   RV_TRACE_TAIL(2);
-  __syncthreads();  // redf reads done, es complete
+  cta_sync<NT>();  // redf reads done, es complete
   if (lane == 0) red[warp] = part;
-  __syncthreads();
+  cta_sync<NT>();
   RV_TRACE_TAIL(3);
   // Any order of these <= 256 non-negative terms is within 2^-44 relative of
   // the reference's serial sum; recompute serially when 1/sum is that close
@@ -257,13 +261,13 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
       if (e < d.E && !(p == p && p != INFINITY && p != -INFINITY)) finite = false;
     }
   }
-  const bool all_finite = __syncthreads_and(finite);
+  const bool all_finite = cta_sync_and<NT>(finite);
   RV_TRACE_TAIL(4);
   if (!all_finite) {
-    if (warp == 0) route_token_warp(d, B, t, lane, es, counts);
-    __syncthreads();
+    if (warp == 0) route_token_warp(d, B, t, lg, lane, es, counts);
+    cta_sync<NT>();
     if (tid < d.K) sids[t * d.K + tid] = __ldcg(B.ids + (size_t)t * d.K + tid);
-    __syncthreads();
+    cta_sync<NT>();
     return;
   }
 #pragma unroll
@@ -296,7 +300,7 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
     }
   }
   RV_TRACE_TAIL(5);
-  __syncthreads();
+  cta_sync<NT>();
   RV_TRACE_TAIL(6);
   if (tid < d.K) {
     float wsum = -0.0f;  // the in-order sum of the selected weights
@@ -304,7 +308,7 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, doubl
     const float w = d.norm_topk ? __fdiv_rn(sel[tid], wsum) : sel[tid];
     B.w[(size_t)t * d.K + tid] = w;
   }
-  __syncthreads();
+  cta_sync<NT>();
   RV_TRACE_TAIL(7);
 }
 
@@ -313,7 +317,7 @@ __global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + warp;
   if (t >= B.T) return;
-  route_token_warp(d, B, t, lane, es[warp], B.counts);
+  route_token_warp(d, B, t, B.logits + (size_t)t * d.E, lane, es[warp], B.counts);
 }
 
 // ----------------------------------------------------------- dispatch
@@ -484,6 +488,66 @@ RV_DEVFN float serial_dot_f32(const float4 *a, const float4 *b, int n4) {
   return acc;
 }
 
+// RMSNorm (norm.rs:17-60) of T rows held in shared memory at stride
+// xstride, in place, by a 128-thread CTA.  The f64 sum of squares is split
+// over the four warps (each row in four quarters); any summation order lies
+// within the 2^-38 bound f32_rounding_stable checks, and the serial order
+// is recomputed when the f32 result is not stable.  Then x = (x * inv) * w.
+// red: [T][4] doubles, s_inv: [T] floats, both shared.
+template <int NT = 0>
+RV_DEVFN void norm_rows_cta(const MoeDims &d, int T, float *xs, int xstride, const float *nw, double *red,
+                            float *s_inv) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = d.H / 4;  // elements per warp per token
+  for (int t = 0; t < T; t++) {
+    const float *x = xs + t * xstride + warp * q;
+    double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
+    for (int k = 4 * lane; k < q; k += 128) {
+      const float4 v = *(const float4 *)(x + k);
+      p0 = __dadd_rn(p0, __dmul_rn((double)v.x, (double)v.x));
+      p1 = __dadd_rn(p1, __dmul_rn((double)v.y, (double)v.y));
+      p2 = __dadd_rn(p2, __dmul_rn((double)v.z, (double)v.z));
+      p3 = __dadd_rn(p3, __dmul_rn((double)v.w, (double)v.w));
+    }
+    double part = __dadd_rn(__dadd_rn(p0, p1), __dadd_rn(p2, p3));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+    if (lane == 0) red[4 * t + warp] = part;
+  }
+  cta_sync<NT>();
+  if (threadIdx.x < T) {
+    const int t = threadIdx.x;
+    const double sum = __dadd_rn(__dadd_rn(red[4 * t], red[4 * t + 1]), __dadd_rn(red[4 * t + 2], red[4 * t + 3]));
+    const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)d.H), (double)d.eps)));
+    float inv = __double2float_rn(r);
+    if (!f32_rounding_stable(r, 0x1p-38)) {
+      const float *x = xs + t * xstride;
+      double ser = 0.0;  // the reference's serial order
+      for (int k = 0; k < d.H; k++) {
+        const double v = (double)x[k];
+        ser = __dadd_rn(ser, __dmul_rn(v, v));
+      }
+      inv = rms_inv_from_sum(ser, (size_t)d.H, d.eps);
+    }
+    s_inv[t] = inv;
+  }
+  cta_sync<NT>();
+  for (int t = 0; t < T; t++) {
+    float4 *x = (float4 *)(xs + t * xstride);
+    const float inv = s_inv[t];
+    for (int k = threadIdx.x; k < d.H / 4; k += (NT ? NT : (int)blockDim.x)) {
+      float4 v = x[k];
+      const float4 w = ((const float4 *)nw)[k];
+      v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
+      v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
+      v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
+      v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
+      x[k] = v;
+    }
+  }
+  cta_sync<NT>();
+}
+
 __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   extern __shared__ __align__(16) uint8_t sm[];
   __shared__ double es[4][256];
@@ -533,52 +597,7 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   if (xbulk && !mbar_wait_bounded(bar + 1, 0)) return;
   if (rbulk && !mbar_wait_bounded(bar, 0)) return;
   RV_PHASE(0, 2);
-  // RMSNorm (norm.rs:17-60), in place.  The f64 sum of squares is split
-  // over the four warps (each token's row in four quarters); any summation
-  // order lies within the 2^-38 bound f32_rounding_stable checks, and the
-  // serial order is recomputed when the f32 result is not stable.
-  {
-    const int q = d.H / 4;  // elements per warp per token
-    for (int t = 0; t < T; t++) {
-      const float *x = xs + t * xstride + warp * q;
-      double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
-      for (int k = 4 * lane; k < q; k += 128) {
-        const float4 v = *(const float4 *)(x + k);
-        p0 = __dadd_rn(p0, __dmul_rn((double)v.x, (double)v.x));
-        p1 = __dadd_rn(p1, __dmul_rn((double)v.y, (double)v.y));
-        p2 = __dadd_rn(p2, __dmul_rn((double)v.z, (double)v.z));
-        p3 = __dadd_rn(p3, __dmul_rn((double)v.w, (double)v.w));
-      }
-      double part = __dadd_rn(__dadd_rn(p0, p1), __dadd_rn(p2, p3));
-#pragma unroll
-      for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
-      if (lane == 0) red[4 * t + warp] = part;
-    }
-    __syncthreads();
-    if (threadIdx.x < T) {
-      const int t = threadIdx.x;
-      const double sum = __dadd_rn(__dadd_rn(red[4 * t], red[4 * t + 1]), __dadd_rn(red[4 * t + 2], red[4 * t + 3]));
-      const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)d.H), (double)d.eps)));
-      float inv = __double2float_rn(r);
-      if (!f32_rounding_stable(r, 0x1p-38)) {
-        const float *x = xs + t * xstride;
-        double ser = 0.0;  // the reference's serial order
-        for (int k = 0; k < d.H; k++) {
-          const double v = (double)x[k];
-          ser = __dadd_rn(ser, __dmul_rn(v, v));
-        }
-        inv = rms_inv_from_sum(ser, (size_t)d.H, d.eps);
-      }
-      s_inv[t] = inv;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < T * d.H; i += blockDim.x) {
-      const int t = i / d.H, k = i % d.H;
-      float *x = xs + t * xstride + k;
-      *x = __fmul_rn(__fmul_rn(*x, s_inv[t]), nw[k]);
-    }
-  }
-  __syncthreads();
+  norm_rows_cta(d, T, xs, xstride, nw, red, s_inv);
   // The Q8_K rows of the normed tokens and the normed tap do not depend on
   // the routing: CTA e's warps 1-3 write block e (of T*hb) while warp 0
   // runs the router chain.
@@ -622,9 +641,10 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
     __shared__ __align__(16) float s_ps[256];
     __shared__ float s_sel[16];
     __shared__ double s_red[8];
-    for (int t = 0; t < T; t++) route_token_block(d, B, t, es[0], s_ps, s_sel, s_red, s_cnt, s_ids);
+    for (int t = 0; t < T; t++)
+      route_token_block(d, B, t, B.logits + (size_t)t * d.E, es[0], s_ps, s_sel, s_red, s_cnt, s_ids);
   } else {
-    for (int t = warp; t < T; t += 4) route_token_warp(d, B, t, lane, es[warp], s_cnt);
+    for (int t = warp; t < T; t += 4) route_token_warp(d, B, t, B.logits + (size_t)t * d.E, lane, es[warp], s_cnt);
     __syncthreads();
     for (int i = threadIdx.x; i < T * d.K && i < 32; i += blockDim.x) s_ids[i] = __ldcg(B.ids + i);
   }
@@ -633,6 +653,207 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
   if (T * d.K <= 32) build_index_small(d, B, s_ids);
   else build_index_cta(d, B, s_cnt, s_st, s_cur, s_us);
   RV_PHASE(0, 8);
+}
+
+// ------------------------------------------- speculative decode routing
+// k_route_spec: grid = ceil(E / 4) CTAs of four warps; warp w of CTA c owns
+// expert 4c + w.  Stages the CTA's four router rows and the norm weight
+// (before waiting on the previous kernel), then the T residual rows;
+// RMSNorm of every token; the f32 interval of logit (t, e) for every token
+// (spec_bounds_warp); the Q8_K rows and the normed tap, block b of token t
+// by warp (t*hb + b) of the grid.  Everything the expert kernels need
+// before the exact router chains have run.
+#define RV_SPEC_EPC 4  // experts per k_route_spec CTA
+__global__ void __launch_bounds__(128) k_route_spec(MoeDims d, MoeBufs B) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ float s_inv[RV_SMALL_T];
+  __shared__ double s_red[4 * RV_SMALL_T];
+  RV_PHASE(0, 0);
+  const int T = B.T, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * RV_SPEC_EPC, ne = min(RV_SPEC_EPC, d.E - e0);
+  const int xstride = d.H + 4;
+  uint64_t *bar = (uint64_t *)sm;                // [2]: router rows + norm weight, residual rows
+  float *rows = (float *)(sm + 16);              // [4][H]
+  float *nw = rows + RV_SPEC_EPC * d.H;          // [H] ffn_norm weight
+  float *xs = nw + d.H;                          // [T][H + 4]
+  const float *rsrc = B.router + (size_t)e0 * d.H;
+  const bool rbulk = rv_bulk_ok(rsrc, rows, (size_t)ne * d.H * 4) && rv_bulk_ok(B.ffn_norm, nw, (size_t)d.H * 4);
+  const bool xbulk = rv_bulk_ok(B.residual, xs, (size_t)d.H * 4);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
+    if (rbulk) {
+      mbar_arrive_expect_tx(bar, (uint32_t)((ne + 1) * d.H * 4));
+      bulk_g2s(rows, rsrc, (uint32_t)(ne * d.H * 4), bar);
+      bulk_g2s(nw, B.ffn_norm, (uint32_t)(d.H * 4), bar);
+    }
+  }
+  if (!rbulk) {
+    for (int k = threadIdx.x; k < ne * d.H; k += blockDim.x) rows[k] = rsrc[k];
+    for (int k = threadIdx.x; k < d.H; k += blockDim.x) nw[k] = B.ffn_norm[k];
+  }
+  pdl_wait();  // the residual is the previous kernel's output
+  // The exact-chain kernel reads the residual without waiting: it may
+  // launch only now.
+  pdl_trigger();
+  RV_PHASE(0, 1);
+  if (threadIdx.x == 0 && xbulk) {
+    mbar_arrive_expect_tx(bar + 1, (uint32_t)(T * d.H * 4));
+    for (int t = 0; t < T; t++)
+      bulk_g2s(xs + t * xstride, B.residual + (size_t)t * d.H, (uint32_t)(d.H * 4), bar + 1);
+  }
+  if (!xbulk)
+    for (int t = 0; t < T; t++)
+      for (int k = threadIdx.x; k < d.H; k += blockDim.x) xs[t * xstride + k] = B.residual[(size_t)t * d.H + k];
+  __syncthreads();
+  if (xbulk && !mbar_wait_bounded(bar + 1, 0)) return;
+  if (rbulk && !mbar_wait_bounded(bar, 0)) return;
+  RV_PHASE(0, 2);
+  norm_rows_cta(d, T, xs, xstride, nw, s_red, s_inv);
+  RV_PHASE(0, 3);
+  if (warp < ne)
+    for (int t = 0; t < T; t++) {
+      const float2 b = spec_bounds_warp(rows + (size_t)warp * d.H, xs + t * xstride, d.H, lane);
+      if (lane == 0) B.spec[(size_t)t * d.E + e0 + warp] = b;
+    }
+  RV_PHASE(0, 4);
+  const int gw = blockIdx.x * 4 + warp, nwg = gridDim.x * 4;
+  for (int tb = gw; tb < T * d.hb; tb += nwg) {
+    const int t = tb / d.hb, b = tb % d.hb;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = xs[t * xstride + b * 256 + 8 * lane + e];
+    q8k_quantize_warp(v, lane, B.acts + (size_t)t * d.act_stride + (size_t)b * 292);
+#pragma unroll
+    for (int e = 0; e < 8; e++) B.normed[(size_t)t * d.H + b * 256 + 8 * lane + e] = v[e];
+  }
+  RV_PHASE(0, 5);
+}
+
+// k_route_chain: the exact router chains, CH experts per CTA (grid =
+// ceil(E / CH), one cluster when CLUSTER), 160 threads.  Warps 0-3 stage
+// the CTA's router rows, the residual rows and the norm weight, compute
+// the RMSNorm themselves (the same arithmetic as k_route_spec, so the same
+// bits) and run one serial f32 chain per (token, expert): thread i < T*CH
+// owns logit (i / CH, blockIdx.x*CH + i % CH).  The logits are gathered in
+// CTA 0 of the cluster through distributed shared memory (or, without a
+// cluster, by the last CTA through global memory), which routes every token
+// (f64 softmax, top-k, renormalization).  Warp 4 only gates the launch of
+// the next (speculative gate/up) kernel: that kernel reads k_route_spec's
+// output without waiting, so this grid triggers once k_route_spec has
+// completed.  The residual was written by the previous layer, complete
+// before k_route_spec triggered this launch.
+#define RV_CHAIN_THREADS 160
+template <bool CLUSTER>
+__global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims d, MoeBufs B, int CH) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ double es[4][256];
+  __shared__ int s_cnt[256];
+  __shared__ uint32_t s_ids[32];
+  __shared__ __align__(16) float s_ps[256];
+  __shared__ float s_sel[16];
+  __shared__ double s_red[8];
+  __shared__ float s_inv[RV_SMALL_T];
+  __shared__ double s_nred[4 * RV_SMALL_T];
+  __shared__ __align__(16) float s_lg[CLUSTER ? RV_SPEC_MAX_T * 256 : 1];  // CTA 0: the gathered logits
+  __shared__ __align__(8) uint64_t s_gbar;                                  // CTA 0: one arrival per logit
+  __shared__ int s_last;
+  RV_PHASE(5, 0);
+  const int T = B.T, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int xstride = d.H + 4;
+  const int ef = blockIdx.x * CH, ne = min(CH, d.E - ef);
+  const bool lead = CLUSTER ? cluster_ctarank() == 0 : true;
+  uint64_t *bar = (uint64_t *)sm;           // [2]: router rows, residual rows + norm weight
+  float *rows = (float *)(sm + 16);         // [CH][H + 4]
+  float *xs = rows + (size_t)CH * xstride;  // [T][H + 4]
+  float *nw = xs + (size_t)T * xstride;     // [H]
+  const bool rbulk = rv_bulk_ok(B.router + (size_t)ef * d.H, rows, (size_t)d.H * 4);
+  const bool xbulk = rv_bulk_ok(B.residual, xs, (size_t)d.H * 4) && rv_bulk_ok(B.ffn_norm, nw, (size_t)d.H * 4);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
+    if (CLUSTER && lead) mbar_init(&s_gbar, (uint32_t)(T * d.E));
+  }
+  if constexpr (CLUSTER) cluster_sync_all();  // CTA 0's gather barrier exists before any arrival
+  else __syncthreads();
+  if (warp == 4) {
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
+  if (tid == 0) {
+    if (rbulk) {
+      mbar_arrive_expect_tx(bar, (uint32_t)(ne * d.H * 4));
+      for (int r = 0; r < ne; r++)
+        bulk_g2s(rows + (size_t)r * xstride, B.router + (size_t)(ef + r) * d.H, (uint32_t)(d.H * 4), bar);
+    }
+    if (xbulk) {
+      mbar_arrive_expect_tx(bar + 1, (uint32_t)((T + 1) * d.H * 4));
+      for (int t = 0; t < T; t++)
+        bulk_g2s(xs + (size_t)t * xstride, B.residual + (size_t)t * d.H, (uint32_t)(d.H * 4), bar + 1);
+      bulk_g2s(nw, B.ffn_norm, (uint32_t)(d.H * 4), bar + 1);
+    }
+  }
+  if (!rbulk)
+    for (int r = 0; r < ne; r++)
+      for (int k = tid; k < d.H; k += 128) rows[(size_t)r * xstride + k] = B.router[(size_t)(ef + r) * d.H + k];
+  if (!xbulk) {
+    for (int t = 0; t < T; t++)
+      for (int k = tid; k < d.H; k += 128) xs[(size_t)t * xstride + k] = B.residual[(size_t)t * d.H + k];
+    for (int k = tid; k < d.H; k += 128) nw[k] = B.ffn_norm[k];
+  }
+  cta_sync<128>();
+  bool ok = true;
+  if (xbulk) ok = mbar_wait_bounded(bar + 1, 0);
+  RV_PHASE(5, 1);
+  if (!ok) return;
+  norm_rows_cta<128>(d, T, xs, xstride, nw, s_nred, s_inv);
+  if (rbulk) ok = mbar_wait_bounded(bar, 0);
+  RV_PHASE(5, 2);
+  if (!ok) return;
+  if (tid < T * CH) {
+    const int t = tid / CH, el = tid % CH;
+    if (el < ne) {
+      const int e = ef + el;
+      const float lg = serial_dot_f32((const float4 *)(rows + (size_t)el * xstride),
+                                      (const float4 *)(xs + (size_t)t * xstride), d.H / 4);
+      B.logits[(size_t)t * d.E + e] = lg;
+      if constexpr (CLUSTER) {
+        st_cluster_f32(dsmem_addr(&s_lg[t * d.E + e], 0), lg);
+        mbar_arrive_cluster(dsmem_addr(&s_gbar, 0));
+      }
+    }
+  }
+  RV_PHASE(5, 3);
+  const float *lgs;
+  if constexpr (CLUSTER) {
+    if (!lead) return;
+    ok = mbar_wait_cluster_bounded(&s_gbar, 0);
+    if (!ok) return;
+    lgs = s_lg;
+  } else {
+    __threadfence();
+    cta_sync<128>();
+    if (tid == 0) {
+      const int old = atomicAdd(B.route_cnt, 1);
+      s_last = old == (int)gridDim.x - 1;
+      if (s_last) *B.route_cnt = 0;
+    }
+    cta_sync<128>();
+    if (!s_last) return;
+    __threadfence();
+    lgs = B.logits;
+  }
+  RV_PHASE(5, 4);
+  for (int e = tid; e < 256; e += 128) s_cnt[e] = 0;
+  cta_sync<128>();
+  if (T <= 2) {
+    for (int t = 0; t < T; t++)
+      route_token_block<128>(d, B, t, lgs + (size_t)t * d.E, es[0], s_ps, s_sel, s_red, s_cnt, s_ids);
+  } else {
+    for (int t = warp; t < T; t += 4) route_token_warp(d, B, t, lgs + (size_t)t * d.E, lane, es[warp], s_cnt);
+  }
+  RV_PHASE(5, 5);
 }
 
 // Large-T router logits: CTA = 4 experts x 32 tokens; lane t of warp w runs
@@ -732,30 +953,19 @@ RV_DEVFN uint32_t stage_rows(uint8_t *dst, const uint8_t *src, size_t row_bytes,
 }
 
 // ------------------------------------------------- gate/up + SwiGLU + Q8_K
-// grid = (max_units, M / R).  A CTA computes rows [tile*R, tile*R+R) of
-// both gate and up of one unit's expert for all of the unit's tokens, staged
-// B.ms at a time.  G > 1: split mode (one token at a time, G lanes per row,
-// NBG blocks each); G == 1: token mode (a thread per row, up to 8 tokens in
-// flight).  2*R*G/32 warps.  Then SwiGLU with the host-libm exponential, and
-// the last of the tiles of each 256-row block quantizes that block of every
-// token.  Launched as a programmatic dependent of the routing kernel; lets
-// the next (down) kernel launch at once.
-template <int FMT, int G, int NBG, int R>
-__global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d, MoeBufs B, MoeWeights W) {
-  extern __shared__ __align__(16) uint8_t sm[];
+// A CTA computes rows [tile*R, tile*R+R) of both gate and up of one unit's
+// expert for all of the unit's positions, staged B.ms at a time.  G > 1:
+// split mode (one token at a time, G lanes per row, NBG blocks each);
+// G == 1: token mode (a thread per row, up to 8 tokens in flight).
+// 2*R*G/32 warps.  Then SwiGLU with the host-libm exponential, and the last
+// of the tiles of each 256-row block quantizes that block of every
+// position.  tok(c): the token of position c.  phase: parity of the CTA's
+// mbarrier, carried from unit to unit.  Returns false when a wait ran out.
+template <int FMT, int G, int NBG, int R, typename TokOf>
+RV_DEVFN bool gate_up_unit(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, uint8_t *sm, int u, int e,
+                           int p0, int p1, int tile, TokOf tok, uint32_t &phase) {
   constexpr int MT = RV_MOE_MT, RPW = 32 / G, NW = 2 * R * G / 32;
-  RV_PHASE(1, 0);
-  // The dispatch index and activations are the routing kernel's output.
-  // The down kernel reads the index before its own wait, so it may launch
-  // only once the routing grid has completed: trigger after the wait.
-  pdl_wait();
-  pdl_trigger();
-  const int u = blockIdx.x, tile = blockIdx.y;
-  if (u >= *B.n_units) return;
-  const int4 unit = B.units[u];
-  const int e = unit.x, p0 = unit.y, p1 = unit.z;
   const int ms = B.ms;
-  RV_PHASE(1, 1);
   __shared__ int s_last;
   uint64_t *bar = (uint64_t *)sm;
   const size_t st = tile_stride<FMT>(W.gu_row_bytes);
@@ -768,8 +978,6 @@ __global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d,
   const uint8_t *gsrc = blob + W.gate_off + (size_t)tile * R * W.gu_row_bytes;
   const uint8_t *usrc = blob + W.up_off + (size_t)tile * R * W.gu_row_bytes;
   const bool abulk = rv_bulk_ok(B.acts, asm_, d.act_stride);
-  if (threadIdx.x == 0) mbar_init(bar, 1);
-  __syncthreads();
   const uint32_t wtx = stage_rows<FMT>(wsm, gsrc, W.gu_row_bytes, R, bar, false) +
                        stage_rows<FMT>(wsm + wtile, usrc, W.gu_row_bytes, R, bar, false);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -777,7 +985,6 @@ __global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d,
   const int rsub = lane / G, g = lane % G;
   const int r = (warp % (NW / 2)) * RPW + rsub;  // row within the part
   const uint8_t *wrow = wsm + (size_t)part * wtile + (size_t)r * st;
-  uint32_t phase = 0;
   bool ok = true;
   for (int c0 = p0; c0 < p1; c0 += ms) {
     const int mt = min(ms, p1 - c0);
@@ -793,14 +1000,13 @@ __global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d,
       stage_rows<FMT>(wsm + wtile, usrc, W.gu_row_bytes, R, bar, true);
     }
     for (int m = 0; m < mt; m++) {
-      const uint32_t tok = B.index[c0 + m] / (uint32_t)d.K;
+      const uint32_t t = tok(c0 + m);
       if (abulk) {
         if (threadIdx.x == 0)
-          bulk_g2s(asm_ + (size_t)m * d.act_stride, B.acts + (size_t)tok * d.act_stride,
-                   (uint32_t)d.act_stride, bar);
+          bulk_g2s(asm_ + (size_t)m * d.act_stride, B.acts + (size_t)t * d.act_stride, (uint32_t)d.act_stride,
+                   bar);
       } else {
-        rv_copy_bytes_block(asm_ + (size_t)m * d.act_stride, B.acts + (size_t)tok * d.act_stride,
-                            d.act_stride);
+        rv_copy_bytes_block(asm_ + (size_t)m * d.act_stride, B.acts + (size_t)t * d.act_stride, d.act_stride);
       }
     }
     if (tx) {
@@ -808,7 +1014,7 @@ __global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d,
       phase ^= 1;
     }
     __syncthreads();
-    if (!ok) return;
+    if (!ok) return false;
     RV_PHASE(1, 2);
     if constexpr (FMT == RV_Q6_K) {
       for (int m = 0; m < mt; m++) act_word_sums(asm_ + (size_t)m * d.act_stride, d.hb, asum + m * d.hb * 64);
@@ -851,7 +1057,7 @@ __global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d,
     if (s_last) *cnt = 0;
   }
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last) return true;
   RV_PHASE(1, 4);
   __threadfence();
   const int nwarps = blockDim.x >> 5;
@@ -862,37 +1068,82 @@ __global__ void __launch_bounds__(2 * R * G, G > 1 ? 4 : 4) k_gate_up(MoeDims d,
     for (int k = 0; k < 8; k++) v[k] = __ldcg(src + k);
     q8k_quantize_warp(v, lane, B.acts_moe + (size_t)pos * d.amoe_stride + (size_t)qb * 292);
   }
+  return true;
+}
+
+// grid = (units, M / R).  Dispatch from the index (SPEC false: launched as a
+// programmatic dependent of the routing kernel) or from the speculated
+// pairs (SPEC true: every CTA rebuilds them from the logit bounds and
+// strides over the units).
+template <int FMT, int G, int NBG, int R, bool SPEC>
+__global__ void __launch_bounds__(2 * R * G, 4) k_gate_up(MoeDims d, MoeBufs B, MoeWeights W) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  RV_PHASE(1, 0);
+  const int tile = blockIdx.y;
+  uint32_t phase = 0;
+  if (threadIdx.x == 0) mbar_init((uint64_t *)sm, 1);
+  if constexpr (SPEC) {
+    // Reads only the bounds and activations of the routing kernel, which
+    // completed before the exact-chain kernel ahead of this one passed its
+    // wait, i.e. before this grid launched.  The down kernel may launch at
+    // once: before its own wait it too reads only the bounds.
+    pdl_trigger();
+    __shared__ SpecSmem ss;
+    spec_build(d.E, d.K, B.T, B.spec, ss);
+    RV_PHASE(1, 1);
+    for (int u = blockIdx.x; u < ss.n_units; u += gridDim.x) {
+      const int e = ss.uexp[u], p0 = ss.start[e];
+      const uint32_t msk = ss.mask[e];
+      if (!gate_up_unit<FMT, G, NBG, R>(d, B, W, sm, u, e, p0, p0 + __popc(msk), tile,
+                                        [&](int c) { return (uint32_t)spec_nth_bit(msk, c - p0); }, phase))
+        break;
+    }
+    // The down kernel waits for this grid only; one CTA waiting for the
+    // exact-chain kernel makes this grid's completion imply that one's.
+    if (blockIdx.x == 0 && blockIdx.y == 0) pdl_wait();
+  } else {
+    // The dispatch index and activations are the routing kernel's output.
+    // The down kernel reads the index before its own wait, so it may launch
+    // only once the routing grid has completed: trigger after the wait.
+    pdl_wait();
+    pdl_trigger();
+    __syncthreads();
+    const int u = blockIdx.x;
+    if (u >= *B.n_units) return;
+    RV_PHASE(1, 1);
+    const int4 unit = B.units[u];
+    gate_up_unit<FMT, G, NBG, R>(d, B, W, sm, u, unit.x, unit.y, unit.z, tile,
+                                 [&](int c) { return B.index[c] / (uint32_t)d.K; }, phase);
+  }
 }
 
 // ------------------------------------------------------------- down
-// grid = (max_units, ceil(H / ROWS)), one warp per CTA (ROWS * G <= 32):
-// ROWS rows of one unit's expert for all its tokens.  Launched as a
+// grid = (units, ceil(H / ROWS)), one warp per CTA (ROWS * G <= 32): ROWS
+// rows of one unit's expert for all its positions.  Launched as a
 // programmatic dependent of k_gate_up: the weight tile (which depends only
-// on the routing) is requested before waiting for gate/up to finish.
-// With COMBINE, the last unit to finish a row tile also performs the fixed
-// top-k-order reduction and residual add for those rows of every token
-// (forward.rs:2744-2753); otherwise k_combine does it.
-template <int FMT, int G, int NBG, int ROWS, bool COMBINE>
+// on the dispatch) is requested before waiting for gate/up to finish.
+// SPEC: the units are the speculated pairs (rebuilt from the logit bounds
+// by every CTA), and only the positions the exact routing selected are
+// stored.  With COMBINE, the last unit to finish a row tile also performs
+// the fixed top-k-order reduction and residual add for those rows of every
+// token (forward.rs:2744-2753); otherwise k_combine does it.
+template <int FMT, int G, int NBG, int ROWS, bool COMBINE, bool SPEC>
 __global__ void __launch_bounds__(32, 16) k_down(MoeDims d, MoeBufs B, MoeWeights W) {
   extern __shared__ __align__(16) uint8_t sm[];
   constexpr int MT = RV_MOE_MT;
   static_assert(ROWS * G <= 32, "one warp per CTA");
   RV_PHASE(2, 0);
   pdl_trigger();
-  const int u = blockIdx.x, tile = blockIdx.y;
-  const int nu = *B.n_units;
-  if (u >= nu) return;
-  const int4 unit = B.units[u];
-  const int e = unit.x, p0 = unit.y, p1 = unit.z;
+  const int tile = blockIdx.y;
   const int ms = B.ms;
   const int row0 = tile * ROWS, nrows = min(ROWS, d.H - row0);
   __shared__ int s_last;
+  __shared__ uint32_t s_pair[RV_SPEC_MAX_T];
   uint64_t *bar = (uint64_t *)sm;  // [2]: weights, activations
   const size_t st = tile_stride<FMT>(W.down_row_bytes);
   uint8_t *wsm = sm + 16;
   uint8_t *asm_ = wsm + (((size_t)ROWS * st + 15) & ~(size_t)15) + 16;
   int *asum = (int *)(asm_ + ms * d.amoe_stride);
-  const uint8_t *dsrc = W.base + (size_t)e * W.stride + W.down_off + (size_t)row0 * W.down_row_bytes;
   const bool abulk = rv_bulk_ok(B.acts_moe, asm_, d.amoe_stride);
   const int lane = threadIdx.x;
   if (lane == 0) {
@@ -900,94 +1151,171 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims d, MoeBufs B, MoeWeight
     mbar_init(bar + 1, 1);
   }
   __syncwarp();
-  const uint32_t wtx = stage_rows<FMT>(wsm, dsrc, W.down_row_bytes, nrows, bar, false);
-  if (lane == 0 && wtx) mbar_arrive_expect_tx(bar, wtx);
-  stage_rows<FMT>(wsm, dsrc, W.down_row_bytes, nrows, bar, true);
-  RV_PHASE(2, 1);
-  pdl_wait();  // acts_moe is k_gate_up's output
-  RV_PHASE(2, 2);
+  int nu;
+  const SpecSmem *ssp = nullptr;
+  if constexpr (SPEC) {
+    __shared__ SpecSmem ss;
+    spec_build(d.E, d.K, B.T, B.spec, ss);
+    nu = ss.n_units;
+    ssp = &ss;
+  } else {
+    nu = *B.n_units;
+  }
   const int rsub = lane / G, g = lane % G;
   const bool live = rsub < ROWS && rsub < nrows;
-  const uint8_t *wrow = wsm + (size_t)(live ? rsub : 0) * st;
-  uint32_t phase = 0;
-  bool ok = true;
-  bool wdone = wtx == 0;
-  for (int c0 = p0; c0 < p1; c0 += ms) {
-    const int mt = min(ms, p1 - c0);
-    __syncwarp();
-    const uint8_t *asrc = B.acts_moe + (size_t)c0 * d.amoe_stride;
-    if (abulk) {
-      if (lane == 0) {
-        fence_proxy_async();
-        mbar_arrive_expect_tx(bar + 1, (uint32_t)(mt * d.amoe_stride));
-        bulk_g2s(asm_, asrc, (uint32_t)(mt * d.amoe_stride), bar + 1);
-      }
+  uint32_t wphase = 0, aphase = 0;
+  for (int u = blockIdx.x; u < nu; u += gridDim.x) {
+    int e, p0, p1;
+    uint32_t msk = 0;
+    if constexpr (SPEC) {
+      e = ssp->uexp[u];
+      p0 = ssp->start[e];
+      msk = ssp->mask[e];
+      p1 = p0 + __popc(msk);
     } else {
-      rv_copy_bytes_block(asm_, asrc, (size_t)mt * d.amoe_stride);
+      const int4 unit = B.units[u];
+      e = unit.x;
+      p0 = unit.y;
+      p1 = unit.z;
     }
-    if (!wdone) {
-      ok = mbar_wait_bounded(bar, 0);
-      wdone = true;
-    }
-    if (abulk) {
-      ok = ok && mbar_wait_bounded(bar + 1, phase);
-      phase ^= 1;
-    }
+    const uint8_t *dsrc = W.base + (size_t)e * W.stride + W.down_off + (size_t)row0 * W.down_row_bytes;
     __syncwarp();
-    if (!ok) return;
-    RV_PHASE(2, 3);
-    if constexpr (FMT == RV_Q6_K) {
-      for (int m = 0; m < mt; m++) act_word_sums(asm_ + (size_t)m * d.amoe_stride, d.mb, asum + m * d.mb * 64);
+    const uint32_t wtx = stage_rows<FMT>(wsm, dsrc, W.down_row_bytes, nrows, bar, false);
+    if (lane == 0 && wtx) {
+      fence_proxy_async();
+      mbar_arrive_expect_tx(bar, wtx);
+    }
+    stage_rows<FMT>(wsm, dsrc, W.down_row_bytes, nrows, bar, true);
+    RV_PHASE(2, 1);
+    pdl_wait();  // acts_moe is k_gate_up's output (and the exact routing, SPEC)
+    RV_PHASE(2, 2);
+    bool any = true;
+    if constexpr (SPEC) {
+      // The token-major pair of each position, ~0 where the exact routing
+      // did not select the expert.
+      if (lane < p1 - p0) {
+        const int t = spec_nth_bit(msk, lane);
+        uint32_t pair = ~0u;
+        for (int k = 0; k < d.K; k++)
+          if (B.ids[(size_t)t * d.K + k] == (uint32_t)e) pair = (uint32_t)(t * d.K + k);
+        s_pair[lane] = pair;
+      }
+      any = __any_sync(RV_FULL, lane < p1 - p0 && s_pair[lane] != ~0u);
       __syncwarp();
     }
-    for (int m0 = 0; m0 < mt; m0 += MT) {
-      const int mm = min(MT, mt - m0);
-      if constexpr (G > 1) {
-        for (int m = 0; m < mm; m++) {
-          const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.amoe_stride,
-                                                        asum + (m0 + m) * d.mb * 64, g);
-          if (g == G - 1 && live) {
-            const uint32_t pair = B.index[c0 + m0 + m];
-            B.staged[(size_t)pair * d.H + row0 + rsub] = res;
-          }
+    const uint8_t *wrow = wsm + (size_t)(live ? rsub : 0) * st;
+    bool ok = true, wdone = wtx == 0;
+    for (int c0 = p0; c0 < p1 && any; c0 += ms) {
+      const int mt = min(ms, p1 - c0);
+      __syncwarp();
+      const uint8_t *asrc = B.acts_moe + (size_t)c0 * d.amoe_stride;
+      if (abulk) {
+        if (lane == 0) {
+          fence_proxy_async();
+          mbar_arrive_expect_tx(bar + 1, (uint32_t)(mt * d.amoe_stride));
+          bulk_g2s(asm_, asrc, (uint32_t)(mt * d.amoe_stride), bar + 1);
         }
       } else {
-        float res[MT];
-        row_dot_tokens<FMT, MT>(wrow, d.mb, asm_ + (size_t)m0 * d.amoe_stride, d.amoe_stride,
-                                asum + m0 * d.mb * 64, (size_t)d.mb * 64, mm, res);
-#pragma unroll
-        for (int m = 0; m < MT; m++)
-          if (m < mm && live) {
-            const uint32_t pair = B.index[c0 + m0 + m];
-            B.staged[(size_t)pair * d.H + row0 + rsub] = res[m];
+        rv_copy_bytes_block(asm_, asrc, (size_t)mt * d.amoe_stride);
+      }
+      if (!wdone) {
+        ok = mbar_wait_bounded(bar, wphase);
+        wphase ^= 1;
+        wdone = true;
+      }
+      if (abulk) {
+        ok = mbar_wait_bounded(bar + 1, aphase) && ok;
+        aphase ^= 1;
+      }
+      __syncwarp();
+      if (!ok) return;
+      RV_PHASE(2, 3);
+      if constexpr (FMT == RV_Q6_K) {
+        for (int m = 0; m < mt; m++) act_word_sums(asm_ + (size_t)m * d.amoe_stride, d.mb, asum + m * d.mb * 64);
+        __syncwarp();
+      }
+      auto pair_of = [&](int c) -> uint32_t {
+        if constexpr (SPEC) return s_pair[c - p0];
+        else return B.index[c];
+      };
+      for (int m0 = 0; m0 < mt; m0 += MT) {
+        const int mm = min(MT, mt - m0);
+        if constexpr (G > 1) {
+          for (int m = 0; m < mm; m++) {
+            const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.amoe_stride,
+                                                          asum + (m0 + m) * d.mb * 64, g);
+            const uint32_t pair = pair_of(c0 + m0 + m);
+            if (g == G - 1 && live && pair != ~0u) B.staged[(size_t)pair * d.H + row0 + rsub] = res;
           }
+        } else {
+          float res[MT];
+          row_dot_tokens<FMT, MT>(wrow, d.mb, asm_ + (size_t)m0 * d.amoe_stride, d.amoe_stride,
+                                  asum + m0 * d.mb * 64, (size_t)d.mb * 64, mm, res);
+#pragma unroll
+          for (int m = 0; m < MT; m++)
+            if (m < mm && live) {
+              const uint32_t pair = pair_of(c0 + m0 + m);
+              if (pair != ~0u) B.staged[(size_t)pair * d.H + row0 + rsub] = res[m];
+            }
+        }
+      }
+    }
+    if (!wdone) {  // no selected position: the weight copy still has to land
+      ok = mbar_wait_bounded(bar, wphase);
+      wphase ^= 1;
+      __syncwarp();
+      if (!ok) return;
+    }
+    RV_PHASE(2, 4);
+    if constexpr (COMBINE) {
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) {
+        int *cnt = &B.down_cnt[tile];
+        const int old = atomicAdd(cnt, 1);
+        s_last = old == nu - 1;
+        if (s_last) *cnt = 0;
+      }
+      __syncwarp();
+      if (!s_last) continue;
+      RV_PHASE(2, 5);
+      __threadfence();
+      // acc = 0; acc += w_k * d_k in top-k order; residual += acc.
+      for (int i = lane; i < B.T * nrows; i += 32) {
+        const int t = i / nrows, h = row0 + i % nrows;
+        float acc = 0.0f;
+        for (int k = 0; k < d.K; k++) {
+          const size_t pair = (size_t)t * d.K + k;
+          acc = __fadd_rn(acc, __fmul_rn(B.w[pair], __ldcg(B.staged + pair * d.H + h)));
+        }
+        float *res = B.residual + (size_t)t * d.H + h;
+        *res = __fadd_rn(*res, acc);
       }
     }
   }
-  RV_PHASE(2, 4);
-  if constexpr (COMBINE) {
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) {
-      int *cnt = &B.down_cnt[tile];
-      const int old = atomicAdd(cnt, 1);
-      s_last = old == nu - 1;
-      if (s_last) *cnt = 0;
-    }
-    __syncwarp();
-    if (!s_last) return;
-    RV_PHASE(2, 5);
-    __threadfence();
-    // acc = 0; acc += w_k * d_k in top-k order; residual += acc.
-    for (int i = lane; i < B.T * nrows; i += 32) {
-      const int t = i / nrows, h = row0 + i % nrows;
-      float acc = 0.0f;
-      for (int k = 0; k < d.K; k++) {
-        const size_t pair = (size_t)t * d.K + k;
-        acc = __fadd_rn(acc, __fmul_rn(B.w[pair], __ldcg(B.staged + pair * d.H + h)));
+  if constexpr (SPEC) {
+    if (blockIdx.x == 0 && blockIdx.y == 0) {
+      // After the wait above (every CTA has a unit): the exact routing is
+      // final.  Check that the speculated set held it, and write the
+      // dispatch taps (position -> token-major pair, ~0 where unselected).
+      for (int p = lane; p < B.T * d.K; p += 32) {
+        const uint32_t e = B.ids[p];
+        // Cannot happen: the speculated set holds the exact top-k.
+        if (e >= (uint32_t)d.E || !((ssp->mask[e] >> (p / d.K)) & 1u)) rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
       }
-      float *res = B.residual + (size_t)t * d.H + h;
-      *res = __fadd_rn(*res, acc);
+      for (int e = lane; e < d.E; e += 32) {
+        uint32_t msk = ssp->mask[e];
+        int pos = ssp->start[e];
+        while (msk) {
+          const int t = __ffs(msk) - 1;
+          msk &= msk - 1;
+          uint32_t pair = ~0u;
+          for (int k = 0; k < d.K; k++)
+            if (B.ids[(size_t)t * d.K + k] == (uint32_t)e) pair = (uint32_t)(t * d.K + k);
+          B.index[pos++] = pair;
+        }
+      }
+      for (int e = lane; e <= d.E; e += 32) B.index_start[e] = ssp->start[e];
     }
   }
 }

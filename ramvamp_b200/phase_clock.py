@@ -6,6 +6,7 @@ every kernel stamps %globaltimer (nanoseconds, common to all SMs) at its
 phases; the normal build compiles the stamps out.
 
     python -m ramvamp_b200.phase_clock decode [layers]   # one decode layer, CTA phases
+                                                         # (RV_DECODE_SPEC=0: without speculation)
     python -m ramvamp_b200.phase_clock tensor [tokens]   # tensor-path GEMM: per-CTA phases + one CTA's stages
 
 Output: microseconds from the first stamp of the traced layer.
@@ -85,10 +86,17 @@ def decode(n_layers: int = 4) -> None:
             res.copy_(toks[i:i + 1])
             g.replay()
     s.synchronize()
-    bufs = [_read(lib, k) for k in range(4)]
-    t0 = bufs[0][:E, 0].min()
-    _print_phases("route", bufs[0], t0, ["start", "pdl_wait", "residual", "norm", "rows", "chain done",
-                                         "LAST:start", "LAST:routed", "LAST:index"])
+    bufs = [_read(lib, k) for k in range(6)]
+    first = bufs[0][:, 0]
+    t0 = first[first != 0].min()
+    if os.environ.get("RV_DECODE_SPEC", "1") != "0":
+        _print_phases("route (norm, bounds)", bufs[0], t0, ["start", "pdl_wait", "residual", "norm", "bounds",
+                                                            "q8k"])
+        _print_phases("exact chains", bufs[5], t0, ["start", "pdl_wait", "rows", "chain done", "LAST:start",
+                                                    "LAST:routed", "LAST:index"])
+    else:
+        _print_phases("route", bufs[0], t0, ["start", "pdl_wait", "residual", "norm", "rows", "chain done",
+                                             "LAST:start", "LAST:routed", "LAST:index"])
     _print_phases("gate_up", bufs[1], t0, ["start", "unit", "data", "compute", "LAST:quant"])
     _print_phases("down", bufs[2], t0, ["start", "weights issued", "pdl_wait", "data", "compute", "LAST:combine"])
     tail = bufs[3][0]

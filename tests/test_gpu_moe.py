@@ -78,15 +78,19 @@ def run_gpu(rv, world, li, x):
 def taps(rv, eng, T):
     t = eng.taps()
     a = lambda p, n, dt=torch.float32: host(rv.alias(p, n, dt))
+    n = int(a(t.index_start, E + 1, torch.int32)[E])  # positions: T*K, or the speculated pairs
     return dict(
         normed=a(t.normed, T * H).reshape(T, H),
         acts=a(t.acts, T * t.acts_stride, torch.uint8).reshape(T, t.acts_stride),
         logits=a(t.logits, T * E).reshape(T, E),
-        index=a(t.index, T * K, torch.int32).view(np.uint32),
-        swiglu=a(t.swiglu, T * K * M).reshape(T * K, M),
-        acts_moe=a(t.acts_moe, T * K * t.acts_moe_stride, torch.uint8).reshape(T * K, t.acts_moe_stride),
+        index=a(t.index, n, torch.int32).view(np.uint32),
+        swiglu=a(t.swiglu, n * M).reshape(n, M),
+        acts_moe=a(t.acts_moe, n * t.acts_moe_stride, torch.uint8).reshape(n, t.acts_moe_stride),
         staged=a(t.staged, T * K * H).reshape(T * K, H),
     )
+
+
+UNSELECTED = 0xFFFFFFFF  # a speculated position the exact routing did not select
 
 
 @pytest.mark.parametrize("li", [0, 1])
@@ -107,9 +111,14 @@ def test_decode_token_bit_identical_with_every_intermediate(rv, orc, world, li):
         gate, up = t["gate_up"][:, 0, :], t["gate_up"][:, 1, :]
         sw = np.stack([orc.swiglu_combine(gate[p], up[p]) for p in range(K)])
         amoe = t["acts_moe"].view(np.uint8).reshape(K, 3 * 292)
+        seen = []
         for pos, pair in enumerate(g["index"]):
+            if pair == UNSELECTED:
+                continue
+            seen.append(pair)
             assert bits(g["swiglu"][pos]).tobytes() == bits(sw[pair]).tobytes()
             assert g["acts_moe"][pos, :3 * 292].tobytes() == amoe[pair].tobytes()
+        assert sorted(seen) == list(range(K))
         assert bits(g["staged"]).tobytes() == bits(t["staged"]).tobytes()
         assert bits(res).tobytes() == bits(want).tobytes()
 
@@ -172,6 +181,95 @@ def test_router_tie_goes_to_lowest_expert(rv, orc, world):
     want, wids, ww, _ = orc.moe_decode(L, host(x), threads=THREADS)
     assert (got.view(np.uint32) == wids).all()
     assert bits(host(res)).tobytes() == bits(want).tobytes()
+
+
+def oracle_with_router(orc, table, layers, router):
+    return orc.make_layer(H, M, E, K, 1e-6, host(layers[0].ffn_norm), host(router), layers[0].blobs,
+                          table.layouts[0].stride, table.layouts[0].gate_off, table.layouts[0].up_off,
+                          table.layouts[0].down_off, 0, 0, 2)
+
+
+def test_decode_logit_bounds_hold_and_cover_top_k(rv, world):
+    """Speculative decode dispatch: every router logit lies in its (lo, hi)
+    interval, and the experts with hi + 2^-18 >= the K-th largest lo hold
+    the exact top-k -- usually exactly k of them."""
+    table, layers, eng = world
+    sizes = []
+    for li in (0, 1):
+        for seed in range(20, 32):
+            T = 1 + seed % 4
+            x = inputs(rv, T, seed)
+            _, ids, _ = run_gpu(rv, world, li, x)
+            t = eng.taps()
+            lg = host(rv.alias(t.logits, T * E, torch.float32)).reshape(T, E)
+            b = host(rv.alias(t.logit_bounds, T * E * 2, torch.float32)).reshape(T, E, 2)
+            assert (b[..., 0] <= lg).all() and (lg <= b[..., 1]).all()
+            assert (b[..., 1] - b[..., 0] < 1e-2).all()
+            for tt in range(T):
+                thr = np.sort(b[tt, :, 0])[::-1][K - 1]
+                spec = np.nonzero(b[tt, :, 1].astype(np.float64) + 2.0 ** -18 >= thr)[0]
+                assert set(ids[tt].tolist()) <= set(spec.tolist())
+                sizes.append(len(spec))
+    assert np.mean(sizes) < K + 0.5, sizes
+
+
+def test_decode_speculation_with_a_tie_at_the_cut(rv, orc, world):
+    """Two experts tied for the K-th place are both speculated; the exact
+    routing keeps the lower index (forward.rs:2688-2699) and the result is
+    the oracle's, bit for bit."""
+    table, layers, eng = world
+    x = inputs(rv, 1, 91)
+    run_gpu(rv, world, 0, x)
+    order = np.argsort(-taps(rv, eng, 1)["logits"][0], kind="stable")
+    kth, nxt = int(order[K - 1]), int(order[K])
+    router = layers[0].router.clone()
+    router[nxt] = router[kth]
+    res = x.clone()
+    ids = torch.empty(K, dtype=torch.int32, device="cuda")
+    w = torch.empty(K, dtype=torch.float32, device="cuda")
+    eng.forward(table, 0, layers[0].ffn_norm, router, res, ids, w)
+    g = taps(rv, eng, 1)
+    assert len(g["index"]) > K and (g["index"] == UNSELECTED).sum() == len(g["index"]) - K
+    want, wids, ww, _ = orc.moe_decode(oracle_with_router(orc, table, layers, router), host(x), threads=THREADS)
+    assert (host(ids).view(np.uint32) == wids[0]).all() and min(kth, nxt) in wids[0]
+    assert bits(host(w)).tobytes() == bits(ww[0]).tobytes()
+    assert bits(host(res)).tobytes() == bits(want).tobytes()
+
+
+def test_decode_speculation_of_every_expert(rv, orc, world):
+    """Identical router rows tie every logit: all experts are speculated
+    (more units than the expert grids hold, so their CTAs stride), and the
+    exact routing picks experts 0..K-1."""
+    table, layers, eng = world
+    x = inputs(rv, 2, 93)
+    router = (0.01 * x[0]).expand(E, H).contiguous()
+    res = x.clone()
+    ids = torch.empty(2 * K, dtype=torch.int32, device="cuda")
+    w = torch.empty(2 * K, dtype=torch.float32, device="cuda")
+    eng.forward(table, 0, layers[0].ffn_norm, router, res, ids, w)
+    g = taps(rv, eng, 2)
+    assert len(g["index"]) == 2 * E
+    want, wids, ww, _ = orc.moe_decode(oracle_with_router(orc, table, layers, router), host(x), threads=THREADS)
+    got = host(ids).view(np.uint32).reshape(2, K)
+    assert (got == wids).all() and (got == np.arange(K)).all()
+    assert bits(host(w)).tobytes() == bits(ww.reshape(-1)).tobytes()
+    assert bits(host(res)).tobytes() == bits(want).tobytes()
+    rv.device_status(0)
+
+
+def test_decode_without_speculation_is_identical(rv, world, monkeypatch):
+    """RV_DECODE_SPEC=0 (routing first, then the experts) gives the same
+    bits as the speculative dispatch."""
+    table, layers, eng = world
+    monkeypatch.setenv("RV_DECODE_SPEC", "0")
+    plain = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=8, device=0)
+    for li, T, seed in ((0, 1, 41), (1, 1, 42), (0, 5, 43), (1, 8, 44)):
+        x = inputs(rv, T, seed)
+        a = x.clone()
+        b = x.clone()
+        eng.forward(table, li, layers[li].ffn_norm, layers[li].router, a)
+        plain.forward(table, li, layers[li].ffn_norm, layers[li].router, b)
+        assert bits(host(a)).tobytes() == bits(host(b)).tobytes()
 
 
 def test_forward_errors(rv, world):
