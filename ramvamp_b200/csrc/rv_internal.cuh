@@ -231,6 +231,20 @@ RV_DEVFN long long rv_globaltimer() {
     const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                   \
     if (cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = rv_globaltimer();         \
   } while (0)
+// %globaltimer of thread 0 in slot i, from a helper shared by several
+// kernels (slot k only meaningful for the kernel that owns it).
+#define RV_PHASE_ANY_T0(k, i)                                                              \
+  do {                                                                                    \
+    const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                            \
+    if (threadIdx.x == 0 && cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = rv_globaltimer(); \
+  } while (0)
+// clock64 of thread 0 in slot i (pairs with a %globaltimer stamp to give
+// the SM clock rate during a phase).
+#define RV_PHASE_CLK(k, i)                                                                    \
+  do {                                                                                       \
+    const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                               \
+    if (threadIdx.x == 0 && cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = (long long)clock64(); \
+  } while (0)
 // Per-stage event trace of one CTA (blockIdx.x == 0, blockIdx.y == 20):
 // row `stage` of kernel slot k.
 #define RV_TRACE(k, stage, ev)                                                          \
@@ -253,6 +267,12 @@ RV_DEVFN long long rv_globaltimer() {
 #define RV_PHASE_ANY(k, i) \
   do {                   \
   } while (0)
+#define RV_PHASE_CLK(k, i) \
+  do {                   \
+  } while (0)
+#define RV_PHASE_ANY_T0(k, i) \
+  do {                      \
+  } while (0)
 #define RV_PHASE(k, i) \
   do {                 \
   } while (0)
@@ -267,16 +287,19 @@ RV_DEVFN long long rv_globaltimer() {
 RV_DEVFN void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 RV_DEVFN void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// True when every double within rel*|r| of r rounds to the same float as r:
-// the f32 result of a double computation is then independent of how the
-// double was summed, within that error bound.
-RV_DEVFN bool f32_rounding_stable(double r, double rel) {
-  if (!isfinite(r)) return false;
-  const float f = __double2float_rn(r);
-  const double df = (double)f, tol = fabs(r) * rel;
-  const double mh = 0.5 * (df + (double)nextafterf(f, INFINITY));
-  const double ml = 0.5 * (df + (double)nextafterf(f, -INFINITY));
-  return fabs(mh - r) > tol && fabs(r - ml) > tol;
+// True when every double within 2^-k * |r| of r (k in 30..52) rounds to the
+// same float as r, so the f32 result of a double computation does not
+// depend on how the double was summed within that bound.  Decided from the
+// 29 mantissa bits the float rounding drops: the rounding boundaries (the
+// midpoints between floats) are where they equal 2^28, and 2^-k * |r| is
+// less than 2^(53-k) units of r's last place.  False outside the normal
+// float range.
+RV_DEVFN bool f32_rounding_stable(double r, int k) {
+  const uint64_t b = (uint64_t)__double_as_longlong(r);
+  const int ex = (int)((b >> 52) & 0x7ff) - 1023;
+  if (ex < -125 || ex > 126) return false;
+  const long long low = (long long)(b & ((1ull << 29) - 1));
+  return llabs(low - (1ll << 28)) > (1ll << (53 - k));
 }
 
 // ------------------------------------------------ Q8_K warp quantizer

@@ -97,12 +97,10 @@ static std::mutex g_init_mu;
 static bool g_dev_ready[64];
 
 #define RV_ROUTE_SMEM_ONE_PER_SM (120u * 1024u)
-// Speculative decode: router rows per exact-chain CTA, that kernel's
-// shared-memory budget, and the units the expert grids cover beyond T*K
-// (more speculated experts than that are strided over).
+// Speculative decode: router rows per exact-chain CTA.  The expert grids
+// cover T*K units (usually all there are); CTAs stride over any more.
 #define RV_CHAIN_EXPERTS 16
 #define RV_SMEM_PER_CTA (227u * 1024u)  // the per-CTA shared-memory limit of sm_100
-#define RV_SPEC_SLACK_UNITS 2
 
 static int ensure_device(int dev) {
   if (dev < 0 || dev >= 64) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
@@ -135,7 +133,8 @@ static int ensure_device(int dev) {
   cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_prologue, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_route_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_route_spec, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_route_spec<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_route_spec<RV_GEO_QWEN3>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
 
   cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaError_t e3 = cudaGetLastError();
@@ -763,6 +762,10 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// The decode kernels come in a Qwen3-geometry instantiation (hidden 2048,
+// moe 768, 128 experts, top-8) with the dimensions as constants.
+static bool geo_qwen3(const MoeDims &d) { return d.H == 2048 && d.M == 768 && d.E == 128 && d.K == 8; }
+
 // The exact router chains of speculative decode: RV_CHAIN_EXPERTS router
 // rows per CTA (fewer when the rows and T residual rows would not fit), one
 // cluster of all the CTAs when there are at most 8 of them.  Each CTA takes
@@ -776,7 +779,9 @@ static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, cudaStr
   void (*kern)(MoeDims, MoeBufs, int) = nullptr;
   size_t room = 0;
   for (int v = 0; v < 2 && !kern; v++) {  // the cluster variant first
-    void (*k)(MoeDims, MoeBufs, int) = v == 0 ? k_route_chain<true> : k_route_chain<false>;
+    const bool q3 = geo_qwen3(d);
+    void (*k)(MoeDims, MoeBufs, int) = v == 0 ? (q3 ? k_route_chain<true, RV_GEO_QWEN3> : k_route_chain<true, 0>)
+                                              : (q3 ? k_route_chain<false, RV_GEO_QWEN3> : k_route_chain<false, 0>);
     cudaFuncAttributes fa;
     RV_CUDA(cudaFuncGetAttributes(&fa, k));
     room = (size_t)RV_SMEM_PER_CTA - fa.sharedSizeBytes;
@@ -812,57 +817,64 @@ static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, cudaStr
 // mode (a thread per row, up to 8 tokens in flight) serves larger batches.
 // units: the grid's first dimension (the unit capacity, or for the
 // speculative kernels the units expected; they stride over the rest).
-template <int FMT, int G, int NBG, int R, bool SPEC>
+
+template <int FMT, int G, int NBG, int R, bool SPEC, int GEO>
 static void launch_gate_up_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int units, cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.gu_row_bytes : W.gu_row_bytes + 16;
   const size_t smem = 16 + round16(2 * (size_t)R * st) + 16 + (size_t)B.ms * d.act_stride +
                       (FMT == RV_Q6_K ? (size_t)B.ms * d.hb * 64 * 4 : 0) + 2 * R * RV_MOE_MT * 4;
   dim3 grid((unsigned)units, (unsigned)(d.M / R));
-  cudaFuncSetAttribute(k_gate_up<FMT, G, NBG, R, SPEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl(k_gate_up<FMT, G, NBG, R, SPEC>, grid, dim3(2 * R * G), smem, s, d, B, W);
+  cudaFuncSetAttribute(k_gate_up<FMT, G, NBG, R, SPEC, GEO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl(k_gate_up<FMT, G, NBG, R, SPEC, GEO>, grid, dim3(2 * R * G), smem, s, d, B, W);
 }
 template <int FMT>
 static void launch_gate_up(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int T, int spec_units,
                            cudaStream_t s) {
+  const bool q3 = geo_qwen3(d);
   if (spec_units) {
-    if (d.hb == 8) launch_gate_up_t<FMT, 4, 2, 8, true>(d, B, W, spec_units, s);
-    else launch_gate_up_t<FMT, 1, 1, 32, true>(d, B, W, spec_units, s);
+    if (q3) launch_gate_up_t<FMT, 4, 2, 8, true, RV_GEO_QWEN3>(d, B, W, spec_units, s);
+    else if (d.hb == 8) launch_gate_up_t<FMT, 4, 2, 8, true, 0>(d, B, W, spec_units, s);
+    else launch_gate_up_t<FMT, 1, 1, 32, true, 0>(d, B, W, spec_units, s);
   } else if (T <= RV_SMALL_T && d.hb == 8) {
-    launch_gate_up_t<FMT, 4, 2, 8, false>(d, B, W, B.max_units, s);
+    if (q3) launch_gate_up_t<FMT, 4, 2, 8, false, RV_GEO_QWEN3>(d, B, W, B.max_units, s);
+    else launch_gate_up_t<FMT, 4, 2, 8, false, 0>(d, B, W, B.max_units, s);
   } else {
-    launch_gate_up_t<FMT, 1, 1, 32, false>(d, B, W, B.max_units, s);
+    launch_gate_up_t<FMT, 1, 1, 32, false, 0>(d, B, W, B.max_units, s);
   }
 }
-template <int FMT, int G, int NBG, int ROWS, bool COMBINE, bool SPEC>
+template <int FMT, int G, int NBG, int ROWS, bool COMBINE, bool SPEC, int GEO>
 static cudaError_t launch_down_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int units,
                                  cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.down_row_bytes : W.down_row_bytes + 16;
   const size_t smem = 16 + round16((size_t)ROWS * st) + 16 + (size_t)B.ms * d.amoe_stride +
                       (FMT == RV_Q6_K ? (size_t)B.ms * d.mb * 64 * 4 : 0) + 16;
   dim3 grid((unsigned)units, (unsigned)((d.H + ROWS - 1) / ROWS));
-  cudaFuncSetAttribute(k_down<FMT, G, NBG, ROWS, COMBINE, SPEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaFuncSetAttribute(k_down<FMT, G, NBG, ROWS, COMBINE, SPEC, GEO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)smem);
-  return launch_pdl(k_down<FMT, G, NBG, ROWS, COMBINE, SPEC>, grid, dim3(32), smem, s, d, B, W);
+  return launch_pdl(k_down<FMT, G, NBG, ROWS, COMBINE, SPEC, GEO>, grid, dim3(32), smem, s, d, B, W);
 }
 // Returns true when the down kernel also performed the combine (only when
 // fuse_combine allows it; always for the speculative kernels).
 template <int FMT>
 static bool launch_down(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int T, bool fuse_combine,
                         int spec_units, cudaStream_t s) {
+  const bool q3 = geo_qwen3(d);
   if (spec_units) {
-    if (d.mb == 3) launch_down_t<FMT, 3, 1, 8, true, true>(d, B, W, spec_units, s);
-    else launch_down_t<FMT, 1, 1, 32, true, true>(d, B, W, spec_units, s);
+    if (q3) launch_down_t<FMT, 3, 1, 8, true, true, RV_GEO_QWEN3>(d, B, W, spec_units, s);
+    else if (d.mb == 3) launch_down_t<FMT, 3, 1, 8, true, true, 0>(d, B, W, spec_units, s);
+    else launch_down_t<FMT, 1, 1, 32, true, true, 0>(d, B, W, spec_units, s);
     return true;
   }
   if (T <= RV_SMALL_T && d.mb == 3) {
     if (fuse_combine) {
-      launch_down_t<FMT, 3, 1, 8, true, false>(d, B, W, B.max_units, s);
+      if (q3) launch_down_t<FMT, 3, 1, 8, true, false, RV_GEO_QWEN3>(d, B, W, B.max_units, s);
+      else launch_down_t<FMT, 3, 1, 8, true, false, 0>(d, B, W, B.max_units, s);
       return true;
     }
-    launch_down_t<FMT, 3, 1, 8, false, false>(d, B, W, B.max_units, s);
+    launch_down_t<FMT, 3, 1, 8, false, false, 0>(d, B, W, B.max_units, s);
     return false;
   }
-  launch_down_t<FMT, 1, 1, 32, false, false>(d, B, W, B.max_units, s);
+  launch_down_t<FMT, 1, 1, 32, false, false, 0>(d, B, W, B.max_units, s);
   return false;
 }
 
@@ -1071,10 +1083,13 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
     // router chains beside gate/up on the speculated experts; then down
     // and combine on the exact routing.
     const size_t xrow = (size_t)(d.H + 4) * 4;
-    RV_CUDA(launch_pdl(k_route_spec, dim3((unsigned)((d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC)), dim3(128),
-                       16 + (size_t)(RV_SPEC_EPC + 1) * d.H * 4 + T * xrow, s, d, B));
+    // Shared memory padded past half an SM's: one routing CTA per SM.
+    const size_t rs_need = 16 + (size_t)(RV_SPEC_EPC + 1) * d.H * 4 + T * xrow;
+    RV_CUDA(launch_pdl(geo_qwen3(d) ? k_route_spec<RV_GEO_QWEN3> : k_route_spec<0>,
+                       dim3((unsigned)((d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC)), dim3(128),
+                       std::max(rs_need, (size_t)RV_ROUTE_SMEM_ONE_PER_SM), s, d, B));
     if ((rc = launch_route_chain(d, B, T, s))) return rc;
-    spec_units = std::min(d.E, T * d.K + RV_SPEC_SLACK_UNITS);
+    spec_units = std::min(d.E, T * d.K);
   } else if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch
     // Shared memory padded past half an SM's so that no two routing CTAs

@@ -76,6 +76,26 @@ struct MoeWeights {
   size_t gu_row_bytes, down_row_bytes;
 };
 
+// The geometry as compile-time constants when GEO == 1 (Qwen3-30B-A3B:
+// hidden 2048, moe 768, 128 experts, top-8), so the decode kernels' loops
+// and index arithmetic fold; GEO == 0 keeps the engine's runtime values.
+#define RV_GEO_QWEN3 1
+template <int GEO>
+RV_DEVFN MoeDims geo_dims(const MoeDims &d) {
+  MoeDims g = d;
+  if constexpr (GEO == RV_GEO_QWEN3) {
+    g.H = 2048;
+    g.M = 768;
+    g.E = 128;
+    g.K = 8;
+    g.hb = 8;
+    g.mb = 3;
+    g.act_stride = 2336;
+    g.amoe_stride = 880;
+  }
+  return g;
+}
+
 // ------------------------------------------------------------ prologue
 __global__ void __launch_bounds__(256) k_prologue(MoeDims d, MoeBufs B) {
   extern __shared__ __align__(16) uint8_t sm[];
@@ -146,7 +166,7 @@ RV_DEVFN void route_token_warp(const MoeDims &d, const MoeBufs &B, int t, const 
 #pragma unroll
   for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
   double rinv = __drcp_rn(part);
-  if (!f32_rounding_stable(rinv, 0x1p-42)) {
+  if (!f32_rounding_stable(rinv, 42)) {
     double sum = 0.0;
     if (lane == 0)
       for (int e = 0; e < d.E; e++) sum = __dadd_rn(sum, es[e]);
@@ -202,7 +222,8 @@ RV_DEVFN void route_token_warp(const MoeDims &d, const MoeBufs &B, int t, const 
 // doubles, ps [256] floats, sel [16] floats, red [8] doubles, flag.
 template <int NT = 0>
 RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, const float *lg, double *es, float *ps,
-                                float *sel, double *red, int *counts, uint32_t *sids) {
+                                float *sel, double *red, int *counts, uint32_t *sids, const uint8_t *cand = nullptr,
+                                int ncand = 0, const uint32_t *cmask = nullptr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float x[2];
   float mx = -INFINITY;
@@ -245,7 +266,7 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, const
   // the reference's serial sum; recompute serially when 1/sum is that close
   // to a float rounding midpoint.
   double rinv = __drcp_rn(__dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3])));
-  if (!f32_rounding_stable(rinv, 0x1p-42)) {
+  if (!f32_rounding_stable(rinv, 42)) {
     double sum = 0.0;
     for (int e = 0; e < d.E; e++) sum = __dadd_rn(sum, es[e]);
     rinv = __drcp_rn(sum);
@@ -270,6 +291,26 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, const
     cta_sync<NT>();
     return;
   }
+  if (cand) {
+    // Only the listed experts can be in the top-k, so ranking them among
+    // themselves gives the same order (checked below).
+    for (int ci = tid; ci < ncand; ci += 128) {
+      const int e = cand[ci];
+      const float p = ps[e];
+      int rank = 0;
+      for (int i = 0; i < ncand; i++) {
+        const int f = cand[i];
+        const float q = ps[f];
+        rank += (q > p) | ((q == p) & (f < e));
+      }
+      if (rank < d.K) {
+        B.ids[(size_t)t * d.K + rank] = (uint32_t)e;
+        sids[t * d.K + rank] = (uint32_t)e;
+        sel[rank] = p;
+        atomicAdd(&counts[e], 1);
+      }
+    }
+  } else
 #pragma unroll
   for (int j = 0; j < 2; j++) {
     const int e = tid + 128 * j;
@@ -302,6 +343,17 @@ RV_DEVFN void route_token_block(const MoeDims &d, const MoeBufs &B, int t, const
   RV_TRACE_TAIL(5);
   cta_sync<NT>();
   RV_TRACE_TAIL(6);
+  if (cand) {
+    // No unlisted expert beats the k-th selected one.
+    const float pk = sel[d.K - 1];
+    const uint32_t ek = sids[t * d.K + d.K - 1];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int e = tid + 128 * j;
+      if (e < d.E && !((cmask[e >> 5] >> (e & 31)) & 1u) && (ps[e] > pk || (ps[e] == pk && (uint32_t)e < ek)))
+        rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
+    }
+  }
   if (tid < d.K) {
     float wsum = -0.0f;  // the in-order sum of the selected weights
     for (int k = 0; k < d.K; k++) wsum = __fadd_rn(wsum, sel[k]);
@@ -450,35 +502,54 @@ __global__ void __launch_bounds__(1024) k_index(MoeDims d, MoeBufs B) {
 // and its Q8_K, routes every token and builds the dispatch index.
 #define RV_SMALL_T 8
 // dot_f32 (forward.rs:1231-1237): acc = acc + a[k]*b[k] for k in order, no
-// FMA.  The adds form one dependent chain; the operands of the next 32
-// products are loaded into registers before the current 32 adds so the
-// chain runs at the add latency.  n4 (float4 count) must be a multiple of 8.
+// FMA.  The adds form one dependent chain; the products of the next 32
+// elements are formed between the adds of the current 32 (and their
+// operands loaded one block earlier), so the chain runs near the add
+// latency.  n4 (float4 count) must be a multiple of 8.
 RV_DEVFN float serial_dot_f32(const float4 *a, const float4 *b, int n4) {
   float acc = 0.0f;
+  float p[32];
   float4 ra[8], rb[8];
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     ra[j] = a[j];
     rb[j] = b[j];
   }
-  for (int k = 0; k < n4; k += 8) {
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    p[4 * j + 0] = __fmul_rn(ra[j].x, rb[j].x);
+    p[4 * j + 1] = __fmul_rn(ra[j].y, rb[j].y);
+    p[4 * j + 2] = __fmul_rn(ra[j].z, rb[j].z);
+    p[4 * j + 3] = __fmul_rn(ra[j].w, rb[j].w);
+  }
+  const int k1 = 8 < n4 ? 8 : 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    ra[j] = a[k1 + j];
+    rb[j] = b[k1 + j];
+  }
+  for (int k = 8; k <= n4; k += 8) {
+    const int kn = k + 8 < n4 ? k + 8 : 0;
     float4 na[8], nb[8];
-    const int kn = k + 8 < n4 ? k + 8 : k;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       na[j] = a[kn + j];
       nb[j] = b[kn + j];
     }
-    float p[32];
+    float q[32];
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      p[4 * j + 0] = __fmul_rn(ra[j].x, rb[j].x);
-      p[4 * j + 1] = __fmul_rn(ra[j].y, rb[j].y);
-      p[4 * j + 2] = __fmul_rn(ra[j].z, rb[j].z);
-      p[4 * j + 3] = __fmul_rn(ra[j].w, rb[j].w);
+      acc = __fadd_rn(acc, p[4 * j + 0]);
+      q[4 * j + 0] = __fmul_rn(ra[j].x, rb[j].x);
+      acc = __fadd_rn(acc, p[4 * j + 1]);
+      q[4 * j + 1] = __fmul_rn(ra[j].y, rb[j].y);
+      acc = __fadd_rn(acc, p[4 * j + 2]);
+      q[4 * j + 2] = __fmul_rn(ra[j].z, rb[j].z);
+      acc = __fadd_rn(acc, p[4 * j + 3]);
+      q[4 * j + 3] = __fmul_rn(ra[j].w, rb[j].w);
     }
 #pragma unroll
-    for (int j = 0; j < 32; j++) acc = __fadd_rn(acc, p[j]);
+    for (int j = 0; j < 32; j++) p[j] = q[j];
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       ra[j] = na[j];
@@ -504,23 +575,28 @@ RV_DEVFN void norm_rows_cta(const MoeDims &d, int T, float *xs, int xstride, con
     double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
     for (int k = 4 * lane; k < q; k += 128) {
       const float4 v = *(const float4 *)(x + k);
-      p0 = __dadd_rn(p0, __dmul_rn((double)v.x, (double)v.x));
-      p1 = __dadd_rn(p1, __dmul_rn((double)v.y, (double)v.y));
-      p2 = __dadd_rn(p2, __dmul_rn((double)v.z, (double)v.z));
-      p3 = __dadd_rn(p3, __dmul_rn((double)v.w, (double)v.w));
+      // (double)v * (double)v is exact, so the fused form adds the same value.
+      p0 = __fma_rn((double)v.x, (double)v.x, p0);
+      p1 = __fma_rn((double)v.y, (double)v.y, p1);
+      p2 = __fma_rn((double)v.z, (double)v.z, p2);
+      p3 = __fma_rn((double)v.w, (double)v.w, p3);
     }
     double part = __dadd_rn(__dadd_rn(p0, p1), __dadd_rn(p2, p3));
 #pragma unroll
     for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
     if (lane == 0) red[4 * t + warp] = part;
   }
+  RV_PHASE_ANY_T0(0, 6);
   cta_sync<NT>();
   if (threadIdx.x < T) {
     const int t = threadIdx.x;
     const double sum = __dadd_rn(__dadd_rn(red[4 * t], red[4 * t + 1]), __dadd_rn(red[4 * t + 2], red[4 * t + 3]));
-    const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)d.H), (double)d.eps)));
+    // The reference rounds sum/n, + eps, sqrt and 1/x one by one in f64;
+    // the f64 reciprocal square root of the mean lies within a few ulps
+    // (2^-50 relative) of that, far inside the 2^-38 the check allows.
+    const double r = rsqrt(__dadd_rn(__dmul_rn(sum, 1.0 / (double)d.H), (double)d.eps));
     float inv = __double2float_rn(r);
-    if (!f32_rounding_stable(r, 0x1p-38)) {
+    if (!f32_rounding_stable(r, 38)) {
       const float *x = xs + t * xstride;
       double ser = 0.0;  // the reference's serial order
       for (int k = 0; k < d.H; k++) {
@@ -531,6 +607,7 @@ RV_DEVFN void norm_rows_cta(const MoeDims &d, int T, float *xs, int xstride, con
     }
     s_inv[t] = inv;
   }
+  RV_PHASE_ANY_T0(0, 9);
   cta_sync<NT>();
   for (int t = 0; t < T; t++) {
     float4 *x = (float4 *)(xs + t * xstride);
@@ -664,7 +741,9 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
 // by warp (t*hb + b) of the grid.  Everything the expert kernels need
 // before the exact router chains have run.
 #define RV_SPEC_EPC 4  // experts per k_route_spec CTA
-__global__ void __launch_bounds__(128) k_route_spec(MoeDims d, MoeBufs B) {
+template <int GEO>
+__global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
+  const MoeDims d = geo_dims<GEO>(dd);
   extern __shared__ __align__(16) uint8_t sm[];
   __shared__ float s_inv[RV_SMALL_T];
   __shared__ double s_red[4 * RV_SMALL_T];
@@ -709,8 +788,10 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims d, MoeBufs B) {
   if (xbulk && !mbar_wait_bounded(bar + 1, 0)) return;
   if (rbulk && !mbar_wait_bounded(bar, 0)) return;
   RV_PHASE(0, 2);
+  RV_PHASE_CLK(0, 7);
   norm_rows_cta(d, T, xs, xstride, nw, s_red, s_inv);
   RV_PHASE(0, 3);
+  RV_PHASE_CLK(0, 8);
   if (warp < ne)
     for (int t = 0; t < T; t++) {
       const float2 b = spec_bounds_warp(rows + (size_t)warp * d.H, xs + t * xstride, d.H, lane);
@@ -744,8 +825,9 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims d, MoeBufs B) {
 // completed.  The residual was written by the previous layer, complete
 // before k_route_spec triggered this launch.
 #define RV_CHAIN_THREADS 160
-template <bool CLUSTER>
-__global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims d, MoeBufs B, int CH) {
+template <bool CLUSTER, int GEO>
+__global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, MoeBufs B, int CH) {
+  const MoeDims d = geo_dims<GEO>(dd);
   extern __shared__ __align__(16) uint8_t sm[];
   __shared__ double es[4][256];
   __shared__ int s_cnt[256];
@@ -757,6 +839,9 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims d, Moe
   __shared__ double s_nred[4 * RV_SMALL_T];
   __shared__ __align__(16) float s_lg[CLUSTER ? RV_SPEC_MAX_T * 256 : 1];  // CTA 0: the gathered logits
   __shared__ __align__(8) uint64_t s_gbar;                                  // CTA 0: one arrival per logit
+  __shared__ uint8_t s_cand[CLUSTER ? RV_SPEC_MAX_T * 256 : 1];             // CTA 0: speculated experts per token
+  __shared__ int s_ncand[RV_SPEC_MAX_T];
+  __shared__ uint32_t s_cmask[RV_SPEC_MAX_T * 8];
   __shared__ int s_last;
   RV_PHASE(5, 0);
   const int T = B.T, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -779,19 +864,26 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims d, Moe
   if (warp == 4) {
     pdl_wait();
     pdl_trigger();
+    if (CLUSTER && lead) {
+      // While the chains run: the speculated experts of every token, so
+      // the routing below ranks only those (named barrier 2 hands them over).
+      spec_candidates_warp(d.E, d.K, T, B.spec, s_cand, s_ncand, s_cmask, lane);
+      __syncwarp();
+      asm volatile("bar.arrive 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");
+    }
     return;
   }
-  if (tid == 0) {
-    if (rbulk) {
-      mbar_arrive_expect_tx(bar, (uint32_t)(ne * d.H * 4));
-      for (int r = 0; r < ne; r++)
-        bulk_g2s(rows + (size_t)r * xstride, B.router + (size_t)(ef + r) * d.H, (uint32_t)(d.H * 4), bar);
-    }
+  if (tid == 0) {  // the residual and norm weight first: the norm needs them before the chains need the rows
     if (xbulk) {
       mbar_arrive_expect_tx(bar + 1, (uint32_t)((T + 1) * d.H * 4));
       for (int t = 0; t < T; t++)
         bulk_g2s(xs + (size_t)t * xstride, B.residual + (size_t)t * d.H, (uint32_t)(d.H * 4), bar + 1);
       bulk_g2s(nw, B.ffn_norm, (uint32_t)(d.H * 4), bar + 1);
+    }
+    if (rbulk) {
+      mbar_arrive_expect_tx(bar, (uint32_t)(ne * d.H * 4));
+      for (int r = 0; r < ne; r++)
+        bulk_g2s(rows + (size_t)r * xstride, B.router + (size_t)(ef + r) * d.H, (uint32_t)(d.H * 4), bar);
     }
   }
   if (!rbulk)
@@ -803,25 +895,32 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims d, Moe
     for (int k = tid; k < d.H; k += 128) nw[k] = B.ffn_norm[k];
   }
   cta_sync<128>();
+  // Every compute thread takes the same exit, so no named barrier below
+  // is left waiting for a thread that returned.
   bool ok = true;
   if (xbulk) ok = mbar_wait_bounded(bar + 1, 0);
   RV_PHASE(5, 1);
-  if (!ok) return;
+  if (!cta_sync_and<128>(ok)) return;
   norm_rows_cta<128>(d, T, xs, xstride, nw, s_nred, s_inv);
   if (rbulk) ok = mbar_wait_bounded(bar, 0);
   RV_PHASE(5, 2);
-  if (!ok) return;
+  if (!cta_sync_and<128>(ok)) return;
+  float lg = 0.0f;
+  int e_mine = -1, t_mine = 0;
   if (tid < T * CH) {
     const int t = tid / CH, el = tid % CH;
     if (el < ne) {
-      const int e = ef + el;
-      const float lg = serial_dot_f32((const float4 *)(rows + (size_t)el * xstride),
-                                      (const float4 *)(xs + (size_t)t * xstride), d.H / 4);
-      B.logits[(size_t)t * d.E + e] = lg;
-      if constexpr (CLUSTER) {
-        st_cluster_f32(dsmem_addr(&s_lg[t * d.E + e], 0), lg);
-        mbar_arrive_cluster(dsmem_addr(&s_gbar, 0));
-      }
+      e_mine = ef + el;
+      t_mine = t;
+      lg = serial_dot_f32((const float4 *)(rows + (size_t)el * xstride), (const float4 *)(xs + (size_t)t * xstride),
+                          d.H / 4);
+    }
+  }
+  if (e_mine >= 0) {
+    B.logits[(size_t)t_mine * d.E + e_mine] = lg;
+    if constexpr (CLUSTER) {
+      st_cluster_f32(dsmem_addr(&s_lg[t_mine * d.E + e_mine], 0), lg);
+      mbar_arrive_cluster(dsmem_addr(&s_gbar, 0));
     }
   }
   RV_PHASE(5, 3);
@@ -829,7 +928,7 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims d, Moe
   if constexpr (CLUSTER) {
     if (!lead) return;
     ok = mbar_wait_cluster_bounded(&s_gbar, 0);
-    if (!ok) return;
+    if (!cta_sync_and<128>(ok)) return;
     lgs = s_lg;
   } else {
     __threadfence();
@@ -846,10 +945,16 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims d, Moe
   }
   RV_PHASE(5, 4);
   for (int e = tid; e < 256; e += 128) s_cnt[e] = 0;
-  cta_sync<128>();
+  if constexpr (CLUSTER) asm volatile("bar.sync 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");
+  else cta_sync<128>();
   if (T <= 2) {
-    for (int t = 0; t < T; t++)
-      route_token_block<128>(d, B, t, lgs + (size_t)t * d.E, es[0], s_ps, s_sel, s_red, s_cnt, s_ids);
+    for (int t = 0; t < T; t++) {
+      if constexpr (CLUSTER)
+        route_token_block<128>(d, B, t, lgs + (size_t)t * d.E, es[0], s_ps, s_sel, s_red, s_cnt, s_ids,
+                               s_cand + t * 256, s_ncand[t], s_cmask + t * 8);
+      else
+        route_token_block<128>(d, B, t, lgs + (size_t)t * d.E, es[0], s_ps, s_sel, s_red, s_cnt, s_ids);
+    }
   } else {
     for (int t = warp; t < T; t += 4) route_token_warp(d, B, t, lgs + (size_t)t * d.E, lane, es[warp], s_cnt);
   }
@@ -1075,8 +1180,9 @@ RV_DEVFN bool gate_up_unit(const MoeDims &d, const MoeBufs &B, const MoeWeights 
 // programmatic dependent of the routing kernel) or from the speculated
 // pairs (SPEC true: every CTA rebuilds them from the logit bounds and
 // strides over the units).
-template <int FMT, int G, int NBG, int R, bool SPEC>
-__global__ void __launch_bounds__(2 * R * G, 4) k_gate_up(MoeDims d, MoeBufs B, MoeWeights W) {
+template <int FMT, int G, int NBG, int R, bool SPEC, int GEO>
+__global__ void __launch_bounds__(2 * R * G, 4) k_gate_up(MoeDims dd, MoeBufs B, MoeWeights W) {
+  const MoeDims d = geo_dims<GEO>(dd);
   extern __shared__ __align__(16) uint8_t sm[];
   RV_PHASE(1, 0);
   const int tile = blockIdx.y;
@@ -1127,8 +1233,9 @@ __global__ void __launch_bounds__(2 * R * G, 4) k_gate_up(MoeDims d, MoeBufs B, 
 // stored.  With COMBINE, the last unit to finish a row tile also performs
 // the fixed top-k-order reduction and residual add for those rows of every
 // token (forward.rs:2744-2753); otherwise k_combine does it.
-template <int FMT, int G, int NBG, int ROWS, bool COMBINE, bool SPEC>
-__global__ void __launch_bounds__(32, 16) k_down(MoeDims d, MoeBufs B, MoeWeights W) {
+template <int FMT, int G, int NBG, int ROWS, bool COMBINE, bool SPEC, int GEO>
+__global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeights W) {
+  const MoeDims d = geo_dims<GEO>(dd);
   extern __shared__ __align__(16) uint8_t sm[];
   constexpr int MT = RV_MOE_MT;
   static_assert(ROWS * G <= 32, "one warp per CTA");

@@ -49,34 +49,44 @@ RV_DEVFN uint32_t spec_key(float f) {
 RV_DEVFN float spec_unkey(uint32_t k) { return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k); }
 
 // The interval [lo, hi] holding the serial chain acc = acc + row[k]*x[k]
-// (k = 0..H-1, f32, no FMA), from the f64 sums of the same f32 products,
-// by one warp.  Lane l owns the c = H/32 elements from B = l*c on and
-// bounds their share of sum_k |S_k| by c*|S_B| + sum_j (c - j)*|p_{B+j}|
-// (|S_{B+j}| <= |S_B| + |p_B| + ... + |p_{B+j}|), so one pass over the
-// products and one scan of the lane sums suffice.  Lane l visits its float4
-// groups from a rotation by l, which keeps the shared-memory reads free of
-// bank conflicts.  The result is valid in lane 0; the pair is (NaN, NaN)
-// when a product or the bound is not finite or too large for the chain to
-// stay finite.
+// (k = 0..H-1, f32, no FMA), by one warp.  Lane l owns the c = H/32
+// elements from B = l*c on.  Its products are summed in f32, four
+// interleaved running sums (element 4q+i into sum i) combined pairwise, so
+// each product passes through at most c/4 + 2 roundings: the lane sum is
+// within gamma = (c/4+2)u/(1-(c/4+2)u) * sum|p| of exact (u = 2^-24).  The
+// lane's share of sum_k |S_k| is at most c*|S_B| + sum_j (c - j)*|p_{B+j}|
+// (|S_{B+j}| <= |S_B| + |p_B| + ... + |p_{B+j}|); that weighted sum and
+// sum |p| are accumulated rounding upward, so they bound their exact
+// values from above.  The lane sums are then scanned exactly enough in
+// f64, and
+//   |chain - A| <= u' * (Spre + H*(gamma + g)*Sa) + (gamma + g)*Sa,
+// with u' = u/(1 - H u), g = 2^-39 covering the f64 steps, Spre the bound
+// on sum_k |S_k| from the scanned lane starts, Sa = sum |p|.  Lane l visits
+// its float4 groups from a rotation by l, which keeps the shared-memory
+// reads free of bank conflicts.  The result is valid in lane 0; the pair
+// is (NaN, NaN) when a product or the bound is not finite or too large for
+// the chain to stay finite.
 RV_DEVFN float2 spec_bounds_warp(const float *row, const float *x, int H, int lane) {
   const int c = H >> 5, nq = c >> 2;  // H is a multiple of 256: nq >= 2
   const float4 *r4 = (const float4 *)(row + lane * c), *x4 = (const float4 *)(x + lane * c);
-  double s[4] = {0.0, 0.0, 0.0, 0.0}, sa[4] = {0.0, 0.0, 0.0, 0.0}, ws[4] = {0.0, 0.0, 0.0, 0.0};
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, ws[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int qq = lane % nq;
   for (int q = 0; q < nq; q++) {
-    const int qq = (q + lane) % nq;
     const float4 a = r4[qq], b = x4[qq];
     const float pf[4] = {__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w)};
+    const float w0 = (float)(c - 4 * qq);  // exact: c <= 128
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const double p = (double)pf[i], ap = fabs(p);
-      s[i] = __dadd_rn(s[i], p);
-      sa[i] = __dadd_rn(sa[i], ap);
-      ws[i] = __fma_rn((double)(c - 4 * qq - i), ap, ws[i]);
+      const float ap = fabsf(pf[i]);
+      s[i] = __fadd_rn(s[i], pf[i]);
+      sa[i] = __fadd_ru(sa[i], ap);
+      ws[i] = __fmaf_ru(w0 - (float)i, ap, ws[i]);
     }
+    qq = qq + 1 == nq ? 0 : qq + 1;
   }
-  const double sum = __dadd_rn(__dadd_rn(s[0], s[1]), __dadd_rn(s[2], s[3]));
-  double sabs = __dadd_rn(__dadd_rn(sa[0], sa[1]), __dadd_rn(sa[2], sa[3]));
-  const double wsum = __dadd_rn(__dadd_rn(ws[0], ws[1]), __dadd_rn(ws[2], ws[3]));
+  const double sum = (double)__fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3]));
+  double sabs = (double)__fadd_ru(__fadd_ru(sa[0], sa[1]), __fadd_ru(sa[2], sa[3]));
+  const double wsum = (double)__fadd_ru(__fadd_ru(ws[0], ws[1]), __fadd_ru(ws[2], ws[3]));
   double inc = sum;  // inclusive scan of the lane sums
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -92,10 +102,13 @@ RV_DEVFN float2 spec_bounds_warp(const float *row, const float *x, int H, int la
   }
   float2 out = make_float2(0.0f, 0.0f);
   if (lane == 0) {
-    // Every f64 sum above has fewer than 2^13 roundings of magnitude at
-    // most 2^-53 * sabs each: g = 2^-39 bounds them with room to spare.
-    const double g = 0x1p-39, u = 0x1p-24 / (1.0 - (double)H * 0x1p-24);
-    const double bd = (u * (spre + (double)H * g * sabs) + g * sabs) * (1.0 + g) * (1.0 + 0x1p-30);
+    // gamma and u' through 1/(1 - x) <= 1 + 2x (x <= 1/2): upper bounds
+    // without a division.
+    const double u = 0x1p-24, g = 0x1p-39;
+    const double gam = (double)(nq + 2) * u * (1.0 + 2.0 * (double)(nq + 2) * u);
+    const double up = u * (1.0 + 2.0 * (double)H * u);
+    const double sa = sabs * (1.0 + g);
+    const double bd = (up * (spre * (1.0 + g) + (double)H * (gam + g) * sa) + (gam + g) * sa) * (1.0 + 0x1p-30);
     if (isfinite(sabs) && sabs < 0x1p100 && isfinite(bd)) {
       out.x = __double2float_rd(__dsub_rd(A, bd));
       out.y = __double2float_ru(__dadd_ru(A, bd));
@@ -123,6 +136,49 @@ RV_DEVFN int spec_nth_bit(uint32_t m, int j) {
   return __ffs(m) - 1;
 }
 
+// Token t's speculated experts, by one warp: lane l holds experts l + 32j.
+// Loads the token's E bounds once (b), finds the threshold (the K-th
+// largest lower bound, or lower) and returns the lane's membership bits
+// (bit j: expert l + 32j is speculated).
+RV_DEVFN uint32_t spec_token_bits(int E, int K, const float2 *spec_t, int lane) {
+  float2 b[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int e = lane + 32 * j;
+    b[j] = e < E ? spec_t[e] : make_float2(-INFINITY, -INFINITY);
+  }
+  uint32_t key[8];
+  bool bad = false;
+  float mhi = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    key[j] = lane + 32 * j < E ? spec_key(b[j].x) : 0u;  // 0 sorts below every float
+    bad |= isnan(b[j].x) || isnan(b[j].y);
+    mhi = fmaxf(mhi, b[j].y);
+  }
+  bad = __any_sync(RV_FULL, bad);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mhi = fmaxf(mhi, __shfl_xor_sync(RV_FULL, mhi, o));
+  // K rounds, each removing every copy of the current maximum: with tied
+  // keys this reaches a lower key than the K-th largest with multiplicity,
+  // i.e. a lower threshold and a larger (still safe) set.
+  uint32_t m = 0u;
+  for (int k = 0; k < K; k++) {
+    const uint32_t lm =
+        max(max(max(key[0], key[1]), max(key[2], key[3])), max(max(key[4], key[5]), max(key[6], key[7])));
+    m = __reduce_max_sync(RV_FULL, lm);
+#pragma unroll
+    for (int j = 0; j < 8; j++) key[j] = key[j] == m ? 0u : key[j];
+  }
+  const float thr = spec_unkey(m);
+  const bool all = bad || m == 0u || !(__fsub_rd(thr, mhi) >= -RV_SPEC_UNDERFLOW);
+  uint32_t bits = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+    if (lane + 32 * j < E && (all || __fadd_ru(b[j].y, RV_SPEC_DELTA) >= thr)) bits |= 1u << j;
+  return bits;
+}
+
 // Any block size that is a multiple of 32 (all threads call); E <= 256,
 // K <= 16, T <= 8.  spec: [T][E] (lo, hi) written by an earlier kernel,
 // read once (warp w handles tokens w, w + warps, ...).
@@ -131,84 +187,58 @@ RV_DEVFN void spec_build(int E, int K, int T, const float2 *spec, SpecSmem &ss) 
   for (int e = tid; e < 256; e += blockDim.x) ss.mask[e] = 0u;
   __syncthreads();
   for (int t = warp; t < T; t += nw) {
-    float2 b[8];
+    const uint32_t bits = spec_token_bits(E, K, spec + (size_t)t * E, lane);
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const int e = lane + 32 * j;
-      b[j] = e < E ? spec[(size_t)t * E + e] : make_float2(-INFINITY, -INFINITY);
-    }
-    uint32_t key[8];
-    bool bad = false;
-    float mhi = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      key[j] = lane + 32 * j < E ? spec_key(b[j].x) : 0u;  // 0 sorts below every float
-      bad |= isnan(b[j].x) || isnan(b[j].y);
-      mhi = fmaxf(mhi, b[j].y);
-    }
-    bad = __any_sync(RV_FULL, bad);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mhi = fmaxf(mhi, __shfl_xor_sync(RV_FULL, mhi, o));
-    uint32_t m = 0u;
-    for (int k = 0; k < K; k++) {  // remove the largest key K times
-      uint32_t lm = key[0];
-#pragma unroll
-      for (int j = 1; j < 8; j++) lm = max(lm, key[j]);
-      m = __reduce_max_sync(RV_FULL, lm);
-      const unsigned win = __ballot_sync(RV_FULL, lm == m);
-      if (lane == __ffs(win) - 1) {
-        bool done = false;
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-          if (!done && key[j] == m) {
-            key[j] = 0u;
-            done = true;
-          }
-      }
-    }
-    const float thr = spec_unkey(m);
-    const bool all = bad || !(__fsub_rd(thr, mhi) >= -RV_SPEC_UNDERFLOW);
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const int e = lane + 32 * j;
-      if (e < E && (all || __fadd_ru(b[j].y, RV_SPEC_DELTA) >= thr)) atomicOr(&ss.mask[e], 1u << t);
-    }
+    for (int j = 0; j < 8; j++)
+      if ((bits >> j) & 1u) atomicOr(&ss.mask[lane + 32 * j], 1u << t);
   }
   __syncthreads();
-  if (warp == 0) {
-    int c[8], sc = 0, su = 0;
+  if (warp == 0) {  // experts in rows of 32: unit ranks by ballot, positions by a scan
+    int pbase = 0, ubase = 0;
+    for (int r = 0; r * 32 < E; r++) {
+      const int e = r * 32 + lane;
+      const int cnt = e < E ? __popc(ss.mask[e]) : 0;
+      const unsigned has = __ballot_sync(RV_FULL, cnt > 0);
+      int inc = cnt;
+      if (T > 1) {
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const int e = lane * 8 + i;
-      c[i] = e < E ? __popc(ss.mask[e]) : 0;
-      sc += c[i];
-      su += c[i] > 0;
-    }
-    int xc = sc, xu = su;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int yc = __shfl_up_sync(RV_FULL, xc, o), yu = __shfl_up_sync(RV_FULL, xu, o);
-      if (lane >= o) {
-        xc += yc;
-        xu += yu;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(RV_FULL, inc, o);
+          if (lane >= o) inc += y;
+        }
+      } else {
+        inc = __popc(has & (0xffffffffu >> (31 - lane)));
       }
-    }
-    const int tc = __shfl_sync(RV_FULL, xc, 31), tu = __shfl_sync(RV_FULL, xu, 31);
-    xc -= sc;
-    xu -= su;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const int e = lane * 8 + i;
       if (e < E) {
-        ss.start[e] = (uint16_t)xc;
-        if (c[i]) ss.uexp[xu++] = (uint8_t)e;
+        ss.start[e] = (uint16_t)(pbase + inc - cnt);
+        if (cnt) ss.uexp[ubase + __popc(has & ((1u << lane) - 1u))] = (uint8_t)e;
       }
-      xc += c[i];
+      pbase += __shfl_sync(RV_FULL, inc, 31);
+      ubase += __popc(has);
     }
     if (lane == 0) {
-      ss.start[E] = (uint16_t)tc;
-      ss.n_units = tu;
+      ss.start[E] = (uint16_t)pbase;
+      ss.n_units = ubase;
     }
   }
   __syncthreads();
+}
+
+// The speculated experts of every token, by one warp, as ascending lists
+// cand[t * 256 + i], i < ncand[t], and as bit sets cmask[t * 8 + w] (bit
+// b: expert 32w + b).  Only listed experts can be in token t's top-k.
+RV_DEVFN void spec_candidates_warp(int E, int K, int T, const float2 *spec, uint8_t *cand, int *ncand,
+                                   uint32_t *cmask, int lane) {
+  for (int t = 0; t < T; t++) {
+    const uint32_t bits = spec_token_bits(E, K, spec + (size_t)t * E, lane);
+    int n = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const unsigned in = __ballot_sync(RV_FULL, (bits >> j) & 1u);
+      if ((bits >> j) & 1u) cand[t * 256 + n + __popc(in & ((1u << lane) - 1u))] = (uint8_t)(lane + 32 * j);
+      if (lane == 0) cmask[t * 8 + j] = in;
+      n += __popc(in);
+    }
+    if (lane == 0) ncand[t] = n;
+  }
 }

@@ -48,6 +48,8 @@ def _print_phases(name, b, t0, labels):
     used = b[:, 0] != 0
     print(f"{name}: {int(used.sum())} CTAs")
     for i, lab in enumerate(labels):
+        if not lab:
+            continue
         v = b[used, i]
         v = v[(v != 0) & (v >= t0) & (v < t0 + 10**7)]
         if v.size:
@@ -91,12 +93,17 @@ def decode(n_layers: int = 4) -> None:
     t0 = first[first != 0].min()
     if os.environ.get("RV_DECODE_SPEC", "1") != "0":
         _print_phases("route (norm, bounds)", bufs[0], t0, ["start", "pdl_wait", "residual", "norm", "bounds",
-                                                            "q8k"])
+                                                            "q8k", "norm:squares", "", "", "norm:inv"])
         _print_phases("exact chains", bufs[5], t0, ["start", "pdl_wait", "rows", "chain done", "LAST:start",
                                                     "LAST:routed", "LAST:index"])
     else:
         _print_phases("route", bufs[0], t0, ["start", "pdl_wait", "residual", "norm", "rows", "chain done",
                                              "LAST:start", "LAST:routed", "LAST:index"])
+    b0 = bufs[0]
+    used = (b0[:, 7] != 0) & (b0[:, 8] != 0) & (b0[:, 3] > b0[:, 2])
+    if used.any():
+        mhz = (b0[used, 8] - b0[used, 7]) / (b0[used, 3] - b0[used, 2]) * 1e3
+        print(f"   SM clock during the norm (clock64 / globaltimer): p50 {np.median(mhz):.0f} MHz")
     _print_phases("gate_up", bufs[1], t0, ["start", "unit", "data", "compute", "LAST:quant"])
     _print_phases("down", bufs[2], t0, ["start", "weights issued", "pdl_wait", "data", "compute", "LAST:combine"])
     tail = bufs[3][0]
