@@ -349,7 +349,8 @@ def run_cuda(args):
             "e2e": {"value": round(e2e_tok_s, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": n_layers * H * 4, "d2h_bytes_per_step": n_layers * H * 4,
                     "path": "rv_moe_forward_host per layer (pinned host residual in, result out)"},
-            "gpu_launches": args.steps * n_layers * 7,
+            # per layer: k_route_spec, k_route_chain, k_gate_up, k_down (the speculative pipeline)
+            "gpu_launches": args.steps * n_layers * 4,
             "clocks": clk,
             "cpu_baseline": cpu,
         }

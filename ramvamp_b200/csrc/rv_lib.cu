@@ -16,6 +16,7 @@
 #include "rv_moe.cuh"
 #include "rv_tc.cuh"
 #include "rv_ep.cuh"
+#include "rv_fused.cuh"
 
 #include "_gen/expf_exceptions.inc"
 
@@ -580,7 +581,8 @@ struct rv_moe {
   void *arena;
   float *dres;  // [max_tokens][H] device residual of rv_moe_forward_host
   int last_T = 0;
-  bool spec = true;  // speculative expert dispatch for decode (RV_DECODE_SPEC=0 turns it off)
+  bool spec = true;   // speculative expert dispatch for decode (RV_DECODE_SPEC=0 turns it off)
+  bool fused = false;  // one-token decode in one cooperative kernel (RV_DECODE_FUSED=1 turns it on)
   std::vector<cudaEvent_t> prof;  // 5 events per set
   size_t prof_next = 0;
 };
@@ -674,6 +676,7 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
   const size_t PS = std::max(P, std::min<size_t>(T, RV_SPEC_MAX_T) * (size_t)d.E);
   const size_t units_cap = std::max<size_t>((size_t)m->max_units, (size_t)d.E);
   if (const char *v = getenv("RV_DECODE_SPEC")) m->spec = atoi(v) != 0;
+  if (const char *v = getenv("RV_DECODE_FUSED")) m->fused = atoi(v) != 0;
   const size_t max_tc = std::min<size_t>((size_t)d.E, P) + P / RV_TC_NT + 1;
   const size_t padded_rows = (P + 16 * (size_t)d.E + 16 + 15) & ~(size_t)15;  // every expert's rows rounded up to 16
   // One arena for every scratch buffer the forward touches.
@@ -697,6 +700,7 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
       {16, (void **)&B.route_cnt},
       {((size_t)d.H / 8 + 1) * 4, (void **)&B.down_cnt},
       {std::min<size_t>(T, RV_SPEC_MAX_T) * (size_t)d.E * 8, (void **)&B.spec},
+      {(size_t)RV_FZ_INTS * 4, (void **)&B.fz},
       {T * d.H * 4, (void **)&m->dres},
       {padded_rows * d.H * 2, (void **)&B.xq},
       {padded_rows * d.hb * 32, (void **)&B.xm},
@@ -771,7 +775,14 @@ static bool geo_qwen3(const MoeDims &d) { return d.H == 2048 && d.M == 768 && d.
 // cluster of all the CTAs when there are at most 8 of them.  Each CTA takes
 // a whole SM's shared memory, so no other kernel's CTA shares an SM with a
 // serial chain.
-static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, cudaStream_t s) {
+template <bool FUSED>
+static void (*route_chain_kernel(bool cluster, bool q3))(MoeDims, MoeBufs, int) {
+  if (cluster) return q3 ? k_route_chain<true, RV_GEO_QWEN3, FUSED> : k_route_chain<true, 0, FUSED>;
+  return q3 ? k_route_chain<false, RV_GEO_QWEN3, FUSED> : k_route_chain<false, 0, FUSED>;
+}
+
+// fused: the next kernel is k_decode_fused (see k_route_chain).
+static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, bool fused, cudaStream_t s) {
   const size_t xrow = (size_t)(d.H + 4) * 4;
   const size_t fixed = 16 + (size_t)T * xrow + (size_t)d.H * 4;
   int ch = 0, grid = 0;
@@ -780,8 +791,8 @@ static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, cudaStr
   size_t room = 0;
   for (int v = 0; v < 2 && !kern; v++) {  // the cluster variant first
     const bool q3 = geo_qwen3(d);
-    void (*k)(MoeDims, MoeBufs, int) = v == 0 ? (q3 ? k_route_chain<true, RV_GEO_QWEN3> : k_route_chain<true, 0>)
-                                              : (q3 ? k_route_chain<false, RV_GEO_QWEN3> : k_route_chain<false, 0>);
+    void (*k)(MoeDims, MoeBufs, int) =
+        fused ? route_chain_kernel<true>(v == 0, q3) : route_chain_kernel<false>(v == 0, q3);
     cudaFuncAttributes fa;
     RV_CUDA(cudaFuncGetAttributes(&fa, k));
     room = (size_t)RV_SMEM_PER_CTA - fa.sharedSizeBytes;
@@ -1043,6 +1054,64 @@ static int check_engine_layer(const rv_moe *m, const rv_expert_table *table, uin
   return RV_OK;
 }
 
+// One-token decode through k_route_chain + k_decode_fused (the Qwen3
+// geometry with Q4_K gate/up and Q4_K or Q6_K down).  Returns 1 when this
+// layer does not qualify (the caller takes the multi-kernel path), 0 when
+// launched, or -status.
+template <int FGU, int FDN>
+static int launch_fused_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
+  void (*kern)(MoeDims, MoeBufs, MoeWeights) = k_decode_fused<FGU, FDN, RV_GEO_QWEN3>;
+  const FusedLayout FL = fused_layout<FGU, FDN>(d, W.gu_row_bytes, W.down_row_bytes);
+  static int checked[3][3];  // 1: fits, -1: does not
+  int &ck = checked[FGU][FDN];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -RV_ERR_CUDA;
+  const int units = d.K;  // one token: its top-k units, the grids stride over more
+  const int nb = (d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC;
+  const int ncta = std::max(nb, std::max(units * (d.M / RV_FUSED_GU_R), units * (d.H / RV_FUSED_DN_ROWS) / 4));
+  if (ck == 0) {
+    ck = -1;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FL.total) == cudaSuccess) {
+      int per_sm = 0, sms = 0;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, RV_FUSED_THREADS, FL.total);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      // Room beside the chain kernel's CTAs (one per SM, at most 8).
+      if (per_sm > 0 && (long)per_sm * (sms - 8) >= ncta) ck = 1;
+    }
+    cudaGetLastError();
+  }
+  if (ck < 0) return 1;
+  int rc = launch_route_chain(d, B, 1, true, s);
+  if (rc) return -rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ncta);
+  cfg.blockDim = dim3(RV_FUSED_THREADS);
+  cfg.dynamicSmemBytes = FL.total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, d, B, W);
+  if (e != cudaSuccess) {
+    rv_set_error(RV_ERR_CUDA, "fused decode launch: %s", cudaGetErrorString(e));
+    return -RV_ERR_CUDA;
+  }
+  return 0;
+}
+
+static int launch_decode_fused(rv_moe *m, const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
+                               const rv_layer_layout &L, cudaStream_t s) {
+  (void)m;
+  if (!geo_qwen3(d) || L.gate_format != RV_Q4_K || L.up_format != RV_Q4_K) return 1;
+  if (L.down_format == RV_Q6_K) return launch_fused_t<RV_Q4_K, RV_Q6_K>(d, B, W, s);
+  if (L.down_format == RV_Q4_K) return launch_fused_t<RV_Q4_K, RV_Q4_K>(d, B, W, s);
+  return 1;
+}
+
 extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t layer,
                               const float *ffn_norm, const float *router, float *residual,
                               size_t n_tokens, uint32_t *topk_ids, float *topk_weights,
@@ -1078,6 +1147,20 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   if ((rc = prof_record(ev, 0, evflags, s))) return rc;
   B.ms = T < RV_MOE_MT ? T : RV_MOE_MT;
   int spec_units = 0;
+  int frc = 1;
+  if (!(flags & RV_MOE_TENSOR) && T == 1 && m->spec && m->fused &&
+      (frc = launch_decode_fused(m, d, B, W, L, s)) <= 0) {
+    // one token: the exact chains, then everything else in one cooperative kernel
+    if (frc < 0) return -frc;
+    if ((rc = prof_record(ev, 1, evflags, s))) return rc;
+    if ((rc = prof_record(ev, 2, evflags, s))) return rc;
+    if ((rc = prof_record(ev, 3, evflags, s))) return rc;
+    if ((rc = prof_record(ev, 4, evflags, s))) return rc;
+    m->last_T = T;
+    if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+    if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
+    return RV_OK;
+  }
   if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T && m->spec) {
     // decode, speculative: norm, Q8_K and logit bounds; then the exact
     // router chains beside gate/up on the speculated experts; then down
@@ -1088,7 +1171,7 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
     RV_CUDA(launch_pdl(geo_qwen3(d) ? k_route_spec<RV_GEO_QWEN3> : k_route_spec<0>,
                        dim3((unsigned)((d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC)), dim3(128),
                        std::max(rs_need, (size_t)RV_ROUTE_SMEM_ONE_PER_SM), s, d, B));
-    if ((rc = launch_route_chain(d, B, T, s))) return rc;
+    if ((rc = launch_route_chain(d, B, T, false, s))) return rc;
     spec_units = std::min(d.E, T * d.K);
   } else if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch

@@ -54,6 +54,8 @@ struct MoeBufs {
   int *route_cnt;          // [1] CTAs done in k_route_decode, zero between calls
   int *down_cnt;           // [H/8] units done per down row tile, zero between calls
   float2 *spec;            // [T][E] (lo, hi) bounds of the router logits (speculative decode)
+  int *fz;                 // fused decode kernel counters, one per 128-byte line (RV_FZ_*); zero
+                           // between calls
   int T;
   int ms;                  // activation slots per CTA pass: min(T, RV_MOE_MT)
   int max_units;
@@ -741,15 +743,16 @@ __global__ void __launch_bounds__(128) k_route_decode(MoeDims d, MoeBufs B) {
 // by warp (t*hb + b) of the grid.  Everything the expert kernels need
 // before the exact router chains have run.
 #define RV_SPEC_EPC 4  // experts per k_route_spec CTA
-template <int GEO>
-__global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
-  const MoeDims d = geo_dims<GEO>(dd);
-  extern __shared__ __align__(16) uint8_t sm[];
+// The body of k_route_spec for CTA `cta` of `ncta` (128 threads, shared
+// memory `sm`).  PDL: wait for the previous kernel before reading the
+// residual and then let the next kernel launch (a kernel whose residual is
+// already final passes false).  Returns false when a copy timed out.
+template <bool PDL>
+RV_DEVFN bool route_spec_cta(const MoeDims &d, const MoeBufs &B, uint8_t *sm, int cta, int ncta) {
   __shared__ float s_inv[RV_SMALL_T];
   __shared__ double s_red[4 * RV_SMALL_T];
-  RV_PHASE(0, 0);
   const int T = B.T, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = blockIdx.x * RV_SPEC_EPC, ne = min(RV_SPEC_EPC, d.E - e0);
+  const int e0 = cta * RV_SPEC_EPC, ne = min(RV_SPEC_EPC, d.E - e0);
   const int xstride = d.H + 4;
   uint64_t *bar = (uint64_t *)sm;                // [2]: router rows + norm weight, residual rows
   float *rows = (float *)(sm + 16);              // [4][H]
@@ -771,10 +774,12 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
     for (int k = threadIdx.x; k < ne * d.H; k += blockDim.x) rows[k] = rsrc[k];
     for (int k = threadIdx.x; k < d.H; k += blockDim.x) nw[k] = B.ffn_norm[k];
   }
-  pdl_wait();  // the residual is the previous kernel's output
-  // The exact-chain kernel reads the residual without waiting: it may
-  // launch only now.
-  pdl_trigger();
+  if constexpr (PDL) {
+    pdl_wait();  // the residual is the previous kernel's output
+    // The exact-chain kernel reads the residual without waiting: it may
+    // launch only now.
+    pdl_trigger();
+  }
   RV_PHASE(0, 1);
   if (threadIdx.x == 0 && xbulk) {
     mbar_arrive_expect_tx(bar + 1, (uint32_t)(T * d.H * 4));
@@ -785,8 +790,10 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
     for (int t = 0; t < T; t++)
       for (int k = threadIdx.x; k < d.H; k += blockDim.x) xs[t * xstride + k] = B.residual[(size_t)t * d.H + k];
   __syncthreads();
-  if (xbulk && !mbar_wait_bounded(bar + 1, 0)) return;
-  if (rbulk && !mbar_wait_bounded(bar, 0)) return;
+  bool ok = true;
+  if (xbulk) ok = mbar_wait_bounded(bar + 1, 0);
+  if (rbulk) ok = mbar_wait_bounded(bar, 0) && ok;
+  if (!__syncthreads_and(ok)) return false;
   RV_PHASE(0, 2);
   RV_PHASE_CLK(0, 7);
   norm_rows_cta(d, T, xs, xstride, nw, s_red, s_inv);
@@ -798,7 +805,7 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
       if (lane == 0) B.spec[(size_t)t * d.E + e0 + warp] = b;
     }
   RV_PHASE(0, 4);
-  const int gw = blockIdx.x * 4 + warp, nwg = gridDim.x * 4;
+  const int gw = cta * 4 + warp, nwg = ncta * 4;
   for (int tb = gw; tb < T * d.hb; tb += nwg) {
     const int t = tb / d.hb, b = tb % d.hb;
     float v[8];
@@ -809,6 +816,15 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
     for (int e = 0; e < 8; e++) B.normed[(size_t)t * d.H + b * 256 + 8 * lane + e] = v[e];
   }
   RV_PHASE(0, 5);
+  return true;
+}
+
+template <int GEO>
+__global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
+  const MoeDims d = geo_dims<GEO>(dd);
+  extern __shared__ __align__(16) uint8_t sm[];
+  RV_PHASE(0, 0);
+  route_spec_cta<true>(d, B, sm, blockIdx.x, gridDim.x);
 }
 
 // k_route_chain: the exact router chains, CH experts per CTA (grid =
@@ -825,7 +841,11 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
 // completed.  The residual was written by the previous layer, complete
 // before k_route_spec triggered this launch.
 #define RV_CHAIN_THREADS 160
-template <bool CLUSTER, int GEO>
+// FUSED: the next kernel is k_decode_fused, which computes the logit bounds
+// itself; this grid then follows the previous layer directly, so its
+// compute warps wait for it before reading the residual, and the routing
+// ranks every expert (the bounds are not written yet).
+template <bool CLUSTER, int GEO, bool FUSED>
 __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, MoeBufs B, int CH) {
   const MoeDims d = geo_dims<GEO>(dd);
   extern __shared__ __align__(16) uint8_t sm[];
@@ -864,7 +884,7 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, Mo
   if (warp == 4) {
     pdl_wait();
     pdl_trigger();
-    if (CLUSTER && lead) {
+    if (CLUSTER && lead && !FUSED) {
       // While the chains run: the speculated experts of every token, so
       // the routing below ranks only those (named barrier 2 hands them over).
       spec_candidates_warp(d.E, d.K, T, B.spec, s_cand, s_ncand, s_cmask, lane);
@@ -873,6 +893,7 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, Mo
     }
     return;
   }
+  if constexpr (FUSED) pdl_wait();  // the residual is the previous kernel's output
   if (tid == 0) {  // the residual and norm weight first: the norm needs them before the chains need the rows
     if (xbulk) {
       mbar_arrive_expect_tx(bar + 1, (uint32_t)((T + 1) * d.H * 4));
@@ -945,11 +966,11 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, Mo
   }
   RV_PHASE(5, 4);
   for (int e = tid; e < 256; e += 128) s_cnt[e] = 0;
-  if constexpr (CLUSTER) asm volatile("bar.sync 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");
+  if constexpr (CLUSTER && !FUSED) asm volatile("bar.sync 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");
   else cta_sync<128>();
   if (T <= 2) {
     for (int t = 0; t < T; t++) {
-      if constexpr (CLUSTER)
+      if constexpr (CLUSTER && !FUSED)
         route_token_block<128>(d, B, t, lgs + (size_t)t * d.E, es[0], s_ps, s_sel, s_red, s_cnt, s_ids,
                                s_cand + t * 256, s_ncand[t], s_cmask + t * 8);
       else
@@ -1068,7 +1089,8 @@ RV_DEVFN uint32_t stage_rows(uint8_t *dst, const uint8_t *src, size_t row_bytes,
 // mbarrier, carried from unit to unit.  Returns false when a wait ran out.
 template <int FMT, int G, int NBG, int R, typename TokOf>
 RV_DEVFN bool gate_up_unit(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, uint8_t *sm, int u, int e,
-                           int p0, int p1, int tile, TokOf tok, uint32_t &phase) {
+                           int p0, int p1, int tile, TokOf tok, uint32_t &phase, int *ready = nullptr,
+                           int ready_stride = 1) {
   constexpr int MT = RV_MOE_MT, RPW = 32 / G, NW = 2 * R * G / 32;
   const int ms = B.ms;
   __shared__ int s_last;
@@ -1172,6 +1194,11 @@ RV_DEVFN bool gate_up_unit(const MoeDims &d, const MoeBufs &B, const MoeWeights 
 #pragma unroll
     for (int k = 0; k < 8; k++) v[k] = __ldcg(src + k);
     q8k_quantize_warp(v, lane, B.acts_moe + (size_t)pos * d.amoe_stride + (size_t)qb * 292);
+  }
+  if (ready) {  // one more 256-row block of this unit's SwiGLU rows is quantized
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(&ready[(size_t)u * ready_stride], 1);
   }
   return true;
 }

@@ -205,8 +205,13 @@ RV_DEVFN float row_dot_split(const uint8_t *wrow, const uint8_t *act_row, const 
 
 // Per-word byte sums of staged activation blocks (Q6_K's -32 offset):
 // asum[b*64 + w] = sum of the four int8 in word w of block b.
-RV_DEVFN void act_word_sums(const uint8_t *act_row, int nb, int *asum) {
-  for (int i = threadIdx.x; i < nb * 64; i += blockDim.x) {
+// Threads t0, t0 + nt, ... of the caller's group (default: the whole block).
+RV_DEVFN void act_word_sums(const uint8_t *act_row, int nb, int *asum, int t0 = -1, int nt = 0) {
+  if (t0 < 0) {
+    t0 = threadIdx.x;
+    nt = blockDim.x;
+  }
+  for (int i = t0; i < nb * 64; i += nt) {
     const int b = i >> 6, w = i & 63;
     asum[i] = __dp4a(*(const int *)(act_row + (size_t)b * 292 + 4 + 4 * w), 0x01010101, 0);
   }
