@@ -85,7 +85,10 @@ __host__ __device__ inline FusedLayout fused_layout(const MoeDims &d, size_t gu_
 // for the unit's positions [p0, p1) (tokens = set bits of msk), into
 // B.staged at the exact pairs.  smw: the warp's shared memory (two
 // mbarriers, then the weight rows, the activations, the Q6_K word sums).
-template <int FMT, int G, int NBG>
+// ACTS_AFTER_WAIT: the activations are the previous kernel's output (copy
+// them after the PDL wait); otherwise they are already final (only the
+// routing read waits).
+template <int FMT, int G, int NBG, bool ACTS_AFTER_WAIT = false>
 RV_DEVFN bool down_tile_warp(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, uint8_t *smw, int e, int p0,
                              int p1, uint32_t msk, int tile, uint32_t *s_pair, uint32_t &wphase, uint32_t &aphase) {
   constexpr int ROWS = RV_FUSED_DN_ROWS, MT = RV_MOE_MT;
@@ -117,17 +120,27 @@ RV_DEVFN bool down_tile_warp(const MoeDims &d, const MoeBufs &B, const MoeWeight
           bulk_g2s(wsm + r * st, dsrc + (size_t)r * W.down_row_bytes, (uint32_t)W.down_row_bytes, bar);
       }
     }
-    if (abulk) {
+    if (abulk && !ACTS_AFTER_WAIT) {
       mbar_arrive_expect_tx(bar + 1, abytes);
       bulk_g2s(asm_, asrc, abytes, bar + 1);
     }
   }
   if (!wbulk)
     for (size_t i = lane; i < wbytes; i += 32) wsm[(i / W.down_row_bytes) * st + i % W.down_row_bytes] = dsrc[i];
-  if (!abulk)
+  if (!abulk && !ACTS_AFTER_WAIT)
     for (uint32_t i = lane; i < abytes; i += 32) asm_[i] = asrc[i];
   // The exact pair of each position (the chain kernel's routing).
   pdl_wait();
+  if constexpr (ACTS_AFTER_WAIT) {
+    if (abulk) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar + 1, abytes);
+        bulk_g2s(asm_, asrc, abytes, bar + 1);
+      }
+    } else {
+      for (uint32_t i = lane; i < abytes; i += 32) asm_[i] = asrc[i];
+    }
+  }
   if (lane < p1 - p0) {
     const int t = spec_nth_bit(msk, lane);
     uint32_t pair = ~0u;
@@ -340,3 +353,4 @@ __global__ void __launch_bounds__(RV_FUSED_THREADS, 4) k_decode_fused(MoeDims dd
     }
   }
 }
+

@@ -101,6 +101,7 @@ static bool g_dev_ready[64];
 // Speculative decode: router rows per exact-chain CTA.  The expert grids
 // cover T*K units (usually all there are); CTAs stride over any more.
 #define RV_CHAIN_EXPERTS 16
+
 #define RV_SMEM_PER_CTA (227u * 1024u)  // the per-CTA shared-memory limit of sm_100
 
 static int ensure_device(int dev) {
@@ -698,7 +699,7 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
       {P * d.H * 4, (void **)&B.staged},
       {units_cap * d.mb * 4, (void **)&B.tile_cnt},
       {16, (void **)&B.route_cnt},
-      {((size_t)d.H / 8 + 1) * 4, (void **)&B.down_cnt},
+      {((size_t)d.H / 4 + 1) * 4, (void **)&B.down_cnt},  // one per down row tile (>= 4 rows)
       {std::min<size_t>(T, RV_SPEC_MAX_T) * (size_t)d.E * 8, (void **)&B.spec},
       {(size_t)RV_FZ_INTS * 4, (void **)&B.fz},
       {T * d.H * 4, (void **)&m->dres},
