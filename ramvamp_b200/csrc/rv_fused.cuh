@@ -53,11 +53,6 @@ RV_DEVFN bool wait_count_geq(const int *p, int target) {
   }
 }
 
-// L2 prefetch of `bytes` (multiple of 16, 16-byte aligned) at src.
-RV_DEVFN void prefetch_l2(const void *src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // Shared memory of the fused kernel: the largest of the three phases.
 struct FusedLayout {
   size_t a, b, c_warp, total;

@@ -777,22 +777,23 @@ static bool geo_qwen3(const MoeDims &d) { return d.H == 2048 && d.M == 768 && d.
 // a whole SM's shared memory, so no other kernel's CTA shares an SM with a
 // serial chain.
 template <bool FUSED>
-static void (*route_chain_kernel(bool cluster, bool q3))(MoeDims, MoeBufs, int) {
+static void (*route_chain_kernel(bool cluster, bool q3))(MoeDims, MoeBufs, int, MoeWeights) {
   if (cluster) return q3 ? k_route_chain<true, RV_GEO_QWEN3, FUSED> : k_route_chain<true, 0, FUSED>;
   return q3 ? k_route_chain<false, RV_GEO_QWEN3, FUSED> : k_route_chain<false, 0, FUSED>;
 }
 
 // fused: the next kernel is k_decode_fused (see k_route_chain).
-static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, bool fused, cudaStream_t s) {
+static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, bool fused, const MoeWeights &W,
+                              cudaStream_t s) {
   const size_t xrow = (size_t)(d.H + 4) * 4;
   const size_t fixed = 16 + (size_t)T * xrow + (size_t)d.H * 4;
   int ch = 0, grid = 0;
   bool cluster = false;
-  void (*kern)(MoeDims, MoeBufs, int) = nullptr;
+  void (*kern)(MoeDims, MoeBufs, int, MoeWeights) = nullptr;
   size_t room = 0;
   for (int v = 0; v < 2 && !kern; v++) {  // the cluster variant first
     const bool q3 = geo_qwen3(d);
-    void (*k)(MoeDims, MoeBufs, int) =
+    void (*k)(MoeDims, MoeBufs, int, MoeWeights) =
         fused ? route_chain_kernel<true>(v == 0, q3) : route_chain_kernel<false>(v == 0, q3);
     cudaFuncAttributes fa;
     RV_CUDA(cudaFuncGetAttributes(&fa, k));
@@ -821,7 +822,7 @@ static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, bool fu
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = cluster ? 2 : 1;
-  RV_CUDA(cudaLaunchKernelEx(&cfg, kern, d, B, ch));
+  RV_CUDA(cudaLaunchKernelEx(&cfg, kern, d, B, ch, W));
   return RV_OK;
 }
 
@@ -1082,7 +1083,7 @@ static int launch_fused_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &
     cudaGetLastError();
   }
   if (ck < 0) return 1;
-  int rc = launch_route_chain(d, B, 1, true, s);
+  int rc = launch_route_chain(d, B, 1, true, W, s);
   if (rc) return -rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ncta);
@@ -1172,7 +1173,7 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
     RV_CUDA(launch_pdl(geo_qwen3(d) ? k_route_spec<RV_GEO_QWEN3> : k_route_spec<0>,
                        dim3((unsigned)((d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC)), dim3(128),
                        std::max(rs_need, (size_t)RV_ROUTE_SMEM_ONE_PER_SM), s, d, B));
-    if ((rc = launch_route_chain(d, B, T, false, s))) return rc;
+    if ((rc = launch_route_chain(d, B, T, false, W, s))) return rc;
     spec_units = std::min(d.E, T * d.K);
   } else if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch

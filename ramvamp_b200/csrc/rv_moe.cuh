@@ -846,7 +846,8 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
 // compute warps wait for it before reading the residual, and the routing
 // ranks every expert (the bounds are not written yet).
 template <bool CLUSTER, int GEO, bool FUSED>
-__global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, MoeBufs B, int CH) {
+__global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, MoeBufs B, int CH, MoeWeights W) {
+  (void)W;  // the layer's expert slabs (unused: L2 prefetches from here delayed the pipeline)
   const MoeDims d = geo_dims<GEO>(dd);
   extern __shared__ __align__(16) uint8_t sm[];
   __shared__ double es[4][256];
@@ -889,8 +890,7 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, Mo
       // the routing below ranks only those (named barrier 2 hands them over).
       spec_candidates_warp(d.E, d.K, T, B.spec, s_cand, s_ncand, s_cmask, lane);
       __syncwarp();
-      asm volatile("bar.arrive 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");
-    }
+      asm volatile("bar.arrive 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");    }
     return;
   }
   if constexpr (FUSED) pdl_wait();  // the residual is the previous kernel's output
