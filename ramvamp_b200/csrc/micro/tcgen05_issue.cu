@@ -1,6 +1,8 @@
 // Microbenchmark: how fast one thread can issue tcgen05.mma (kind::f16,
 // M = 128, K = 16, f32 accumulator in tensor memory) for N = 16..256, and
-// what a stage's commit / wait / fence adds.  This is the rate that bounds
+// what a stage's commit / wait / fence adds; and the int8 rate (kind::i8,
+// signed 8-bit A and B, s32 accumulator, K = 32 per instruction) that the
+// tensor-peak roofline of an int8 design would use.  This is the rate that bounds
 // the tensor-core prefill path when an expert holds few tokens.
 // Modes: back-to-back MMAs; commit + wait after every 4; two commits per 4
 // (one per ring, as the GEMM's MMA thread does); two commits, two waits on
@@ -11,6 +13,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 __device__ __forceinline__ uint32_t sa(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+template <bool I8>
 __global__ void k(int n, int reps, int mode, long long *out) {
   extern __shared__ __align__(1024) uint8_t sm[];
   __shared__ uint32_t tm;
@@ -35,15 +38,22 @@ __global__ void k(int n, int reps, int mode, long long *out) {
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t t = tm;
   if (threadIdx.x == 0) {
-    const uint32_t idesc = (1u << 4) | ((uint32_t)(n >> 3) << 17) | (8u << 24);
+    // c_format bits [4,6): F32 = 1 / S32 = 2; a/b format bits [7,10) and
+    // [10,13): F16 = 0 / signed 8-bit = 1; N >> 3 at bit 17; M >> 4 at bit 24.
+    const uint32_t idesc = (I8 ? (2u << 4) | (1u << 7) | (1u << 10) : (1u << 4)) | ((uint32_t)(n >> 3) << 17) |
+                           (8u << 24);
     const uint32_t lo = (8u << 16) | (sa(sm) >> 4), hi = 64u | (1u << 14);
     uint32_t ph = 0;
     long long t0 = clock64();
     for (int r = 0; r < reps; r++) {
       for (int kk = 0; kk < 4; kk++) {
         const uint64_t a = ((uint64_t)hi << 32) | (lo + 16 * kk), b = ((uint64_t)hi << 32) | (lo + 1024 + 16 * kk);
-        asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-                     ::"r"(t), "l"(a), "l"(b), "r"(idesc), "r"(1) : "memory");
+        if constexpr (I8)
+          asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n"
+                       ::"r"(t), "l"(a), "l"(b), "r"(idesc), "r"(1) : "memory");
+        else
+          asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+                       ::"r"(t), "l"(a), "l"(b), "r"(idesc), "r"(1) : "memory");
       }
       if (mode >= 2) {
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa(&bar2[0])) : "memory");
@@ -85,17 +95,30 @@ __global__ void k(int n, int reps, int mode, long long *out) {
 int main() {
   long long *out;
   cudaMalloc(&out, 1024 * 8);
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+  cudaFuncSetAttribute(k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+  cudaFuncSetAttribute(k<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
   for (int mode = 0; mode < 4; mode++)
     for (int n : {16, 32, 64, 128, 256}) {
       const int reps = 256;
-      k<<<1, 128, 64 * 1024>>>(n, reps, mode, out);
+      k<false><<<1, 128, 64 * 1024>>>(n, reps, mode, out);
       long long c;
       cudaMemcpy(&c, out, 8, cudaMemcpyDeviceToHost);
       const double per = (double)c / (reps * 4);
-      printf("mode %s N=%3d: %.1f cycles per MMA (128x%dx16), %.0f MAC/clk\n", mode == 0 ? "back-to-back " : mode == 1 ? "commit+wait/4" : mode == 2 ? "2 commits/4  " : "2cm+2wait+f/4", n, per, n,
+      printf("f16  mode %s N=%3d: %.1f cycles per MMA (128x%dx16), %.0f MAC/clk\n", mode == 0 ? "back-to-back " : mode == 1 ? "commit+wait/4" : mode == 2 ? "2 commits/4  " : "2cm+2wait+f/4", n, per, n,
              128.0 * n * 16 / per);
     }
+  int sms = 0, clk_khz = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  cudaDeviceGetAttribute(&clk_khz, cudaDevAttrClockRate, 0);
+  for (int n : {64, 128, 256}) {
+    const int reps = 256;
+    k<true><<<1, 128, 64 * 1024>>>(n, reps, 0, out);
+    long long c;
+    cudaMemcpy(&c, out, 8, cudaMemcpyDeviceToHost);
+    const double per = (double)c / (reps * 4), mac = 128.0 * n * 32 / per;
+    printf("i8   back-to-back N=%3d: %.1f cycles per MMA (128x%dx32), %.0f MAC/clk per SM = %.2f POPS at %d SMs x %.0f MHz\n",
+           n, per, n, mac, 2.0 * mac * sms * clk_khz * 1e3 / 1e15, sms, clk_khz / 1e3);
+  }
   printf("status: %s\n", cudaGetErrorString(cudaDeviceSynchronize()));
   return 0;
 }
