@@ -58,7 +58,8 @@ typedef enum rv_status {
   RV_ERR_INVALID_ARGUMENT = 13,            /* null pointer, misaligned buffer, bad flag */
   RV_ERR_CUDA = 14,                        /* a CUDA runtime call failed */
   RV_ERR_NCCL = 15,                        /* a collective failed */
-  RV_ERR_TIMEOUT = 16                      /* a bounded device-side wait ran out */
+  RV_ERR_TIMEOUT = 16,                     /* a bounded device-side wait ran out */
+  RV_ERR_IO = 17                           /* IoError::Io: a file could not be opened or read */
 } rv_status;
 
 /* Quantization formats (kernels/quants/mod.rs:57-70). */
@@ -210,6 +211,15 @@ RV_API void rv_expert_table_destroy(rv_expert_table *t);
 RV_API int rv_expert_table_upload(rv_expert_table *t, uint32_t layer, uint32_t expert_first,
                            uint32_t n_experts, const void *src, size_t len, int src_on_device,
                            rv_stream stream);
+/* Loads layer `layer` from an install's expert file (the file behind
+ * layers[i].file of experts/layout.json, format/layout.rs:1-13): the
+ * n_experts*stride bytes from file_offset on, read in chunks and copied to
+ * the device as they arrive (the load-time half of io/stream.rs, whose
+ * steady-state reads become table hits).  RV_ERR_IO when the file cannot be
+ * opened or read, RV_ERR_LENGTH_MISMATCH when it is shorter than the layer.
+ * Synchronizes `stream`. */
+RV_API int rv_expert_table_load_file(rv_expert_table *t, uint32_t layer, const char *path,
+                                     uint64_t file_offset, rv_stream stream);
 RV_API int rv_expert_table_layout(const rv_expert_table *t, uint32_t layer, rv_layer_layout *out);
 RV_API uint32_t rv_expert_table_n_layers(const rv_expert_table *t);
 /* io/stream.rs:1472 (begin_layer): opens a step for `experts` (host array).

@@ -10,12 +10,14 @@ stream.  Names and error kinds follow the reference:
 - ``FusedPart`` / ``gemv_q8_k_fused_rows``   kernels/gemv.rs:655, 747
 - ``CudaBackend`` (the ``Backend`` trait)    kernels/backend.rs:23-59
 - ``ExpertTable`` (``ExpertStream`` API)      io/stream.rs:1472-2160
+- ``rvmp.load_expert_table`` (install files) format/layout.rs, io/expert.rs
 - ``MoeEngine.forward`` (the MoE block)      model/forward.rs:2654-2754,
                                              model/prefill.rs:2136-2263
 """
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 from enum import IntEnum
 from typing import Optional, Sequence
@@ -281,6 +283,11 @@ class ExpertTable:
             n = len(mv) // self.layouts[layer].stride
             _check(lib().rv_expert_table_upload(self.handle, layer, expert_first, n, buf, len(mv), 0,
                                                 _stream()))
+
+    def load_file(self, layer: int, path: str, offset: int = 0) -> None:
+        """Layer `layer`'s expert file (n_experts * stride bytes from
+        `offset`), read and copied to the device by the native loader."""
+        _check(lib().rv_expert_table_load_file(self.handle, layer, os.fsencode(path), offset, _stream()))
 
     def fill_synthetic(self, layer: int, seed: int, sigma: float = 0.02, first_expert: int = 0,
                        expert_step: int = 1) -> None:

@@ -25,6 +25,7 @@ STATUS_NAMES = {
     8: "Unimplemented", 9: "UnsupportedFormat", 10: "RoutedExpertOutOfRange",
     11: "LayerOutOfRange", 12: "Protocol", 13: "InvalidArgument", 14: "Cuda", 15: "Nccl",
     16: "Timeout",
+    17: "Io",
 }
 
 
@@ -93,6 +94,7 @@ SIGNATURES = {
     "rv_expert_table_create": (I32, [I32, ctypes.POINTER(LayerLayout), U32, ctypes.POINTER(P)]),
     "rv_expert_table_destroy": (None, [P]),
     "rv_expert_table_upload": (I32, [P, U32, U32, U32, P, SZ, I32, P]),
+    "rv_expert_table_load_file": (I32, [P, U32, ctypes.c_char_p, U64, P]),
     "rv_expert_table_layout": (I32, [P, U32, ctypes.POINTER(LayerLayout)]),
     "rv_expert_table_n_layers": (U32, [P]),
     "rv_expert_table_begin_layer": (I32, [P, U32, P, SZ]),

@@ -2,6 +2,9 @@
 // include/ramvamp_b200.h.  One translation unit (the kernels come in as
 // headers) so every device global lives in one module.
 #include <algorithm>
+#include <cerrno>
+#include <cstdio>
+#include <cstring>
 #include <cstdlib>
 #include <mutex>
 #include <new>
@@ -57,6 +60,7 @@ extern "C" const char *rv_status_name(int s) {
     case RV_ERR_CUDA: return "Cuda";
     case RV_ERR_NCCL: return "Nccl";
     case RV_ERR_TIMEOUT: return "Timeout";
+    case RV_ERR_IO: return "Io";
   }
   return "Unknown";
 }
@@ -481,6 +485,79 @@ extern "C" int rv_expert_table_upload(rv_expert_table *t, uint32_t layer, uint32
                           src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
   RV_CUDA(cudaStreamSynchronize(s));
   return RV_OK;
+}
+
+// One layer's expert file (`experts/layer_XX.bin` of an install: n_experts
+// blobs of `stride` bytes from file_offset on; format/layout.rs:1-13) into
+// the table.  The file is read in 8 MiB chunks into two pinned staging
+// buffers, each chunk copied to the device while the next is read.
+extern "C" int rv_expert_table_load_file(rv_expert_table *t, uint32_t layer, const char *path,
+                                         uint64_t file_offset, rv_stream stream) {
+  if (!t || !path) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "load_file: null pointer");
+  if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
+  const rv_layer_layout &L = t->layouts[layer];
+  const uint64_t total = (uint64_t)L.n_experts * L.stride;
+  FILE *f = fopen(path, "rb");
+  if (!f) RV_FAIL(RV_ERR_IO, "layer %u: cannot open %s: %s", layer, path, strerror(errno));
+  struct Closer {
+    FILE *f;
+    ~Closer() { fclose(f); }
+  } closer{f};
+  if (fseeko(f, 0, SEEK_END) != 0) RV_FAIL(RV_ERR_IO, "layer %u: cannot seek %s", layer, path);
+  const uint64_t size = (uint64_t)ftello(f);
+  if (size < file_offset || size - file_offset < total)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "layer %u: %s holds %llu bytes from offset %llu, the layer needs %llu", layer,
+            path, (unsigned long long)(size - std::min(size, file_offset)), (unsigned long long)file_offset,
+            (unsigned long long)total);
+  if (fseeko(f, (off_t)file_offset, SEEK_SET) != 0) RV_FAIL(RV_ERR_IO, "layer %u: cannot seek %s", layer, path);
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(t->device));
+  const size_t chunk = 8u << 20;
+  void *stage[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = RV_OK;
+  cudaError_t e = cudaSuccess;
+  for (int i = 0; i < 2 && e == cudaSuccess; i++) {
+    e = cudaHostAlloc(&stage[i], chunk, cudaHostAllocDefault);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming);
+  }
+  if (e != cudaSuccess) {
+    rv_set_error(RV_ERR_CUDA, "load_file: staging buffers: %s", cudaGetErrorString(e));
+    rc = RV_ERR_CUDA;
+  }
+  for (uint64_t off = 0, k = 0; rc == RV_OK && off < total; off += chunk, k++) {
+    const int b = (int)(k & 1);
+    const size_t n = (size_t)std::min<uint64_t>(chunk, total - off);
+    if (k >= 2 && (e = cudaEventSynchronize(done[b])) != cudaSuccess) {  // the copy that used this buffer
+      rv_set_error(RV_ERR_CUDA, "load_file: %s", cudaGetErrorString(e));
+      rc = RV_ERR_CUDA;
+      break;
+    }
+    if (fread(stage[b], 1, n, f) != n) {
+      rv_set_error(RV_ERR_IO, "layer %u: short read of %s at byte %llu", layer, path,
+                   (unsigned long long)(file_offset + off));
+      rc = RV_ERR_IO;
+      break;
+    }
+    if ((e = cudaMemcpyAsync(t->base[layer] + off, stage[b], n, cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+        (e = cudaEventRecord(done[b], s)) != cudaSuccess) {
+      rv_set_error(RV_ERR_CUDA, "load_file: %s", cudaGetErrorString(e));
+      rc = RV_ERR_CUDA;
+    }
+  }
+  const cudaError_t es = cudaStreamSynchronize(s);
+  if (rc == RV_OK && es != cudaSuccess) {
+    rv_set_error(RV_ERR_CUDA, "load_file: %s", cudaGetErrorString(es));
+    rc = RV_ERR_CUDA;
+  }
+  for (int i = 0; i < 2; i++) {
+    if (done[i]) cudaEventDestroy(done[i]);
+    if (stage[i]) cudaFreeHost(stage[i]);
+  }
+  cudaSetDevice(prev);
+  return rc;
 }
 
 extern "C" int rv_expert_table_begin_layer(rv_expert_table *t, uint32_t layer, const uint32_t *experts,
