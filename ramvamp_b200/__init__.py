@@ -482,3 +482,5 @@ class MoeEngine:
 def device_status(device: int = 0) -> None:
     """Raise if a device-side bounded wait or check failed since the last call."""
     _check(lib().rv_device_status(device, _stream()))
+
+from . import rvmp  # noqa: E402  (install reader; imports this module lazily)
