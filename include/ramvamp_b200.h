@@ -59,7 +59,8 @@ typedef enum rv_status {
   RV_ERR_CUDA = 14,                        /* a CUDA runtime call failed */
   RV_ERR_NCCL = 15,                        /* a collective failed */
   RV_ERR_TIMEOUT = 16,                     /* a bounded device-side wait ran out */
-  RV_ERR_IO = 17                           /* IoError::Io: a file could not be opened or read */
+  RV_ERR_IO = 17,                          /* IoError::Io: a file could not be opened or read */
+  RV_ERR_TOKEN_OUT_OF_RANGE = 18           /* ModelError::TokenOutOfRange (a row id past the matrix) */
 } rv_status;
 
 /* Quantization formats (kernels/quants/mod.rs:57-70). */
@@ -79,6 +80,14 @@ typedef struct rv_block_q8k {
   int8_t qs[256];
   int16_t bsums[16];
 } rv_block_q8k;
+
+/* One Q8_0 activation block: the reference's BlockQ8_0
+ * (kernels/quants/blocks.rs:167-178), d already rounded through f16, in a
+ * 36-byte C layout: d at 0, qs at 4. */
+typedef struct rv_block_q8_0 {
+  float d;
+  int8_t qs[32];
+} rv_block_q8_0;
 
 /* ------------------------------------------------------------ library */
 /* Version string of the library build. */
@@ -131,6 +140,53 @@ RV_API int rv_gemv_q8_k_batched(int format, const uint8_t *weight, size_t weight
                          size_t out_dim, const rv_block_q8k *acts, size_t acts_len, size_t n_acts,
                          size_t row_start, size_t row_end, float *out, size_t out_len,
                          rv_stream stream);
+
+/* Replaces quants::quantize_row_q8_0 (kernels/quants/quantize.rs:37-54):
+ * per 32 floats d = amax/127, values times 1/d rounded half away from zero
+ * with Rust's saturating cast (NaN -> 0), d stored rounded through f16.
+ * x: device, n floats; out: device, out_blocks blocks.  Byte-identical to
+ * the scalar arm on every input.  (The AVX2 arm, avx2.rs:1022-1056, agrees
+ * with it except on blocks whose amax is below ~3.7e-37, where 1/d
+ * overflows and cvtps_epi32 turns every value into -128.)
+ * RV_ERR_QUANTIZE_LEN_MISMATCH when n != 32*out_blocks. */
+RV_API int rv_quantize_row_q8_0(const float *x, size_t n, rv_block_q8_0 *out, size_t out_blocks,
+                         rv_stream stream);
+
+/* Replaces gemv::gemv_q8_0 / Backend::gemv_q8_0 (kernels/gemv.rs:544-565,
+ * kernels/backend.rs:89-98): Q8_0 weights (34 B / 32 weights) against Q8_0
+ * activations, out[r] = weight_row_r . acts.  weight: device, any 2-byte
+ * alignment; acts: device, acts_len blocks; out: device.  Bit-identical to
+ * the AVX2 arm (avx2.rs:942-963): eight i32 lanes of four products per
+ * block, one FMA per lane per block, then hsum_ps_8's fixed tree. */
+RV_API int rv_gemv_q8_0(const uint8_t *weight, size_t weight_len, size_t in_dim, size_t out_dim,
+                 const rv_block_q8_0 *acts, size_t acts_len, float *out, size_t out_len,
+                 rv_stream stream);
+
+/* Replaces gemv::gemv_q8_0_rows (kernels/gemv.rs:579-601): rows
+ * [row_start, row_end) only, out holds row_end-row_start floats. */
+RV_API int rv_gemv_q8_0_rows(const uint8_t *weight, size_t weight_len, size_t in_dim, size_t out_dim,
+                      const rv_block_q8_0 *acts, size_t acts_len, size_t row_start, size_t row_end,
+                      float *out, size_t out_len, rv_stream stream);
+
+/* Replaces gemv::gemv_q8_0_batched (kernels/gemv.rs:616-640):
+ * out[i*n_acts + a] = weight_row_(row_start+i) . act_row_a. */
+RV_API int rv_gemv_q8_0_batched(const uint8_t *weight, size_t weight_len, size_t in_dim, size_t out_dim,
+                         const rv_block_q8_0 *acts, size_t acts_len, size_t n_acts, size_t row_start,
+                         size_t row_end, float *out, size_t out_len, rv_stream stream);
+
+/* Replaces quants::dequantize_row_{q4_k,q5_k,q6_k,q8_0}
+ * (kernels/quants/dequant.rs:28-147) over chosen rows of a matrix, which is
+ * also Weights::embed (model/weights.rs:371-384) for token ids:
+ * out[i][0..in_dim) = dequantize(row rows[i]).  weight: device, out_dim
+ * rows of row_bytes(in_dim); rows: device, n_rows ids, or NULL for rows
+ * 0..n_rows-1; out: device, n_rows*in_dim floats.  Bit-identical (every
+ * product and difference rounded as the reference's f32 expressions).
+ * A device id >= out_dim cannot be checked before the launch: its row is
+ * written as zeros and the device error word is set to
+ * RV_ERR_TOKEN_OUT_OF_RANGE, which rv_device_status reports. */
+RV_API int rv_dequantize_rows(int format, const uint8_t *weight, size_t weight_len, size_t in_dim,
+                       size_t out_dim, const uint32_t *rows, size_t n_rows, float *out, size_t out_len,
+                       rv_stream stream);
 
 /* One matrix of a fused row space (gemv::FusedPart, kernels/gemv.rs:655-686).
  * weight and acts are device pointers. */

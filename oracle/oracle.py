@@ -23,6 +23,9 @@ BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, Q8_0: 34, Q8_K: 292}
 # BlockQ8K (blocks.rs:260-268) as a packed 292-byte record.
 Q8K_DTYPE = np.dtype([("d", "<f4"), ("qs", "i1", (256,)), ("bsums", "<i2", (16,))])
 assert Q8K_DTYPE.itemsize == 292
+# BlockQ8_0 (blocks.rs:167-178): d (already f16-rounded) + 32 i8, 36 bytes.
+Q8_0_DTYPE = np.dtype([("d", "<f4"), ("qs", "i1", (32,))])
+assert Q8_0_DTYPE.itemsize == 36
 
 ERRORS = {
     0: "Ok",
@@ -97,7 +100,11 @@ def _declare(L):
     L.or_gemv.argtypes = [I32, P, SZ, SZ, SZ, P, SZ, SZ, SZ, P, SZ, I32, I32]
     L.or_lcg_next_u64.argtypes = [P]; L.or_lcg_next_u64.restype = ctypes.c_uint64
     L.or_lcg_fill_f32.argtypes = [P, P, SZ, ctypes.c_float]
-    for f in ("or_quantize_row_q4_k_test", "or_quantize_row_q5_k_test", "or_quantize_row_q6_k_test"):
+    L.or_quantize_row_q8_0.argtypes = [P, SZ, P, SZ, I32]
+    L.or_vec_dot_q8_0.argtypes = [P, SZ, P, SZ, I32, P]
+    L.or_gemv_q8_0.argtypes = [P, SZ, SZ, SZ, P, SZ, SZ, SZ, SZ, P, SZ, I32, I32]
+    for f in ("or_quantize_row_q4_k_test", "or_quantize_row_q5_k_test", "or_quantize_row_q6_k_test",
+              "or_quantize_row_q8_0_test"):
         getattr(L, f).argtypes = [P, SZ, P]
     L.or_dequantize_row.argtypes = [I32, P, SZ, P]
     L.or_rmsnorm.argtypes = [P, P, SZ, ctypes.c_float, P]
@@ -192,6 +199,39 @@ def gemv(fmt: int, w, in_dim: int, out_dim: int, acts, n_acts: int = 1, rows=Non
     return out
 
 
+# -------------------------------------------------------------- Q8_0
+def quantize_row_q8_0(x, impl: int | None = None, out_blocks: int | None = None) -> np.ndarray:
+    """quantize.rs:37-54 (scalar) / avx2.rs:1022-1056 (AVX2)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    nb = x.size // 32 if out_blocks is None else out_blocks
+    out = np.zeros(max(nb, 0), dtype=Q8_0_DTYPE)
+    _check(lib().or_quantize_row_q8_0(_p(x), x.size, _p(out), nb,
+                                      default_impl() if impl is None else impl), "quantize_row_q8_0")
+    return out
+
+
+def vec_dot_q8_0(w, acts, impl: int | None = None) -> float:
+    """dot.rs:190-201 / avx2.rs:942-963 / the lane model."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    acts = np.ascontiguousarray(acts, dtype=Q8_0_DTYPE)
+    out = np.zeros(1, dtype=np.float32)
+    _check(lib().or_vec_dot_q8_0(_p(w), w.size, _p(acts), acts.size,
+                                 default_impl() if impl is None else impl, _p(out)), "vec_dot_q8_0")
+    return float(out[0])
+
+
+def gemv_q8_0(w, in_dim: int, out_dim: int, acts, n_acts: int = 1, rows=None,
+              impl: int | None = None, threads: int = 1) -> np.ndarray:
+    """gemv.rs:544-640 (gemv_q8_0 / _rows / _batched)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    acts = np.ascontiguousarray(acts, dtype=Q8_0_DTYPE)
+    r0, r1 = (0, out_dim) if rows is None else rows
+    out = np.zeros(max(r1 - r0, 0) * n_acts, dtype=np.float32)
+    _check(lib().or_gemv_q8_0(_p(w), w.size, in_dim, out_dim, _p(acts), acts.size, n_acts, r0, r1, _p(out),
+                              out.size, default_impl() if impl is None else impl, threads), "gemv_q8_0")
+    return out
+
+
 # -------------------------------------------------------------- Lcg
 class Lcg:
     """test_support.rs:23-39."""
@@ -210,19 +250,20 @@ class Lcg:
 
 # ------------------------------------------------- weight quantizers
 def quantize_weights(fmt: int, x) -> np.ndarray:
-    """The reference's weight quantizers (test_support.rs:106-219)."""
+    """The reference's weight quantizers (test_support.rs:106-234)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    assert x.size % 256 == 0
-    out = np.zeros(x.size // 256 * BLOCK_BYTES[fmt], dtype=np.uint8)
+    bw = 32 if fmt == Q8_0 else 256
+    assert x.size % bw == 0
+    out = np.zeros(x.size // bw * BLOCK_BYTES[fmt], dtype=np.uint8)
     fn = {Q4_K: "or_quantize_row_q4_k_test", Q5_K: "or_quantize_row_q5_k_test",
-          Q6_K: "or_quantize_row_q6_k_test"}[fmt]
+          Q6_K: "or_quantize_row_q6_k_test", Q8_0: "or_quantize_row_q8_0_test"}[fmt]
     getattr(lib(), fn)(_p(x), x.size, _p(out))
     return out
 
 
 def dequantize_row(fmt: int, b) -> np.ndarray:
     b = np.ascontiguousarray(b, dtype=np.uint8)
-    out = np.zeros(b.size // BLOCK_BYTES[fmt] * 256, dtype=np.float32)
+    out = np.zeros(b.size // BLOCK_BYTES[fmt] * (32 if fmt == Q8_0 else 256), dtype=np.float32)
     _check(lib().or_dequantize_row(fmt, _p(b), b.size, _p(out)), "dequantize_row")
     return out
 

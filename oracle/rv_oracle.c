@@ -747,6 +747,173 @@ int or_gemv(int fmt, const uint8_t *w, size_t w_len, size_t in_dim, size_t out_d
   return OR_OK;
 }
 
+/* ------------------------------------------------------------------ Q8_0 */
+/* Rust's saturating `f32 as i8`: NaN -> 0, out-of-range -> the nearest bound. */
+static inline int8_t sat_i8(float r) {
+  if (r != r) return 0;
+  if (r >= 127.0f) return 127;
+  if (r <= -128.0f) return -128;
+  return (int8_t)r;
+}
+
+/* quantize.rs:37-54 (scalar).  amax starts at 0 and f32::max ignores NaN,
+ * as fmaxf does. */
+static void quantize_q8_0_scalar(const float *xs, or_block_q8_0 *b) {
+  float amax = 0.0f;
+  for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(xs[j]));
+  float d = amax / 127.0f;
+  float id = d != 0.0f ? 1.0f / d : 0.0f;
+  b->d = or_f16_to_f32(or_f32_to_f16(d));
+  for (int j = 0; j < 32; j++) b->qs[j] = sat_i8(roundf(xs[j] * id));
+}
+
+#if OR_HAVE_X86
+/* avx2.rs:997-1012 (round_away_ps): ties-to-even, then ties fixed away. */
+__attribute__((target("avx2,fma"))) static inline __m256 round_away_ps(__m256 x) {
+  __m256 t = _mm256_round_ps(x, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC);
+  __m256 diff = _mm256_sub_ps(x, t);
+  __m256 one = _mm256_set1_ps(1.0f), zero = _mm256_setzero_ps();
+  __m256 tie_up = _mm256_and_ps(_mm256_cmp_ps(diff, _mm256_set1_ps(0.5f), _CMP_EQ_OQ),
+                                _mm256_cmp_ps(x, zero, _CMP_GT_OQ));
+  __m256 tie_dn = _mm256_and_ps(_mm256_cmp_ps(diff, _mm256_set1_ps(-0.5f), _CMP_EQ_OQ),
+                                _mm256_cmp_ps(x, zero, _CMP_LT_OQ));
+  t = _mm256_add_ps(t, _mm256_and_ps(tie_up, one));
+  return _mm256_sub_ps(t, _mm256_and_ps(tie_dn, one));
+}
+
+/* avx2.rs:1022-1056 */
+__attribute__((target("avx2,fma"))) static void quantize_q8_0_avx2(const float *xs, or_block_q8_0 *b) {
+  const __m256 sm = _mm256_set1_ps(-0.0f);
+  __m256 v0 = _mm256_loadu_ps(xs), v1 = _mm256_loadu_ps(xs + 8);
+  __m256 v2 = _mm256_loadu_ps(xs + 16), v3 = _mm256_loadu_ps(xs + 24);
+  __m256 a01 = _mm256_max_ps(_mm256_andnot_ps(sm, v0), _mm256_andnot_ps(sm, v1));
+  __m256 a23 = _mm256_max_ps(_mm256_andnot_ps(sm, v2), _mm256_andnot_ps(sm, v3));
+  float amax = hmax_ps_8(_mm256_max_ps(a01, a23));
+  float d = amax / 127.0f;
+  float id = d != 0.0f ? 1.0f / d : 0.0f;
+  b->d = or_f16_to_f32(or_f32_to_f16(d));
+  __m256 iv = _mm256_set1_ps(id);
+  __m256i i0 = _mm256_cvtps_epi32(round_away_ps(_mm256_mul_ps(v0, iv)));
+  __m256i i1 = _mm256_cvtps_epi32(round_away_ps(_mm256_mul_ps(v1, iv)));
+  __m256i i2 = _mm256_cvtps_epi32(round_away_ps(_mm256_mul_ps(v2, iv)));
+  __m256i i3 = _mm256_cvtps_epi32(round_away_ps(_mm256_mul_ps(v3, iv)));
+  pack_store_i8(b->qs, i0, i1, i2, i3);
+}
+
+/* avx2.rs:942-963: sign trick, maddubs + madd -> eight i32 lanes (lane i =
+ * products 4i..4i+3), one FMA per lane per block, hsum_ps_8. */
+__attribute__((target("avx2,fma"))) static float dot_q8_0_avx2(const uint8_t *w, const or_block_q8_0 *a,
+                                                               size_t nb) {
+  const __m256i ones = _mm256_set1_epi16(1);
+  __m256 acc = _mm256_setzero_ps();
+  for (size_t b = 0; b < nb; b++) {
+    const uint8_t *blk = w + 34 * b;
+    float d = f16_at(blk, 0) * a[b].d;
+    __m256i qx = _mm256_loadu_si256((const __m256i *)(blk + 2));
+    __m256i qy = _mm256_loadu_si256((const __m256i *)a[b].qs);
+    __m256i dot16 = _mm256_maddubs_epi16(_mm256_sign_epi8(qx, qx), _mm256_sign_epi8(qy, qx));
+    __m256i sum32 = _mm256_madd_epi16(ones, dot16);
+    acc = _mm256_fmadd_ps(_mm256_set1_ps(d), _mm256_cvtepi32_ps(sum32), acc);
+  }
+  return hsum_ps_8(acc);
+}
+#endif
+
+/* dot.rs:190-201 (scalar ground truth). */
+static float dot_q8_0_scalar(const uint8_t *w, const or_block_q8_0 *a, size_t nb) {
+  float sumf = 0.0f;
+  for (size_t b = 0; b < nb; b++) {
+    const uint8_t *blk = w + 34 * b;
+    int32_t sumi = 0;
+    for (int l = 0; l < 32; l++) sumi += (int32_t)(int8_t)blk[2 + l] * (int32_t)a[b].qs[l];
+    sumf += (float)sumi * (f16_at(blk, 0) * a[b].d);
+  }
+  return sumf;
+}
+
+/* Lane model of avx2.rs:942-963: lane i of block b is the exact sum of
+ * products 4i..4i+3; acc[i] = fma(d_b, lane, acc[i]); hsum_ps_8 order. */
+static float dot_q8_0_lanes(const uint8_t *w, const or_block_q8_0 *a, size_t nb) {
+  float acc[8] = {0};
+  for (size_t b = 0; b < nb; b++) {
+    const uint8_t *blk = w + 34 * b;
+    float d = f16_at(blk, 0) * a[b].d;
+    for (int i = 0; i < 8; i++) {
+      int32_t s = 0;
+      for (int t = 0; t < 4; t++) s += (int32_t)(int8_t)blk[2 + 4 * i + t] * (int32_t)a[b].qs[4 * i + t];
+      acc[i] = fmaf(d, (float)s, acc[i]);
+    }
+  }
+  return lane_hsum8(acc);
+}
+
+static float dot_q8_0_one(const uint8_t *w, const or_block_q8_0 *a, size_t nb, int impl) {
+#if OR_HAVE_X86
+  if (impl == OR_IMPL_AVX2 && or_has_avx2()) return dot_q8_0_avx2(w, a, nb);
+#endif
+  if (impl == OR_IMPL_LANES) return dot_q8_0_lanes(w, a, nb);
+  return dot_q8_0_scalar(w, a, nb);
+}
+
+int or_quantize_row_q8_0(const float *x, size_t n, or_block_q8_0 *out, size_t out_blocks, int impl) {
+  if (n != out_blocks * 32) return OR_ERR_QUANTIZE_LEN_MISMATCH;
+  for (size_t b = 0; b < out_blocks; b++) {
+#if OR_HAVE_X86
+    if (impl == OR_IMPL_AVX2 && or_has_avx2()) {
+      quantize_q8_0_avx2(x + 32 * b, out + b);
+      continue;
+    }
+#endif
+    quantize_q8_0_scalar(x + 32 * b, out + b);
+  }
+  return OR_OK;
+}
+
+/* dot.rs:30-51 (weight_blocks) + the arm chosen by impl. */
+int or_vec_dot_q8_0(const uint8_t *w, size_t w_len, const or_block_q8_0 *a, size_t n_blocks, int impl,
+                    float *out) {
+  if (w_len % 34 != 0) return OR_ERR_ROW_BYTES_NOT_BLOCK_MULTIPLE;
+  if (w_len / 34 != n_blocks) return OR_ERR_BLOCK_COUNT_MISMATCH;
+  *out = dot_q8_0_one(w, a, n_blocks, impl);
+  return OR_OK;
+}
+
+/* gemv.rs:544-640 (gemv_q8_0 / _rows / _batched through gemv_impl,
+ * :212-264 validation): out[i*n_acts+a] = row(r0+i) . act_a. */
+int or_gemv_q8_0(const uint8_t *w, size_t w_len, size_t in_dim, size_t out_dim, const or_block_q8_0 *acts,
+                 size_t acts_len, size_t n_acts, size_t r0, size_t r1, float *out, size_t out_len, int impl,
+                 int threads) {
+  if (in_dim % 32 != 0) return OR_ERR_INDIVISIBLE_ROW;
+  size_t nb = in_dim / 32, row_bytes = nb * 34;
+  if (row_bytes * out_dim != w_len) return OR_ERR_LENGTH_MISMATCH;
+  if (r0 > r1 || r1 > out_dim) return OR_ERR_LENGTH_MISMATCH;
+  if ((r1 - r0) * n_acts != out_len) return OR_ERR_LENGTH_MISMATCH;
+  if (nb * n_acts != acts_len) return OR_ERR_BLOCK_COUNT_MISMATCH;
+  if (n_acts == 0) return OR_OK;
+  long rows = (long)(r1 - r0);
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(threads > 0 ? threads : 1) schedule(static)
+#endif
+  for (long i = 0; i < rows; i++)
+    for (size_t a = 0; a < n_acts; a++)
+      out[(size_t)i * n_acts + a] = dot_q8_0_one(w + (r0 + (size_t)i) * row_bytes, acts + a * nb, nb, impl);
+  (void)threads;
+  return OR_OK;
+}
+
+/* test_support.rs:221-234: packed 34-byte blocks via the activation
+ * quantizer (d is already f16-rounded, so the f16 store is exact). */
+void or_quantize_row_q8_0_test(const float *x, size_t n, uint8_t *out) {
+  for (size_t b = 0; b < n / 32; b++) {
+    or_block_q8_0 blk;
+    quantize_q8_0_scalar(x + 32 * b, &blk);
+    uint16_t h = or_f32_to_f16(blk.d);
+    out[34 * b] = (uint8_t)(h & 0xFF);
+    out[34 * b + 1] = (uint8_t)(h >> 8);
+    memcpy(out + 34 * b + 2, blk.qs, 32);
+  }
+}
+
 /* ------------------------------------------------------------------ Lcg */
 /* test_support.rs:23-39 */
 uint64_t or_lcg_next_u64(uint64_t *s) {
@@ -927,6 +1094,14 @@ void or_quantize_row_q6_k_test(const float *x, size_t n, uint8_t *out) {
 
 /* dequant.rs:28-132 */
 int or_dequantize_row(int fmt, const uint8_t *bytes, size_t len, float *out) {
+  if (fmt == OR_Q8_0) { /* dequant.rs:134-147 */
+    if (len % 34 != 0) return OR_ERR_ROW_BYTES_NOT_BLOCK_MULTIPLE;
+    for (size_t b = 0; b < len / 34; b++) {
+      float d = f16_at(bytes + 34 * b, 0);
+      for (int l = 0; l < 32; l++) out[32 * b + l] = d * (float)(int8_t)bytes[34 * b + 2 + l];
+    }
+    return OR_OK;
+  }
   if (!fmt_is_k(fmt)) return OR_ERR_UNSUPPORTED_FORMAT;
   size_t bb = or_block_bytes(fmt);
   if (len % bb != 0) return OR_ERR_ROW_BYTES_NOT_BLOCK_MULTIPLE;

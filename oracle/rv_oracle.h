@@ -55,6 +55,12 @@ typedef struct or_block_q8k {
   int16_t bsums[16];
 } or_block_q8k;
 
+/* BlockQ8_0 (blocks.rs:167-178): d already rounded through f16, 36 bytes. */
+typedef struct or_block_q8_0 {
+  float d;
+  int8_t qs[32];
+} or_block_q8_0;
+
 /* One MoE layer: norm, router, and 128 expert blobs laid out like the
  * .rvmp expert file (format/layout.rs:1-13): blob e starts at
  * blobs + e * stride; gate/up/down slabs at the given offsets. */
@@ -114,6 +120,18 @@ int or_gemv(int fmt, const uint8_t *w, size_t w_len, size_t in_dim, size_t out_d
             const or_block_q8k *acts, size_t n_acts, size_t r0, size_t r1, float *out,
             size_t out_len, int impl, int threads);
 
+/* quantize.rs:37-54 (scalar) / avx2.rs:1022-1056 (AVX2). */
+int or_quantize_row_q8_0(const float *x, size_t n, or_block_q8_0 *out, size_t out_blocks, int impl);
+/* dot.rs:190-201 / avx2.rs:942-963 / lane model. */
+int or_vec_dot_q8_0(const uint8_t *w, size_t w_len, const or_block_q8_0 *a, size_t n_blocks, int impl,
+                    float *out);
+/* gemv.rs:544-640: out[i*n_acts+a] = row(r0+i) . act_a. */
+int or_gemv_q8_0(const uint8_t *w, size_t w_len, size_t in_dim, size_t out_dim, const or_block_q8_0 *acts,
+                 size_t acts_len, size_t n_acts, size_t r0, size_t r1, float *out, size_t out_len, int impl,
+                 int threads);
+/* test_support.rs:221-234 */
+void or_quantize_row_q8_0_test(const float *x, size_t n, uint8_t *out);
+
 /* test_support.rs:23-39 */
 uint64_t or_lcg_next_u64(uint64_t *state);
 float or_lcg_next_f32(uint64_t *state);
@@ -123,7 +141,7 @@ void or_lcg_fill_f32(uint64_t *state, float *out, size_t n, float scale);
 void or_quantize_row_q4_k_test(const float *x, size_t n, uint8_t *out);
 void or_quantize_row_q5_k_test(const float *x, size_t n, uint8_t *out);
 void or_quantize_row_q6_k_test(const float *x, size_t n, uint8_t *out);
-/* dequant.rs */
+/* dequant.rs (Q4_K, Q5_K, Q6_K, Q8_0) */
 int or_dequantize_row(int fmt, const uint8_t *bytes, size_t len, float *out);
 
 /* primitives: norm.rs:17-60, softmax.rs:18-40, activation.rs:14-42 */

@@ -8,6 +8,10 @@ stream.  Names and error kinds follow the reference:
 - ``quantize_row_q8_k``                    kernels/quants/quantize.rs:68
 - ``gemv_q8_k`` / ``_rows`` / ``_batched``   kernels/gemv.rs:347, 386, 444
 - ``FusedPart`` / ``gemv_q8_k_fused_rows``   kernels/gemv.rs:655, 747
+- ``quantize_row_q8_0``                    kernels/quants/quantize.rs:37
+- ``gemv_q8_0`` / ``_rows`` / ``_batched``   kernels/gemv.rs:544, 579, 616
+- ``dequantize_rows`` / ``embed``          kernels/quants/dequant.rs:28-147,
+                                             model/weights.rs:371-384
 - ``CudaBackend`` (the ``Backend`` trait)    kernels/backend.rs:23-59
 - ``ExpertTable`` (``ExpertStream`` API)      io/stream.rs:1472-2160
 - ``rvmp.load_expert_table`` (install files) format/layout.rs, io/expert.rs
@@ -33,10 +37,12 @@ __all__ = [
     "gemv_q8_k_batched", "FusedPart", "gemv_q8_k_fused_rows", "rmsnorm", "softmax",
     "swiglu_combine", "debug_block_sums", "CudaBackend", "ExpertTable", "MoeEngine", "MoeConfig",
     "LayerLayout", "qwen3_layer_layout", "QWEN3_Q6K_DOWN_LAYERS", "synth_normal",
-    "quantize_weights", "EXACT", "TENSOR", "lib",
+    "quantize_weights", "EXACT", "TENSOR", "lib", "Q8_0_BYTES", "quantize_row_q8_0", "gemv_q8_0",
+    "gemv_q8_0_rows", "gemv_q8_0_batched", "dequantize_rows", "embed", "device_status",
 ]
 
 Q8K_BYTES = 292
+Q8_0_BYTES = 36  # rv_block_q8_0: f32 d + 32 i8
 EXACT = 0
 TENSOR = 1
 
@@ -83,6 +89,13 @@ def _blocks(acts: torch.Tensor) -> int:
     return n // Q8K_BYTES
 
 
+def _blocks_q8_0(acts: torch.Tensor) -> int:
+    n = _nbytes(acts)
+    if n % Q8_0_BYTES:
+        raise ValueError("Q8_0 activations must be a whole number of 36-byte blocks")
+    return n // Q8_0_BYTES
+
+
 # ---------------------------------------------------------------- kernels
 def quantize_row_q8_k(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Q8_K of ``x`` (device f32) into ``out`` (device uint8, 292 B/block)."""
@@ -111,6 +124,64 @@ def gemv_q8_k_batched(format, weight, in_dim, out_dim, acts, n_acts, rows: range
                                       _p(acts), _blocks(acts), n_acts, rows.start, rows.stop,
                                       _p(out), out.numel(), _stream()))
     return out
+
+
+def quantize_row_q8_0(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Q8_0 of ``x`` (device f32) into ``out`` (device uint8, 36 B/block):
+    quantize.rs:37-54."""
+    n = x.numel()
+    if out is None:
+        out = torch.empty((n // 32) * Q8_0_BYTES, dtype=torch.uint8, device=x.device)
+    _check(lib().rv_quantize_row_q8_0(_p(x), n, _p(out), _blocks_q8_0(out), _stream()))
+    return out
+
+
+def gemv_q8_0(weight, in_dim, out_dim, acts, out):
+    """gemv.rs:544-565: Q8_0 weights against Q8_0 activations."""
+    _check(lib().rv_gemv_q8_0(_p(weight), _nbytes(weight), in_dim, out_dim, _p(acts), _blocks_q8_0(acts),
+                              _p(out), out.numel(), _stream()))
+    return out
+
+
+def gemv_q8_0_rows(weight, in_dim, out_dim, acts, rows: range, out):
+    """gemv.rs:579-601."""
+    _check(lib().rv_gemv_q8_0_rows(_p(weight), _nbytes(weight), in_dim, out_dim, _p(acts), _blocks_q8_0(acts),
+                                   rows.start, rows.stop, _p(out), out.numel(), _stream()))
+    return out
+
+
+def gemv_q8_0_batched(weight, in_dim, out_dim, acts, n_acts, rows: range, out):
+    """gemv.rs:616-640: out[i * n_acts + a] = row(rows.start + i) . act_a."""
+    _check(lib().rv_gemv_q8_0_batched(_p(weight), _nbytes(weight), in_dim, out_dim, _p(acts),
+                                      _blocks_q8_0(acts), n_acts, rows.start, rows.stop, _p(out), out.numel(),
+                                      _stream()))
+    return out
+
+
+def dequantize_rows(format, weight, in_dim, out_dim, rows: Optional[torch.Tensor] = None,
+                    n_rows: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """dequant.rs:28-147 over chosen rows: out[i] = dequantize(row rows[i])
+    (rows: device int32/uint32 ids, or None for rows 0..n_rows-1)."""
+    if rows is not None:
+        if rows.dtype not in (torch.int32, torch.uint32):
+            raise ValueError("row ids must be 32-bit")
+        n_rows = rows.numel()
+    elif n_rows is None:
+        n_rows = out_dim
+    if out is None:
+        out = torch.empty(n_rows * in_dim, dtype=torch.float32, device=weight.device)
+    _check(lib().rv_dequantize_rows(int(format), _p(weight), _nbytes(weight), in_dim, out_dim, _p(rows), n_rows,
+                                    _p(out), out.numel(), _stream()))
+    return out
+
+
+def embed(embedding, hidden, vocab, tokens: torch.Tensor, format=None, out=None) -> torch.Tensor:
+    """Weights::embed (model/weights.rs:371-384) for a batch of token ids on
+    the device: one dequantized embedding row (``hidden`` floats) per token.
+    An id >= vocab zeroes its row and is reported by ``device_status`` as
+    TokenOutOfRange."""
+    fmt = QuantFormat.Q4_K if format is None else format
+    return dequantize_rows(fmt, embedding, hidden, vocab, rows=tokens, out=out)
 
 
 @dataclass
@@ -186,7 +257,7 @@ class CudaBackend:
         return gemv_q8_k(format, weight, in_dim, out_dim, acts, out)
 
     def gemv_q8_0(self, weight, in_dim, out_dim, acts, out):
-        raise KernelError(8, "Unimplemented: gemv_q8_0 is not on the routed-expert path")
+        return gemv_q8_0(weight, in_dim, out_dim, acts, out)
 
     def rmsnorm(self, x, weight, eps, out):
         return rmsnorm(x, weight, eps, out)

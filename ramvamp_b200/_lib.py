@@ -26,6 +26,7 @@ STATUS_NAMES = {
     11: "LayerOutOfRange", 12: "Protocol", 13: "InvalidArgument", 14: "Cuda", 15: "Nccl",
     16: "Timeout",
     17: "Io",
+    18: "TokenOutOfRange",
 }
 
 
@@ -86,6 +87,11 @@ SIGNATURES = {
     "rv_gemv_q8_k": (I32, [I32, P, SZ, SZ, SZ, P, SZ, P, SZ, P]),
     "rv_gemv_q8_k_rows": (I32, [I32, P, SZ, SZ, SZ, P, SZ, SZ, SZ, P, SZ, P]),
     "rv_gemv_q8_k_batched": (I32, [I32, P, SZ, SZ, SZ, P, SZ, SZ, SZ, SZ, P, SZ, P]),
+    "rv_quantize_row_q8_0": (I32, [P, SZ, P, SZ, P]),
+    "rv_gemv_q8_0": (I32, [P, SZ, SZ, SZ, P, SZ, P, SZ, P]),
+    "rv_gemv_q8_0_rows": (I32, [P, SZ, SZ, SZ, P, SZ, SZ, SZ, P, SZ, P]),
+    "rv_gemv_q8_0_batched": (I32, [P, SZ, SZ, SZ, P, SZ, SZ, SZ, SZ, P, SZ, P]),
+    "rv_dequantize_rows": (I32, [I32, P, SZ, SZ, SZ, P, SZ, P, SZ, P]),
     "rv_gemv_q8_k_fused_rows": (I32, [ctypes.POINTER(FusedPartC), SZ, SZ, SZ, P, SZ, P]),
     "rv_rmsnorm": (I32, [P, P, SZ, SZ, F32, P, P]),
     "rv_softmax": (I32, [P, SZ, SZ, P]),

@@ -95,6 +95,145 @@ __global__ void __launch_bounds__(256) k_gemv(GemvArgs g) {
   }
 }
 
+// ------------------------------------------------------- lm_head GEMV
+// Streaming Q6_K GEMV for one activation row, 8 blocks per row (hidden
+// 2048) and many rows: output.weight, 151,936 rows of 1,680 bytes, the
+// largest weight read of a decode step.  Same integer lane sums and float
+// order as k_gemv (lane_step, lane_reduce), hence bit-identical, but laid
+// out to stream HBM:
+// - a persistent grid walks 16-row tiles blockIdx.x, + gridDim.x, ...;
+//   each CTA keeps RV_LMH_STAGES tiles in flight (one bulk copy per tile,
+//   an mbarrier per stage) and refills a stage once every thread is done
+//   with it;
+// - thread (p, lane) computes lane `lane` of one row; the lane's 64
+//   activation words and 8 block scales stay in registers for the whole
+//   kernel (they are the same for every row);
+// - blocks are 210 bytes, so in a 4-byte-aligned row block b starts 2
+//   bytes past a word boundary exactly when b is odd: the unrolled loop
+//   knows each block's alignment at compile time (one load per aligned
+//   word, two and a funnel shift otherwise);
+// - rows are 420 words (4 mod 8), so the four rows a warp reads at once
+//   are taken two apart (8 banks apart): no bank conflicts;
+// - Q6_K's (q - 32) a is dp4a(q, a, dp4a(-32 x 4, a, 0)), an exact
+//   integer identity, so the 6-bit values need no per-byte subtraction.
+#define RV_LMH_ROWS 16
+#define RV_LMH_STAGES 3
+
+// prmt.b32 in its default mode: a selector nibble with bit 3 set fills the
+// byte with the sign of the byte its low bits select.
+RV_DEVFN uint32_t prmt_sext(uint32_t x, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(x), "r"(sel));
+  return r;
+}
+
+// The word at p (shared memory); MIS: p is 2 bytes past a word boundary.
+template <bool MIS>
+RV_DEVFN uint32_t ld32c(const uint8_t *p) {
+  if constexpr (MIS) {
+    const uint32_t *a = (const uint32_t *)(p - 2);
+    return __funnelshift_r(a[0], a[1], 16);
+  } else {
+    return *(const uint32_t *)p;
+  }
+}
+
+// Lane `lane`'s view of one Q6_K block: the eight 6-bit vectors (without
+// the -32), their signed scales, d.
+struct W6 {
+  uint32_t q[8];
+  int sc[8];
+  float d;
+};
+template <bool MIS>
+RV_DEVFN void load_w6(const uint8_t *blk, int lane, uint32_t sel_lo, uint32_t sel_hi, W6 &w) {
+  w.d = h2f(*(const uint16_t *)(blk + 208));
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const uint32_t ql0 = ld32c<MIS>(blk + 64 * h + 4 * lane);
+    const uint32_t ql1 = ld32c<MIS>(blk + 64 * h + 32 + 4 * lane);
+    const uint32_t qh = ld32c<MIS>(blk + 128 + 32 * h + 4 * lane);
+    w.q[4 * h + 0] = (ql0 & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
+    w.q[4 * h + 1] = (ql1 & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
+    w.q[4 * h + 2] = ((ql0 >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
+    w.q[4 * h + 3] = ((ql1 >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
+  }
+  // Vector (h, k)'s scale is byte 192 + 8h + 2k + (lane >= 4): byte
+  // 2(k & 1) + hi of word 2h + (k >> 1) of the 16 scale bytes.
+#pragma unroll
+  for (int m = 0; m < 4; m++) {
+    const uint32_t word = ld32c<MIS>(blk + 192 + 4 * m);
+    w.sc[2 * m] = (int)prmt_sext(word, sel_lo);
+    w.sc[2 * m + 1] = (int)prmt_sext(word, sel_hi);
+  }
+}
+
+__global__ void __launch_bounds__(RV_LMH_ROWS * 8, 2) k_gemv_lm_head(GemvArgs g) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint64_t *bar = (uint64_t *)sm;  // one per stage
+  constexpr int R = RV_LMH_ROWS, S = RV_LMH_STAGES;
+  constexpr size_t RB = 8 * 210, SB = (size_t)R * RB;
+  uint8_t *stage0 = sm + 64;
+  const size_t n_tiles = (g.nrows + R - 1) / R;
+  const uint8_t *w = g.w + g.r0 * RB;
+  auto issue = [&](size_t tile, int st) {
+    const uint32_t bytes = (uint32_t)(min((size_t)R, g.nrows - tile * R) * RB);
+    mbar_arrive_expect_tx(&bar[st], bytes);
+    bulk_g2s(stage0 + st * SB, w + tile * SB, bytes, &bar[st]);
+  };
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < S; i++) mbar_init(&bar[i], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < S; i++)
+      if (blockIdx.x + (size_t)i * gridDim.x < n_tiles) issue(blockIdx.x + (size_t)i * gridDim.x, i);
+  }
+  const int p = threadIdx.x >> 3, lane = threadIdx.x & 7;
+  int ax[8][8];
+  float yd[8];
+#pragma unroll
+  for (int b = 0; b < 8; b++) {
+    const uint8_t *act = g.acts + 292 * b;
+    yd[b] = *(const float *)act;
+#pragma unroll
+    for (int v = 0; v < 8; v++) ax[b][v] = *(const int *)(act + 4 + 128 * (v >> 2) + 32 * (v & 3) + 4 * lane);
+  }
+  const int wq = p >> 2, rt = 8 * (wq >> 1) + 2 * (p & 3) + (wq & 1);  // rows two apart within a warp
+  const uint32_t jlo = lane >= 4 ? 1u : 0u, jhi = jlo + 2u;
+  const uint32_t sel_lo = jlo | ((8u + jlo) * 0x1110u), sel_hi = jhi | ((8u + jhi) * 0x1110u);
+  uint32_t phase = 0;  // bit st = parity of stage st's next completion
+  int st = 0;
+  for (size_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, st = st + 1 == S ? 0 : st + 1) {
+    const bool ok = mbar_wait_bounded(&bar[st], (phase >> st) & 1);
+    phase ^= 1u << st;
+    if (!__syncthreads_and(ok)) return;
+    const int rows_here = (int)min((size_t)R, g.nrows - tile * R);
+    // Rows past the matrix compute row 0 of the tile and are never stored.
+    const uint8_t *wrow = stage0 + st * SB + (size_t)(rt < rows_here ? rt : 0) * RB;
+    float acc = 0.0f;
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+      W6 x;
+      if (b & 1) load_w6<true>(wrow + 210 * b, lane, sel_lo, sel_hi, x);
+      else load_w6<false>(wrow + 210 * b, lane, sel_lo, sel_hi, x);
+      int s = 0;
+#pragma unroll
+      for (int v = 0; v < 8; v++) s += x.sc[v] * __dp4a((int)x.q[v], ax[b][v], __dp4a((int)0xE0E0E0E0u, ax[b][v], 0));
+      acc = __fmaf_rn(__fmul_rn(x.d, yd[b]), __int2float_rn(s), acc);
+    }
+    const float r = lane_reduce<RV_Q6_K>(acc, 0.0f);
+    if (lane == 0 && rt < rows_here) g.out[tile * R + rt] = r;
+    __syncthreads();  // every thread is done with this stage
+    if (threadIdx.x == 0 && tile + (size_t)S * gridDim.x < n_tiles) {
+      fence_proxy_async();  // the reads above happen before the copy overwrites the stage
+      issue(tile + (size_t)S * gridDim.x, st);
+    }
+  }
+}
+
 // ------------------------------------------------------- integer taps
 // One warp per block: lanes 0..7 write the eight lane sums, 0..3 the mins.
 template <int FMT>
@@ -399,4 +538,153 @@ __global__ void k_quantize_weights(const float *__restrict__ x, uint8_t *__restr
     for (int g = 0; g < 16; g++) o[192 + g] = ls[g];
     put_f16(o + 208, d);
   }
+}
+
+// ------------------------------------------------------------ Q8_0
+// quantize.rs:37-54, one warp per 32-float block (lane = value).  amax
+// starts at 0 and fmaxf drops NaN, as f32::max does; the scale math is
+// IEEE f32; roundf rounds half away from zero; the cast saturates with
+// NaN -> 0 like Rust's `as i8`.
+RV_DEVFN int8_t sat_i8(float r) {
+  if (r != r) return 0;
+  if (r >= 127.0f) return 127;
+  if (r <= -128.0f) return -128;
+  return (int8_t)r;
+}
+
+__global__ void k_quantize_q8_0(const float *__restrict__ x, uint8_t *__restrict__ out, size_t n_blocks) {
+  const int lane = threadIdx.x & 31;
+  const size_t b = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= n_blocks) return;  // warp-uniform
+  const float v = x[b * 32 + lane];
+  float amax = fmaxf(0.0f, fabsf(v));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float d = __fdiv_rn(amax, 127.0f);
+  const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+  uint8_t *o = out + b * 36;
+  if (lane == 0) *(float *)o = f16_round(d);
+  o[4 + lane] = (uint8_t)sat_i8(roundf(__fmul_rn(v, id)));
+}
+
+// gemv.rs:296-330 with avx2.rs:942-963 as the dot: out[(r - r0) * n_acts
+// + a] = row(r) . act_a.  Block = R rows x 8 lanes; lane i of a row owns
+// bytes 4i..4i+3 of every block: s = dp4a (exact), d = f16(w.d) * y.d,
+// acc = fma(d, s, acc) in block order, then hsum_ps_8's tree across the
+// eight lanes.  Weight tile staged like k_gemv; activations MT rows at a
+// time (36-byte blocks).
+template <int MT>
+__global__ void __launch_bounds__(256) k_gemv_q8_0(GemvArgs g) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint64_t *bar = (uint64_t *)sm;
+  const int R = g.R;
+  const size_t act_row = (size_t)g.nb * 36;
+  uint8_t *wsm = sm + 16;
+  uint8_t *asm_ = wsm + ((R * g.row_bytes + 15) & ~(size_t)15) + 16;
+  const size_t tile0 = (size_t)blockIdx.x * R;
+  const int rows_here = (int)min((size_t)R, g.nrows - tile0);
+  const uint8_t *wsrc = g.w + (g.r0 + tile0) * g.row_bytes;
+  const size_t wbytes = (size_t)rows_here * g.row_bytes;
+  const bool bulk = rv_bulk_ok(wsrc, wsm, wbytes);
+  if (threadIdx.x == 0) mbar_init(bar, 1);
+  __syncthreads();
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(bar, (uint32_t)wbytes);
+      bulk_g2s(wsm, wsrc, (uint32_t)wbytes, bar);
+    }
+  } else {
+    rv_copy_bytes_block(wsm, wsrc, wbytes);
+  }
+  const int r = threadIdx.x >> 3, lane = threadIdx.x & 7;
+  const int rr = r < rows_here ? r : 0;  // idle rows compute row 0, never store
+  const uint8_t *wrow = wsm + (size_t)rr * g.row_bytes;
+  bool ok = true;
+  for (size_t a0 = 0; a0 < g.n_acts; a0 += MT) {
+    const int mt = (int)min((size_t)MT, g.n_acts - a0);
+    __syncthreads();  // previous chunk fully consumed
+    {
+      const uint32_t *src = (const uint32_t *)(g.acts + a0 * act_row);
+      uint32_t *dst = (uint32_t *)asm_;
+      const size_t words = (size_t)mt * act_row / 4;
+      for (size_t k = threadIdx.x; k < words; k += blockDim.x) dst[k] = src[k];
+    }
+    if (a0 == 0 && bulk) ok = mbar_wait_bounded(bar, 0);
+    __syncthreads();
+    if (!ok) return;
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) acc[m] = 0.0f;
+    for (int b = 0; b < g.nb; b++) {
+      const uint16_t *blk = (const uint16_t *)(wrow + (size_t)b * 34);  // 34-byte blocks: 2-byte aligned
+      const float wd = h2f(blk[0]);
+      const int w4 = (int)((uint32_t)blk[1 + 2 * lane] | ((uint32_t)blk[2 + 2 * lane] << 16));
+#pragma unroll
+      for (int m = 0; m < MT; m++)
+        if (m < mt) {
+          const uint8_t *ab = asm_ + m * act_row + (size_t)b * 36;
+          const int s = __dp4a(w4, *(const int *)(ab + 4 + 4 * lane), 0);
+          acc[m] = __fmaf_rn(__fmul_rn(wd, *(const float *)ab), (float)s, acc[m]);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      float s = __fadd_rn(acc[m], __shfl_xor_sync(0xffffffffu, acc[m], 4));
+      s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
+      s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+      if (lane == 0 && r < rows_here && m < mt) g.out[(tile0 + r) * g.n_acts + a0 + m] = s;
+    }
+  }
+}
+
+// ------------------------------------------------------- dequantization
+// dequant.rs:28-147, one thread per output value, f32 expressions with the
+// reference's roundings (no contraction).  Row i of the output is weight
+// row rows[i] (or i when rows is null); an id past out_dim writes zeros
+// and sets the device error word.
+template <int FMT>
+__global__ void k_dequant_rows(const uint8_t *__restrict__ w, size_t row_bytes, size_t in_dim, size_t out_dim,
+                               const uint32_t *__restrict__ rows, size_t n_rows, float *__restrict__ out) {
+  const size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n_rows * in_dim) return;
+  const size_t i = e / in_dim, c = e % in_dim;
+  const size_t row = rows ? rows[i] : i;
+  if (row >= out_dim) {
+    if (c == 0) rv_dev_fail(RV_ERR_TOKEN_OUT_OF_RANGE);
+    out[e] = 0.0f;
+    return;
+  }
+  const uint8_t *wr = w + row * row_bytes;
+  float v;
+  if constexpr (FMT == RV_Q8_0) {
+    const uint8_t *blk = wr + (c >> 5) * 34;
+    v = __fmul_rn(h2f((uint16_t)(blk[0] | (blk[1] << 8))), (float)(int8_t)blk[2 + (c & 31)]);
+  } else if constexpr (FMT == RV_Q6_K) {
+    const uint8_t *blk = wr + (c >> 8) * 210;
+    const int p = (int)(c & 255), half = p >> 7, quarter = (p & 127) >> 5, l = p & 31;
+    const uint8_t *ql = blk + 64 * half, *qh = blk + 128 + 32 * half, *sc = blk + 192 + 8 * half;
+    const int lo = (quarter & 1) ? ql[l + 32] : ql[l];
+    const int q = (((quarter >= 2) ? (lo >> 4) : (lo & 0xF)) | (((qh[l] >> (2 * quarter)) & 3) << 4)) - 32;
+    const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
+    v = __fmul_rn(__fmul_rn(d, (float)(int8_t)sc[(l >> 4) + 2 * quarter]), (float)q);
+  } else {
+    constexpr int BB = FMT == RV_Q4_K ? 144 : 176;
+    const uint8_t *blk = wr + (c >> 8) * BB;
+    const int p = (int)(c & 255), span = p >> 6, hi = (p >> 5) & 1, l = p & 31, j = 2 * span + hi;
+    const uint8_t *s = blk + 4;
+    int sc, m;
+    if (j < 4) {
+      sc = s[j] & 63;
+      m = s[j + 4] & 63;
+    } else {
+      sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+      m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+    const uint8_t qb = blk[(FMT == RV_Q4_K ? 16 : 48) + 32 * span + l];
+    int q = hi ? (qb >> 4) : (qb & 0xF);
+    if constexpr (FMT == RV_Q5_K) q += ((blk[16 + l] >> j) & 1) ? 16 : 0;
+    const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8))), dmin = h2f((uint16_t)(blk[2] | (blk[3] << 8)));
+    v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+  }
+  out[e] = v;
 }

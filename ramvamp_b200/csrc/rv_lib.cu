@@ -61,6 +61,7 @@ extern "C" const char *rv_status_name(int s) {
     case RV_ERR_NCCL: return "Nccl";
     case RV_ERR_TIMEOUT: return "Timeout";
     case RV_ERR_IO: return "Io";
+    case RV_ERR_TOKEN_OUT_OF_RANGE: return "TokenOutOfRange";
   }
   return "Unknown";
 }
@@ -100,6 +101,7 @@ static size_t sat_mul(size_t a, size_t b) {
 // kernel that uses it; rv_moe_create does it, so forward calls never do.
 static std::mutex g_init_mu;
 static bool g_dev_ready[64];
+static int g_dev_sms[64];  // multiprocessor count, read at set-up
 
 #define RV_ROUTE_SMEM_ONE_PER_SM (120u * 1024u)
 // Speculative decode: router rows per exact-chain CTA.  The expert grids
@@ -136,6 +138,12 @@ static int ensure_device(int dev) {
   cudaFuncSetAttribute(k_gemv<RV_Q5_K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv<RV_Q6_K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv<RV_Q6_K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv_lm_head, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv_lm_head, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  cudaFuncSetAttribute(k_gemv_q8_0<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv_q8_0<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  g_dev_sms[dev] = 148;
+  cudaDeviceGetAttribute(&g_dev_sms[dev], cudaDevAttrMultiProcessorCount, dev);
   cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_prologue, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_route_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
@@ -242,6 +250,20 @@ static int gemv_launch(int format, const uint8_t *weight, size_t row_bytes, size
   const size_t act_row = (size_t)g.nb * 292;
   if ((size_t)g.R * row_bytes + 8 * act_row > 180 * 1024)
     RV_FAIL(RV_ERR_UNIMPLEMENTED, "gemv: rows of %zu bytes exceed the staged-tile limit", row_bytes);
+  // lm_head shape (Q6_K, 8 blocks per row, one activation row, more tiles
+  // than two waves): the streaming kernel.  Its bulk copies need a
+  // 16-byte-aligned first row (rows are 1,680 = 105 x 16 bytes).
+  int dev = 0;
+  RV_CUDA(cudaGetDevice(&dev));
+  const int sms = g_dev_sms[dev] > 0 ? g_dev_sms[dev] : 148;
+  const size_t lmh_tiles = (g.nrows + RV_LMH_ROWS - 1) / RV_LMH_ROWS;
+  if (format == RV_Q6_K && g.nb == 8 && n_acts == 1 && ((uintptr_t)(weight + r0 * row_bytes) & 15) == 0 &&
+      lmh_tiles > (size_t)2 * sms) {
+    const size_t smem = 64 + (size_t)RV_LMH_STAGES * RV_LMH_ROWS * row_bytes;
+    k_gemv_lm_head<<<(unsigned)std::min(lmh_tiles, (size_t)2 * sms), RV_LMH_ROWS * 8, smem, s>>>(g);
+    RV_LAUNCH_CHECK();
+    return RV_OK;
+  }
   switch (format) {
     case RV_Q4_K: launch_gemv<RV_Q4_K>(g, s); break;
     case RV_Q5_K: launch_gemv<RV_Q5_K>(g, s); break;
@@ -282,6 +304,138 @@ extern "C" int rv_gemv_q8_k_batched(int format, const uint8_t *weight, size_t we
   if (rc) return rc;
   return gemv_launch(format, weight, rb, in_dim, acts, n_acts, row_start, row_end, out,
                      (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------------------ Q8_0
+extern "C" int rv_quantize_row_q8_0(const float *x, size_t n, rv_block_q8_0 *out, size_t out_blocks,
+                                    rv_stream stream) {
+  if (n != sat_mul(out_blocks, 32))
+    RV_FAIL(RV_ERR_QUANTIZE_LEN_MISMATCH, "Q8_0 quantize: %zu input floats do not fill %zu output blocks exactly",
+            n, out_blocks);
+  if (out_blocks == 0) return RV_OK;
+  if (!x || !out || ((uintptr_t)x & 3) || ((uintptr_t)out & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "quantize_row_q8_0: null or misaligned pointer");
+  const size_t grid = (out_blocks + 7) / 8;
+  k_quantize_q8_0<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(x, (uint8_t *)out, out_blocks);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+// gemv.rs:212-264 (validate) for Format::Q8_0, same checks and precedence.
+static int validate_gemv_q8_0(const char *what, size_t weight_len, size_t in_dim, size_t out_dim,
+                              size_t acts_len, size_t n_acts, size_t r0, size_t r1, size_t out_len,
+                              size_t *row_bytes) {
+  int rc = rv_row_bytes(RV_Q8_0, in_dim, row_bytes);
+  if (rc) return rc;
+  if (sat_mul(*row_bytes, out_dim) != weight_len)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "%s: weight bytes vs rows (%zu vs %zu)", what, weight_len,
+            sat_mul(*row_bytes, out_dim));
+  if (r0 > r1) RV_FAIL(RV_ERR_LENGTH_MISMATCH, "gemv rows: row range start vs end (%zu vs %zu)", r0, r1);
+  if (r1 > out_dim)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "gemv rows: row range end vs out_dim (%zu vs %zu)", r1, out_dim);
+  if (out_len != sat_mul(r1 - r0, n_acts))
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "%s: out vs range (%zu vs %zu)", what, out_len, sat_mul(r1 - r0, n_acts));
+  const size_t wb = sat_mul(in_dim / 32, n_acts);
+  if (wb != acts_len)
+    RV_FAIL(RV_ERR_BLOCK_COUNT_MISMATCH, "dot length mismatch: weight row has %zu blocks, activations %zu", wb,
+            acts_len);
+  return RV_OK;
+}
+
+static int gemv_q8_0_launch(const uint8_t *weight, size_t row_bytes, size_t in_dim, const rv_block_q8_0 *acts,
+                            size_t n_acts, size_t r0, size_t r1, float *out, cudaStream_t s) {
+  if (n_acts == 0 || r1 == r0) return RV_OK;
+  if (!weight || !acts || !out || ((uintptr_t)weight & 1) || ((uintptr_t)acts & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "gemv_q8_0: null pointer, weight not 2-byte or activations not 4-byte aligned");
+  int rc = ensure_current_device();
+  if (rc) return rc;
+  GemvArgs g;
+  g.w = weight;
+  g.row_bytes = row_bytes;
+  g.nb = (int)(in_dim / 32);
+  g.r0 = r0;
+  g.nrows = r1 - r0;
+  g.acts = (const uint8_t *)acts;
+  g.n_acts = n_acts;
+  g.out = out;
+  // Rows per CTA: as many as fit, but at least two CTAs per SM while the
+  // matrix allows it (the attention matrices have only 512-4096 rows).
+  int R = row_bytes <= 2048 ? 32 : row_bytes <= 4096 ? 16 : 8;
+  while (R > 4 && (g.nrows + R - 1) / R < 2 * 148) R /= 2;
+  g.R = R;
+  const size_t act_row = (size_t)g.nb * 36;
+  const int mt = n_acts > 1 ? 8 : 1;
+  const size_t smem = 16 + ((R * row_bytes + 15) & ~(size_t)15) + 16 + mt * act_row + 16;
+  if (smem > 200 * 1024)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "gemv_q8_0: rows of %zu bytes exceed the staged-tile limit", row_bytes);
+  const unsigned grid = (unsigned)((g.nrows + R - 1) / R);
+  if (mt == 1) k_gemv_q8_0<1><<<grid, R * 8, smem, s>>>(g);
+  else k_gemv_q8_0<8><<<grid, R * 8, smem, s>>>(g);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_gemv_q8_0(const uint8_t *weight, size_t weight_len, size_t in_dim, size_t out_dim,
+                            const rv_block_q8_0 *acts, size_t acts_len, float *out, size_t out_len,
+                            rv_stream stream) {
+  size_t rb = 0;
+  int rc = validate_gemv_q8_0("gemv_q8_0", weight_len, in_dim, out_dim, acts_len, 1, 0, out_dim, out_len, &rb);
+  if (rc) return rc;
+  return gemv_q8_0_launch(weight, rb, in_dim, acts, 1, 0, out_dim, out, (cudaStream_t)stream);
+}
+
+extern "C" int rv_gemv_q8_0_rows(const uint8_t *weight, size_t weight_len, size_t in_dim, size_t out_dim,
+                                 const rv_block_q8_0 *acts, size_t acts_len, size_t row_start, size_t row_end,
+                                 float *out, size_t out_len, rv_stream stream) {
+  size_t rb = 0;
+  int rc = validate_gemv_q8_0("gemv_q8_0_rows", weight_len, in_dim, out_dim, acts_len, 1, row_start, row_end,
+                              out_len, &rb);
+  if (rc) return rc;
+  return gemv_q8_0_launch(weight, rb, in_dim, acts, 1, row_start, row_end, out, (cudaStream_t)stream);
+}
+
+extern "C" int rv_gemv_q8_0_batched(const uint8_t *weight, size_t weight_len, size_t in_dim, size_t out_dim,
+                                    const rv_block_q8_0 *acts, size_t acts_len, size_t n_acts, size_t row_start,
+                                    size_t row_end, float *out, size_t out_len, rv_stream stream) {
+  size_t rb = 0;
+  int rc = validate_gemv_q8_0("gemv_q8_0_batched", weight_len, in_dim, out_dim, acts_len, n_acts, row_start,
+                              row_end, out_len, &rb);
+  if (rc) return rc;
+  return gemv_q8_0_launch(weight, rb, in_dim, acts, n_acts, row_start, row_end, out, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------- dequantization
+extern "C" int rv_dequantize_rows(int format, const uint8_t *weight, size_t weight_len, size_t in_dim,
+                                  size_t out_dim, const uint32_t *rows, size_t n_rows, float *out, size_t out_len,
+                                  rv_stream stream) {
+  if (format != RV_Q4_K && format != RV_Q5_K && format != RV_Q6_K && format != RV_Q8_0)
+    RV_FAIL(RV_ERR_UNSUPPORTED_FORMAT, "dequantize_rows: unsupported weight format %d", format);
+  size_t rb = 0;
+  int rc = rv_row_bytes(format, in_dim, &rb);
+  if (rc) return rc;
+  if (sat_mul(rb, out_dim) != weight_len)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "dequantize_rows: weight bytes vs rows (%zu vs %zu)", weight_len,
+            sat_mul(rb, out_dim));
+  if (out_len != sat_mul(n_rows, in_dim))
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "dequantize_rows: out vs rows x in_dim (%zu vs %zu)", out_len,
+            sat_mul(n_rows, in_dim));
+  if (!rows && n_rows > out_dim)
+    RV_FAIL(RV_ERR_TOKEN_OUT_OF_RANGE, "dequantize_rows: %zu rows of a %zu-row matrix", n_rows, out_dim);
+  if (out_len == 0) return RV_OK;
+  if (!weight || !out || ((uintptr_t)out & 3) || ((uintptr_t)rows & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "dequantize_rows: null or misaligned pointer");
+  rc = ensure_current_device();
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned grid = (unsigned)((out_len + 255) / 256);
+  switch (format) {
+    case RV_Q4_K: k_dequant_rows<RV_Q4_K><<<grid, 256, 0, s>>>(weight, rb, in_dim, out_dim, rows, n_rows, out); break;
+    case RV_Q5_K: k_dequant_rows<RV_Q5_K><<<grid, 256, 0, s>>>(weight, rb, in_dim, out_dim, rows, n_rows, out); break;
+    case RV_Q6_K: k_dequant_rows<RV_Q6_K><<<grid, 256, 0, s>>>(weight, rb, in_dim, out_dim, rows, n_rows, out); break;
+    default: k_dequant_rows<RV_Q8_0><<<grid, 256, 0, s>>>(weight, rb, in_dim, out_dim, rows, n_rows, out); break;
+  }
+  RV_LAUNCH_CHECK();
+  return RV_OK;
 }
 
 // gemv.rs:747-823: rows of the concatenated row spaces, part by part.
