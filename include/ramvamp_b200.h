@@ -60,7 +60,9 @@ typedef enum rv_status {
   RV_ERR_NCCL = 15,                        /* a collective failed */
   RV_ERR_TIMEOUT = 16,                     /* a bounded device-side wait ran out */
   RV_ERR_IO = 17,                          /* IoError::Io: a file could not be opened or read */
-  RV_ERR_TOKEN_OUT_OF_RANGE = 18           /* ModelError::TokenOutOfRange (a row id past the matrix) */
+  RV_ERR_TOKEN_OUT_OF_RANGE = 18,          /* ModelError::TokenOutOfRange (a row id past the matrix) */
+  RV_ERR_POSITION_MISMATCH = 19,           /* ForwardError::PositionMismatch (position != cached length) */
+  RV_ERR_CAPACITY_EXCEEDED = 20            /* KvError::CapacityExceeded (the layer's cache is full) */
 } rv_status;
 
 /* Quantization formats (kernels/quants/mod.rs:57-70). */
@@ -462,6 +464,70 @@ RV_API int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_layout
                                  uint32_t *topk_ids, float *topk_weights, rv_stream stream);
 
 /* ------------------------------------------------ synthetic inputs */
+/* ---------------------------------------------------------- attention */
+/* The attention half of a decode step (model/forward.rs:2614-2631): the
+ * KV cache of every layer (f16, the reference's KvCache, kv/mod.rs), the
+ * NeoX rotation table and scratch, on one device. */
+typedef struct rv_attn_config {
+  uint32_t n_layers;
+  uint32_t n_heads;       /* query heads (32 for Qwen3-30B-A3B) */
+  uint32_t n_kv_heads;    /* key/value heads (4); n_heads % n_kv_heads == 0 */
+  uint32_t head_dim;      /* 128; even, a multiple of 8, <= 256 */
+  uint32_t max_positions; /* cache capacity per layer */
+  float rope_theta;       /* the manifest's rope_theta as f32 (model/forward.rs:2474) */
+  float eps;              /* the QK-norm epsilon (the layer norms' eps) */
+} rv_attn_config;
+
+typedef struct rv_attn rv_attn;
+
+/* Allocates the caches (2 * n_layers * max_positions * n_kv_heads *
+ * head_dim f16) and scratch, and builds the rotation table: for every
+ * position p < max_positions and i < head_dim/2, (cos, sin) of
+ * p * theta^(-2i/head_dim) formed in f64 with the host libm and rounded to
+ * f32, exactly as rope.rs:30-45 computes them per call. */
+RV_API int rv_attn_create(int device, const rv_attn_config *cfg, rv_attn **out);
+RV_API void rv_attn_destroy(rv_attn *a);
+/* KvCache::len / clear (kv/mod.rs). */
+RV_API int rv_attn_len(const rv_attn *a, uint32_t layer, uint32_t *len_out);
+RV_API int rv_attn_clear(rv_attn *a);
+/* Device pointers to one layer's caches, [max_positions][n_kv_heads * head_dim]. */
+RV_API int rv_attn_cache(const rv_attn *a, uint32_t layer, const uint16_t **k_out, const uint16_t **v_out);
+/* Copies rows 0..positions-1 of one layer's caches to k_out / v_out
+ * (device, positions * n_kv_heads * head_dim halves each), on `stream`. */
+RV_API int rv_attn_copy_cache(const rv_attn *a, uint32_t layer, uint32_t positions, uint16_t *k_out, uint16_t *v_out,
+                       rv_stream stream);
+
+/* One layer of one decode step (forward.rs:2614-2631): per-head
+ * QK-RMSNorm of q and k (norm.rs:72-90, weights q_norm / k_norm
+ * [head_dim]), NeoX RoPE of both at `position` (rope.rs:80-111), the f16
+ * append of k and v (kv/mod.rs:336-373), then decode attention over
+ * positions 0..position (attention.rs:1075-1303, scale 1/sqrt(head_dim) in
+ * f32).  q [n_heads*head_dim] and k [n_kv_heads*head_dim] are updated in
+ * place (normed and rotated), as the reference does; v is read; out
+ * [n_heads*head_dim] receives the attention output.  All device pointers.
+ * RV_ERR_POSITION_MISMATCH unless position == rv_attn_len(layer);
+ * RV_ERR_CAPACITY_EXCEEDED when the layer is full; nothing is written then.
+ * Bit-identical to the reference except that its f64 exp (glibc) and
+ * CUDA's may differ in the last bit, which changes an f32 probability only
+ * when the exact value lies within ~2^-29 ulp of a rounding boundary. */
+RV_API int rv_attn_decode(rv_attn *a, uint32_t layer, uint32_t position, float *q, float *k, const float *v,
+                   const float *q_norm, const float *k_norm, float *out, rv_stream stream);
+
+/* Replaces primitives::rope_neox_heads / Backend::rope_neox_heads
+ * (kernels/primitives/rope.rs:80-111): x [n_heads*head_dim] (device)
+ * rotated in place at `position`.  RV_ERR_INVALID_HEAD_DIM for a zero or odd
+ * head_dim; RV_ERR_LENGTH_MISMATCH when x_len != n_heads*head_dim. */
+RV_API int rv_rope_neox_heads(float *x, size_t x_len, size_t n_heads, size_t head_dim, uint32_t position,
+                       float theta, rv_stream stream);
+
+/* Replaces kernels::attention::decode_attention (attention.rs:426-438,
+ * body :1075-1303) over caller caches: q [n_heads*head_dim] f32, k_cache /
+ * v_cache [positions][n_kv_heads*head_dim] f16 bits, out [n_heads*head_dim];
+ * scratch: 2*n_heads*positions floats.  All device pointers. */
+RV_API int rv_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, size_t positions,
+                 size_t n_heads, size_t n_kv_heads, size_t head_dim, float scale, float *scratch,
+                 size_t scratch_len, float *out, rv_stream stream);
+
 /* Seeded N(0, sigma^2)-like values: element i is the Irwin-Hall sum of
  * twelve 24-bit uniforms drawn from SplitMix64(seed, offset + i), so the
  * same (seed, offset) gives the same floats on every device and host.

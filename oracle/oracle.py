@@ -35,6 +35,7 @@ ERRORS = {
     4: "QuantizeLenMismatch",
     5: "LengthMismatch",
     6: "Empty",
+    7: "InvalidHeadDim",
     9: "UnsupportedFormat",
     20: "RoutedExpertOutOfRange",
 }
@@ -100,6 +101,10 @@ def _declare(L):
     L.or_gemv.argtypes = [I32, P, SZ, SZ, SZ, P, SZ, SZ, SZ, P, SZ, I32, I32]
     L.or_lcg_next_u64.argtypes = [P]; L.or_lcg_next_u64.restype = ctypes.c_uint64
     L.or_lcg_fill_f32.argtypes = [P, P, SZ, ctypes.c_float]
+    L.or_rope_neox_heads.argtypes = [P, SZ, SZ, ctypes.c_uint32, ctypes.c_float]
+    L.or_rope_factors.argtypes = [SZ, ctypes.c_uint32, ctypes.c_float, P, P]
+    L.or_attention.argtypes = [P, P, P, SZ, SZ, SZ, SZ, ctypes.c_float, P]
+    L.or_attn_decode_step.argtypes = [P, P, P, P, P, P, P, SZ, SZ, SZ, SZ, ctypes.c_float, ctypes.c_float, P]
     L.or_quantize_row_q8_0.argtypes = [P, SZ, P, SZ, I32]
     L.or_vec_dot_q8_0.argtypes = [P, SZ, P, SZ, I32, P]
     L.or_gemv_q8_0.argtypes = [P, SZ, SZ, SZ, P, SZ, SZ, SZ, SZ, P, SZ, I32, I32]
@@ -230,6 +235,52 @@ def gemv_q8_0(w, in_dim: int, out_dim: int, acts, n_acts: int = 1, rows=None,
     _check(lib().or_gemv_q8_0(_p(w), w.size, in_dim, out_dim, _p(acts), acts.size, n_acts, r0, r1, _p(out),
                               out.size, default_impl() if impl is None else impl, threads), "gemv_q8_0")
     return out
+
+
+# --------------------------------------------------------- attention
+def rope_neox_heads(x, n_heads: int, head_dim: int, position: int, theta: float) -> np.ndarray:
+    """rope.rs:80-111 (returns a rotated copy)."""
+    x = np.array(x, dtype=np.float32, copy=True)
+    _check(lib().or_rope_neox_heads(_p(x), n_heads, head_dim, position, ctypes.c_float(theta)), "rope_neox_heads")
+    return x
+
+
+def rope_factors(head_dim: int, position: int, theta: float):
+    """The f32 (cos, sin) pairs rope.rs:30-45 forms at one position."""
+    c = np.zeros(head_dim // 2, np.float32)
+    s = np.zeros(head_dim // 2, np.float32)
+    lib().or_rope_factors(head_dim, position, ctypes.c_float(theta), _p(c), _p(s))
+    return c, s
+
+
+def attention(q, k_cache, v_cache, positions: int, n_heads: int, n_kv_heads: int, head_dim: int,
+              scale: float) -> np.ndarray:
+    """attention.rs:1075-1303 (scalar arm); caches are f16 bits [pos][kv_dim]."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k_cache = np.ascontiguousarray(k_cache, dtype=np.uint16)
+    v_cache = np.ascontiguousarray(v_cache, dtype=np.uint16)
+    out = np.zeros(n_heads * head_dim, np.float32)
+    _check(lib().or_attention(_p(q), _p(k_cache), _p(v_cache), positions, n_heads, n_kv_heads, head_dim,
+                              ctypes.c_float(scale), _p(out)), "attention")
+    return out
+
+
+def attn_decode_step(q, k, v, q_norm, k_norm, k_cache, v_cache, position: int, n_heads: int, n_kv_heads: int,
+                     head_dim: int, eps: float, theta: float):
+    """model/forward.rs:2614-2631: QK-norm, RoPE, f16 append (into the given
+    cache arrays, in place), attention.  Returns (out, q_rotated, k_rotated)."""
+    q = np.array(q, dtype=np.float32, copy=True)
+    k = np.array(k, dtype=np.float32, copy=True)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    qn = np.ascontiguousarray(q_norm, dtype=np.float32)
+    kn = np.ascontiguousarray(k_norm, dtype=np.float32)
+    assert k_cache.dtype == np.uint16 and v_cache.dtype == np.uint16
+    assert k_cache.flags.c_contiguous and v_cache.flags.c_contiguous
+    out = np.zeros(n_heads * head_dim, np.float32)
+    _check(lib().or_attn_decode_step(_p(q), _p(k), _p(v), _p(qn), _p(kn), _p(k_cache), _p(v_cache), position,
+                                     n_heads, n_kv_heads, head_dim, ctypes.c_float(eps), ctypes.c_float(theta),
+                                     _p(out)), "attn_decode_step")
+    return out, q, k
 
 
 # -------------------------------------------------------------- Lcg

@@ -914,6 +914,100 @@ void or_quantize_row_q8_0_test(const float *x, size_t n, uint8_t *out) {
   }
 }
 
+/* ------------------------------------------------------------- attention */
+/* rope.rs:30-45 (rotate_head): f64 inverse frequency and angle, libm sin and
+ * cos, applied in f32 as separate multiplies. */
+static void rope_rotate_head(float *head, size_t half, uint32_t position, float theta) {
+  double pos = (double)position, base = (double)theta, dim = (double)(2 * half);
+  for (size_t i = 0; i < half; i++) {
+    double inv_freq = pow(base, -2.0 * (double)i / dim);
+    double ang = pos * inv_freq;
+    float sn = (float)sin(ang), cs = (float)cos(ang);
+    float x0 = head[i], x1 = head[i + half];
+    head[i] = x0 * cs - x1 * sn;
+    head[i + half] = x0 * sn + x1 * cs;
+  }
+}
+
+/* rope.rs:80-111 (rope_neox_heads) */
+int or_rope_neox_heads(float *x, size_t n_heads, size_t head_dim, uint32_t position, float theta) {
+  if (head_dim == 0 || head_dim % 2) return OR_ERR_INVALID_HEAD_DIM;
+  for (size_t h = 0; h < n_heads; h++) rope_rotate_head(x + h * head_dim, head_dim / 2, position, theta);
+  return OR_OK;
+}
+
+/* The f32 rotation factors rotate_head forms for one position. */
+void or_rope_factors(size_t head_dim, uint32_t position, float theta, float *cos_out, float *sin_out) {
+  double pos = (double)position, base = (double)theta, dim = (double)head_dim;
+  for (size_t i = 0; i < head_dim / 2; i++) {
+    double ang = pos * pow(base, -2.0 * (double)i / dim);
+    cos_out[i] = (float)cos(ang);
+    sin_out[i] = (float)sin(ang);
+  }
+}
+
+/* attention.rs:1075-1303, the scalar arm (the AVX2 + F16C arm is pinned
+ * bit-identical to it): per kv head, scores[g][t] = scale * (q_g . K[t])
+ * with one f32 accumulator over i ascending (separate multiply and add),
+ * softmax per query head, out[g][i] = sum over t ascending of w_t * V[t][i].
+ * Caches are f16 bits, [positions][n_kv_heads * head_dim]. */
+int or_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, size_t positions,
+                 size_t n_heads, size_t n_kv_heads, size_t head_dim, float scale, float *out) {
+  if (positions == 0 || n_kv_heads == 0 || head_dim == 0) return OR_ERR_EMPTY;
+  if (n_heads % n_kv_heads) return OR_ERR_LENGTH_MISMATCH;
+  size_t group = n_heads / n_kv_heads, kv_dim = n_kv_heads * head_dim;
+  float *scores = (float *)malloc(group * positions * sizeof(float));
+  float *buf = (float *)malloc(head_dim * sizeof(float));
+  if (!scores || !buf) { free(scores); free(buf); return OR_ERR_EMPTY; }
+  for (size_t kvh = 0; kvh < n_kv_heads; kvh++) {
+    const float *qg = q + kvh * group * head_dim;
+    float *og = out + kvh * group * head_dim;
+    size_t col = kvh * head_dim;
+    for (size_t t = 0; t < positions; t++) {
+      for (size_t i = 0; i < head_dim; i++) buf[i] = or_f16_to_f32(k_cache[t * kv_dim + col + i]);
+      for (size_t g = 0; g < group; g++) {
+        float acc = 0.0f;
+        for (size_t i = 0; i < head_dim; i++) acc += qg[g * head_dim + i] * buf[i];
+        scores[g * positions + t] = scale * acc;
+      }
+    }
+    for (size_t g = 0; g < group; g++) or_softmax(scores + g * positions, positions);
+    for (size_t k = 0; k < group * head_dim; k++) og[k] = 0.0f;
+    for (size_t t = 0; t < positions; t++) {
+      for (size_t i = 0; i < head_dim; i++) buf[i] = or_f16_to_f32(v_cache[t * kv_dim + col + i]);
+      for (size_t g = 0; g < group; g++) {
+        float w = scores[g * positions + t];
+        for (size_t i = 0; i < head_dim; i++) og[g * head_dim + i] += w * buf[i];
+      }
+    }
+  }
+  free(scores);
+  free(buf);
+  return OR_OK;
+}
+
+/* The attention half of one decode step (model/forward.rs:2614-2631): per-head
+ * QK-RMSNorm of q and k (norm.rs:72-90, shared [head_dim] weights), NeoX RoPE
+ * of both at `position`, the f16 append of k and v at row `position`
+ * (kv/mod.rs:336-373), then attention over positions 0..position.  q and k
+ * are updated in place, as the reference does. */
+int or_attn_decode_step(float *q, float *k, const float *v, const float *q_norm, const float *k_norm,
+                        uint16_t *k_cache, uint16_t *v_cache, size_t position, size_t n_heads, size_t n_kv_heads,
+                        size_t head_dim, float eps, float theta, float *out) {
+  for (size_t h = 0; h < n_heads; h++) or_rmsnorm(q + h * head_dim, q_norm, head_dim, eps, q + h * head_dim);
+  for (size_t h = 0; h < n_kv_heads; h++) or_rmsnorm(k + h * head_dim, k_norm, head_dim, eps, k + h * head_dim);
+  int rc = or_rope_neox_heads(q, n_heads, head_dim, (uint32_t)position, theta);
+  if (rc) return rc;
+  or_rope_neox_heads(k, n_kv_heads, head_dim, (uint32_t)position, theta);
+  size_t kv_dim = n_kv_heads * head_dim;
+  for (size_t i = 0; i < kv_dim; i++) {
+    k_cache[position * kv_dim + i] = or_f32_to_f16(k[i]);
+    v_cache[position * kv_dim + i] = or_f32_to_f16(v[i]);
+  }
+  float scale = 1.0f / sqrtf((float)head_dim);
+  return or_attention(q, k_cache, v_cache, position + 1, n_heads, n_kv_heads, head_dim, scale, out);
+}
+
 /* ------------------------------------------------------------------ Lcg */
 /* test_support.rs:23-39 */
 uint64_t or_lcg_next_u64(uint64_t *s) {

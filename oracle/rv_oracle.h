@@ -44,6 +44,7 @@ enum {
   OR_ERR_QUANTIZE_LEN_MISMATCH = 4,
   OR_ERR_LENGTH_MISMATCH = 5,
   OR_ERR_EMPTY = 6,
+  OR_ERR_INVALID_HEAD_DIM = 7,
   OR_ERR_UNSUPPORTED_FORMAT = 9,
   OR_ERR_ROUTED_OUT_OF_RANGE = 20
 };
@@ -131,6 +132,16 @@ int or_gemv_q8_0(const uint8_t *w, size_t w_len, size_t in_dim, size_t out_dim, 
                  int threads);
 /* test_support.rs:221-234 */
 void or_quantize_row_q8_0_test(const float *x, size_t n, uint8_t *out);
+
+/* Attention half of the decode step: rope.rs:30-111, attention.rs:1075-1303,
+ * kv/mod.rs:336-373, model/forward.rs:2614-2631. */
+int or_rope_neox_heads(float *x, size_t n_heads, size_t head_dim, uint32_t position, float theta);
+void or_rope_factors(size_t head_dim, uint32_t position, float theta, float *cos_out, float *sin_out);
+int or_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, size_t positions,
+                 size_t n_heads, size_t n_kv_heads, size_t head_dim, float scale, float *out);
+int or_attn_decode_step(float *q, float *k, const float *v, const float *q_norm, const float *k_norm,
+                        uint16_t *k_cache, uint16_t *v_cache, size_t position, size_t n_heads, size_t n_kv_heads,
+                        size_t head_dim, float eps, float theta, float *out);
 
 /* test_support.rs:23-39 */
 uint64_t or_lcg_next_u64(uint64_t *state);

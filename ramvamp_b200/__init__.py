@@ -12,6 +12,9 @@ stream.  Names and error kinds follow the reference:
 - ``gemv_q8_0`` / ``_rows`` / ``_batched``   kernels/gemv.rs:544, 579, 616
 - ``dequantize_rows`` / ``embed``          kernels/quants/dequant.rs:28-147,
                                              model/weights.rs:371-384
+- ``rope_neox_heads``, ``attention``       kernels/primitives/rope.rs:80,
+                                             kernels/attention.rs:426
+- ``AttnEngine`` (KV cache + decode step)  kv/mod.rs, model/forward.rs:2614-2631
 - ``CudaBackend`` (the ``Backend`` trait)    kernels/backend.rs:23-59
 - ``ExpertTable`` (``ExpertStream`` API)      io/stream.rs:1472-2160
 - ``rvmp.load_expert_table`` (install files) format/layout.rs, io/expert.rs
@@ -39,6 +42,7 @@ __all__ = [
     "LayerLayout", "qwen3_layer_layout", "QWEN3_Q6K_DOWN_LAYERS", "synth_normal",
     "quantize_weights", "EXACT", "TENSOR", "lib", "Q8_0_BYTES", "quantize_row_q8_0", "gemv_q8_0",
     "gemv_q8_0_rows", "gemv_q8_0_batched", "dequantize_rows", "embed", "device_status",
+    "rope_neox_heads", "attention", "AttnEngine",
 ]
 
 Q8K_BYTES = 292
@@ -184,6 +188,25 @@ def embed(embedding, hidden, vocab, tokens: torch.Tensor, format=None, out=None)
     return dequantize_rows(fmt, embedding, hidden, vocab, rows=tokens, out=out)
 
 
+def rope_neox_heads(x: torch.Tensor, n_heads: int, head_dim: int, position: int, theta_base: float):
+    """rope.rs:80-111, in place on a device tensor."""
+    _check(lib().rv_rope_neox_heads(_p(x), x.numel(), n_heads, head_dim, position, theta_base, _stream()))
+    return x
+
+
+def attention(q, k_cache, v_cache, positions: int, n_heads: int, n_kv_heads: int, head_dim: int, scale: float,
+              out: Optional[torch.Tensor] = None, scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """kernels/attention.rs:426-438 over device caches (f16 bits as int16 /
+    uint16 / float16 tensors, [positions][n_kv_heads * head_dim])."""
+    if out is None:
+        out = torch.empty(n_heads * head_dim, dtype=torch.float32, device=q.device)
+    if scratch is None:
+        scratch = torch.empty(2 * n_heads * positions, dtype=torch.float32, device=q.device)
+    _check(lib().rv_attention(_p(q), _p(k_cache), _p(v_cache), positions, n_heads, n_kv_heads, head_dim, scale,
+                              _p(scratch), scratch.numel(), _p(out), _stream()))
+    return out
+
+
 @dataclass
 class FusedPart:
     """kernels/gemv.rs:655-686."""
@@ -263,7 +286,7 @@ class CudaBackend:
         return rmsnorm(x, weight, eps, out)
 
     def rope_neox_heads(self, x, n_heads, head_dim, position, theta_base):
-        raise KernelError(8, "Unimplemented: rope_neox_heads is not on the routed-expert path")
+        return rope_neox_heads(x, n_heads, head_dim, position, theta_base)
 
     def softmax(self, x):
         return softmax(x)
@@ -548,6 +571,64 @@ class MoeEngine:
         t = _lib.MoeTaps()
         _check(lib().rv_moe_get_taps(self.handle, ctypes.byref(t)))
         return t
+
+
+class AttnEngine:
+    """The attention half of a decode step on one device: the f16 KV cache
+    of every layer (kv/mod.rs ``KvCache``), the NeoX rotation table and
+    scratch.  ``decode`` is model/forward.rs:2614-2631 for one layer."""
+
+    def __init__(self, n_layers=48, n_heads=32, n_kv_heads=4, head_dim=128, max_positions=4096,
+                 rope_theta=1e7, eps=1e-6, device: int = 0):
+        self.cfg = _lib.AttnConfig(n_layers, n_heads, n_kv_heads, head_dim, max_positions, rope_theta, eps)
+        h = ctypes.c_void_p()
+        _check(lib().rv_attn_create(device, ctypes.byref(self.cfg), ctypes.byref(h)))
+        self.handle = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().rv_attn_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def len(self, layer: int) -> int:
+        n = ctypes.c_uint32()
+        _check(lib().rv_attn_len(self.handle, layer, ctypes.byref(n)))
+        return n.value
+
+    def clear(self):
+        _check(lib().rv_attn_clear(self.handle))
+
+    def cache(self, layer: int):
+        """(k, v) device addresses of one layer's caches."""
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        _check(lib().rv_attn_cache(self.handle, layer, ctypes.byref(k), ctypes.byref(v)))
+        return k.value, v.value
+
+    def cache_tensors(self, layer: int, positions: Optional[int] = None):
+        """Copies (k, v) of one layer's first `positions` rows, f16 bits as
+        int16 device tensors [positions][n_kv_heads * head_dim]."""
+        n = self.len(layer) if positions is None else positions
+        kv_dim = self.cfg.n_kv_heads * self.cfg.head_dim
+        k = torch.empty((n, kv_dim), dtype=torch.int16, device=f"cuda:{self.device}")
+        v = torch.empty_like(k)
+        _check(lib().rv_attn_copy_cache(self.handle, layer, n, _p(k), _p(v), _stream()))
+        return k, v
+
+    def decode(self, layer: int, position: int, q, k, v, q_norm, k_norm, out=None) -> torch.Tensor:
+        """QK-norm + RoPE of q and k (in place), f16 append of k and v at
+        `position`, attention over positions 0..position into `out`."""
+        if out is None:
+            out = torch.empty_like(q)
+        _check(lib().rv_attn_decode(self.handle, layer, position, _p(q), _p(k), _p(v), _p(q_norm), _p(k_norm),
+                                    _p(out), _stream()))
+        return out
 
 
 def device_status(device: int = 0) -> None:

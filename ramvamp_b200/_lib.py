@@ -27,6 +27,8 @@ STATUS_NAMES = {
     16: "Timeout",
     17: "Io",
     18: "TokenOutOfRange",
+    19: "PositionMismatch",
+    20: "CapacityExceeded",
 }
 
 
@@ -68,6 +70,11 @@ class MoeConfig(ctypes.Structure):
                 ("norm_topk_prob", ctypes.c_int32), ("eps", F32)]
 
 
+class AttnConfig(ctypes.Structure):
+    _fields_ = [("n_layers", U32), ("n_heads", U32), ("n_kv_heads", U32), ("head_dim", U32),
+                ("max_positions", U32), ("rope_theta", F32), ("eps", F32)]
+
+
 class MoeTaps(ctypes.Structure):
     _fields_ = [("normed", P), ("acts", P), ("acts_stride", SZ), ("logits", P), ("weights", P),
                 ("ids", P), ("index", P), ("index_start", P), ("swiglu", P), ("acts_moe", P),
@@ -92,6 +99,15 @@ SIGNATURES = {
     "rv_gemv_q8_0_rows": (I32, [P, SZ, SZ, SZ, P, SZ, SZ, SZ, P, SZ, P]),
     "rv_gemv_q8_0_batched": (I32, [P, SZ, SZ, SZ, P, SZ, SZ, SZ, SZ, P, SZ, P]),
     "rv_dequantize_rows": (I32, [I32, P, SZ, SZ, SZ, P, SZ, P, SZ, P]),
+    "rv_attn_create": (I32, [I32, ctypes.POINTER(AttnConfig), ctypes.POINTER(P)]),
+    "rv_attn_destroy": (None, [P]),
+    "rv_attn_len": (I32, [P, U32, ctypes.POINTER(U32)]),
+    "rv_attn_clear": (I32, [P]),
+    "rv_attn_cache": (I32, [P, U32, ctypes.POINTER(P), ctypes.POINTER(P)]),
+    "rv_attn_copy_cache": (I32, [P, U32, U32, P, P, P]),
+    "rv_attn_decode": (I32, [P, U32, U32, P, P, P, P, P, P, P]),
+    "rv_rope_neox_heads": (I32, [P, SZ, SZ, SZ, U32, F32, P]),
+    "rv_attention": (I32, [P, P, P, SZ, SZ, SZ, SZ, F32, P, SZ, P, P]),
     "rv_gemv_q8_k_fused_rows": (I32, [ctypes.POINTER(FusedPartC), SZ, SZ, SZ, P, SZ, P]),
     "rv_rmsnorm": (I32, [P, P, SZ, SZ, F32, P, P]),
     "rv_softmax": (I32, [P, SZ, SZ, P]),

@@ -1,0 +1,194 @@
+// rv_attn.cuh -- the attention half of a decode step on the GPU: per-head
+// QK-RMSNorm, NeoX RoPE, the f16 KV append and grouped-query attention over
+// the cached positions, each with the reference's float order
+// (model/forward.rs:2614-2631, kernels/primitives/{norm,rope,softmax}.rs,
+// kernels/attention.rs:1075-1303, kv/mod.rs:336-373).
+//
+// Rotation factors: the reference forms cos/sin of position * inv_freq in
+// f64 with the host libm (pow, sin, cos) and rounds them to f32.  The
+// engine builds that table once on the host with the same calls (the
+// frequency cache the reference's rope.rs describes) and the kernels read
+// row `position` of it, so the rotation is bit-identical.
+#pragma once
+#include "rv_kernels.cuh"
+
+struct AttnArgs {
+  float *q;              // [n_heads][hd], normed + rotated in place
+  float *k;              // [n_kv][hd], normed + rotated in place
+  const float *v;        // [n_kv][hd]
+  const float *q_norm;   // [hd]
+  const float *k_norm;   // [hd]
+  uint16_t *k_cache;     // this layer: [max_positions][n_kv * hd] f16 bits
+  uint16_t *v_cache;
+  const float2 *rot;     // [max_positions][hd / 2] (cos, sin)
+  float *scores;         // [n_heads][positions]
+  float *probs;          // [n_heads][positions]
+  float *out;            // [n_heads][hd]
+  int n_heads, n_kv, hd;
+  int position;          // the row appended; attention covers 0..position
+  float eps, scale;
+};
+
+// One CTA (hd threads) per head: CTAs 0..n_heads-1 take q heads, the rest
+// k heads (which also append k and v to the cache).  rmsnorm_in_place
+// (norm.rs:72-90): v * inv * w with inv from rms_inv_block (exact); then
+// rotate_head (rope.rs:30-45): x0*cos - x1*sin, x0*sin + x1*cos in f32.
+__global__ void __launch_bounds__(256) k_attn_prep(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  double *red = (double *)sm;
+  float *xs = (float *)(sm + 34 * sizeof(double));
+  const bool is_q = (int)blockIdx.x < a.n_heads;
+  const int head = is_q ? (int)blockIdx.x : (int)blockIdx.x - a.n_heads;
+  float *x = (is_q ? a.q : a.k) + (size_t)head * a.hd;
+  const float *w = is_q ? a.q_norm : a.k_norm;
+  const int i = threadIdx.x, half = a.hd >> 1;
+  for (int k = i; k < a.hd; k += blockDim.x) xs[k] = x[k];
+  __syncthreads();
+  const float inv = rms_inv_block(xs, (size_t)a.hd, a.eps, red);
+  for (int k = i; k < a.hd; k += blockDim.x) xs[k] = __fmul_rn(__fmul_rn(xs[k], inv), w[k]);
+  __syncthreads();
+  const float2 *rot = a.rot + (size_t)a.position * half;
+  const size_t kv_dim = (size_t)a.n_kv * a.hd;
+  for (int k = i; k < half; k += blockDim.x) {
+    const float2 cs = rot[k];
+    const float x0 = xs[k], x1 = xs[k + half];
+    const float y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+    const float y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+    x[k] = y0;
+    x[k + half] = y1;
+    if (!is_q) {
+      uint16_t *kc = a.k_cache + (size_t)a.position * kv_dim + (size_t)head * a.hd;
+      kc[k] = f32_to_f16_bits(y0);
+      kc[k + half] = f32_to_f16_bits(y1);
+    }
+  }
+  if (!is_q) {
+    uint16_t *vc = a.v_cache + (size_t)a.position * kv_dim + (size_t)head * a.hd;
+    const float *vh = a.v + (size_t)head * a.hd;
+    for (int k = i; k < a.hd; k += blockDim.x) vc[k] = f32_to_f16_bits(vh[k]);
+  }
+}
+
+// qk_scores_scalar (attention.rs): scores[h][t] = scale * (q_h . K[t]) with
+// one f32 accumulator over i ascending, separate multiply and add.  Grid
+// (n_heads, position tiles of 128); thread = position; q_h in shared
+// memory; the K row read 8 halves at a time.
+__global__ void __launch_bounds__(128) k_attn_scores(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  float *qs = (float *)sm;
+  const int h = blockIdx.x, group = a.n_heads / a.n_kv, kvh = h / group;
+  for (int k = threadIdx.x; k < a.hd; k += blockDim.x) qs[k] = a.q[(size_t)h * a.hd + k];
+  __syncthreads();
+  const int positions = a.position + 1;
+  const int t = blockIdx.y * blockDim.x + threadIdx.x;
+  if (t >= positions) return;
+  const size_t kv_dim = (size_t)a.n_kv * a.hd;
+  const uint4 *kr = (const uint4 *)(a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd);
+  float acc = 0.0f;
+  for (int c = 0; c < a.hd / 8; c++) {
+    const uint4 u = kr[c];
+    const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j], h2f((uint16_t)(wds[j] & 0xFFFFu))));
+      acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j + 1], h2f((uint16_t)(wds[j] >> 16))));
+    }
+  }
+  a.scores[(size_t)h * positions + t] = __fmul_rn(a.scale, acc);
+}
+
+// One CTA (hd threads) per query head: softmax over the positions
+// (softmax.rs:18-40: f32 max, e = exp(f64(s) - max) in f64, f32 copies, the
+// f64 sum in position order, f32 reciprocal), then v_reduce_scalar:
+// out[i] = sum over t ascending of p_t * V[t][i], separate multiply and add.
+// The f64 sum is taken in blocks; summation in any order of P positive
+// terms errs by at most (P-1)u of the sum, so block and serial sums differ by
+// at most 2(P-1)u: when f32(1/sum) is the same for every sum within that
+// bound, the blocked sum gives the serial result; otherwise thread 0 redoes
+// the serial sum.
+__global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
+  __shared__ double red[34];
+  __shared__ float s_max, s_inv;
+  const int h = blockIdx.x, group = a.n_heads / a.n_kv, kvh = h / group;
+  const int positions = a.position + 1;
+  const float *sc = a.scores + (size_t)h * positions;
+  float *pr = a.probs + (size_t)h * positions;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  float mx = -INFINITY;
+  for (int t = tid; t < positions; t += blockDim.x) mx = fmaxf(mx, sc[t]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(RV_FULL, mx, o));
+  if (lane == 0) red[warp] = (double)mx;
+  __syncthreads();
+  if (tid == 0) {
+    float m = -INFINITY;
+    for (int w = 0; w < nw; w++) m = fmaxf(m, (float)red[w]);
+    s_max = m;
+  }
+  __syncthreads();
+  const double dmx = (double)s_max;
+  double part = 0.0;
+  for (int t = tid; t < positions; t += blockDim.x) {
+    const double e = exp(__dsub_rn((double)sc[t], dmx));
+    pr[t] = __double2float_rn(e);
+    part = __dadd_rn(part, e);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = part;
+  __syncthreads();
+  if (tid == 0) {
+    double s = 0.0;
+    for (int w = 0; w < nw; w++) s = __dadd_rn(s, red[w]);
+    const double r = __drcp_rn(s);
+    const unsigned long long bound = 2ull * (unsigned long long)positions + 2ull;
+    const int k = 52 - (64 - __clzll((long long)bound));
+    float inv = __double2float_rn(r);
+    if (!(k >= 30 && isfinite(r) && f32_rounding_stable(r, k))) {
+      double ser = 0.0;
+      for (int t = 0; t < positions; t++) ser = __dadd_rn(ser, exp(__dsub_rn((double)sc[t], dmx)));
+      inv = __double2float_rn(__drcp_rn(ser));
+    }
+    s_inv = inv;
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  for (int t = tid; t < positions; t += blockDim.x) pr[t] = __fmul_rn(pr[t], inv);
+  __syncthreads();
+  const size_t kv_dim = (size_t)a.n_kv * a.hd;
+  const uint16_t *vc = a.v_cache + (size_t)kvh * a.hd;
+  for (int i = tid; i < a.hd; i += blockDim.x) {
+    float acc = 0.0f;
+    int t = 0;
+    for (; t + 4 <= positions; t += 4) {
+      const float v0 = h2f(vc[(size_t)t * kv_dim + i]), v1 = h2f(vc[(size_t)(t + 1) * kv_dim + i]);
+      const float v2 = h2f(vc[(size_t)(t + 2) * kv_dim + i]), v3 = h2f(vc[(size_t)(t + 3) * kv_dim + i]);
+      acc = __fadd_rn(acc, __fmul_rn(pr[t], v0));
+      acc = __fadd_rn(acc, __fmul_rn(pr[t + 1], v1));
+      acc = __fadd_rn(acc, __fmul_rn(pr[t + 2], v2));
+      acc = __fadd_rn(acc, __fmul_rn(pr[t + 3], v3));
+    }
+    for (; t < positions; t++) acc = __fadd_rn(acc, __fmul_rn(pr[t], h2f(vc[(size_t)t * kv_dim + i])));
+    a.out[(size_t)h * a.hd + i] = acc;
+  }
+}
+
+// rope_neox_heads (rope.rs:80-111) for one position, the factors passed by
+// value (formed on the host with the reference's f64 libm calls).
+#define RV_ROPE_MAX_HALF 256
+struct RopeFactors {
+  float2 cs[RV_ROPE_MAX_HALF];
+};
+__global__ void k_rope_heads(float *x, int n_heads, int hd, RopeFactors f) {
+  const int half = hd >> 1;
+  const size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (size_t)n_heads * half) return;
+  const size_t h = e / half;
+  const int k = (int)(e % half);
+  float *xh = x + h * hd;
+  const float x0 = xh[k], x1 = xh[k + half];
+  const float2 cs = f.cs[k];
+  xh[k] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+  xh[k + half] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+}

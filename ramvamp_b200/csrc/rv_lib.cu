@@ -20,6 +20,7 @@
 #include "rv_tc.cuh"
 #include "rv_ep.cuh"
 #include "rv_fused.cuh"
+#include "rv_attn.cuh"
 
 #include "_gen/expf_exceptions.inc"
 
@@ -62,6 +63,8 @@ extern "C" const char *rv_status_name(int s) {
     case RV_ERR_TIMEOUT: return "Timeout";
     case RV_ERR_IO: return "Io";
     case RV_ERR_TOKEN_OUT_OF_RANGE: return "TokenOutOfRange";
+    case RV_ERR_POSITION_MISMATCH: return "PositionMismatch";
+    case RV_ERR_CAPACITY_EXCEEDED: return "CapacityExceeded";
   }
   return "Unknown";
 }
@@ -1567,6 +1570,230 @@ extern "C" int rv_moe_get_taps(const rv_moe *m, rv_moe_taps *o) {
 }
 
 // ==================================================== synthetic inputs
+// ============================================================ attention
+// rope.rs:30-45: inv_freq = theta^(-2i/dim) and the angle in f64 (host
+// libm pow), cos and sin of the angle (host libm), rounded to f32.
+static void rope_inv_freq(size_t hd, float theta, std::vector<double> &inv) {
+  const double base = (double)theta, dim = (double)hd;
+  inv.resize(hd / 2);
+  for (size_t i = 0; i < hd / 2; i++) inv[i] = pow(base, -2.0 * (double)i / dim);
+}
+static void rope_row(const std::vector<double> &inv, uint32_t position, float2 *out) {
+  const double pos = (double)position;
+  for (size_t i = 0; i < inv.size(); i++) {
+    const double ang = pos * inv[i];
+    out[i] = make_float2((float)cos(ang), (float)sin(ang));
+  }
+}
+
+struct rv_attn {
+  int device = 0;
+  rv_attn_config cfg{};
+  uint16_t *k_cache = nullptr, *v_cache = nullptr;
+  float2 *rot = nullptr;
+  float *scratch = nullptr;
+  std::vector<uint32_t> lens;
+  float scale = 0.0f;
+  size_t plane = 0;  // halves per layer and cache
+};
+
+extern "C" void rv_attn_destroy(rv_attn *a) {
+  if (!a) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(a->device);
+  cudaFree(a->k_cache);
+  cudaFree(a->v_cache);
+  cudaFree(a->rot);
+  cudaFree(a->scratch);
+  if (prev >= 0) cudaSetDevice(prev);
+  delete a;
+}
+
+extern "C" int rv_attn_create(int device, const rv_attn_config *cfg, rv_attn **out) {
+  if (!cfg || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_create: null argument");
+  *out = nullptr;
+  const rv_attn_config c = *cfg;
+  if (c.head_dim == 0 || c.head_dim % 2) RV_FAIL(RV_ERR_INVALID_HEAD_DIM, "head_dim %u", c.head_dim);
+  if (c.head_dim % 8 || c.head_dim > 256)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "head_dim %u: the kernels take multiples of 8 up to 256", c.head_dim);
+  if (c.n_layers == 0 || c.n_heads == 0 || c.n_kv_heads == 0 || c.max_positions == 0)
+    RV_FAIL(RV_ERR_EMPTY, "rv_attn_create: zero layers, heads or positions");
+  if (c.n_heads % c.n_kv_heads)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "n_heads %u is not a multiple of n_kv_heads %u", c.n_heads, c.n_kv_heads);
+  if (c.max_positions > (1u << 20)) RV_FAIL(RV_ERR_UNIMPLEMENTED, "max_positions %u > 2^20", c.max_positions);
+  int rc = ensure_device(device);
+  if (rc) return rc;
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(device));
+  rv_attn *a = new rv_attn;
+  a->device = device;
+  a->cfg = c;
+  a->lens.assign(c.n_layers, 0);
+  a->scale = 1.0f / sqrtf((float)c.head_dim);  // model/forward.rs:2475
+  a->plane = (size_t)c.max_positions * c.n_kv_heads * c.head_dim;
+  const size_t half = c.head_dim / 2;
+  cudaError_t e = cudaMalloc(&a->k_cache, 2 * a->plane * c.n_layers);
+  if (e == cudaSuccess) e = cudaMalloc(&a->v_cache, 2 * a->plane * c.n_layers);
+  if (e == cudaSuccess) e = cudaMalloc(&a->rot, sizeof(float2) * half * c.max_positions);
+  if (e == cudaSuccess) e = cudaMalloc(&a->scratch, sizeof(float) * 2 * (size_t)c.n_heads * c.max_positions);
+  if (e == cudaSuccess) {
+    std::vector<double> inv;
+    rope_inv_freq(c.head_dim, c.rope_theta, inv);
+    std::vector<float2> table(half * c.max_positions);
+    for (uint32_t p = 0; p < c.max_positions; p++) rope_row(inv, p, table.data() + (size_t)p * half);
+    e = cudaMemcpy(a->rot, table.data(), sizeof(float2) * table.size(), cudaMemcpyHostToDevice);
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    rv_attn_destroy(a);
+    RV_FAIL(RV_ERR_CUDA, "rv_attn_create: %s", cudaGetErrorString(e));
+  }
+  *out = a;
+  return RV_OK;
+}
+
+extern "C" int rv_attn_len(const rv_attn *a, uint32_t layer, uint32_t *len_out) {
+  if (!a || !len_out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_len: null argument");
+  if (layer >= a->cfg.n_layers) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %u", layer, a->cfg.n_layers);
+  *len_out = a->lens[layer];
+  return RV_OK;
+}
+
+extern "C" int rv_attn_clear(rv_attn *a) {
+  if (!a) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_clear: null engine");
+  std::fill(a->lens.begin(), a->lens.end(), 0u);
+  return RV_OK;
+}
+
+extern "C" int rv_attn_cache(const rv_attn *a, uint32_t layer, const uint16_t **k_out, const uint16_t **v_out) {
+  if (!a) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_cache: null engine");
+  if (layer >= a->cfg.n_layers) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %u", layer, a->cfg.n_layers);
+  if (k_out) *k_out = a->k_cache + (size_t)layer * a->plane;
+  if (v_out) *v_out = a->v_cache + (size_t)layer * a->plane;
+  return RV_OK;
+}
+
+extern "C" int rv_attn_copy_cache(const rv_attn *a, uint32_t layer, uint32_t positions, uint16_t *k_out,
+                                  uint16_t *v_out, rv_stream stream) {
+  if (!a) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_copy_cache: null engine");
+  if (layer >= a->cfg.n_layers) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %u", layer, a->cfg.n_layers);
+  if (positions > a->cfg.max_positions)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "%u positions of a %u-position cache", positions, a->cfg.max_positions);
+  const size_t bytes = 2 * (size_t)positions * a->cfg.n_kv_heads * a->cfg.head_dim;
+  if (bytes == 0) return RV_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (k_out) RV_CUDA(cudaMemcpyAsync(k_out, a->k_cache + (size_t)layer * a->plane, bytes, cudaMemcpyDeviceToDevice, s));
+  if (v_out) RV_CUDA(cudaMemcpyAsync(v_out, a->v_cache + (size_t)layer * a->plane, bytes, cudaMemcpyDeviceToDevice, s));
+  return RV_OK;
+}
+
+// Scores and softmax-out over positions 0..args.position, shared by
+// rv_attn_decode and rv_attention.
+static int attn_launch_core(const AttnArgs &args, cudaStream_t s) {
+  const int positions = args.position + 1;
+  dim3 grid((unsigned)args.n_heads, (unsigned)((positions + 127) / 128));
+  k_attn_scores<<<grid, 128, args.hd * sizeof(float), s>>>(args);
+  k_attn_softmax_out<<<(unsigned)args.n_heads, args.hd > 128 ? args.hd : 128, 0, s>>>(args);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_attn_decode(rv_attn *a, uint32_t layer, uint32_t position, float *q, float *k, const float *v,
+                              const float *q_norm, const float *k_norm, float *out, rv_stream stream) {
+  if (!a) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_decode: null engine");
+  const rv_attn_config &c = a->cfg;
+  if (layer >= c.n_layers) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %u", layer, c.n_layers);
+  if (position != a->lens[layer])
+    RV_FAIL(RV_ERR_POSITION_MISMATCH, "position %u, layer %u holds %u", position, layer, a->lens[layer]);
+  if (position >= c.max_positions)
+    RV_FAIL(RV_ERR_CAPACITY_EXCEEDED, "layer %u is full (%u positions)", layer, c.max_positions);
+  if (!q || !k || !v || !q_norm || !k_norm || !out)
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_decode: null pointer");
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  if (prev != a->device) RV_CUDA(cudaSetDevice(a->device));
+  AttnArgs args;
+  args.q = q;
+  args.k = k;
+  args.v = v;
+  args.q_norm = q_norm;
+  args.k_norm = k_norm;
+  args.k_cache = a->k_cache + (size_t)layer * a->plane;
+  args.v_cache = a->v_cache + (size_t)layer * a->plane;
+  args.rot = a->rot;
+  args.scores = a->scratch;
+  args.probs = a->scratch + (size_t)c.n_heads * c.max_positions;
+  args.out = out;
+  args.n_heads = (int)c.n_heads;
+  args.n_kv = (int)c.n_kv_heads;
+  args.hd = (int)c.head_dim;
+  args.position = (int)position;
+  args.eps = c.eps;
+  args.scale = a->scale;
+  cudaStream_t s = (cudaStream_t)stream;
+  k_attn_prep<<<c.n_heads + c.n_kv_heads, c.head_dim, 34 * sizeof(double) + c.head_dim * sizeof(float), s>>>(args);
+  int rc = attn_launch_core(args, s);
+  if (prev != a->device) cudaSetDevice(prev);
+  if (rc) return rc;
+  a->lens[layer] = position + 1;
+  return RV_OK;
+}
+
+extern "C" int rv_rope_neox_heads(float *x, size_t x_len, size_t n_heads, size_t head_dim, uint32_t position,
+                                  float theta, rv_stream stream) {
+  if (head_dim == 0 || head_dim % 2) RV_FAIL(RV_ERR_INVALID_HEAD_DIM, "rope_neox_heads: head_dim %zu", head_dim);
+  if (x_len != sat_mul(n_heads, head_dim))
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "rope_neox_heads: x vs n_heads * head_dim (%zu vs %zu)", x_len,
+            sat_mul(n_heads, head_dim));
+  if (head_dim / 2 > RV_ROPE_MAX_HALF) RV_FAIL(RV_ERR_UNIMPLEMENTED, "rope_neox_heads: head_dim %zu > 512", head_dim);
+  if (x_len == 0) return RV_OK;
+  if (!x || ((uintptr_t)x & 3)) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rope_neox_heads: null or misaligned x");
+  int rc = ensure_current_device();
+  if (rc) return rc;
+  std::vector<double> inv;
+  rope_inv_freq(head_dim, theta, inv);
+  RopeFactors f;
+  rope_row(inv, position, f.cs);
+  const size_t pairs = n_heads * (head_dim / 2);
+  k_rope_heads<<<(unsigned)((pairs + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, (int)n_heads, (int)head_dim, f);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, size_t positions,
+                            size_t n_heads, size_t n_kv_heads, size_t head_dim, float scale, float *scratch,
+                            size_t scratch_len, float *out, rv_stream stream) {
+  if (positions == 0 || n_heads == 0 || n_kv_heads == 0) RV_FAIL(RV_ERR_EMPTY, "attention: nothing to attend");
+  if (head_dim == 0 || head_dim % 2) RV_FAIL(RV_ERR_INVALID_HEAD_DIM, "attention: head_dim %zu", head_dim);
+  if (head_dim % 8 || head_dim > 256)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "attention: head_dim %zu (multiples of 8 up to 256)", head_dim);
+  if (n_heads % n_kv_heads)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "attention: %zu query heads over %zu kv heads", n_heads, n_kv_heads);
+  if (positions > (1u << 20)) RV_FAIL(RV_ERR_UNIMPLEMENTED, "attention: %zu positions > 2^20", positions);
+  if (scratch_len < sat_mul(2 * n_heads, positions))
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "attention: scratch of %zu floats, needs %zu", scratch_len,
+            sat_mul(2 * n_heads, positions));
+  if (!q || !k_cache || !v_cache || !scratch || !out || ((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 1))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "attention: null pointer or k_cache not 16-byte aligned");
+  int rc = ensure_current_device();
+  if (rc) return rc;
+  AttnArgs args{};
+  args.q = const_cast<float *>(q);
+  args.k_cache = const_cast<uint16_t *>(k_cache);
+  args.v_cache = const_cast<uint16_t *>(v_cache);
+  args.scores = scratch;
+  args.probs = scratch + n_heads * positions;
+  args.out = out;
+  args.n_heads = (int)n_heads;
+  args.n_kv = (int)n_kv_heads;
+  args.hd = (int)head_dim;
+  args.position = (int)positions - 1;
+  args.scale = scale;
+  return attn_launch_core(args, (cudaStream_t)stream);
+}
+
 extern "C" int rv_synth_normal(uint64_t seed, uint64_t offset, float sigma, float *out, size_t n,
                                rv_stream stream) {
   if (n == 0) return RV_OK;

@@ -1,0 +1,135 @@
+"""GPU parity of the attention half of the decode step (NeoX RoPE, decode
+attention, QK-norm + f16 KV append through the engine) against the CPU
+oracle, bit for bit, through the C ABI."""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+THETA = 1e7
+
+
+@pytest.fixture(scope="module")
+def rv():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import ramvamp_b200
+
+    return ramvamp_b200
+
+
+def dev(a):
+    return torch.from_numpy(np.array(a, copy=True)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def _f16(x):
+    return np.asarray(x, np.float32).astype(np.float16).view(np.uint16)
+
+
+@pytest.mark.parametrize("head_dim", [4, 128, 256])
+def test_rope_bit_identical(rv, orc, head_dim):
+    """rope.rs:80-111 on the GPU, the reference's test positions and more."""
+    rng = np.random.default_rng(head_dim)
+    n_heads = 32 if head_dim == 128 else 3
+    for position in (0, 1, 2, 3, 17, 511, 4096, 100_000, 2**31 + 5):
+        x = rng.uniform(-5, 5, n_heads * head_dim).astype(np.float32)
+        got = host(rv.rope_neox_heads(dev(x), n_heads, head_dim, position, THETA))
+        assert got.tobytes() == orc.rope_neox_heads(x, n_heads, head_dim, position, THETA).tobytes(), position
+    x = dev(rng.uniform(-1, 1, n_heads * head_dim).astype(np.float32))
+    want = orc.rope_neox_heads(host(x), n_heads, head_dim, 9, 1e6)
+    rv.CudaBackend().rope_neox_heads(x, n_heads, head_dim, 9, 1e6)
+    assert host(x).tobytes() == want.tobytes()
+
+
+@pytest.mark.parametrize("positions", [1, 2, 7, 128, 129, 576, 1000, 4097])
+def test_attention_bit_identical(rv, orc, positions):
+    """attention.rs:1075-1303 (scalar arm, which its AVX2 arm equals) over
+    random f16 caches at Qwen3 geometry (32 query heads, 4 kv heads, 128)."""
+    n_q, n_kv, hd = 32, 4, 128
+    rng = np.random.default_rng(positions)
+    k = _f16(rng.standard_normal(positions * n_kv * hd))
+    v = _f16(rng.standard_normal(positions * n_kv * hd))
+    q = (rng.standard_normal(n_q * hd) * 0.5).astype(np.float32)
+    scale = float(np.float32(1) / np.sqrt(np.float32(hd)))
+    want = orc.attention(q, k, v, positions, n_q, n_kv, hd, scale)
+    got = host(rv.attention(dev(q), dev(k), dev(v), positions, n_q, n_kv, hd, scale))
+    assert got.tobytes() == want.tobytes()
+
+
+def test_attention_peaked_and_tied_scores(rv, orc):
+    """Scores that underflow the exponential for most positions, exact ties,
+    and a group of one (attention.rs:2425)."""
+    n, hd, P = 4, 8, 300
+    rng = np.random.default_rng(11)
+    k = np.zeros((P, n * hd), np.float32)
+    k[::3, :] = rng.standard_normal((len(range(0, P, 3)), n * hd)) * 30
+    k[5] = k[7]  # a tie
+    kb, vb = _f16(k).reshape(-1), _f16(rng.standard_normal((P, n * hd))).reshape(-1)
+    q = rng.standard_normal(n * hd).astype(np.float32)
+    for scale in (1.0, 0.35355339):
+        want = orc.attention(q, kb, vb, P, n, n, hd, scale)
+        got = host(rv.attention(dev(q), dev(kb), dev(vb), P, n, n, hd, scale))
+        assert got.tobytes() == want.tobytes()
+
+
+def test_decode_steps_bit_identical(rv, orc):
+    """forward.rs:2614-2631 step by step on two layers: the normed, rotated
+    q and k, the cache rows, and the attention output against the oracle for
+    every position 0..299."""
+    n_layers, n_q, n_kv, hd, P = 2, 32, 4, 128, 300
+    eng = rv.AttnEngine(n_layers, n_q, n_kv, hd, max_positions=P, rope_theta=THETA, eps=1e-6)
+    rng = np.random.default_rng(5)
+    qn = [rng.uniform(0.5, 1.5, hd).astype(np.float32) for _ in range(n_layers)]
+    kn = [rng.uniform(0.5, 1.5, hd).astype(np.float32) for _ in range(n_layers)]
+    caches = [(np.zeros(P * n_kv * hd, np.uint16), np.zeros(P * n_kv * hd, np.uint16)) for _ in range(n_layers)]
+    qn_d, kn_d = [dev(x) for x in qn], [dev(x) for x in kn]
+    for pos in range(P):
+        for layer in range(n_layers):
+            q = (rng.standard_normal(n_q * hd) * 2).astype(np.float32)
+            k = (rng.standard_normal(n_kv * hd) * 2).astype(np.float32)
+            v = rng.standard_normal(n_kv * hd).astype(np.float32)
+            qd, kd, vd = dev(q), dev(k), dev(v)
+            out = eng.decode(layer, pos, qd, kd, vd, qn_d[layer], kn_d[layer])
+            want, qr, kr = orc.attn_decode_step(q, k, v, qn[layer], kn[layer], caches[layer][0], caches[layer][1],
+                                                pos, n_q, n_kv, hd, 1e-6, THETA)
+            if pos % 23 == 0 or pos == P - 1:
+                assert host(qd).tobytes() == qr.tobytes(), (pos, layer)
+                assert host(kd).tobytes() == kr.tobytes(), (pos, layer)
+                assert host(out).tobytes() == want.tobytes(), (pos, layer)
+    for layer in range(n_layers):
+        kc, vc = eng.cache_tensors(layer)
+        assert host(kc).view(np.uint16).reshape(-1).tobytes() == caches[layer][0].tobytes()
+        assert host(vc).view(np.uint16).reshape(-1).tobytes() == caches[layer][1].tobytes()
+        assert eng.len(layer) == P
+
+
+def test_engine_errors_and_clear(rv):
+    """PositionMismatch, CapacityExceeded, LayerOutOfRange; clear() restarts."""
+    eng = rv.AttnEngine(1, 4, 2, 8, max_positions=2)
+    z = lambda n: torch.zeros(n, dtype=torch.float32, device="cuda")
+    q, k, v, w = z(32), z(16), z(16), torch.ones(8, device="cuda")
+    with pytest.raises(rv.KernelError) as e:
+        eng.decode(0, 1, q, k, v, w, w)
+    assert e.value.kind == "PositionMismatch"
+    with pytest.raises(rv.KernelError) as e:
+        eng.decode(1, 0, q, k, v, w, w)
+    assert e.value.kind == "LayerOutOfRange"
+    eng.decode(0, 0, q, k, v, w, w)
+    eng.decode(0, 1, q, k, v, w, w)
+    with pytest.raises(rv.KernelError) as e:
+        eng.decode(0, 2, q, k, v, w, w)
+    assert e.value.kind == "CapacityExceeded"
+    eng.clear()
+    assert eng.len(0) == 0
+    eng.decode(0, 0, q, k, v, w, w)
+    torch.cuda.synchronize()
+    rv.device_status(0)
