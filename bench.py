@@ -40,7 +40,7 @@ SEED = 20261201
 METRIC = "decode tok/s (expert FFN, 48 MoE layers, batch 1)"
 
 
-WORKLOADS = ("decode", "prefill", "batch", "ep")
+WORKLOADS = ("decode", "prefill", "batch", "ep", "model")
 
 
 def parse():
@@ -50,12 +50,14 @@ def parse():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--workload", choices=WORKLOADS, default="decode",
-                    help="decode: config 1 (default); prefill: config 2; batch: config 3; ep: config 4")
+                    help="decode: config 1's expert FFN (default); prefill: config 2; batch: config 3; "
+                         "ep: config 4; model: config 1 whole model (attention + MoE + lm_head, greedy)")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--exact", action="store_true", help="prefill/batch/ep: the exact (AVX2-order) path")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
-    steps, warmup = {"decode": (30, 5), "prefill": (20, 5), "batch": (10, 3), "ep": (5, 3)}[a.workload]
+    steps, warmup = {"decode": (30, 5), "prefill": (20, 5), "batch": (10, 3), "ep": (5, 3),
+                     "model": (64, 3)}[a.workload]
     a.steps = steps if a.steps is None else a.steps
     a.warmup = warmup if a.warmup is None else a.warmup
     return a
@@ -415,6 +417,214 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ================================================ config 1, whole model
+# Qwen3-30B-A3B, 48 layers, random-init weights through the reference's
+# quantizers; a 512-token prompt of seeded uniform-random ids, then greedy
+# decoding.  A step is one token through the whole model (embedding, 48 x
+# (attention half + MoE block), final norm, lm_head, argmax), replayed from
+# one captured CUDA graph with the token, position and sampled id in device
+# memory.  W untimed generated tokens after the prompt, then K timed.
+MODEL_PROMPT = 512
+MODEL_SEED = SEED % 1000 + 1
+MODEL_METRIC = "decode tok/s (whole model, greedy, batch 1, after a 512-token prompt)"
+
+
+def model_launches_per_step(n_layers):
+    # embedding; per layer: attn_norm, Q8_K, Q8_0, q/k/v GEMVs, attention
+    # (prep, scores, softmax+out), Q8_K, attn_output, residual add, MoE (4);
+    # final norm, Q8_K, lm_head, argmax, advance
+    return 1 + n_layers * 17 + 5
+
+
+def run_cuda_model(args):
+    import torch
+    import torch.distributed as dist
+
+    import ramvamp_b200 as rv
+    from ramvamp_b200.model import Decoder, ModelConfig, Qwen3Weights
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
+    dev = local if world > 1 else 0
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig(n_layers=args.layers)
+    w = Qwen3Weights.synthetic(cfg, seed=MODEL_SEED, device=dev)
+    n_gen = args.warmup + args.steps
+    dec = Decoder(w, max_positions=MODEL_PROMPT + n_gen + 1, device=dev)
+    dec.capture()
+    prompt = np.random.default_rng(SEED + rank).integers(0, cfg.vocab, MODEL_PROMPT).astype(np.int32)
+    prompt_d = torch.from_numpy(prompt).cuda()
+    stream = torch.cuda.current_stream()
+    dec.reset()
+    dec.token.copy_(prompt_d[:1])
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record(stream)
+    for i in range(MODEL_PROMPT):
+        dec.step()
+        if i + 1 < MODEL_PROMPT:
+            dec.token.copy_(prompt_d[i + 1:i + 2])
+    ev[1].record(stream)
+    for _ in range(args.warmup):
+        dec.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(dev)
+    uuid = str(getattr(props, "uuid", ""))
+    clocks = ClockSampler(("GPU-" + uuid if uuid and not uuid.startswith("GPU-") else uuid) or str(dev))
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    ev[2].record(stream)
+    for _ in range(args.steps):
+        dec.step()
+    ev[3].record(stream)
+    ev[3].synchronize()
+    clk = clocks.stop()
+    ms = ev[2].elapsed_time(ev[3])
+    prompt_ms = ev[0].elapsed_time(ev[1])
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ids = dec.ids[MODEL_PROMPT - 1:MODEL_PROMPT - 1 + n_gen].cpu().numpy().tolist()
+    rv.device_status(dev)
+
+    # lm_head roofline, live: the same GEMV launched alone after a clean
+    # (read) L2 flush, CUDA events on its stream.
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device="cuda")
+    lm_ms = []
+    for i in range(12):
+        flush.sum()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        rv.gemv_q8_k(rv.QuantFormat.Q6_K, w.lm_head, cfg.hidden, cfg.vocab, dec.acts_k, dec.logits)
+        b.record(stream)
+        b.synchronize()
+        if i >= 2:
+            lm_ms.append(a.elapsed_time(b))
+    lm_ms = statistics.median(lm_ms)
+    lm_bytes = w.lm_head.numel()
+    peak, peak_kind = measured_peaks()
+    achieved = lm_bytes / (lm_ms * 1e-3) / 1e9
+    del flush
+
+    # e2e: a host-driven loop through the public API: each token's id goes
+    # in from pinned host memory (4 B) and the sampled id comes back (4 B).
+    # The cache continues from the timed run, so positions stay in range.
+    tok_h = torch.zeros(1, dtype=torch.int32).pin_memory()
+    out_h = torch.zeros(1, dtype=torch.int32).pin_memory()
+    tok_h[0] = ids[-1]
+    e2e_steps = min(args.steps, 16)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        dec.token.copy_(tok_h, non_blocking=True)
+        dec.step()
+        out_h.copy_(dec.next_token, non_blocking=True)
+        stream.synchronize()
+        tok_h[0] = out_h[0]
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = model_cpu_baseline(cfg)
+    if rank == 0:
+        line = {
+            "metric": MODEL_METRIC, "value": round(world * args.steps / (ms / 1e3), 2), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 (dp4a) + f32 + f16 KV",
+            "data": "synthetic: random-init weights (seeded N(0,0.02), embedding N(0,1)) through the reference's "
+                    "quantizers (Q4_K/Q8_0/Q6_K/Q5_K as Q4_K_M), 512 seeded uniform-random prompt ids",
+            "config": {"workload": f"config1 whole model: Qwen3-30B-A3B ({cfg.n_layers} layers, 32/4 heads, "
+                                   "head_dim 128, 128 experts top-8, vocab 151936), batch-1 greedy decode after "
+                                   "a 512-token prompt, all weights resident in HBM",
+                       "layers": cfg.n_layers, "prompt": MODEL_PROMPT, "generated": n_gen,
+                       "numerics": "bit-identical to the reference's step (f64 exp caveat)",
+                       "l2": "inputs larger than L2: each step reads ~1.9 GB of weights",
+                       "parallelism": "replicas" if world > 1 else "single GPU", "cuda_graph": True},
+            "prompt_tok_s": round(MODEL_PROMPT / (prompt_ms / 1e3), 2),
+            "generated_ids_head": ids[:8],
+            "roofline": {"kernel": "k_gemv_lm_head", "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                         "bytes_per_launch": lm_bytes, "traffic": ncu_traffic("k_gemv_lm_head")},
+            "e2e": {"value": round(world * e2e_steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4, "path": "Decoder.step with the token id from pinned host memory "
+                                                     "and the sampled id read back, one sync per token"},
+            "gpu_launches": args.steps * model_launches_per_step(cfg.n_layers),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def model_cpu_baseline(cfg, sample_layers=(0, 6), positions=64):
+    """The reference's step on this host's cores (C oracle), bounded: one
+    token at position `positions` through two sampled layers (a Q6_K and a
+    Q4_K layer) plus the lm_head, scaled to all layers.  The weights are the
+    CUDA arm's (same seeds through the CPU restatement of the generator and
+    quantizers)."""
+    from oracle import oracle as orc
+    from oracle.model_ref import RefModel, synthetic_host
+
+    orc.build()
+    threads = os.cpu_count() or 1
+    layers = [l for l in sample_layers if l < cfg.n_layers]
+    weights, moe = synthetic_host(cfg, MODEL_SEED, layers, threads)
+    sub = type(cfg)(**{**cfg.__dict__, "n_layers": len(layers)})
+    impl = orc.default_impl()  # the arm the reference dispatches to on this host
+    ref = RefModel(sub, weights, moe, positions + 2, threads, impl=impl)
+    for p in range(positions):  # fill the caches (untimed)
+        ref.step(p % cfg.vocab, p)
+    t0 = time.perf_counter()
+    ref.step(7, positions)
+    t1 = time.perf_counter()
+    # lm_head alone, to split the fixed part from the per-layer part
+    normed = orc.rmsnorm(np.ones(cfg.hidden, np.float32), weights["output_norm"], cfg.eps)
+    t2 = time.perf_counter()
+    orc.gemv(orc.Q6_K, weights["lm_head"], cfg.hidden, cfg.vocab, orc.quantize_row_q8_k(normed), impl=impl,
+             threads=threads)
+    t3 = time.perf_counter()
+    per_layer = max((t1 - t0) - (t3 - t2), 0.0) / len(layers)
+    s_tok = per_layer * cfg.n_layers + (t3 - t2)
+    return {"value": round(1.0 / s_tok, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"one token at position {positions} through layers {layers} and the lm_head on the C "
+                      f"oracle ({'AVX2' if impl == orc.AVX2 else 'scalar'} arm, {threads} threads), per-layer "
+                      f"time scaled to {cfg.n_layers} layers"}
+
+
+def run_reference_model(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from ramvamp_b200.model import ModelConfig  # configuration only (no GPU calls)
+
+    cfg = ModelConfig(n_layers=args.layers)
+    cpu = model_cpu_baseline(cfg)
+    line = {
+        "impl": "reference", "metric": MODEL_METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": 1, "warmup": 64, "ms_per_step": round(1e3 / cpu["value"], 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 + f32 + f16 KV",
+        "data": "synthetic (same seeds and weights as the CUDA arm)",
+        "config": {"workload": "config1 whole model (sampled layers, scaled)", "layers": cfg.n_layers},
+        "cpu_baseline": cpu,
+        "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ===================================================== configs 2, 3, 4
 # prefill (config 2): 512 tokens through one MoE layer (Q4_K gate/up, Q6_K
 #   down), near-uniform routing from N(0,1) rows and an N(0,0.02) router.
@@ -755,6 +965,9 @@ def run_reference_batched(args):
 
 def main():
     args = parse()
+    if args.workload == "model":
+        (run_reference_model if args.impl == "reference" else run_cuda_model)(args)
+        return
     if args.workload != "decode":
         (run_reference_batched if args.impl == "reference" else run_cuda_batched)(args)
         return

@@ -513,6 +513,27 @@ RV_API int rv_attn_copy_cache(const rv_attn *a, uint32_t layer, uint32_t positio
 RV_API int rv_attn_decode(rv_attn *a, uint32_t layer, uint32_t position, float *q, float *k, const float *v,
                    const float *q_norm, const float *k_norm, float *out, rv_stream stream);
 
+/* rv_attn_decode for graph-driven decoding: the position is read from
+ * position_dev (device int32) when the kernels run, so one captured CUDA
+ * graph serves every step.  The host length bookkeeping is not used
+ * (rv_attn_len does not change).  A position outside [0, max_positions)
+ * makes every kernel write nothing and sets RV_ERR_CAPACITY_EXCEEDED in
+ * the device error word (rv_device_status). */
+RV_API int rv_attn_decode_dev(rv_attn *a, uint32_t layer, const int32_t *position_dev, float *q, float *k,
+                       const float *v, const float *q_norm, const float *k_norm, float *out, rv_stream stream);
+/* The end of a graph-driven decode step, on the device: when next_token
+ * is given, ids_out[position] = next_token[0] (if ids_out and position <
+ * ids_cap) and token[0] = next_token[0] (if token); then position += 1. */
+RV_API int rv_decode_advance(int32_t *position_dev, const uint32_t *next_token, int32_t *token, uint32_t *ids_out,
+                      size_t ids_cap, rv_stream stream);
+
+/* Sampler::argmax (generate/mod.rs:321-331): out[0] = the first index of
+ * the largest of x[0..n) (device); NaN never wins; 0 when nothing beats
+ * -inf.  RV_ERR_EMPTY for n == 0. */
+RV_API int rv_argmax(const float *x, size_t n, uint32_t *out, rv_stream stream);
+/* primitives::vec_add (kernels/primitives/vec.rs:10-22): a[i] += b[i]. */
+RV_API int rv_vec_add(float *a, const float *b, size_t n, rv_stream stream);
+
 /* Replaces primitives::rope_neox_heads / Backend::rope_neox_heads
  * (kernels/primitives/rope.rs:80-111): x [n_heads*head_dim] (device)
  * rotated in place at `position`.  RV_ERR_INVALID_HEAD_DIM for a zero or odd

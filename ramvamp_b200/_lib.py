@@ -107,6 +107,10 @@ SIGNATURES = {
     "rv_attn_copy_cache": (I32, [P, U32, U32, P, P, P]),
     "rv_attn_decode": (I32, [P, U32, U32, P, P, P, P, P, P, P]),
     "rv_rope_neox_heads": (I32, [P, SZ, SZ, SZ, U32, F32, P]),
+    "rv_attn_decode_dev": (I32, [P, U32, P, P, P, P, P, P, P, P]),
+    "rv_decode_advance": (I32, [P, P, P, P, SZ, P]),
+    "rv_argmax": (I32, [P, SZ, P, P]),
+    "rv_vec_add": (I32, [P, P, SZ, P]),
     "rv_attention": (I32, [P, P, P, SZ, SZ, SZ, SZ, F32, P, SZ, P, P]),
     "rv_gemv_q8_k_fused_rows": (I32, [ctypes.POINTER(FusedPartC), SZ, SZ, SZ, P, SZ, P]),
     "rv_rmsnorm": (I32, [P, P, SZ, SZ, F32, P, P]),

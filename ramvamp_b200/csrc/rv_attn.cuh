@@ -26,8 +26,23 @@ struct AttnArgs {
   float *out;            // [n_heads][hd]
   int n_heads, n_kv, hd;
   int position;          // the row appended; attention covers 0..position
+  const int *pos_dev;    // when set, the position is read here when the kernels run
+  int max_positions;
   float eps, scale;
 };
+
+// The step's position: from device memory in graph-driven decoding.  Past
+// the cache (device mode only: the host checks its own) every kernel
+// writes nothing and the device error word says CapacityExceeded.
+RV_DEVFN int attn_position(const AttnArgs &a) {
+  if (!a.pos_dev) return a.position;
+  const int p = *a.pos_dev;
+  if (p < 0 || p >= a.max_positions) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) rv_dev_fail(RV_ERR_CAPACITY_EXCEEDED);
+    return -1;
+  }
+  return p;
+}
 
 // One CTA (hd threads) per head: CTAs 0..n_heads-1 take q heads, the rest
 // k heads (which also append k and v to the cache).  rmsnorm_in_place
@@ -37,6 +52,8 @@ __global__ void __launch_bounds__(256) k_attn_prep(AttnArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
   double *red = (double *)sm;
   float *xs = (float *)(sm + 34 * sizeof(double));
+  const int position = attn_position(a);
+  if (position < 0) return;  // uniform over the CTA
   const bool is_q = (int)blockIdx.x < a.n_heads;
   const int head = is_q ? (int)blockIdx.x : (int)blockIdx.x - a.n_heads;
   float *x = (is_q ? a.q : a.k) + (size_t)head * a.hd;
@@ -47,7 +64,7 @@ __global__ void __launch_bounds__(256) k_attn_prep(AttnArgs a) {
   const float inv = rms_inv_block(xs, (size_t)a.hd, a.eps, red);
   for (int k = i; k < a.hd; k += blockDim.x) xs[k] = __fmul_rn(__fmul_rn(xs[k], inv), w[k]);
   __syncthreads();
-  const float2 *rot = a.rot + (size_t)a.position * half;
+  const float2 *rot = a.rot + (size_t)position * half;
   const size_t kv_dim = (size_t)a.n_kv * a.hd;
   for (int k = i; k < half; k += blockDim.x) {
     const float2 cs = rot[k];
@@ -57,13 +74,13 @@ __global__ void __launch_bounds__(256) k_attn_prep(AttnArgs a) {
     x[k] = y0;
     x[k + half] = y1;
     if (!is_q) {
-      uint16_t *kc = a.k_cache + (size_t)a.position * kv_dim + (size_t)head * a.hd;
+      uint16_t *kc = a.k_cache + (size_t)position * kv_dim + (size_t)head * a.hd;
       kc[k] = f32_to_f16_bits(y0);
       kc[k + half] = f32_to_f16_bits(y1);
     }
   }
   if (!is_q) {
-    uint16_t *vc = a.v_cache + (size_t)a.position * kv_dim + (size_t)head * a.hd;
+    uint16_t *vc = a.v_cache + (size_t)position * kv_dim + (size_t)head * a.hd;
     const float *vh = a.v + (size_t)head * a.hd;
     for (int k = i; k < a.hd; k += blockDim.x) vc[k] = f32_to_f16_bits(vh[k]);
   }
@@ -71,30 +88,32 @@ __global__ void __launch_bounds__(256) k_attn_prep(AttnArgs a) {
 
 // qk_scores_scalar (attention.rs): scores[h][t] = scale * (q_h . K[t]) with
 // one f32 accumulator over i ascending, separate multiply and add.  Grid
-// (n_heads, position tiles of 128); thread = position; q_h in shared
-// memory; the K row read 8 halves at a time.
+// (n_heads, tiles); thread = position, CTAs striding over 128-position
+// tiles; q_h in shared memory; the K row read 8 halves at a time.
 __global__ void __launch_bounds__(128) k_attn_scores(AttnArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
   float *qs = (float *)sm;
+  const int position = attn_position(a);
+  if (position < 0) return;
   const int h = blockIdx.x, group = a.n_heads / a.n_kv, kvh = h / group;
   for (int k = threadIdx.x; k < a.hd; k += blockDim.x) qs[k] = a.q[(size_t)h * a.hd + k];
   __syncthreads();
-  const int positions = a.position + 1;
-  const int t = blockIdx.y * blockDim.x + threadIdx.x;
-  if (t >= positions) return;
+  const int positions = position + 1;
   const size_t kv_dim = (size_t)a.n_kv * a.hd;
-  const uint4 *kr = (const uint4 *)(a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd);
-  float acc = 0.0f;
-  for (int c = 0; c < a.hd / 8; c++) {
-    const uint4 u = kr[c];
-    const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
+  for (int t = blockIdx.y * blockDim.x + threadIdx.x; t < positions; t += gridDim.y * blockDim.x) {
+    const uint4 *kr = (const uint4 *)(a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd);
+    float acc = 0.0f;
+    for (int c = 0; c < a.hd / 8; c++) {
+      const uint4 u = kr[c];
+      const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j], h2f((uint16_t)(wds[j] & 0xFFFFu))));
-      acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j + 1], h2f((uint16_t)(wds[j] >> 16))));
+      for (int j = 0; j < 4; j++) {
+        acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j], h2f((uint16_t)(wds[j] & 0xFFFFu))));
+        acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j + 1], h2f((uint16_t)(wds[j] >> 16))));
+      }
     }
+    a.scores[(size_t)h * positions + t] = __fmul_rn(a.scale, acc);
   }
-  a.scores[(size_t)h * positions + t] = __fmul_rn(a.scale, acc);
 }
 
 // One CTA (hd threads) per query head: softmax over the positions
@@ -109,8 +128,10 @@ __global__ void __launch_bounds__(128) k_attn_scores(AttnArgs a) {
 __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
   __shared__ double red[34];
   __shared__ float s_max, s_inv;
+  const int position = attn_position(a);
+  if (position < 0) return;
   const int h = blockIdx.x, group = a.n_heads / a.n_kv, kvh = h / group;
-  const int positions = a.position + 1;
+  const int positions = position + 1;
   const float *sc = a.scores + (size_t)h * positions;
   float *pr = a.probs + (size_t)h * positions;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
@@ -191,4 +212,65 @@ __global__ void k_rope_heads(float *x, int n_heads, int hd, RopeFactors f) {
   const float2 cs = f.cs[k];
   xh[k] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
   xh[k + half] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+}
+
+// End of a graph-driven decode step: record the sampled id at the step's
+// position, feed it back as the next input token, advance the position.
+__global__ void k_decode_advance(int *pos, const uint32_t *next, int *token, uint32_t *ids, int ids_cap) {
+  const int p = pos[0];
+  if (next) {
+    if (ids && p >= 0 && p < ids_cap) ids[p] = next[0];
+    if (token) token[0] = (int)next[0];
+  }
+  pos[0] = p + 1;
+}
+
+// Sampler::argmax (generate/mod.rs:321-331): the first index of the
+// largest value; NaN never wins and an all -inf/NaN row gives 0.  One CTA.
+__global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ x, size_t n, uint32_t *out) {
+  __shared__ float sv[32];
+  __shared__ uint32_t si[32];
+  float bv = -INFINITY;
+  uint32_t bi = 0xFFFFFFFFu;
+  for (size_t k = threadIdx.x; k < n; k += blockDim.x) {
+    const float v = x[k];
+    if (v > bv) {
+      bv = v;
+      bi = (uint32_t)k;
+    }
+  }
+  auto better = [](float v, uint32_t i, float bv_, uint32_t bi_) {
+    return i != 0xFFFFFFFFu && (bi_ == 0xFFFFFFFFu || v > bv_ || (v == bv_ && i < bi_));
+  };
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float v = __shfl_xor_sync(RV_FULL, bv, o);
+    const uint32_t i = __shfl_xor_sync(RV_FULL, bi, o);
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = -INFINITY;
+    uint32_t i = 0xFFFFFFFFu;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++)
+      if (better(sv[w], si[w], v, i)) {
+        v = sv[w];
+        i = si[w];
+      }
+    out[0] = i == 0xFFFFFFFFu ? 0u : i;
+  }
+}
+
+// vec_add (primitives/vec.rs:10-22): a[i] += b[i] in f32.
+__global__ void k_vec_add(float *a, const float *b, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) a[i] = __fadd_rn(a[i], b[i]);
 }

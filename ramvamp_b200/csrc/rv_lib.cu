@@ -1692,8 +1692,12 @@ extern "C" int rv_attn_copy_cache(const rv_attn *a, uint32_t layer, uint32_t pos
 // Scores and softmax-out over positions 0..args.position, shared by
 // rv_attn_decode and rv_attention.
 static int attn_launch_core(const AttnArgs &args, cudaStream_t s) {
-  const int positions = args.position + 1;
-  dim3 grid((unsigned)args.n_heads, (unsigned)((positions + 127) / 128));
+  // Host mode: one 128-position tile per CTA row.  Device mode (the
+  // position known only when the kernels run): up to 16 tile rows that
+  // stride over the positions.
+  const int positions = args.pos_dev ? args.max_positions : args.position + 1;
+  const int tiles = (positions + 127) / 128;
+  dim3 grid((unsigned)args.n_heads, (unsigned)(args.pos_dev ? std::min(tiles, 16) : tiles));
   k_attn_scores<<<grid, 128, args.hd * sizeof(float), s>>>(args);
   k_attn_softmax_out<<<(unsigned)args.n_heads, args.hd > 128 ? args.hd : 128, 0, s>>>(args);
   RV_LAUNCH_CHECK();
@@ -1730,6 +1734,8 @@ extern "C" int rv_attn_decode(rv_attn *a, uint32_t layer, uint32_t position, flo
   args.n_kv = (int)c.n_kv_heads;
   args.hd = (int)c.head_dim;
   args.position = (int)position;
+  args.pos_dev = nullptr;
+  args.max_positions = (int)c.max_positions;
   args.eps = c.eps;
   args.scale = a->scale;
   cudaStream_t s = (cudaStream_t)stream;
@@ -1790,8 +1796,73 @@ extern "C" int rv_attention(const float *q, const uint16_t *k_cache, const uint1
   args.n_kv = (int)n_kv_heads;
   args.hd = (int)head_dim;
   args.position = (int)positions - 1;
+  args.pos_dev = nullptr;
+  args.max_positions = (int)positions;
   args.scale = scale;
   return attn_launch_core(args, (cudaStream_t)stream);
+}
+
+extern "C" int rv_attn_decode_dev(rv_attn *a, uint32_t layer, const int32_t *position_dev, float *q, float *k,
+                                  const float *v, const float *q_norm, const float *k_norm, float *out,
+                                  rv_stream stream) {
+  if (!a) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_decode_dev: null engine");
+  const rv_attn_config &c = a->cfg;
+  if (layer >= c.n_layers) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %u", layer, c.n_layers);
+  if (!position_dev || !q || !k || !v || !q_norm || !k_norm || !out || ((uintptr_t)position_dev & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_decode_dev: null or misaligned pointer");
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  if (prev != a->device) RV_CUDA(cudaSetDevice(a->device));
+  AttnArgs args;
+  args.q = q;
+  args.k = k;
+  args.v = v;
+  args.q_norm = q_norm;
+  args.k_norm = k_norm;
+  args.k_cache = a->k_cache + (size_t)layer * a->plane;
+  args.v_cache = a->v_cache + (size_t)layer * a->plane;
+  args.rot = a->rot;
+  args.scores = a->scratch;
+  args.probs = a->scratch + (size_t)c.n_heads * c.max_positions;
+  args.out = out;
+  args.n_heads = (int)c.n_heads;
+  args.n_kv = (int)c.n_kv_heads;
+  args.hd = (int)c.head_dim;
+  args.position = 0;
+  args.pos_dev = position_dev;
+  args.max_positions = (int)c.max_positions;
+  args.eps = c.eps;
+  args.scale = a->scale;
+  cudaStream_t s = (cudaStream_t)stream;
+  k_attn_prep<<<c.n_heads + c.n_kv_heads, c.head_dim, 34 * sizeof(double) + c.head_dim * sizeof(float), s>>>(args);
+  int rc = attn_launch_core(args, s);
+  if (prev != a->device) cudaSetDevice(prev);
+  return rc;
+}
+
+extern "C" int rv_decode_advance(int32_t *position_dev, const uint32_t *next_token, int32_t *token,
+                                 uint32_t *ids_out, size_t ids_cap, rv_stream stream) {
+  if (!position_dev || ((uintptr_t)position_dev & 3)) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_decode_advance: bad pointer");
+  k_decode_advance<<<1, 1, 0, (cudaStream_t)stream>>>(position_dev, next_token, token, ids_out,
+                                                      (int)std::min(ids_cap, (size_t)INT32_MAX));
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_argmax(const float *x, size_t n, uint32_t *out, rv_stream stream) {
+  if (n == 0) RV_FAIL(RV_ERR_EMPTY, "argmax: no logits");
+  if (!x || !out || ((uintptr_t)x & 3) || ((uintptr_t)out & 3)) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "argmax: bad pointer");
+  k_argmax<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, out);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_vec_add(float *a, const float *b, size_t n, rv_stream stream) {
+  if (n == 0) return RV_OK;
+  if (!a || !b) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "vec_add: null pointer");
+  k_vec_add<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a, b, n);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
 }
 
 extern "C" int rv_synth_normal(uint64_t seed, uint64_t offset, float sigma, float *out, size_t n,
