@@ -476,6 +476,7 @@ typedef struct rv_attn_config {
   uint32_t max_positions; /* cache capacity per layer */
   float rope_theta;       /* the manifest's rope_theta as f32 (model/forward.rs:2474) */
   float eps;              /* the QK-norm epsilon (the layer norms' eps) */
+  uint32_t hidden;        /* model width for rv_attn_block's scratch (0: rv_attn_decode only) */
 } rv_attn_config;
 
 typedef struct rv_attn rv_attn;
@@ -533,6 +534,36 @@ RV_API int rv_decode_advance(int32_t *position_dev, const uint32_t *next_token, 
 RV_API int rv_argmax(const float *x, size_t n, uint32_t *out, rv_stream stream);
 /* primitives::vec_add (kernels/primitives/vec.rs:10-22): a[i] += b[i]. */
 RV_API int rv_vec_add(float *a, const float *b, size_t n, rv_stream stream);
+
+/* One layer's weights for rv_attn_block (device pointers, the GGUF-style
+ * row-major packed matrices of model/shapes.rs:14-35). */
+typedef struct rv_attn_weights {
+  const float *attn_norm;      /* [hidden] */
+  const uint8_t *attn_q;       /* [n_heads*head_dim][hidden], Q4_K/Q5_K/Q6_K */
+  const uint8_t *attn_k;       /* [n_kv_heads*head_dim][hidden], Q8_0 */
+  const uint8_t *attn_v;       /* [n_kv_heads*head_dim][hidden], Q4_K/Q5_K/Q6_K */
+  const uint8_t *attn_output;  /* [hidden][n_heads*head_dim], Q4_K/Q5_K/Q6_K */
+  const float *q_norm;         /* [head_dim] */
+  const float *k_norm;         /* [head_dim] */
+  int32_t attn_q_format, attn_v_format, attn_output_format;
+} rv_attn_weights;
+
+/* The whole attention half of one decode step for one layer
+ * (model/forward.rs:2572-2652), residual in place: rmsnorm(residual,
+ * attn_norm) -> Q8_K and Q8_0 (one fused kernel) -> the q, k, v projections
+ * (one launch) -> QK-norm, RoPE, f16 append, attention -> Q8_K ->
+ * attn_output with the residual add in its epilogue.  Needs cfg.hidden.
+ * position_dev NULL: `position` is checked as in rv_attn_decode; else the
+ * position is read on the device as in rv_attn_decode_dev.  Bit-identical
+ * to the reference's sequence (same caveat as rv_attn_decode). */
+RV_API int rv_attn_block(rv_attn *a, uint32_t layer, const rv_attn_weights *w, float *residual,
+                  const int32_t *position_dev, uint32_t position, rv_stream stream);
+
+/* rmsnorm (norm.rs:38-60) of x [n] with weight w fused with
+ * quantize_row_q8_k (q8k_out: n/256 blocks) and, when q80_out is given,
+ * quantize_row_q8_0 (n/32 blocks); n a multiple of 256, <= 16384. */
+RV_API int rv_rmsnorm_quantize(const float *x, const float *w, size_t n, float eps, rv_block_q8k *q8k_out,
+                        rv_block_q8_0 *q80_out, rv_stream stream);
 
 /* Replaces primitives::rope_neox_heads / Backend::rope_neox_heads
  * (kernels/primitives/rope.rs:80-111): x [n_heads*head_dim] (device)

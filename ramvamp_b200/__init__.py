@@ -42,7 +42,7 @@ __all__ = [
     "LayerLayout", "qwen3_layer_layout", "QWEN3_Q6K_DOWN_LAYERS", "synth_normal",
     "quantize_weights", "EXACT", "TENSOR", "lib", "Q8_0_BYTES", "quantize_row_q8_0", "gemv_q8_0",
     "gemv_q8_0_rows", "gemv_q8_0_batched", "dequantize_rows", "embed", "device_status",
-    "rope_neox_heads", "attention", "AttnEngine",
+    "rope_neox_heads", "attention", "AttnEngine", "attn_weights", "rmsnorm_quantize",
 ]
 
 Q8K_BYTES = 292
@@ -579,8 +579,9 @@ class AttnEngine:
     scratch.  ``decode`` is model/forward.rs:2614-2631 for one layer."""
 
     def __init__(self, n_layers=48, n_heads=32, n_kv_heads=4, head_dim=128, max_positions=4096,
-                 rope_theta=1e7, eps=1e-6, device: int = 0):
-        self.cfg = _lib.AttnConfig(n_layers, n_heads, n_kv_heads, head_dim, max_positions, rope_theta, eps)
+                 rope_theta=1e7, eps=1e-6, device: int = 0, hidden: int = 0):
+        self.cfg = _lib.AttnConfig(n_layers, n_heads, n_kv_heads, head_dim, max_positions, rope_theta, eps,
+                                   hidden)
         h = ctypes.c_void_p()
         _check(lib().rv_attn_create(device, ctypes.byref(self.cfg), ctypes.byref(h)))
         self.handle = h
@@ -621,6 +622,15 @@ class AttnEngine:
         _check(lib().rv_attn_copy_cache(self.handle, layer, n, _p(k), _p(v), _stream()))
         return k, v
 
+    def block(self, layer: int, weights, residual: torch.Tensor, position: Optional[int] = None,
+              position_dev: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """model/forward.rs:2572-2652 for one layer, residual in place.
+        `weights` is an rv_attn_weights (``attn_weights(...)``); the
+        position is a host int (checked) or an int32 device tensor."""
+        _check(lib().rv_attn_block(self.handle, layer, ctypes.byref(weights), _p(residual), _p(position_dev),
+                                   0 if position is None else position, _stream()))
+        return residual
+
     def decode(self, layer: int, position: int, q, k, v, q_norm, k_norm, out=None) -> torch.Tensor:
         """QK-norm + RoPE of q and k (in place), f16 append of k and v at
         `position`, attention over positions 0..position into `out`."""
@@ -629,6 +639,21 @@ class AttnEngine:
         _check(lib().rv_attn_decode(self.handle, layer, position, _p(q), _p(k), _p(v), _p(q_norm), _p(k_norm),
                                     _p(out), _stream()))
         return out
+
+
+def attn_weights(attn_norm, attn_q, attn_k, attn_v, attn_output, q_norm, k_norm, attn_q_format=QuantFormat.Q4_K,
+                 attn_v_format=QuantFormat.Q6_K, attn_output_format=QuantFormat.Q5_K):
+    """An rv_attn_weights for AttnEngine.block (device tensors; the caller
+    keeps them alive)."""
+    return _lib.AttnWeights(_p(attn_norm), _p(attn_q), _p(attn_k), _p(attn_v), _p(attn_output), _p(q_norm),
+                            _p(k_norm), int(attn_q_format), int(attn_v_format), int(attn_output_format))
+
+
+def rmsnorm_quantize(x: torch.Tensor, w: torch.Tensor, eps: float, q8k_out: torch.Tensor,
+                     q80_out: Optional[torch.Tensor] = None):
+    """rmsnorm fused with quantize_row_q8_k (and quantize_row_q8_0)."""
+    _check(lib().rv_rmsnorm_quantize(_p(x), _p(w), x.numel(), eps, _p(q8k_out), _p(q80_out), _stream()))
+    return q8k_out
 
 
 def device_status(device: int = 0) -> None:

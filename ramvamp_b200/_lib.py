@@ -72,7 +72,13 @@ class MoeConfig(ctypes.Structure):
 
 class AttnConfig(ctypes.Structure):
     _fields_ = [("n_layers", U32), ("n_heads", U32), ("n_kv_heads", U32), ("head_dim", U32),
-                ("max_positions", U32), ("rope_theta", F32), ("eps", F32)]
+                ("max_positions", U32), ("rope_theta", F32), ("eps", F32), ("hidden", U32)]
+
+
+class AttnWeights(ctypes.Structure):
+    _fields_ = [("attn_norm", P), ("attn_q", P), ("attn_k", P), ("attn_v", P), ("attn_output", P),
+                ("q_norm", P), ("k_norm", P), ("attn_q_format", ctypes.c_int32), ("attn_v_format", ctypes.c_int32),
+                ("attn_output_format", ctypes.c_int32)]
 
 
 class MoeTaps(ctypes.Structure):
@@ -109,6 +115,8 @@ SIGNATURES = {
     "rv_rope_neox_heads": (I32, [P, SZ, SZ, SZ, U32, F32, P]),
     "rv_attn_decode_dev": (I32, [P, U32, P, P, P, P, P, P, P, P]),
     "rv_decode_advance": (I32, [P, P, P, P, SZ, P]),
+    "rv_attn_block": (I32, [P, U32, ctypes.POINTER(AttnWeights), P, P, U32, P]),
+    "rv_rmsnorm_quantize": (I32, [P, P, SZ, F32, P, P, P]),
     "rv_argmax": (I32, [P, SZ, P, P]),
     "rv_vec_add": (I32, [P, P, SZ, P]),
     "rv_attention": (I32, [P, P, P, SZ, SZ, SZ, SZ, F32, P, SZ, P, P]),

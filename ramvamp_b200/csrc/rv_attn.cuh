@@ -226,19 +226,51 @@ __global__ void k_decode_advance(int *pos, const uint32_t *next, int *token, uin
 }
 
 // Sampler::argmax (generate/mod.rs:321-331): the first index of the
-// largest value; NaN never wins and an all -inf/NaN row gives 0.  One CTA.
+// largest value; NaN never wins and an all -inf/NaN row gives 0.  One CTA;
+// each thread scans its 16-byte chunks (and the unaligned head and tail) in
+// index order with eight loads in flight, then a (value, index) reduction
+// that prefers the smaller index on equal values.
+RV_DEVFN void argmax_take(float v, uint32_t i, float &bv, uint32_t &bi) {
+  if (v > bv) {  // strict: the earlier index keeps a tie; NaN never passes
+    bv = v;
+    bi = i;
+  }
+}
 __global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ x, size_t n, uint32_t *out) {
   __shared__ float sv[32];
   __shared__ uint32_t si[32];
   float bv = -INFINITY;
   uint32_t bi = 0xFFFFFFFFu;
-  for (size_t k = threadIdx.x; k < n; k += blockDim.x) {
-    const float v = x[k];
-    if (v > bv) {
-      bv = v;
-      bi = (uint32_t)k;
+  const size_t head = (16 - ((uintptr_t)x & 15)) / 4 % 4;  // floats before the first 16-byte boundary
+  const size_t h = head < n ? head : n;
+  const size_t n4 = (n - h) / 4;
+  const float4 *x4 = (const float4 *)(x + h);
+  if (threadIdx.x == 0)
+    for (size_t k = 0; k < h; k++) argmax_take(x[k], (uint32_t)k, bv, bi);
+  const size_t T = blockDim.x;
+  size_t c = threadIdx.x;
+  for (; c + 7 * T < n4; c += 8 * T) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) v[u] = x4[c + u * T];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const uint32_t i0 = (uint32_t)(h + 4 * (c + u * T));
+      argmax_take(v[u].x, i0, bv, bi);
+      argmax_take(v[u].y, i0 + 1, bv, bi);
+      argmax_take(v[u].z, i0 + 2, bv, bi);
+      argmax_take(v[u].w, i0 + 3, bv, bi);
     }
   }
+  for (; c < n4; c += T) {
+    const float4 v = x4[c];
+    const uint32_t i0 = (uint32_t)(h + 4 * c);
+    argmax_take(v.x, i0, bv, bi);
+    argmax_take(v.y, i0 + 1, bv, bi);
+    argmax_take(v.z, i0 + 2, bv, bi);
+    argmax_take(v.w, i0 + 3, bv, bi);
+  }
+  for (size_t k = h + 4 * n4 + threadIdx.x; k < n; k += T) argmax_take(x[k], (uint32_t)k, bv, bi);
   auto better = [](float v, uint32_t i, float bv_, uint32_t bi_) {
     return i != 0xFFFFFFFFu && (bi_ == 0xFFFFFFFFu || v > bv_ || (v == bv_ && i < bi_));
   };

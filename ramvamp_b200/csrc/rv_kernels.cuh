@@ -34,17 +34,22 @@ struct GemvArgs {
   size_t n_acts;
   float *out;
   int R;              // rows per CTA
+  int accumulate;     // out[...] = out[...] + dot (a fused residual add, vec.rs:10-22)
 };
 
+RV_DEVFN void gemv_store(const GemvArgs &g, size_t idx, float v) {
+  g.out[idx] = g.accumulate ? __fadd_rn(g.out[idx], v) : v;
+}
+
+// One R-row tile `tile` of a k-quant GEMV (the body of k_gemv).
 template <int FMT, int MT>
-__global__ void __launch_bounds__(256) k_gemv(GemvArgs g) {
-  extern __shared__ __align__(16) uint8_t sm[];
+RV_DEVFN void gemv_tile(const GemvArgs &g, size_t tile, uint8_t *sm) {
   uint64_t *bar = (uint64_t *)sm;
   const int R = g.R;
   const size_t act_row = (size_t)g.nb * 292;
   uint8_t *wsm = sm + 16;
   uint8_t *asm_ = wsm + ((R * g.row_bytes + 15) & ~(size_t)15) + 16;
-  const size_t tile0 = (size_t)blockIdx.x * R;
+  const size_t tile0 = tile * R;
   const int rows_here = (int)min((size_t)R, g.nrows - tile0);
   const uint8_t *wsrc = g.w + (g.r0 + tile0) * g.row_bytes;
   const size_t wbytes = (size_t)rows_here * g.row_bytes;
@@ -89,10 +94,15 @@ __global__ void __launch_bounds__(256) k_gemv(GemvArgs g) {
 #pragma unroll
     for (int m = 0; m < MT; m++) {
       const float res = lane_reduce<FMT>(acc[m], accm[m]);
-      if (lane == 0 && r < rows_here && m < mt)
-        g.out[(tile0 + r) * g.n_acts + a0 + m] = res;
+      if (lane == 0 && r < rows_here && m < mt) gemv_store(g, (tile0 + r) * g.n_acts + a0 + m, res);
     }
   }
+}
+
+template <int FMT, int MT>
+__global__ void __launch_bounds__(256) k_gemv(GemvArgs g) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  gemv_tile<FMT, MT>(g, blockIdx.x, sm);
 }
 
 // ------------------------------------------------------- lm_head GEMV
@@ -574,14 +584,13 @@ __global__ void k_quantize_q8_0(const float *__restrict__ x, uint8_t *__restrict
 // eight lanes.  Weight tile staged like k_gemv; activations MT rows at a
 // time (36-byte blocks).
 template <int MT>
-__global__ void __launch_bounds__(256) k_gemv_q8_0(GemvArgs g) {
-  extern __shared__ __align__(16) uint8_t sm[];
+RV_DEVFN void gemv_q8_0_tile(const GemvArgs &g, size_t tile, uint8_t *sm) {
   uint64_t *bar = (uint64_t *)sm;
   const int R = g.R;
   const size_t act_row = (size_t)g.nb * 36;
   uint8_t *wsm = sm + 16;
   uint8_t *asm_ = wsm + ((R * g.row_bytes + 15) & ~(size_t)15) + 16;
-  const size_t tile0 = (size_t)blockIdx.x * R;
+  const size_t tile0 = tile * R;
   const int rows_here = (int)min((size_t)R, g.nrows - tile0);
   const uint8_t *wsrc = g.w + (g.r0 + tile0) * g.row_bytes;
   const size_t wbytes = (size_t)rows_here * g.row_bytes;
@@ -632,8 +641,38 @@ __global__ void __launch_bounds__(256) k_gemv_q8_0(GemvArgs g) {
       float s = __fadd_rn(acc[m], __shfl_xor_sync(0xffffffffu, acc[m], 4));
       s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
       s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
-      if (lane == 0 && r < rows_here && m < mt) g.out[(tile0 + r) * g.n_acts + a0 + m] = s;
+      if (lane == 0 && r < rows_here && m < mt) gemv_store(g, (tile0 + r) * g.n_acts + a0 + m, s);
     }
+  }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(256) k_gemv_q8_0(GemvArgs g) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  gemv_q8_0_tile<MT>(g, blockIdx.x, sm);
+}
+
+// Several single-activation GEMVs in one launch (the attention projections
+// q, k, v): CTAs [cta0[j], cta0[j+1]) run job j's tiles with job j's format
+// (Q4_K / Q5_K / Q6_K against Q8_K activations, Q8_0 against Q8_0).  Every
+// job uses the same R (rows per CTA, blockDim = 8R).
+#define RV_GEMV_MULTI 4
+struct GemvMulti {
+  GemvArgs job[RV_GEMV_MULTI];
+  int fmt[RV_GEMV_MULTI];
+  unsigned cta0[RV_GEMV_MULTI + 1];
+  int n;
+};
+__global__ void __launch_bounds__(256) k_gemv_multi(GemvMulti m) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  int j = 0;
+  while (j + 1 < m.n && blockIdx.x >= m.cta0[j + 1]) j++;
+  const size_t tile = blockIdx.x - m.cta0[j];
+  switch (m.fmt[j]) {
+    case RV_Q4_K: gemv_tile<RV_Q4_K, 1>(m.job[j], tile, sm); break;
+    case RV_Q5_K: gemv_tile<RV_Q5_K, 1>(m.job[j], tile, sm); break;
+    case RV_Q6_K: gemv_tile<RV_Q6_K, 1>(m.job[j], tile, sm); break;
+    default: gemv_q8_0_tile<1>(m.job[j], tile, sm); break;
   }
 }
 
@@ -687,4 +726,41 @@ __global__ void k_dequant_rows(const uint8_t *__restrict__ w, size_t row_bytes, 
     v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
   }
   out[e] = v;
+}
+
+// rmsnorm (norm.rs:38-60) fused with quantize_row_q8_k and, optionally,
+// quantize_row_q8_0 of the normed row: the attention projections' and the
+// lm_head's inputs.  One CTA (256 threads) per 256-value block; every CTA
+// computes the row's exact inverse RMS (rms_inv_block), normalizes its
+// block (x * inv * w, separate f32 multiplies), writes the Q8_K block (warp
+// 0) and the block's eight Q8_0 blocks (warps 0..7, lane = value).
+__global__ void __launch_bounds__(256) k_norm_quant(const float *__restrict__ x, const float *__restrict__ w, int n,
+                                                    float eps, uint8_t *__restrict__ q8k, uint8_t *__restrict__ q80) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  double *red = (double *)sm;
+  float *xs = (float *)(sm + 34 * sizeof(double));
+  for (int k = threadIdx.x; k < n; k += blockDim.x) xs[k] = x[k];
+  __syncthreads();
+  const float inv = rms_inv_block(xs, (size_t)n, eps, red);
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float *ys = xs + n;  // this block's normed values
+  for (int k = threadIdx.x; k < 256; k += blockDim.x) ys[k] = __fmul_rn(__fmul_rn(xs[256 * b + k], inv), w[256 * b + k]);
+  __syncthreads();
+  if (warp == 0) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = ys[8 * lane + e];
+    q8k_quantize_warp(v, lane, q8k + (size_t)b * 292);
+  }
+  if (q80 && warp < 8) {
+    const float v = ys[32 * warp + lane];
+    float amax = fmaxf(0.0f, fabsf(v));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint8_t *o = q80 + (size_t)(8 * b + warp) * 36;
+    if (lane == 0) *(float *)o = f16_round(d);
+    o[4 + lane] = (uint8_t)sat_i8(roundf(__fmul_rn(v, id)));
+  }
 }

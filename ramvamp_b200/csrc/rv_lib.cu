@@ -144,6 +144,8 @@ static int ensure_device(int dev) {
   cudaFuncSetAttribute(k_gemv_lm_head, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv_lm_head, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   cudaFuncSetAttribute(k_gemv_q8_0<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_gemv_multi, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv_q8_0<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   g_dev_sms[dev] = 148;
   cudaDeviceGetAttribute(&g_dev_sms[dev], cudaDevAttrMultiProcessorCount, dev);
@@ -240,7 +242,7 @@ static int gemv_launch(int format, const uint8_t *weight, size_t row_bytes, size
     RV_FAIL(RV_ERR_INVALID_ARGUMENT, "gemv: null pointer or activations not 4-byte aligned");
   int rc = ensure_current_device();
   if (rc) return rc;
-  GemvArgs g;
+  GemvArgs g{};
   g.w = weight;
   g.row_bytes = row_bytes;
   g.nb = (int)(in_dim / 256);
@@ -250,6 +252,9 @@ static int gemv_launch(int format, const uint8_t *weight, size_t row_bytes, size
   g.n_acts = n_acts;
   g.out = out;
   g.R = row_bytes <= 2048 ? 32 : row_bytes <= 4096 ? 16 : 8;
+  // Small matrices (the attention projections: 512-4096 rows): fewer rows
+  // per CTA until the grid covers two waves of SMs.
+  while (g.R > 4 && (g.nrows + g.R - 1) / g.R < 2 * 148) g.R /= 2;
   const size_t act_row = (size_t)g.nb * 292;
   if ((size_t)g.R * row_bytes + 8 * act_row > 180 * 1024)
     RV_FAIL(RV_ERR_UNIMPLEMENTED, "gemv: rows of %zu bytes exceed the staged-tile limit", row_bytes);
@@ -352,7 +357,7 @@ static int gemv_q8_0_launch(const uint8_t *weight, size_t row_bytes, size_t in_d
     RV_FAIL(RV_ERR_INVALID_ARGUMENT, "gemv_q8_0: null pointer, weight not 2-byte or activations not 4-byte aligned");
   int rc = ensure_current_device();
   if (rc) return rc;
-  GemvArgs g;
+  GemvArgs g{};
   g.w = weight;
   g.row_bytes = row_bytes;
   g.nb = (int)(in_dim / 32);
@@ -1595,6 +1600,9 @@ struct rv_attn {
   std::vector<uint32_t> lens;
   float scale = 0.0f;
   size_t plane = 0;  // halves per layer and cache
+  // rv_attn_block scratch (cfg.hidden > 0)
+  uint8_t *acts_k = nullptr, *acts_0 = nullptr, *acts_attn = nullptr;
+  float *q = nullptr, *k = nullptr, *v = nullptr, *attn_out = nullptr;
 };
 
 extern "C" void rv_attn_destroy(rv_attn *a) {
@@ -1606,6 +1614,13 @@ extern "C" void rv_attn_destroy(rv_attn *a) {
   cudaFree(a->v_cache);
   cudaFree(a->rot);
   cudaFree(a->scratch);
+  cudaFree(a->acts_k);
+  cudaFree(a->acts_0);
+  cudaFree(a->acts_attn);
+  cudaFree(a->q);
+  cudaFree(a->k);
+  cudaFree(a->v);
+  cudaFree(a->attn_out);
   if (prev >= 0) cudaSetDevice(prev);
   delete a;
 }
@@ -1622,6 +1637,10 @@ extern "C" int rv_attn_create(int device, const rv_attn_config *cfg, rv_attn **o
   if (c.n_heads % c.n_kv_heads)
     RV_FAIL(RV_ERR_LENGTH_MISMATCH, "n_heads %u is not a multiple of n_kv_heads %u", c.n_heads, c.n_kv_heads);
   if (c.max_positions > (1u << 20)) RV_FAIL(RV_ERR_UNIMPLEMENTED, "max_positions %u > 2^20", c.max_positions);
+  if (c.hidden % 256 || c.hidden > 16384)
+    RV_FAIL(RV_ERR_INDIVISIBLE_ROW, "hidden %u: a multiple of 256 up to 16384 (0 for no block scratch)", c.hidden);
+  if (c.hidden && ((c.n_heads * c.head_dim) % 256))
+    RV_FAIL(RV_ERR_INDIVISIBLE_ROW, "n_heads * head_dim %u is not a multiple of 256", c.n_heads * c.head_dim);
   int rc = ensure_device(device);
   if (rc) return rc;
   int prev = -1;
@@ -1638,6 +1657,16 @@ extern "C" int rv_attn_create(int device, const rv_attn_config *cfg, rv_attn **o
   if (e == cudaSuccess) e = cudaMalloc(&a->v_cache, 2 * a->plane * c.n_layers);
   if (e == cudaSuccess) e = cudaMalloc(&a->rot, sizeof(float2) * half * c.max_positions);
   if (e == cudaSuccess) e = cudaMalloc(&a->scratch, sizeof(float) * 2 * (size_t)c.n_heads * c.max_positions);
+  if (e == cudaSuccess && c.hidden) {
+    const size_t qd = (size_t)c.n_heads * c.head_dim, kvd = (size_t)c.n_kv_heads * c.head_dim;
+    e = cudaMalloc(&a->acts_k, c.hidden / 256 * 292);
+    if (e == cudaSuccess) e = cudaMalloc(&a->acts_0, c.hidden / 32 * 36);
+    if (e == cudaSuccess) e = cudaMalloc(&a->acts_attn, qd / 256 * 292);
+    if (e == cudaSuccess) e = cudaMalloc(&a->q, qd * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&a->k, kvd * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&a->v, kvd * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&a->attn_out, qd * sizeof(float));
+  }
   if (e == cudaSuccess) {
     std::vector<double> inv;
     rope_inv_freq(c.head_dim, c.rope_theta, inv);
@@ -1744,6 +1773,126 @@ extern "C" int rv_attn_decode(rv_attn *a, uint32_t layer, uint32_t position, flo
   if (prev != a->device) cudaSetDevice(prev);
   if (rc) return rc;
   a->lens[layer] = position + 1;
+  return RV_OK;
+}
+
+// One GEMV job of the multi-job launch: whole matrix, one activation row.
+static GemvArgs gemv_job(const uint8_t *w, size_t row_bytes, int nb, size_t rows, const uint8_t *acts, float *out,
+                         int R) {
+  GemvArgs g{};
+  g.w = w;
+  g.row_bytes = row_bytes;
+  g.nb = nb;
+  g.r0 = 0;
+  g.nrows = rows;
+  g.acts = acts;
+  g.n_acts = 1;
+  g.out = out;
+  g.R = R;
+  g.accumulate = 0;
+  return g;
+}
+
+extern "C" int rv_rmsnorm_quantize(const float *x, const float *w, size_t n, float eps, rv_block_q8k *q8k_out,
+                                   rv_block_q8_0 *q80_out, rv_stream stream) {
+  if (n == 0) RV_FAIL(RV_ERR_EMPTY, "rmsnorm_quantize: empty row");
+  if (n % 256 || n > 16384) RV_FAIL(RV_ERR_QUANTIZE_LEN_MISMATCH, "rmsnorm_quantize: n %zu (multiples of 256 <= 16384)", n);
+  if (!x || !w || !q8k_out || ((uintptr_t)q8k_out & 3) || ((uintptr_t)q80_out & 3))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rmsnorm_quantize: null or misaligned pointer");
+  int rc = ensure_current_device();
+  if (rc) return rc;
+  const size_t smem = 34 * sizeof(double) + (n + 256) * sizeof(float);
+  k_norm_quant<<<(unsigned)(n / 256), 256, smem, (cudaStream_t)stream>>>(x, w, (int)n, eps, (uint8_t *)q8k_out,
+                                                                         (uint8_t *)q80_out);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_attn_block(rv_attn *a, uint32_t layer, const rv_attn_weights *w, float *residual,
+                             const int32_t *position_dev, uint32_t position, rv_stream stream) {
+  if (!a || !w || !residual) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_block: null argument");
+  const rv_attn_config &c = a->cfg;
+  if (!c.hidden) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_block: the engine was created with hidden = 0");
+  if (layer >= c.n_layers) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %u", layer, c.n_layers);
+  if (!w->attn_norm || !w->attn_q || !w->attn_k || !w->attn_v || !w->attn_output || !w->q_norm || !w->k_norm)
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_block: null weight");
+  for (int f : {w->attn_q_format, w->attn_v_format, w->attn_output_format})
+    if (!rv_fmt_is_kquant(f)) RV_FAIL(RV_ERR_UNSUPPORTED_FORMAT, "rv_attn_block: weight format %d", f);
+  if (!position_dev) {
+    if (position != a->lens[layer])
+      RV_FAIL(RV_ERR_POSITION_MISMATCH, "position %u, layer %u holds %u", position, layer, a->lens[layer]);
+    if (position >= c.max_positions)
+      RV_FAIL(RV_ERR_CAPACITY_EXCEEDED, "layer %u is full (%u positions)", layer, c.max_positions);
+  } else if ((uintptr_t)position_dev & 3) {
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "rv_attn_block: misaligned position pointer");
+  }
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  if (prev != a->device) RV_CUDA(cudaSetDevice(a->device));
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t H = c.hidden, qd = (size_t)c.n_heads * c.head_dim, kvd = (size_t)c.n_kv_heads * c.head_dim;
+  // 1. attn_norm -> Q8_K and Q8_0 of the normed row
+  k_norm_quant<<<(unsigned)(H / 256), 256, 34 * sizeof(double) + (H + 256) * sizeof(float), s>>>(
+      residual, w->attn_norm, (int)H, c.eps, a->acts_k, a->acts_0);
+  // 2. q, k, v projections in one launch (8 rows per CTA)
+  const int R = 8;
+  GemvMulti m{};
+  const size_t rb_q = H / 256 * rv_fmt_block_bytes(w->attn_q_format);
+  const size_t rb_v = H / 256 * rv_fmt_block_bytes(w->attn_v_format);
+  const size_t rb_k = H / 32 * 34;
+  m.job[0] = gemv_job(w->attn_q, rb_q, (int)(H / 256), qd, a->acts_k, a->q, R);
+  m.fmt[0] = w->attn_q_format;
+  m.job[1] = gemv_job(w->attn_k, rb_k, (int)(H / 32), kvd, a->acts_0, a->k, R);
+  m.fmt[1] = RV_Q8_0;
+  m.job[2] = gemv_job(w->attn_v, rb_v, (int)(H / 256), kvd, a->acts_k, a->v, R);
+  m.fmt[2] = w->attn_v_format;
+  m.n = 3;
+  m.cta0[0] = 0;
+  for (int j = 0; j < 3; j++) m.cta0[j + 1] = m.cta0[j] + (unsigned)((m.job[j].nrows + R - 1) / R);
+  const size_t rb_max = std::max(rb_q, std::max(rb_v, rb_k));
+  const size_t act_max = std::max(H / 256 * 292, H / 32 * 36);
+  const size_t smem = 16 + ((R * rb_max + 15) & ~(size_t)15) + 16 + act_max + 16;
+  k_gemv_multi<<<m.cta0[3], R * 8, smem, s>>>(m);
+  // 3. QK-norm, RoPE, append, attention
+  AttnArgs args;
+  args.q = a->q;
+  args.k = a->k;
+  args.v = a->v;
+  args.q_norm = w->q_norm;
+  args.k_norm = w->k_norm;
+  args.k_cache = a->k_cache + (size_t)layer * a->plane;
+  args.v_cache = a->v_cache + (size_t)layer * a->plane;
+  args.rot = a->rot;
+  args.scores = a->scratch;
+  args.probs = a->scratch + (size_t)c.n_heads * c.max_positions;
+  args.out = a->attn_out;
+  args.n_heads = (int)c.n_heads;
+  args.n_kv = (int)c.n_kv_heads;
+  args.hd = (int)c.head_dim;
+  args.position = (int)position;
+  args.pos_dev = position_dev;
+  args.max_positions = (int)c.max_positions;
+  args.eps = c.eps;
+  args.scale = a->scale;
+  k_attn_prep<<<c.n_heads + c.n_kv_heads, c.head_dim, 34 * sizeof(double) + c.head_dim * sizeof(float), s>>>(args);
+  int rc = attn_launch_core(args, s);
+  if (rc) {
+    if (prev != a->device) cudaSetDevice(prev);
+    return rc;
+  }
+  // 4. Q8_K of the attention output, 5. attn_output + residual add
+  k_quantize_q8k<<<(unsigned)((qd / 256 + 7) / 8), 256, 0, s>>>(a->attn_out, a->acts_attn, qd / 256);
+  GemvArgs g = gemv_job(w->attn_output, qd / 256 * rv_fmt_block_bytes(w->attn_output_format), (int)(qd / 256), H,
+                        a->acts_attn, residual, 4);
+  g.accumulate = 1;
+  switch (w->attn_output_format) {
+    case RV_Q4_K: launch_gemv<RV_Q4_K>(g, s); break;
+    case RV_Q5_K: launch_gemv<RV_Q5_K>(g, s); break;
+    default: launch_gemv<RV_Q6_K>(g, s); break;
+  }
+  RV_LAUNCH_CHECK();
+  if (prev != a->device) cudaSetDevice(prev);
+  if (!position_dev) a->lens[layer] = position + 1;
   return RV_OK;
 }
 

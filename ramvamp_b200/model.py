@@ -21,8 +21,8 @@ import numpy as np
 import torch
 
 from . import (AttnEngine, ExpertTable, MoeEngine, QuantFormat, QWEN3_Q6K_DOWN_LAYERS, _check, _p, _stream,
-               dequantize_rows, gemv_q8_0, gemv_q8_k, lib, qwen3_layer_layout, quantize_row_q8_0,
-               quantize_row_q8_k, quantize_weights, rmsnorm, synth_normal)
+               attn_weights, dequantize_rows, gemv_q8_k, lib, qwen3_layer_layout, quantize_row_q8_0,
+               quantize_weights, rmsnorm_quantize, synth_normal)
 
 Q = QuantFormat
 
@@ -145,17 +145,16 @@ class Decoder:
         self.w, self.cfg, self.device = weights, cfg, device
         self.max_positions = max_positions
         self.attn = AttnEngine(cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, max_positions,
-                               cfg.rope_theta, cfg.eps, device)
+                               cfg.rope_theta, cfg.eps, device, hidden=cfg.hidden)
+        self.attn_w = [attn_weights(l.attn_norm, l.attn_q, l.attn_k, l.attn_v, l.attn_output, l.attn_q_norm,
+                                    l.attn_k_norm, Q.Q4_K, l.attn_v_format, Q.Q5_K) for l in weights.layers]
         self.moe = MoeEngine(cfg.hidden, cfg.moe, cfg.n_experts, cfg.top_k, cfg.norm_topk_prob, cfg.eps,
                              max_tokens=1, device=device)
         d = f"cuda:{device}"
         f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=d)
         H = cfg.hidden
-        self.residual, self.normed, self.o_proj = f32(H), f32(H), f32(H)
-        self.q, self.k, self.v, self.attn_out = f32(cfg.q_dim), f32(cfg.kv_dim), f32(cfg.kv_dim), f32(cfg.q_dim)
+        self.residual = f32(H)
         self.acts_k = torch.zeros(H // 256 * 292, dtype=torch.uint8, device=d)
-        self.acts_0 = torch.zeros(H // 32 * 36, dtype=torch.uint8, device=d)
-        self.acts_attn = torch.zeros(cfg.q_dim // 256 * 292, dtype=torch.uint8, device=d)
         self.logits = f32(cfg.vocab)
         self.token = torch.zeros(1, dtype=torch.int32, device=d)
         self.next_token = torch.zeros(1, dtype=torch.int32, device=d)
@@ -174,21 +173,11 @@ class Decoder:
         H = cfg.hidden
         dequantize_rows(Q.Q4_K, w.token_embd, H, cfg.vocab, rows=self.token, out=self.residual)
         for l, lw in enumerate(w.layers):
-            rmsnorm(self.residual, lw.attn_norm, cfg.eps, self.normed)
-            quantize_row_q8_k(self.normed, self.acts_k)
-            quantize_row_q8_0(self.normed, self.acts_0)
-            gemv_q8_k(Q.Q4_K, lw.attn_q, H, cfg.q_dim, self.acts_k, self.q)
-            gemv_q8_0(lw.attn_k, H, cfg.kv_dim, self.acts_0, self.k)
-            gemv_q8_k(lw.attn_v_format, lw.attn_v, H, cfg.kv_dim, self.acts_k, self.v)
-            _check(lib().rv_attn_decode_dev(self.attn.handle, l, _p(self.position), _p(self.q), _p(self.k),
-                                            _p(self.v), _p(lw.attn_q_norm), _p(lw.attn_k_norm), _p(self.attn_out),
-                                            s))
-            quantize_row_q8_k(self.attn_out, self.acts_attn)
-            gemv_q8_k(Q.Q5_K, lw.attn_output, cfg.q_dim, H, self.acts_attn, self.o_proj)
-            _check(lib().rv_vec_add(_p(self.residual), _p(self.o_proj), H, s))
+            # attention half (forward.rs:2572-2652), residual in place
+            self.attn.block(l, self.attn_w[l], self.residual, position_dev=self.position)
+            # MoE block (forward.rs:2654-2754), residual in place
             self.moe.forward(w.experts, l, lw.ffn_norm, lw.router, self.residual)
-        rmsnorm(self.residual, w.output_norm, cfg.eps, self.normed)
-        quantize_row_q8_k(self.normed, self.acts_k)
+        rmsnorm_quantize(self.residual, w.output_norm, cfg.eps, self.acts_k)
         gemv_q8_k(Q.Q6_K, w.lm_head, H, cfg.vocab, self.acts_k, self.logits)
         _check(lib().rv_argmax(_p(self.logits), cfg.vocab, _p(self.next_token), s))
         _check(lib().rv_decode_advance(_p(self.position), _p(self.next_token), _p(self.token), _p(self.ids),

@@ -133,3 +133,85 @@ def test_engine_errors_and_clear(rv):
     eng.decode(0, 0, q, k, v, w, w)
     torch.cuda.synchronize()
     rv.device_status(0)
+
+
+def test_rmsnorm_quantize_bytes(rv, orc):
+    """rmsnorm (norm.rs:38-60) then quantize_row_q8_k and quantize_row_q8_0,
+    fused: the same bytes as the separate reference steps."""
+    rng = np.random.default_rng(21)
+    for n in (256, 2048, 4096):
+        x = (rng.standard_normal(n) * 3).astype(np.float32)
+        w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+        q8k = torch.zeros(n // 256 * 292, dtype=torch.uint8, device="cuda")
+        q80 = torch.zeros(n // 32 * 36, dtype=torch.uint8, device="cuda")
+        rv.rmsnorm_quantize(dev(x), dev(w), 1e-6, q8k, q80)
+        normed = orc.rmsnorm(x, w, 1e-6)
+        assert host(q8k).tobytes() == orc.quantize_row_q8_k(normed).tobytes()
+        assert host(q80).tobytes() == orc.quantize_row_q8_0(normed, orc.SCALAR).tobytes()
+
+
+@pytest.mark.parametrize("device_position", [False, True])
+def test_attn_block_matches_reference(rv, orc, device_position):
+    """rv_attn_block (forward.rs:2572-2652 for one layer, residual in place)
+    against the reference's step sequence on the oracle, over 40 positions."""
+    H, n_q, n_kv, hd, P = 2048, 32, 4, 128, 40
+    rng = np.random.default_rng(31)
+    eng = rv.AttnEngine(1, n_q, n_kv, hd, max_positions=P, rope_theta=1e6, eps=1e-6, hidden=H)
+    qd, kvd = n_q * hd, n_kv * hd
+    x_norm = rng.uniform(0.8, 1.2, H).astype(np.float32)
+    wq = orc.quantize_weights(orc.Q4_K, (rng.standard_normal(qd * H) * 0.02).astype(np.float32))
+    wk = orc.quantize_weights(orc.Q8_0, (rng.standard_normal(kvd * H) * 0.02).astype(np.float32))
+    wv = orc.quantize_weights(orc.Q6_K, (rng.standard_normal(kvd * H) * 0.02).astype(np.float32))
+    wo = orc.quantize_weights(orc.Q5_K, (rng.standard_normal(H * qd) * 0.02).astype(np.float32))
+    qn, kn = rng.uniform(0.8, 1.2, hd).astype(np.float32), rng.uniform(0.8, 1.2, hd).astype(np.float32)
+    d = [dev(a) for a in (x_norm, wq, wk, wv, wo, qn, kn)]
+    aw = rv.attn_weights(*d, attn_q_format=rv.QuantFormat.Q4_K, attn_v_format=rv.QuantFormat.Q6_K,
+                         attn_output_format=rv.QuantFormat.Q5_K)
+    kc, vc = np.zeros(P * kvd, np.uint16), np.zeros(P * kvd, np.uint16)
+    pos_d = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for pos in range(P):
+        x = rng.standard_normal(H).astype(np.float32)
+        res = dev(x)
+        if device_position:
+            pos_d.fill_(pos)
+            eng.block(0, aw, res, position_dev=pos_d)
+        else:
+            eng.block(0, aw, res, position=pos)
+        normed = orc.rmsnorm(x, x_norm, 1e-6)
+        a8k, a80 = orc.quantize_row_q8_k(normed), orc.quantize_row_q8_0(normed, orc.SCALAR)
+        q = orc.gemv(orc.Q4_K, wq, H, qd, a8k, impl=orc.LANES)
+        k = orc.gemv_q8_0(wk, H, kvd, a80, impl=orc.LANES)
+        v = orc.gemv(orc.Q6_K, wv, H, kvd, a8k, impl=orc.LANES)
+        out, _, _ = orc.attn_decode_step(q, k, v, qn, kn, kc, vc, pos, n_q, n_kv, hd, 1e-6, 1e6)
+        o = orc.gemv(orc.Q5_K, wo, qd, H, orc.quantize_row_q8_k(out), impl=orc.LANES)
+        want = (x + o).astype(np.float32)
+        assert host(res).tobytes() == want.tobytes(), pos
+    assert eng.len(0) == (0 if device_position else P)
+    rv.device_status(0)
+
+
+def test_argmax_edge_cases(rv):
+    """Sampler::argmax: first index wins ties, NaN never wins, all -inf or
+    NaN gives 0; unaligned starts and lengths not a multiple of 4."""
+    from ramvamp_b200.model import top1
+
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rng = np.random.default_rng(41)
+    cases = [rng.standard_normal(151936).astype(np.float32)]
+    t = rng.standard_normal(10007).astype(np.float32)
+    t[[17, 5000, 9999]] = 50.0
+    cases.append(t)
+    cases.append(np.full(33, -np.inf, np.float32))
+    cases.append(np.full(33, np.nan, np.float32))
+    t = rng.standard_normal(1000).astype(np.float32)
+    t[::3] = np.nan
+    t[500] = np.inf
+    t[900] = np.inf
+    cases.append(t)
+    cases.append(np.array([-np.inf, -1.0], np.float32))
+    for x in cases:
+        for shift in (0, 1, 2, 3):
+            buf = dev(np.concatenate([np.zeros(shift, np.float32), x]))
+            rc = rv.lib().rv_argmax(buf.data_ptr() + 4 * shift, x.size, out.data_ptr(), rv._stream())
+            assert rc == 0
+            assert int(host(out)[0]) == top1(x), (x.size, shift)
