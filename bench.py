@@ -234,7 +234,6 @@ def run_cuda(args):
                 resid.copy_(tokens[i:i + 1])
                 graph.replay()
 
-    run_steps(0, args.warmup)
     stream.synchronize()
     if world > 1:
         dist.barrier()
@@ -243,6 +242,7 @@ def run_cuda(args):
     clocks = ClockSampler(("GPU-" + uuid if uuid and not uuid.startswith("GPU-") else uuid) or str(dev))
     clocks.start()
     time.sleep(0.3)
+    run_steps(0, args.warmup)  # warm-up right before the timed steps
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ev0.record(stream)
@@ -454,7 +454,9 @@ def run_cuda_model(args):
     cfg = ModelConfig(n_layers=args.layers)
     w = Qwen3Weights.synthetic(cfg, seed=MODEL_SEED, device=dev)
     n_gen = args.warmup + args.steps
-    dec = Decoder(w, max_positions=MODEL_PROMPT + n_gen + 1, device=dev)
+    e2e_steps = min(args.steps, 16)
+    # room for the prompt, the warm-up and timed tokens and the e2e tokens
+    dec = Decoder(w, max_positions=MODEL_PROMPT + n_gen + e2e_steps + 1, device=dev)
     dec.capture()
     prompt = np.random.default_rng(SEED + rank).integers(0, cfg.vocab, MODEL_PROMPT).astype(np.int32)
     prompt_d = torch.from_numpy(prompt).cuda()
@@ -468,8 +470,6 @@ def run_cuda_model(args):
         if i + 1 < MODEL_PROMPT:
             dec.token.copy_(prompt_d[i + 1:i + 2])
     ev[1].record(stream)
-    for _ in range(args.warmup):
-        dec.step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -478,6 +478,10 @@ def run_cuda_model(args):
     clocks = ClockSampler(("GPU-" + uuid if uuid and not uuid.startswith("GPU-") else uuid) or str(dev))
     clocks.start()
     time.sleep(0.3)
+    # warm-up right before the timed steps, so the GPU is not coming out of
+    # the idle pause above
+    for _ in range(args.warmup):
+        dec.step()
     torch.cuda.synchronize()
     ev[2].record(stream)
     for _ in range(args.steps):
@@ -519,7 +523,6 @@ def run_cuda_model(args):
     tok_h = torch.zeros(1, dtype=torch.int32).pin_memory()
     out_h = torch.zeros(1, dtype=torch.int32).pin_memory()
     tok_h[0] = ids[-1]
-    e2e_steps = min(args.steps, 16)
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
@@ -530,6 +533,7 @@ def run_cuda_model(args):
         stream.synchronize()
         tok_h[0] = out_h[0]
     e2e_s = time.perf_counter() - t0
+    rv.device_status(dev)  # every step stayed inside the cache
     if world > 1:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -754,7 +758,6 @@ def run_cuda_batched(args):
                 resid.copy_(tokens[i % n_batches])
                 graph.replay() if graph is not None else step_body()
 
-    run_steps(0, args.warmup)
     stream.synchronize()
     if world > 1:
         dist.barrier()
@@ -763,6 +766,7 @@ def run_cuda_batched(args):
     clocks = ClockSampler(("GPU-" + uuid if uuid and not uuid.startswith("GPU-") else uuid) or str(dev))
     clocks.start()
     time.sleep(0.3)
+    run_steps(0, args.warmup)  # warm-up right before the timed steps
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ev0.record(stream)

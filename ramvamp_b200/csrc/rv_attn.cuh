@@ -12,6 +12,19 @@
 #pragma once
 #include "rv_kernels.cuh"
 
+// Positions of V staged per chunk by k_attn_softmax_out (two chunks of
+// RV_ATTN_VCHUNK * head_dim halves plus their probabilities in shared memory).
+#define RV_ATTN_VCHUNK 64
+__host__ __device__ inline size_t attn_out_smem(int hd) { return 2 * (size_t)RV_ATTN_VCHUNK * (2 * hd + 4); }
+
+// 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned).
+RV_DEVFN void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+RV_DEVFN void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+RV_DEVFN void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 struct AttnArgs {
   float *q;              // [n_heads][hd], normed + rotated in place
   float *k;              // [n_kv][hd], normed + rotated in place
@@ -177,22 +190,47 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
   const float inv = s_inv;
   for (int t = tid; t < positions; t += blockDim.x) pr[t] = __fmul_rn(pr[t], inv);
   __syncthreads();
+  // Values: one serial chain per output element over t ascending.  This kv
+  // head's V rows (hd halves each) and the probabilities are staged in
+  // shared memory RV_ATTN_VCHUNK positions at a time, double-buffered with
+  // 16-byte cp.async copies, so the chain reads on-chip memory while the
+  // next chunk streams in.  blockDim >= hd: thread i owns element i.
+  extern __shared__ __align__(16) uint8_t vsm[];
   const size_t kv_dim = (size_t)a.n_kv * a.hd;
   const uint16_t *vc = a.v_cache + (size_t)kvh * a.hd;
-  for (int i = tid; i < a.hd; i += blockDim.x) {
-    float acc = 0.0f;
-    int t = 0;
-    for (; t + 4 <= positions; t += 4) {
-      const float v0 = h2f(vc[(size_t)t * kv_dim + i]), v1 = h2f(vc[(size_t)(t + 1) * kv_dim + i]);
-      const float v2 = h2f(vc[(size_t)(t + 2) * kv_dim + i]), v3 = h2f(vc[(size_t)(t + 3) * kv_dim + i]);
-      acc = __fadd_rn(acc, __fmul_rn(pr[t], v0));
-      acc = __fadd_rn(acc, __fmul_rn(pr[t + 1], v1));
-      acc = __fadd_rn(acc, __fmul_rn(pr[t + 2], v2));
-      acc = __fadd_rn(acc, __fmul_rn(pr[t + 3], v3));
+  const int row_bytes = 2 * a.hd, pieces = a.hd / 8;
+  uint8_t *vbuf[2] = {vsm, vsm + RV_ATTN_VCHUNK * row_bytes};
+  float *pbuf[2] = {(float *)(vsm + 2 * RV_ATTN_VCHUNK * row_bytes),
+                    (float *)(vsm + 2 * RV_ATTN_VCHUNK * row_bytes) + RV_ATTN_VCHUNK};
+  const int nchunks = (positions + RV_ATTN_VCHUNK - 1) / RV_ATTN_VCHUNK;
+  auto stage = [&](int ch) {
+    const int t0 = ch * RV_ATTN_VCHUNK, n = min(RV_ATTN_VCHUNK, positions - t0);
+    uint8_t *dst = vbuf[ch & 1];
+    for (int k = tid; k < n * pieces; k += blockDim.x) {
+      const int r = k / pieces, c = k % pieces;
+      cp_async16(dst + r * row_bytes + 16 * c, (const uint8_t *)(vc + (size_t)(t0 + r) * kv_dim) + 16 * c);
     }
-    for (; t < positions; t++) acc = __fadd_rn(acc, __fmul_rn(pr[t], h2f(vc[(size_t)t * kv_dim + i])));
-    a.out[(size_t)h * a.hd + i] = acc;
+    for (int r = tid; r < n; r += blockDim.x) pbuf[ch & 1][r] = pr[t0 + r];
+    cp_async_commit();
+  };
+  float acc = 0.0f;
+  stage(0);
+  for (int ch = 0; ch < nchunks; ch++) {
+    if (ch + 1 < nchunks) {
+      stage(ch + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint16_t *vs = (const uint16_t *)vbuf[ch & 1];
+    const float *ps = pbuf[ch & 1];
+    const int n = min(RV_ATTN_VCHUNK, positions - ch * RV_ATTN_VCHUNK);
+    if (tid < a.hd)
+      for (int r = 0; r < n; r++) acc = __fadd_rn(acc, __fmul_rn(ps[r], h2f(vs[r * a.hd + tid])));
+    __syncthreads();  // this buffer is restaged for chunk ch + 2
   }
+  if (tid < a.hd) a.out[(size_t)h * a.hd + tid] = acc;
 }
 
 // rope_neox_heads (rope.rs:80-111) for one position, the factors passed by

@@ -146,6 +146,7 @@ static int ensure_device(int dev) {
   cudaFuncSetAttribute(k_gemv_q8_0<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv_multi, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_attn_softmax_out, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv_q8_0<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   g_dev_sms[dev] = 148;
   cudaDeviceGetAttribute(&g_dev_sms[dev], cudaDevAttrMultiProcessorCount, dev);
@@ -1728,7 +1729,7 @@ static int attn_launch_core(const AttnArgs &args, cudaStream_t s) {
   const int tiles = (positions + 127) / 128;
   dim3 grid((unsigned)args.n_heads, (unsigned)(args.pos_dev ? std::min(tiles, 16) : tiles));
   k_attn_scores<<<grid, 128, args.hd * sizeof(float), s>>>(args);
-  k_attn_softmax_out<<<(unsigned)args.n_heads, args.hd > 128 ? args.hd : 128, 0, s>>>(args);
+  k_attn_softmax_out<<<(unsigned)args.n_heads, args.hd > 128 ? args.hd : 128, attn_out_smem(args.hd), s>>>(args);
   RV_LAUNCH_CHECK();
   return RV_OK;
 }
@@ -1930,8 +1931,8 @@ extern "C" int rv_attention(const float *q, const uint16_t *k_cache, const uint1
   if (scratch_len < sat_mul(2 * n_heads, positions))
     RV_FAIL(RV_ERR_LENGTH_MISMATCH, "attention: scratch of %zu floats, needs %zu", scratch_len,
             sat_mul(2 * n_heads, positions));
-  if (!q || !k_cache || !v_cache || !scratch || !out || ((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 1))
-    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "attention: null pointer or k_cache not 16-byte aligned");
+  if (!q || !k_cache || !v_cache || !scratch || !out || ((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15))
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "attention: null pointer or caches not 16-byte aligned");
   int rc = ensure_current_device();
   if (rc) return rc;
   AttnArgs args{};

@@ -249,3 +249,31 @@ def top1(logits) -> int:
     if not valid.any():
         return 0
     return int(np.flatnonzero(valid & (x == x[valid].max()))[0])
+
+
+def _main(argv=None):
+    """python -m ramvamp_b200.model [--layers N] [--profile-step K]: build
+    the synthetic Qwen3 model, run K eager steps, then one more inside the
+    NVTX range "step" (for a profiler restricted to that range)."""
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--profile-step", type=int, default=8)
+    a = ap.parse_args(argv)
+    w = Qwen3Weights.synthetic(ModelConfig(n_layers=a.layers), seed=1)
+    dec = Decoder(w, max_positions=a.profile_step + 8)
+    dec.reset()
+    dec.token.fill_(5)
+    for _ in range(a.profile_step):
+        dec.step()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("step")
+    dec.step()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print("next token", int(dec.next_token.item()))
+
+
+if __name__ == "__main__":
+    _main()
