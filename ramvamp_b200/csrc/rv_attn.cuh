@@ -15,7 +15,9 @@
 // Positions of V staged per chunk by k_attn_softmax_out (two chunks of
 // RV_ATTN_VCHUNK * head_dim halves plus their probabilities in shared memory).
 #define RV_ATTN_VCHUNK 64
-__host__ __device__ inline size_t attn_out_smem(int hd) { return 2 * (size_t)RV_ATTN_VCHUNK * (2 * hd + 4); }
+__host__ __device__ inline size_t attn_out_smem(int hd, int hpc = 1) {
+  return 2 * (size_t)RV_ATTN_VCHUNK * (2 * hd + 4 * hpc);
+}
 
 // 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned).
 RV_DEVFN void cp_async16(void *dst, const void *src) {
@@ -37,6 +39,7 @@ struct AttnArgs {
   float *scores;         // [n_heads][positions]
   float *probs;          // [n_heads][positions]
   float *out;            // [n_heads][hd]
+  uint8_t *q8k_out;      // when set (2 heads of 128 per CTA): Q8_K of out, one block per CTA
   int n_heads, n_kv, hd;
   int position;          // the row appended; attention covers 0..position
   const int *pos_dev;    // when set, the position is read here when the kernels run
@@ -129,40 +132,45 @@ __global__ void __launch_bounds__(128) k_attn_scores(AttnArgs a) {
   }
 }
 
-// One CTA (hd threads) per query head: softmax over the positions
-// (softmax.rs:18-40: f32 max, e = exp(f64(s) - max) in f64, f32 copies, the
-// f64 sum in position order, f32 reciprocal), then v_reduce_scalar:
-// out[i] = sum over t ascending of p_t * V[t][i], separate multiply and add.
-// The f64 sum is taken in blocks; summation in any order of P positive
-// terms errs by at most (P-1)u of the sum, so block and serial sums differ by
-// at most 2(P-1)u: when f32(1/sum) is the same for every sum within that
-// bound, the blocked sum gives the serial result; otherwise thread 0 redoes
-// the serial sum.
+// HPC query heads per CTA (threads split into HPC segments, segment j
+// owning head blockIdx.x * HPC + j; the heads share one kv head): softmax
+// over the positions (softmax.rs:18-40: f32 max, e = exp(f64(s) - max) in
+// f64, f32 copies, the f64 sum in position order, f32 reciprocal), then
+// v_reduce_scalar: out[i] = sum over t ascending of p_t * V[t][i], separate
+// multiply and add.  The f64 sum is taken in blocks; summation in any order
+// of P positive terms errs by at most (P-1)u of the sum, so block and serial
+// sums differ by at most 2(P-1)u: when f32(1/sum) is the same for every sum
+// within that bound, the blocked sum gives the serial result; otherwise the
+// segment's first thread redoes the serial sum.  With q8k_out set and
+// HPC * hd == 256 the CTA's outputs are one Q8_K block, quantized here
+// (quantize_row_q8_k, the input of attn_output).
+template <int HPC>
 __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
   __shared__ double red[34];
-  __shared__ float s_max, s_inv;
+  __shared__ float s_max[HPC], s_inv[HPC];
   const int position = attn_position(a);
   if (position < 0) return;
-  const int h = blockIdx.x, group = a.n_heads / a.n_kv, kvh = h / group;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seg = blockDim.x / HPC, j = tid / seg, st = tid % seg, wps = seg >> 5, w0 = j * wps;
+  const int h = blockIdx.x * HPC + j, group = a.n_heads / a.n_kv, kvh = (blockIdx.x * HPC) / group;
   const int positions = position + 1;
   const float *sc = a.scores + (size_t)h * positions;
   float *pr = a.probs + (size_t)h * positions;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
   float mx = -INFINITY;
-  for (int t = tid; t < positions; t += blockDim.x) mx = fmaxf(mx, sc[t]);
+  for (int t = st; t < positions; t += seg) mx = fmaxf(mx, sc[t]);
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(RV_FULL, mx, o));
   if (lane == 0) red[warp] = (double)mx;
   __syncthreads();
-  if (tid == 0) {
+  if (st == 0) {
     float m = -INFINITY;
-    for (int w = 0; w < nw; w++) m = fmaxf(m, (float)red[w]);
-    s_max = m;
+    for (int w = w0; w < w0 + wps; w++) m = fmaxf(m, (float)red[w]);
+    s_max[j] = m;
   }
   __syncthreads();
-  const double dmx = (double)s_max;
+  const double dmx = (double)s_max[j];
   double part = 0.0;
-  for (int t = tid; t < positions; t += blockDim.x) {
+  for (int t = st; t < positions; t += seg) {
     const double e = exp(__dsub_rn((double)sc[t], dmx));
     pr[t] = __double2float_rn(e);
     part = __dadd_rn(part, e);
@@ -172,10 +180,10 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
   __syncthreads();
   if (lane == 0) red[warp] = part;
   __syncthreads();
-  if (tid == 0) {
-    double s = 0.0;
-    for (int w = 0; w < nw; w++) s = __dadd_rn(s, red[w]);
-    const double r = __drcp_rn(s);
+  if (st == 0) {
+    double sum = 0.0;
+    for (int w = w0; w < w0 + wps; w++) sum = __dadd_rn(sum, red[w]);
+    const double r = __drcp_rn(sum);
     const unsigned long long bound = 2ull * (unsigned long long)positions + 2ull;
     const int k = 52 - (64 - __clzll((long long)bound));
     float inv = __double2float_rn(r);
@@ -184,24 +192,25 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
       for (int t = 0; t < positions; t++) ser = __dadd_rn(ser, exp(__dsub_rn((double)sc[t], dmx)));
       inv = __double2float_rn(__drcp_rn(ser));
     }
-    s_inv = inv;
+    s_inv[j] = inv;
   }
   __syncthreads();
-  const float inv = s_inv;
-  for (int t = tid; t < positions; t += blockDim.x) pr[t] = __fmul_rn(pr[t], inv);
+  const float inv = s_inv[j];
+  for (int t = st; t < positions; t += seg) pr[t] = __fmul_rn(pr[t], inv);
   __syncthreads();
-  // Values: one serial chain per output element over t ascending.  This kv
-  // head's V rows (hd halves each) and the probabilities are staged in
-  // shared memory RV_ATTN_VCHUNK positions at a time, double-buffered with
-  // 16-byte cp.async copies, so the chain reads on-chip memory while the
-  // next chunk streams in.  blockDim >= hd: thread i owns element i.
+  // Values: one serial chain per output element over t ascending.  The kv
+  // head's V rows (hd halves each) and each head's probabilities are staged
+  // in shared memory RV_ATTN_VCHUNK positions at a time, double-buffered
+  // with 16-byte cp.async copies, so the chains read on-chip memory while
+  // the next chunk streams in.  Thread st (< hd) of segment j owns element st
+  // of head j.
   extern __shared__ __align__(16) uint8_t vsm[];
   const size_t kv_dim = (size_t)a.n_kv * a.hd;
   const uint16_t *vc = a.v_cache + (size_t)kvh * a.hd;
   const int row_bytes = 2 * a.hd, pieces = a.hd / 8;
   uint8_t *vbuf[2] = {vsm, vsm + RV_ATTN_VCHUNK * row_bytes};
-  float *pbuf[2] = {(float *)(vsm + 2 * RV_ATTN_VCHUNK * row_bytes),
-                    (float *)(vsm + 2 * RV_ATTN_VCHUNK * row_bytes) + RV_ATTN_VCHUNK};
+  float *pbuf0 = (float *)(vsm + 2 * RV_ATTN_VCHUNK * row_bytes);
+  float *pbuf[2] = {pbuf0, pbuf0 + HPC * RV_ATTN_VCHUNK};
   const int nchunks = (positions + RV_ATTN_VCHUNK - 1) / RV_ATTN_VCHUNK;
   auto stage = [&](int ch) {
     const int t0 = ch * RV_ATTN_VCHUNK, n = min(RV_ATTN_VCHUNK, positions - t0);
@@ -210,7 +219,7 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
       const int r = k / pieces, c = k % pieces;
       cp_async16(dst + r * row_bytes + 16 * c, (const uint8_t *)(vc + (size_t)(t0 + r) * kv_dim) + 16 * c);
     }
-    for (int r = tid; r < n; r += blockDim.x) pbuf[ch & 1][r] = pr[t0 + r];
+    for (int r = st; r < n; r += seg) pbuf[ch & 1][j * RV_ATTN_VCHUNK + r] = pr[t0 + r];
     cp_async_commit();
   };
   float acc = 0.0f;
@@ -224,13 +233,24 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
     }
     __syncthreads();
     const uint16_t *vs = (const uint16_t *)vbuf[ch & 1];
-    const float *ps = pbuf[ch & 1];
+    const float *ps = pbuf[ch & 1] + j * RV_ATTN_VCHUNK;
     const int n = min(RV_ATTN_VCHUNK, positions - ch * RV_ATTN_VCHUNK);
-    if (tid < a.hd)
-      for (int r = 0; r < n; r++) acc = __fadd_rn(acc, __fmul_rn(ps[r], h2f(vs[r * a.hd + tid])));
+    if (st < a.hd)
+      for (int r = 0; r < n; r++) acc = __fadd_rn(acc, __fmul_rn(ps[r], h2f(vs[r * a.hd + st])));
     __syncthreads();  // this buffer is restaged for chunk ch + 2
   }
-  if (tid < a.hd) a.out[(size_t)h * a.hd + tid] = acc;
+  if (st < a.hd) a.out[(size_t)h * a.hd + st] = acc;
+  if (HPC == 2 && a.q8k_out && a.hd == 128) {
+    float *ys = (float *)vsm;  // the staging buffers are free now
+    if (st < a.hd) ys[j * a.hd + st] = acc;
+    __syncthreads();
+    if (warp == 0) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = ys[8 * lane + e];
+      q8k_quantize_warp(v, lane, a.q8k_out + (size_t)blockIdx.x * 292);
+    }
+  }
 }
 
 // rope_neox_heads (rope.rs:80-111) for one position, the factors passed by

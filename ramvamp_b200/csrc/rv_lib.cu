@@ -146,7 +146,8 @@ static int ensure_device(int dev) {
   cudaFuncSetAttribute(k_gemv_q8_0<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv_multi, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_attn_softmax_out, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_attn_softmax_out<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_attn_softmax_out<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_gemv_q8_0<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   g_dev_sms[dev] = 148;
   cudaDeviceGetAttribute(&g_dev_sms[dev], cudaDevAttrMultiProcessorCount, dev);
@@ -1721,6 +1722,12 @@ extern "C" int rv_attn_copy_cache(const rv_attn *a, uint32_t layer, uint32_t pos
 
 // Scores and softmax-out over positions 0..args.position, shared by
 // rv_attn_decode and rv_attention.
+// The Q8_K of the attention output is formed inside the softmax-out kernel
+// when two heads of 128 (one Q8_K block) share a CTA and a kv head.
+static bool attn_fold_q8k(const AttnArgs &args) {
+  return args.q8k_out && args.hd == 128 && (args.n_heads / args.n_kv) % 2 == 0;
+}
+
 static int attn_launch_core(const AttnArgs &args, cudaStream_t s) {
   // Host mode: one 128-position tile per CTA row.  Device mode (the
   // position known only when the kernels run): up to 16 tile rows that
@@ -1729,7 +1736,10 @@ static int attn_launch_core(const AttnArgs &args, cudaStream_t s) {
   const int tiles = (positions + 127) / 128;
   dim3 grid((unsigned)args.n_heads, (unsigned)(args.pos_dev ? std::min(tiles, 16) : tiles));
   k_attn_scores<<<grid, 128, args.hd * sizeof(float), s>>>(args);
-  k_attn_softmax_out<<<(unsigned)args.n_heads, args.hd > 128 ? args.hd : 128, attn_out_smem(args.hd), s>>>(args);
+  if (attn_fold_q8k(args))
+    k_attn_softmax_out<2><<<(unsigned)args.n_heads / 2, 256, attn_out_smem(args.hd, 2), s>>>(args);
+  else
+    k_attn_softmax_out<1><<<(unsigned)args.n_heads, args.hd > 128 ? args.hd : 128, attn_out_smem(args.hd), s>>>(args);
   RV_LAUNCH_CHECK();
   return RV_OK;
 }
@@ -1748,7 +1758,7 @@ extern "C" int rv_attn_decode(rv_attn *a, uint32_t layer, uint32_t position, flo
   int prev = -1;
   RV_CUDA(cudaGetDevice(&prev));
   if (prev != a->device) RV_CUDA(cudaSetDevice(a->device));
-  AttnArgs args;
+  AttnArgs args{};
   args.q = q;
   args.k = k;
   args.v = v;
@@ -1855,7 +1865,7 @@ extern "C" int rv_attn_block(rv_attn *a, uint32_t layer, const rv_attn_weights *
   const size_t smem = 16 + ((R * rb_max + 15) & ~(size_t)15) + 16 + act_max + 16;
   k_gemv_multi<<<m.cta0[3], R * 8, smem, s>>>(m);
   // 3. QK-norm, RoPE, append, attention
-  AttnArgs args;
+  AttnArgs args{};
   args.q = a->q;
   args.k = a->k;
   args.v = a->v;
@@ -1867,6 +1877,7 @@ extern "C" int rv_attn_block(rv_attn *a, uint32_t layer, const rv_attn_weights *
   args.scores = a->scratch;
   args.probs = a->scratch + (size_t)c.n_heads * c.max_positions;
   args.out = a->attn_out;
+  args.q8k_out = a->acts_attn;  // the block quantizes the output in the softmax-out kernel where it can
   args.n_heads = (int)c.n_heads;
   args.n_kv = (int)c.n_kv_heads;
   args.hd = (int)c.head_dim;
@@ -1882,7 +1893,8 @@ extern "C" int rv_attn_block(rv_attn *a, uint32_t layer, const rv_attn_weights *
     return rc;
   }
   // 4. Q8_K of the attention output, 5. attn_output + residual add
-  k_quantize_q8k<<<(unsigned)((qd / 256 + 7) / 8), 256, 0, s>>>(a->attn_out, a->acts_attn, qd / 256);
+  if (!attn_fold_q8k(args))
+    k_quantize_q8k<<<(unsigned)((qd / 256 + 7) / 8), 256, 0, s>>>(a->attn_out, a->acts_attn, qd / 256);
   GemvArgs g = gemv_job(w->attn_output, qd / 256 * rv_fmt_block_bytes(w->attn_output_format), (int)(qd / 256), H,
                         a->acts_attn, residual, 4);
   g.accumulate = 1;
@@ -1936,6 +1948,7 @@ extern "C" int rv_attention(const float *q, const uint16_t *k_cache, const uint1
   int rc = ensure_current_device();
   if (rc) return rc;
   AttnArgs args{};
+  args.q8k_out = nullptr;
   args.q = const_cast<float *>(q);
   args.k_cache = const_cast<uint16_t *>(k_cache);
   args.v_cache = const_cast<uint16_t *>(v_cache);
@@ -1963,7 +1976,7 @@ extern "C" int rv_attn_decode_dev(rv_attn *a, uint32_t layer, const int32_t *pos
   int prev = -1;
   RV_CUDA(cudaGetDevice(&prev));
   if (prev != a->device) RV_CUDA(cudaSetDevice(a->device));
-  AttnArgs args;
+  AttnArgs args{};
   args.q = q;
   args.k = k;
   args.v = v;
