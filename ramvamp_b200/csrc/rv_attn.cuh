@@ -132,6 +132,87 @@ __global__ void __launch_bounds__(128) k_attn_scores(AttnArgs a) {
   }
 }
 
+// k_attn_prep folded into k_attn_scores (rv_attn_block): CTA (h, y) forms
+// its own normed and rotated query head (rmsnorm_in_place + rotate_head, as
+// k_attn_prep), and the CTA whose tile holds the current position also
+// forms this step's key for its kv head, rounded through f16 as the cache
+// holds it, and uses it for that position; the first query head of each kv
+// head (h % group == 0) writes that position's K and V cache rows.  No CTA
+// of this launch reads the current cache row; the next kernel reads V after
+// the launch boundary.
+RV_DEVFN void attn_norm_rope(const float *x, const float *w, const float2 *rot, int hd, float eps, float *xs,
+                             double *red) {
+  for (int k = threadIdx.x; k < hd; k += blockDim.x) xs[k] = x[k];
+  __syncthreads();
+  const float inv = rms_inv_block(xs, (size_t)hd, eps, red);
+  for (int k = threadIdx.x; k < hd; k += blockDim.x) xs[k] = __fmul_rn(__fmul_rn(xs[k], inv), w[k]);
+  __syncthreads();
+  const int half = hd >> 1;
+  float y0 = 0.0f, y1 = 0.0f;
+  const int k = threadIdx.x;
+  if (k < half) {
+    const float2 cs = rot[k];
+    const float x0 = xs[k], x1 = xs[k + half];
+    y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+    y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+  }
+  __syncthreads();
+  if (k < half) {
+    xs[k] = y0;
+    xs[k + half] = y1;
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(128) k_attn_scores_prep(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  double *red = (double *)sm;
+  float *qs = (float *)(sm + 34 * sizeof(double));
+  float *ks = qs + a.hd;
+  const int position = attn_position(a);
+  if (position < 0) return;
+  const int h = blockIdx.x, group = a.n_heads / a.n_kv, kvh = h / group;
+  const float2 *rot = a.rot + (size_t)position * (a.hd >> 1);
+  const size_t kv_dim = (size_t)a.n_kv * a.hd;
+  attn_norm_rope(a.q + (size_t)h * a.hd, a.q_norm, rot, a.hd, a.eps, qs, red);
+  const bool holds_pos = (int)blockIdx.y == (position / (int)blockDim.x) % (int)gridDim.y;
+  if (holds_pos) {
+    attn_norm_rope(a.k + (size_t)kvh * a.hd, a.k_norm, rot, a.hd, a.eps, ks, red);
+    const bool writer = h % group == 0;
+    uint16_t *kc = a.k_cache + (size_t)position * kv_dim + (size_t)kvh * a.hd;
+    uint16_t *vc = a.v_cache + (size_t)position * kv_dim + (size_t)kvh * a.hd;
+    const float *vh = a.v + (size_t)kvh * a.hd;
+    for (int k = threadIdx.x; k < a.hd; k += blockDim.x) {
+      const uint16_t kb = f32_to_f16_bits(ks[k]);
+      ks[k] = h2f(kb);  // the value attention reads back from the cache
+      if (writer) {
+        kc[k] = kb;
+        vc[k] = f32_to_f16_bits(vh[k]);
+      }
+    }
+    __syncthreads();
+  }
+  const int positions = position + 1;
+  for (int t = blockIdx.y * blockDim.x + threadIdx.x; t < positions; t += gridDim.y * blockDim.x) {
+    float acc = 0.0f;
+    if (t == position) {
+      for (int i = 0; i < a.hd; i++) acc = __fadd_rn(acc, __fmul_rn(qs[i], ks[i]));
+    } else {
+      const uint4 *kr = (const uint4 *)(a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd);
+      for (int c = 0; c < a.hd / 8; c++) {
+        const uint4 u = kr[c];
+        const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j], h2f((uint16_t)(wds[j] & 0xFFFFu))));
+          acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j + 1], h2f((uint16_t)(wds[j] >> 16))));
+        }
+      }
+    }
+    a.scores[(size_t)h * positions + t] = __fmul_rn(a.scale, acc);
+  }
+}
+
 // HPC query heads per CTA (threads split into HPC segments, segment j
 // owning head blockIdx.x * HPC + j; the heads share one kv head): softmax
 // over the positions (softmax.rs:18-40: f32 max, e = exp(f64(s) - max) in

@@ -1728,14 +1728,17 @@ static bool attn_fold_q8k(const AttnArgs &args) {
   return args.q8k_out && args.hd == 128 && (args.n_heads / args.n_kv) % 2 == 0;
 }
 
-static int attn_launch_core(const AttnArgs &args, cudaStream_t s) {
+static int attn_launch_core(const AttnArgs &args, cudaStream_t s, bool fused_prep = false) {
   // Host mode: one 128-position tile per CTA row.  Device mode (the
   // position known only when the kernels run): up to 16 tile rows that
   // stride over the positions.
   const int positions = args.pos_dev ? args.max_positions : args.position + 1;
   const int tiles = (positions + 127) / 128;
   dim3 grid((unsigned)args.n_heads, (unsigned)(args.pos_dev ? std::min(tiles, 16) : tiles));
-  k_attn_scores<<<grid, 128, args.hd * sizeof(float), s>>>(args);
+  if (fused_prep)
+    k_attn_scores_prep<<<grid, 128, 34 * sizeof(double) + 2 * args.hd * sizeof(float), s>>>(args);
+  else
+    k_attn_scores<<<grid, 128, args.hd * sizeof(float), s>>>(args);
   if (attn_fold_q8k(args))
     k_attn_softmax_out<2><<<(unsigned)args.n_heads / 2, 256, attn_out_smem(args.hd, 2), s>>>(args);
   else
@@ -1886,8 +1889,7 @@ extern "C" int rv_attn_block(rv_attn *a, uint32_t layer, const rv_attn_weights *
   args.max_positions = (int)c.max_positions;
   args.eps = c.eps;
   args.scale = a->scale;
-  k_attn_prep<<<c.n_heads + c.n_kv_heads, c.head_dim, 34 * sizeof(double) + c.head_dim * sizeof(float), s>>>(args);
-  int rc = attn_launch_core(args, s);
+  int rc = attn_launch_core(args, s, /*fused_prep=*/true);
   if (rc) {
     if (prev != a->device) cudaSetDevice(prev);
     return rc;
