@@ -102,6 +102,39 @@ __global__ void __launch_bounds__(256) k_attn_prep(AttnArgs a) {
   }
 }
 
+// q . K[t] with one f32 accumulator over i ascending (separate multiply and
+// add).  For head_dim 128 the whole 256-byte row is loaded before the chain
+// starts, so the loads overlap instead of each waiting on the adds.
+RV_DEVFN float attn_dot_row(const float *qs, const uint16_t *krow, int hd) {
+  const uint4 *kr = (const uint4 *)krow;
+  float acc = 0.0f;
+  if (hd == 128) {
+    uint4 u[16];
+#pragma unroll
+    for (int c = 0; c < 16; c++) u[c] = kr[c];
+#pragma unroll
+    for (int c = 0; c < 16; c++) {
+      const uint32_t wds[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j], h2f((uint16_t)(wds[j] & 0xFFFFu))));
+        acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j + 1], h2f((uint16_t)(wds[j] >> 16))));
+      }
+    }
+    return acc;
+  }
+  for (int c = 0; c < hd / 8; c++) {
+    const uint4 u = kr[c];
+    const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j], h2f((uint16_t)(wds[j] & 0xFFFFu))));
+      acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j + 1], h2f((uint16_t)(wds[j] >> 16))));
+    }
+  }
+  return acc;
+}
+
 // qk_scores_scalar (attention.rs): scores[h][t] = scale * (q_h . K[t]) with
 // one f32 accumulator over i ascending, separate multiply and add.  Grid
 // (n_heads, tiles); thread = position, CTAs striding over 128-position
@@ -117,17 +150,7 @@ __global__ void __launch_bounds__(128) k_attn_scores(AttnArgs a) {
   const int positions = position + 1;
   const size_t kv_dim = (size_t)a.n_kv * a.hd;
   for (int t = blockIdx.y * blockDim.x + threadIdx.x; t < positions; t += gridDim.y * blockDim.x) {
-    const uint4 *kr = (const uint4 *)(a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd);
-    float acc = 0.0f;
-    for (int c = 0; c < a.hd / 8; c++) {
-      const uint4 u = kr[c];
-      const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j], h2f((uint16_t)(wds[j] & 0xFFFFu))));
-        acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j + 1], h2f((uint16_t)(wds[j] >> 16))));
-      }
-    }
+    const float acc = attn_dot_row(qs, a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd, a.hd);
     a.scores[(size_t)h * positions + t] = __fmul_rn(a.scale, acc);
   }
 }
@@ -198,16 +221,7 @@ __global__ void __launch_bounds__(128) k_attn_scores_prep(AttnArgs a) {
     if (t == position) {
       for (int i = 0; i < a.hd; i++) acc = __fadd_rn(acc, __fmul_rn(qs[i], ks[i]));
     } else {
-      const uint4 *kr = (const uint4 *)(a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd);
-      for (int c = 0; c < a.hd / 8; c++) {
-        const uint4 u = kr[c];
-        const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j], h2f((uint16_t)(wds[j] & 0xFFFFu))));
-          acc = __fadd_rn(acc, __fmul_rn(qs[8 * c + 2 * j + 1], h2f((uint16_t)(wds[j] >> 16))));
-        }
-      }
+      acc = attn_dot_row(qs, a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd, a.hd);
     }
     a.scores[(size_t)h * positions + t] = __fmul_rn(a.scale, acc);
   }
@@ -289,18 +303,19 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
   const size_t kv_dim = (size_t)a.n_kv * a.hd;
   const uint16_t *vc = a.v_cache + (size_t)kvh * a.hd;
   const int row_bytes = 2 * a.hd, pieces = a.hd / 8;
-  uint8_t *vbuf[2] = {vsm, vsm + RV_ATTN_VCHUNK * row_bytes};
   float *pbuf0 = (float *)(vsm + 2 * RV_ATTN_VCHUNK * row_bytes);
-  float *pbuf[2] = {pbuf0, pbuf0 + HPC * RV_ATTN_VCHUNK};
+  // buffer b of the V rows and of the probabilities
+  auto vbuf = [&](int b) { return vsm + b * RV_ATTN_VCHUNK * row_bytes; };
+  auto pbuf = [&](int b) { return pbuf0 + b * HPC * RV_ATTN_VCHUNK; };
   const int nchunks = (positions + RV_ATTN_VCHUNK - 1) / RV_ATTN_VCHUNK;
   auto stage = [&](int ch) {
     const int t0 = ch * RV_ATTN_VCHUNK, n = min(RV_ATTN_VCHUNK, positions - t0);
-    uint8_t *dst = vbuf[ch & 1];
+    uint8_t *dst = vbuf(ch & 1);
     for (int k = tid; k < n * pieces; k += blockDim.x) {
       const int r = k / pieces, c = k % pieces;
       cp_async16(dst + r * row_bytes + 16 * c, (const uint8_t *)(vc + (size_t)(t0 + r) * kv_dim) + 16 * c);
     }
-    for (int r = st; r < n; r += seg) pbuf[ch & 1][j * RV_ATTN_VCHUNK + r] = pr[t0 + r];
+    for (int r = st; r < n; r += seg) pbuf(ch & 1)[j * RV_ATTN_VCHUNK + r] = pr[t0 + r];
     cp_async_commit();
   };
   float acc = 0.0f;
@@ -313,11 +328,13 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const uint16_t *vs = (const uint16_t *)vbuf[ch & 1];
-    const float *ps = pbuf[ch & 1] + j * RV_ATTN_VCHUNK;
+    const uint16_t *vs = (const uint16_t *)vbuf(ch & 1);
+    const float *ps = pbuf(ch & 1) + j * RV_ATTN_VCHUNK;
     const int n = min(RV_ATTN_VCHUNK, positions - ch * RV_ATTN_VCHUNK);
-    if (st < a.hd)
+    if (st < a.hd) {
+#pragma unroll 8
       for (int r = 0; r < n; r++) acc = __fadd_rn(acc, __fmul_rn(ps[r], h2f(vs[r * a.hd + st])));
+    }
     __syncthreads();  // this buffer is restaged for chunk ch + 2
   }
   if (st < a.hd) a.out[(size_t)h * a.hd + st] = acc;
