@@ -19,14 +19,6 @@ __host__ __device__ inline size_t attn_out_smem(int hd, int hpc = 1) {
   return 2 * (size_t)RV_ATTN_VCHUNK * (2 * hd + 4 * hpc);
 }
 
-// 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned).
-RV_DEVFN void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-RV_DEVFN void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-RV_DEVFN void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 struct AttnArgs {
   float *q;              // [n_heads][hd], normed + rotated in place
   float *k;              // [n_kv][hd], normed + rotated in place
@@ -163,26 +155,41 @@ __global__ void __launch_bounds__(128) k_attn_scores(AttnArgs a) {
 // head (h % group == 0) writes that position's K and V cache rows.  No CTA
 // of this launch reads the current cache row; the next kernel reads V after
 // the launch boundary.
-RV_DEVFN void attn_norm_rope(const float *x, const float *w, const float2 *rot, int hd, float eps, float *xs,
-                             double *red) {
-  for (int k = threadIdx.x; k < hd; k += blockDim.x) xs[k] = x[k];
-  __syncthreads();
-  const float inv = rms_inv_block(xs, (size_t)hd, eps, red);
-  for (int k = threadIdx.x; k < hd; k += blockDim.x) xs[k] = __fmul_rn(__fmul_rn(xs[k], inv), w[k]);
-  __syncthreads();
-  const int half = hd >> 1;
-  float y0 = 0.0f, y1 = 0.0f;
-  const int k = threadIdx.x;
+// One head's inputs for attn_norm_rope, held in registers: thread k < hd/2
+// owns the rotation pair (k, k + hd/2) of x and of the norm weights and the
+// pair's cos/sin.  Loaded at kernel entry so that every global load of the
+// launch is in flight at once.
+struct HeadPair {
+  float x0, x1, w0, w1;
+  float2 cs;
+};
+RV_DEVFN HeadPair head_pair_load(const float *x, const float *w, const float2 *rot, int hd) {
+  HeadPair r{0.0f, 0.0f, 0.0f, 0.0f, make_float2(0.0f, 0.0f)};
+  const int k = threadIdx.x, half = hd >> 1;
   if (k < half) {
-    const float2 cs = rot[k];
-    const float x0 = xs[k], x1 = xs[k + half];
-    y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-    y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+    r.x0 = x[k];
+    r.x1 = x[k + half];
+    r.w0 = w[k];
+    r.w1 = w[k + half];
+    r.cs = rot[k];
+  }
+  return r;
+}
+
+// rmsnorm_in_place then rotate_head (as k_attn_prep) of one head whose
+// pairs the threads hold; the result lands in xs (smem[hd]).
+RV_DEVFN void attn_norm_rope(const HeadPair &r, int hd, float eps, float *xs, double *red) {
+  const int k = threadIdx.x, half = hd >> 1;
+  if (k < half) {
+    xs[k] = r.x0;
+    xs[k + half] = r.x1;
   }
   __syncthreads();
+  const float inv = rms_inv_block(xs, (size_t)hd, eps, red);  // ends with a CTA barrier: xs is free
   if (k < half) {
-    xs[k] = y0;
-    xs[k + half] = y1;
+    const float x0 = __fmul_rn(__fmul_rn(r.x0, inv), r.w0), x1 = __fmul_rn(__fmul_rn(r.x1, inv), r.w1);
+    xs[k] = __fsub_rn(__fmul_rn(x0, r.cs.x), __fmul_rn(x1, r.cs.y));
+    xs[k + half] = __fadd_rn(__fmul_rn(x0, r.cs.y), __fmul_rn(x1, r.cs.x));
   }
   __syncthreads();
 }
@@ -194,23 +201,35 @@ __global__ void __launch_bounds__(128) k_attn_scores_prep(AttnArgs a) {
   float *ks = qs + a.hd;
   const int position = attn_position(a);
   if (position < 0) return;
-  const int h = blockIdx.x, group = a.n_heads / a.n_kv, kvh = h / group;
-  const float2 *rot = a.rot + (size_t)position * (a.hd >> 1);
+  const int h = blockIdx.x, group = a.n_heads / a.n_kv, kvh = h / group, half = a.hd >> 1;
+  const float2 *rot = a.rot + (size_t)position * half;
   const size_t kv_dim = (size_t)a.n_kv * a.hd;
-  attn_norm_rope(a.q + (size_t)h * a.hd, a.q_norm, rot, a.hd, a.eps, qs, red);
   const bool holds_pos = (int)blockIdx.y == (position / (int)blockDim.x) % (int)gridDim.y;
+  const bool writer = holds_pos && h % group == 0;
+  const HeadPair qp = head_pair_load(a.q + (size_t)h * a.hd, a.q_norm, rot, a.hd);
+  HeadPair kp{0.0f, 0.0f, 0.0f, 0.0f, make_float2(0.0f, 0.0f)};
+  float v0 = 0.0f, v1 = 0.0f;
+  const float *vh = a.v + (size_t)kvh * a.hd;
+  if (holds_pos) kp = head_pair_load(a.k + (size_t)kvh * a.hd, a.k_norm, rot, a.hd);
+  if (writer && (int)threadIdx.x < half) {
+    v0 = vh[threadIdx.x];
+    v1 = vh[threadIdx.x + half];
+  }
+  attn_norm_rope(qp, a.hd, a.eps, qs, red);
   if (holds_pos) {
-    attn_norm_rope(a.k + (size_t)kvh * a.hd, a.k_norm, rot, a.hd, a.eps, ks, red);
-    const bool writer = h % group == 0;
+    attn_norm_rope(kp, a.hd, a.eps, ks, red);
     uint16_t *kc = a.k_cache + (size_t)position * kv_dim + (size_t)kvh * a.hd;
     uint16_t *vc = a.v_cache + (size_t)position * kv_dim + (size_t)kvh * a.hd;
-    const float *vh = a.v + (size_t)kvh * a.hd;
-    for (int k = threadIdx.x; k < a.hd; k += blockDim.x) {
-      const uint16_t kb = f32_to_f16_bits(ks[k]);
-      ks[k] = h2f(kb);  // the value attention reads back from the cache
+    const int k = threadIdx.x;
+    if (k < half) {
+      const uint16_t kb0 = f32_to_f16_bits(ks[k]), kb1 = f32_to_f16_bits(ks[k + half]);
+      ks[k] = h2f(kb0);  // the value attention reads back from the cache
+      ks[k + half] = h2f(kb1);
       if (writer) {
-        kc[k] = kb;
-        vc[k] = f32_to_f16_bits(vh[k]);
+        kc[k] = kb0;
+        kc[k + half] = kb1;
+        vc[k] = f32_to_f16_bits(v0);
+        vc[k + half] = f32_to_f16_bits(v1);
       }
     }
     __syncthreads();

@@ -293,6 +293,33 @@ RV_DEVFN long long rv_globaltimer() {
 RV_DEVFN void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 RV_DEVFN void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned).
+RV_DEVFN void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+RV_DEVFN void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+RV_DEVFN void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Copies `bytes` from global to shared memory with every thread of the CTA,
+// all copies in flight at once: 16-byte cp.async pieces when both ends and
+// the size are 16-byte aligned, else 4-byte words (both ends 4-byte aligned)
+// loaded four at a time.  The caller synchronizes the CTA before reading.
+RV_DEVFN void stage_to_smem(void *dst, const void *src, size_t bytes) {
+  if ((((uintptr_t)dst | (uintptr_t)src | bytes) & 15) == 0) {
+    for (size_t k = threadIdx.x; k < bytes / 16; k += blockDim.x)
+      cp_async16((uint8_t *)dst + 16 * k, (const uint8_t *)src + 16 * k);
+    cp_async_commit();
+    cp_async_wait<0>();
+  } else {
+    const uint32_t *s = (const uint32_t *)src;
+    uint32_t *d = (uint32_t *)dst;
+    const size_t words = bytes / 4;
+#pragma unroll 4
+    for (size_t k = threadIdx.x; k < words; k += blockDim.x) d[k] = s[k];
+  }
+}
+
 // True when every double within 2^-k * |r| of r (k in 30..52) rounds to the
 // same float as r, so the f32 result of a double computation does not
 // depend on how the double was summed within that bound.  Decided from the

@@ -72,12 +72,7 @@ RV_DEVFN void gemv_tile(const GemvArgs &g, size_t tile, uint8_t *sm) {
   for (size_t a0 = 0; a0 < g.n_acts; a0 += MT) {
     const int mt = (int)min((size_t)MT, g.n_acts - a0);
     __syncthreads();  // previous chunk fully consumed
-    {
-      const uint32_t *src = (const uint32_t *)(g.acts + a0 * act_row);
-      uint32_t *dst = (uint32_t *)asm_;
-      const size_t words = (size_t)mt * act_row / 4;
-      for (size_t k = threadIdx.x; k < words; k += blockDim.x) dst[k] = src[k];
-    }
+    stage_to_smem(asm_, g.acts + a0 * act_row, (size_t)mt * act_row);
     if (a0 == 0 && bulk) ok = mbar_wait_bounded(bar, 0);
     __syncthreads();
     if (!ok) return;
@@ -612,12 +607,7 @@ RV_DEVFN void gemv_q8_0_tile(const GemvArgs &g, size_t tile, uint8_t *sm) {
   for (size_t a0 = 0; a0 < g.n_acts; a0 += MT) {
     const int mt = (int)min((size_t)MT, g.n_acts - a0);
     __syncthreads();  // previous chunk fully consumed
-    {
-      const uint32_t *src = (const uint32_t *)(g.acts + a0 * act_row);
-      uint32_t *dst = (uint32_t *)asm_;
-      const size_t words = (size_t)mt * act_row / 4;
-      for (size_t k = threadIdx.x; k < words; k += blockDim.x) dst[k] = src[k];
-    }
+    stage_to_smem(asm_, g.acts + a0 * act_row, (size_t)mt * act_row);
     if (a0 == 0 && bulk) ok = mbar_wait_bounded(bar, 0);
     __syncthreads();
     if (!ok) return;
@@ -739,12 +729,13 @@ __global__ void __launch_bounds__(256) k_norm_quant(const float *__restrict__ x,
   extern __shared__ __align__(16) uint8_t sm[];
   double *red = (double *)sm;
   float *xs = (float *)(sm + 34 * sizeof(double));
-  for (int k = threadIdx.x; k < n; k += blockDim.x) xs[k] = x[k];
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float wk = w[256 * b + threadIdx.x];  // blockDim.x == 256: one weight per thread, loaded up front
+  stage_to_smem(xs, x, (size_t)n * sizeof(float));
   __syncthreads();
   const float inv = rms_inv_block(xs, (size_t)n, eps, red);
-  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float *ys = xs + n;  // this block's normed values
-  for (int k = threadIdx.x; k < 256; k += blockDim.x) ys[k] = __fmul_rn(__fmul_rn(xs[256 * b + k], inv), w[256 * b + k]);
+  ys[threadIdx.x] = __fmul_rn(__fmul_rn(xs[256 * b + threadIdx.x], inv), wk);
   __syncthreads();
   if (warp == 0) {
     float v[8];
