@@ -535,6 +535,15 @@ RV_API int rv_argmax(const float *x, size_t n, uint32_t *out, rv_stream stream);
 /* primitives::vec_add (kernels/primitives/vec.rs:10-22): a[i] += b[i]. */
 RV_API int rv_vec_add(float *a, const float *b, size_t n, rv_stream stream);
 
+/* Asks the L2 cache to fetch up to 8 device byte ranges (the 16-byte
+ * aligned part of each), with cp.async.bulk.prefetch.L2 from a small grid
+ * that exits once the requests are issued: a hint with no result, for
+ * pulling the next layer's weights into L2 while the current one runs (a
+ * decode step's parallel graph branch).  Not in the reference (its weights
+ * live in host memory).  RV_ERR_INVALID_ARGUMENT for n > 8 or a null range
+ * of non-zero size. */
+RV_API int rv_prefetch_l2(const void *const *ptrs, const size_t *bytes, uint32_t n, rv_stream stream);
+
 /* One layer's weights for rv_attn_block (device pointers, the GGUF-style
  * row-major packed matrices of model/shapes.rs:14-35). */
 typedef struct rv_attn_weights {

@@ -2030,6 +2030,33 @@ extern "C" int rv_vec_add(float *a, const float *b, size_t n, rv_stream stream) 
   return RV_OK;
 }
 
+extern "C" int rv_prefetch_l2(const void *const *ptrs, const size_t *bytes, uint32_t n, rv_stream stream) {
+  if (n == 0) return RV_OK;
+  if (!ptrs || !bytes) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "prefetch_l2: null pointer");
+  if (n > RV_PF_MAX) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "prefetch_l2: %u ranges (at most %d)", n, RV_PF_MAX);
+  PrefetchList L{};
+  size_t total = 0;
+  for (uint32_t i = 0; i < n; i++) {
+    if (bytes[i] && !ptrs[i]) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "prefetch_l2: range %u is null", i);
+    // The 16-byte-aligned part of the range; a range with none is skipped.
+    const uintptr_t b = ((uintptr_t)ptrs[i] + 15) & ~(uintptr_t)15;
+    const uintptr_t e = ((uintptr_t)ptrs[i] + bytes[i]) & ~(uintptr_t)15;
+    if (!ptrs[i] || e <= b) continue;
+    L.p[L.n] = (const uint8_t *)b;
+    L.bytes[L.n] = e - b;
+    L.chunk0[L.n] = total;
+    total += (L.bytes[L.n] + RV_PF_CHUNK - 1) / RV_PF_CHUNK;
+    L.n++;
+  }
+  if (L.n == 0) return RV_OK;
+  L.chunk0[L.n] = total;
+  // About four chunks per CTA, at most one CTA per SM of a B200.
+  const unsigned grid = (unsigned)std::min<size_t>(148, (total + 3) / 4);
+  k_prefetch_l2<<<grid, 32, 0, (cudaStream_t)stream>>>(L);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
 extern "C" int rv_synth_normal(uint64_t seed, uint64_t offset, float sigma, float *out, size_t n,
                                rv_stream stream) {
   if (n == 0) return RV_OK;
