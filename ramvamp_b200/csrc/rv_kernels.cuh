@@ -642,6 +642,137 @@ __global__ void __launch_bounds__(256) k_gemv_q8_0(GemvArgs g) {
   gemv_q8_0_tile<MT>(g, blockIdx.x, sm);
 }
 
+// ----------------------------------------------- one warp per row (decode)
+// Single-activation GEMV with a warp per row.  Lane 8g + l (group g, lane l
+// of the reference's eight) computes the integer lane sums of blocks g,
+// g + 4, g + 8, ... and their scale products (lane_sums, d * yd, dmin * yd);
+// then every group runs lane l's float chain over blocks 0..nb-1 in order,
+// taking each block's values by shuffle from the group that computed them,
+// and reduces as lane_reduce does: the float steps of gemv_tile (lane_step
+// per block) in the same order, so the same bits, with four times the warps
+// and a quarter of the integer work per thread.  The host picks this tile
+// when gemv_wide_nbg(format, nb) > 0 (nb = 4 * NBG) and there is one
+// activation row; blockDim = 32 * R.
+__host__ __device__ constexpr int gemv_wide_nbg(int fmt, int nb) {
+  return fmt == RV_Q8_0 ? (nb == 64 ? 16 : 0) : (nb == 8 ? 2 : nb == 16 ? 4 : 0);
+}
+
+// Shared memory of a warp-per-row tile: [16: mbarrier][R rows][16][act_row][16].
+__host__ __device__ inline size_t gemv_tile_smem(int R, size_t row_bytes, size_t act_row) {
+  return 16 + ((R * row_bytes + 15) & ~(size_t)15) + 16 + ((act_row + 15) & ~(size_t)15) + 16;
+}
+
+// Stages an R-row weight tile (bulk copy when aligned) and the activation
+// row; false when the copy's wait gave up.
+RV_DEVFN bool gemv_stage_row_tile(const GemvArgs &g, size_t tile, uint8_t *sm, size_t act_row, uint8_t *&wsm,
+                                  uint8_t *&asm_, int &rows_here) {
+  uint64_t *bar = (uint64_t *)sm;
+  wsm = sm + 16;
+  asm_ = wsm + ((g.R * g.row_bytes + 15) & ~(size_t)15) + 16;
+  const size_t tile0 = tile * g.R;
+  rows_here = (int)min((size_t)g.R, g.nrows - tile0);
+  const uint8_t *wsrc = g.w + (g.r0 + tile0) * g.row_bytes;
+  const size_t wbytes = (size_t)rows_here * g.row_bytes;
+  const bool bulk = rv_bulk_ok(wsrc, wsm, wbytes);
+  if (threadIdx.x == 0) mbar_init(bar, 1);
+  __syncthreads();
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(bar, (uint32_t)wbytes);
+      bulk_g2s(wsm, wsrc, (uint32_t)wbytes, bar);
+    }
+  } else {
+    rv_copy_bytes_block(wsm, wsrc, wbytes);
+  }
+  stage_to_smem(asm_, g.acts, act_row);
+  bool ok = true;
+  if (bulk) ok = mbar_wait_bounded(bar, 0);
+  return __syncthreads_and(ok);
+}
+
+template <int FMT, int NBG>
+RV_DEVFN void gemv_tile_wide(const GemvArgs &g, size_t tile, uint8_t *sm) {
+  constexpr int NB = 4 * NBG;
+  constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
+  uint8_t *wsm, *asm_;
+  int rows_here;
+  if (!gemv_stage_row_tile(g, tile, sm, (size_t)NB * 292, wsm, asm_, rows_here)) return;
+  const int r = threadIdx.x >> 5, lane = threadIdx.x & 31, l = lane & 7, grp = lane >> 3;
+  const uint8_t *wrow = wsm + (size_t)(r < rows_here ? r : 0) * g.row_bytes;  // idle rows compute row 0
+  int S[NBG], M[NBG];
+  float dy[NBG], dmy[NBG];
+#pragma unroll
+  for (int i = 0; i < NBG; i++) {
+    const int b = 4 * i + grp;
+    const uint8_t *act = asm_ + (size_t)b * 292;
+    WBlock w;
+    load_wblock<FMT>(wrow + (size_t)b * BB, l, w);
+    M[i] = 0;
+    lane_sums<FMT>(w, act, l, S[i], M[i]);
+    const float yd = *(const float *)act;
+    dy[i] = __fmul_rn(w.d, yd);
+    dmy[i] = __fmul_rn(w.dmin, yd);
+  }
+  float acc = 0.0f, accm = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    const int src = 8 * (b & 3) + l;
+    const int Sb = __shfl_sync(RV_FULL, S[b >> 2], src);
+    const float d = __shfl_sync(RV_FULL, dy[b >> 2], src);
+    if constexpr (FMT != RV_Q6_K) {
+      const int Mb = __shfl_sync(RV_FULL, M[b >> 2], src);
+      const float dm = __shfl_sync(RV_FULL, dmy[b >> 2], src);
+      if (l < 4) accm = __fmaf_rn(dm, __int2float_rn(Mb), accm);
+    }
+    acc = __fmaf_rn(d, __int2float_rn(Sb), acc);
+  }
+  const float res = lane_reduce<FMT>(acc, accm);
+  if (lane == 0 && r < rows_here) gemv_store(g, tile * g.R + r, res);
+}
+
+// The Q8_0 form (34-byte blocks of an f16 scale and 32 int8; 36-byte Q8_0
+// activation blocks of an f32 scale and 32 int8): lane l's step per block
+// is acc = fma(wd * ad, dp4a(w word l, a word l), acc), then the xor 4, 2,
+// 1 reduction, as gemv_q8_0_tile.
+template <int NBG>
+RV_DEVFN void gemv_q8_0_tile_wide(const GemvArgs &g, size_t tile, uint8_t *sm) {
+  constexpr int NB = 4 * NBG;
+  uint8_t *wsm, *asm_;
+  int rows_here;
+  if (!gemv_stage_row_tile(g, tile, sm, (size_t)NB * 36, wsm, asm_, rows_here)) return;
+  const int r = threadIdx.x >> 5, lane = threadIdx.x & 31, l = lane & 7, grp = lane >> 3;
+  const uint8_t *wrow = wsm + (size_t)(r < rows_here ? r : 0) * g.row_bytes;
+  int S[NBG];
+  float p[NBG];
+#pragma unroll
+  for (int i = 0; i < NBG; i++) {
+    const int b = 4 * i + grp;
+    const uint16_t *blk = (const uint16_t *)(wrow + (size_t)b * 34);  // 34-byte blocks: 2-byte aligned
+    const uint8_t *ab = asm_ + (size_t)b * 36;
+    const int w4 = (int)((uint32_t)blk[1 + 2 * l] | ((uint32_t)blk[2 + 2 * l] << 16));
+    S[i] = __dp4a(w4, *(const int *)(ab + 4 + 4 * l), 0);
+    p[i] = __fmul_rn(h2f(blk[0]), *(const float *)ab);
+  }
+  float acc = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    const int src = 8 * (b & 3) + l;
+    const int Sb = __shfl_sync(RV_FULL, S[b >> 2], src);
+    const float pb = __shfl_sync(RV_FULL, p[b >> 2], src);
+    acc = __fmaf_rn(pb, (float)Sb, acc);
+  }
+  float v = __fadd_rn(acc, __shfl_xor_sync(RV_FULL, acc, 4));
+  v = __fadd_rn(v, __shfl_xor_sync(RV_FULL, v, 2));
+  v = __fadd_rn(v, __shfl_xor_sync(RV_FULL, v, 1));
+  if (lane == 0 && r < rows_here) gemv_store(g, tile * g.R + r, v);
+}
+
+template <int FMT, int NBG>
+__global__ void __launch_bounds__(256) k_gemv_wide(GemvArgs g) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  gemv_tile_wide<FMT, NBG>(g, blockIdx.x, sm);
+}
+
 // Several single-activation GEMVs in one launch (the attention projections
 // q, k, v): CTAs [cta0[j], cta0[j+1]) run job j's tiles with job j's format
 // (Q4_K / Q5_K / Q6_K against Q8_K activations, Q8_0 against Q8_0).  Every
@@ -658,11 +789,21 @@ __global__ void __launch_bounds__(256) k_gemv_multi(GemvMulti m) {
   int j = 0;
   while (j + 1 < m.n && blockIdx.x >= m.cta0[j + 1]) j++;
   const size_t tile = blockIdx.x - m.cta0[j];
-  switch (m.fmt[j]) {
-    case RV_Q4_K: gemv_tile<RV_Q4_K, 1>(m.job[j], tile, sm); break;
-    case RV_Q5_K: gemv_tile<RV_Q5_K, 1>(m.job[j], tile, sm); break;
-    case RV_Q6_K: gemv_tile<RV_Q6_K, 1>(m.job[j], tile, sm); break;
-    default: gemv_q8_0_tile<1>(m.job[j], tile, sm); break;
+  // The host sized each job's R for the tile chosen here: blockDim / 32 rows
+  // for the warp-per-row tiles, blockDim / 8 for the others.
+  const GemvArgs &g = m.job[j];
+  switch (m.fmt[j] * 100 + gemv_wide_nbg(m.fmt[j], g.nb)) {
+    case RV_Q4_K * 100 + 2: gemv_tile_wide<RV_Q4_K, 2>(g, tile, sm); break;
+    case RV_Q4_K * 100 + 4: gemv_tile_wide<RV_Q4_K, 4>(g, tile, sm); break;
+    case RV_Q5_K * 100 + 2: gemv_tile_wide<RV_Q5_K, 2>(g, tile, sm); break;
+    case RV_Q5_K * 100 + 4: gemv_tile_wide<RV_Q5_K, 4>(g, tile, sm); break;
+    case RV_Q6_K * 100 + 2: gemv_tile_wide<RV_Q6_K, 2>(g, tile, sm); break;
+    case RV_Q6_K * 100 + 4: gemv_tile_wide<RV_Q6_K, 4>(g, tile, sm); break;
+    case RV_Q8_0 * 100 + 16: gemv_q8_0_tile_wide<16>(g, tile, sm); break;
+    case RV_Q4_K * 100: gemv_tile<RV_Q4_K, 1>(g, tile, sm); break;
+    case RV_Q5_K * 100: gemv_tile<RV_Q5_K, 1>(g, tile, sm); break;
+    case RV_Q6_K * 100: gemv_tile<RV_Q6_K, 1>(g, tile, sm); break;
+    default: gemv_q8_0_tile<1>(g, tile, sm); break;
   }
 }
 

@@ -228,6 +228,19 @@ static int validate_gemv(const char *what, int format, size_t weight_len, size_t
 
 template <int FMT>
 static void launch_gemv(const GemvArgs &g, cudaStream_t s) {
+  // One activation row and 8 or 16 blocks per row: the warp-per-row tile,
+  // R rows per CTA (fewer until the grid covers two waves of SMs).
+  const int nbg = g.n_acts == 1 ? gemv_wide_nbg(FMT, g.nb) : 0;
+  if (nbg) {
+    GemvArgs w = g;
+    w.R = 8;
+    while (w.R > 1 && (w.nrows + w.R - 1) / w.R < 2 * 148) w.R /= 2;
+    const size_t smem = gemv_tile_smem(w.R, w.row_bytes, (size_t)w.nb * 292);
+    const unsigned grid = (unsigned)((w.nrows + w.R - 1) / w.R);
+    if (nbg == 2) k_gemv_wide<FMT, 2><<<grid, 32 * w.R, smem, s>>>(w);
+    else k_gemv_wide<FMT, 4><<<grid, 32 * w.R, smem, s>>>(w);
+    return;
+  }
   const size_t act_row = (size_t)g.nb * 292;
   const int mt = g.n_acts > 1 ? 8 : 1;
   const size_t smem = 16 + ((g.R * g.row_bytes + 15) & ~(size_t)15) + 16 + mt * act_row + 16;
@@ -1848,25 +1861,31 @@ extern "C" int rv_attn_block(rv_attn *a, uint32_t layer, const rv_attn_weights *
   // 1. attn_norm -> Q8_K and Q8_0 of the normed row
   k_norm_quant<<<(unsigned)(H / 256), 256, 34 * sizeof(double) + (H + 256) * sizeof(float), s>>>(
       residual, w->attn_norm, (int)H, c.eps, a->acts_k, a->acts_0);
-  // 2. q, k, v projections in one launch (8 rows per CTA)
-  const int R = 8;
+  // 2. q, k, v projections in one launch of 256-thread CTAs: 8 rows per CTA
+  // for the warp-per-row tiles (gemv_wide_nbg), 32 for the others.
+  const int TPB = 256;
+  auto rows_per_cta = [&](int fmt, int nb) { return gemv_wide_nbg(fmt, nb) ? TPB / 32 : TPB / 8; };
   GemvMulti m{};
   const size_t rb_q = H / 256 * rv_fmt_block_bytes(w->attn_q_format);
   const size_t rb_v = H / 256 * rv_fmt_block_bytes(w->attn_v_format);
   const size_t rb_k = H / 32 * 34;
-  m.job[0] = gemv_job(w->attn_q, rb_q, (int)(H / 256), qd, a->acts_k, a->q, R);
+  const int nb_k = (int)(H / 256), nb_0 = (int)(H / 32);
+  m.job[0] = gemv_job(w->attn_q, rb_q, nb_k, qd, a->acts_k, a->q, rows_per_cta(w->attn_q_format, nb_k));
   m.fmt[0] = w->attn_q_format;
-  m.job[1] = gemv_job(w->attn_k, rb_k, (int)(H / 32), kvd, a->acts_0, a->k, R);
+  m.job[1] = gemv_job(w->attn_k, rb_k, nb_0, kvd, a->acts_0, a->k, rows_per_cta(RV_Q8_0, nb_0));
   m.fmt[1] = RV_Q8_0;
-  m.job[2] = gemv_job(w->attn_v, rb_v, (int)(H / 256), kvd, a->acts_k, a->v, R);
+  m.job[2] = gemv_job(w->attn_v, rb_v, nb_k, kvd, a->acts_k, a->v, rows_per_cta(w->attn_v_format, nb_k));
   m.fmt[2] = w->attn_v_format;
   m.n = 3;
   m.cta0[0] = 0;
-  for (int j = 0; j < 3; j++) m.cta0[j + 1] = m.cta0[j] + (unsigned)((m.job[j].nrows + R - 1) / R);
-  const size_t rb_max = std::max(rb_q, std::max(rb_v, rb_k));
-  const size_t act_max = std::max(H / 256 * 292, H / 32 * 36);
-  const size_t smem = 16 + ((R * rb_max + 15) & ~(size_t)15) + 16 + act_max + 16;
-  k_gemv_multi<<<m.cta0[3], R * 8, smem, s>>>(m);
+  size_t smem = 0;
+  for (int j = 0; j < 3; j++) {
+    const GemvArgs &g = m.job[j];
+    m.cta0[j + 1] = m.cta0[j] + (unsigned)((g.nrows + g.R - 1) / g.R);
+    const size_t act_row = m.fmt[j] == RV_Q8_0 ? (size_t)g.nb * 36 : (size_t)g.nb * 292;
+    smem = std::max(smem, gemv_tile_smem(g.R, g.row_bytes, act_row));
+  }
+  k_gemv_multi<<<m.cta0[3], TPB, smem, s>>>(m);
   // 3. QK-norm, RoPE, append, attention
   AttnArgs args{};
   args.q = a->q;
