@@ -767,6 +767,12 @@ RV_DEVFN void gemv_q8_0_tile_wide(const GemvArgs &g, size_t tile, uint8_t *sm) {
   if (lane == 0 && r < rows_here) gemv_store(g, tile * g.R + r, v);
 }
 
+template <int NBG>
+__global__ void __launch_bounds__(256) k_gemv_q8_0_wide(GemvArgs g) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  gemv_q8_0_tile_wide<NBG>(g, blockIdx.x, sm);
+}
+
 template <int FMT, int NBG>
 __global__ void __launch_bounds__(256) k_gemv_wide(GemvArgs g) {
   extern __shared__ __align__(16) uint8_t sm[];

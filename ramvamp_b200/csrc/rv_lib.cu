@@ -391,6 +391,14 @@ static int gemv_q8_0_launch(const uint8_t *weight, size_t row_bytes, size_t in_d
   const size_t smem = 16 + ((R * row_bytes + 15) & ~(size_t)15) + 16 + mt * act_row + 16;
   if (smem > 200 * 1024)
     RV_FAIL(RV_ERR_UNIMPLEMENTED, "gemv_q8_0: rows of %zu bytes exceed the staged-tile limit", row_bytes);
+  if (mt == 1 && gemv_wide_nbg(RV_Q8_0, g.nb)) {  // one activation row, 64 blocks: the warp-per-row tile
+    g.R = 8;
+    while (g.R > 1 && (g.nrows + g.R - 1) / g.R < 2 * 148) g.R /= 2;
+    k_gemv_q8_0_wide<16><<<(unsigned)((g.nrows + g.R - 1) / g.R), 32 * g.R,
+                           gemv_tile_smem(g.R, row_bytes, act_row), s>>>(g);
+    RV_LAUNCH_CHECK();
+    return RV_OK;
+  }
   const unsigned grid = (unsigned)((g.nrows + R - 1) / R);
   if (mt == 1) k_gemv_q8_0<1><<<grid, R * 8, smem, s>>>(g);
   else k_gemv_q8_0<8><<<grid, R * 8, smem, s>>>(g);
