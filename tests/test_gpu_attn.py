@@ -150,11 +150,12 @@ def test_rmsnorm_quantize_bytes(rv, orc):
         assert host(q80).tobytes() == orc.quantize_row_q8_0(normed, orc.SCALAR).tobytes()
 
 
-@pytest.mark.parametrize("device_position", [False, True])
-def test_attn_block_matches_reference(rv, orc, device_position):
+@pytest.mark.parametrize("device_position,P", [(False, 40), (True, 40), (True, 150)])
+def test_attn_block_matches_reference(rv, orc, device_position, P):
     """rv_attn_block (forward.rs:2572-2652 for one layer, residual in place)
-    against the reference's step sequence on the oracle, over 40 positions."""
-    H, n_q, n_kv, hd, P = 2048, 32, 4, 128, 40
+    against the reference's step sequence on the oracle, over P positions
+    (150: the values staged in three 64-position chunks)."""
+    H, n_q, n_kv, hd = 2048, 32, 4, 128
     rng = np.random.default_rng(31)
     eng = rv.AttnEngine(1, n_q, n_kv, hd, max_positions=P, rope_theta=1e6, eps=1e-6, hidden=H)
     qd, kvd = n_q * hd, n_kv * hd
