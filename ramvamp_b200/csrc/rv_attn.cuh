@@ -370,6 +370,204 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
   }
 }
 
+// rmsnorm_in_place then rotate_head (as k_attn_prep) of one 128-value head
+// by one warp: lane l holds x[l + 32i], i = 0..3, so the rotation pairs
+// (k, k + 64) are elements (i, i + 2) of one lane.  The sum of squares is a
+// lane sum of four and a shuffle tree; rms_inv_tail makes the inverse RMS
+// the serial sum's (the tree sum of 128 squares differs from it by far less
+// than the 2^-38 its check allows).  xs (smem[128]) holds the input for
+// that check's serial redo, then the result.
+RV_DEVFN void norm_rope_warp128(const float *x, const float *w, const float2 *rot, float eps, float *xs, int lane) {
+  float v[4], wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    v[i] = x[lane + 32 * i];
+    wv[i] = w[lane + 32 * i];
+  }
+  const float2 c0 = rot[lane], c1 = rot[lane + 32];
+  double part = 0.0;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    xs[lane + 32 * i] = v[i];
+    const double d = (double)v[i];
+    part = __dadd_rn(part, __dmul_rn(d, d));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+  __syncwarp();
+  float inv = 0.0f;
+  if (lane == 0) inv = rms_inv_tail(part, xs, 128, eps);
+  inv = __shfl_sync(RV_FULL, inv, 0);
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) n[i] = __fmul_rn(__fmul_rn(v[i], inv), wv[i]);
+  xs[lane] = __fsub_rn(__fmul_rn(n[0], c0.x), __fmul_rn(n[2], c0.y));
+  xs[lane + 64] = __fadd_rn(__fmul_rn(n[0], c0.y), __fmul_rn(n[2], c0.x));
+  xs[lane + 32] = __fsub_rn(__fmul_rn(n[1], c1.x), __fmul_rn(n[3], c1.y));
+  xs[lane + 96] = __fadd_rn(__fmul_rn(n[1], c1.y), __fmul_rn(n[3], c1.x));
+}
+
+// k_attn_scores_prep and k_attn_softmax_out<2> (with the Q8_K epilogue) as
+// one launch: CTA p (256 threads) owns query heads 2p and 2p + 1, which
+// share one kv head (hd 128).  Warps 0 and 1 form the two normed, rotated
+// query heads, warp 2 this step's key (rounded through f16 as the cache
+// holds it) and warp 3 this step's V row in f16; the first pair of each kv
+// head also appends both rows to the caches.  No CTA reads the cache rows
+// of the current position: it uses its own copies of them.  Thread st of
+// head j (tid = 128j + st) then forms the scores of positions st, st + 128,
+// ... (the scores kernel's chains), and the softmax, the value chains and
+// the Q8_K of the pair's outputs follow as in k_attn_softmax_out<2>, with
+// scores and probabilities in shared memory.
+#define RV_ATTN_FUSED_MAX 256
+__host__ __device__ inline size_t attn_fused_smem(int positions) {
+  // red[34] f64 | q 2x128 f32 | k 128 f32 | v row 128 f16 | V staging 2 x 64 x 256 B | scores, probs 2 x P f32 each
+  return 34 * 8 + 3 * 128 * 4 + 128 * 2 + 2 * (size_t)RV_ATTN_VCHUNK * 256 + 4 * (size_t)positions * sizeof(float);
+}
+__global__ void __launch_bounds__(256) k_attn_fused(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ float s_max[2], s_inv[2];
+  double *red = (double *)sm;
+  float *qs = (float *)(sm + 34 * 8);
+  float *ks = qs + 256;
+  uint16_t *vrow = (uint16_t *)(ks + 128);
+  uint8_t *vstage = (uint8_t *)(vrow + 128);
+  float *sbase = (float *)(vstage + 2 * RV_ATTN_VCHUNK * 256);
+  const int position = attn_position(a);
+  if (position < 0) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int p = blockIdx.x, group = a.n_heads / a.n_kv, kvh = (2 * p) / group;
+  const size_t kv_dim = (size_t)a.n_kv * 128;
+  const bool writer = (2 * p) % group == 0;
+  const float2 *rot = a.rot + (size_t)position * 64;
+  if (warp < 2) {
+    norm_rope_warp128(a.q + (size_t)(2 * p + warp) * 128, a.q_norm, rot, a.eps, qs + warp * 128, lane);
+  } else if (warp == 2) {
+    norm_rope_warp128(a.k + (size_t)kvh * 128, a.k_norm, rot, a.eps, ks, lane);
+    uint16_t *kc = a.k_cache + (size_t)position * kv_dim + (size_t)kvh * 128;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int k = lane + 32 * i;
+      const uint16_t kb = f32_to_f16_bits(ks[k]);
+      ks[k] = h2f(kb);  // the value attention reads back from the cache
+      if (writer) kc[k] = kb;
+    }
+  } else if (warp == 3) {
+    uint16_t *vc = a.v_cache + (size_t)position * kv_dim + (size_t)kvh * 128;
+    const float *vh = a.v + (size_t)kvh * 128;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int k = lane + 32 * i;
+      const uint16_t vb = f32_to_f16_bits(vh[k]);
+      vrow[k] = vb;
+      if (writer) vc[k] = vb;
+    }
+  }
+  __syncthreads();
+  // Scores: acc = sum over i ascending of q[i] * k[i], separate multiply and add.
+  const int j = tid >> 7, st = tid & 127, h = 2 * p + j, positions = position + 1;
+  const float *qj = qs + j * 128;
+  float *sc = sbase + (size_t)j * positions;
+  float *pr = sbase + (size_t)(2 + j) * positions;
+  for (int t = st; t < positions; t += 128) {
+    float acc = 0.0f;
+    if (t == position) {
+      for (int i = 0; i < 128; i++) acc = __fadd_rn(acc, __fmul_rn(qj[i], ks[i]));
+    } else {
+      acc = attn_dot_row(qj, a.k_cache + (size_t)t * kv_dim + (size_t)kvh * 128, 128);
+    }
+    sc[t] = __fmul_rn(a.scale, acc);
+  }
+  // Softmax (softmax.rs:18-40), as k_attn_softmax_out: segment j = warps 4j..4j+3.
+  float mx = -INFINITY;
+  for (int t = st; t < positions; t += 128) mx = fmaxf(mx, sc[t]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(RV_FULL, mx, o));
+  if (lane == 0) red[warp] = (double)mx;
+  __syncthreads();
+  if (st == 0) {
+    float m = -INFINITY;
+    for (int w = 4 * j; w < 4 * j + 4; w++) m = fmaxf(m, (float)red[w]);
+    s_max[j] = m;
+  }
+  __syncthreads();
+  const double dmx = (double)s_max[j];
+  double part = 0.0;
+  for (int t = st; t < positions; t += 128) {
+    const double e = exp(__dsub_rn((double)sc[t], dmx));
+    pr[t] = __double2float_rn(e);
+    part = __dadd_rn(part, e);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = part;
+  __syncthreads();
+  if (st == 0) {
+    double sum = 0.0;
+    for (int w = 4 * j; w < 4 * j + 4; w++) sum = __dadd_rn(sum, red[w]);
+    const double r = __drcp_rn(sum);
+    const unsigned long long bound = 2ull * (unsigned long long)positions + 2ull;
+    const int k = 52 - (64 - __clzll((long long)bound));
+    float inv = __double2float_rn(r);
+    if (!(k >= 30 && isfinite(r) && f32_rounding_stable(r, k))) {
+      double ser = 0.0;
+      for (int t = 0; t < positions; t++) ser = __dadd_rn(ser, exp(__dsub_rn((double)sc[t], dmx)));
+      inv = __double2float_rn(__drcp_rn(ser));
+    }
+    s_inv[j] = inv;
+  }
+  __syncthreads();
+  const float inv = s_inv[j];
+  for (int t = st; t < positions; t += 128) pr[t] = __fmul_rn(pr[t], inv);
+  // Values: one serial chain per output element over t ascending, the V
+  // rows staged 64 positions at a time (double-buffered cp.async); the
+  // current position's row comes from this CTA's own copy.
+  const uint16_t *vcg = a.v_cache + (size_t)kvh * 128;
+  auto vbuf = [&](int b) { return vstage + b * RV_ATTN_VCHUNK * 256; };
+  const int nchunks = (positions + RV_ATTN_VCHUNK - 1) / RV_ATTN_VCHUNK;
+  auto stage = [&](int ch) {
+    const int t0 = ch * RV_ATTN_VCHUNK, n = min(RV_ATTN_VCHUNK, positions - t0);
+    uint8_t *dst = vbuf(ch & 1);
+    for (int k = tid; k < n * 16; k += blockDim.x) {
+      const int r = k >> 4, c = k & 15;
+      if (t0 + r == position)
+        ((uint4 *)(dst + r * 256))[c] = ((const uint4 *)vrow)[c];
+      else
+        cp_async16(dst + r * 256 + 16 * c, (const uint8_t *)(vcg + (size_t)(t0 + r) * kv_dim) + 16 * c);
+    }
+    cp_async_commit();
+  };
+  float acc = 0.0f;
+  stage(0);
+  for (int ch = 0; ch < nchunks; ch++) {
+    if (ch + 1 < nchunks) {
+      stage(ch + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // this chunk's rows (and, the first time, every probability) are in place
+    const uint16_t *vs = (const uint16_t *)vbuf(ch & 1);
+    const float *pc = pr + ch * RV_ATTN_VCHUNK;
+    const int n = min(RV_ATTN_VCHUNK, positions - ch * RV_ATTN_VCHUNK);
+#pragma unroll 8
+    for (int r = 0; r < n; r++) acc = __fadd_rn(acc, __fmul_rn(pc[r], h2f(vs[r * 128 + st])));
+    __syncthreads();  // this buffer is restaged for chunk ch + 2
+  }
+  a.out[(size_t)h * 128 + st] = acc;
+  if (a.q8k_out) {
+    float *ys = (float *)vstage;  // the staging buffers are free now
+    ys[j * 128 + st] = acc;
+    __syncthreads();
+    if (warp == 0) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = ys[8 * lane + e];
+      q8k_quantize_warp(v, lane, a.q8k_out + (size_t)p * 292);
+    }
+  }
+}
+
 // rope_neox_heads (rope.rs:80-111) for one position, the factors passed by
 // value (formed on the host with the reference's f64 libm calls).
 #define RV_ROPE_MAX_HALF 256

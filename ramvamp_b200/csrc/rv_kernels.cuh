@@ -275,6 +275,29 @@ RV_DEVFN float rms_inv_from_sum(double sum, size_t n, float eps) {
   return __double2float_rn(__drcp_rn(__dsqrt_rn(__dadd_rn(mean, (double)eps))));
 }
 
+// The inverse RMS from a sum of squares `s` taken in some order other than
+// the reference's: the correctly rounded f64 steps, and, when the result
+// lies within 2^-38 of an f32 rounding midpoint (or is not finite), the
+// serial sum over xs[0..n) redone here.
+RV_DEVFN float rms_inv_tail(double s, const float *xs, size_t n, float eps) {
+  const double mean = __ddiv_rn(s, (double)n);
+  const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(mean, (double)eps)));
+  const float f = __double2float_rn(r);
+  const double df = (double)f;
+  const double up = (double)nextafterf(f, INFINITY), dn = (double)nextafterf(f, -INFINITY);
+  const double mh = 0.5 * (df + up), ml = 0.5 * (df + dn);
+  const double tol = fabs(r) * 0x1p-38;
+  if (fabs(mh - r) <= tol || fabs(r - ml) <= tol || !isfinite(r)) {
+    double ser = 0.0;
+    for (size_t k = 0; k < n; k++) {
+      const double v = (double)xs[k];
+      ser = __dadd_rn(ser, __dmul_rn(v, v));
+    }
+    return rms_inv_from_sum(ser, n, eps);
+  }
+  return f;
+}
+
 // The reference sums v*v serially in f64 (norm.rs:38-60).  The tree sum
 // used here differs from it by at most 2^-41 relative; when the resulting
 // inverse RMS lies that close to a float rounding midpoint, thread 0 redoes
@@ -293,23 +316,7 @@ RV_DEVFN float rms_inv_block(const float *xs /*smem*/, size_t n, float eps, doub
   if (threadIdx.x == 0) {
     double s = 0.0;
     for (int w = 0; w < (int)(blockDim.x >> 5); w++) s = __dadd_rn(s, red[w]);
-    const double mean = __ddiv_rn(s, (double)n);
-    const double r = __drcp_rn(__dsqrt_rn(__dadd_rn(mean, (double)eps)));
-    const float f = __double2float_rn(r);
-    const double df = (double)f;
-    const double up = (double)nextafterf(f, INFINITY), dn = (double)nextafterf(f, -INFINITY);
-    const double mh = 0.5 * (df + up), ml = 0.5 * (df + dn);
-    const double tol = fabs(r) * 0x1p-38;
-    float inv = f;
-    if (fabs(mh - r) <= tol || fabs(r - ml) <= tol || !isfinite(r)) {
-      double ser = 0.0;
-      for (size_t k = 0; k < n; k++) {
-        const double v = (double)xs[k];
-        ser = __dadd_rn(ser, __dmul_rn(v, v));
-      }
-      inv = rms_inv_from_sum(ser, n, eps);
-    }
-    red[32] = (double)inv;
+    red[32] = (double)rms_inv_tail(s, xs, n, eps);
   }
   __syncthreads();
   return (float)red[32];

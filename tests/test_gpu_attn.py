@@ -150,14 +150,18 @@ def test_rmsnorm_quantize_bytes(rv, orc):
         assert host(q80).tobytes() == orc.quantize_row_q8_0(normed, orc.SCALAR).tobytes()
 
 
-@pytest.mark.parametrize("device_position,P", [(False, 40), (True, 40), (True, 150)])
-def test_attn_block_matches_reference(rv, orc, device_position, P):
+@pytest.mark.parametrize("device_position,P,cap", [(False, 40, 40), (True, 40, 40), (True, 150, 150),
+                                                   (True, 150, 300), (False, 300, 300)])
+def test_attn_block_matches_reference(rv, orc, device_position, P, cap):
     """rv_attn_block (forward.rs:2572-2652 for one layer, residual in place)
     against the reference's step sequence on the oracle, over P positions
-    (150: the values staged in three 64-position chunks)."""
+    of a cache of `cap` (the values staged in 64-position chunks).  Up to
+    256 positions the block runs attention as one fused launch (host mode:
+    by position; device mode: by capacity), beyond that as two: cap 300
+    covers the two-launch form in both modes."""
     H, n_q, n_kv, hd = 2048, 32, 4, 128
     rng = np.random.default_rng(31)
-    eng = rv.AttnEngine(1, n_q, n_kv, hd, max_positions=P, rope_theta=1e6, eps=1e-6, hidden=H)
+    eng = rv.AttnEngine(1, n_q, n_kv, hd, max_positions=cap, rope_theta=1e6, eps=1e-6, hidden=H)
     qd, kvd = n_q * hd, n_kv * hd
     x_norm = rng.uniform(0.8, 1.2, H).astype(np.float32)
     wq = orc.quantize_weights(orc.Q4_K, (rng.standard_normal(qd * H) * 0.02).astype(np.float32))
@@ -168,7 +172,7 @@ def test_attn_block_matches_reference(rv, orc, device_position, P):
     d = [dev(a) for a in (x_norm, wq, wk, wv, wo, qn, kn)]
     aw = rv.attn_weights(*d, attn_q_format=rv.QuantFormat.Q4_K, attn_v_format=rv.QuantFormat.Q6_K,
                          attn_output_format=rv.QuantFormat.Q5_K)
-    kc, vc = np.zeros(P * kvd, np.uint16), np.zeros(P * kvd, np.uint16)
+    kc, vc = np.zeros(cap * kvd, np.uint16), np.zeros(cap * kvd, np.uint16)
     pos_d = torch.zeros(1, dtype=torch.int32, device="cuda")
     for pos in range(P):
         x = rng.standard_normal(H).astype(np.float32)
