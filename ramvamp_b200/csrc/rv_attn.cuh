@@ -155,6 +155,43 @@ __global__ void __launch_bounds__(128) k_attn_scores(AttnArgs a) {
 // head (h % group == 0) writes that position's K and V cache rows.  No CTA
 // of this launch reads the current cache row; the next kernel reads V after
 // the launch boundary.
+// rmsnorm_in_place then rotate_head (as k_attn_prep) of one 128-value head
+// by one warp: lane l holds x[l + 32i], i = 0..3, so the rotation pairs
+// (k, k + 64) are elements (i, i + 2) of one lane.  The sum of squares is a
+// lane sum of four and a shuffle tree; rms_inv_tail makes the inverse RMS
+// the serial sum's (the tree sum of 128 squares differs from it by far less
+// than the 2^-38 its check allows).  xs (smem[128]) holds the input for
+// that check's serial redo, then the result.
+RV_DEVFN void norm_rope_warp128(const float *x, const float *w, const float2 *rot, float eps, float *xs, int lane) {
+  float v[4], wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    v[i] = x[lane + 32 * i];
+    wv[i] = w[lane + 32 * i];
+  }
+  const float2 c0 = rot[lane], c1 = rot[lane + 32];
+  double part = 0.0;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    xs[lane + 32 * i] = v[i];
+    const double d = (double)v[i];
+    part = __dadd_rn(part, __dmul_rn(d, d));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
+  __syncwarp();
+  float inv = 0.0f;
+  if (lane == 0) inv = rms_inv_tail(part, xs, 128, eps);
+  inv = __shfl_sync(RV_FULL, inv, 0);
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) n[i] = __fmul_rn(__fmul_rn(v[i], inv), wv[i]);
+  xs[lane] = __fsub_rn(__fmul_rn(n[0], c0.x), __fmul_rn(n[2], c0.y));
+  xs[lane + 64] = __fadd_rn(__fmul_rn(n[0], c0.y), __fmul_rn(n[2], c0.x));
+  xs[lane + 32] = __fsub_rn(__fmul_rn(n[1], c1.x), __fmul_rn(n[3], c1.y));
+  xs[lane + 96] = __fadd_rn(__fmul_rn(n[1], c1.y), __fmul_rn(n[3], c1.x));
+}
+
 // One head's inputs for attn_norm_rope, held in registers: thread k < hd/2
 // owns the rotation pair (k, k + hd/2) of x and of the norm weights and the
 // pair's cos/sin.  Loaded at kernel entry so that every global load of the
@@ -194,6 +231,23 @@ RV_DEVFN void attn_norm_rope(const HeadPair &r, int hd, float eps, float *xs, do
   __syncthreads();
 }
 
+// The scores of this CTA's positions (blockIdx.y's tiles) for query head
+// blockIdx.x: one serial f32 chain per position, separate multiply and
+// add; the current position uses this CTA's own key (ks).
+RV_DEVFN void attn_scores_tile(const AttnArgs &a, const float *qs, const float *ks, int position, int kvh,
+                               size_t kv_dim) {
+  const int h = blockIdx.x, positions = position + 1;
+  for (int t = blockIdx.y * blockDim.x + threadIdx.x; t < positions; t += gridDim.y * blockDim.x) {
+    float acc = 0.0f;
+    if (t == position) {
+      for (int i = 0; i < a.hd; i++) acc = __fadd_rn(acc, __fmul_rn(qs[i], ks[i]));
+    } else {
+      acc = attn_dot_row(qs, a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd, a.hd);
+    }
+    a.scores[(size_t)h * positions + t] = __fmul_rn(a.scale, acc);
+  }
+}
+
 __global__ void __launch_bounds__(128) k_attn_scores_prep(AttnArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
   double *red = (double *)sm;
@@ -206,6 +260,32 @@ __global__ void __launch_bounds__(128) k_attn_scores_prep(AttnArgs a) {
   const size_t kv_dim = (size_t)a.n_kv * a.hd;
   const bool holds_pos = (int)blockIdx.y == (position / (int)blockDim.x) % (int)gridDim.y;
   const bool writer = holds_pos && h % group == 0;
+  if (a.hd == 128) {
+    // Warp 0 forms the query head, warp 1 the key, warp 2 appends the V
+    // row, all at once (norm_rope_warp128: the same values as below).
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == 0) {
+      norm_rope_warp128(a.q + (size_t)h * 128, a.q_norm, rot, a.eps, qs, lane);
+    } else if (warp == 1 && holds_pos) {
+      norm_rope_warp128(a.k + (size_t)kvh * 128, a.k_norm, rot, a.eps, ks, lane);
+      uint16_t *kc = a.k_cache + (size_t)position * kv_dim + (size_t)kvh * 128;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int k = lane + 32 * i;
+        const uint16_t kb = f32_to_f16_bits(ks[k]);
+        ks[k] = h2f(kb);  // the value attention reads back from the cache
+        if (writer) kc[k] = kb;
+      }
+    } else if (warp == 2 && writer) {
+      uint16_t *vc = a.v_cache + (size_t)position * kv_dim + (size_t)kvh * 128;
+      const float *vh = a.v + (size_t)kvh * 128;
+#pragma unroll
+      for (int i = 0; i < 4; i++) vc[lane + 32 * i] = f32_to_f16_bits(vh[lane + 32 * i]);
+    }
+    __syncthreads();
+    attn_scores_tile(a, qs, ks, position, kvh, kv_dim);
+    return;
+  }
   const HeadPair qp = head_pair_load(a.q + (size_t)h * a.hd, a.q_norm, rot, a.hd);
   HeadPair kp{0.0f, 0.0f, 0.0f, 0.0f, make_float2(0.0f, 0.0f)};
   float v0 = 0.0f, v1 = 0.0f;
@@ -234,16 +314,7 @@ __global__ void __launch_bounds__(128) k_attn_scores_prep(AttnArgs a) {
     }
     __syncthreads();
   }
-  const int positions = position + 1;
-  for (int t = blockIdx.y * blockDim.x + threadIdx.x; t < positions; t += gridDim.y * blockDim.x) {
-    float acc = 0.0f;
-    if (t == position) {
-      for (int i = 0; i < a.hd; i++) acc = __fadd_rn(acc, __fmul_rn(qs[i], ks[i]));
-    } else {
-      acc = attn_dot_row(qs, a.k_cache + (size_t)t * kv_dim + (size_t)kvh * a.hd, a.hd);
-    }
-    a.scores[(size_t)h * positions + t] = __fmul_rn(a.scale, acc);
-  }
+  attn_scores_tile(a, qs, ks, position, kvh, kv_dim);
 }
 
 // HPC query heads per CTA (threads split into HPC segments, segment j
@@ -368,43 +439,6 @@ __global__ void __launch_bounds__(256) k_attn_softmax_out(AttnArgs a) {
       q8k_quantize_warp(v, lane, a.q8k_out + (size_t)blockIdx.x * 292);
     }
   }
-}
-
-// rmsnorm_in_place then rotate_head (as k_attn_prep) of one 128-value head
-// by one warp: lane l holds x[l + 32i], i = 0..3, so the rotation pairs
-// (k, k + 64) are elements (i, i + 2) of one lane.  The sum of squares is a
-// lane sum of four and a shuffle tree; rms_inv_tail makes the inverse RMS
-// the serial sum's (the tree sum of 128 squares differs from it by far less
-// than the 2^-38 its check allows).  xs (smem[128]) holds the input for
-// that check's serial redo, then the result.
-RV_DEVFN void norm_rope_warp128(const float *x, const float *w, const float2 *rot, float eps, float *xs, int lane) {
-  float v[4], wv[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    v[i] = x[lane + 32 * i];
-    wv[i] = w[lane + 32 * i];
-  }
-  const float2 c0 = rot[lane], c1 = rot[lane + 32];
-  double part = 0.0;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    xs[lane + 32 * i] = v[i];
-    const double d = (double)v[i];
-    part = __dadd_rn(part, __dmul_rn(d, d));
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(RV_FULL, part, o));
-  __syncwarp();
-  float inv = 0.0f;
-  if (lane == 0) inv = rms_inv_tail(part, xs, 128, eps);
-  inv = __shfl_sync(RV_FULL, inv, 0);
-  float n[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++) n[i] = __fmul_rn(__fmul_rn(v[i], inv), wv[i]);
-  xs[lane] = __fsub_rn(__fmul_rn(n[0], c0.x), __fmul_rn(n[2], c0.y));
-  xs[lane + 64] = __fadd_rn(__fmul_rn(n[0], c0.y), __fmul_rn(n[2], c0.x));
-  xs[lane + 32] = __fsub_rn(__fmul_rn(n[1], c1.x), __fmul_rn(n[3], c1.y));
-  xs[lane + 96] = __fadd_rn(__fmul_rn(n[1], c1.y), __fmul_rn(n[3], c1.x));
 }
 
 // k_attn_scores_prep and k_attn_softmax_out<2> (with the Q8_K epilogue) as
