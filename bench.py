@@ -369,12 +369,11 @@ def run_reference(args):
     if rank != 0:
         return
     from oracle import oracle as orc
-
-    import ramvamp_b200 as rv  # layout arithmetic only (no GPU calls)
+    from oracle.layout import layer_layout
 
     orc.build()
     n_layers = args.layers
-    lays = layouts(rv, n_layers)
+    lays = [layer_layout(l) for l in range(n_layers)]
     threads = os.cpu_count() or 1
     sample = [0, 6] if n_layers > 6 else [0]
     blobs = {l: orc.fill_layer_synthetic(lays[l], SEED + l, 0.02, threads) for l in sample}
@@ -587,7 +586,9 @@ def model_cpu_baseline(cfg, sample_layers=(0, 6), positions=64):
     threads = os.cpu_count() or 1
     layers = [l for l in sample_layers if l < cfg.n_layers]
     weights, moe = synthetic_host(cfg, MODEL_SEED, layers, threads)
-    sub = type(cfg)(**{**cfg.__dict__, "n_layers": len(layers)})
+    import dataclasses
+
+    sub = dataclasses.replace(cfg, n_layers=len(layers))
     impl = orc.default_impl()  # the arm the reference dispatches to on this host
     ref = RefModel(sub, weights, moe, positions + 2, threads, impl=impl)
     for p in range(positions):  # fill the caches (untimed)
@@ -613,9 +614,9 @@ def run_reference_model(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from ramvamp_b200.model import ModelConfig  # configuration only (no GPU calls)
+    from oracle.layout import ModelShape
 
-    cfg = ModelConfig(n_layers=args.layers)
+    cfg = ModelShape(n_layers=args.layers)
     cpu = model_cpu_baseline(cfg)
     line = {
         "impl": "reference", "metric": MODEL_METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": args.gpus,
@@ -928,13 +929,12 @@ def run_reference_batched(args):
     if rank != 0:
         return
     from oracle import oracle as orc
-
-    import ramvamp_b200 as rv  # layout arithmetic only (no GPU calls)
+    from oracle.layout import layer_layout
 
     orc.build()
     threads = os.cpu_count() or 1
     n_layers, n_tok = workload_shape(args)
-    full = rv.qwen3_layer_layout(0)
+    full = layer_layout(0)
     blobs = orc.fill_layer_synthetic(full, SEED, 0.02, threads)
     router = orc.synth_normal(SEED + 1000, 0, 0.02, E * H).reshape(E, H)
     x = orc.synth_normal(SEED + 7, 0, 1.0, 32 * H).reshape(32, H)

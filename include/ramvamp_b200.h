@@ -75,7 +75,7 @@ typedef enum rv_quant_format {
 } rv_quant_format;
 
 /* One Q8_K activation block.  The reference's BlockQ8K
- * (kernels/quants/blocks.rs:260-268) is not repr(C); this is the packed
+ * (kernels/quants/blocks.rs:146-153) is not repr(C); this is the packed
  * 292-byte C layout every rv_ call uses: d at 0, qs at 4, bsums at 260. */
 typedef struct rv_block_q8k {
   float d;
@@ -219,7 +219,7 @@ RV_API int rv_rmsnorm(const float *x, const float *weight, size_t n, size_t n_ro
 RV_API int rv_softmax(float *x, size_t n, size_t n_rows, rv_stream stream);
 
 /* Replaces Backend::swiglu_combine / primitives::swiglu_combine
- * (kernels/primitives/activation.rs:153-165): gate[i] <- silu(gate[i]) * up[i]
+ * (kernels/primitives/activation.rs:30-42): gate[i] <- silu(gate[i]) * up[i]
  * (device).  The SiLU's exponential reproduces glibc expf bit for bit. */
 RV_API int rv_swiglu_combine(float *gate, size_t gate_len, const float *up, size_t up_len,
                       rv_stream stream);
@@ -451,7 +451,9 @@ RV_API int rv_moe_profile_read(rv_moe *m, float *ms_out, size_t cap, size_t *n_s
  * RV_ERR_LENGTH_MISMATCH (or RV_ERR_UNIMPLEMENTED for the geometry) before
  * any work is queued.  The first call on each device looks up the array's
  * device address and uploads the SiLU exception table, so make that first
- * call before any stream capture.  Every call shares the one array and it
+ * call before any stream capture.  The looked-up address is kept for the
+ * life of the process, so the library must not be used across a
+ * cudaDeviceReset of that device.  Every call shares the one array and it
  * keeps the previous call's contents (counters are cleared at the start of
  * each call): calls that overlap on the GPU -- on two streams, or from two
  * threads -- race and must be serialized by the caller.  Results are
@@ -534,15 +536,6 @@ RV_API int rv_decode_advance(int32_t *position_dev, const uint32_t *next_token, 
 RV_API int rv_argmax(const float *x, size_t n, uint32_t *out, rv_stream stream);
 /* primitives::vec_add (kernels/primitives/vec.rs:10-22): a[i] += b[i]. */
 RV_API int rv_vec_add(float *a, const float *b, size_t n, rv_stream stream);
-
-/* Asks the L2 cache to fetch up to 8 device byte ranges (the 16-byte
- * aligned part of each), with cp.async.bulk.prefetch.L2 from a small grid
- * that exits once the requests are issued: a hint with no result, for
- * pulling the next layer's weights into L2 while the current one runs (a
- * decode step's parallel graph branch).  Not in the reference (its weights
- * live in host memory).  RV_ERR_INVALID_ARGUMENT for n > 8 or a null range
- * of non-zero size. */
-RV_API int rv_prefetch_l2(const void *const *ptrs, const size_t *bytes, uint32_t n, rv_stream stream);
 
 /* One layer's weights for rv_attn_block (device pointers, the GGUF-style
  * row-major packed matrices of model/shapes.rs:14-35). */

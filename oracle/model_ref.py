@@ -21,7 +21,7 @@ def synthetic_host(cfg, seed: int, layers, threads: int = 8):
     layers: the same seeded values (or_synth_normal, bit-identical to the GPU
     generator) at the same offsets, through the oracle's restatement of the
     reference's quantizers.  Returns (weights dict, MoE layers) for RefModel."""
-    from ramvamp_b200 import qwen3_layer_layout  # layout arithmetic only
+    from .layout import layer_layout
 
     H, off = cfg.hidden, [0]
 
@@ -52,8 +52,8 @@ def synthetic_host(cfg, seed: int, layers, threads: int = 8):
         ffn_norm = norm_w(H, keep)
         router = normal(cfg.n_experts * H, 0.02, keep)
         if keep:
-            lay = qwen3_layer_layout(l, hidden=H, moe=cfg.moe, n_experts=cfg.n_experts,
-                                     down_format=O.Q6_K if cfg.q6k_layer(l) else O.Q4_K)
+            lay = layer_layout(l, hidden=H, moe=cfg.moe, n_experts=cfg.n_experts,
+                               down_format=O.Q6_K if cfg.q6k_layer(l) else O.Q4_K)
             blobs = O.fill_layer_synthetic(lay, seed * 1000 + l, 0.02, threads)
             moe.append(O.make_layer(H, cfg.moe, cfg.n_experts, cfg.top_k, cfg.eps, ffn_norm, router, blobs,
                                     lay.stride, lay.gate_off, lay.up_off, lay.down_off, lay.gate_format,
@@ -103,7 +103,7 @@ class RefModel:
     def generate(self, prompt, n_new: int, on_logits=None):
         """Greedy continuation: the prompt one token per step, then each
         argmax (first index wins ties) as the next input."""
-        from ramvamp_b200.model import top1
+        from .layout import top1
 
         tok, out = prompt[0], []
         for i in range(len(prompt) + n_new - 1):

@@ -20,7 +20,7 @@ Q4_K, Q5_K, Q6_K, Q8_0, Q8_K = 0, 1, 2, 3, 4
 SCALAR, AVX2, LANES = 0, 1, 2
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, Q8_0: 34, Q8_K: 292}
 
-# BlockQ8K (blocks.rs:260-268) as a packed 292-byte record.
+# BlockQ8K (blocks.rs:146-153) as a packed 292-byte record.
 Q8K_DTYPE = np.dtype([("d", "<f4"), ("qs", "i1", (256,)), ("bsums", "<i2", (16,))])
 assert Q8K_DTYPE.itemsize == 292
 # BlockQ8_0 (blocks.rs:167-178): d (already f16-rounded) + 32 i8, 36 bytes.

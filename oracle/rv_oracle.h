@@ -49,7 +49,7 @@ enum {
   OR_ERR_ROUTED_OUT_OF_RANGE = 20
 };
 
-/* BlockQ8K (blocks.rs:260-268) in a packed 292-byte C layout. */
+/* BlockQ8K (blocks.rs:146-153) in a packed 292-byte C layout. */
 typedef struct or_block_q8k {
   float d;
   int8_t qs[256];

@@ -36,7 +36,6 @@ from ._lib import RvError as KernelError
 from ._lib import check as _check
 
 __all__ = [
-    "prefetch_l2",
     "QuantFormat", "KernelError", "Q8K_BYTES", "quantize_row_q8_k", "gemv_q8_k", "gemv_q8_k_rows",
     "gemv_q8_k_batched", "FusedPart", "gemv_q8_k_fused_rows", "rmsnorm", "softmax",
     "swiglu_combine", "debug_block_sums", "CudaBackend", "ExpertTable", "MoeEngine", "MoeConfig",
@@ -648,16 +647,6 @@ def attn_weights(attn_norm, attn_q, attn_k, attn_v, attn_output, q_norm, k_norm,
     keeps them alive)."""
     return _lib.AttnWeights(_p(attn_norm), _p(attn_q), _p(attn_k), _p(attn_v), _p(attn_output), _p(q_norm),
                             _p(k_norm), int(attn_q_format), int(attn_v_format), int(attn_output_format))
-
-
-def prefetch_l2(tensors: Sequence[torch.Tensor]) -> None:
-    """Ask the L2 cache to fetch these device tensors' bytes (at most 8; a
-    hint, nothing waits on it): the next layer's weights while the current
-    layer runs."""
-    n = len(tensors)
-    ptrs = (_lib.P * max(n, 1))(*[_p(t) for t in tensors])
-    sizes = (_lib.SZ * max(n, 1))(*[_nbytes(t) for t in tensors])
-    _check(lib().rv_prefetch_l2(ptrs, sizes, n, _stream()))
 
 
 def rmsnorm_quantize(x: torch.Tensor, w: torch.Tensor, eps: float, q8k_out: torch.Tensor,

@@ -119,7 +119,6 @@ SIGNATURES = {
     "rv_rmsnorm_quantize": (I32, [P, P, SZ, F32, P, P, P]),
     "rv_argmax": (I32, [P, SZ, P, P]),
     "rv_vec_add": (I32, [P, P, SZ, P]),
-    "rv_prefetch_l2": (I32, [ctypes.POINTER(P), ctypes.POINTER(SZ), U32, P]),
     "rv_attention": (I32, [P, P, P, SZ, SZ, SZ, SZ, F32, P, SZ, P, P]),
     "rv_gemv_q8_k_fused_rows": (I32, [ctypes.POINTER(FusedPartC), SZ, SZ, SZ, P, SZ, P]),
     "rv_rmsnorm": (I32, [P, P, SZ, SZ, F32, P, P]),

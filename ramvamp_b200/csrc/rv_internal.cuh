@@ -128,12 +128,6 @@ RV_DEVFN bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t sleep_n
   }
 }
 
-// L2 prefetch of `bytes` (multiple of 16, 16-byte aligned) at src.  The
-// issuing grid completes only once the prefetch has landed.
-RV_DEVFN void prefetch_l2(const void *src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // ------------------------------------------------- thread-block clusters
 RV_DEVFN uint32_t cluster_ctarank() {
   uint32_t r;

@@ -909,31 +909,3 @@ __global__ void __launch_bounds__(256) k_norm_quant(const float *__restrict__ x,
     o[4 + lane] = (uint8_t)sat_i8(roundf(__fmul_rn(v, id)));
   }
 }
-
-// ------------------------------------------------------- L2 prefetch
-// cp.async.bulk.prefetch.L2 of up to RV_PF_MAX byte ranges (16-byte aligned
-// starts, sizes multiples of 16), cut into RV_PF_CHUNK pieces spread over
-// the grid's threads.  A hint to the L2: it returns nothing and nothing
-// waits on it, so the CTAs exit as soon as their requests are issued.  Used
-// to pull a decode step's next-layer weights into L2 while the current layer
-// runs.
-#define RV_PF_MAX 8
-#define RV_PF_CHUNK 32768
-struct PrefetchList {
-  const uint8_t *p[RV_PF_MAX];
-  size_t bytes[RV_PF_MAX];
-  size_t chunk0[RV_PF_MAX + 1];  // first chunk of range r; chunk0[n] = total
-  int n;
-};
-
-__global__ void __launch_bounds__(32) k_prefetch_l2(PrefetchList L) {
-  const size_t total = L.chunk0[L.n];
-  // Chunk c goes to CTA c % gridDim.x: consecutive chunks leave from different SMs.
-  for (size_t c = blockIdx.x + (size_t)threadIdx.x * gridDim.x; c < total; c += (size_t)gridDim.x * blockDim.x) {
-    int r = 0;
-    while (r + 1 < L.n && c >= L.chunk0[r + 1]) r++;
-    const size_t off = (c - L.chunk0[r]) * RV_PF_CHUNK;
-    const uint32_t len = (uint32_t)min((size_t)RV_PF_CHUNK, L.bytes[r] - off);
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(L.p[r] + off), "r"(len) : "memory");
-  }
-}

@@ -19,7 +19,6 @@
 #include "rv_moe.cuh"
 #include "rv_tc.cuh"
 #include "rv_ep.cuh"
-#include "rv_fused.cuh"
 #include "rv_attn.cuh"
 
 #include "_gen/expf_exceptions.inc"
@@ -846,7 +845,6 @@ struct rv_moe {
   float *dres;  // [max_tokens][H] device residual of rv_moe_forward_host
   int last_T = 0;
   bool spec = true;   // speculative expert dispatch for decode (RV_DECODE_SPEC=0 turns it off)
-  bool fused = false;  // one-token decode in one cooperative kernel (RV_DECODE_FUSED=1 turns it on)
   std::vector<cudaEvent_t> prof;  // 5 events per set
   size_t prof_next = 0;
 };
@@ -940,7 +938,6 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
   const size_t PS = std::max(P, std::min<size_t>(T, RV_SPEC_MAX_T) * (size_t)d.E);
   const size_t units_cap = std::max<size_t>((size_t)m->max_units, (size_t)d.E);
   if (const char *v = getenv("RV_DECODE_SPEC")) m->spec = atoi(v) != 0;
-  if (const char *v = getenv("RV_DECODE_FUSED")) m->fused = atoi(v) != 0;
   const size_t max_tc = std::min<size_t>((size_t)d.E, P) + P / RV_TC_NT + 1;
   const size_t padded_rows = (P + 16 * (size_t)d.E + 16 + 15) & ~(size_t)15;  // every expert's rows rounded up to 16
   // One arena for every scratch buffer the forward touches.
@@ -964,7 +961,6 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
       {16, (void **)&B.route_cnt},
       {((size_t)d.H / 4 + 1) * 4, (void **)&B.down_cnt},  // one per down row tile (>= 4 rows)
       {std::min<size_t>(T, RV_SPEC_MAX_T) * (size_t)d.E * 8, (void **)&B.spec},
-      {(size_t)RV_FZ_INTS * 4, (void **)&B.fz},
       {T * d.H * 4, (void **)&m->dres},
       {padded_rows * d.H * 2, (void **)&B.xq},
       {padded_rows * d.hb * 32, (void **)&B.xm},
@@ -1039,15 +1035,12 @@ static bool geo_qwen3(const MoeDims &d) { return d.H == 2048 && d.M == 768 && d.
 // cluster of all the CTAs when there are at most 8 of them.  Each CTA takes
 // a whole SM's shared memory, so no other kernel's CTA shares an SM with a
 // serial chain.
-template <bool FUSED>
 static void (*route_chain_kernel(bool cluster, bool q3))(MoeDims, MoeBufs, int, MoeWeights) {
-  if (cluster) return q3 ? k_route_chain<true, RV_GEO_QWEN3, FUSED> : k_route_chain<true, 0, FUSED>;
-  return q3 ? k_route_chain<false, RV_GEO_QWEN3, FUSED> : k_route_chain<false, 0, FUSED>;
+  if (cluster) return q3 ? k_route_chain<true, RV_GEO_QWEN3> : k_route_chain<true, 0>;
+  return q3 ? k_route_chain<false, RV_GEO_QWEN3> : k_route_chain<false, 0>;
 }
 
-// fused: the next kernel is k_decode_fused (see k_route_chain).
-static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, bool fused, const MoeWeights &W,
-                              cudaStream_t s) {
+static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, const MoeWeights &W, cudaStream_t s) {
   const size_t xrow = (size_t)(d.H + 4) * 4;
   const size_t fixed = 16 + (size_t)T * xrow + (size_t)d.H * 4;
   int ch = 0, grid = 0;
@@ -1056,8 +1049,7 @@ static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, bool fu
   size_t room = 0;
   for (int v = 0; v < 2 && !kern; v++) {  // the cluster variant first
     const bool q3 = geo_qwen3(d);
-    void (*k)(MoeDims, MoeBufs, int, MoeWeights) =
-        fused ? route_chain_kernel<true>(v == 0, q3) : route_chain_kernel<false>(v == 0, q3);
+    void (*k)(MoeDims, MoeBufs, int, MoeWeights) = route_chain_kernel(v == 0, q3);
     cudaFuncAttributes fa;
     RV_CUDA(cudaFuncGetAttributes(&fa, k));
     room = (size_t)RV_SMEM_PER_CTA - fa.sharedSizeBytes;
@@ -1319,64 +1311,6 @@ static int check_engine_layer(const rv_moe *m, const rv_expert_table *table, uin
   return RV_OK;
 }
 
-// One-token decode through k_route_chain + k_decode_fused (the Qwen3
-// geometry with Q4_K gate/up and Q4_K or Q6_K down).  Returns 1 when this
-// layer does not qualify (the caller takes the multi-kernel path), 0 when
-// launched, or -status.
-template <int FGU, int FDN>
-static int launch_fused_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, cudaStream_t s) {
-  void (*kern)(MoeDims, MoeBufs, MoeWeights) = k_decode_fused<FGU, FDN, RV_GEO_QWEN3>;
-  const FusedLayout FL = fused_layout<FGU, FDN>(d, W.gu_row_bytes, W.down_row_bytes);
-  static int checked[3][3];  // 1: fits, -1: does not
-  int &ck = checked[FGU][FDN];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return -RV_ERR_CUDA;
-  const int units = d.K;  // one token: its top-k units, the grids stride over more
-  const int nb = (d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC;
-  const int ncta = std::max(nb, std::max(units * (d.M / RV_FUSED_GU_R), units * (d.H / RV_FUSED_DN_ROWS) / 4));
-  if (ck == 0) {
-    ck = -1;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FL.total) == cudaSuccess) {
-      int per_sm = 0, sms = 0;
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, RV_FUSED_THREADS, FL.total);
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      // Room beside the chain kernel's CTAs (one per SM, at most 8).
-      if (per_sm > 0 && (long)per_sm * (sms - 8) >= ncta) ck = 1;
-    }
-    cudaGetLastError();
-  }
-  if (ck < 0) return 1;
-  int rc = launch_route_chain(d, B, 1, true, W, s);
-  if (rc) return -rc;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ncta);
-  cfg.blockDim = dim3(RV_FUSED_THREADS);
-  cfg.dynamicSmemBytes = FL.total;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeCooperative;
-  attr[1].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, d, B, W);
-  if (e != cudaSuccess) {
-    rv_set_error(RV_ERR_CUDA, "fused decode launch: %s", cudaGetErrorString(e));
-    return -RV_ERR_CUDA;
-  }
-  return 0;
-}
-
-static int launch_decode_fused(rv_moe *m, const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
-                               const rv_layer_layout &L, cudaStream_t s) {
-  (void)m;
-  if (!geo_qwen3(d) || L.gate_format != RV_Q4_K || L.up_format != RV_Q4_K) return 1;
-  if (L.down_format == RV_Q6_K) return launch_fused_t<RV_Q4_K, RV_Q6_K>(d, B, W, s);
-  if (L.down_format == RV_Q4_K) return launch_fused_t<RV_Q4_K, RV_Q4_K>(d, B, W, s);
-  return 1;
-}
-
 extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t layer,
                               const float *ffn_norm, const float *router, float *residual,
                               size_t n_tokens, uint32_t *topk_ids, float *topk_weights,
@@ -1412,20 +1346,6 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
   if ((rc = prof_record(ev, 0, evflags, s))) return rc;
   B.ms = T < RV_MOE_MT ? T : RV_MOE_MT;
   int spec_units = 0;
-  int frc = 1;
-  if (!(flags & RV_MOE_TENSOR) && T == 1 && m->spec && m->fused &&
-      (frc = launch_decode_fused(m, d, B, W, L, s)) <= 0) {
-    // one token: the exact chains, then everything else in one cooperative kernel
-    if (frc < 0) return -frc;
-    if ((rc = prof_record(ev, 1, evflags, s))) return rc;
-    if ((rc = prof_record(ev, 2, evflags, s))) return rc;
-    if ((rc = prof_record(ev, 3, evflags, s))) return rc;
-    if ((rc = prof_record(ev, 4, evflags, s))) return rc;
-    m->last_T = T;
-    if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
-    if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, n_tokens * d.K * 4, cudaMemcpyDeviceToDevice, s));
-    return RV_OK;
-  }
   if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T && m->spec) {
     // decode, speculative: norm, Q8_K and logit bounds; then the exact
     // router chains beside gate/up on the speculated experts; then down
@@ -1436,7 +1356,7 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
     RV_CUDA(launch_pdl(geo_qwen3(d) ? k_route_spec<RV_GEO_QWEN3> : k_route_spec<0>,
                        dim3((unsigned)((d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC)), dim3(128),
                        std::max(rs_need, (size_t)RV_ROUTE_SMEM_ONE_PER_SM), s, d, B));
-    if ((rc = launch_route_chain(d, B, T, false, W, s))) return rc;
+    if ((rc = launch_route_chain(d, B, T, W, s))) return rc;
     spec_units = std::min(d.E, T * d.K);
   } else if (!(flags & RV_MOE_TENSOR) && T <= RV_SMALL_T) {
     // decode: routing, norm, Q8_K and dispatch in one launch
@@ -2069,33 +1989,6 @@ extern "C" int rv_vec_add(float *a, const float *b, size_t n, rv_stream stream) 
   return RV_OK;
 }
 
-extern "C" int rv_prefetch_l2(const void *const *ptrs, const size_t *bytes, uint32_t n, rv_stream stream) {
-  if (n == 0) return RV_OK;
-  if (!ptrs || !bytes) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "prefetch_l2: null pointer");
-  if (n > RV_PF_MAX) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "prefetch_l2: %u ranges (at most %d)", n, RV_PF_MAX);
-  PrefetchList L{};
-  size_t total = 0;
-  for (uint32_t i = 0; i < n; i++) {
-    if (bytes[i] && !ptrs[i]) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "prefetch_l2: range %u is null", i);
-    // The 16-byte-aligned part of the range; a range with none is skipped.
-    const uintptr_t b = ((uintptr_t)ptrs[i] + 15) & ~(uintptr_t)15;
-    const uintptr_t e = ((uintptr_t)ptrs[i] + bytes[i]) & ~(uintptr_t)15;
-    if (!ptrs[i] || e <= b) continue;
-    L.p[L.n] = (const uint8_t *)b;
-    L.bytes[L.n] = e - b;
-    L.chunk0[L.n] = total;
-    total += (L.bytes[L.n] + RV_PF_CHUNK - 1) / RV_PF_CHUNK;
-    L.n++;
-  }
-  if (L.n == 0) return RV_OK;
-  L.chunk0[L.n] = total;
-  // About four chunks per CTA, at most one CTA per SM of a B200.
-  const unsigned grid = (unsigned)std::min<size_t>(148, (total + 3) / 4);
-  k_prefetch_l2<<<grid, 32, 0, (cudaStream_t)stream>>>(L);
-  RV_LAUNCH_CHECK();
-  return RV_OK;
-}
-
 extern "C" int rv_synth_normal(uint64_t seed, uint64_t offset, float sigma, float *out, size_t n,
                                rv_stream stream) {
   if (n == 0) return RV_OK;
@@ -2223,7 +2116,8 @@ extern "C" int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_la
   }
   // The same geometry and scratch carving as rv_moe_create, for
   // RV_STATIC_MAX_TOKENS rows; counters first so one memset clears them.
-  rv_moe m;
+  // Value-initialized: every buffer this path does not carve stays null.
+  rv_moe m{};
   m.device = dev;
   m.cfg = *cfg;
   m.max_tokens = RV_STATIC_MAX_TOKENS;
@@ -2246,7 +2140,7 @@ extern "C" int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_la
       {(size_t)d.E * 4, (void **)&B.counts},
       {(size_t)m.max_units * d.mb * 4, (void **)&B.tile_cnt},
       {16, (void **)&B.route_cnt},
-      {((size_t)d.H / 8 + 1) * 4, (void **)&B.down_cnt},
+      {((size_t)d.H / 4 + 1) * 4, (void **)&B.down_cnt},  // as rv_moe_create: one per down row tile
       {16, (void **)&B.n_units},
       {T * d.H * 4, (void **)&B.normed},
       {T * d.act_stride, (void **)&B.acts},
@@ -2286,7 +2180,10 @@ extern "C" int rv_moe_forward_static(const rv_moe_config *cfg, const rv_layer_la
   rv_row_bytes(L->gate_format, L->hidden, &W.gu_row_bytes);
   rv_row_bytes(L->down_format, L->moe, &W.down_row_bytes);
   const int Tn = (int)n_tokens;
-  const size_t smem = 16 + (size_t)2 * d.H * 4 + (size_t)Tn * (d.H + 4) * 4 + 4 * (size_t)Tn * sizeof(double) + 16;
+  // Shared memory padded past half an SM's, as in rv_moe_forward: no two
+  // routing CTAs (each running one serial router chain) share an SM.
+  const size_t need = 16 + (size_t)2 * d.H * 4 + (size_t)Tn * (d.H + 4) * 4 + 4 * (size_t)Tn * sizeof(double) + 16;
+  const size_t smem = need < RV_ROUTE_SMEM_ONE_PER_SM ? RV_ROUTE_SMEM_ONE_PER_SM : need;
   RV_CUDA(launch_pdl(k_route_decode, dim3((unsigned)d.E), dim3(128), smem, s, d, B));
   switch (L->gate_format) {
     case RV_Q4_K: launch_gate_up<RV_Q4_K>(d, B, W, Tn, 0, s); break;

@@ -54,8 +54,6 @@ struct MoeBufs {
   int *route_cnt;          // [1] CTAs done in k_route_decode, zero between calls
   int *down_cnt;           // [H/8] units done per down row tile, zero between calls
   float2 *spec;            // [T][E] (lo, hi) bounds of the router logits (speculative decode)
-  int *fz;                 // fused decode kernel counters, one per 128-byte line (RV_FZ_*); zero
-                           // between calls
   int T;
   int ms;                  // activation slots per CTA pass: min(T, RV_MOE_MT)
   int max_units;
@@ -841,11 +839,7 @@ __global__ void __launch_bounds__(128) k_route_spec(MoeDims dd, MoeBufs B) {
 // completed.  The residual was written by the previous layer, complete
 // before k_route_spec triggered this launch.
 #define RV_CHAIN_THREADS 160
-// FUSED: the next kernel is k_decode_fused, which computes the logit bounds
-// itself; this grid then follows the previous layer directly, so its
-// compute warps wait for it before reading the residual, and the routing
-// ranks every expert (the bounds are not written yet).
-template <bool CLUSTER, int GEO, bool FUSED>
+template <bool CLUSTER, int GEO>
 __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, MoeBufs B, int CH, MoeWeights W) {
   (void)W;  // the layer's expert slabs (unused: L2 prefetches from here delayed the pipeline)
   const MoeDims d = geo_dims<GEO>(dd);
@@ -885,7 +879,7 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, Mo
   if (warp == 4) {
     pdl_wait();
     pdl_trigger();
-    if (CLUSTER && lead && !FUSED) {
+    if (CLUSTER && lead) {
       // While the chains run: the speculated experts of every token, so
       // the routing below ranks only those (named barrier 2 hands them over).
       spec_candidates_warp(d.E, d.K, T, B.spec, s_cand, s_ncand, s_cmask, lane);
@@ -893,7 +887,6 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, Mo
       asm volatile("bar.arrive 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");    }
     return;
   }
-  if constexpr (FUSED) pdl_wait();  // the residual is the previous kernel's output
   if (tid == 0) {  // the residual and norm weight first: the norm needs them before the chains need the rows
     if (xbulk) {
       mbar_arrive_expect_tx(bar + 1, (uint32_t)((T + 1) * d.H * 4));
@@ -966,11 +959,11 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, Mo
   }
   RV_PHASE(5, 4);
   for (int e = tid; e < 256; e += 128) s_cnt[e] = 0;
-  if constexpr (CLUSTER && !FUSED) asm volatile("bar.sync 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");
+  if constexpr (CLUSTER) asm volatile("bar.sync 2, %0;" ::"n"(RV_CHAIN_THREADS) : "memory");
   else cta_sync<128>();
   if (T <= 2) {
     for (int t = 0; t < T; t++) {
-      if constexpr (CLUSTER && !FUSED)
+      if constexpr (CLUSTER)
         route_token_block<128>(d, B, t, lgs + (size_t)t * d.E, es[0], s_ps, s_sel, s_red, s_cnt, s_ids,
                                s_cand + t * 256, s_ncand[t], s_cmask + t * 8);
       else

@@ -21,7 +21,6 @@ import numpy as np
 import torch
 
 from . import (AttnEngine, ExpertTable, MoeEngine, QuantFormat, QWEN3_Q6K_DOWN_LAYERS, _check, _p, _stream,
-               prefetch_l2,
                attn_weights, dequantize_rows, gemv_q8_k, lib, qwen3_layer_layout, quantize_row_q8_0,
                quantize_weights, rmsnorm_quantize, synth_normal)
 
@@ -141,16 +140,9 @@ class Decoder:
     forward_token_traced (model/forward.rs:2548-2780) plus the greedy
     argmax; all state (token, position, caches) is on the device."""
 
-    def __init__(self, weights: Qwen3Weights, max_positions: int = 1024, device: int = 0, prefetch: bool = False):
+    def __init__(self, weights: Qwen3Weights, max_positions: int = 1024, device: int = 0):
         cfg = weights.cfg
         self.w, self.cfg, self.device = weights, cfg, device
-        # prefetch: while layer l's MoE block runs, a parallel branch asks
-        # the L2 to fetch layer l+1's attention matrices and router rows
-        # (~13.5 MB), so the next attention block's GEMVs read them from L2.
-        # Off by default: measured at 2.95 ms per step against 2.82-2.93 ms
-        # without it.
-        self.prefetch = prefetch
-        self.pf_stream = torch.cuda.Stream(device) if prefetch else None
         self.max_positions = max_positions
         self.attn = AttnEngine(cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, max_positions,
                                cfg.rope_theta, cfg.eps, device, hidden=cfg.hidden)
@@ -179,20 +171,12 @@ class Decoder:
     def _launch_step(self):
         cfg, w, s = self.cfg, self.w, _stream()
         H = cfg.hidden
-        main = torch.cuda.current_stream()
         dequantize_rows(Q.Q4_K, w.token_embd, H, cfg.vocab, rows=self.token, out=self.residual)
         for l, lw in enumerate(w.layers):
             # attention half (forward.rs:2572-2652), residual in place
             self.attn.block(l, self.attn_w[l], self.residual, position_dev=self.position)
-            if self.prefetch and l + 1 < len(w.layers):
-                nxt = w.layers[l + 1]
-                self.pf_stream.wait_stream(main)
-                with torch.cuda.stream(self.pf_stream):
-                    prefetch_l2([nxt.attn_q, nxt.attn_k, nxt.attn_v, nxt.attn_output, nxt.router])
             # MoE block (forward.rs:2654-2754), residual in place
             self.moe.forward(w.experts, l, lw.ffn_norm, lw.router, self.residual)
-        if self.prefetch:
-            main.wait_stream(self.pf_stream)  # joins the branch (required to end a graph capture)
         rmsnorm_quantize(self.residual, w.output_norm, cfg.eps, self.acts_k)
         gemv_q8_k(Q.Q6_K, w.lm_head, H, cfg.vocab, self.acts_k, self.logits)
         _check(lib().rv_argmax(_p(self.logits), cfg.vocab, _p(self.next_token), s))

@@ -6,8 +6,7 @@ every kernel stamps %globaltimer (nanoseconds, common to all SMs) at its
 phases; the normal build compiles the stamps out.
 
     python -m ramvamp_b200.phase_clock decode [layers]   # one decode layer, CTA phases
-                                                         # (RV_DECODE_FUSED=1: the one-token cooperative
-                                                         # kernel; RV_DECODE_SPEC=0: without speculation)
+                                                         # (RV_DECODE_SPEC=0: without speculation)
     python -m ramvamp_b200.phase_clock tensor [tokens]   # tensor-path GEMM: per-CTA phases + one CTA's stages
 
 Output: microseconds from the first stamp of the traced layer.
@@ -92,22 +91,6 @@ def decode(n_layers: int = 4) -> None:
     bufs = [_read(lib, k) for k in range(6)]
     first = bufs[0][:, 0]
     t0 = first[first != 0].min()
-    fused = os.environ.get("RV_DECODE_SPEC", "1") != "0" and os.environ.get("RV_DECODE_FUSED", "0") == "1"
-    if fused:
-        _print_phases("fused: norm + bounds CTAs", bufs[0], t0, ["start", "", "residual", "norm", "bounds", "q8k",
-                                                                "norm:squares", "", "", "norm:inv"])
-        _print_phases("exact chains", bufs[5], t0, ["start", "residual", "rows", "chain done", "LAST:start",
-                                                    "LAST:routed"])
-        _print_phases("fused: all CTAs", bufs[1], t0, ["start", "bounds visible", "gate/up data", "", "gate/up:quant",
-                                                       "end"])
-        _print_phases("fused: warp 0, first down tile", bufs[2], t0, ["start", "", "unit ready", "", "done"])
-        tail = bufs[3][0]
-        print("routing tail (chain CTA 0):")
-        for i, n in enumerate(["logits+max(warp)", "max(block)", "exp+sum(warp)", "sum(block)", "probs+finite",
-                               "rank", "sync", "weights"]):
-            if tail[i]:
-                print(f"   {n:16s} {(tail[i] - t0) / 1e3:8.2f}")
-        return
     if os.environ.get("RV_DECODE_SPEC", "1") != "0":
         _print_phases("route (norm, bounds)", bufs[0], t0, ["start", "pdl_wait", "residual", "norm", "bounds",
                                                             "q8k", "norm:squares", "", "", "norm:inv"])

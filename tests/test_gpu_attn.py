@@ -220,27 +220,3 @@ def test_argmax_edge_cases(rv):
             rc = rv.lib().rv_argmax(buf.data_ptr() + 4 * shift, x.size, out.data_ptr(), rv._stream())
             assert rc == 0
             assert int(host(out)[0]) == top1(x), (x.size, shift)
-
-
-def test_prefetch_l2_hint(rv):
-    """rv_prefetch_l2: a hint with no result — ranges of any alignment and
-    size (including ones with no aligned 16 bytes) launch and leave memory
-    as it was; more than 8 ranges or a null range of non-zero size fail."""
-    import ctypes
-
-    from ramvamp_b200 import _lib
-
-    big = torch.arange(3 << 20, dtype=torch.int32, device="cuda")  # 12 MiB
-    small = torch.arange(7, dtype=torch.uint8, device="cuda")
-    before = (big.clone(), small.clone())
-    rv.prefetch_l2([big, small, big[1:], big[5:9]])
-    rv.prefetch_l2([])
-    torch.cuda.synchronize()
-    assert torch.equal(big, before[0]) and torch.equal(small, before[1])
-    ptrs = (_lib.P * 9)(*([big.data_ptr()] * 9))
-    sizes = (_lib.SZ * 9)(*([64] * 9))
-    assert rv.lib().rv_prefetch_l2(ptrs, sizes, 9, rv._stream()) != 0
-    ptrs = (_lib.P * 1)(None)
-    sizes = (_lib.SZ * 1)(64)
-    assert rv.lib().rv_prefetch_l2(ptrs, sizes, 1, rv._stream()) != 0
-    rv.device_status()

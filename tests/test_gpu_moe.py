@@ -236,30 +236,6 @@ def test_decode_speculation_with_a_tie_at_the_cut(rv, orc, world):
     assert bits(host(res)).tobytes() == bits(want).tobytes()
 
 
-def test_fused_decode_kernel_bit_identical(rv, orc, world, monkeypatch):
-    """The one-token cooperative kernel (RV_DECODE_FUSED=1): every
-    intermediate tap and the residual equal the oracle's, including a
-    layer whose every expert is speculated (all its CTAs stride)."""
-    table, layers, eng = world
-    monkeypatch.setenv("RV_DECODE_FUSED", "1")
-    fused = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=1, device=0)
-    for li, seed in ((0, 61), (1, 62)):
-        x = inputs(rv, 1, seed)
-        res = x.clone()
-        fused.forward(table, li, layers[li].ffn_norm, layers[li].router, res)
-        want, wids, ww, t = orc.moe_decode(layers[li].oracle, host(x), threads=THREADS, taps=True)
-        g = taps(rv, fused, 1)
-        assert bits(g["staged"]).tobytes() == bits(t["staged"]).tobytes()
-        assert bits(host(res)).tobytes() == bits(want).tobytes()
-    x = inputs(rv, 1, 63)
-    router = (0.01 * x[0]).expand(E, H).contiguous()
-    res = x.clone()
-    fused.forward(table, 0, layers[0].ffn_norm, router, res)
-    want, _, _, _ = orc.moe_decode(oracle_with_router(orc, table, layers, router), host(x), threads=THREADS)
-    assert bits(host(res)).tobytes() == bits(want).tobytes()
-    rv.device_status(0)
-
-
 @pytest.mark.parametrize("T", [1, 2])
 def test_decode_speculation_of_every_expert(rv, orc, world, T):
     """Identical router rows tie every logit: all experts are speculated
@@ -282,11 +258,10 @@ def test_decode_speculation_of_every_expert(rv, orc, world, T):
     rv.device_status(0)
 
 
-@pytest.mark.parametrize("env,val", [("RV_DECODE_SPEC", "0"), ("RV_DECODE_FUSED", "1")])
+@pytest.mark.parametrize("env,val", [("RV_DECODE_SPEC", "0")])
 def test_decode_pipelines_are_identical(rv, world, monkeypatch, env, val):
-    """RV_DECODE_SPEC=0 (routing first, then the experts) and
-    RV_DECODE_FUSED=1 (one token through one cooperative kernel beside the
-    router chains) give the same bits as the default speculative pipeline."""
+    """RV_DECODE_SPEC=0 (routing first, then the experts) gives the same
+    bits as the default speculative pipeline."""
     table, layers, eng = world
     monkeypatch.setenv(env, val)
     other = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=8, device=0)

@@ -94,7 +94,7 @@ def test_empty_calls_are_noops(rv):
 
 
 def test_quantize_and_primitive_errors(rv):
-    """quantize.rs:340-363, norm.rs / softmax.rs / activation.rs error tests."""
+    """quantize.rs:179-200, norm.rs / softmax.rs / activation.rs error tests."""
     lib = rv.lib()
     name = lambda c: lib.rv_status_name(c).decode()
     assert name(lib.rv_quantize_row_q8_k(None, 100, None, 1, None)) == "QuantizeLenMismatch"
@@ -142,3 +142,25 @@ def test_moe_create_rejects_bad_geometry(rv):
     assert name(lib.rv_moe_create(0, ctypes.byref(cfg), 1, ctypes.byref(h))) == "Unimplemented"
     cfg = _lib.MoeConfig(2048, 768, 128, 8, 1, 1e-6)
     assert name(lib.rv_moe_create(0, ctypes.byref(cfg), 0, ctypes.byref(h))) == "InvalidArgument"
+
+
+def test_oracle_layout_twin_matches_the_product(rv):
+    """oracle/layout.py (what the reference arm uses, so that it never loads
+    this library) gives the product's blob geometry for all 48 layers and a
+    small geometry, and the same model shapes."""
+    import dataclasses
+
+    from oracle.layout import Layout, ModelShape, layer_layout
+    from ramvamp_b200.model import ModelConfig
+
+    names = [f.name for f in dataclasses.fields(Layout)]
+    for l in range(48):
+        a, b = layer_layout(l), rv.qwen3_layer_layout(l)
+        assert [getattr(a, n) for n in names] == [getattr(b, n) for n in names], l
+    a = layer_layout(0, hidden=1024, moe=512, n_experts=64, down_format=0)
+    b = rv.qwen3_layer_layout(0, hidden=1024, moe=512, n_experts=64, down_format=rv.QuantFormat.Q4_K)
+    assert [getattr(a, n) for n in names] == [getattr(b, n) for n in names]
+    assert dataclasses.asdict(ModelShape()) == dataclasses.asdict(ModelConfig())
+    for n in (48, 3):
+        assert [ModelShape(n_layers=n).q6k_layer(l) for l in range(n)] == \
+            [ModelConfig(n_layers=n).q6k_layer(l) for l in range(n)]

@@ -71,7 +71,7 @@ def test_f32_to_f16_nearest_even(orc):
 # ----------------------------------------------------------------- Q8_K
 @pytest.mark.parametrize("impl", [0, 1])
 def test_q8_k_anchors_extreme_to_minus_127(orc, impl):
-    """kernels/quants/quantize.rs:301-313."""
+    """kernels/quants/quantize.rs:140-152."""
     x = np.zeros(256, np.float32)
     x[10] = -3.0
     x[20] = 1.5
@@ -83,7 +83,7 @@ def test_q8_k_anchors_extreme_to_minus_127(orc, impl):
 
 @pytest.mark.parametrize("impl", [0, 1])
 def test_q8_k_positive_extreme_maps_to_minus_127(orc, impl):
-    """kernels/quants/quantize.rs:315-326."""
+    """kernels/quants/quantize.rs:154-165."""
     x = np.zeros(256, np.float32)
     x[0] = 4.0
     x[1] = -2.0
@@ -95,13 +95,13 @@ def test_q8_k_positive_extreme_maps_to_minus_127(orc, impl):
 
 @pytest.mark.parametrize("impl", [0, 1])
 def test_q8_k_zero_row_zeroes_everything(orc, impl):
-    """kernels/quants/quantize.rs:328-338."""
+    """kernels/quants/quantize.rs:167-177."""
     b = orc.quantize_row_q8_k(np.zeros(256, np.float32), impl)[0]
     assert b["d"] == 0.0 and not b["qs"].any() and not b["bsums"].any()
 
 
 def test_quantize_len_mismatch_errors(orc):
-    """kernels/quants/quantize.rs:340-363."""
+    """kernels/quants/quantize.rs:179-200."""
     with pytest.raises(orc.OracleError) as e:
         orc.quantize_row_q8_k(np.zeros(100, np.float32), out_blocks=1)
     assert e.value.kind == "QuantizeLenMismatch"
@@ -301,7 +301,7 @@ def test_softmax_all_equal(orc):
 
 
 def test_swiglu_matches_f64_formula(orc):
-    """primitives/activation.rs:201-212."""
+    """primitives/activation.rs:78-89."""
     rng = np.random.default_rng(0x5716)
     g = rng.uniform(-12, 12, 768).astype(np.float32)
     u = rng.uniform(-3, 3, 768).astype(np.float32)
