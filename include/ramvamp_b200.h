@@ -110,6 +110,17 @@ RV_API int rv_row_bytes(int format, size_t in_dim, size_t *out);
  * set when a bounded wait ran out (RV_ERR_TIMEOUT) or a device check failed.
  * Synchronizes `stream`. */
 RV_API int rv_device_status(int device, rv_stream stream);
+/* Failure-path probe.  No counterpart in the reference; its analogue there
+ * is the injected EBUSY of io/stream.rs:2794-2830, which drives the
+ * streamer's typed-error path in tests.  Launches one small kernel that
+ * waits, through the same bounded-wait helper the library's kernels use, on
+ * something nothing will complete -- what = 0: an mbarrier phase no thread
+ * arrives on (the tensor GEMM's and bulk-copy waits); 1: a device flag no
+ * peer sets (the expert-parallel exchange's waits) -- and gives up after
+ * `cycles` SM cycles (1..2e9).  The kernel returns normally and the timeout
+ * lands in the device error word: the next rv_device_status reports
+ * RV_ERR_TIMEOUT, and the device stays usable for the calls after it. */
+RV_API int rv_debug_wait_probe(int device, uint32_t what, uint64_t cycles, rv_stream stream);
 
 /* ----------------------------------------------------------- kernels */
 /* Replaces quants::quantize_row_q8_k (kernels/quants/quantize.rs:68-103,

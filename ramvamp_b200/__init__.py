@@ -660,4 +660,14 @@ def device_status(device: int = 0) -> None:
     """Raise if a device-side bounded wait or check failed since the last call."""
     _check(lib().rv_device_status(device, _stream()))
 
+
+WAIT_MBARRIER, WAIT_FLAG = 0, 1
+
+
+def wait_probe(what: int, cycles: int, device: int = 0) -> None:
+    """rv_debug_wait_probe: one kernel whose bounded wait on `what`
+    (WAIT_MBARRIER or WAIT_FLAG) runs out after `cycles` SM cycles; the
+    next device_status raises Timeout."""
+    _check(lib().rv_debug_wait_probe(device, what, cycles, _stream()))
+
 from . import rvmp  # noqa: E402  (install reader; imports this module lazily)

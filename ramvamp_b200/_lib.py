@@ -96,6 +96,7 @@ SIGNATURES = {
     "rv_block_weights": (SZ, [I32]),
     "rv_row_bytes": (I32, [I32, SZ, ctypes.POINTER(SZ)]),
     "rv_device_status": (I32, [I32, P]),
+    "rv_debug_wait_probe": (I32, [I32, U32, U64, P]),
     "rv_quantize_row_q8_k": (I32, [P, SZ, P, SZ, P]),
     "rv_gemv_q8_k": (I32, [I32, P, SZ, SZ, SZ, P, SZ, P, SZ, P]),
     "rv_gemv_q8_k_rows": (I32, [I32, P, SZ, SZ, SZ, P, SZ, SZ, SZ, P, SZ, P]),

@@ -112,16 +112,47 @@ RV_DEVFN bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: false (and the device error word set) if the phase did not
-// complete within RV_WAIT_CYCLES.  The clock is read only every 32nd probe,
-// and waiters off the critical path pass sleep_ns > 0 to back off between
-// probes, so spinning warps leave the issue slots to warps with work.
-RV_DEVFN bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t sleep_ns = 0) {
+// complete within `limit` SM cycles.  The clock is read only every 32nd
+// probe, and waiters off the critical path pass sleep_ns > 0 to back off
+// between probes, so spinning warps leave the issue slots to warps with work.
+RV_DEVFN bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t sleep_ns = 0,
+                                long long limit = RV_WAIT_CYCLES) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t i = 1;; i++) {
     if (sleep_ns) __nanosleep(sleep_ns);
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 31) == 0 && clock64() - t0 > RV_WAIT_CYCLES) {
+    if ((i & 31) == 0 && clock64() - t0 > limit) {
+      rv_dev_fail(RV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------- flags shared with other GPUs
+// A 32-bit flag another GPU (or this one) sets with a release store at
+// system scope; waiters read it with acquire loads, so everything the
+// setter wrote before its release is visible to the waiter after it.
+// Flags count upwards: a wait for `target` is satisfied by any value at or
+// past it (compared modulo 2^32).
+RV_DEVFN uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+RV_DEVFN void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+RV_DEVFN bool flag_reached(uint32_t v, uint32_t target) { return (int32_t)(v - target) >= 0; }
+// Bounded: false (and the device error word set) if the flag did not reach
+// target within `limit` SM cycles.
+RV_DEVFN bool flag_wait_bounded(const uint32_t *flag, uint32_t target, long long limit = RV_WAIT_CYCLES) {
+  if (flag_reached(ld_acquire_sys(flag), target)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; i++) {
+    __nanosleep(32);
+    if (flag_reached(ld_acquire_sys(flag), target)) return true;
+    if ((i & 15) == 0 && clock64() - t0 > limit) {
       rv_dev_fail(RV_ERR_TIMEOUT);
       return false;
     }

@@ -188,6 +188,48 @@ extern "C" int rv_device_status(int device, rv_stream stream) {
   return RV_OK;
 }
 
+// One CTA waits, through the library's bounded-wait helpers, on something
+// nothing will complete, and gives up after `limit` cycles.
+__global__ void k_wait_probe(uint32_t what, long long limit, const uint32_t *flag) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  if (what == 0) {
+    mbar_init(&bar, 1);  // one arrival expected; none comes
+    mbar_wait_bounded(&bar, 0, 0, limit);
+  } else {
+    flag_wait_bounded(flag, 1u, limit);  // the flag stays 0
+  }
+}
+
+extern "C" int rv_debug_wait_probe(int device, uint32_t what, uint64_t cycles, rv_stream stream) {
+  if (what > 1) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "wait probe: unknown target %u", what);
+  if (cycles == 0 || cycles > (uint64_t)RV_WAIT_CYCLES)
+    RV_FAIL(RV_ERR_INVALID_ARGUMENT, "wait probe: %llu cycles (1..%lld)", (unsigned long long)cycles,
+            (long long)RV_WAIT_CYCLES);
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(device));
+  cudaStream_t s = (cudaStream_t)stream;
+  uint32_t *flag = nullptr;
+  cudaError_t e = cudaSuccess;
+  if (what == 1) {
+    // A flag nothing sets: 4 bytes of the library's own zeroed memory.
+    e = cudaMallocAsync((void **)&flag, 4, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(flag, 0, 4, s);
+  }
+  if (e == cudaSuccess) {
+    k_wait_probe<<<1, 32, 0, s>>>(what, (long long)cycles, flag);
+    e = cudaGetLastError();
+  }
+  if (flag) {
+    const cudaError_t f = cudaFreeAsync(flag, s);
+    if (e == cudaSuccess) e = f;
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) RV_FAIL(RV_ERR_CUDA, "wait probe: %s", cudaGetErrorString(e));
+  return RV_OK;
+}
+
 // =============================================================== kernels
 extern "C" int rv_quantize_row_q8_k(const float *x, size_t n, rv_block_q8k *out, size_t out_blocks,
                                     rv_stream stream) {
