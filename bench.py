@@ -15,9 +15,16 @@ Arms:
                      ramvamp's AVX2 path) on this host's cores, on a bounded
                      sample of layers, scaled to 48 layers
 
-Prints one JSON line (rank 0).  Multi-GPU (torchrun, N>1): batch-1 decode
-does not shard, so every rank runs an independent replica ("replicas only");
-the value is the sum over ranks, timed as the max over ranks.
+Prints one JSON line (rank 0).  On one GPU the line also carries config 4
+at N=1 ("ep_prefill", the base point of the multi-GPU curve) and config 2
+("prefill", with the tensor-pipe fraction of its gate/up stage).
+
+Multi-GPU (torchrun, N>1): batch-1 decode does not shard, so the default
+workload there is config 4, expert-parallel prefill of 4096 tokens through
+48 MoE layers with the 128 experts spread over the N GPUs and the exchange
+done by the library through GPU memory (rv_moe_ep_forward); strong scaling,
+timed as the max over ranks.  `--workload decode` under torchrun runs
+independent decode replicas instead.
 """
 from __future__ import annotations
 
@@ -49,14 +56,19 @@ def parse():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
-    ap.add_argument("--workload", choices=WORKLOADS, default="decode",
-                    help="decode: config 1's expert FFN (default); prefill: config 2; batch: config 3; "
-                         "ep: config 4; model: config 1 whole model (attention + MoE + lm_head, greedy)")
+    ap.add_argument("--workload", choices=WORKLOADS, default=None,
+                    help="decode: config 1's expert FFN (the default on one GPU); prefill: config 2; batch: "
+                         "config 3; ep: config 4 (the default under torchrun with N > 1); model: config 1 "
+                         "whole model (attention + MoE + lm_head, greedy)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode: skip the config-4 (N=1) and config-2 measurements added to the line")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--exact", action="store_true", help="prefill/batch/ep: the exact (AVX2-order) path")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
-    steps, warmup = {"decode": (30, 5), "prefill": (20, 5), "batch": (10, 3), "ep": (5, 3),
+    if a.workload is None:
+        a.workload = "ep" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "decode"
+    steps, warmup = {"decode": (30, 5), "prefill": (20, 5), "batch": (10, 3), "ep": (10, 3),
                      "model": (64, 3)}[a.workload]
     a.steps = steps if a.steps is None else a.steps
     a.warmup = warmup if a.warmup is None else a.warmup
@@ -84,13 +96,21 @@ class ClockSampler:
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.proc = None
 
-    def start(self):
+    def start(self, wait_s: float = 10.0):
+        """Starts sampling and returns once the first sample is written (so
+        a short timed region right after still gets samples)."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
         except (OSError, ValueError):
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < wait_s and self.proc.poll() is None:
+            if os.path.getsize(self.file.name) > 0:
+                break
+            time.sleep(0.05)
 
     def stop(self):
         if self.proc is None:
@@ -326,6 +346,25 @@ def run_cuda(args):
                "sample": f"{n_tok} tokens through layers {used} (one Q6_K-down, one Q4_K-down) on the "
                          f"C oracle's AVX2 arm, time scaled to {n_layers} layers"}
 
+    extras = {}
+    if world == 1 and not args.no_extras:
+        import copy
+
+        a4 = copy.copy(args)
+        a4.workload, a4.steps, a4.warmup, a4.exact = "ep", 10, 3, False
+        l4 = run_ep(a4, table=table, quiet=True)
+        extras["ep_prefill"] = {k: l4[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup",
+                                                   "ms_per_step", "scaling", "parity", "load", "roofline", "e2e",
+                                                   "gpu_launches")}
+        extras["ep_prefill"]["note"] = ("config 4 at N=1 through the same exchange code (one rank); the N>1 "
+                                        "points are the torchrun lines of the same metric")
+        a2 = copy.copy(args)
+        a2.workload, a2.steps, a2.warmup, a2.exact, a2.no_cpu_baseline = "prefill", 20, 5, False, True
+        l2 = run_cuda_batched(a2, quiet=True)
+        extras["prefill"] = {k: l2.get(k) for k in ("metric", "value", "unit", "ms_per_step", "stage_ms_per_layer",
+                                                    "tensor", "roofline", "e2e")}
+        extras["prefill"]["config"] = l2["config"]["workload"]
+
     if rank == 0:
         step_bytes = expert_bytes_per_token(lays)
         line = {
@@ -356,6 +395,7 @@ def run_cuda(args):
             "clocks": clk,
             "cpu_baseline": cpu,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -646,19 +686,23 @@ def run_reference_model(args):
 ZIPF_S = 1.1
 
 
-def zipf_parts(seed):
-    """(u [H], s [E]) of the Zipf bias, from the seed (numpy, host)."""
+def zipf_parts(seed, perm_seed=None):
+    """(u [H], s [E]) of the Zipf bias (numpy, host): u from `seed`, the
+    expert popularity order from `perm_seed` (default: the same generator)."""
     rng = np.random.default_rng(seed)
     u = rng.standard_normal(H).astype(np.float64)
     u /= np.linalg.norm(u)
-    rank = rng.permutation(E)
+    rank = rng.permutation(E) if perm_seed is None else np.random.default_rng(perm_seed).permutation(E)
     s = -ZIPF_S * np.log(rank + 1.0)
     return u.astype(np.float32), s.astype(np.float32)
 
 
-def zipf_inputs(base_router, tokens, seed):
-    """Bias an [E,H] router and [T,H] token rows (numpy float32 in, out)."""
-    u, s = zipf_parts(seed)
+def zipf_inputs(base_router, tokens, seed, perm_seed=None):
+    """Bias an [E,H] router and [T,H] token rows (numpy float32 in, out).
+    Layers that share `seed` share the direction u the tokens carry, so the
+    skew holds in every layer; perm_seed gives each layer its own popular
+    experts."""
+    u, s = zipf_parts(seed, perm_seed)
     c = 0.5 * np.sqrt(H)
     C = c / np.sqrt(1.0 + c * c / H)
     router = (base_router + (s / C)[:, None] * u[None, :]).astype(np.float32)
@@ -688,7 +732,7 @@ def workload_desc(args, n_layers, tokens, world):
     return d[args.workload]
 
 
-def run_cuda_batched(args):
+def run_cuda_batched(args, quiet=False):
     import datetime
 
     import torch
@@ -719,7 +763,7 @@ def run_cuda_batched(args):
     for l in range(n_layers):
         r = rv.synth_normal(SEED + 1000 + l, 0, 0.02, E * H).view(E, H).cpu().numpy()
         if zipf:
-            r, _ = zipf_inputs(r, np.zeros((1, H), np.float32), SEED + 77 + l)
+            r, _ = zipf_inputs(r, np.zeros((1, H), np.float32), SEED + 77, perm_seed=SEED + 77 + l)
         routers_np.append(r)
     routers = [torch.from_numpy(r).cuda() for r in routers_np]
     norm = torch.ones(H, dtype=torch.float32, device="cuda")
@@ -880,10 +924,236 @@ def run_cuda_batched(args):
                               "frac": round(gu_flop / (gu_ms * 1e-3) / 1e12 / tpk, 4),
                               "peak_source": f"{tpk_kind} bf16_tflops (dense f16 runs at the same rate)",
                               "flops": "2 * pairs * (gate + up) * hidden, useful products only"}
-        print(json.dumps(line), flush=True)
+        if not quiet:
+            print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return line if rank == 0 else None
+
+
+# ============================= config 4 through the library's exchange
+EP_TOKENS = 4096
+EP_METRIC = "expert-parallel prefill tok/s (4096 tokens, 48 MoE layers)"
+
+
+def ep_launches_per_layer(tensor: bool) -> int:
+    # routing (k_prologue, k_router_logits, k_route), k_ep_dispatch,
+    # k_ep_receive, the expert stage (tensor: k_tc_tiles, k_tc_gather,
+    # k_tc_gemm, k_tc_quant, k_tc_gemm; exact: k_gate_up, k_down),
+    # k_ep_signal, k_ep_combine
+    return 3 + 2 + (5 if tensor else 2) + 2
+
+
+def run_ep(args, table=None, quiet=False):
+    """Config 4: 4096 tokens (8 x 512) with Zipf s=1.1 routing through all
+    48 MoE layers, the 128 experts spread over the N ranks by id mod N.
+    Each rank routes 4096/N home tokens; dispatch, expert outputs and the
+    per-layer flags go through GPU memory (rv_moe_ep_forward), and a step
+    (48 layers) is one captured CUDA graph.  Strong scaling: the total work
+    is fixed.  `table`: the full 48-layer table to reuse at N=1.  Returns the
+    JSON line (rank 0), printed unless quiet."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ramvamp_b200 as rv
+    from ramvamp_b200.ep import connect_group
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = local if world > 1 else 0
+    torch.cuda.set_device(dev)
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", dev))
+    n_layers = args.layers
+    home = EP_TOKENS // world
+    flags = rv.EXACT if args.exact else rv.TENSOR
+    if table is None or world > 1:
+        lays = [rv.qwen3_layer_layout(l, n_experts=E // world) for l in range(n_layers)]
+        table = rv.ExpertTable(lays, device=dev)
+        for l in range(n_layers):
+            table.fill_synthetic(l, SEED + l, 0.02, first_expert=rank, expert_step=world)
+    routers_np = []
+    for l in range(n_layers):
+        r = rv.synth_normal(SEED + 1000 + l, 0, 0.02, E * H).view(E, H).cpu().numpy()
+        r, _ = zipf_inputs(r, np.zeros((1, H), np.float32), SEED + 77, perm_seed=SEED + 77 + l)
+        routers_np.append(r)
+    routers = [torch.from_numpy(r).cuda() for r in routers_np]
+    n_batches = 2
+    xs = rv.synth_normal(SEED + 7 + rank, 0, 1.0, n_batches * home * H).view(n_batches, home, H).cpu().numpy()
+    xs = np.stack([zipf_inputs(routers_np[0], xs[i], SEED + 77, perm_seed=SEED + 77)[1] for i in range(n_batches)])
+    tokens = torch.from_numpy(np.ascontiguousarray(xs)).cuda()
+    norm = torch.ones(H, dtype=torch.float32, device="cuda")
+    eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=EP_TOKENS, device=dev)
+    ep = rv.ExpertParallel(eng, world, rank, home)
+    if world > 1:
+        connect_group(ep)
+    else:
+        ep.connect([ep.handle_bytes()])
+    resid = torch.empty(home, H, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def step_body():
+        for l in range(n_layers):
+            ep.forward(table, l, norm, routers[l], resid, flags=flags)
+
+    # Every rank runs the same exchange steps in the same order: eager once,
+    # capture (no steps run), replays.
+    with torch.cuda.stream(stream):
+        resid.copy_(tokens[0])
+        step_body()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_body()
+    torch.cuda.synchronize()
+    # Parity 1: the captured step equals the eager one.
+    with torch.cuda.stream(stream):
+        resid.copy_(tokens[1])
+        graph.replay()
+        g_out = resid.clone()
+        resid.copy_(tokens[1])
+        step_body()
+    stream.synchronize()
+    same_graph = bool(torch.equal(g_out.view(torch.int32), resid.view(torch.int32)))
+    # Parity 2: one layer through the exchange equals this rank's own
+    # single-GPU forward of its tokens (layer 0's full table on this GPU).
+    full0 = rv.ExpertTable([rv.qwen3_layer_layout(0)], device=dev)
+    full0.fill_synthetic(0, SEED, 0.02)
+    with torch.cuda.stream(stream):
+        resid.copy_(tokens[0])
+        ep.forward(table, 0, norm, routers[0], resid, flags=flags)
+        ep_l0 = resid.clone()
+        resid.copy_(tokens[0])
+        eng.forward(full0, 0, norm, routers[0], resid, flags=flags)
+    stream.synchronize()
+    same_1gpu = bool(torch.equal(ep_l0.view(torch.int32), resid.view(torch.int32)))
+    # Parity 3 (rank 0): 16 rows of that layer against the oracle's arm.
+    same_oracle = None
+    if rank == 0:
+        from oracle import oracle as orc
+
+        orc.build()
+        L0 = rv.qwen3_layer_layout(0)
+        blobs = rv.alias(full0.view(0, 0).blob, E * L0.stride).cpu().numpy()
+        OL = orc.make_layer(H, M, E, K, 1e-6, np.ones(H, np.float32), routers_np[0], blobs, L0.stride,
+                            L0.gate_off, L0.up_off, L0.down_off, L0.gate_format, L0.up_format, L0.down_format)
+        want, _, _ = orc.moe_prefill(OL, np.ascontiguousarray(xs[0][:16]), impl=0 if flags == rv.TENSOR else 2,
+                                     threads=os.cpu_count() or 1)
+        same_oracle = bool((ep_l0[:16].cpu().numpy().view(np.uint32) == want.view(np.uint32)).all())
+    full0.close()
+    ok = torch.tensor([int(same_graph and same_1gpu)], device="cuda")
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+
+    if world > 1:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(dev)
+    uuid = str(getattr(props, "uuid", ""))
+    clocks = ClockSampler(("GPU-" + uuid if uuid and not uuid.startswith("GPU-") else uuid) or str(dev))
+    clocks.start()
+
+    def run_steps(lo, hi):
+        with torch.cuda.stream(stream):
+            for i in range(lo, hi):
+                resid.copy_(tokens[i % n_batches])
+                graph.replay()
+
+    run_steps(0, args.warmup)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    run_steps(args.warmup, args.warmup + args.steps)
+    ev1.record(stream)
+    ev1.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    tok_s = EP_TOKENS * args.steps / (ms / 1e3)
+    # Load: the pairs each rank's experts ran in the last layer.
+    recv = [int(sum(ep.received()))]
+    if world > 1:
+        allr = [None] * world
+        dist.all_gather_object(allr, recv[0])
+        recv = allr
+    # e2e through the public call: pinned host rows in, 48 rv_moe_ep_forward
+    # calls (eager), the result back to the host, every step.
+    host_tok = torch.empty(n_batches, home, H, dtype=torch.float32).pin_memory()
+    host_tok.copy_(tokens.cpu())
+    hres = torch.empty(home, H, dtype=torch.float32).pin_memory()
+    n_e2e = max(2, min(args.steps, 5))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        with torch.cuda.stream(stream):
+            resid.copy_(host_tok[i % n_batches], non_blocking=True)
+            step_body()
+            hres.copy_(resid, non_blocking=True)
+        stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_tok_s = EP_TOKENS * n_e2e / e2e_s
+
+    line = None
+    if rank == 0:
+        tpk, tpk_kind = measured_tensor_peak()
+        flops = 2.0 * 3 * M * H * EP_TOKENS * K * n_layers  # useful products of gate, up and down
+        achieved = flops / (ms_per_step * 1e-3) / 1e12 / world  # per GPU
+        line = {
+            "metric": EP_METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8/int4 levels as exact f16 integers on tcgen05, f32 accumulate" if flags == rv.TENSOR
+            else "int8 (dp4a) + f32",
+            "data": "synthetic: seeded N(0,1) rows and N(0,0.02) router and expert weights quantized by the "
+                    "reference's Q4_K/Q6_K quantizers; router and rows biased to Zipf s=1.1 expert popularity",
+            "config": {"workload": f"config4 expert-parallel prefill: {EP_TOKENS} tokens (8 x 512) through "
+                                   f"{n_layers} MoE layers, Zipf s=1.1, 128 experts over {world} GPU(s) by id "
+                                   f"mod {world}", "layers": n_layers, "tokens_per_step": EP_TOKENS,
+                       "path": "tensor (bit-identical to the reference's scalar arm)" if flags == rv.TENSOR
+                       else "exact (bit-identical to the reference's AVX2 arm)",
+                       "parallelism": f"ep{world}", "exchange": "rv_moe_ep_forward: peer stores over NVLink + "
+                       "release/acquire flags, no host synchronization", "cuda_graph": True,
+                       "l2": "inputs larger than L2: each step streams every touched expert's weights (17.5 GB "
+                             "over all ranks)"},
+            "parity": {"graph_equals_eager": same_graph, "ep_equals_single_gpu_layer0": bool(ok.item()),
+                       "oracle_rank0_16_rows_layer0": same_oracle},
+            "load": {"pairs_per_rank_last_layer": recv,
+                     "max_over_mean": round(max(recv) / (sum(recv) / len(recv)), 3) if sum(recv) else None},
+            "roofline": {"kernel": "whole EP step (routing, exchange, tcgen05 expert GEMMs, combine)",
+                         "bound": "tensor", "achieved": round(achieved, 2), "peak": tpk, "unit": "TFLOP/s",
+                         "frac": round(achieved / tpk, 4), "peak_source": f"{tpk_kind} bf16_tflops",
+                         "flops_per_step": flops, "traffic": None},
+            "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": EP_TOKENS * H * 4,
+                    "d2h_bytes_per_step": EP_TOKENS * H * 4,
+                    "path": "per rank: pinned home rows in, 48 rv_moe_ep_forward calls, rows out"},
+            "gpu_launches": args.steps * n_layers * ep_launches_per_layer(flags == rv.TENSOR),
+            "clocks": clk,
+            "cpu_baseline": None,
+        }
+        if not quiet:
+            print(json.dumps(line), flush=True)
+    del graph
+    ep.close()
+    if world > 1:
+        dist.barrier()
+    return line
 
 
 def cpu_baseline_batched(args, rv, table, routers_np, x0, lays):
@@ -939,7 +1209,7 @@ def run_reference_batched(args):
     router = orc.synth_normal(SEED + 1000, 0, 0.02, E * H).reshape(E, H)
     x = orc.synth_normal(SEED + 7, 0, 1.0, 32 * H).reshape(32, H)
     if args.workload in ("batch", "ep"):
-        router, x = zipf_inputs(router, x, SEED + 77)
+        router, x = zipf_inputs(router, x, SEED + 77, perm_seed=SEED + 77)  # layer 0 of the CUDA arm
     OL = orc.make_layer(H, M, E, K, 1e-6, np.ones(H, np.float32), router, blobs, full.stride, full.gate_off,
                         full.up_off, full.down_off, full.gate_format, full.up_format, full.down_format)
     sample = 64 if args.workload == "batch" else 128
@@ -971,6 +1241,9 @@ def main():
     args = parse()
     if args.workload == "model":
         (run_reference_model if args.impl == "reference" else run_cuda_model)(args)
+        return
+    if args.workload == "ep" and args.impl != "reference":
+        run_ep(args)
         return
     if args.workload != "decode":
         (run_reference_batched if args.impl == "reference" else run_cuda_batched)(args)

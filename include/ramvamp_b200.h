@@ -62,7 +62,9 @@ typedef enum rv_status {
   RV_ERR_IO = 17,                          /* IoError::Io: a file could not be opened or read */
   RV_ERR_TOKEN_OUT_OF_RANGE = 18,          /* ModelError::TokenOutOfRange (a row id past the matrix) */
   RV_ERR_POSITION_MISMATCH = 19,           /* ForwardError::PositionMismatch (position != cached length) */
-  RV_ERR_CAPACITY_EXCEEDED = 20            /* KvError::CapacityExceeded (the layer's cache is full) */
+  RV_ERR_CAPACITY_EXCEEDED = 20,           /* KvError::CapacityExceeded (the layer's cache is full) */
+  RV_ERR_PEER = 21                         /* an expert-parallel peer's handle does not fit this group,
+                                              or its memory could not be mapped */
 } rv_status;
 
 /* Quantization formats (kernels/quants/mod.rs:57-70). */
@@ -406,6 +408,62 @@ RV_API int rv_moe_combine(rv_moe *m, float *residual, const float *topk_weights,
 RV_API int rv_ep_plan(rv_moe *m, const uint32_t *topk_ids, const uint8_t *acts, size_t n_tokens, uint32_t world,
                       int32_t *send_counts, uint32_t *pos_of, uint32_t *send_local, uint8_t *send_acts,
                       rv_stream stream);
+
+/* ---- expert parallelism over the GPUs of one node -----------------------
+ * No counterpart in the reference, which runs the MoE block on one host.
+ * The 128 experts of a layer are spread over `world` ranks (one process or
+ * thread per GPU) by expert id modulo world: rank r holds experts r, r+world,
+ * ... as its local experts 0, 1, ... (its rv_expert_table holds only those).
+ * Each rank routes its own tokens; the exchange runs through GPU memory:
+ * every rank owns an exchange window in its HBM that the others map (CUDA
+ * IPC across processes, peer access inside one), dispatch stores each
+ * pair's Q8_K row into the window of its expert's rank, the down projection
+ * there stores the expert output row straight back into the home rank's
+ * window over NVLink, and release/acquire flags at system scope, counted
+ * per layer, order the steps.  No host synchronization and no collective
+ * library call sits on the data path, so a layer's call can be captured
+ * into a CUDA graph.  Every pair's output comes from the same kernels on
+ * the same bytes as on one GPU and each home rank reduces in top-k order,
+ * so the result is bit-identical to rv_moe_forward for every world size
+ * (prefill.rs:2734-2778).
+ *
+ * Set-up (once per rank): rv_ep_create, then rv_ep_handle; the caller
+ * gathers the world handles (RV_EP_HANDLE_BYTES each, in rank order) by any
+ * out-of-band means (a TCP store, MPI, torch.distributed) and passes them
+ * all to rv_ep_connect on every rank.  Each rank must be on its own GPU.
+ * Every rank then calls rv_moe_ep_forward for the same layers in the same
+ * order (n_tokens may differ, 0 included).  Waits on peers are bounded
+ * (~1 s): a peer that does not arrive leaves RV_ERR_TIMEOUT in the device
+ * error word (rv_device_status) and the layer's result undefined; the group
+ * must then be destroyed and created again on every rank. */
+#define RV_EP_HANDLE_BYTES 256
+typedef struct rv_ep rv_ep;
+/* `m`'s geometry and device; max_tokens = home tokens per call on this rank.
+ * The engine runs the experts on up to world * max_tokens received rows, so
+ * it must have been created with max_tokens >= world * max_tokens.  The
+ * window holds world * max_tokens * top_k received rows plus max_tokens *
+ * top_k output rows (77 MB + 34 MB for Qwen3 at 512 tokens per rank). */
+RV_API int rv_ep_create(rv_moe *m, uint32_t world, uint32_t rank, size_t max_tokens, rv_ep **out);
+RV_API void rv_ep_destroy(rv_ep *ep);
+/* Writes this rank's handle (RV_EP_HANDLE_BYTES bytes, host) to out. */
+RV_API int rv_ep_handle(const rv_ep *ep, void *out, size_t len);
+/* handles: world * RV_EP_HANDLE_BYTES bytes (host), rank order.
+ * RV_ERR_PEER if a handle is not one of this group's (wrong world, rank,
+ * geometry or capacity, two ranks on one GPU) or cannot be mapped; nothing
+ * is mapped then. */
+RV_API int rv_ep_connect(rv_ep *ep, const void *handles, size_t len);
+/* The MoE block of one layer for this rank's n_tokens home rows, in place on
+ * `residual` (device), as rv_moe_forward: ffn_norm [hidden], router
+ * [n_experts][hidden] (all experts, device), table = this rank's experts;
+ * topk_ids/topk_weights optional [n_tokens][top_k] outputs.  flags:
+ * RV_MOE_EXACT or RV_MOE_TENSOR.  Enqueues only (no host synchronization).
+ * RV_ERR_PROTOCOL before rv_ep_connect. */
+RV_API int rv_moe_ep_forward(rv_ep *ep, const rv_expert_table *table, uint32_t layer, const float *ffn_norm,
+                             const float *router, float *residual, size_t n_tokens, uint32_t *topk_ids,
+                             float *topk_weights, uint32_t flags, rv_stream stream);
+/* received[r] = pairs rank r sent this rank in the most recent layer (host,
+ * len >= world); synchronizes the device. */
+RV_API int rv_ep_counts(const rv_ep *ep, uint32_t *received, size_t len);
 
 /* Device addresses of the intermediates the most recent forward left in the
  * engine's scratch, for parity tests.  Layout per field below. */

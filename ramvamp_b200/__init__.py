@@ -42,7 +42,8 @@ __all__ = [
     "LayerLayout", "qwen3_layer_layout", "QWEN3_Q6K_DOWN_LAYERS", "synth_normal",
     "quantize_weights", "EXACT", "TENSOR", "lib", "Q8_0_BYTES", "quantize_row_q8_0", "gemv_q8_0",
     "gemv_q8_0_rows", "gemv_q8_0_batched", "dequantize_rows", "embed", "device_status",
-    "rope_neox_heads", "attention", "AttnEngine", "attn_weights", "rmsnorm_quantize",
+    "rope_neox_heads", "attention", "AttnEngine", "attn_weights", "rmsnorm_quantize", "ExpertParallel",
+    "EP_HANDLE_BYTES", "wait_probe",
 ]
 
 Q8K_BYTES = 292
@@ -571,6 +572,62 @@ class MoeEngine:
         t = _lib.MoeTaps()
         _check(lib().rv_moe_get_taps(self.handle, ctypes.byref(t)))
         return t
+
+
+EP_HANDLE_BYTES = 256  # RV_EP_HANDLE_BYTES
+
+
+class ExpertParallel:
+    """One rank of an expert-parallel group (rv_ep_*): experts spread over
+    `world` GPUs by id modulo world, tokens dispatched and expert outputs
+    returned through GPU memory with no host synchronization.  Usage, on
+    every rank: ``ep = ExpertParallel(engine, world, rank, max_tokens)``;
+    gather every rank's ``ep.handle()`` in rank order (any out-of-band
+    channel; ``ramvamp_b200.ep.connect_group`` uses torch.distributed);
+    ``ep.connect(handles)``; then ``ep.forward(...)`` per layer on every
+    rank.  The engine must hold world * max_tokens rows."""
+
+    def __init__(self, engine: "MoeEngine", world: int, rank: int, max_tokens: int):
+        h = ctypes.c_void_p()
+        _check(lib().rv_ep_create(engine.handle, world, rank, max_tokens, ctypes.byref(h)))
+        self.handle, self.engine = h, engine
+        self.world, self.rank, self.max_tokens = world, rank, max_tokens
+
+    def handle_bytes(self) -> bytes:
+        buf = ctypes.create_string_buffer(EP_HANDLE_BYTES)
+        _check(lib().rv_ep_handle(self.handle, buf, EP_HANDLE_BYTES))
+        return buf.raw
+
+    def connect(self, handles: Sequence[bytes]) -> None:
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        _check(lib().rv_ep_connect(self.handle, buf, len(blob)))
+
+    def forward(self, table: ExpertTable, layer: int, ffn_norm: torch.Tensor, router: torch.Tensor,
+                residual: torch.Tensor, topk_ids: Optional[torch.Tensor] = None,
+                topk_weights: Optional[torch.Tensor] = None, flags: int = EXACT) -> torch.Tensor:
+        """In place on this rank's home rows: residual += MoE(residual)."""
+        T = residual.numel() // self.engine.cfg.hidden
+        _check(lib().rv_moe_ep_forward(self.handle, table.handle, layer, _p(ffn_norm), _p(router),
+                                       _p(residual), T, _p(topk_ids), _p(topk_weights), flags, _stream()))
+        return residual
+
+    def received(self) -> list:
+        """Pairs each rank sent this rank in the most recent layer."""
+        arr = (ctypes.c_uint32 * self.world)()
+        _check(lib().rv_ep_counts(self.handle, arr, self.world))
+        return list(arr)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().rv_ep_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class AttnEngine:

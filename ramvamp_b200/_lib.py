@@ -29,6 +29,7 @@ STATUS_NAMES = {
     18: "TokenOutOfRange",
     19: "PositionMismatch",
     20: "CapacityExceeded",
+    21: "Peer",
 }
 
 
@@ -149,6 +150,12 @@ SIGNATURES = {
     "rv_moe_experts": (I32, [P, P, U32, P, P, SZ, P, U32, P]),
     "rv_moe_combine": (I32, [P, P, P, P, P, SZ, P]),
     "rv_ep_plan": (I32, [P, P, P, SZ, U32, P, P, P, P, P]),
+    "rv_ep_create": (I32, [P, U32, U32, SZ, ctypes.POINTER(P)]),
+    "rv_ep_destroy": (None, [P]),
+    "rv_ep_handle": (I32, [P, P, SZ]),
+    "rv_ep_connect": (I32, [P, P, SZ]),
+    "rv_moe_ep_forward": (I32, [P, P, U32, P, P, P, SZ, P, P, U32, P]),
+    "rv_ep_counts": (I32, [P, P, SZ]),
     "rv_moe_profile_enable": (I32, [P, SZ]),
     "rv_moe_profile_rewind": (I32, [P]),
     "rv_moe_profile_read": (I32, [P, P, SZ, ctypes.POINTER(SZ)]),

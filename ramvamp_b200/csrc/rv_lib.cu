@@ -8,6 +8,7 @@
 #include <cstdlib>
 #include <mutex>
 #include <new>
+#include <unistd.h>
 #include <vector>
 
 #include <cuda.h>
@@ -64,6 +65,7 @@ extern "C" const char *rv_status_name(int s) {
     case RV_ERR_TOKEN_OUT_OF_RANGE: return "TokenOutOfRange";
     case RV_ERR_POSITION_MISMATCH: return "PositionMismatch";
     case RV_ERR_CAPACITY_EXCEEDED: return "CapacityExceeded";
+    case RV_ERR_PEER: return "Peer";
   }
   return "Unknown";
 }
@@ -218,6 +220,7 @@ extern "C" int rv_debug_wait_probe(int device, uint32_t what, uint64_t cycles, r
     if (e == cudaSuccess) e = cudaMemsetAsync(flag, 0, 4, s);
   }
   if (e == cudaSuccess) {
+    cudaGetLastError();  // clear any earlier error so the check below sees this launch's
     k_wait_probe<<<1, 32, 0, s>>>(what, (long long)cycles, flag);
     e = cudaGetLastError();
   }
@@ -682,6 +685,7 @@ extern "C" void rv_expert_table_destroy(rv_expert_table *t) {
   cudaSetDevice(t->device);
   for (uint8_t *p : t->base) cudaFree(p);
   cudaSetDevice(prev);
+  cudaGetLastError();  // a void call: leave no error behind for the caller's next check
   delete t;
 }
 
@@ -1047,6 +1051,7 @@ extern "C" void rv_moe_destroy(rv_moe *m) {
   prof_release(m);
   cudaFree(m->arena);
   cudaSetDevice(prev);
+  cudaGetLastError();  // a void call: leave no error behind for the caller's next check
   delete m;
 }
 
@@ -1292,7 +1297,9 @@ static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
     if (rc) return rc;
     const unsigned P = (unsigned)(T * d.K);
     k_tc_tiles<<<1, 256, 0, s>>>(d, B);
-    k_tc_gather<<<P, 32 * d.hb, 0, s>>>(d, B);
+    // Position-striding grids: P is the capacity, the index holds how many.
+    const unsigned pg = std::min(P, 4096u);
+    k_tc_gather<<<pg, 32 * d.hb, 0, s>>>(d, B);
     RV_LAUNCH_CHECK();
     if ((rc = prof_record(ev, 1, evflags, s))) return rc;
     CUtensorMap gmap;
@@ -1300,7 +1307,7 @@ static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
     rc = L.gate_format == RV_Q4_K ? launch_tc_gemm<RV_Q4_K, false>(d, B, W, gmap, s)
                                   : launch_tc_gemm<RV_Q5_K, false>(d, B, W, gmap, s);
     if (rc) return rc;
-    k_tc_quant<<<P, 32 * d.mb, 0, s>>>(d, B);
+    k_tc_quant<<<pg, 32 * d.mb, 0, s>>>(d, B);
     RV_LAUNCH_CHECK();
     if ((rc = prof_record(ev, 2, evflags, s))) return rc;
     switch (L.down_format) {
@@ -1519,6 +1526,294 @@ extern "C" int rv_ep_plan(rv_moe *m, const uint32_t *topk_ids, const uint8_t *ac
   return RV_OK;
 }
 
+// ============================================== expert-parallel exchange
+// One rv_ep per rank: its exchange window (see rv_ep.cuh), the peers'
+// windows as this GPU addresses them, and the state of the step protocol.
+#define RV_EP_MAGIC "RVEPWIN1"
+struct EpHandle {  // what rv_ep_handle exports (RV_EP_HANDLE_BYTES)
+  char magic[8];
+  uint32_t world, rank, cap, act_stride, hidden, n_experts;
+  int64_t pid;
+  uint64_t win_bytes, win_ptr;
+  char bus_id[32];
+  cudaIpcMemHandle_t ipc;
+};
+static_assert(sizeof(EpHandle) <= RV_EP_HANDLE_BYTES, "handle layout");
+
+struct rv_ep {
+  rv_moe *m = nullptr;
+  int device = 0;              // the engine's device (kept here: destroy does not touch the engine)
+  uint32_t world = 0, rank = 0;
+  size_t max_tokens = 0;
+  uint8_t *window = nullptr;   // this rank's window (cudaMalloc, exported)
+  EpState *state = nullptr;    // device
+  uint8_t **d_win = nullptr;   // device [world]: every rank's window
+  float **d_out = nullptr;     // device [world]: every rank's output rows (window + o_out)
+  uint32_t *slot_ids = nullptr;  // device [world*cap]: the received slots' local experts
+  std::vector<void *> opened;  // peer windows mapped through IPC (closed on destroy)
+  bool connected = false;
+  char bus_id[32] = {0};
+  EpArgs A{};
+};
+
+extern "C" void rv_ep_destroy(rv_ep *ep) {
+  if (!ep) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(ep->device);
+  cudaStreamSynchronize(nullptr);
+  for (void *p : ep->opened) cudaIpcCloseMemHandle(p);
+  cudaFree(ep->window);
+  cudaFree(ep->state);
+  cudaFree(ep->d_win);
+  cudaFree(ep->d_out);
+  cudaFree(ep->slot_ids);
+  if (prev >= 0) cudaSetDevice(prev);
+  cudaGetLastError();  // a void call: leave no error behind for the caller's next check
+  delete ep;
+}
+
+extern "C" int rv_ep_create(rv_moe *m, uint32_t world, uint32_t rank, size_t max_tokens, rv_ep **out) {
+  if (!m || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_create: null pointer");
+  *out = nullptr;
+  if (world == 0 || world > 64) RV_FAIL(RV_ERR_UNIMPLEMENTED, "ep_create: world size %u (1..64)", world);
+  if (rank >= world) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_create: rank %u of %u", rank, world);
+  if ((uint32_t)m->d.E % world)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "ep_create: %d experts do not split evenly over %u ranks", m->d.E, world);
+  if (max_tokens == 0 || max_tokens > m->max_tokens)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "ep_create: %zu tokens per rank vs engine capacity %zu", max_tokens,
+            m->max_tokens);
+  if ((size_t)world * max_tokens > m->max_tokens)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH,
+            "ep_create: the engine runs the experts on up to world x max_tokens = %zu rows; it holds %zu",
+            (size_t)world * max_tokens, m->max_tokens);
+  rv_ep *ep = new (std::nothrow) rv_ep();
+  if (!ep) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "out of host memory");
+  ep->m = m;
+  ep->device = m->device;
+  ep->world = world;
+  ep->rank = rank;
+  ep->max_tokens = max_tokens;
+  EpArgs &A = ep->A;
+  A.world = world;
+  A.rank = rank;
+  A.cap = (uint32_t)(max_tokens * (size_t)m->d.K);
+  A.act_stride = (uint32_t)m->d.act_stride;
+  A.H = m->d.H;
+  ep_layout(A);
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(m->device);
+  cudaError_t e = cudaMalloc((void **)&ep->window, A.bytes);
+  if (e == cudaSuccess) e = cudaMemset(ep->window, 0, A.bytes);
+  if (e == cudaSuccess) e = cudaMalloc((void **)&ep->state, sizeof(EpState));
+  if (e == cudaSuccess) e = cudaMemset(ep->state, 0, sizeof(EpState));
+  if (e == cudaSuccess) e = cudaMalloc((void **)&ep->d_win, world * sizeof(uint8_t *));
+  if (e == cudaSuccess) e = cudaMalloc((void **)&ep->d_out, world * sizeof(float *));
+  if (e == cudaSuccess) e = cudaMalloc((void **)&ep->slot_ids, (size_t)world * A.cap * 4);
+  if (e == cudaSuccess) e = cudaDeviceGetPCIBusId(ep->bus_id, (int)sizeof ep->bus_id, m->device);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    rv_ep_destroy(ep);
+    RV_FAIL(RV_ERR_CUDA, "ep_create: %zu-byte exchange window: %s", A.bytes, cudaGetErrorString(e));
+  }
+  A.mine = ep->window;
+  A.st = ep->state;
+  A.win = ep->d_win;
+  *out = ep;
+  return RV_OK;
+}
+
+extern "C" int rv_ep_handle(const rv_ep *ep, void *out, size_t len) {
+  if (!ep || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_handle: null pointer");
+  if (len < RV_EP_HANDLE_BYTES) RV_FAIL(RV_ERR_LENGTH_MISMATCH, "ep_handle: %zu bytes (needs %d)", len,
+                                        RV_EP_HANDLE_BYTES);
+  EpHandle h;
+  memset(&h, 0, sizeof h);
+  memcpy(h.magic, RV_EP_MAGIC, 8);
+  h.world = ep->world;
+  h.rank = ep->rank;
+  h.cap = ep->A.cap;
+  h.act_stride = ep->A.act_stride;
+  h.hidden = (uint32_t)ep->m->d.H;
+  h.n_experts = (uint32_t)ep->m->d.E;
+  h.pid = (int64_t)getpid();
+  h.win_bytes = ep->A.bytes;
+  h.win_ptr = (uint64_t)(uintptr_t)ep->window;
+  memcpy(h.bus_id, ep->bus_id, sizeof h.bus_id);
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(ep->m->device));
+  const cudaError_t e = cudaIpcGetMemHandle(&h.ipc, ep->window);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) RV_FAIL(RV_ERR_CUDA, "ep_handle: cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  memset(out, 0, RV_EP_HANDLE_BYTES);
+  memcpy(out, &h, sizeof h);
+  return RV_OK;
+}
+
+extern "C" int rv_ep_connect(rv_ep *ep, const void *handles, size_t len) {
+  if (!ep || !handles) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_connect: null pointer");
+  if (ep->connected) RV_FAIL(RV_ERR_PROTOCOL, "ep_connect: already connected");
+  if (len != (size_t)ep->world * RV_EP_HANDLE_BYTES)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "ep_connect: %zu bytes for %u handles of %d", len, ep->world,
+            RV_EP_HANDLE_BYTES);
+  // Check every handle before mapping anything.
+  std::vector<EpHandle> hs(ep->world);
+  for (uint32_t r = 0; r < ep->world; r++) {
+    EpHandle &h = hs[r];
+    memcpy(&h, (const uint8_t *)handles + (size_t)r * RV_EP_HANDLE_BYTES, sizeof h);
+    if (memcmp(h.magic, RV_EP_MAGIC, 8) != 0) RV_FAIL(RV_ERR_PEER, "ep_connect: handle %u is not an exchange handle", r);
+    if (h.world != ep->world || h.rank != r)
+      RV_FAIL(RV_ERR_PEER, "ep_connect: handle %u is rank %u of %u; this group is %u ranks", r, h.rank, h.world,
+              ep->world);
+    if (h.cap != ep->A.cap || h.act_stride != ep->A.act_stride || h.hidden != (uint32_t)ep->m->d.H ||
+        h.n_experts != (uint32_t)ep->m->d.E || h.win_bytes != ep->A.bytes)
+      RV_FAIL(RV_ERR_PEER, "ep_connect: rank %u was created with another geometry or capacity", r);
+    h.bus_id[sizeof h.bus_id - 1] = 0;
+    if (r != ep->rank && strcmp(h.bus_id, ep->bus_id) == 0)
+      RV_FAIL(RV_ERR_PEER, "ep_connect: ranks %u and %u are on the same GPU (%s); each rank needs its own", r,
+              ep->rank, ep->bus_id);
+  }
+  if (hs[ep->rank].win_ptr != (uint64_t)(uintptr_t)ep->window || hs[ep->rank].pid != (int64_t)getpid())
+    RV_FAIL(RV_ERR_PEER, "ep_connect: handle %u is not this rank's own", ep->rank);
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(ep->m->device));
+  std::vector<uint8_t *> win(ep->world, nullptr);
+  int status = RV_OK;
+  for (uint32_t r = 0; r < ep->world && status == RV_OK; r++) {
+    const EpHandle &h = hs[r];
+    if (r == ep->rank) {
+      win[r] = ep->window;
+    } else if (h.pid == (int64_t)getpid()) {
+      // Another device of this process: direct peer access.
+      int pdev = -1, can = 0;
+      cudaError_t e = cudaDeviceGetByPCIBusId(&pdev, h.bus_id);
+      if (e == cudaSuccess) e = cudaDeviceCanAccessPeer(&can, ep->m->device, pdev);
+      if (e == cudaSuccess && !can) {
+        rv_set_error(RV_ERR_PEER, "ep_connect: device %d cannot access rank %u's device %d", ep->m->device, r, pdev);
+        status = RV_ERR_PEER;
+        break;
+      }
+      if (e == cudaSuccess) {
+        e = cudaDeviceEnablePeerAccess(pdev, 0);
+        if (e == cudaErrorPeerAccessAlreadyEnabled) {
+          cudaGetLastError();
+          e = cudaSuccess;
+        }
+      }
+      if (e != cudaSuccess) {
+        rv_set_error(RV_ERR_PEER, "ep_connect: peer access to rank %u: %s", r, cudaGetErrorString(e));
+        status = RV_ERR_PEER;
+        break;
+      }
+      win[r] = (uint8_t *)(uintptr_t)h.win_ptr;
+    } else {
+      void *p = nullptr;
+      const cudaError_t e = cudaIpcOpenMemHandle(&p, h.ipc, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        rv_set_error(RV_ERR_PEER, "ep_connect: mapping rank %u's window: %s", r, cudaGetErrorString(e));
+        status = RV_ERR_PEER;
+        break;
+      }
+      ep->opened.push_back(p);
+      win[r] = (uint8_t *)p;
+    }
+  }
+  if (status == RV_OK) {
+    std::vector<float *> outs(ep->world);
+    for (uint32_t r = 0; r < ep->world; r++) outs[r] = (float *)(win[r] + ep->A.o_out);
+    cudaError_t e = cudaMemcpy(ep->d_win, win.data(), ep->world * sizeof(uint8_t *), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(ep->d_out, outs.data(), ep->world * sizeof(float *), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      rv_set_error(RV_ERR_CUDA, "ep_connect: %s", cudaGetErrorString(e));
+      status = RV_ERR_CUDA;
+    }
+  }
+  if (status != RV_OK) {
+    for (void *p : ep->opened) cudaIpcCloseMemHandle(p);
+    ep->opened.clear();
+  } else {
+    ep->connected = true;
+  }
+  cudaSetDevice(prev);
+  return status;
+}
+
+extern "C" int rv_moe_ep_forward(rv_ep *ep, const rv_expert_table *table, uint32_t layer, const float *ffn_norm,
+                                 const float *router, float *residual, size_t n_tokens, uint32_t *topk_ids,
+                                 float *topk_weights, uint32_t flags, rv_stream stream) {
+  if (!ep || !table) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_ep_forward: null exchange or table");
+  if (!ep->connected) RV_FAIL(RV_ERR_PROTOCOL, "moe_ep_forward: rv_ep_connect has not completed");
+  rv_moe *m = ep->m;
+  int rc = check_engine_layer(m, table, layer, true);
+  if (rc) return rc;
+  const rv_layer_layout &L = table->layouts[layer];
+  if (L.n_experts * ep->world != (uint32_t)m->d.E)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_ep_forward: layer %u holds %u experts; rank %u of %u needs %d", layer,
+            L.n_experts, ep->rank, ep->world, m->d.E / (int)ep->world);
+  if (flags & ~RV_MOE_TENSOR) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+  if (n_tokens > ep->max_tokens)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "moe_ep_forward: %zu tokens vs capacity %zu", n_tokens, ep->max_tokens);
+  if (n_tokens && (!ffn_norm || !router || !residual)) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_ep_forward: null pointer");
+  if ((uintptr_t)router & 15) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_ep_forward: router must be 16-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  const MoeDims &d = m->d;
+  const int T = (int)n_tokens;
+  MoeBufs B = m->B;
+  B.ffn_norm = ffn_norm;
+  B.router = router;
+  B.residual = residual;
+  B.T = T;
+  // 1. route the home tokens (forward.rs:2655-2705, prefill.rs:2165-2204)
+  if (T > 0 && (rc = route_stage(d, B, T, s))) return rc;
+  // 2. dispatch: rows and metadata into the experts' ranks, then the flags
+  const int P = T * d.K;
+  const unsigned dgrid = (unsigned)std::max(1, (P + 255) / 256);
+  k_ep_dispatch<<<dgrid, 256, 0, s>>>(ep->A, B.ids, B.acts, P, d.K, d.E, B.counts);
+  RV_LAUNCH_CHECK();
+  if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, (size_t)P * 4, cudaMemcpyDeviceToDevice, s));
+  if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, (size_t)P * 4, cudaMemcpyDeviceToDevice, s));
+  // 3. receive: wait for every source, lay out this rank's dispatch list
+  MoeDims dx = d;  // the expert stage: one slot per received row, local experts
+  dx.K = 1;
+  dx.E = (int)L.n_experts;
+  MoeBufs X = m->B;
+  X.T = (int)(ep->world * ep->A.cap);
+  X.ms = X.T < RV_MOE_MT ? X.T : RV_MOE_MT;
+  X.ids = ep->slot_ids;
+  X.acts = ep->window + ep->A.o_acts;
+  X.ep_out = ep->d_out;
+  X.ep_home = (const uint32_t *)(ep->window + ep->A.o_home);
+  X.ep_cap = ep->A.cap;
+  k_ep_receive<<<1, 1024, 0, s>>>(ep->A, dx, X);
+  RV_LAUNCH_CHECK();
+  // 4. the experts; the down projection stores each row into its home rank
+  bool combined = false;
+  if ((rc = expert_stage(dx, X, layer_weights(table, layer), L, layer, X.T, flags, false, 0, nullptr, 0, s,
+                         &combined)))
+    return rc;
+  // 5. tell every rank its rows are in, 6. combine once every rank has
+  k_ep_signal<<<1, 64, 0, s>>>(ep->A);
+  k_ep_combine<<<dim3((unsigned)std::max(T, 1), (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(ep->A, d, residual,
+                                                                                            B.w, T);
+  RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_ep_counts(const rv_ep *ep, uint32_t *received, size_t len) {
+  if (!ep || !received) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_counts: null pointer");
+  if (len < ep->world) RV_FAIL(RV_ERR_LENGTH_MISMATCH, "ep_counts: %zu entries for %u ranks", len, ep->world);
+  int prev = -1;
+  RV_CUDA(cudaGetDevice(&prev));
+  RV_CUDA(cudaSetDevice(ep->m->device));
+  const cudaError_t e = cudaMemcpy(received, ep->window + ep->A.o_cnt, ep->world * 4, cudaMemcpyDeviceToHost);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) RV_FAIL(RV_ERR_CUDA, "ep_counts: %s", cudaGetErrorString(e));
+  return RV_OK;
+}
+
 extern "C" int rv_moe_forward_host(rv_moe *m, const rv_expert_table *table, uint32_t layer,
                                    const float *ffn_norm, const float *router, float *residual_host,
                                    size_t n_tokens, uint32_t *topk_ids_host, float *topk_weights_host,
@@ -1608,6 +1903,7 @@ extern "C" void rv_attn_destroy(rv_attn *a) {
   cudaFree(a->v);
   cudaFree(a->attn_out);
   if (prev >= 0) cudaSetDevice(prev);
+  cudaGetLastError();  // a void call: leave no error behind for the caller's next check
   delete a;
 }
 

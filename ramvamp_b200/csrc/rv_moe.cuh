@@ -68,7 +68,20 @@ struct MoeBufs {
   int *n_tc;               // [1]
   uint32_t *tc_pstart;     // [E] padded first row of each expert
   int max_tc;
+  // Expert-parallel output (null otherwise): the down projection of
+  // dispatch slot p goes to row ep_home[p] of the output buffer of the rank
+  // that sent it, ep_out[p / ep_cap] (that rank's memory, mapped here).
+  float *const *ep_out;
+  const uint32_t *ep_home;
+  uint32_t ep_cap;
 };
+
+// The row the down projection of dispatch slot `pair` is stored to: the
+// engine's staged rows, or (expert parallel) the home rank's output row.
+RV_DEVFN float *down_out_row(const MoeBufs &B, uint32_t pair, int H) {
+  if (B.ep_out) return B.ep_out[pair / B.ep_cap] + (size_t)B.ep_home[pair] * H;
+  return B.staged + (size_t)pair * H;
+}
 
 struct MoeWeights {
   const uint8_t *base;     // layer blob 0
@@ -377,8 +390,9 @@ __global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
 // CTA from per-expert counts in shared memory: warp 0 scans the counts and
 // the unit counts, every thread writes units, then the (token, slot) pairs
 // are placed by expert.  s_cnt/s_cur: [256] ints, s_st/s_us: [257].
+// sparse: dispatch slots whose expert id is ~0 are empty and skipped.
 RV_DEVFN void build_index_cta(const MoeDims &d, const MoeBufs &B, int *s_cnt, uint32_t *s_st,
-                              uint32_t *s_cur, int *s_us) {
+                              uint32_t *s_cur, int *s_us, bool sparse = false) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pairs = B.T * d.K;
   if (warp == 0) {
@@ -417,7 +431,7 @@ RV_DEVFN void build_index_cta(const MoeDims &d, const MoeBufs &B, int *s_cnt, ui
     if (lane == 0) {
       s_st[d.E] = (uint32_t)tc;
       s_us[d.E] = tu;
-      if (tc != pairs || tu > B.max_units) rv_dev_fail(RV_ERR_LENGTH_MISMATCH);
+      if ((sparse ? tc > pairs : tc != pairs) || tu > B.max_units) rv_dev_fail(RV_ERR_LENGTH_MISMATCH);
       *B.n_units = min(tu, B.max_units);
     }
   }
@@ -433,7 +447,7 @@ RV_DEVFN void build_index_cta(const MoeDims &d, const MoeBufs &B, int *s_cnt, ui
   for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
     const uint32_t e = B.ids[p];
     if (e >= (uint32_t)d.E) {
-      rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
+      if (!(sparse && e == ~0u)) rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
       continue;
     }
     const uint32_t pos = atomicAdd(&s_cur[e], 1u);
@@ -1372,7 +1386,7 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
             const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.amoe_stride,
                                                           asum + (m0 + m) * d.mb * 64, g);
             const uint32_t pair = pair_of(c0 + m0 + m);
-            if (g == G - 1 && live && pair != ~0u) B.staged[(size_t)pair * d.H + row0 + rsub] = res;
+            if (g == G - 1 && live && pair != ~0u) down_out_row(B, pair, d.H)[row0 + rsub] = res;
           }
         } else {
           float res[MT];
@@ -1382,7 +1396,7 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
           for (int m = 0; m < MT; m++)
             if (m < mm && live) {
               const uint32_t pair = pair_of(c0 + m0 + m);
-              if (pair != ~0u) B.staged[(size_t)pair * d.H + row0 + rsub] = res[m];
+              if (pair != ~0u) down_out_row(B, pair, d.H)[row0 + rsub] = res[m];
             }
         }
       }
@@ -1420,6 +1434,7 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
       }
     }
   }
+  if (B.ep_out) __threadfence_system();  // rows stored into other ranks' memory
   if constexpr (SPEC) {
     if (blockIdx.x == 0 && blockIdx.y == 0) {
       // After the wait above (every CTA has a unit): the exact routing is

@@ -293,24 +293,25 @@ RV_DEVFN void tc_q8k_operands(const uint8_t *blk, int b, int nb, int G, int lane
   if (lane == 0) dsc[(size_t)pp * nb + b] = *(const float *)blk;
 }
 
-// Gate/up operand B: the Q8_K row of each position's token.  grid = T*K
-// CTAs of hb warps.
+// Gate/up operand B: the Q8_K row of each position's token.  CTAs of hb
+// warps stride over the index's positions.
 __global__ void k_tc_gather(MoeDims d, MoeBufs B) {
-  const uint32_t pos = blockIdx.x;
+  const uint32_t total = B.index_start[d.E];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t tok = B.index[pos] / (uint32_t)d.K;
-  const uint32_t pp = tc_padded(d, B, pos);
-  for (int b = warp; b < d.hb; b += blockDim.x >> 5)
-    tc_q8k_operands(B.acts + (size_t)tok * d.act_stride + (size_t)b * 292, b, d.hb, B.tc_groups, lane, B.xq, B.xm,
-                    B.xd, pp);
+  for (uint32_t pos = blockIdx.x; pos < total; pos += gridDim.x) {
+    const uint32_t tok = B.index[pos] / (uint32_t)d.K;
+    const uint32_t pp = tc_padded(d, B, pos);
+    for (int b = warp; b < d.hb; b += blockDim.x >> 5)
+      tc_q8k_operands(B.acts + (size_t)tok * d.act_stride + (size_t)b * 292, b, d.hb, B.tc_groups, lane, B.xq,
+                      B.xm, B.xd, pp);
+  }
 }
 
 // SwiGLU of each position's gate and up rows (the exact path's
 // swiglu_ref), the reference's Q8_K of the result (acts_moe, bit-identical
-// to the exact path) and the down operand B.  grid = T*K CTAs of mb warps.
-__global__ void k_tc_quant(MoeDims d, MoeBufs B) {
-  const uint32_t pos = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// to the exact path) and the down operand B.  CTAs of mb warps stride over
+// the index's positions.
+RV_DEVFN void tc_quant_pos(const MoeDims &d, const MoeBufs &B, uint32_t pos, int warp, int lane) {
   const uint32_t pp = tc_padded(d, B, pos);
   const float *g = B.gu + (size_t)pos * 2 * d.M, *u = g + d.M;
   for (int b = warp; b < d.mb; b += blockDim.x >> 5) {
@@ -326,6 +327,11 @@ __global__ void k_tc_quant(MoeDims d, MoeBufs B) {
     __syncwarp();
     tc_q8k_operands(blk, b, d.mb, B.tc_groups, lane, B.hq, B.hm, B.hdsc, pp);
   }
+}
+__global__ void k_tc_quant(MoeDims d, MoeBufs B) {
+  const uint32_t total = B.index_start[d.E];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (uint32_t pos = blockIdx.x; pos < total; pos += gridDim.x) tc_quant_pos(d, B, pos, warp, lane);
 }
 
 // ----------------------------------------------------- the GEMM kernel
@@ -732,10 +738,11 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
         for (int i = 0; i < 8; i++) {
           const int col = 8 * (half + 2 * c) + i;
           if (col < n) {
-            if constexpr (DOWN) B.staged[(size_t)s_pair[col] * d.H + row0 + er] = acc[c][i];
+            if constexpr (DOWN) down_out_row(B, s_pair[col], d.H)[row0 + er] = acc[c][i];
             else B.gu[(size_t)(p0 + col) * 2 * d.M + (size_t)mat * d.M + row0 + er] = acc[c][i];
           }
         }
+      if (DOWN && B.ep_out) __threadfence_system();  // rows stored into other ranks' memory
     }
     if (!ok) *s_fail = 1;
   }

@@ -1,4 +1,14 @@
-"""Expert-parallel MoE layer over a torch.distributed process group.
+"""Expert parallelism: joining a group, and a host-collective harness.
+
+The product path is ``ramvamp_b200.ExpertParallel`` (rv_ep_* in the C ABI):
+dispatch and combine run through GPU memory inside the library, with no host
+synchronization.  ``connect_group`` below is its set-up over a
+torch.distributed group (the handles are small host byte strings).
+
+``ExpertParallelMoe`` is the same layer with the exchange written as
+torch.distributed all-to-alls.  It is kept as the harness of the CPU tests,
+which check the exchange logic on gloo ranks with the oracle as the local
+compute.
 
 The 128 experts of a layer are spread over the G ranks of a group by expert
 id modulo G: rank r holds experts r, r+G, r+2G, ... as its local experts
@@ -31,6 +41,15 @@ import torch
 import torch.distributed as dist
 
 from . import EXACT, ExpertTable, MoeEngine
+
+
+def connect_group(ep, group=None) -> None:
+    """rv_ep_connect for every rank of `group` (None: the default group):
+    all-gathers each rank's handle and connects.  Collective: every rank
+    calls it, after creating its ExpertParallel."""
+    handles = [None] * dist.get_world_size(group)
+    dist.all_gather_object(handles, ep.handle_bytes(), group=group)
+    ep.connect(handles)
 
 
 def expert_owner(expert: int, world: int) -> int:
