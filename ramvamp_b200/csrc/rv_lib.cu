@@ -945,6 +945,17 @@ extern "C" int rv_moe_profile_read(rv_moe *m, float *ms_out, size_t cap, size_t 
 
 static size_t round16(size_t x) { return (x + 15) & ~(size_t)15; }
 
+// Bytes of the tensor path's dequantized-stage cache: room for every expert's
+// largest matrix (gate|up, or down in any format), for engines of at least
+// 1024 tokens (where experts often hold several 128-position tiles); 0
+// otherwise.
+static size_t tc_cache_bytes(const MoeDims &d, size_t max_tokens) {
+  if (max_tokens < 1024 || d.H % RV_TC_ROWS || d.M % RV_TC_ROWS) return 0;
+  const size_t gu = tc_predeq_bytes<RV_Q4_K, false>(2 * d.M, d.H);
+  const size_t dn = std::max(tc_predeq_bytes<RV_Q6_K, true>(d.H, d.M), tc_predeq_bytes<RV_Q4_K, true>(d.H, d.M));
+  return (size_t)d.E * std::max(gu, dn);
+}
+
 extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_tokens, rv_moe **out) {
   if (!cfg || !out) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_create: null pointer");
   *out = nullptr;
@@ -1018,6 +1029,10 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
       {max_tc * 16, (void **)&B.tc_units},
       {16, (void **)&B.n_tc},
       {(size_t)d.E * 4, (void **)&B.tc_pstart},
+      // Dequantized weight stages (tensor path, experts with two or more
+      // position tiles): only engines large enough for that to happen often.
+      {tc_cache_bytes(d, max_tokens), (void **)&B.tc_a},
+      {(size_t)d.E * 4, (void **)&B.tc_apre},
   };
   size_t total = 0;
   for (const Part &p : parts) total += (p.bytes + 255) & ~(size_t)255;
@@ -1036,6 +1051,7 @@ extern "C" int rv_moe_create(int device, const rv_moe_config *cfg, size_t max_to
     *p.slot = (uint8_t *)m->arena + off;
     off += (p.bytes + 255) & ~(size_t)255;
   }
+  if (tc_cache_bytes(d, max_tokens) == 0) B.tc_a = nullptr;
   B.max_units = m->max_units;
   B.max_tc = (int)max_tc;
   B.tc_groups = (int)(padded_rows / 8);
@@ -1304,11 +1320,26 @@ static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
     if ((rc = prof_record(ev, 1, evflags, s))) return rc;
     CUtensorMap gmap;
     if ((rc = gate_up_map(W, L, &gmap))) return rc;
+    if (B.tc_a) {
+      const dim3 g((unsigned)(2 * d.M / RV_TC_ROWS), (unsigned)(2 * d.hb), (unsigned)d.E);
+      if (L.gate_format == RV_Q4_K) k_tc_predeq<RV_Q4_K, false><<<g, 256, 0, s>>>(d, B, W);
+      else k_tc_predeq<RV_Q5_K, false><<<g, 256, 0, s>>>(d, B, W);
+      RV_LAUNCH_CHECK();
+    }
     rc = L.gate_format == RV_Q4_K ? launch_tc_gemm<RV_Q4_K, false>(d, B, W, gmap, s)
                                   : launch_tc_gemm<RV_Q5_K, false>(d, B, W, gmap, s);
     if (rc) return rc;
     k_tc_quant<<<pg, 32 * d.mb, 0, s>>>(d, B);
     RV_LAUNCH_CHECK();
+    if (B.tc_a) {  // after the gate/up GEMM: the cache now takes the down stages
+      const unsigned gx = (unsigned)(d.H / RV_TC_ROWS);
+      switch (L.down_format) {
+        case RV_Q4_K: k_tc_predeq<RV_Q4_K, true><<<dim3(gx, 2 * d.mb, d.E), 256, 0, s>>>(d, B, W); break;
+        case RV_Q5_K: k_tc_predeq<RV_Q5_K, true><<<dim3(gx, 2 * d.mb, d.E), 256, 0, s>>>(d, B, W); break;
+        default: k_tc_predeq<RV_Q6_K, true><<<dim3(gx, 4 * d.mb, d.E), 256, 0, s>>>(d, B, W); break;
+      }
+      RV_LAUNCH_CHECK();
+    }
     if ((rc = prof_record(ev, 2, evflags, s))) return rc;
     switch (L.down_format) {
       case RV_Q4_K: rc = launch_tc_gemm<RV_Q4_K, true>(d, B, W, gmap, s); break;
@@ -1339,8 +1370,8 @@ static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
 // B.counts).
 static int route_stage(const MoeDims &d, const MoeBufs &B, int T, cudaStream_t s) {
   k_prologue<<<T, 256, 34 * sizeof(double) + (size_t)d.H * 4, s>>>(d, B);
-  const size_t smem = 16 + 2 * (size_t)(4 * RV_RCHUNK + 32 * (RV_RCHUNK + 4)) * 4;
-  k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + 3) / 4)), 128, smem, s>>>(d, B);
+  k_router_logits<<<dim3((unsigned)((T + 31) / 32), (unsigned)((d.E + RV_REXP - 1) / RV_REXP)), 128,
+                    router_logits_smem(), s>>>(d, B);
   k_route<<<(unsigned)((T + 3) / 4), 128, 0, s>>>(d, B);
   RV_LAUNCH_CHECK();
   return RV_OK;

@@ -68,6 +68,8 @@ struct MoeBufs {
   int *n_tc;               // [1]
   uint32_t *tc_pstart;     // [E] padded first row of each expert
   int max_tc;
+  uint8_t *tc_a;           // dequantized weight stages per expert (k_tc_predeq), null when the engine has none
+  int *tc_apre;            // [E] 1: this call's k_tc_predeq wrote the expert's stages
   // Expert-parallel output (null otherwise): the down projection of
   // dispatch slot p goes to row ep_home[p] of the output buffer of the rank
   // that sent it, ep_out[p / ep_cap] (that rank's memory, mapped here).
@@ -989,20 +991,28 @@ __global__ void __launch_bounds__(RV_CHAIN_THREADS) k_route_chain(MoeDims dd, Mo
   RV_PHASE(5, 5);
 }
 
-// Large-T router logits: CTA = 4 experts x 32 tokens; lane t of warp w runs
-// the chain of (token blockIdx.x*32+t, expert blockIdx.y*4+w) over
-// RV_RCHUNK-wide slices of the router rows and normed rows staged in shared
-// memory (bulk copies, double-buffered).
-#define RV_RCHUNK 256
+// Large-T router logits: CTA = 16 experts x 32 tokens; lane t of warp w
+// runs the chains of token blockIdx.x*32+t with the four experts
+// blockIdx.y*16+4w .. +3, so each token value read from shared memory feeds
+// four chains (the router values are warp-wide broadcasts).  Router rows
+// and normed rows are staged RV_RCHUNK floats at a time (bulk copies,
+// double-buffered; token rows padded so the lanes' 16-byte reads hit
+// distinct banks).  Each chain is dot_f32's (forward.rs:1231-1237): acc =
+// acc + r[k]*x[k] for k ascending, separate multiply and add.
+#define RV_RCHUNK 128
+#define RV_REXP 16
+__host__ __device__ constexpr size_t router_logits_smem() {
+  return 16 + 2 * (size_t)(RV_REXP * RV_RCHUNK + 32 * (RV_RCHUNK + 4)) * 4;
+}
 __global__ void __launch_bounds__(128) k_router_logits(MoeDims d, MoeBufs B) {
   extern __shared__ __align__(16) uint8_t sm[];
-  uint64_t *bar = (uint64_t *)sm;               // [2]
+  uint64_t *bar = (uint64_t *)sm;  // [2]
   const int xs_stride = RV_RCHUNK + 4;
   float *buf = (float *)(sm + 16);
-  const int stage_floats = 4 * RV_RCHUNK + 32 * xs_stride;
+  const int stage_floats = RV_REXP * RV_RCHUNK + 32 * xs_stride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = blockIdx.y * 4, t0 = blockIdx.x * 32;
-  const int ne = min(4, d.E - e0), nt = min(32, B.T - t0);
+  const int e0 = blockIdx.y * RV_REXP, t0 = blockIdx.x * 32;
+  const int ne = min(RV_REXP, d.E - e0), nt = min(32, B.T - t0);
   const int nchunks = d.H / RV_RCHUNK;
   if (threadIdx.x == 0) {
     mbar_init(bar, 1);
@@ -1016,27 +1026,34 @@ __global__ void __launch_bounds__(128) k_router_logits(MoeDims d, MoeBufs B) {
       bulk_g2s(st + i * RV_RCHUNK, B.router + (size_t)(e0 + i) * d.H + (size_t)c * RV_RCHUNK, RV_RCHUNK * 4,
                bar + (c & 1));
     for (int i = 0; i < nt; i++)
-      bulk_g2s(st + 4 * RV_RCHUNK + i * xs_stride, B.normed + (size_t)(t0 + i) * d.H + (size_t)c * RV_RCHUNK,
+      bulk_g2s(st + RV_REXP * RV_RCHUNK + i * xs_stride, B.normed + (size_t)(t0 + i) * d.H + (size_t)c * RV_RCHUNK,
                RV_RCHUNK * 4, bar + (c & 1));
   };
   if (threadIdx.x == 0) {
     issue(0);
     if (nchunks > 1) issue(1);
   }
-  float acc = 0.0f;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const bool live = lane < nt && 4 * warp < ne;
   for (int c = 0; c < nchunks; c++) {
     if (!mbar_wait_bounded(bar + (c & 1), (uint32_t)((c >> 1) & 1))) return;
     const float *st = buf + (c & 1) * stage_floats;
-    if (warp < ne && lane < nt) {
-      const float4 *r4 = (const float4 *)(st + warp * RV_RCHUNK);
-      const float4 *x4 = (const float4 *)(st + 4 * RV_RCHUNK + lane * xs_stride);
-#pragma unroll 8
+    if (live) {
+      // Rows past ne were not staged: their chains compute on stale values
+      // and are not stored.
+      const float4 *r4 = (const float4 *)(st + 4 * warp * RV_RCHUNK);
+      const float4 *x4 = (const float4 *)(st + RV_REXP * RV_RCHUNK + lane * xs_stride);
+#pragma unroll 4
       for (int k = 0; k < RV_RCHUNK / 4; k++) {
-        const float4 r = r4[k], x = x4[k];
-        acc = __fadd_rn(acc, __fmul_rn(r.x, x.x));
-        acc = __fadd_rn(acc, __fmul_rn(r.y, x.y));
-        acc = __fadd_rn(acc, __fmul_rn(r.z, x.z));
-        acc = __fadd_rn(acc, __fmul_rn(r.w, x.w));
+        const float4 x = x4[k];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float4 r = r4[i * (RV_RCHUNK / 4) + k];
+          acc[i] = __fadd_rn(acc[i], __fmul_rn(r.x, x.x));
+          acc[i] = __fadd_rn(acc[i], __fmul_rn(r.y, x.y));
+          acc[i] = __fadd_rn(acc[i], __fmul_rn(r.z, x.z));
+          acc[i] = __fadd_rn(acc[i], __fmul_rn(r.w, x.w));
+        }
       }
     }
     __syncthreads();  // stage (c & 1) consumed
@@ -1045,7 +1062,10 @@ __global__ void __launch_bounds__(128) k_router_logits(MoeDims d, MoeBufs B) {
       issue(c + 2);
     }
   }
-  if (warp < ne && lane < nt) B.logits[(size_t)(t0 + lane) * d.E + e0 + warp] = acc;
+  if (lane < nt)
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (4 * warp + i < ne) B.logits[(size_t)(t0 + lane) * d.E + e0 + 4 * warp + i] = acc[i];
 }
 
 // ------------------------------------------------- weight-tile staging
@@ -1434,7 +1454,10 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
       }
     }
   }
-  if (B.ep_out) __threadfence_system();  // rows stored into other ranks' memory
+  if (B.ep_out) {  // rows stored into other ranks' memory: one fence after the warp's stores
+    __syncwarp();
+    if (lane == 0) __threadfence_system();
+  }
   if constexpr (SPEC) {
     if (blockIdx.x == 0 && blockIdx.y == 0) {
       // After the wait above (every CTA has a unit): the exact routing is

@@ -234,6 +234,9 @@ __global__ void __launch_bounds__(256) k_tc_tiles(MoeDims d, MoeBufs B) {
   }
   const int t0 = s_t[e] - nt, pp0 = s_p[e] - np;
   if (e < d.E) {
+    // Experts with two or more position tiles get their weight stages
+    // dequantized once (k_tc_predeq) instead of once per tile.
+    if (B.tc_a) B.tc_apre[e] = nt >= 2;
     B.tc_pstart[e] = (uint32_t)pp0;
     const int p0 = (int)B.index_start[e];
     for (int k = 0; k < nt; k++)
@@ -405,6 +408,8 @@ RV_DEVFN void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z
 // may read are 32*(warp % 4)..+31.  The MMA-issuing warp (1) keeps its
 // scheduler nearly to itself: the dequantizing warps sit on schedulers 0,
 // 2 and 3, the eight epilogue warps (two per lane quadrant) mostly sleep.
+// (Registers are granted per four warps: 20 warps at 96 registers fill the
+// 64K-register file, and so would 18.)
 RV_DEVFN int tc_prod_index(int warp) {  // -1: not a producer
   switch (warp) {
     case 2: return 0;
@@ -420,6 +425,68 @@ RV_DEVFN int tc_prod_index(int warp) {  // -1: not a producer
 }
 #define RV_TC_W_EPI0 4   // warps 4-11: epilogue
 #define RV_TC_W_EPI1 12
+
+// Bytes of the dequantized stages of one expert's matrix (all row tiles).
+template <int FMT, bool DOWN>
+__host__ __device__ constexpr size_t tc_predeq_bytes(int rows, int kdim) {
+  return (size_t)(rows / RV_TC_ROWS) * (4 / TcStage<FMT, DOWN>::SUB) * (kdim / 256) * TcStage<FMT, DOWN>::bytes;
+}
+
+// The weight stages of experts holding two or more position tiles, written
+// once to B.tc_a exactly as the GEMM's dequantizing warps would write them
+// into shared memory (same functions, same layout); the GEMM then copies
+// each stage in with one bulk copy per 32 KB.  grid = (row tiles, stages
+// per row tile, experts); thread p: weight row p & 127, half p >> 7, as
+// the dequantizing warps.  Q6_K rows (2-byte aligned, read through 32-bit
+// word pairs) are first copied into shared memory, so no read leaves the
+// slab.
+template <int FMT, bool DOWN>
+__global__ void __launch_bounds__(256) k_tc_predeq(MoeDims d, MoeBufs B, MoeWeights W) {
+  using F = TcFmt<FMT>;
+  using SL = TcStage<FMT, DOWN>;
+  constexpr int BB = F::BB, SUB = SL::SUB, SPB = 4 / SUB;
+  __shared__ __align__(16) uint8_t s_raw[FMT == RV_Q6_K ? RV_TC_ROWS * BB + 16 : 16];
+  const int e = blockIdx.z;
+  if (!B.tc_apre[e]) return;
+  const int rt = blockIdx.x, it = blockIdx.y, NS = gridDim.y;
+  const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
+  int mat = 0, row0;
+  if constexpr (DOWN) {
+    row0 = rt * RV_TC_ROWS;
+  } else {
+    const int rtm = d.M / RV_TC_ROWS;
+    mat = rt / rtm;
+    row0 = (rt % rtm) * RV_TC_ROWS;
+  }
+  const uint8_t *wsrc = W.base + (size_t)e * W.stride + (DOWN ? W.down_off : mat ? W.up_off : W.gate_off) +
+                        (size_t)row0 * rb;
+  const int b = it / SPB, js = it % SPB;
+  const int p = threadIdx.x, r = p & 127, h = p >> 7;
+  uint8_t *st = B.tc_a + (((size_t)e * gridDim.x + rt) * NS + it) * SL::bytes;
+  if constexpr (FMT == RV_Q6_K) {
+    for (int i = threadIdx.x; i < RV_TC_ROWS * (BB / 2); i += blockDim.x) {
+      const int rr = i / (BB / 2), c = i % (BB / 2);
+      *(uint16_t *)(s_raw + rr * BB + 2 * c) = ld16(wsrc + (size_t)rr * rb + (size_t)b * BB + 2 * c);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < SUB; u++) {
+      const int j = SUB * js + u;
+      tc_stage_q6(s_raw + r * BB, j, h, st + SL::a + (size_t)u * RV_TC_ROWS * 128,
+                  st + SL::ah + (size_t)u * RV_TC_ROWS * 128, r);
+    }
+  } else {
+    const uint8_t *blk = wsrc + (size_t)r * rb + (size_t)b * BB;  // 16-byte aligned
+    const uint4 hdr = *(const uint4 *)blk;
+    uint32_t u0, u1, u2, u3;
+    k4_unpack_words(hdr.y, hdr.z, hdr.w, u0, u1, u2, u3);
+#pragma unroll
+    for (int u = 0; u < SUB; u++) {
+      const int j = SUB * js + u;
+      tc_stage_k45<FMT>(blk, j, h, u0, u1, u2, u3, st + SL::a + (size_t)u * RV_TC_ROWS * 128, st + SL::a2, r);
+    }
+  }
+}
 
 // One pair tile x 128 weight rows of one matrix.  Gate/up (DOWN = false):
 // grid.x = 2*M/128 row tiles (gate tiles first), output rows of gu
@@ -447,6 +514,9 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   RV_PHASE(PK, 0);
   const int4 tile = B.tc_units[u];
   const int e = tile.x, p0 = tile.y, n = tile.z - tile.y, pp0 = tile.w;
+  // apre: this expert's weight stages were dequantized by k_tc_predeq and
+  // arrive by bulk copy; the dequantizing warps stay idle.
+  const bool apre = B.tc_a != nullptr && B.tc_apre[e] != 0;
   const int nmma = (n + 15) & ~15, ng = nmma / 8, g0 = pp0 / 8;
   const int kdim = DOWN ? d.M : d.H, nb = kdim / 256, NS = SPB * nb;
   const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
@@ -482,7 +552,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       mbar_init(&raw_empty[i], RV_TC_PROD_WARPS);
     }
     for (int i = 0; i < SA; i++) {
-      mbar_init(&a_full[i], RV_TC_PROD_WARPS);
+      mbar_init(&a_full[i], apre ? 1 : RV_TC_PROD_WARPS);
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < C::SBMAX; i++) {
@@ -513,12 +583,32 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     if (lane == 0) {
       // ---------------------------------------------- weight staging
       bool ok = true;
-      if constexpr (DOWN) {
+      if (apre) {
+        const uint8_t *asrc = B.tc_a + ((size_t)e * gridDim.x + blockIdx.x) * NS * SL::bytes;
+        for (int it = 0; it < NS; it++) {
+          const int sa = it % SA;
+          if (!mbar_wait_bounded(&a_empty[sa], ((it / SA) & 1) ^ 1, 128)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&a_full[sa], (uint32_t)SL::bytes);
+          for (size_t o = 0; o < SL::bytes; o += 32768)
+            bulk_g2s(sm + (size_t)sa * SL::bytes + o, asrc + (size_t)it * SL::bytes + o,
+                     (uint32_t)(SL::bytes - o < 32768 ? SL::bytes - o : 32768), &a_full[sa]);
+        }
+      } else if constexpr (DOWN) {
         const size_t tb = (size_t)RV_TC_ROWS * rb;
         mbar_arrive_expect_tx(&raw_full[0], (uint32_t)tb);
         for (size_t o = 0; o < tb; o += 32768)
           bulk_g2s(raw + o, wsrc + o, (uint32_t)(tb - o < 32768 ? tb - o : 32768), &raw_full[0]);
       } else {
+        // The tile's rows are contiguous: ask the L2 for all of them now so
+        // each super-block's box below comes from L2, not HBM.
+        const uint32_t tile_b = (uint32_t)(RV_TC_ROWS * rb);
+        for (uint32_t o = 0; o < tile_b; o += 32768)
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(wsrc + o),
+                       "r"(tile_b - o < 32768u ? tile_b - o : 32768u)
+                       : "memory");
         for (int b = 0; b < nb; b++) {
           const int slot = b % R;
           if (!mbar_wait_bounded(&raw_empty[slot], ((b / R) & 1) ^ 1, 128)) {
@@ -631,7 +721,7 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       if (!ok) *s_fail = 1;
     }
     __syncwarp();
-  } else if (tc_prod_index(warp) >= 0) {
+  } else if (tc_prod_index(warp) >= 0 && !apre) {
     // ------------------------------------------------------ producers
     // Thread p: weight row p & 127, half p >> 7 of every stage.
     const int p = 32 * tc_prod_index(warp) + lane, r = p & 127, h = p >> 7;
@@ -742,7 +832,6 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
             else B.gu[(size_t)(p0 + col) * 2 * d.M + (size_t)mat * d.M + row0 + er] = acc[c][i];
           }
         }
-      if (DOWN && B.ep_out) __threadfence_system();  // rows stored into other ranks' memory
     }
     if (!ok) *s_fail = 1;
   }
@@ -752,5 +841,8 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     tc_fence_after();
     tc_dealloc(tmem, 4 * RV_TC_NT);
   }
+  // Expert-parallel down rows went to other ranks' memory: one system-scope
+  // fence after the barrier orders every thread's stores of this CTA.
+  if (DOWN && B.ep_out && threadIdx.x == 32) __threadfence_system();
   RV_PHASE(PK, 9);
 }
