@@ -959,7 +959,7 @@ def run_ep(args, table=None, quiet=False):
     import torch.distributed as dist
 
     import ramvamp_b200 as rv
-    from ramvamp_b200.ep import connect_group
+    from ramvamp_b200.ep import balanced_placement, connect_group, placement_tensor
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -972,23 +972,41 @@ def run_ep(args, table=None, quiet=False):
     n_layers = args.layers
     home = EP_TOKENS // world
     flags = rv.EXACT if args.exact else rv.TENSOR
-    if table is None or world > 1:
-        lays = [rv.qwen3_layer_layout(l, n_experts=E // world) for l in range(n_layers)]
-        table = rv.ExpertTable(lays, device=dev)
-        for l in range(n_layers):
-            table.fill_synthetic(l, SEED + l, 0.02, first_expert=rank, expert_step=world)
     routers_np = []
     for l in range(n_layers):
         r = rv.synth_normal(SEED + 1000 + l, 0, 0.02, E * H).view(E, H).cpu().numpy()
         r, _ = zipf_inputs(r, np.zeros((1, H), np.float32), SEED + 77, perm_seed=SEED + 77 + l)
         routers_np.append(r)
     routers = [torch.from_numpy(r).cuda() for r in routers_np]
+    norm = torch.ones(H, dtype=torch.float32, device="cuda")
+    eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=EP_TOKENS, device=dev)
+    # Expert placement (N > 1): route a calibration batch of 512 rows of the
+    # workload's distribution (the same on every rank, so every rank derives
+    # the same placement) through each layer's router and spread the
+    # experts by measured load, n_experts / N per rank.
+    placements, loads = [None] * n_layers, None
+    if world > 1:
+        cal = rv.synth_normal(SEED + 99, 0, 1.0, 512 * H).view(512, H).cpu().numpy()
+        cal = torch.from_numpy(zipf_inputs(routers_np[0], cal, SEED + 77, perm_seed=SEED + 77)[1]).cuda()
+        ranks_of = []
+        for l in range(n_layers):
+            ids, _, _ = eng.route(norm, routers[l], cal)
+            cnt = torch.bincount(ids.reshape(-1).long(), minlength=E).cpu().numpy()
+            ranks = balanced_placement(cnt.tolist(), world)
+            ranks_of.append(ranks)
+            placements[l] = placement_tensor(ranks, f"cuda:{dev}")
+    if table is None or world > 1:
+        lays = [rv.qwen3_layer_layout(l, n_experts=E // world) for l in range(n_layers)]
+        table = rv.ExpertTable(lays, device=dev)
+        for l in range(n_layers):
+            if world > 1:
+                table.fill_synthetic_list(l, SEED + l, 0.02, ranks_of[l][rank])
+            else:
+                table.fill_synthetic(l, SEED + l, 0.02)
     n_batches = 2
     xs = rv.synth_normal(SEED + 7 + rank, 0, 1.0, n_batches * home * H).view(n_batches, home, H).cpu().numpy()
     xs = np.stack([zipf_inputs(routers_np[0], xs[i], SEED + 77, perm_seed=SEED + 77)[1] for i in range(n_batches)])
     tokens = torch.from_numpy(np.ascontiguousarray(xs)).cuda()
-    norm = torch.ones(H, dtype=torch.float32, device="cuda")
-    eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=EP_TOKENS, device=dev)
     ep = rv.ExpertParallel(eng, world, rank, home)
     if world > 1:
         connect_group(ep)
@@ -999,7 +1017,7 @@ def run_ep(args, table=None, quiet=False):
 
     def step_body():
         for l in range(n_layers):
-            ep.forward(table, l, norm, routers[l], resid, flags=flags)
+            ep.forward(table, l, norm, routers[l], resid, flags=flags, placement=placements[l])
 
     # Every rank runs the same exchange steps in the same order: eager once,
     # capture (no steps run), replays.
@@ -1026,7 +1044,7 @@ def run_ep(args, table=None, quiet=False):
     full0.fill_synthetic(0, SEED, 0.02)
     with torch.cuda.stream(stream):
         resid.copy_(tokens[0])
-        ep.forward(table, 0, norm, routers[0], resid, flags=flags)
+        ep.forward(table, 0, norm, routers[0], resid, flags=flags, placement=placements[0])
         ep_l0 = resid.clone()
         resid.copy_(tokens[0])
         eng.forward(full0, 0, norm, routers[0], resid, flags=flags)
@@ -1130,6 +1148,8 @@ def run_ep(args, table=None, quiet=False):
                        else "exact (bit-identical to the reference's AVX2 arm)",
                        "parallelism": f"ep{world}", "exchange": "rv_moe_ep_forward: peer stores over NVLink + "
                        "release/acquire flags, no host synchronization", "cuda_graph": True,
+                       "placement": "per layer, experts spread by load measured on a 512-row calibration batch "
+                                    "(n_experts/N per rank)" if world > 1 else "all experts local",
                        "l2": "inputs larger than L2: each step streams every touched expert's weights (17.5 GB "
                              "over all ranks)"},
             "parity": {"graph_equals_eager": same_graph, "ep_equals_single_gpu_layer0": bool(ok.item()),
@@ -1244,6 +1264,10 @@ def main():
         return
     if args.workload == "ep" and args.impl != "reference":
         run_ep(args)
+        import torch.distributed as dist
+
+        if dist.is_available() and dist.is_initialized():
+            dist.destroy_process_group()
         return
     if args.workload != "decode":
         (run_reference_batched if args.impl == "reference" else run_cuda_batched)(args)

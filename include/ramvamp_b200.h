@@ -412,8 +412,11 @@ RV_API int rv_ep_plan(rv_moe *m, const uint32_t *topk_ids, const uint8_t *acts, 
 /* ---- expert parallelism over the GPUs of one node -----------------------
  * No counterpart in the reference, which runs the MoE block on one host.
  * The 128 experts of a layer are spread over `world` ranks (one process or
- * thread per GPU) by expert id modulo world: rank r holds experts r, r+world,
- * ... as its local experts 0, 1, ... (its rv_expert_table holds only those).
+ * thread per GPU), n_experts / world per rank, by a placement: rank r's
+ * rv_expert_table holds its experts as local experts 0, 1, ...  Without an
+ * explicit placement expert e lives on rank e % world as local expert
+ * e / world; a placement built from measured expert loads (see
+ * rv_ep_check_placement) evens out a skewed router.
  * Each rank routes its own tokens; the exchange runs through GPU memory:
  * every rank owns an exchange window in its HBM that the others map (CUDA
  * IPC across processes, peer access inside one), dispatch stores each
@@ -455,12 +458,19 @@ RV_API int rv_ep_connect(rv_ep *ep, const void *handles, size_t len);
 /* The MoE block of one layer for this rank's n_tokens home rows, in place on
  * `residual` (device), as rv_moe_forward: ffn_norm [hidden], router
  * [n_experts][hidden] (all experts, device), table = this rank's experts;
- * topk_ids/topk_weights optional [n_tokens][top_k] outputs.  flags:
+ * topk_ids/topk_weights optional [n_tokens][top_k] outputs.  placement:
+ * device [n_experts], entry e = rank << 16 | local id of global expert e,
+ * the same on every rank for this layer (NULL: e % world, e / world); an
+ * entry out of range is reported in the device error word.  flags:
  * RV_MOE_EXACT or RV_MOE_TENSOR.  Enqueues only (no host synchronization).
  * RV_ERR_PROTOCOL before rv_ep_connect. */
 RV_API int rv_moe_ep_forward(rv_ep *ep, const rv_expert_table *table, uint32_t layer, const float *ffn_norm,
                              const float *router, float *residual, size_t n_tokens, uint32_t *topk_ids,
-                             float *topk_weights, uint32_t flags, rv_stream stream);
+                             float *topk_weights, const uint32_t *placement, uint32_t flags, rv_stream stream);
+/* Checks a placement (host, len == n_experts) before it is used: every rank
+ * holds exactly n_experts / world experts with local ids 0..n_experts/world-1
+ * each used once (RV_ERR_ROUTED_OUT_OF_RANGE, RV_ERR_INVALID_ARGUMENT). */
+RV_API int rv_ep_check_placement(uint32_t n_experts, uint32_t world, const uint32_t *placement, size_t len);
 /* received[r] = pairs rank r sent this rank in the most recent layer (host,
  * len >= world); synchronizes the device. */
 RV_API int rv_ep_counts(const rv_ep *ep, uint32_t *received, size_t len);
@@ -670,6 +680,11 @@ RV_API int rv_expert_table_fill_synthetic(rv_expert_table *t, uint32_t layer, ui
  * rank holding experts r, r+G, r+2G, ...). */
 RV_API int rv_expert_table_fill_synthetic_strided(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
                                                   uint32_t first_expert, uint32_t expert_step, rv_stream stream);
+/* Local expert i of `layer` gets global expert experts[i]'s synthetic
+ * weights (host list, n == the layer's n_experts): an expert-parallel
+ * rank's experts under any placement. */
+RV_API int rv_expert_table_fill_synthetic_list(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
+                                               const uint32_t *experts, size_t n, rv_stream stream);
 
 #ifdef __cplusplus
 }

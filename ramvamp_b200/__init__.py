@@ -392,6 +392,12 @@ class ExpertTable:
         _check(lib().rv_expert_table_fill_synthetic_strided(self.handle, layer, seed, sigma, first_expert,
                                                             expert_step, _stream()))
 
+    def fill_synthetic_list(self, layer: int, seed: int, sigma: float, experts: Sequence[int]) -> None:
+        """Local expert i gets global expert experts[i]'s synthetic weights."""
+        arr = (ctypes.c_uint32 * max(len(experts), 1))(*experts)
+        _check(lib().rv_expert_table_fill_synthetic_list(self.handle, layer, seed, sigma, arr, len(experts),
+                                                         _stream()))
+
     def begin_layer(self, layer: int, experts: Sequence[int]) -> None:
         arr = (ctypes.c_uint32 * max(len(experts), 1))(*experts)
         _check(lib().rv_expert_table_begin_layer(self.handle, layer, arr, len(experts)))
@@ -605,11 +611,16 @@ class ExpertParallel:
 
     def forward(self, table: ExpertTable, layer: int, ffn_norm: torch.Tensor, router: torch.Tensor,
                 residual: torch.Tensor, topk_ids: Optional[torch.Tensor] = None,
-                topk_weights: Optional[torch.Tensor] = None, flags: int = EXACT) -> torch.Tensor:
-        """In place on this rank's home rows: residual += MoE(residual)."""
+                topk_weights: Optional[torch.Tensor] = None, flags: int = EXACT,
+                placement: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """In place on this rank's home rows: residual += MoE(residual).
+        placement: device int32 [n_experts] of rank << 16 | local id (the
+        same on every rank), from ``ramvamp_b200.ep.placement_tensor``;
+        None: expert e on rank e % world."""
         T = residual.numel() // self.engine.cfg.hidden
         _check(lib().rv_moe_ep_forward(self.handle, table.handle, layer, _p(ffn_norm), _p(router),
-                                       _p(residual), T, _p(topk_ids), _p(topk_weights), flags, _stream()))
+                                       _p(residual), T, _p(topk_ids), _p(topk_weights), _p(placement), flags,
+                                       _stream()))
         return residual
 
     def received(self) -> list:

@@ -154,7 +154,8 @@ SIGNATURES = {
     "rv_ep_destroy": (None, [P]),
     "rv_ep_handle": (I32, [P, P, SZ]),
     "rv_ep_connect": (I32, [P, P, SZ]),
-    "rv_moe_ep_forward": (I32, [P, P, U32, P, P, P, SZ, P, P, U32, P]),
+    "rv_moe_ep_forward": (I32, [P, P, U32, P, P, P, SZ, P, P, P, U32, P]),
+    "rv_ep_check_placement": (I32, [U32, U32, P, SZ]),
     "rv_ep_counts": (I32, [P, P, SZ]),
     "rv_moe_profile_enable": (I32, [P, SZ]),
     "rv_moe_profile_rewind": (I32, [P]),
@@ -164,6 +165,7 @@ SIGNATURES = {
     "rv_quantize_weights": (I32, [I32, P, SZ, P, P]),
     "rv_expert_table_fill_synthetic": (I32, [P, U32, U64, F32, P]),
     "rv_expert_table_fill_synthetic_strided": (I32, [P, U32, U64, F32, U32, U32, P]),
+    "rv_expert_table_fill_synthetic_list": (I32, [P, U32, U64, F32, P, SZ, P]),
 }
 
 _lib = None

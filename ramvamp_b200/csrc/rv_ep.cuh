@@ -152,12 +152,15 @@ RV_DEVFN bool ep_wait(const uint32_t *flag, uint32_t epoch) {
 
 // Dispatch of this rank's P = T*top_k pairs: one thread per pair reserves a
 // slot in its expert's rank (warp-aggregated atomics per destination),
+// the rank and local id of global expert e coming from `place[e]` (rank <<
+// 16 | local id; an entry out of range is reported and its pair dropped) or,
+// without a placement, e mod world and e / world;
 // writes the slot's metadata there and the warp copies its pairs' Q8_K rows
 // with 16-byte stores over NVLink.  The last CTA to finish publishes the
 // counts, clears the reservations and raises this layer's flag on every
 // rank.  Also clears the router's per-expert counts (`counts`, E ints).
-__global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs A, const uint32_t *ids, const uint8_t *acts, int P,
-                                                     int K, int E, int *counts) {
+__global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs A, const uint32_t *place, const uint32_t *ids,
+                                                     const uint8_t *acts, int P, int K, int E, int *counts) {
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (blockIdx.x == 0)
@@ -169,7 +172,21 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs A, const uint32_t *i
     rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
     e = ~0u;
   }
-  const uint32_t dest = e != ~0u ? e % A.world : ~0u;
+  uint32_t dest = ~0u, local = 0;
+  if (e != ~0u) {
+    if (place) {
+      const uint32_t pl = place[e];
+      dest = pl >> 16;
+      local = pl & 0xFFFFu;
+      if (dest >= A.world || local >= (uint32_t)E / A.world) {
+        rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
+        dest = ~0u;
+      }
+    } else {
+      dest = e % A.world;
+      local = e / A.world;
+    }
+  }
   const unsigned same = __match_any_sync(RV_FULL, dest);
   const int leader = __ffs(same) - 1;
   uint32_t base = 0;
@@ -181,7 +198,7 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs A, const uint32_t *i
       uint8_t *w = A.win[dest];
       const size_t i = (size_t)A.rank * A.cap + slot;
       ep_u32(w, A.o_home)[i] = (uint32_t)p;
-      ep_u32(w, A.o_eid)[i] = e / A.world;
+      ep_u32(w, A.o_eid)[i] = local;
     } else {
       rv_dev_fail(RV_ERR_LENGTH_MISMATCH);  // cannot happen: P <= cap
     }

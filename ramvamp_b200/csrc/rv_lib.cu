@@ -1774,7 +1774,7 @@ extern "C" int rv_ep_connect(rv_ep *ep, const void *handles, size_t len) {
 
 extern "C" int rv_moe_ep_forward(rv_ep *ep, const rv_expert_table *table, uint32_t layer, const float *ffn_norm,
                                  const float *router, float *residual, size_t n_tokens, uint32_t *topk_ids,
-                                 float *topk_weights, uint32_t flags, rv_stream stream) {
+                                 float *topk_weights, const uint32_t *placement, uint32_t flags, rv_stream stream) {
   if (!ep || !table) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "moe_ep_forward: null exchange or table");
   if (!ep->connected) RV_FAIL(RV_ERR_PROTOCOL, "moe_ep_forward: rv_ep_connect has not completed");
   rv_moe *m = ep->m;
@@ -1802,7 +1802,7 @@ extern "C" int rv_moe_ep_forward(rv_ep *ep, const rv_expert_table *table, uint32
   // 2. dispatch: rows and metadata into the experts' ranks, then the flags
   const int P = T * d.K;
   const unsigned dgrid = (unsigned)std::max(1, (P + 255) / 256);
-  k_ep_dispatch<<<dgrid, 256, 0, s>>>(ep->A, B.ids, B.acts, P, d.K, d.E, B.counts);
+  k_ep_dispatch<<<dgrid, 256, 0, s>>>(ep->A, placement, B.ids, B.acts, P, d.K, d.E, B.counts);
   RV_LAUNCH_CHECK();
   if (topk_ids) RV_CUDA(cudaMemcpyAsync(topk_ids, B.ids, (size_t)P * 4, cudaMemcpyDeviceToDevice, s));
   if (topk_weights) RV_CUDA(cudaMemcpyAsync(topk_weights, B.w, (size_t)P * 4, cudaMemcpyDeviceToDevice, s));
@@ -1830,6 +1830,24 @@ extern "C" int rv_moe_ep_forward(rv_ep *ep, const rv_expert_table *table, uint32
   k_ep_combine<<<dim3((unsigned)std::max(T, 1), (unsigned)((d.H + 255) / 256)), 256, 0, s>>>(ep->A, d, residual,
                                                                                             B.w, T);
   RV_LAUNCH_CHECK();
+  return RV_OK;
+}
+
+extern "C" int rv_ep_check_placement(uint32_t n_experts, uint32_t world, const uint32_t *placement, size_t len) {
+  if (!placement) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_check_placement: null placement");
+  if (world == 0 || world > 64 || n_experts % world)
+    RV_FAIL(RV_ERR_UNIMPLEMENTED, "ep_check_placement: %u experts over %u ranks", n_experts, world);
+  if (len != n_experts) RV_FAIL(RV_ERR_LENGTH_MISMATCH, "ep_check_placement: %zu entries for %u experts", len, n_experts);
+  const uint32_t per = n_experts / world;
+  std::vector<uint8_t> seen((size_t)n_experts, 0);
+  for (uint32_t e = 0; e < n_experts; e++) {
+    const uint32_t r = placement[e] >> 16, l = placement[e] & 0xFFFFu;
+    if (r >= world || l >= per)
+      RV_FAIL(RV_ERR_ROUTED_OUT_OF_RANGE, "ep_check_placement: expert %u -> rank %u local %u (of %u x %u)", e, r, l,
+              world, per);
+    if (seen[(size_t)r * per + l]++)
+      RV_FAIL(RV_ERR_INVALID_ARGUMENT, "ep_check_placement: rank %u local %u holds two experts", r, l);
+  }
   return RV_OK;
 }
 
@@ -2387,10 +2405,30 @@ extern "C" int rv_expert_table_fill_synthetic(rv_expert_table *t, uint32_t layer
   return rv_expert_table_fill_synthetic_strided(t, layer, seed, sigma, 0, 1, stream);
 }
 
+// Local expert ex of the layer gets global expert ge(ex)'s weights.
+template <typename GE>
+static int fill_synthetic(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma, GE ge_of, rv_stream stream);
+
 extern "C" int rv_expert_table_fill_synthetic_strided(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
                                                       uint32_t first_expert, uint32_t expert_step, rv_stream stream) {
   if (!t) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "null table");
   if (expert_step == 0) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "fill_synthetic: expert_step 0");
+  return fill_synthetic(t, layer, seed, sigma,
+                        [&](uint32_t ex) { return (uint64_t)first_expert + (uint64_t)ex * expert_step; }, stream);
+}
+
+extern "C" int rv_expert_table_fill_synthetic_list(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma,
+                                                   const uint32_t *experts, size_t n, rv_stream stream) {
+  if (!t || !experts) RV_FAIL(RV_ERR_INVALID_ARGUMENT, "fill_synthetic_list: null pointer");
+  if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
+  if (n != t->layouts[layer].n_experts)
+    RV_FAIL(RV_ERR_LENGTH_MISMATCH, "fill_synthetic_list: %zu experts for a layer of %u", n,
+            t->layouts[layer].n_experts);
+  return fill_synthetic(t, layer, seed, sigma, [&](uint32_t ex) { return (uint64_t)experts[ex]; }, stream);
+}
+
+template <typename GE>
+static int fill_synthetic(rv_expert_table *t, uint32_t layer, uint64_t seed, float sigma, GE ge_of, rv_stream stream) {
   if (layer >= t->layouts.size()) RV_FAIL(RV_ERR_LAYER_OUT_OF_RANGE, "layer %u of %zu", layer, t->layouts.size());
   const rv_layer_layout &L = t->layouts[layer];
   const size_t mh = (size_t)L.moe * L.hidden;
@@ -2407,7 +2445,7 @@ extern "C" int rv_expert_table_fill_synthetic_strided(rv_expert_table *t, uint32
   cudaStream_t s = (cudaStream_t)stream;
   for (uint32_t ex = 0; ex < L.n_experts && rc == RV_OK; ex++) {
     uint8_t *blob = t->base[layer] + (size_t)ex * L.stride;
-    const uint64_t ge = (uint64_t)first_expert + (uint64_t)ex * expert_step;  // global expert id
+    const uint64_t ge = ge_of(ex);  // global expert id
     rc = rv_synth_normal(seed, ge * 3 * mh, sigma, tmp, 3 * mh, stream);
     if (!rc) rc = rv_quantize_weights(L.gate_format, tmp, mh, blob + L.gate_off, stream);
     if (!rc) rc = rv_quantize_weights(L.up_format, tmp + mh, mh, blob + L.up_off, stream);

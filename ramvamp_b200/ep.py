@@ -52,6 +52,48 @@ def connect_group(ep, group=None) -> None:
     ep.connect(handles)
 
 
+def balanced_placement(loads: Sequence[float], world: int) -> List[List[int]]:
+    """Experts per rank for one layer, n_experts / world each, evening out
+    the measured loads (pairs routed to each expert): experts in decreasing
+    load (ties: lower id first) go to the rank with the least load so far
+    among those with room (ties: lower rank).  Returns per rank its global
+    expert ids in local-id order."""
+    n = len(loads)
+    if n % world:
+        raise ValueError(f"{n} experts do not split over {world} ranks")
+    per = n // world
+    order = sorted(range(n), key=lambda e: (-float(loads[e]), e))
+    ranks: List[List[int]] = [[] for _ in range(world)]
+    total = [0.0] * world
+    for e in order:
+        r = min((r for r in range(world) if len(ranks[r]) < per), key=lambda r: (total[r], r))
+        ranks[r].append(e)
+        total[r] += float(loads[e])
+    return ranks
+
+
+def placement_entries(ranks: Sequence[Sequence[int]]) -> List[int]:
+    """rank << 16 | local id per global expert (rv_moe_ep_forward's map)."""
+    n = sum(len(r) for r in ranks)
+    out = [0] * n
+    for r, experts in enumerate(ranks):
+        for local, e in enumerate(experts):
+            out[e] = (r << 16) | local
+    return out
+
+
+def placement_tensor(ranks: Sequence[Sequence[int]], device) -> torch.Tensor:
+    """The device map of a placement, checked by rv_ep_check_placement."""
+    import ctypes
+
+    from . import _lib
+
+    entries = placement_entries(ranks)
+    arr = (ctypes.c_uint32 * len(entries))(*entries)
+    _lib.check(_lib.load().rv_ep_check_placement(len(entries), len(ranks), arr, len(entries)))
+    return torch.tensor(entries, dtype=torch.int32, device=device)
+
+
 def expert_owner(expert: int, world: int) -> int:
     """Rank holding global expert `expert`."""
     return expert % world

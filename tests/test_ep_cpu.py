@@ -8,6 +8,7 @@ return of the expert outputs and the top-k-order combine.  Every rank's
 result must equal the single-process oracle forward (prefill.rs:2136-2263)
 bit for bit.
 """
+import ctypes
 import os
 import socket
 
@@ -161,3 +162,39 @@ def test_ep_two_gloo_ranks_bit_identical():
     # every pair sent was received somewhere
     sent = np.sum([r[2] for r in results], axis=0)
     assert sorted(r[3] for r in results) == sorted(sent.tolist())
+
+
+def test_balanced_placement_spreads_hot_experts():
+    """Experts in decreasing load go to the least-loaded rank with room:
+    every rank holds n/world experts, the Zipf-skewed load ends near even,
+    and the entries pass the library's placement check."""
+    import math
+
+    import ramvamp_b200 as rv
+    from ramvamp_b200 import _lib
+    from ramvamp_b200.ep import balanced_placement, placement_entries
+
+    rng = np.random.default_rng(3)
+    loads = [1.0 / (r + 1) ** 1.1 for r in rng.permutation(128)]
+    for world in (1, 2, 4, 8):
+        ranks = balanced_placement(loads, world)
+        assert sorted(e for r in ranks for e in r) == list(range(128))
+        assert all(len(r) == 128 // world for r in ranks)
+        tot = [sum(loads[e] for e in r) for r in ranks]
+        mean = sum(tot) / world
+        # Near the floor set by the mean and by the hottest expert alone.
+        assert max(tot) <= 1.25 * max(mean, max(loads))
+        strided = [sum(loads[e] for e in range(r, 128, world)) for r in range(world)]
+        assert max(tot) <= max(strided) + 1e-12
+        entries = placement_entries(ranks)
+        arr = (ctypes.c_uint32 * 128)(*entries)
+        assert rv.lib().rv_ep_check_placement(128, world, arr, 128) == 0
+    # The checker refuses a rank holding too many experts and duplicates.
+    bad = [0] * 128  # every expert on rank 0, local 0
+    arr = (ctypes.c_uint32 * 128)(*bad)
+    assert rv.lib().rv_ep_check_placement(128, 2, arr, 128) != 0
+    entries = placement_entries(balanced_placement(loads, 4))
+    entries[5] = (9 << 16) | 0  # rank 9 of 4
+    arr = (ctypes.c_uint32 * 128)(*entries)
+    assert _lib.STATUS_NAMES[rv.lib().rv_ep_check_placement(128, 4, arr, 128)] == "RoutedExpertOutOfRange"
+    assert not math.isnan(sum(loads))

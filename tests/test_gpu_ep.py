@@ -168,6 +168,37 @@ def test_library_ep_world1_equals_forward(rv, flags_name, T):
     ep.close()
 
 
+def test_library_ep_world1_with_a_placement(rv):
+    """A placement that permutes the local ids (the table filled in that
+    order) gives the same bits as rv_moe_forward on the natural order."""
+    from ramvamp_b200.ep import placement_tensor
+
+    T = 96
+    rng = np.random.default_rng(11)
+    order = [int(e) for e in rng.permutation(E)]
+    lays = [rv.qwen3_layer_layout(l) for l in (0, 6)]
+    table = rv.ExpertTable(lays, device=0)
+    for i, seed in enumerate((91, 96)):
+        table.fill_synthetic_list(i, seed, 0.02, order)
+    place = placement_tensor([order], "cuda:0")
+    full = _full_layers(rv)
+    routers = _routers(rv)
+    norm = torch.ones(H, device="cuda")
+    eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=T, device=0)
+    ref = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=T, device=0)
+    ep = rv.ExpertParallel(eng, 1, 0, T)
+    ep.connect([ep.handle_bytes()])
+    x = rv.synth_normal(450, 0, 1.0, T * H).view(T, H).contiguous()
+    for flags in (rv.EXACT, rv.TENSOR):
+        got, want = x.clone(), x.clone()
+        for li in range(2):
+            ep.forward(table, li, norm, routers[li], got, flags=flags, placement=place)
+            ref.forward(full, li, norm, routers[li], want, flags=flags)
+        assert (bits(got) == bits(want)).all(), flags
+    rv.device_status(0)
+    ep.close()
+
+
 def test_library_ep_graph_capture_and_empty_calls(rv):
     """Two layers of rv_moe_ep_forward captured in one CUDA graph replay to
     the eager result (the flags count layers on the device, so replays keep
@@ -259,9 +290,17 @@ def _lib_rank_main(rank, world, port, tokens, out_dir, q):
         torch.cuda.set_device(rank)
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60))
+        from ramvamp_b200.ep import balanced_placement, placement_tensor
+
         T = tokens[rank]
         cap = max(tokens)
-        table = _layers(rv, world, rank, device=rank)
+        # Layer 0 by id mod world; layer 1 by a placement from skewed loads.
+        ranks1 = balanced_placement(list(np.random.default_rng(5).zipf(1.5, E).astype(float)), world)
+        lays = [rv.qwen3_layer_layout(l, n_experts=E // world) for l in (0, 6)]
+        table = rv.ExpertTable(lays, device=rank)
+        table.fill_synthetic(0, seed=91, sigma=0.02, first_expert=rank, expert_step=world)
+        table.fill_synthetic_list(1, 96, 0.02, ranks1[rank])
+        places = [None, placement_tensor(ranks1, f"cuda:{rank}")]
         routers = _routers(rv)
         norm = torch.ones(H, device="cuda")
         eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=world * cap, device=rank)
@@ -272,11 +311,12 @@ def _lib_rank_main(rank, world, port, tokens, out_dir, q):
         for name, flags in (("exact", rv.EXACT), ("tensor", rv.TENSOR)):
             res = x.clone()
             for li in range(2):
-                ep.forward(table, li, norm, routers[li], res, flags=flags)
+                ep.forward(table, li, norm, routers[li], res, flags=flags, placement=places[li])
                 # Every rank joins every call; in this extra one rank 0 sends
                 # 16 other tokens and the last rank brings none.
                 extra = rv.synth_normal(700 + li, 0, 1.0, 16 * H).view(16, H).contiguous()
-                ep.forward(table, li, norm, routers[li], extra if rank == 0 else empty, flags=flags)
+                ep.forward(table, li, norm, routers[li], extra if rank == 0 else empty, flags=flags,
+                           placement=places[li])
             torch.cuda.synchronize()
             np.save(os.path.join(out_dir, f"{name}_{rank}.npy"), res.cpu().numpy())
         rv.device_status(rank)
