@@ -256,23 +256,21 @@ __global__ void __launch_bounds__(1024) k_ep_receive(EpArgs A, MoeDims d, MoeBuf
   }
   __syncthreads();
   const uint32_t *eid = ep_u32(A.mine, A.o_eid), *home = ep_u32(A.mine, A.o_home);
-  const uint32_t slots = A.world * A.cap;
-  for (uint32_t p = threadIdx.x; p < slots; p += blockDim.x) {
-    const uint32_t s = p / A.cap, i = p - s * A.cap;
-    uint32_t e = ~0u;
-    if (i < s_n[s]) {
-      e = eid[p];
+  // Only the filled slots: slot (s, i) for i < s_n[s].
+  for (uint32_t s = 0; s < A.world; s++)
+    for (uint32_t i = threadIdx.x; i < s_n[s]; i += blockDim.x) {
+      const uint32_t p = s * A.cap + i;
+      uint32_t e = eid[p];
       if (e >= (uint32_t)d.E || home[p] >= A.cap) {
         rv_dev_fail(RV_ERR_ROUTED_OUT_OF_RANGE);
         e = ~0u;
       } else {
         atomicAdd(&s_cnt[e], 1);
       }
+      B.ids[p] = e;
     }
-    B.ids[p] = e;
-  }
   __syncthreads();
-  build_index_cta(d, B, s_cnt, s_st, s_cur, s_us, /*sparse=*/true);
+  build_index_cta(d, B, s_cnt, s_st, s_cur, s_us, /*sparse=*/true, s_n, (int)A.world, (int)A.cap);
 }
 
 // After the expert stage: every output row this rank owed has been stored

@@ -393,8 +393,12 @@ __global__ void __launch_bounds__(128) k_route(MoeDims d, MoeBufs B) {
 // the unit counts, every thread writes units, then the (token, slot) pairs
 // are placed by expert.  s_cnt/s_cur: [256] ints, s_st/s_us: [257].
 // sparse: dispatch slots whose expert id is ~0 are empty and skipped.
+// slot_n (shared memory, or null): the pairs form n_sources ranges of
+// slot_cap slots of which the first slot_n[s] are filled; only those are
+// placed.
 RV_DEVFN void build_index_cta(const MoeDims &d, const MoeBufs &B, int *s_cnt, uint32_t *s_st,
-                              uint32_t *s_cur, int *s_us, bool sparse = false) {
+                              uint32_t *s_cur, int *s_us, bool sparse = false, const uint32_t *slot_n = nullptr,
+                              int n_sources = 0, int slot_cap = 0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pairs = B.T * d.K;
   if (warp == 0) {
@@ -445,6 +449,19 @@ RV_DEVFN void build_index_cta(const MoeDims &d, const MoeBufs &B, int *s_cnt, ui
     for (int p = 0; p < c; p += RV_MOE_TOK_CHUNK, u++)
       if (u < B.max_units)
         B.units[u] = make_int4(e, (int)s_st[e] + p, (int)s_st[e] + min(c, p + RV_MOE_TOK_CHUNK), 0);
+  }
+  if (slot_n) {  // only the filled slots of each source's range
+    __syncthreads();
+    for (int s = 0; s < n_sources; s++)
+      for (int i = threadIdx.x; i < (int)slot_n[s]; i += blockDim.x) {
+        const int p = s * slot_cap + i;
+        const uint32_t e = B.ids[p];
+        if (e >= (uint32_t)d.E) continue;  // dropped when laid out
+        const uint32_t pos = atomicAdd(&s_cur[e], 1u);
+        if (pos < (uint32_t)pairs) B.index[pos] = (uint32_t)p;
+        else rv_dev_fail(RV_ERR_LENGTH_MISMATCH);
+      }
+    return;
   }
   for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
     const uint32_t e = B.ids[p];
