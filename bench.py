@@ -699,8 +699,8 @@ def run_reference_model(args):
 # batch (config 3): 64 sequences, one token each, through all 48 MoE layers;
 #   router logits biased so expert popularity follows Zipf s=1.1.
 # ep (config 4): 4096 tokens (8 x 512) through all 48 MoE layers with the
-#   Zipf skew, experts sharded over the N GPUs (expert id mod N), NCCL
-#   all-to-all dispatch and combine.
+#   Zipf skew, experts spread over the N GPUs by a load-balanced placement,
+#   dispatch and combine through peer memory inside the library (run_ep).
 # The Zipf skew: every token carries a shared component c*u (u a fixed unit
 # vector, c = sqrt(H)/2) and router row e gets s_e*u/C added, s_e =
 # -1.1*ln(rank_e + 1) over a seeded permutation of the experts and C the
@@ -762,7 +762,6 @@ def run_cuda_batched(args, quiet=False):
     import torch.distributed as dist
 
     import ramvamp_b200 as rv
-    from ramvamp_b200.ep import EngineBackend, ExpertParallelMoe
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -773,14 +772,12 @@ def run_cuda_batched(args, quiet=False):
         dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=120))
     n_layers, n_tok = workload_shape(args)
     flags = rv.EXACT if args.exact else rv.TENSOR
-    ep_mode = args.workload == "ep"
-    shard = world if ep_mode else 1
-    # Each rank of the ep workload holds experts rank, rank+N, ...; other
-    # workloads run independent replicas on N>1.
-    lays = [rv.qwen3_layer_layout(l, n_experts=E // shard) for l in range(n_layers)]
+    assert args.workload in ("prefill", "batch"), "config 4 runs through run_ep"
+    # On N>1 every rank runs an independent replica.
+    lays = [rv.qwen3_layer_layout(l) for l in range(n_layers)]
     table = rv.ExpertTable(lays, device=dev)
     for l in range(n_layers):
-        table.fill_synthetic(l, SEED + l, 0.02, first_expert=rank if ep_mode else 0, expert_step=shard)
+        table.fill_synthetic(l, SEED + l, 0.02)
     zipf = args.workload in ("batch", "ep")
     routers_np = []
     for l in range(n_layers):
@@ -790,34 +787,27 @@ def run_cuda_batched(args, quiet=False):
         routers_np.append(r)
     routers = [torch.from_numpy(r).cuda() for r in routers_np]
     norm = torch.ones(H, dtype=torch.float32, device="cuda")
-    home = n_tok // world if ep_mode else n_tok
+    home = n_tok
     n_batches = 4
     xs = rv.synth_normal(SEED + 7 + rank, 0, 1.0, n_batches * home * H).view(n_batches, home, H).cpu().numpy()
     if zipf:
         xs = np.stack([zipf_inputs(routers_np[0], xs[i], SEED + 77)[1] for i in range(n_batches)])
     tokens = torch.from_numpy(np.ascontiguousarray(xs)).cuda()
-    eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=n_tok if ep_mode else home, device=dev)
+    eng = rv.MoeEngine(H, M, E, K, True, 1e-6, max_tokens=home, device=dev)
     resid = torch.empty(home, H, dtype=torch.float32, device="cuda")
     stream = torch.cuda.Stream()
-    ep = ExpertParallelMoe(EngineBackend(eng, table, [norm] * n_layers, routers, flags), shard, rank if ep_mode else 0)
 
     def step_body():
-        if ep_mode:
-            for l in range(n_layers):
-                ep.forward(l, resid)
-        else:
-            for l in range(n_layers):
-                eng.forward(table, l, norm, routers[l], resid, flags=flags)
+        for l in range(n_layers):
+            eng.forward(table, l, norm, routers[l], resid, flags=flags)
 
     with torch.cuda.stream(stream):
         resid.copy_(tokens[0])
         step_body()
     stream.synchronize()
-    graph = None
-    if not ep_mode:  # the ep step synchronizes on the exchanged counts: no graph
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step_body()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_body()
     torch.cuda.synchronize()
 
     def run_steps(lo, hi):
@@ -848,25 +838,23 @@ def run_cuda_batched(args, quiet=False):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    total_tok = (n_tok if ep_mode else home * world)
+    total_tok = home * world
     tok_s = total_tok * args.steps / (ms / 1e3)
 
     # Per-stage durations on the profile events (single-GPU forward path,
     # outside the timed region): the expert GEMM stages bound the roofline.
-    stage = None
-    if not ep_mode or world == 1:
-        eng.profile_enable(n_layers)
-        sets = []
-        for i in range(3):
-            eng.profile_rewind()
-            with torch.cuda.stream(stream):
-                resid.copy_(tokens[i % n_batches])
-                for l in range(n_layers):
-                    eng.forward(table, l, norm, routers[l], resid, flags=flags)
-            stream.synchronize()
-            sets.append(eng.profile_read())
-        stage = np.stack(sets).mean(0)  # [layers][4] ms
-        eng.profile_enable(0)
+    eng.profile_enable(n_layers)
+    sets = []
+    for i in range(3):
+        eng.profile_rewind()
+        with torch.cuda.stream(stream):
+            resid.copy_(tokens[i % n_batches])
+            for l in range(n_layers):
+                eng.forward(table, l, norm, routers[l], resid, flags=flags)
+        stream.synchronize()
+        sets.append(eng.profile_read())
+    stage = np.stack(sets).mean(0)  # [layers][4] ms
+    eng.profile_enable(0)
     # e2e: host rows in, host rows out, through the public call a caller makes
     host_tok = torch.empty(n_batches, home, H, dtype=torch.float32).pin_memory()
     host_tok.copy_(tokens.cpu())
@@ -878,14 +866,8 @@ def run_cuda_batched(args, quiet=False):
     t0 = time.perf_counter()
     for i in range(n_e2e):
         hres.copy_(host_tok[i % n_batches])
-        if ep_mode:
-            resid.copy_(hres, non_blocking=True)
-            for l in range(n_layers):
-                ep.forward(l, resid)
-            hres.copy_(resid)
-        else:
-            for l in range(n_layers):
-                eng.forward_host(table, l, norm, routers[l], hres, flags=flags)
+        for l in range(n_layers):
+            eng.forward_host(table, l, norm, routers[l], hres, flags=flags)
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     if world > 1:
@@ -896,7 +878,7 @@ def run_cuda_batched(args, quiet=False):
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_batched(args, rv, table if not ep_mode or world == 1 else None, routers_np,
+        cpu = cpu_baseline_batched(args, rv, table, routers_np,
                                    tokens[0].cpu().numpy(), lays)
 
     if rank == 0:
@@ -905,7 +887,7 @@ def run_cuda_batched(args, quiet=False):
         line = {
             "metric": workload_metric(args), "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "strong" if ep_mode else "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8/int4 levels as exact f16 integers on tcgen05, f32 accumulate" if flags == rv.TENSOR
             else "int8 (dp4a) + f32",
             "data": "synthetic: seeded N(0,1) rows, N(0,0.02) router and expert weights quantized by the "
@@ -916,13 +898,12 @@ def run_cuda_batched(args, quiet=False):
                        else "exact (bit-identical to the reference's AVX2 arm)",
                        "l2": "inputs larger than L2: each step streams every touched expert's weights "
                              "(%.0f MB per layer resident)" % (sum(L.stride for L in lays[:1]) * lays[0].n_experts / 1e6),
-                       "parallelism": (f"ep{world}" if ep_mode else ("replicas" if world > 1 else "single GPU")),
+                       "parallelism": "replicas" if world > 1 else "single GPU",
                        "cuda_graph": graph is not None},
             "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s",
-                    "h2d_bytes_per_step": home * H * 4 * (1 if ep_mode else n_layers),
-                    "d2h_bytes_per_step": home * H * 4 * (1 if ep_mode else n_layers),
-                    "path": "ExpertParallelMoe.forward per layer" if ep_mode
-                    else "rv_moe_forward_host per layer (pinned host rows in, result out)"},
+                    "h2d_bytes_per_step": home * H * 4 * n_layers,
+                    "d2h_bytes_per_step": home * H * 4 * n_layers,
+                    "path": "rv_moe_forward_host per layer (pinned host rows in, result out)"},
             "gpu_launches": args.steps * n_layers * (10 if flags == rv.TENSOR else 7),
             "clocks": clk,
             "cpu_baseline": cpu,
