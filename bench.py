@@ -16,8 +16,11 @@ Arms:
                      sample of layers, scaled to 48 layers
 
 Prints one JSON line (rank 0).  On one GPU the line also carries config 4
-at N=1 ("ep_prefill", the base point of the multi-GPU curve) and config 2
-("prefill", with the tensor-pipe fraction of its gate/up stage).
+at N=1 ("ep_prefill", the base point of the multi-GPU curve), config 2
+("prefill", with the tensor-pipe fraction of its gate/up stage), config 3
+("batch": 64 Zipf-skewed sequences through 48 MoE layers) and the whole
+model of config 1 ("model": attention, MoE and lm_head, greedy decode
+after a 512-token prompt), each measured in the same run.
 
 Multi-GPU (torchrun, N>1): batch-1 decode does not shard, so the default
 workload there is config 4, expert-parallel prefill of 4096 tokens through
@@ -382,6 +385,17 @@ def run_cuda(args):
         extras["prefill"] = {k: l2.get(k) for k in ("metric", "value", "unit", "ms_per_step", "stage_ms_per_layer",
                                                     "tensor", "roofline", "e2e")}
         extras["prefill"]["config"] = l2["config"]["workload"]
+        a3 = copy.copy(args)
+        a3.workload, a3.steps, a3.warmup, a3.exact, a3.no_cpu_baseline = "batch", 10, 3, False, True
+        l3 = run_cuda_batched(a3, quiet=True, table=table)
+        extras["batch"] = {k: l3.get(k) for k in ("metric", "value", "unit", "ms_per_step", "tensor", "e2e")}
+        extras["batch"]["config"] = l3["config"]["workload"]
+        a1 = copy.copy(args)
+        a1.workload, a1.steps, a1.warmup, a1.no_cpu_baseline = "model", 64, 3, True
+        l1 = run_cuda_model(a1, quiet=True)
+        extras["model"] = {k: l1[k] for k in ("metric", "value", "unit", "ms_per_step", "prompt_tok_s", "e2e",
+                                              "roofline", "generated_ids_head")}
+        extras["model"]["config"] = l1["config"]["workload"]
 
     if rank == 0:
         step_bytes = expert_bytes_per_token(lays)
@@ -498,7 +512,7 @@ def model_launches_per_step(n_layers):
     return 1 + n_layers * 17 + 5
 
 
-def run_cuda_model(args):
+def run_cuda_model(args, quiet=False):
     import torch
     import torch.distributed as dist
 
@@ -630,10 +644,12 @@ def run_cuda_model(args):
             "clocks": clk,
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        if not quiet:
+            print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return line if rank == 0 else None
 
 
 def model_cpu_baseline(cfg, sample_layers=(0, 6), positions=64):
@@ -755,7 +771,7 @@ def workload_desc(args, n_layers, tokens, world):
     return d[args.workload]
 
 
-def run_cuda_batched(args, quiet=False):
+def run_cuda_batched(args, quiet=False, table=None):
     import datetime
 
     import torch
@@ -773,11 +789,13 @@ def run_cuda_batched(args, quiet=False):
     n_layers, n_tok = workload_shape(args)
     flags = rv.EXACT if args.exact else rv.TENSOR
     assert args.workload in ("prefill", "batch"), "config 4 runs through run_ep"
-    # On N>1 every rank runs an independent replica.
+    # On N>1 every rank runs an independent replica.  `table`: the decode
+    # run's table (the same seeds) to reuse.
     lays = [rv.qwen3_layer_layout(l) for l in range(n_layers)]
-    table = rv.ExpertTable(lays, device=dev)
-    for l in range(n_layers):
-        table.fill_synthetic(l, SEED + l, 0.02)
+    if table is None:
+        table = rv.ExpertTable(lays, device=dev)
+        for l in range(n_layers):
+            table.fill_synthetic(l, SEED + l, 0.02)
     zipf = args.workload in ("batch", "ep")
     routers_np = []
     for l in range(n_layers):
