@@ -276,11 +276,11 @@ RV_DEVFN long long rv_globaltimer() {
     const unsigned cta_ = blockIdx.x + gridDim.x * blockIdx.y;                               \
     if (threadIdx.x == 0 && cta_ < RV_PHASE_CTAS) g_rv_phase[k][cta_][i] = (long long)clock64(); \
   } while (0)
-// Per-stage event trace of one CTA (blockIdx.x == 0, blockIdx.y == 20):
-// row `stage` of kernel slot k.
+// Per-stage event trace of one CTA of a one-dimensional grid (blockIdx.x ==
+// 20): row `stage` of kernel slot k.
 #define RV_TRACE(k, stage, ev)                                                          \
   do {                                                                                 \
-    if (blockIdx.x == 0 && blockIdx.y == 20 && (stage) < RV_PHASE_CTAS)                \
+    if (blockIdx.x == 20 && blockIdx.y == 0 && (stage) < RV_PHASE_CTAS)                \
       g_rv_phase[k][stage][ev] = rv_globaltimer();                                     \
   } while (0)
 // Event ev of the decode routing tail (the last routing CTA, thread 0).

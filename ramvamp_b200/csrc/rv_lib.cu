@@ -1252,8 +1252,15 @@ static int launch_tc_gemm(const MoeDims &d, const MoeBufs &B, const MoeWeights &
   const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
   const size_t smem = TcCfg<FMT, DOWN>::total(rb, (DOWN ? d.M : d.H) / 256);
   RV_CUDA(cudaFuncSetAttribute(k_tc_gemm<FMT, DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const unsigned gx = DOWN ? (unsigned)(d.H / RV_TC_ROWS) : (unsigned)(2 * d.M / RV_TC_ROWS);
-  k_tc_gemm<FMT, DOWN><<<dim3(gx, (unsigned)B.max_tc), RV_TC_THREADS, smem, s>>>(d, B, W, map);
+  const size_t nrt = DOWN ? (size_t)(d.H / RV_TC_ROWS) : (size_t)(2 * d.M / RV_TC_ROWS);
+  // Persistent: one CTA per SM walks the (row tile, pair tile) work items;
+  // the count of pair tiles is the device's (k_tc_tiles), the capacity
+  // bounds the grid.
+  int dev = 0;
+  RV_CUDA(cudaGetDevice(&dev));
+  const size_t sms = g_dev_sms[dev] > 0 ? (size_t)g_dev_sms[dev] : 148;
+  const unsigned grid = (unsigned)std::min(sms, nrt * (size_t)B.max_tc);
+  k_tc_gemm<FMT, DOWN><<<grid, RV_TC_THREADS, smem, s>>>(d, B, W, map);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     cudaFuncAttributes fa = {};
@@ -1321,7 +1328,8 @@ static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
     CUtensorMap gmap;
     if ((rc = gate_up_map(W, L, &gmap))) return rc;
     if (B.tc_a) {
-      const dim3 g((unsigned)(2 * d.M / RV_TC_ROWS), (unsigned)(2 * d.hb), (unsigned)d.E);
+      const int spb = 4 / (L.gate_format == RV_Q4_K ? TcStage<RV_Q4_K, false>::SUB : TcStage<RV_Q5_K, false>::SUB);
+      const dim3 g((unsigned)(2 * d.M / RV_TC_ROWS), (unsigned)(spb * d.hb), (unsigned)d.E);
       if (L.gate_format == RV_Q4_K) k_tc_predeq<RV_Q4_K, false><<<g, 256, 0, s>>>(d, B, W);
       else k_tc_predeq<RV_Q5_K, false><<<g, 256, 0, s>>>(d, B, W);
       RV_LAUNCH_CHECK();
@@ -1334,9 +1342,15 @@ static int expert_stage(const MoeDims &d, const MoeBufs &B, const MoeWeights &W,
     if (B.tc_a) {  // after the gate/up GEMM: the cache now takes the down stages
       const unsigned gx = (unsigned)(d.H / RV_TC_ROWS);
       switch (L.down_format) {
-        case RV_Q4_K: k_tc_predeq<RV_Q4_K, true><<<dim3(gx, 2 * d.mb, d.E), 256, 0, s>>>(d, B, W); break;
-        case RV_Q5_K: k_tc_predeq<RV_Q5_K, true><<<dim3(gx, 2 * d.mb, d.E), 256, 0, s>>>(d, B, W); break;
-        default: k_tc_predeq<RV_Q6_K, true><<<dim3(gx, 4 * d.mb, d.E), 256, 0, s>>>(d, B, W); break;
+        case RV_Q4_K:
+          k_tc_predeq<RV_Q4_K, true><<<dim3(gx, 4 / TcStage<RV_Q4_K, true>::SUB * d.mb, d.E), 256, 0, s>>>(d, B, W);
+          break;
+        case RV_Q5_K:
+          k_tc_predeq<RV_Q5_K, true><<<dim3(gx, 4 / TcStage<RV_Q5_K, true>::SUB * d.mb, d.E), 256, 0, s>>>(d, B, W);
+          break;
+        default:
+          k_tc_predeq<RV_Q6_K, true><<<dim3(gx, 4 / TcStage<RV_Q6_K, true>::SUB * d.mb, d.E), 256, 0, s>>>(d, B, W);
+          break;
       }
       RV_LAUNCH_CHECK();
     }

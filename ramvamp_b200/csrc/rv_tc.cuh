@@ -70,6 +70,12 @@ RV_DEVFN void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
 }
+// 4 consecutive f32 columns of this thread's tensor-memory lane.
+RV_DEVFN void tc_ld4(uint32_t taddr, uint32_t (&v)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(taddr));
+}
 // 8 consecutive f32 columns of this thread's tensor-memory lane.
 RV_DEVFN void tc_ld8(uint32_t taddr, uint32_t (&v)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
@@ -382,11 +388,25 @@ struct TcCfg {
                 : (((size_t)RV_TC_ROWS * TcFmt<FMT>::BB + 1023) & ~(size_t)1023);
   }
   __host__ __device__ static size_t ring(size_t rb) { return raw + R * raw_slot(rb); }
+  // The epilogue's per-work-item buffers of activation scales ([nb][NT]
+  // floats) and down pair ids ([NT]): nbuf(nb) of them, used in turn.  A
+  // warp starting item j has seen all eight warps release the accumulator
+  // of super-block F_j - 3 (F_j: item j's first), so no warp still reads
+  // the buffers of an item older than the one holding that super-block:
+  // nbuf must exceed ceil(3 / nb).
+  __host__ __device__ static int da_cols(int nb) { return 2 * nb > 8 ? 2 * nb : 8; }
+  __host__ __device__ static int nbuf(int nb) { return da_cols(nb) / nb; }
   __host__ __device__ static size_t da(size_t rb) { return ring(rb) + RING; }
-  __host__ __device__ static size_t pair(size_t rb, int nb) { return da(rb) + (size_t)RV_TC_NT * nb * 4; }
-  __host__ __device__ static size_t bars(size_t rb, int nb) { return pair(rb, nb) + RV_TC_NT * 4; }
+  __host__ __device__ static size_t pair(size_t rb, int nb) { return da(rb) + (size_t)RV_TC_NT * da_cols(nb) * 4; }
+  __host__ __device__ static size_t bars(size_t rb, int nb) {
+    return pair(rb, nb) + (DOWN ? (size_t)nbuf(nb) * RV_TC_NT * 4 : 0);
+  }
   static constexpr int NBARS = 2 * R + 2 * SA + 2 * SBMAX + 4;
-  __host__ __device__ static size_t total(size_t rb, int nb) { return 1024 + bars(rb, nb) + NBARS * 8 + 16; }
+  // After the barriers: tensor-memory address, failure flag, padding, and
+  // the activation ring's stage offsets and lengths ([SBMAX] each).
+  __host__ __device__ static size_t total(size_t rb, int nb) {
+    return 1024 + bars(rb, nb) + NBARS * 8 + 16 + 2 * SBMAX * 4;
+  }
 };
 
 // Warp-uniform wait of the dequantizing / draining warps (backing off
@@ -488,16 +508,55 @@ __global__ void __launch_bounds__(256) k_tc_predeq(MoeDims d, MoeBufs B, MoeWeig
   }
 }
 
-// One pair tile x 128 weight rows of one matrix.  Gate/up (DOWN = false):
-// grid.x = 2*M/128 row tiles (gate tiles first), output rows of gu
-// [pos][gate M | up M]; the raw super-blocks arrive one 128-row x 1-block
-// box per block through `wmap` (the layer's [E][gate|up][M][row bytes]
-// slabs).  Down: grid.x = H/128, the whole contiguous 128-row tile in one
-// bulk copy, output staged by (token, slot).  grid.y = max_tc pair tiles.
-// Roles: warp 0 lane 0 stages weights and lane 1 activations, warp 1 lane
-// 0 issues the MMAs, eight warps dequantize (two threads per weight row),
-// eight warps drain each super-block's accumulators out of tensor memory
-// while the next block multiplies (the epilogue), two warps idle.
+// Work items of the tensor GEMM: (row tile rt, pair tile u) numbered
+// w = u * nrt + rt, so the CTAs running at one time share pair tiles (the
+// same activation stages) and experts (the same weight stages) in L2.
+struct TcTile {
+  int e, rt, p0, n, pp0, nmma, mat, row0;
+  bool apre;  // the expert's weight stages come from the cache (k_tc_predeq)
+  const uint8_t *wsrc;
+};
+template <bool DOWN>
+RV_DEVFN TcTile tc_tile(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int w, int nrt, size_t rb) {
+  TcTile t;
+  const int u = w / nrt;
+  t.rt = w - u * nrt;
+  const int4 tl = B.tc_units[u];
+  t.e = tl.x;
+  t.p0 = tl.y;
+  t.n = tl.z - tl.y;
+  t.pp0 = tl.w;
+  t.nmma = (t.n + 15) & ~15;
+  t.apre = B.tc_a != nullptr && B.tc_apre[t.e] != 0;
+  if constexpr (DOWN) {
+    t.mat = 0;
+    t.row0 = t.rt * RV_TC_ROWS;
+  } else {
+    const int rtm = d.M / RV_TC_ROWS;
+    t.mat = t.rt / rtm;
+    t.row0 = (t.rt % rtm) * RV_TC_ROWS;
+  }
+  t.wsrc = W.base + (size_t)t.e * W.stride + (DOWN ? W.down_off : t.mat ? W.up_off : W.gate_off) + (size_t)t.row0 * rb;
+  return t;
+}
+
+// The GEMM as a persistent kernel: one CTA per SM walks the work items
+// w = blockIdx.x, blockIdx.x + gridDim.x, ... of 128 weight rows x one pair
+// tile of one matrix.  Gate/up (DOWN = false): nrt = 2*M/128 row tiles
+// (gate tiles first), output rows of gu [pos][gate M | up M]; the raw
+// super-blocks arrive one 128-row x 1-block box per block through `wmap`
+// (the layer's [E][gate|up][M][row bytes] slabs).  Down: nrt = H/128, the
+// whole contiguous 128-row tile in one bulk copy, output staged by (token,
+// slot).  Roles: warp 0 lane 0 stages raw weights and lane 1 activations,
+// warp 1 lane 0 issues the MMAs, eight warps fill the A stages (dequantized
+// here, or copied from the cache), eight warps drain each super-block's
+// accumulators out of tensor memory while the next block multiplies (the
+// epilogue), two warps idle.  Every ring (raw weights, A stages, activation
+// stages, the two accumulator slots) runs on across work items, so one
+// item's staging and products overlap the previous item's epilogue; each
+// ring has a single filling party, which waits on every phase in order (a
+// parity wait cannot tell phase k from phase k + 2).  The activation ring
+// hands out byte ranges, so items of different widths share it.
 template <int FMT, bool DOWN>
 __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     k_tc_gemm(MoeDims d, MoeBufs B, MoeWeights W, const __grid_constant__ CUtensorMap wmap) {
@@ -505,46 +564,29 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   using SL = TcStage<FMT, DOWN>;
   using C = TcCfg<FMT, DOWN>;
   constexpr int BB = F::BB, SA = C::SA, R = C::R, SUB = SL::SUB, SPB = 4 / SUB;  // stages per super-block
+  constexpr int SBM = C::SBMAX;
   extern __shared__ __align__(16) uint8_t sm_raw_[];
   uint8_t *sm = (uint8_t *)(((uintptr_t)sm_raw_ + 1023) & ~(uintptr_t)1023);
-  const int u = blockIdx.y;
-  if (u >= *B.n_tc) return;
   constexpr int PK = DOWN ? 2 : 1;
   (void)PK;
   RV_PHASE(PK, 0);
-  const int4 tile = B.tc_units[u];
-  const int e = tile.x, p0 = tile.y, n = tile.z - tile.y, pp0 = tile.w;
-  // apre: this expert's weight stages were dequantized by k_tc_predeq and
-  // arrive by bulk copy; the dequantizing warps stay idle.
-  const bool apre = B.tc_a != nullptr && B.tc_apre[e] != 0;
-  const int nmma = (n + 15) & ~15, ng = nmma / 8, g0 = pp0 / 8;
   const int kdim = DOWN ? d.M : d.H, nb = kdim / 256, NS = SPB * nb;
+  const int nrt = DOWN ? d.H / RV_TC_ROWS : 2 * d.M / RV_TC_ROWS;
+  const int nwork = nrt * *B.n_tc;
+  if ((int)blockIdx.x >= nwork) return;
   const size_t rb = DOWN ? W.down_row_bytes : W.gu_row_bytes;
-  const size_t sub_b = (size_t)nmma * 128;  // one 64-K sub-stage of B (whole 1 KB atoms)
-  const size_t slot_b = ((size_t)SUB * sub_b + (F::MINS ? (size_t)nmma * 32 : 0) + 1023) & ~(size_t)1023;
-  const int SB = min(C::SBMAX, (int)(C::RING / slot_b));
-  int mat = 0, row0;
-  if constexpr (DOWN) {
-    row0 = blockIdx.x * RV_TC_ROWS;
-  } else {
-    const int rtm = d.M / RV_TC_ROWS;
-    mat = blockIdx.x / rtm;
-    row0 = (blockIdx.x % rtm) * RV_TC_ROWS;
-  }
-  const uint8_t *wsrc = W.base + (size_t)e * W.stride + (DOWN ? W.down_off : mat ? W.up_off : W.gate_off) +
-                        (size_t)row0 * rb;
   const uint8_t *bq = (const uint8_t *)(DOWN ? B.hq : B.xq), *bm = (const uint8_t *)(DOWN ? B.hm : B.xm);
   const float *bd = DOWN ? B.hdsc : B.xd;
   const size_t rslot = C::raw_slot(rb);
   uint8_t *raw = sm + C::raw, *ring = sm + C::ring(rb);
-  float *s_da = (float *)(sm + C::da(rb));
-  uint32_t *s_pair = (uint32_t *)(sm + C::pair(rb, nb));
+  float *s_da = (float *)(sm + C::da(rb));                // [nbuf][nb][NT], one per work item in turn
+  uint32_t *s_pair = (uint32_t *)(sm + C::pair(rb, nb));  // [nbuf][NT] (down)
   uint64_t *bars = (uint64_t *)(sm + C::bars(rb, nb));
   uint64_t *raw_full = bars, *raw_empty = bars + R, *a_full = bars + 2 * R, *a_empty = a_full + SA,
-           *b_full = a_empty + SA, *b_empty = b_full + C::SBMAX, *acc_full = b_empty + C::SBMAX,
-           *acc_empty = acc_full + 2;
+           *b_full = a_empty + SA, *b_empty = b_full + SBM, *acc_full = b_empty + SBM, *acc_empty = acc_full + 2;
   uint32_t *s_tmem = (uint32_t *)(bars + C::NBARS);
   volatile int *s_fail = (volatile int *)(s_tmem + 1);
+  uint32_t *s_boff = s_tmem + 4, *s_blen = s_boff + SBM;  // activation stage byte ranges in the ring
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < R; i++) {
@@ -552,10 +594,10 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
       mbar_init(&raw_empty[i], RV_TC_PROD_WARPS);
     }
     for (int i = 0; i < SA; i++) {
-      mbar_init(&a_full[i], apre ? 1 : RV_TC_PROD_WARPS);
+      mbar_init(&a_full[i], RV_TC_PROD_WARPS);
       mbar_init(&a_empty[i], 1);
     }
-    for (int i = 0; i < C::SBMAX; i++) {
+    for (int i = 0; i < SBM; i++) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
     }
@@ -565,9 +607,6 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     }
     *s_fail = 0;
   }
-  for (int i = threadIdx.x; i < nmma * nb; i += blockDim.x) s_da[i] = bd[(size_t)pp0 * nb + i];
-  if (DOWN)
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s_pair[i] = B.index[p0 + i];
   __syncwarp();
   if (warp == 0) {
     tc_alloc(s_tmem, 4 * RV_TC_NT);
@@ -582,65 +621,99 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------- weight staging
+      // Raw weights of the work items whose stages are not in the cache;
+      // the A stages themselves are the producer warps' (below).
       bool ok = true;
-      if (apre) {
-        const uint8_t *asrc = B.tc_a + ((size_t)e * gridDim.x + blockIdx.x) * NS * SL::bytes;
-        for (int it = 0; it < NS; it++) {
-          const int sa = it % SA;
-          if (!mbar_wait_bounded(&a_empty[sa], ((it / SA) & 1) ^ 1, 128)) {
+      int graw = 0, gdraw = 0;  // raw gate/up blocks, raw down tiles so far
+      for (int w = blockIdx.x; w < nwork && ok && !*s_fail; w += gridDim.x) {
+        const TcTile t = tc_tile<DOWN>(d, B, W, w, nrt, rb);
+        if (t.apre) continue;
+        if constexpr (DOWN) {
+          if (!mbar_wait_bounded(&raw_empty[0], (gdraw & 1) ^ 1, 128)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&a_full[sa], (uint32_t)SL::bytes);
-          for (size_t o = 0; o < SL::bytes; o += 32768)
-            bulk_g2s(sm + (size_t)sa * SL::bytes + o, asrc + (size_t)it * SL::bytes + o,
-                     (uint32_t)(SL::bytes - o < 32768 ? SL::bytes - o : 32768), &a_full[sa]);
-        }
-      } else if constexpr (DOWN) {
-        const size_t tb = (size_t)RV_TC_ROWS * rb;
-        mbar_arrive_expect_tx(&raw_full[0], (uint32_t)tb);
-        for (size_t o = 0; o < tb; o += 32768)
-          bulk_g2s(raw + o, wsrc + o, (uint32_t)(tb - o < 32768 ? tb - o : 32768), &raw_full[0]);
-      } else {
-        // The tile's rows are contiguous: ask the L2 for all of them now so
-        // each super-block's box below comes from L2, not HBM.
-        const uint32_t tile_b = (uint32_t)(RV_TC_ROWS * rb);
-        for (uint32_t o = 0; o < tile_b; o += 32768)
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(wsrc + o),
-                       "r"(tile_b - o < 32768u ? tile_b - o : 32768u)
-                       : "memory");
-        for (int b = 0; b < nb; b++) {
-          const int slot = b % R;
-          if (!mbar_wait_bounded(&raw_empty[slot], ((b / R) & 1) ^ 1, 128)) {
-            ok = false;
-            break;
+          gdraw++;
+          const size_t tb = (size_t)RV_TC_ROWS * rb;
+          mbar_arrive_expect_tx(&raw_full[0], (uint32_t)tb);
+          for (size_t o = 0; o < tb; o += 32768)
+            bulk_g2s(raw + o, t.wsrc + o, (uint32_t)(tb - o < 32768 ? tb - o : 32768), &raw_full[0]);
+        } else {
+          // The tile's rows are contiguous: ask the L2 for all of them now so
+          // each super-block's box below comes from L2, not HBM.
+          const uint32_t tile_b = (uint32_t)(RV_TC_ROWS * rb);
+          for (uint32_t o = 0; o < tile_b; o += 32768)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(t.wsrc + o),
+                         "r"(tile_b - o < 32768u ? tile_b - o : 32768u)
+                         : "memory");
+          for (int b = 0; b < nb; b++, graw++) {
+            const int slot = graw % R;
+            if (!mbar_wait_bounded(&raw_empty[slot], ((graw / R) & 1) ^ 1, 128)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(RV_TC_ROWS * BB));
+            tma_load_4d(raw + slot * rslot, &wmap, b * BB, t.row0, t.mat, t.e, &raw_full[slot]);
+            RV_TRACE(PK + 2, graw, 6);
           }
-          mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(RV_TC_ROWS * BB));
-          tma_load_4d(raw + slot * rslot, &wmap, b * BB, row0, mat, e, &raw_full[slot]);
-          RV_TRACE(PK + 2, SPB * b, 6);
-          if (b == 0) RV_PHASE_ANY(PK, 2);
         }
+        RV_PHASE_ANY(PK, 2);
       }
       if (!ok) *s_fail = 1;
     } else if (lane == 1) {
       // ------------------------------------------ activation staging
+      // Stage gb takes barrier pair gb % SBM and a byte range of the ring;
+      // ranges are released in order (the MMAs consume stages in order), so
+      // the ring is a queue: `used` bytes from the oldest unreleased stage
+      // `tail` up to `head`, plus any end gap skipped when a range wrapped.
       bool ok = true;
-      for (int it = 0; it < NS; it++) {
-        const int sb = it % SB;
-        if (!mbar_wait_bounded(&b_empty[sb], ((it / SB) & 1) ^ 1, 128)) {
-          ok = false;
-          break;
+      int gb = 0, tail = 0;
+      uint32_t head = 0, used = 0;
+      for (int w = blockIdx.x; w < nwork && ok && !*s_fail; w += gridDim.x) {
+        const TcTile t = tc_tile<DOWN>(d, B, W, w, nrt, rb);
+        const int ng = t.nmma / 8, g0 = t.pp0 / 8;
+        const uint32_t sub_b = (uint32_t)t.nmma * 128;  // one 64-K sub-stage (whole 1 KB atoms)
+        for (int it = 0; it < NS; it++, gb++) {
+          const bool mins = F::MINS && (it % SPB) == 0;
+          const uint32_t sz = (SUB * sub_b + (mins ? (uint32_t)t.nmma * 32 : 0u) + 1023u) & ~1023u;
+          uint32_t off = 0;
+          for (;;) {
+            if (gb - tail < SBM) {
+              if (gb == tail) head = used = 0;
+              const uint32_t fr = (uint32_t)C::RING - used, gap = (uint32_t)C::RING - head;
+              if (sz <= gap && sz <= fr) {
+                off = head;
+                s_blen[gb % SBM] = sz;
+                break;
+              }
+              if (sz > gap && sz + gap <= fr) {
+                off = 0;
+                s_blen[gb % SBM] = sz + gap;
+                break;
+              }
+            }
+            if (!mbar_wait_bounded(&b_empty[tail % SBM], (tail / SBM) & 1, 128)) {
+              ok = false;
+              break;
+            }
+            used -= s_blen[tail % SBM];
+            tail++;
+          }
+          if (!ok) break;
+          const int sb = gb % SBM;
+          used += s_blen[sb];
+          head = off + sz;
+          s_boff[sb] = off;
+          RV_TRACE(PK + 2, gb, 5);
+          uint8_t *dst = ring + off;
+          mbar_arrive_expect_tx(&b_full[sb], (uint32_t)(SUB * ng * 1024 + (mins ? ng * 256 : 0)));
+          for (int u = 0; u < SUB; u++)
+            bulk_g2s(dst + u * sub_b, bq + ((size_t)(SUB * it + u) * B.tc_groups + g0) * 1024, (uint32_t)(ng * 1024),
+                     &b_full[sb]);
+          if (mins)
+            bulk_g2s(dst + SUB * sub_b, bm + ((size_t)(it / SPB) * B.tc_groups + g0) * 256, (uint32_t)(ng * 256),
+                     &b_full[sb]);
         }
-        const bool mins = F::MINS && (it % SPB) == 0;
-        RV_TRACE(PK + 2, it, 5);
-        uint8_t *dst = ring + sb * slot_b;
-        mbar_arrive_expect_tx(&b_full[sb], (uint32_t)(SUB * ng * 1024 + (mins ? ng * 256 : 0)));
-        for (int u = 0; u < SUB; u++)
-          bulk_g2s(dst + u * sub_b, bq + ((size_t)(SUB * it + u) * B.tc_groups + g0) * 1024, (uint32_t)(ng * 1024),
-                   &b_full[sb]);
-        if (mins)
-          bulk_g2s(dst + SUB * sub_b, bm + ((size_t)(it / SPB) * B.tc_groups + g0) * 256, (uint32_t)(ng * 256),
-                   &b_full[sb]);
       }
       if (!ok) *s_fail = 1;
     }
@@ -650,117 +723,152 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     if (lane == 0) {
       // The issue loop is kept short: this warp shares its scheduler with
       // four dequantizing warps.  Descriptor words are formed by adding
-      // 16-byte units to precomputed low words; ring positions and phases
-      // advance without division.
-      const uint32_t idesc = tc_idesc(nmma);
+      // 16-byte units to precomputed low words.
       // A and B tiles: 128-byte swizzle, SBO 1024 (K advances 32 bytes per
       // K=16 step inside the swizzled row); mins tiles: no swizzle, LBO 128,
       // SBO 256.
       const uint32_t hi_sw = (1024u >> 4) | (1u << 14) | (2u << 29), hi256 = (256u >> 4) | (1u << 14);
       const uint32_t lbo_sw = 1u << 16, lbo_none = (128u >> 4) << 16;
       const uint32_t a_lo0 = smem_addr(sm) >> 4, b_lo0 = smem_addr(ring) >> 4;
-      const uint32_t b_step = (uint32_t)(slot_b >> 4), a_step = (uint32_t)(SL::bytes >> 4);
+      const uint32_t a_step = (uint32_t)(SL::bytes >> 4);
       auto mk = [](uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; };
-      int sa = 0, sb = 0;
-      uint32_t pa = 0, pb = 0;
+      int ga = 0, gb = 0, gsb = 0;
       bool ok = true;
-      for (int b = 0; b < nb && ok; b++) {
-        const int slot = b & 1;
-        if (!mbar_wait_bounded(&acc_empty[slot], ((b >> 1) & 1) ^ 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d1 = tmem + (uint32_t)(slot * 2 * RV_TC_NT), d2 = d1 + RV_TC_NT;
-        for (int j = 0; j < SPB; j++) {
-          const int it = SPB * b + j;
-          if (!mbar_wait_bounded(&a_full[sa], pa)) {
+      for (int w = blockIdx.x; w < nwork && ok && !*s_fail; w += gridDim.x) {
+        const TcTile t = tc_tile<DOWN>(d, B, W, w, nrt, rb);
+        const uint32_t idesc = tc_idesc(t.nmma), sub_b = (uint32_t)t.nmma * 128;
+        for (int b = 0; b < nb && ok; b++, gsb++) {
+          const int slot = gsb & 1;
+          if (!mbar_wait_bounded(&acc_empty[slot], ((gsb >> 1) & 1) ^ 1)) {
             ok = false;
             break;
           }
-          RV_TRACE(PK + 2, it, 2);
-          if (!mbar_wait_bounded(&b_full[sb], pb)) {
-            ok = false;
-            break;
-          }
-          RV_TRACE(PK + 2, it, 3);
           tc_fence_after();
-          if (it == 0) RV_PHASE_ANY(PK, 3);
-          const uint32_t al = a_lo0 + (uint32_t)sa * a_step, bl = b_lo0 + (uint32_t)sb * b_step;
-          if (F::MINS && j == 0)
-            tc_mma_f16(d2, mk(lbo_none | (al + (uint32_t)(SL::a2 >> 4)), hi256),
-                       mk(lbo_none | (bl + (uint32_t)(SUB * sub_b >> 4)), hi256), idesc, 0u);
-#pragma unroll
-          for (int u = 0; u < SUB; u++) {
-            const uint32_t au = al + (uint32_t)(u * RV_TC_ROWS * 128 >> 4), bu = bl + (uint32_t)(u * sub_b >> 4);
-#pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-              const uint32_t acc = (j | u | kk) != 0;
-              tc_mma_f16(d1, mk(lbo_sw | (au + 2 * kk), hi_sw), mk(lbo_sw | (bu + 2 * kk), hi_sw), idesc, acc);
-              if (F::SPLIT)
-                tc_mma_f16(d2, mk(lbo_sw | (au + (uint32_t)(SL::ah >> 4) + 2 * kk), hi_sw),
-                           mk(lbo_sw | (bu + 2 * kk), hi_sw), idesc, acc);
+          const uint32_t d1 = tmem + (uint32_t)(slot * 2 * RV_TC_NT), d2 = d1 + RV_TC_NT;
+          for (int j = 0; j < SPB; j++, ga++, gb++) {
+            const int sa = ga % SA, sb = gb % SBM;
+            if (!mbar_wait_bounded(&a_full[sa], (ga / SA) & 1)) {
+              ok = false;
+              break;
             }
+            RV_TRACE(PK + 2, ga, 2);
+            if (!mbar_wait_bounded(&b_full[sb], (gb / SBM) & 1)) {
+              ok = false;
+              break;
+            }
+            RV_TRACE(PK + 2, ga, 3);
+            tc_fence_after();
+            if (gsb == 0 && j == 0) RV_PHASE_ANY(PK, 3);
+            const uint32_t al = a_lo0 + (uint32_t)sa * a_step, bl = b_lo0 + (s_boff[sb] >> 4);
+            if (F::MINS && j == 0)
+              tc_mma_f16(d2, mk(lbo_none | (al + (uint32_t)(SL::a2 >> 4)), hi256),
+                         mk(lbo_none | (bl + (uint32_t)(SUB * sub_b >> 4)), hi256), idesc, 0u);
+#pragma unroll
+            for (int u = 0; u < SUB; u++) {
+              const uint32_t au = al + (uint32_t)(u * RV_TC_ROWS * 128 >> 4), bu = bl + (uint32_t)(u * sub_b >> 4);
+#pragma unroll
+              for (int kk = 0; kk < 4; kk++) {
+                const uint32_t acc = (j | u | kk) != 0;
+                tc_mma_f16(d1, mk(lbo_sw | (au + 2 * kk), hi_sw), mk(lbo_sw | (bu + 2 * kk), hi_sw), idesc, acc);
+                if (F::SPLIT)
+                  tc_mma_f16(d2, mk(lbo_sw | (au + (uint32_t)(SL::ah >> 4) + 2 * kk), hi_sw),
+                             mk(lbo_sw | (bu + 2 * kk), hi_sw), idesc, acc);
+              }
+            }
+            RV_TRACE(PK + 2, ga, 9);
+            tc_commit(&a_empty[sa]);
+            tc_commit(&b_empty[sb]);
+            RV_TRACE(PK + 2, ga, 4);
           }
-          RV_TRACE(PK + 2, it, 9);
-          tc_commit(&a_empty[sa]);
-          tc_commit(&b_empty[sb]);
-          RV_TRACE(PK + 2, it, 4);
-          if (++sa == SA) {
-            sa = 0;
-            pa ^= 1;
-          }
-          if (++sb == SB) {
-            sb = 0;
-            pb ^= 1;
-          }
+          if (!ok) break;
+          tc_commit(&acc_full[slot]);
         }
-        tc_commit(&acc_full[slot]);
       }
       RV_PHASE_ANY(PK, 4);
       if (!ok) *s_fail = 1;
     }
     __syncwarp();
-  } else if (tc_prod_index(warp) >= 0 && !apre) {
+  } else if (tc_prod_index(warp) >= 0) {
     // ------------------------------------------------------ producers
-    // Thread p: weight row p & 127, half p >> 7 of every stage.
-    const int p = 32 * tc_prod_index(warp) + lane, r = p & 127, h = p >> 7;
-    bool ok = true;
-    if (DOWN) ok = tc_wait_warp(&raw_full[0], 0);
-    uint32_t u0 = 0, u1 = 0, u2 = 0, u3 = 0;
-    for (int it = 0; it < NS && ok; it++) {
-      const int b = it / SPB, js = it % SPB, sa = it % SA;
-      if (!DOWN && js == 0 && !tc_wait_warp(&raw_full[b % R], (b / R) & 1)) {
-        ok = false;
-        break;
+    // Every A stage of every work item.  Uncached items: thread p
+    // dequantizes weight row p & 127, half p >> 7 of each stage.  Cached
+    // items (k_tc_predeq wrote the stages): the first producer warp's lane 0
+    // copies each stage in with bulk copies and the other warps arrive.
+    const int pi = tc_prod_index(warp), p = 32 * pi + lane, r = p & 127, h = p >> 7;
+    bool ok = true, first = true;
+    int ga = 0, graw = 0, gdraw = 0;
+    for (int w = blockIdx.x; w < nwork && ok && !*s_fail; w += gridDim.x) {
+      const TcTile t = tc_tile<DOWN>(d, B, W, w, nrt, rb);
+      if (t.apre) {
+        const uint8_t *asrc = B.tc_a + ((size_t)t.e * nrt + t.rt) * NS * SL::bytes;
+        for (int it = 0; it < NS; it++, ga++) {
+          const int sa = ga % SA;
+          if (!tc_wait_warp(&a_empty[sa], ((ga / SA) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            if (pi == 0) {
+              mbar_arrive_expect_tx(&a_full[sa], (uint32_t)SL::bytes);
+              for (size_t o = 0; o < SL::bytes; o += 32768)
+                bulk_g2s(sm + (size_t)sa * SL::bytes + o, asrc + (size_t)it * SL::bytes + o,
+                         (uint32_t)(SL::bytes - o < 32768 ? SL::bytes - o : 32768), &a_full[sa]);
+            } else {
+              mbar_arrive(&a_full[sa]);
+            }
+          }
+          __syncwarp();
+          if (p == 0) RV_TRACE(PK + 2, ga, 0);
+        }
+        continue;
       }
-      if (p == 0 && js == 0) RV_TRACE(PK + 2, it, 8);
-      const uint8_t *blk = DOWN ? raw + (size_t)r * rb + (size_t)b * BB : raw + (b % R) * rslot + (size_t)r * BB;
-      if (F::MINS && js == 0) {
-        const uint4 hdr = *(const uint4 *)blk;
-        k4_unpack_words(hdr.y, hdr.z, hdr.w, u0, u1, u2, u3);
+      if (DOWN) {
+        ok = tc_wait_warp(&raw_full[0], gdraw & 1);
+        if (!ok) break;
       }
-      if (!tc_wait_warp(&a_empty[sa], ((it / SA) & 1) ^ 1)) {
-        ok = false;
-        break;
-      }
-      if (it == 0 && p == 0) RV_PHASE_ANY(PK, 5);
-      if (p == 0) RV_TRACE(PK + 2, it, 0);
-      uint8_t *st = sm + (size_t)sa * SL::bytes;
+      uint32_t u0 = 0, u1 = 0, u2 = 0, u3 = 0;
+      for (int it = 0; it < NS; it++, ga++) {
+        const int b = it / SPB, js = it % SPB, sa = ga % SA;
+        if (!DOWN && js == 0 && !tc_wait_warp(&raw_full[graw % R], (graw / R) & 1)) {
+          ok = false;
+          break;
+        }
+        if (p == 0 && js == 0) RV_TRACE(PK + 2, ga, 8);
+        const uint8_t *blk = DOWN ? raw + (size_t)r * rb + (size_t)b * BB : raw + (graw % R) * rslot + (size_t)r * BB;
+        if (F::MINS && js == 0) {
+          const uint4 hdr = *(const uint4 *)blk;
+          k4_unpack_words(hdr.y, hdr.z, hdr.w, u0, u1, u2, u3);
+        }
+        if (!tc_wait_warp(&a_empty[sa], ((ga / SA) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        if (first && p == 0) RV_PHASE_ANY(PK, 5);
+        first = false;
+        if (p == 0) RV_TRACE(PK + 2, ga, 0);
+        uint8_t *st = sm + (size_t)sa * SL::bytes;
 #pragma unroll
-      for (int u = 0; u < SUB; u++) {
-        const int j = SUB * js + u;  // 64-element stage of the super-block
-        uint8_t *a_sub = st + SL::a + (size_t)u * RV_TC_ROWS * 128;
-        if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, h, a_sub, st + SL::ah + (size_t)u * RV_TC_ROWS * 128, r);
-        else tc_stage_k45<FMT>(blk, j, h, u0, u1, u2, u3, a_sub, st + SL::a2, r);
+        for (int u = 0; u < SUB; u++) {
+          const int j = SUB * js + u;  // 64-element stage of the super-block
+          uint8_t *a_sub = st + SL::a + (size_t)u * RV_TC_ROWS * 128;
+          if constexpr (FMT == RV_Q6_K) tc_stage_q6(blk, j, h, a_sub, st + SL::ah + (size_t)u * RV_TC_ROWS * 128, r);
+          else tc_stage_k45<FMT>(blk, j, h, u0, u1, u2, u3, a_sub, st + SL::a2, r);
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a_full[sa]);
+          if (!DOWN && js == SPB - 1) mbar_arrive(&raw_empty[graw % R]);
+        }
+        if (!DOWN && js == SPB - 1) graw++;
+        if (p == 0) RV_TRACE(PK + 2, ga, 1);
       }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[sa]);
-        if (!DOWN && js == SPB - 1) mbar_arrive(&raw_empty[b % R]);
+      if (!ok) break;
+      if (DOWN) {  // the raw tile may take the next uncached work item's weights
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[0]);
+        gdraw++;
       }
-      if (p == 0) RV_TRACE(PK + 2, it, 1);
     }
     if (p == 0) RV_PHASE_ANY(PK, 6);
     if (!ok) *s_fail = 1;
@@ -768,71 +876,101 @@ __global__ void __launch_bounds__(RV_TC_THREADS, 1)
     // ------------------------------------------------------- epilogue
     // Thread (quadrant q, lane) owns weight row 32q + lane (its tensor-
     // memory lane) and the 8-column chunks half, half+2, ..., half+14 of the
-    // tile, so small tiles spread over both warps of a quadrant.
+    // tile, so small tiles spread over both warps of a quadrant.  Each warp
+    // copies the activation scales (stored [nb][NT]) and, down, the pair ids
+    // of its own columns into the work item's buffer (C::nbuf of them, in
+    // turn); warps of the same half write the same values, and no warp
+    // still reads a buffer when it comes round again (TcCfg).  The 64
+    // running sums stay in registers, so tensor memory is read four columns
+    // at a time.
     const int q = warp & 3, half = (warp - RV_TC_W_EPI0) >> 2, er = 32 * q + lane;
-    const uint8_t *hrow = wsrc + (size_t)er * rb;  // the drained row's super-block headers (global)
-    float acc[8][8];
-#pragma unroll
-    for (int c = 0; c < 8; c++)
-#pragma unroll
-      for (int i = 0; i < 8; i++) acc[c][i] = 0.0f;
-    bool ok = true;
-    uint32_t hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + 208) : *(const uint32_t *)hrow;
-    for (int eb = 0; eb < nb; eb++) {
-      const int slot = eb & 1;
-      const uint32_t hdr = hdr_next;
-      if (eb + 1 < nb)
-        hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + (size_t)(eb + 1) * BB + 208)
-                                  : *(const uint32_t *)(hrow + (size_t)(eb + 1) * BB);
-      const float dw = h2f((uint16_t)(hdr & 0xFFFFu)), dmw = h2f((uint16_t)(hdr >> 16));
-      if (!tc_wait_warp(&acc_full[slot], (eb >> 1) & 1)) {
-        ok = false;
-        break;
+    const int nbuf = C::nbuf(nb);
+    bool ok = true, first = true;
+    int gsb = 0, bi = 0;
+    for (int w = blockIdx.x; w < nwork && ok && !*s_fail; w += gridDim.x, bi = bi + 1 == nbuf ? 0 : bi + 1) {
+      const TcTile t = tc_tile<DOWN>(d, B, W, w, nrt, rb);
+      float *da = s_da + (size_t)bi * RV_TC_NT * nb;
+      uint32_t *pr = s_pair + bi * RV_TC_NT;
+      for (int i = lane; i < 8 * 8 * nb; i += 32) {
+        const int c = i / (8 * nb), rest = i % (8 * nb), col = 8 * (half + 2 * c) + rest / nb;
+        if (col < t.nmma) da[(rest % nb) * RV_TC_NT + col] = bd[(size_t)(t.pp0 + col) * nb + rest % nb];
       }
-      tc_fence_after();
-      if (eb == 0 && warp == RV_TC_W_EPI0 && lane == 0) RV_PHASE_ANY(PK, 7);
-      if (warp == RV_TC_W_EPI0 && lane == 0) RV_TRACE(PK + 2, SPB * eb, 7);
-      const uint32_t t1 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(slot * 2 * RV_TC_NT);
+      if (DOWN)
+        for (int i = lane; i < 64; i += 32) {
+          const int col = 8 * (half + 2 * (i >> 3)) + (i & 7);
+          if (col < t.n) pr[col] = B.index[t.p0 + col];
+        }
+      __syncwarp();
+      const int nch = t.nmma > 8 * half ? (t.nmma - 8 * half + 15) / 16 : 0;  // this warp's chunks
+      const uint8_t *hrow = t.wsrc + (size_t)er * rb;  // the drained row's super-block headers (global)
+      float acc[8][8];
 #pragma unroll
-      for (int c = 0; c < 8; c++) {
-        const int col = 8 * (half + 2 * c);
-        if (col < nmma) {
-          uint32_t v1[8], v2[8];
-          tc_ld8(t1 + (uint32_t)col, v1);
-          tc_ld8(t1 + (uint32_t)(RV_TC_NT + col), v2);
-          tc_wait_ld();
+      for (int c = 0; c < 8; c++)
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const float da = s_da[(col + i) * nb + eb];
-            float blocksum;
-            if constexpr (FMT == RV_Q6_K) {
-              const int sumi = __float2int_rn(__uint_as_float(v1[i])) + 32 * __float2int_rn(__uint_as_float(v2[i]));
-              blocksum = __fmul_rn(__fmul_rn(dw, da), __int2float_rn(sumi));
-            } else {
-              const float dd = __fmul_rn(dw, da), dm = __fmul_rn(dmw, da);
-              blocksum = __fsub_rn(__fmul_rn(dd, __uint_as_float(v1[i])), __fmul_rn(dm, __uint_as_float(v2[i])));
+        for (int i = 0; i < 8; i++) acc[c][i] = 0.0f;
+      uint32_t hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + 208) : *(const uint32_t *)hrow;
+      for (int eb = 0; eb < nb; eb++, gsb++) {
+        const int slot = gsb & 1;
+        const uint32_t hdr = hdr_next;
+        if (eb + 1 < nb)
+          hdr_next = FMT == RV_Q6_K ? (uint32_t)ld16(hrow + (size_t)(eb + 1) * BB + 208)
+                                    : *(const uint32_t *)(hrow + (size_t)(eb + 1) * BB);
+        const float dw = h2f((uint16_t)(hdr & 0xFFFFu)), dmw = h2f((uint16_t)(hdr >> 16));
+        if (!tc_wait_warp(&acc_full[slot], (gsb >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (first && warp == RV_TC_W_EPI0 && lane == 0) RV_PHASE_ANY(PK, 7);
+        first = false;
+        if (warp == RV_TC_W_EPI0 && lane == 0) RV_TRACE(PK + 2, SPB * gsb, 7);
+        const uint32_t t1 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(slot * 2 * RV_TC_NT);
+        const float *dab = da + (size_t)eb * RV_TC_NT;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          if (c < nch) {
+            const int col = 8 * (half + 2 * c);
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+              uint32_t v1[4], v2[4];
+              tc_ld4(t1 + (uint32_t)(col + 4 * hh), v1);
+              tc_ld4(t1 + (uint32_t)(RV_TC_NT + col + 4 * hh), v2);
+              tc_wait_ld();
+#pragma unroll
+              for (int k = 0; k < 4; k++) {
+                const int i = 4 * hh + k;
+                const float dav = dab[col + i];
+                float blocksum;
+                if constexpr (FMT == RV_Q6_K) {
+                  const int sumi =
+                      __float2int_rn(__uint_as_float(v1[k])) + 32 * __float2int_rn(__uint_as_float(v2[k]));
+                  blocksum = __fmul_rn(__fmul_rn(dw, dav), __int2float_rn(sumi));
+                } else {
+                  const float dd = __fmul_rn(dw, dav), dm = __fmul_rn(dmw, dav);
+                  blocksum = __fsub_rn(__fmul_rn(dd, __uint_as_float(v1[k])), __fmul_rn(dm, __uint_as_float(v2[k])));
+                }
+                acc[c][i] = __fadd_rn(acc[c][i], blocksum);
+              }
             }
-            acc[c][i] = __fadd_rn(acc[c][i], blocksum);
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[slot]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[slot]);
-    }
-    if (warp == RV_TC_W_EPI0 && lane == 0) RV_PHASE_ANY(PK, 8);
-    if (ok && !*s_fail) {
+      if (!ok || *s_fail) break;
 #pragma unroll
       for (int c = 0; c < 8; c++)
 #pragma unroll
         for (int i = 0; i < 8; i++) {
           const int col = 8 * (half + 2 * c) + i;
-          if (col < n) {
-            if constexpr (DOWN) down_out_row(B, s_pair[col], d.H)[row0 + er] = acc[c][i];
-            else B.gu[(size_t)(p0 + col) * 2 * d.M + (size_t)mat * d.M + row0 + er] = acc[c][i];
+          if (col < t.n) {
+            if constexpr (DOWN) down_out_row(B, pr[col], d.H)[t.row0 + er] = acc[c][i];
+            else B.gu[(size_t)(t.p0 + col) * 2 * d.M + (size_t)t.mat * d.M + t.row0 + er] = acc[c][i];
           }
         }
     }
+    if (warp == RV_TC_W_EPI0 && lane == 0) RV_PHASE_ANY(PK, 8);
     if (!ok) *s_fail = 1;
   }
   tc_fence_before();

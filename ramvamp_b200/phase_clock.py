@@ -158,7 +158,7 @@ def tensor(tokens: int = 512) -> None:
         if rows.size == 0:
             continue
         t0 = b[rows][b[rows] > 0].min()
-        print(f"{name} CTA (0, 20), stage events (us):")
+        print(f"{name} CTA 20, stage events (us):")
         for st in rows[:16]:
             print(f"  stage {st:2d}: " + "  ".join(f"{ev[i]} {(b[st, i] - t0) / 1e3:.2f}" for i in range(PHASES)
                                                     if b[st, i]))
