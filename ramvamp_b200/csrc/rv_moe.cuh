@@ -1207,6 +1207,7 @@ RV_DEVFN bool gate_up_unit(const MoeDims &d, const MoeBufs &B, const MoeWeights 
         for (int m = 0; m < MT; m++)
           if (m < mm) gu[(part * R + r) * MT + m] = res[m];
       }
+      RV_PHASE(1, 5);
       __syncthreads();
       for (int i = threadIdx.x; i < R * mm; i += blockDim.x) {
         const int rr = i / mm, m = i % mm;
@@ -1412,6 +1413,7 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
         for (int m = 0; m < mt; m++) act_word_sums(asm_ + (size_t)m * d.amoe_stride, d.mb, asum + m * d.mb * 64);
         __syncwarp();
       }
+      RV_PHASE(2, 6);
       auto pair_of = [&](int c) -> uint32_t {
         if constexpr (SPEC) return s_pair[c - p0];
         else return B.index[c];
