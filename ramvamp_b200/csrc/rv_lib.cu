@@ -1152,8 +1152,7 @@ static int launch_route_chain(const MoeDims &d, const MoeBufs &B, int T, const M
 template <int FMT, int G, int NBG, int R, bool SPEC, int GEO>
 static void launch_gate_up_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int units, cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.gu_row_bytes : W.gu_row_bytes + 16;
-  const size_t smem = 16 + round16(2 * (size_t)R * st) + 16 + (size_t)B.ms * d.act_stride +
-                      (FMT == RV_Q6_K ? (size_t)B.ms * d.hb * 64 * 4 : 0) + 2 * R * RV_MOE_MT * 4;
+  const size_t smem = 16 + round16(2 * (size_t)R * st) + 16 + (size_t)B.ms * d.act_stride + 2 * R * RV_MOE_MT * 4;
   dim3 grid((unsigned)units, (unsigned)(d.M / R));
   cudaFuncSetAttribute(k_gate_up<FMT, G, NBG, R, SPEC, GEO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   launch_pdl(k_gate_up<FMT, G, NBG, R, SPEC, GEO>, grid, dim3(2 * R * G), smem, s, d, B, W);
@@ -1177,8 +1176,7 @@ template <int FMT, int G, int NBG, int ROWS, bool COMBINE, bool SPEC, int GEO>
 static cudaError_t launch_down_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int units,
                                  cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.down_row_bytes : W.down_row_bytes + 16;
-  const size_t smem = 16 + round16((size_t)ROWS * st) + 16 + (size_t)B.ms * d.amoe_stride +
-                      (FMT == RV_Q6_K ? (size_t)B.ms * d.mb * 64 * 4 : 0) + 16;
+  const size_t smem = 16 + round16((size_t)ROWS * st) + 16 + (size_t)B.ms * d.amoe_stride + 16;
   dim3 grid((unsigned)units, (unsigned)((d.H + ROWS - 1) / ROWS));
   cudaFuncSetAttribute(k_down<FMT, G, NBG, ROWS, COMBINE, SPEC, GEO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)smem);

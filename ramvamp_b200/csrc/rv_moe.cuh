@@ -1143,8 +1143,7 @@ RV_DEVFN bool gate_up_unit(const MoeDims &d, const MoeBufs &B, const MoeWeights 
   const size_t wtile = (size_t)R * st;
   uint8_t *wsm = sm + 16;                                       // [2][R][st]
   uint8_t *asm_ = wsm + ((2 * wtile + 15) & ~(size_t)15) + 16;  // [ms][act_stride]
-  int *asum = (int *)(asm_ + ms * d.act_stride);                // [ms][hb*64] (Q6_K)
-  float *gu = (float *)(asum + (FMT == RV_Q6_K ? ms * d.hb * 64 : 0));  // [2][R][MT]
+  float *gu = (float *)(asm_ + ms * d.act_stride);              // [2][R][MT]
   const uint8_t *blob = W.base + (size_t)e * W.stride;
   const uint8_t *gsrc = blob + W.gate_off + (size_t)tile * R * W.gu_row_bytes;
   const uint8_t *usrc = blob + W.up_off + (size_t)tile * R * W.gu_row_bytes;
@@ -1187,22 +1186,16 @@ RV_DEVFN bool gate_up_unit(const MoeDims &d, const MoeBufs &B, const MoeWeights 
     __syncthreads();
     if (!ok) return false;
     RV_PHASE(1, 2);
-    if constexpr (FMT == RV_Q6_K) {
-      for (int m = 0; m < mt; m++) act_word_sums(asm_ + (size_t)m * d.act_stride, d.hb, asum + m * d.hb * 64);
-      __syncthreads();
-    }
     for (int m0 = 0; m0 < mt; m0 += MT) {
       const int mm = min(MT, mt - m0);
       if constexpr (G > 1) {
         for (int m = 0; m < mm; m++) {
-          const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.act_stride,
-                                                        asum + (m0 + m) * d.hb * 64, g);
+          const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.act_stride, g);
           if (g == G - 1) gu[(part * R + r) * MT + m] = res;
         }
       } else {
         float res[MT];
-        row_dot_tokens<FMT, MT>(wrow, d.hb, asm_ + (size_t)m0 * d.act_stride, d.act_stride,
-                                asum + m0 * d.hb * 64, (size_t)d.hb * 64, mm, res);
+        row_dot_tokens<FMT, MT>(wrow, d.hb, asm_ + (size_t)m0 * d.act_stride, d.act_stride, mm, res);
 #pragma unroll
         for (int m = 0; m < MT; m++)
           if (m < mm) gu[(part * R + r) * MT + m] = res[m];
@@ -1322,7 +1315,6 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
   const size_t st = tile_stride<FMT>(W.down_row_bytes);
   uint8_t *wsm = sm + 16;
   uint8_t *asm_ = wsm + (((size_t)ROWS * st + 15) & ~(size_t)15) + 16;
-  int *asum = (int *)(asm_ + ms * d.amoe_stride);
   const bool abulk = rv_bulk_ok(B.acts_moe, asm_, d.amoe_stride);
   const int lane = threadIdx.x;
   if (lane == 0) {
@@ -1409,11 +1401,6 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
       __syncwarp();
       if (!ok) return;
       RV_PHASE(2, 3);
-      if constexpr (FMT == RV_Q6_K) {
-        for (int m = 0; m < mt; m++) act_word_sums(asm_ + (size_t)m * d.amoe_stride, d.mb, asum + m * d.mb * 64);
-        __syncwarp();
-      }
-      RV_PHASE(2, 6);
       auto pair_of = [&](int c) -> uint32_t {
         if constexpr (SPEC) return s_pair[c - p0];
         else return B.index[c];
@@ -1422,15 +1409,13 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
         const int mm = min(MT, mt - m0);
         if constexpr (G > 1) {
           for (int m = 0; m < mm; m++) {
-            const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.amoe_stride,
-                                                          asum + (m0 + m) * d.mb * 64, g);
+            const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.amoe_stride, g);
             const uint32_t pair = pair_of(c0 + m0 + m);
             if (g == G - 1 && live && pair != ~0u) down_out_row(B, pair, d.H)[row0 + rsub] = res;
           }
         } else {
           float res[MT];
-          row_dot_tokens<FMT, MT>(wrow, d.mb, asm_ + (size_t)m0 * d.amoe_stride, d.amoe_stride,
-                                  asum + m0 * d.mb * 64, (size_t)d.mb * 64, mm, res);
+          row_dot_tokens<FMT, MT>(wrow, d.mb, asm_ + (size_t)m0 * d.amoe_stride, d.amoe_stride, mm, res);
 #pragma unroll
           for (int m = 0; m < MT; m++)
             if (m < mm && live) {

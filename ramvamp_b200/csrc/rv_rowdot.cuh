@@ -25,13 +25,17 @@ RV_DEVFN void k4_unpack_words(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t &u
 }
 RV_DEVFN int byte_of(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xFFu); }
 
+// Four Q6_K levels q in [0, 63] (one per byte) -> the signed bytes q - 32:
+// each byte's top bit is set before subtracting 32, so no byte borrows from
+// the next, and flipping it back leaves q - 32 modulo 256.
+RV_DEVFN uint32_t q6_centered(uint32_t v) { return ((v | 0x80808080u) - 0x20202020u) ^ 0x80808080u; }
+
 // Integer lanes of one block for one activation block `act` (packed Q8_K in
 // shared memory, 4-byte aligned).  `blk` is the weight block in shared
 // memory: 16-byte aligned for Q4_K/Q5_K, any even address for Q6_K.
-// `asum` (Q6_K only): per activation word, the sum of its four bytes.
 template <int FMT>
-RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, const int *asum, int (&S)[8],
-                          int (&Mn)[4], float &dw, float &dmw) {
+RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, int (&S)[8], int (&Mn)[4], float &dw,
+                          float &dmw) {
   const int *aq = (const int *)(act + 4);
   if constexpr (FMT == RV_Q4_K || FMT == RV_Q5_K) {
     const uint4 hdr = *(const uint4 *)blk;
@@ -70,7 +74,7 @@ RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, const int *asu
       Mn[l] = byte_of(mw, (2 * l) & 3) * ((int)bs[4 * l] + (int)bs[4 * l + 1]) +
               byte_of(mw, (2 * l + 1) & 3) * ((int)bs[4 * l + 2] + (int)bs[4 * l + 3]);
     }
-  } else {  // Q6_K: S[L] = sum_{h,k} sc * sum_t (q - 32) a, via dp4a(q, a) - 32 * sum(a)
+  } else {  // Q6_K: S[L] = sum_{h,k} sc * sum_t (q - 32) a, one dp4a of the centered levels
     dw = h2f(ld16(blk + 208));
     dmw = 0.0f;
     const uint32_t s0 = ld32u(blk + 192), s1 = ld32u(blk + 196), s2 = ld32u(blk + 200),
@@ -93,7 +97,7 @@ RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, const int *asu
           const int w = 32 * h + 8 * k + L;  // activation word
           const int sidx = 8 * h + 2 * k + (L >= 4 ? 1 : 0);
           const int sc = (int)(int8_t)byte_of(sw[sidx >> 2], sidx & 3);
-          S[L] += sc * (__dp4a((int)v[k], aq[w], 0) - 32 * asum[w]);
+          S[L] += sc * __dp4a((int)q6_centered(v[k]), aq[w], 0);
         }
       }
     }
@@ -129,8 +133,8 @@ RV_DEVFN float lanes_final(const float (&acc)[8], const float (&accm)[4]) {
 // One row against MT activation rows (token m at acts + m*astride), all
 // blocks by this thread: the reference dot per token, exactly.
 template <int FMT, int MT>
-RV_DEVFN void row_dot_tokens(const uint8_t *wrow, int nb, const uint8_t *acts, size_t astride,
-                             const int *asum, size_t asum_stride, int mt, float (&out)[MT]) {
+RV_DEVFN void row_dot_tokens(const uint8_t *wrow, int nb, const uint8_t *acts, size_t astride, int mt,
+                             float (&out)[MT]) {
   constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
   float acc[MT][8], accm[MT][4];
 #pragma unroll
@@ -147,7 +151,7 @@ RV_DEVFN void row_dot_tokens(const uint8_t *wrow, int nb, const uint8_t *acts, s
         const uint8_t *act = acts + (size_t)m * astride + (size_t)b * 292;
         int S[8], Mn[4];
         float dw, dmw;
-        block_lanes<FMT>(wrow + (size_t)b * BB, act, asum + (size_t)m * asum_stride + 64 * b, S, Mn, dw, dmw);
+        block_lanes<FMT>(wrow + (size_t)b * BB, act, S, Mn, dw, dmw);
         lanes_fma<FMT>(S, Mn, dw, dmw, *(const float *)act, acc[m], accm[m]);
       }
     }
@@ -163,7 +167,7 @@ RV_DEVFN void row_dot_tokens(const uint8_t *wrow, int nb, const uint8_t *acts, s
 // the G lanes in block order, handed on with shuffles.  All 32 lanes must
 // call; the result is valid on lanes with g == G-1.
 template <int FMT, int G, int NBG>
-RV_DEVFN float row_dot_split(const uint8_t *wrow, const uint8_t *act_row, const int *asum, int g) {
+RV_DEVFN float row_dot_split(const uint8_t *wrow, const uint8_t *act_row, int g) {
   constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
   int S[NBG][8], Mn[NBG][4];
   float dw[NBG], dmw[NBG], yd[NBG];
@@ -171,7 +175,7 @@ RV_DEVFN float row_dot_split(const uint8_t *wrow, const uint8_t *act_row, const 
   for (int i = 0; i < NBG; i++) {
     const int b = g * NBG + i;
     const uint8_t *act = act_row + (size_t)b * 292;
-    block_lanes<FMT>(wrow + (size_t)b * BB, act, asum + 64 * b, S[i], Mn[i], dw[i], dmw[i]);
+    block_lanes<FMT>(wrow + (size_t)b * BB, act, S[i], Mn[i], dw[i], dmw[i]);
     yd[i] = *(const float *)act;
   }
   float acc[8], accm[4];
@@ -201,18 +205,4 @@ RV_DEVFN float row_dot_split(const uint8_t *wrow, const uint8_t *act_row, const 
     }
   }
   return lanes_final<FMT>(acc, accm);
-}
-
-// Per-word byte sums of staged activation blocks (Q6_K's -32 offset):
-// asum[b*64 + w] = sum of the four int8 in word w of block b.
-// Threads t0, t0 + nt, ... of the caller's group (default: the whole block).
-RV_DEVFN void act_word_sums(const uint8_t *act_row, int nb, int *asum, int t0 = -1, int nt = 0) {
-  if (t0 < 0) {
-    t0 = threadIdx.x;
-    nt = blockDim.x;
-  }
-  for (int i = t0; i < nb * 64; i += nt) {
-    const int b = i >> 6, w = i & 63;
-    asum[i] = __dp4a(*(const int *)(act_row + (size_t)b * 292 + 4 + 4 * w), 0x01010101, 0);
-  }
 }

@@ -105,7 +105,7 @@ def decode(n_layers: int = 4) -> None:
         mhz = (b0[used, 8] - b0[used, 7]) / (b0[used, 3] - b0[used, 2]) * 1e3
         print(f"   SM clock during the norm (clock64 / globaltimer): p50 {np.median(mhz):.0f} MHz")
     _print_phases("gate_up", bufs[1], t0, ["start", "unit", "data", "compute", "LAST:quant", "row dots (thread 0)"])
-    _print_phases("down", bufs[2], t0, ["start", "weights issued", "pdl_wait", "data", "compute", "LAST:combine", "act sums"])
+    _print_phases("down", bufs[2], t0, ["start", "weights issued", "pdl_wait", "data", "compute", "LAST:combine"])
     tail = bufs[3][0]
     names = ["logits+max(warp)", "max(block)", "exp+sum(warp)", "sum(block)", "probs+finite", "rank", "sync",
              "weights"]
