@@ -1176,7 +1176,8 @@ template <int FMT, int G, int NBG, int ROWS, bool COMBINE, bool SPEC, int GEO>
 static cudaError_t launch_down_t(const MoeDims &d, const MoeBufs &B, const MoeWeights &W, int units,
                                  cudaStream_t s) {
   const size_t st = FMT == RV_Q6_K ? W.down_row_bytes : W.down_row_bytes + 16;
-  const size_t smem = 16 + round16((size_t)ROWS * st) + 16 + (size_t)B.ms * d.amoe_stride + 16;
+  const size_t smem = 16 + round16((size_t)ROWS * st) + 16 + (size_t)B.ms * d.amoe_stride + 16 +
+                      (G > 1 ? (size_t)B.ms * d.mb * RV_ACT_AL : 0);
   dim3 grid((unsigned)units, (unsigned)((d.H + ROWS - 1) / ROWS));
   cudaFuncSetAttribute(k_down<FMT, G, NBG, ROWS, COMBINE, SPEC, GEO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)smem);

@@ -1315,6 +1315,7 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
   const size_t st = tile_stride<FMT>(W.down_row_bytes);
   uint8_t *wsm = sm + 16;
   uint8_t *asm_ = wsm + (((size_t)ROWS * st + 15) & ~(size_t)15) + 16;
+  uint8_t *arp = asm_ + ms * d.amoe_stride;  // split mode: [ms][mb][RV_ACT_AL] aligned copies
   const bool abulk = rv_bulk_ok(B.acts_moe, asm_, d.amoe_stride);
   const int lane = threadIdx.x;
   if (lane == 0) {
@@ -1401,6 +1402,11 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
       __syncwarp();
       if (!ok) return;
       RV_PHASE(2, 3);
+      if constexpr (G > 1) {  // the row dots read aligned copies (measured: 2.6 -> 2.15 us at decode)
+        for (int m = 0; m < mt; m++)
+          act_align_row(asm_ + (size_t)m * d.amoe_stride, d.mb, arp + (size_t)m * d.mb * RV_ACT_AL, lane, 32);
+        __syncwarp();
+      }
       auto pair_of = [&](int c) -> uint32_t {
         if constexpr (SPEC) return s_pair[c - p0];
         else return B.index[c];
@@ -1409,7 +1415,8 @@ __global__ void __launch_bounds__(32, 16) k_down(MoeDims dd, MoeBufs B, MoeWeigh
         const int mm = min(MT, mt - m0);
         if constexpr (G > 1) {
           for (int m = 0; m < mm; m++) {
-            const float res = row_dot_split<FMT, G, NBG>(wrow, asm_ + (size_t)(m0 + m) * d.amoe_stride, g);
+            const float res =
+                row_dot_split<FMT, G, NBG, true>(wrow, arp + (size_t)(m0 + m) * d.mb * RV_ACT_AL, g);
             const uint32_t pair = pair_of(c0 + m0 + m);
             if (g == G - 1 && live && pair != ~0u) down_out_row(B, pair, d.H)[row0 + rsub] = res;
           }

@@ -30,13 +30,36 @@ RV_DEVFN int byte_of(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xFFu); 
 // the next, and flipping it back leaves q - 32 modulo 256.
 RV_DEVFN uint32_t q6_centered(uint32_t v) { return ((v | 0x80808080u) - 0x20202020u) ^ 0x80808080u; }
 
-// Integer lanes of one block for one activation block `act` (packed Q8_K in
-// shared memory, 4-byte aligned).  `blk` is the weight block in shared
-// memory: 16-byte aligned for Q4_K/Q5_K, any even address for Q6_K.
-template <int FMT>
+// Activation blocks in shared memory come in two layouts: the packed Q8_K
+// block (292 bytes: d, 256 levels, 16 i16 block sums), and -- AL -- an
+// aligned copy (RV_ACT_AL bytes: levels at 0, block sums at 256, d at 288,
+// 16-byte aligned), so the levels load four words at a time.
+#define RV_ACT_AL 304
+template <bool AL>
+RV_DEVFN const int *act_levels(const uint8_t *act) { return (const int *)(act + (AL ? 0 : 4)); }
+template <bool AL>
+RV_DEVFN const int16_t *act_bsums(const uint8_t *act) { return (const int16_t *)(act + (AL ? 256 : 260)); }
+template <bool AL>
+RV_DEVFN float act_scale(const uint8_t *act) { return *(const float *)(act + (AL ? 288 : 0)); }
+// Copies nb packed blocks (src, 4-byte aligned) into the aligned layout at
+// dst, 32-bit words, threads t0, t0 + nt, ...
+RV_DEVFN void act_align_row(const uint8_t *src, int nb, uint8_t *dst, int t0, int nt) {
+  for (int i = t0; i < nb * 73; i += nt) {
+    const int b = i / 73, w = i % 73;  // word w of packed block b: 0 = d, 1..64 levels, 65..72 block sums
+    const uint32_t v = *(const uint32_t *)(src + (size_t)b * 292 + 4 * w);
+    uint8_t *o = dst + (size_t)b * RV_ACT_AL;
+    *(uint32_t *)(o + (w == 0 ? 288 : 4 * (w - 1))) = v;
+  }
+}
+
+// Integer lanes of one block for one activation block `act` (in shared
+// memory, packed and 4-byte aligned, or AL: the aligned layout).  `blk` is
+// the weight block in shared memory: 16-byte aligned for Q4_K/Q5_K, any
+// even address for Q6_K.
+template <int FMT, bool AL = false>
 RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, int (&S)[8], int (&Mn)[4], float &dw,
                           float &dmw) {
-  const int *aq = (const int *)(act + 4);
+  const int *aq = act_levels<AL>(act);
   if constexpr (FMT == RV_Q4_K || FMT == RV_Q5_K) {
     const uint4 hdr = *(const uint4 *)blk;
     dw = h2f((uint16_t)(hdr.x & 0xFFFFu));
@@ -55,6 +78,20 @@ RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, int (&S)[8], i
     for (int j = 0; j < 4; j++) {
       const uint4 q0 = *(const uint4 *)(qs + 32 * j), q1 = *(const uint4 *)(qs + 32 * j + 16);
       const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+      int aw[16];  // activation words 16j .. 16j+15
+      if constexpr (AL) {
+#pragma unroll
+        for (int v = 0; v < 4; v++) {
+          const int4 a4 = *(const int4 *)(aq + 16 * j + 4 * v);
+          aw[4 * v] = a4.x;
+          aw[4 * v + 1] = a4.y;
+          aw[4 * v + 2] = a4.z;
+          aw[4 * v + 3] = a4.w;
+        }
+      } else {
+#pragma unroll
+        for (int v = 0; v < 16; v++) aw[v] = aq[16 * j + v];
+      }
       const int sl = byte_of(j < 2 ? u0 : u1, (2 * j) & 3), sh = byte_of(j < 2 ? u0 : u1, (2 * j + 1) & 3);
 #pragma unroll
       for (int L = 0; L < 8; L++) {
@@ -64,10 +101,10 @@ RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, int (&S)[8], i
           lo += ((h >> (2 * j)) & 0x01010101u) << 4;
           hi += ((h >> (2 * j + 1)) & 0x01010101u) << 4;
         }
-        S[L] += sl * __dp4a((int)lo, aq[16 * j + L], 0) + sh * __dp4a((int)hi, aq[16 * j + 8 + L], 0);
+        S[L] += sl * __dp4a((int)lo, aw[L], 0) + sh * __dp4a((int)hi, aw[8 + L], 0);
       }
     }
-    const int16_t *bs = (const int16_t *)(act + 260);
+    const int16_t *bs = act_bsums<AL>(act);
 #pragma unroll
     for (int l = 0; l < 4; l++) {
       const uint32_t mw = l < 2 ? u2 : u3;
@@ -77,17 +114,34 @@ RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, int (&S)[8], i
   } else {  // Q6_K: S[L] = sum_{h,k} sc * sum_t (q - 32) a, one dp4a of the centered levels
     dw = h2f(ld16(blk + 208));
     dmw = 0.0f;
-    const uint32_t s0 = ld32u(blk + 192), s1 = ld32u(blk + 196), s2 = ld32u(blk + 200),
-                   s3 = ld32u(blk + 204);
-    const uint32_t sw[4] = {s0, s1, s2, s3};
+    // Word i of the block (any even address): two aligned words and a
+    // funnel shift; neighbouring words share their aligned loads.
+    const uint32_t *wb = (const uint32_t *)((uintptr_t)blk & ~(uintptr_t)3);
+    const uint32_t wsh = (uint32_t)((uintptr_t)blk & 3) * 8u;
+    auto word = [&](int i) { return __funnelshift_r(wb[i], wb[i + 1], wsh); };
+    const uint32_t sw[4] = {word(48), word(49), word(50), word(51)};
 #pragma unroll
     for (int L = 0; L < 8; L++) S[L] = 0;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
+      int aw[32];  // activation words 32h .. 32h+31
+      if constexpr (AL) {
+#pragma unroll
+        for (int v = 0; v < 8; v++) {
+          const int4 a4 = *(const int4 *)(aq + 32 * h + 4 * v);
+          aw[4 * v] = a4.x;
+          aw[4 * v + 1] = a4.y;
+          aw[4 * v + 2] = a4.z;
+          aw[4 * v + 3] = a4.w;
+        }
+      } else {
+#pragma unroll
+        for (int v = 0; v < 32; v++) aw[v] = aq[32 * h + v];
+      }
 #pragma unroll
       for (int L = 0; L < 8; L++) {
-        const uint32_t ql0 = ld32u(blk + 64 * h + 4 * L), ql1 = ld32u(blk + 64 * h + 32 + 4 * L);
-        const uint32_t qh = ld32u(blk + 128 + 32 * h + 4 * L);
+        const uint32_t ql0 = word(16 * h + L), ql1 = word(16 * h + 8 + L);
+        const uint32_t qh = word(32 + 8 * h + L);
         const uint32_t v[4] = {(ql0 & 0x0F0F0F0Fu) | ((qh & 0x03030303u) << 4),
                                (ql1 & 0x0F0F0F0Fu) | (((qh >> 2) & 0x03030303u) << 4),
                                ((ql0 >> 4) & 0x0F0F0F0Fu) | (((qh >> 4) & 0x03030303u) << 4),
@@ -97,7 +151,7 @@ RV_DEVFN void block_lanes(const uint8_t *blk, const uint8_t *act, int (&S)[8], i
           const int w = 32 * h + 8 * k + L;  // activation word
           const int sidx = 8 * h + 2 * k + (L >= 4 ? 1 : 0);
           const int sc = (int)(int8_t)byte_of(sw[sidx >> 2], sidx & 3);
-          S[L] += sc * __dp4a((int)q6_centered(v[k]), aq[w], 0);
+          S[L] += sc * __dp4a((int)q6_centered(v[k]), aw[w - 32 * h], 0);
         }
       }
     }
@@ -166,7 +220,7 @@ RV_DEVFN void row_dot_tokens(const uint8_t *wrow, int nb, const uint8_t *acts, s
 // integer lane sums are formed in parallel; the FMA chain then runs through
 // the G lanes in block order, handed on with shuffles.  All 32 lanes must
 // call; the result is valid on lanes with g == G-1.
-template <int FMT, int G, int NBG>
+template <int FMT, int G, int NBG, bool AL = false>
 RV_DEVFN float row_dot_split(const uint8_t *wrow, const uint8_t *act_row, int g) {
   constexpr int BB = FMT == RV_Q4_K ? 144 : FMT == RV_Q5_K ? 176 : 210;
   int S[NBG][8], Mn[NBG][4];
@@ -174,9 +228,9 @@ RV_DEVFN float row_dot_split(const uint8_t *wrow, const uint8_t *act_row, int g)
 #pragma unroll
   for (int i = 0; i < NBG; i++) {
     const int b = g * NBG + i;
-    const uint8_t *act = act_row + (size_t)b * 292;
-    block_lanes<FMT>(wrow + (size_t)b * BB, act, S[i], Mn[i], dw[i], dmw[i]);
-    yd[i] = *(const float *)act;
+    const uint8_t *act = act_row + (size_t)b * (AL ? RV_ACT_AL : 292);
+    block_lanes<FMT, AL>(wrow + (size_t)b * BB, act, S[i], Mn[i], dw[i], dmw[i]);
+    yd[i] = act_scale<AL>(act);
   }
   float acc[8], accm[4];
 #pragma unroll
