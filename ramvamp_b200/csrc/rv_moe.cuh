@@ -1256,11 +1256,14 @@ __global__ void __launch_bounds__(2 * R * G, 4) k_gate_up(MoeDims dd, MoeBufs B,
   if constexpr (SPEC) {
     // Reads only the bounds and activations of the routing kernel, which
     // completed before the exact-chain kernel ahead of this one passed its
-    // wait, i.e. before this grid launched.  The down kernel may launch at
-    // once: before its own wait it too reads only the bounds.
-    pdl_trigger();
+    // wait, i.e. before this grid launched.  The down kernel may launch once
+    // the set is rebuilt (before its own wait it too reads only the bounds):
+    // measured 864 against 858 tok/s when it launched at this grid's start
+    // (its early CTAs competed with the set rebuild), 814 when it launched
+    // after the gate/up rows (too late to stage its weights).
     __shared__ SpecSmem ss;
     spec_build(d.E, d.K, B.T, B.spec, ss);
+    pdl_trigger();
     RV_PHASE(1, 1);
     for (int u = blockIdx.x; u < ss.n_units; u += gridDim.x) {
       const int e = ss.uexp[u], p0 = ss.start[e];
