@@ -1446,8 +1446,9 @@ extern "C" int rv_moe_forward(rv_moe *m, const rv_expert_table *table, uint32_t 
     const size_t xrow = (size_t)(d.H + 4) * 4;
     // Shared memory padded past half an SM's: one routing CTA per SM.
     const size_t rs_need = 16 + (size_t)(RV_SPEC_EPC + 1) * d.H * 4 + T * xrow;
+    // The expert CTAs, then one CTA per four Q8_K blocks of the normed rows.
     RV_CUDA(launch_pdl(geo_qwen3(d) ? k_route_spec<RV_GEO_QWEN3> : k_route_spec<0>,
-                       dim3((unsigned)((d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC)), dim3(128),
+                       dim3((unsigned)((d.E + RV_SPEC_EPC - 1) / RV_SPEC_EPC + (T * d.hb + 3) / 4)), dim3(128),
                        std::max(rs_need, (size_t)RV_ROUTE_SMEM_ONE_PER_SM), s, d, B));
     if ((rc = launch_route_chain(d, B, T, W, s))) return rc;
     spec_units = std::min(d.E, T * d.K);
