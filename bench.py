@@ -767,7 +767,8 @@ def workload_desc(args, n_layers, tokens, world):
          "batch": f"config3 batched decode: {tokens} sequences x 1 token through {n_layers} MoE layers, "
                   "router biased to Zipf s=1.1 expert popularity",
          "ep": f"config4 expert-parallel prefill: {tokens} tokens (8 x 512) through {n_layers} MoE layers, "
-               f"Zipf s=1.1, 128 experts sharded over {world} GPU(s) by id mod {world}"}
+               "Zipf s=1.1, " + (f"128 experts sharded over {world} GPUs by measured load, "
+                                   f"{128 // world} per GPU" if world > 1 else "128 experts on one GPU")}
     return d[args.workload]
 
 
@@ -969,9 +970,10 @@ def ep_launches_per_layer(tensor: bool) -> int:
 
 def run_ep(args, table=None, quiet=False):
     """Config 4: 4096 tokens (8 x 512) with Zipf s=1.1 routing through all
-    48 MoE layers, the 128 experts spread over the N ranks by id mod N.
-    Each rank routes 4096/N home tokens; dispatch, expert outputs and the
-    per-layer flags go through GPU memory (rv_moe_ep_forward), and a step
+    48 MoE layers, the 128 experts spread over the N ranks by the load a
+    calibration batch measures through each layer's router
+    (`balanced_placement`, 128/N experts per rank).  Each rank routes 4096/N
+    home tokens; dispatch, expert outputs and the per-layer flags go through GPU memory (rv_moe_ep_forward), and a step
     (48 layers) is one captured CUDA graph.  Strong scaling: the total work
     is fixed.  `table`: the full 48-layer table to reuse at N=1.  Returns the
     JSON line (rank 0), printed unless quiet."""
